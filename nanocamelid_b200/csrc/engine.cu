@@ -1,0 +1,964 @@
+// Host engine behind the C ABI (include/ncm.h): model load (GGUF or on-device synthetic),
+// the per-token decode step captured as CUDA graphs, tensor-parallel plumbing (CUDA IPC
+// peer buffers for the fused NVLink reduction, NCCL for the baseline reducer).
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <math.h>
+#include <string.h>
+#include <string>
+#include <vector>
+#include "../../include/ncm.h"
+#include "gguf.h"
+#include "common.cuh"
+#include "ncm_internal.h"
+#include "synth.h"
+
+using namespace ncm;
+
+static thread_local std::string g_err;
+static ncm_status fail(ncm_status code, const std::string& msg) {
+    g_err = msg;
+    return code;
+}
+#define CK(x)                                                                                   \
+    do {                                                                                        \
+        cudaError_t e_ = (x);                                                                   \
+        if (e_ != cudaSuccess) return fail(NCM_ECUDA, std::string(#x) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+#define CKL(x)                                                                                          \
+    do {                                                                                                \
+        int e_ = (x);                                                                                   \
+        if (e_ != 0) return fail(NCM_ECUDA, std::string(#x) + ": " + cudaGetErrorString((cudaError_t)e_)); \
+    } while (0)
+
+extern "C" const char* ncm_last_error(void) { return g_err.c_str(); }
+extern "C" int ncm_version(void) { return 1; }
+
+// ------------------------------------------------------------------ NCCL (dlopen'd, baseline only)
+namespace {
+typedef struct { char internal[128]; } nccl_uid;
+typedef void* nccl_comm;
+struct Nccl {
+    void* h = nullptr;
+    int (*GetUniqueId)(nccl_uid*) = nullptr;
+    int (*CommInitRank)(nccl_comm*, int, nccl_uid, int) = nullptr;
+    int (*AllReduce)(const void*, void*, size_t, int, int, nccl_comm, cudaStream_t) = nullptr;
+    int (*AllGather)(const void*, void*, size_t, int, nccl_comm, cudaStream_t) = nullptr;
+    int (*CommDestroy)(nccl_comm) = nullptr;
+    bool load() {
+        if (h) return true;
+        const char* names[] = {"libnccl.so.2", "libnccl.so"};
+        for (auto n : names) {
+            h = dlopen(n, RTLD_NOW | RTLD_GLOBAL);
+            if (h) break;
+        }
+        if (!h) return false;
+        GetUniqueId = (int (*)(nccl_uid*))dlsym(h, "ncclGetUniqueId");
+        CommInitRank = (int (*)(nccl_comm*, int, nccl_uid, int))dlsym(h, "ncclCommInitRank");
+        AllReduce = (int (*)(const void*, void*, size_t, int, int, nccl_comm, cudaStream_t))dlsym(h, "ncclAllReduce");
+        AllGather = (int (*)(const void*, void*, size_t, int, nccl_comm, cudaStream_t))dlsym(h, "ncclAllGather");
+        CommDestroy = (int (*)(nccl_comm))dlsym(h, "ncclCommDestroy");
+        return GetUniqueId && CommInitRank && AllReduce && AllGather;
+    }
+};
+Nccl g_nccl;
+constexpr int kNcclFloat = 7;   // ncclFloat32
+constexpr int kNcclSum = 0;     // ncclSum
+}  // namespace
+
+// ------------------------------------------------------------------ model
+struct DevMat {
+    int type = 0, rows = 0, cols = 0, pitch = 0;
+    uint8_t* d = nullptr;
+};
+struct Layer {
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+    DevMat wq, wk, wv, wo, w1, w3, w2;
+};
+
+struct ncm_model {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int emb = 0, layers = 0, heads = 0, kv_heads = 0, hd = 0, ffn = 0, vocab = 0, ctx = 0, rope_dim = 0;
+    float eps = 1e-5f, base = 10000.0f;
+    int nshards = 1, shard = 0;
+    int q0 = 0, qh = 0, k0 = 0, kh = 0, f0 = 0, fl = 0, h0 = 0, hr = 0;
+    DevMat embd, head;
+    float* out_norm = nullptr;
+    std::vector<Layer> L;
+    float *hidden = nullptr, *q = nullptr, *att = nullptr, *act = nullptr, *logits = nullptr, *kc = nullptr,
+          *vc = nullptr, *attn_part = nullptr, *part = nullptr;
+    unsigned *attn_cnt = nullptr, *amax_cnt = nullptr;
+    float2 *amax_part = nullptr, *rope = nullptr, *head_out = nullptr, *gather = nullptr;
+    float* embd_ssq = nullptr;   // per vocab row: sequential f32 sum of squares of the embedding
+    int *state = nullptr, *tokens = nullptr, *err = nullptr;
+    int* h_stage = nullptr;   // pinned staging for small transfers
+    int nsplit = 1, max_per = 1;
+    std::vector<void*> allocs;
+    cudaGraphExec_t g_full = nullptr, g_nohead = nullptr;
+    bool dirty = true;
+    // tensor parallel
+    int world = 1, rank = 0, reduce_mode = NCM_REDUCE_FUSED_P2P;
+    bool tp_ready = false;
+    TpComm comm{};
+    uint8_t* comm_base = nullptr;
+    size_t comm_bytes = 0, off_flags = 0, off_hx = 0, off_hflags = 0;
+    std::vector<void*> ipc_open;
+    nccl_comm nccl = nullptr;
+    uint64_t timeout_ns = 10000000000ull;
+};
+
+static ncm_status dalloc(ncm_model* m, void** p, size_t bytes) {
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e != cudaSuccess) return fail(NCM_ECUDA, std::string("cudaMalloc ") + std::to_string(bytes) + ": " + cudaGetErrorString(e));
+    m->allocs.push_back(*p);
+    return NCM_OK;
+}
+#define DALLOC(ptr, bytes)                                                   \
+    do {                                                                     \
+        ncm_status s_ = dalloc(m, (void**)&(ptr), (size_t)(bytes));          \
+        if (s_ != NCM_OK) return s_;                                         \
+    } while (0)
+
+static bool gemv_type_ok(int t) { return t == NCM_T_Q4_0 || t == NCM_T_Q8_0 || t == NCM_T_Q4_K; }
+static int row_bytes(int t, int cols) { return cols / ncm_type_block_elems(t) * ncm_type_block_bytes(t); }
+
+static void free_model(ncm_model* m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    if (m->g_full) cudaGraphExecDestroy(m->g_full);
+    if (m->g_nohead) cudaGraphExecDestroy(m->g_nohead);
+    for (void* p : m->ipc_open) cudaIpcCloseMemHandle(p);
+    if (m->nccl && g_nccl.CommDestroy) g_nccl.CommDestroy(m->nccl);
+    for (void* p : m->allocs) cudaFree(p);
+    if (m->h_stage) cudaFreeHost(m->h_stage);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+// Shard geometry: tp.rs:641-701 validate_shares + shard_geometry.
+extern "C" ncm_status ncm_shard_geometry(int heads, int kv_heads, int ffn, int vocab, const int* shares,
+                                        int nshards, int shard, int* out) {
+    if (!shares || !out || nshards <= 0 || kv_heads <= 0) return fail(NCM_EINVAL, "bad shard arguments");
+    long sum = 0;
+    for (int i = 0; i < nshards; ++i) {
+        if (shares[i] <= 0) return fail(NCM_EINVAL, "every shard needs at least one kv head");
+        sum += shares[i];
+    }
+    if (sum != kv_heads) return fail(NCM_EINVAL, "shares must sum to the kv head count");
+    for (int i = 0; i < nshards; ++i)
+        if (((long)ffn * shares[i]) % ((long)kv_heads * 32)) return fail(NCM_EINVAL, "ffn not 32-block divisible for a share");
+    if (shard < 0 || shard >= nshards) return fail(NCM_EINVAL, "bad shard index");
+    const int qpk = heads / kv_heads, unit = ffn / kv_heads;
+    int kv_start = 0;
+    for (int i = 0; i < shard; ++i) kv_start += shares[i];
+    long acc = 0, hs = 0, he = 0;
+    for (int i = 0; i < nshards; ++i) {
+        if (i == shard) hs = acc;
+        acc += ((long)vocab * shares[i] / kv_heads) & ~3L;
+        if (i == shard) he = acc;
+    }
+    out[0] = kv_start * qpk;
+    out[1] = shares[shard] * qpk;
+    out[2] = kv_start;
+    out[3] = shares[shard];
+    out[4] = kv_start * unit;
+    out[5] = shares[shard] * unit;
+    out[6] = (int)hs;
+    out[7] = shard + 1 == nshards ? (int)(vocab - hs) : (int)(he - hs);
+    return NCM_OK;
+}
+
+// Common set-up once the global config is known: shard geometry, activation buffers,
+// KV cache, rope table, state.
+static ncm_status setup_buffers(ncm_model* m, const int* shares, int nshards, int shard) {
+    if (m->heads % m->kv_heads) return fail(NCM_EINVAL, "heads must be a multiple of kv heads");
+    if (m->emb % 256) return fail(NCM_EUNSUPPORTED, "embedding length must be a multiple of 256");
+    if (m->hd % 32 || m->hd > 256 || m->heads / m->kv_heads > 8)
+        return fail(NCM_EUNSUPPORTED, "head_dim must be a multiple of 32 (<= 256), group size <= 8");
+    if (nshards > 1) {
+        if (nshards > kMaxWorld) return fail(NCM_EINVAL, "at most 8 shards");
+        int g[8];
+        ncm_status s = ncm_shard_geometry(m->heads, m->kv_heads, m->ffn, m->vocab, shares, nshards, shard, g);
+        if (s) return s;
+        m->q0 = g[0]; m->qh = g[1]; m->k0 = g[2]; m->kh = g[3]; m->f0 = g[4]; m->fl = g[5]; m->h0 = g[6]; m->hr = g[7];
+    } else {
+        m->q0 = 0; m->qh = m->heads; m->k0 = 0; m->kh = m->kv_heads; m->f0 = 0; m->fl = m->ffn; m->h0 = 0; m->hr = m->vocab;
+    }
+    m->nshards = nshards > 1 ? nshards : 1;
+    m->shard = nshards > 1 ? shard : 0;
+    m->world = m->nshards;
+    m->rank = m->shard;
+    if ((m->qh * m->hd) % 64 || m->fl % 64) return fail(NCM_EUNSUPPORTED, "shard widths must be multiples of 64");
+    const int qw = m->qh * m->hd, kw = m->kh * m->hd;
+    DALLOC(m->hidden, 4 * m->emb);
+    DALLOC(m->q, 4 * qw);
+    DALLOC(m->att, 4 * qw);
+    DALLOC(m->act, 4 * m->fl);
+    DALLOC(m->logits, 4 * (size_t)m->hr);
+    DALLOC(m->part, 4 * m->emb);
+    DALLOC(m->kc, 4 * (size_t)m->layers * m->ctx * kw);
+    DALLOC(m->vc, 4 * (size_t)m->layers * m->ctx * kw);
+    m->nsplit = num_sms() / m->kh;
+    if (m->nsplit < 1) m->nsplit = 1;
+    if (m->nsplit > m->ctx) m->nsplit = m->ctx;
+    m->max_per = (m->ctx + m->nsplit - 1) / m->nsplit;
+    DALLOC(m->attn_part, 4 * (size_t)m->qh * m->nsplit * (m->hd + 2));
+    DALLOC(m->attn_cnt, 4 * m->kh);
+    DALLOC(m->amax_part, 8 * num_sms());
+    DALLOC(m->amax_cnt, 4);
+    DALLOC(m->head_out, 8);
+    DALLOC(m->gather, 8 * kMaxWorld);
+    DALLOC(m->state, 4 * ST_COUNT);
+    DALLOC(m->tokens, 4 * (size_t)m->ctx);
+    DALLOC(m->err, 4);
+    CK(cudaMemset(m->attn_cnt, 0, 4 * m->kh));
+    CK(cudaMemset(m->amax_cnt, 0, 4));
+    CK(cudaMemset(m->state, 0, 4 * ST_COUNT));
+    CK(cudaMemset(m->tokens, 0, 4 * (size_t)m->ctx));
+    CK(cudaMemset(m->err, 0, 4));
+    CK(cudaMemset(m->hidden, 0, 4 * m->emb));
+    CK(cudaMemset(m->kc, 0, 4 * (size_t)m->layers * m->ctx * kw));
+    CK(cudaMemset(m->vc, 0, 4 * (size_t)m->layers * m->ctx * kw));
+    CK(cudaMallocHost((void**)&m->h_stage, 4096));
+    // inference.rs:860-900 cached_rope_angles with the host libm (the reference calls the
+    // same glibc powf / sinf / cosf): table[pos][i] = (sin, cos).
+    const int half = m->rope_dim / 2;
+    std::vector<float2> rt((size_t)m->ctx * half);
+    for (int pos = 0; pos < m->ctx; ++pos)
+        for (int i = 0; i < half; ++i) {
+            float theta = powf(m->base, -((float)(i * 2)) / (float)m->rope_dim);
+            float angle = (float)pos * theta;
+            rt[(size_t)pos * half + i] = make_float2(sinf(angle), cosf(angle));
+        }
+    DALLOC(m->rope, sizeof(float2) * rt.size());
+    CK(cudaMemcpy(m->rope, rt.data(), sizeof(float2) * rt.size(), cudaMemcpyHostToDevice));
+    if (m->world > 1) {
+        // Exchange area, identical layout on every rank:
+        // recv[2L][W][H] f32 | flags[2L][grid_max][W] u32 | hx[W] float2 | hflags[W] u32.
+        const size_t W = (size_t)m->world, gm = (size_t)num_sms();
+        size_t off = 4 * 2 * (size_t)m->layers * W * m->emb;
+        off = (off + 255) / 256 * 256;
+        m->off_flags = off;
+        off += 4 * 2 * (size_t)m->layers * gm * W;
+        off = (off + 255) / 256 * 256;
+        m->off_hx = off;
+        off += 8 * W;
+        off = (off + 255) / 256 * 256;
+        m->off_hflags = off;
+        off += 4 * W;
+        m->comm_bytes = (off + 4095) / 4096 * 4096;
+        DALLOC(m->comm_base, m->comm_bytes);
+        CK(cudaMemset(m->comm_base, 0, m->comm_bytes));
+    }
+    return NCM_OK;
+}
+
+static ncm_status check_matrix_shape(const DevMat& d, const char* what) {
+    if (!gemv_type_ok(d.type)) return fail(NCM_EUNSUPPORTED, std::string(what) + ": tensor type outside Q4_0/Q8_0/Q4_K");
+    if (d.cols % 64 || d.cols % ncm_type_block_elems(d.type)) return fail(NCM_EUNSUPPORTED, std::string(what) + ": columns not block aligned");
+    if (d.cols / 64 > 512) return fail(NCM_EUNSUPPORTED, std::string(what) + ": more than 32768 columns");
+    return NCM_OK;
+}
+
+// Upload rows [r0,r0+nrows) x cols [c0,c0+ncols) of a GGUF tensor (raw blocks unchanged;
+// row pitch rounded up to 16 bytes so every row tile is a legal bulk copy).
+static ncm_status upload_slice(ncm_model* m, const GgufFile& g, const char* name, int expect_rows, int expect_cols,
+                               int r0, int nrows, int c0, int ncols, DevMat& out) {
+    const GgufTensor* t = g.find(name);
+    if (!t) return fail(NCM_EIO, std::string("missing tensor ") + name);
+    if (t->dims.size() != 2 || (int)t->dims[0] != expect_cols || (int)t->dims[1] != expect_rows)
+        return fail(NCM_EIO, std::string("unexpected shape for ") + name);
+    out.type = t->type;
+    out.rows = nrows;
+    out.cols = ncols;
+    const int full_rb = row_bytes(t->type, expect_cols), rb = row_bytes(t->type, ncols);
+    out.pitch = (rb + 15) / 16 * 16;
+    const int be = ncm_type_block_elems(t->type);
+    if (c0 % be || ncols % be) return fail(NCM_EINVAL, std::string("column slice not block aligned: ") + name);
+    DALLOC(out.d, (size_t)out.pitch * nrows);
+    const uint8_t* src = g.data(*t) + (size_t)r0 * full_rb + (size_t)(c0 / be) * ncm_type_block_bytes(t->type);
+    CK(cudaMemcpy2D(out.d, out.pitch, src, full_rb, rb, nrows, cudaMemcpyHostToDevice));
+    return NCM_OK;
+}
+
+static ncm_status upload_f32(ncm_model* m, const GgufFile& g, const char* name, int n, float** out) {
+    const GgufTensor* t = g.find(name);
+    if (!t) return fail(NCM_EIO, std::string("missing tensor ") + name);
+    std::vector<float> v(n);
+    const uint8_t* d = g.data(*t);
+    if (t->type == NCM_T_F32) memcpy(v.data(), d, 4 * (size_t)n);
+    else if (t->type == NCM_T_F16) for (int i = 0; i < n; ++i) v[i] = ncm_f16_to_f32((uint16_t)(d[2 * i] | (d[2 * i + 1] << 8)));
+    else return fail(NCM_EUNSUPPORTED, std::string("norm tensor must be F32/F16: ") + name);
+    DALLOC(*out, 4 * (size_t)n);
+    CK(cudaMemcpy(*out, v.data(), 4 * (size_t)n, cudaMemcpyHostToDevice));
+    return NCM_OK;
+}
+
+// Tied head: Q4_0 requant of token_embd rows [h0, h0+hr) (model.rs:471-508).
+static ncm_status build_tied_head(ncm_model* m) {
+    m->head.type = NCM_T_Q4_0;
+    m->head.rows = m->hr;
+    m->head.cols = m->emb;
+    m->head.pitch = (row_bytes(NCM_T_Q4_0, m->emb) + 15) / 16 * 16;
+    DALLOC(m->head.d, (size_t)m->head.pitch * m->hr);
+    CKL(requant_q4_0_launch(m->embd.type, m->embd.d + (size_t)m->h0 * m->embd.pitch, m->hr, m->emb, m->embd.pitch,
+                            m->head.d, m->head.pitch, m->stream));
+    CK(cudaStreamSynchronize(m->stream));
+    return NCM_OK;
+}
+
+static ncm_status check_all_shapes(ncm_model* m) {
+    ncm_status s;
+    DALLOC(m->embd_ssq, 4 * (size_t)m->vocab);
+    CKL(embed_ssq_launch(m->embd.type, m->embd.d, m->embd.pitch, m->emb, m->vocab, m->embd_ssq, m->stream));
+    CK(cudaStreamSynchronize(m->stream));
+    if ((s = check_matrix_shape(m->head, "output"))) return s;
+    for (auto& l : m->L) {
+        const DevMat* ms[] = {&l.wq, &l.wk, &l.wv, &l.wo, &l.w1, &l.w3, &l.w2};
+        for (auto d : ms)
+            if ((s = check_matrix_shape(*d, "layer"))) return s;
+        if (l.wq.type != l.wk.type || l.wq.type != l.wv.type || l.w1.type != l.w3.type)
+            return fail(NCM_EUNSUPPORTED, "q/k/v (and gate/up) must share one quant type");
+    }
+    int t = m->embd.type;
+    if (!(t == NCM_T_Q4_0 || t == NCM_T_Q8_0 || t == NCM_T_Q4_K || t == NCM_T_F32 || t == NCM_T_F16))
+        return fail(NCM_EUNSUPPORTED, "token_embd type");
+    return NCM_OK;
+}
+
+static ncm_status new_model(int device, ncm_model** out) {
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return fail(NCM_ECUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
+    ncm_model* m = new ncm_model();
+    m->device = device;
+    e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) { delete m; return fail(NCM_ECUDA, std::string("stream: ") + cudaGetErrorString(e)); }
+    *out = m;
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_model_load(const char* path, int ctx_limit, int device, const int* shares, int nshards,
+                                    int shard, ncm_model** out) {
+    if (!path || !out) return fail(NCM_EINVAL, "null argument");
+    GgufFile g;
+    std::string err;
+    if (!g.open(path, err)) return fail(NCM_EIO, err);
+    ncm_model* m = nullptr;
+    ncm_status s = new_model(device, &m);
+    if (s) return s;
+    m->emb = g.emb; m->layers = g.layers; m->heads = g.heads; m->kv_heads = g.kv_heads; m->hd = g.head_dim;
+    m->ffn = g.ffn; m->vocab = g.vocab; m->rope_dim = g.rope_dim; m->eps = g.eps; m->base = g.rope_base;
+    m->ctx = (ctx_limit > 0 && ctx_limit < g.ctx) ? ctx_limit : g.ctx;
+    if (m->emb <= 0 || m->layers <= 0 || m->ctx <= 0) { free_model(m); return fail(NCM_EIO, "incomplete llama metadata"); }
+    if ((s = setup_buffers(m, shares, nshards, shard))) { free_model(m); return s; }
+    const int H = m->emb, QW = m->heads * m->hd, KW = m->kv_heads * m->hd, F = m->ffn;
+    const int hd = m->hd;
+#define TRY(x) do { if ((s = (x))) { free_model(m); return s; } } while (0)
+    TRY(upload_slice(m, g, "token_embd.weight", m->vocab, H, 0, m->vocab, 0, H, m->embd));
+    TRY(upload_f32(m, g, "output_norm.weight", H, &m->out_norm));
+    if (g.find("output.weight")) TRY(upload_slice(m, g, "output.weight", m->vocab, H, m->h0, m->hr, 0, H, m->head));
+    else TRY(build_tied_head(m));
+    m->L.resize(m->layers);
+    char nm[128];
+    for (int i = 0; i < m->layers; ++i) {
+        Layer& l = m->L[i];
+#define NM(s_) (snprintf(nm, sizeof nm, "blk.%d." s_ ".weight", i), nm)
+        TRY(upload_f32(m, g, NM("attn_norm"), H, &l.attn_norm));
+        TRY(upload_f32(m, g, NM("ffn_norm"), H, &l.ffn_norm));
+        TRY(upload_slice(m, g, NM("attn_q"), QW, H, m->q0 * hd, m->qh * hd, 0, H, l.wq));
+        TRY(upload_slice(m, g, NM("attn_k"), KW, H, m->k0 * hd, m->kh * hd, 0, H, l.wk));
+        TRY(upload_slice(m, g, NM("attn_v"), KW, H, m->k0 * hd, m->kh * hd, 0, H, l.wv));
+        TRY(upload_slice(m, g, NM("attn_output"), H, QW, 0, H, m->q0 * hd, m->qh * hd, l.wo));
+        TRY(upload_slice(m, g, NM("ffn_gate"), F, H, m->f0, m->fl, 0, H, l.w1));
+        TRY(upload_slice(m, g, NM("ffn_up"), F, H, m->f0, m->fl, 0, H, l.w3));
+        TRY(upload_slice(m, g, NM("ffn_down"), H, F, 0, H, m->f0, m->fl, l.w2));
+#undef NM
+    }
+    TRY(check_all_shapes(m));
+#undef TRY
+    *out = m;
+    return NCM_OK;
+}
+
+static ncm_status synth_mat(ncm_model* m, const ncm_synth_spec& sp, const char* name, int type, int full_cols,
+                            int r0, int nrows, int c0, int ncols, DevMat& out) {
+    out.type = type;
+    out.rows = nrows;
+    out.cols = ncols;
+    out.pitch = (row_bytes(type, ncols) + 15) / 16 * 16;
+    DALLOC(out.d, (size_t)out.pitch * nrows);
+    CKL(synth_launch(type, ncm_synth_key(sp.seed, name), r0, nrows, c0, ncols, full_cols, out.d, out.pitch, m->stream));
+    return NCM_OK;
+}
+static ncm_status ones(ncm_model* m, int n, float** out) {
+    std::vector<float> v(n, 1.0f);
+    DALLOC(*out, 4 * (size_t)n);
+    CK(cudaMemcpy(*out, v.data(), 4 * (size_t)n, cudaMemcpyHostToDevice));
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_model_create_synthetic(const ncm_synth_spec* spec, int ctx_limit, int device,
+                                                const int* shares, int nshards, int shard, ncm_model** out) {
+    if (!spec || !out) return fail(NCM_EINVAL, "null argument");
+    const ncm_synth_spec& sp = *spec;
+    ncm_model* m = nullptr;
+    ncm_status s = new_model(device, &m);
+    if (s) return s;
+    m->emb = sp.emb; m->layers = sp.layers; m->heads = sp.heads; m->kv_heads = sp.kv_heads; m->hd = sp.head_dim;
+    m->ffn = sp.ffn; m->vocab = sp.vocab; m->rope_dim = sp.head_dim; m->eps = sp.eps; m->base = sp.rope_base;
+    m->ctx = (ctx_limit > 0 && ctx_limit < sp.ctx) ? ctx_limit : sp.ctx;
+#define TRY(x) do { if ((s = (x))) { free_model(m); return s; } } while (0)
+    TRY(setup_buffers(m, shares, nshards, shard));
+    const int H = m->emb, QW = m->heads * m->hd, F = m->ffn, hd = m->hd;
+    TRY(synth_mat(m, sp, "token_embd.weight", sp.t_embd, H, 0, m->vocab, 0, H, m->embd));
+    TRY(ones(m, H, &m->out_norm));
+    if (!sp.tied) TRY(synth_mat(m, sp, "output.weight", sp.t_out, H, m->h0, m->hr, 0, H, m->head));
+    else {
+        if (cudaStreamSynchronize(m->stream) != cudaSuccess) { free_model(m); return fail(NCM_ECUDA, "synth"); }
+        TRY(build_tied_head(m));
+    }
+    m->L.resize(m->layers);
+    char nm[128];
+    for (int i = 0; i < m->layers; ++i) {
+        Layer& l = m->L[i];
+#define NM(s_) (snprintf(nm, sizeof nm, "blk.%d." s_ ".weight", i), nm)
+        TRY(ones(m, H, &l.attn_norm));
+        TRY(ones(m, H, &l.ffn_norm));
+        TRY(synth_mat(m, sp, NM("attn_q"), sp.t_attn, H, m->q0 * hd, m->qh * hd, 0, H, l.wq));
+        TRY(synth_mat(m, sp, NM("attn_k"), sp.t_attn, H, m->k0 * hd, m->kh * hd, 0, H, l.wk));
+        TRY(synth_mat(m, sp, NM("attn_v"), sp.t_attn, H, m->k0 * hd, m->kh * hd, 0, H, l.wv));
+        TRY(synth_mat(m, sp, NM("attn_output"), sp.t_attn, QW, 0, H, m->q0 * hd, m->qh * hd, l.wo));
+        TRY(synth_mat(m, sp, NM("ffn_gate"), sp.t_ffn, H, m->f0, m->fl, 0, H, l.w1));
+        TRY(synth_mat(m, sp, NM("ffn_up"), sp.t_ffn, H, m->f0, m->fl, 0, H, l.w3));
+        TRY(synth_mat(m, sp, NM("ffn_down"), sp.t_ffn, F, 0, H, m->f0, m->fl, l.w2));
+#undef NM
+    }
+    if (cudaStreamSynchronize(m->stream) != cudaSuccess) { free_model(m); return fail(NCM_ECUDA, "synthetic init"); }
+    TRY(check_all_shapes(m));
+#undef TRY
+    *out = m;
+    return NCM_OK;
+}
+
+extern "C" void ncm_model_free(ncm_model* m) { free_model(m); }
+
+extern "C" ncm_status ncm_model_info(const ncm_model* m, int* out) {
+    if (!m || !out) return fail(NCM_EINVAL, "null argument");
+    int v[12] = {m->emb, m->layers, m->heads, m->kv_heads, m->hd, m->ffn, m->vocab, m->ctx, m->qh, m->kh, m->fl, m->hr};
+    memcpy(out, v, sizeof v);
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_model_reset(ncm_model* m) {
+    if (!m) return fail(NCM_EINVAL, "null model");
+    CK(cudaSetDevice(m->device));
+    const size_t kvn = 4 * (size_t)m->layers * m->ctx * m->kh * m->hd;
+    CK(cudaMemsetAsync(m->kc, 0, kvn, m->stream));
+    CK(cudaMemsetAsync(m->vc, 0, kvn, m->stream));
+    // Position and prompt length only: the step counter stays monotonic because the
+    // peer flags compare against it.
+    CK(cudaMemsetAsync(m->state + ST_POS, 0, 4, m->stream));
+    CK(cudaMemsetAsync(m->state + ST_NPROMPT, 0, 4, m->stream));
+    CK(cudaStreamSynchronize(m->stream));
+    return NCM_OK;
+}
+
+// ------------------------------------------------------------------ the decode step
+static GemvParams base_params(ncm_model* m) {
+    GemvParams p;
+    memset(&p, 0, sizeof p);
+    p.eps = m->eps;
+    p.state = m->state;
+    p.rope = m->rope;
+    p.rope_half = m->rope_dim / 2;
+    p.head_dim = m->hd;
+    p.tokens = m->tokens;
+    p.ctx = m->ctx;
+    p.err = m->err;
+    p.tp.world = 1;
+    p.tp.timeout_ns = m->timeout_ns;
+    return p;
+}
+
+static int launch_gemv(ncm_model* m, const DevMat& w, int in_mode, int epi, GemvParams& p, bool dual,
+                       cudaStream_t s) {
+    p.pitch = w.pitch;
+    int grid;
+    size_t smem;
+    gemv_plan(w.type, w.cols, p.total_rows, dual, epi == EPI_QKV, 0, p, grid, smem);
+    return gemv_launch(w.type, in_mode, epi, p, grid, s, true);
+}
+
+// Row-parallel projection (wo / w2) with its reduction: one GPU -> hidden += out;
+// fused P2P -> NVLink stores + rank-ordered sum in the epilogue; NCCL -> partial,
+// ncclAllReduce, residual add.
+static ncm_status row_parallel(ncm_model* m, const DevMat& w, const float* x, int slot, cudaStream_t s) {
+    GemvParams p = base_params(m);
+    p.nseg = 1;
+    p.total_rows = m->emb;
+    p.x = x;
+    p.hidden = m->hidden;
+    if (m->world == 1) {
+        p.seg[0] = {w.d, nullptr, m->hidden, m->emb, 0, SEG_OUT};
+        CKL(launch_gemv(m, w, IN_F32, EPI_RESID, p, false, s));
+    } else if (m->reduce_mode == NCM_REDUCE_FUSED_P2P) {
+        p.seg[0] = {w.d, nullptr, nullptr, m->emb, 0, SEG_OUT};
+        p.tp = m->comm;
+        p.tp_slot = slot;
+        CKL(launch_gemv(m, w, IN_F32, EPI_TP_RESID, p, false, s));
+    } else {
+        p.seg[0] = {w.d, nullptr, m->part, m->emb, 0, SEG_OUT};
+        CKL(launch_gemv(m, w, IN_F32, EPI_PLAIN, p, false, s));
+        int r = g_nccl.AllReduce(m->part, m->part, (size_t)m->emb, kNcclFloat, kNcclSum, m->nccl, s);
+        if (r != 0) return fail(NCM_EPEER, "ncclAllReduce failed");
+        CKL(resid_add_launch(m->hidden, m->part, m->emb, s, true));
+    }
+    return NCM_OK;
+}
+
+static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
+    const int qw = m->qh * m->hd, kw = m->kh * m->hd;
+    CKL(embed_launch(m->embd.type, m->embd.d, m->embd.pitch, m->emb, m->tokens, m->state, m->hidden, s, true));
+    for (int l = 0; l < m->layers; ++l) {
+        const Layer& L = m->L[l];
+        // rms_norm -> quantize -> wq/wk/wv -> rope -> store_kv (inference.rs:4521-4646)
+        GemvParams p = base_params(m);
+        p.nseg = 3;
+        p.seg[0] = {L.wq.d, nullptr, m->q, qw, 0, SEG_Q};
+        p.seg[1] = {L.wk.d, nullptr, nullptr, kw, qw, SEG_K};
+        p.seg[2] = {L.wv.d, nullptr, nullptr, kw, qw + kw, SEG_V};
+        p.total_rows = qw + 2 * kw;
+        p.x = m->hidden;
+        p.norm_w = L.attn_norm;
+        p.kcache = m->kc + (size_t)l * m->ctx * kw;
+        p.vcache = m->vc + (size_t)l * m->ctx * kw;
+        p.kv_width = kw;
+        if (l == 0) p.ssq_tok = m->embd_ssq;
+        CKL(launch_gemv(m, L.wq, IN_F32_RMS, EPI_QKV, p, false, s));
+        // attention (inference.rs:4648-4665)
+        AttnParams a;
+        a.q = m->q;
+        a.kc = p.kcache;
+        a.vc = p.vcache;
+        a.out = m->att;
+        a.part = m->attn_part;
+        a.counter = m->attn_cnt;
+        a.state = m->state;
+        a.heads = m->qh;
+        a.kv_heads = m->kh;
+        a.hd = m->hd;
+        a.kvw = kw;
+        a.nsplit = m->nsplit;
+        a.max_per = m->max_per;
+        a.scale = 1.0f / sqrtf((float)m->hd);   // inference.rs:4653
+        CKL(attention_launch(a, s, true));
+        // quantize -> wo -> residual (inference.rs:4667-4673), reduce #1 (tp.rs:356-363)
+        ncm_status st = row_parallel(m, L.wo, m->att, 2 * l, s);
+        if (st) return st;
+        // rms_norm -> quantize -> w1, w3 -> silu*mul (inference.rs:4679-4730)
+        GemvParams f = base_params(m);
+        f.nseg = 1;
+        f.seg[0] = {L.w1.d, L.w3.d, m->act, m->fl, 0, SEG_OUT};
+        f.total_rows = m->fl;
+        f.x = m->hidden;
+        f.norm_w = L.ffn_norm;
+        CKL(launch_gemv(m, L.w1, IN_F32_RMS, EPI_SILU, f, true, s));
+        // quantize -> w2 -> residual (inference.rs:4732-4748), reduce #2 (tp.rs:416-424)
+        st = row_parallel(m, L.w2, m->act, 2 * l + 1, s);
+        if (st) return st;
+    }
+    if (!with_head) {
+        CKL(advance_launch(m->state, s, true));
+        return NCM_OK;
+    }
+    // output norm -> quantize -> head -> greedy argmax (inference.rs:4783-4845)
+    GemvParams h = base_params(m);
+    h.nseg = 1;
+    h.seg[0] = {m->head.d, nullptr, m->logits, m->hr, 0, SEG_OUT};
+    h.total_rows = m->hr;
+    h.x = m->hidden;
+    h.norm_w = m->out_norm;
+    h.amax_part = m->amax_part;
+    h.counter = m->amax_cnt;
+    h.head_row0 = m->h0;
+    if (m->world > 1 && m->reduce_mode == NCM_REDUCE_FUSED_P2P) h.tp = m->comm;
+    if (m->world > 1 && m->reduce_mode == NCM_REDUCE_NCCL) h.head_out = m->head_out;
+    CKL(launch_gemv(m, m->head, IN_F32_RMS, EPI_ARGMAX, h, false, s));
+    if (h.head_out) {
+        int r = g_nccl.AllGather(m->head_out, m->gather, 2, kNcclFloat, m->nccl, s);
+        if (r != 0) return fail(NCM_EPEER, "ncclAllGather failed");
+        CKL(argmax_merge_launch(m->gather, m->world, m->tokens, m->state, m->ctx, s, true));
+    }
+    return NCM_OK;
+}
+
+static ncm_status capture(ncm_model* m, bool with_head, cudaGraphExec_t* exec) {
+    cudaGraph_t graph;
+    CK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    ncm_status st = enqueue_step(m, with_head, m->stream);
+    cudaError_t e = cudaStreamEndCapture(m->stream, &graph);
+    if (st) {
+        if (e == cudaSuccess) cudaGraphDestroy(graph);
+        return st;
+    }
+    CK(e);
+    e = cudaGraphInstantiate(exec, graph, 0);
+    cudaGraphDestroy(graph);
+    CK(e);
+    return NCM_OK;
+}
+
+static ncm_status ensure_graphs(ncm_model* m) {
+    if (m->world > 1 && !m->tp_ready) return fail(NCM_EINVAL, "tensor-parallel peers not set up (ncm_tp_import / ncm_tp_nccl_init)");
+    if (!m->dirty && m->g_full) return NCM_OK;
+    if (m->g_full) { cudaGraphExecDestroy(m->g_full); m->g_full = nullptr; }
+    if (m->g_nohead) { cudaGraphExecDestroy(m->g_nohead); m->g_nohead = nullptr; }
+    ncm_status s = capture(m, true, &m->g_full);
+    if (s) return s;
+    s = capture(m, false, &m->g_nohead);
+    if (s) return s;
+    m->dirty = false;
+    return NCM_OK;
+}
+
+static ncm_status check_err(ncm_model* m) {
+    int e = 0;
+    CK(cudaMemcpy(&e, m->err, 4, cudaMemcpyDeviceToHost));
+    if (e) {
+        CK(cudaMemset(m->err, 0, 4));
+        if (e & NCM_DEVERR_PEER_TIMEOUT) return fail(NCM_ETIMEOUT, "a device-side wait on a peer GPU timed out");
+        return fail(NCM_ECUDA, "device error word " + std::to_string(e));
+    }
+    return NCM_OK;
+}
+
+static ncm_status set_pos(ncm_model* m, int pos, int nprompt, cudaStream_t s) {
+    m->h_stage[0] = pos;
+    m->h_stage[1] = nprompt;
+    CK(cudaMemcpyAsync(m->state + ST_POS, &m->h_stage[0], 4, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(m->state + ST_NPROMPT, &m->h_stage[1], 4, cudaMemcpyHostToDevice, s));
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_prefill_tokens(ncm_model* m, const int* prompt, int n_prompt, void* stream) {
+    if (!m || !prompt || n_prompt <= 0 || n_prompt > m->ctx) return fail(NCM_EINVAL, "bad prompt");
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= m->vocab) return fail(NCM_EINVAL, "token id out of range");
+    CK(cudaSetDevice(m->device));
+    ncm_status s = ensure_graphs(m);
+    if (s) return s;
+    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
+    CK(cudaStreamSynchronize(st));
+    CK(cudaMemcpyAsync(m->tokens, prompt, 4 * (size_t)n_prompt, cudaMemcpyHostToDevice, st));
+    if ((s = set_pos(m, 0, n_prompt, st))) return s;
+    for (int i = 0; i + 1 < n_prompt; ++i) CK(cudaGraphLaunch(m->g_nohead, st));
+    CK(cudaGraphLaunch(m->g_full, st));
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_decode_steps(ncm_model* m, int n, void* stream) {
+    if (!m || n < 0) return fail(NCM_EINVAL, "bad arguments");
+    CK(cudaSetDevice(m->device));
+    ncm_status s = ensure_graphs(m);
+    if (s) return s;
+    cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
+    for (int i = 0; i < n; ++i) CK(cudaGraphLaunch(m->g_full, st));
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_sync_tokens(ncm_model* m, int* tokens, int count, int* pos_out) {
+    if (!m) return fail(NCM_EINVAL, "null model");
+    CK(cudaSetDevice(m->device));
+    CK(cudaDeviceSynchronize());
+    ncm_status s = check_err(m);
+    if (s) return s;
+    if (tokens && count > 0) CK(cudaMemcpy(tokens, m->tokens, 4 * (size_t)(count < m->ctx ? count : m->ctx), cudaMemcpyDeviceToHost));
+    if (pos_out) CK(cudaMemcpy(pos_out, m->state + ST_POS, 4, cudaMemcpyDeviceToHost));
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_generate(ncm_model* m, const int* prompt, int n_prompt, int n_gen, int* out_tokens) {
+    if (!m || !out_tokens || n_gen < 0) return fail(NCM_EINVAL, "bad arguments");
+    if (n_prompt + n_gen > m->ctx) return fail(NCM_EINVAL, "prompt + generation exceeds the context");
+    ncm_status s = ncm_prefill_tokens(m, prompt, n_prompt, nullptr);
+    if (s) return s;
+    if (n_gen > 1 && (s = ncm_decode_steps(m, n_gen - 1, nullptr))) return s;
+    CK(cudaStreamSynchronize(m->stream));
+    if ((s = check_err(m))) return s;
+    if (n_gen > 0) CK(cudaMemcpy(out_tokens, m->tokens + n_prompt, 4 * (size_t)n_gen, cudaMemcpyDeviceToHost));
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_forward_pass(ncm_model* m, int token, int pos, float* logits, int* argmax) {
+    if (!m || pos < 0 || pos >= m->ctx || token < 0 || token >= m->vocab) return fail(NCM_EINVAL, "bad token or position");
+    CK(cudaSetDevice(m->device));
+    ncm_status s = ensure_graphs(m);
+    if (s) return s;
+    cudaStream_t st = m->stream;
+    m->h_stage[2] = token;
+    CK(cudaMemcpyAsync(m->tokens + pos, &m->h_stage[2], 4, cudaMemcpyHostToDevice, st));
+    if ((s = set_pos(m, pos, pos + 1, st))) return s;
+    CK(cudaGraphLaunch(m->g_full, st));
+    CK(cudaMemcpyAsync(&m->h_stage[3], m->state + ST_LAST_TOKEN, 4, cudaMemcpyDeviceToHost, st));
+    if (logits) CK(cudaMemcpyAsync(logits, m->logits, 4 * (size_t)m->hr, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if ((s = check_err(m))) return s;
+    if (argmax) *argmax = m->h_stage[3];
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_debug_read(ncm_model* m, int which, int layer, float* out, int64_t n) {
+    if (!m || !out || n < 0) return fail(NCM_EINVAL, "bad arguments");
+    CK(cudaSetDevice(m->device));
+    CK(cudaStreamSynchronize(m->stream));
+    const size_t kw = (size_t)m->kh * m->hd;
+    const float* src = nullptr;
+    size_t cap = 0;
+    switch (which) {
+        case 0: src = m->hidden; cap = m->emb; break;
+        case 1: src = m->q; cap = (size_t)m->qh * m->hd; break;
+        case 2: src = m->att; cap = (size_t)m->qh * m->hd; break;
+        case 3: src = m->act; cap = m->fl; break;
+        case 4: src = m->kc + (size_t)layer * m->ctx * kw; cap = (size_t)m->ctx * kw; break;
+        case 5: src = m->vc + (size_t)layer * m->ctx * kw; cap = (size_t)m->ctx * kw; break;
+        case 6: src = m->logits; cap = m->hr; break;
+        default: return fail(NCM_EINVAL, "unknown buffer");
+    }
+    if ((size_t)n > cap) return fail(NCM_EINVAL, "read past the buffer");
+    CK(cudaMemcpy(out, src, 4 * (size_t)n, cudaMemcpyDeviceToHost));
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_get_hidden(ncm_model* m, float* hidden) {
+    if (!m || !hidden) return fail(NCM_EINVAL, "null argument");
+    CK(cudaSetDevice(m->device));
+    CK(cudaStreamSynchronize(m->stream));
+    CK(cudaMemcpy(hidden, m->hidden, 4 * (size_t)m->emb, cudaMemcpyDeviceToHost));
+    return NCM_OK;
+}
+
+// ------------------------------------------------------------------ tensor parallel
+extern "C" ncm_status ncm_tp_export(ncm_model* m, uint8_t* handle_out) {
+    if (!m || !handle_out) return fail(NCM_EINVAL, "null argument");
+    if (m->world <= 1) return fail(NCM_EINVAL, "model is not sharded");
+    CK(cudaSetDevice(m->device));
+    cudaIpcMemHandle_t h;
+    CK(cudaIpcGetMemHandle(&h, m->comm_base));
+    memset(handle_out, 0, NCM_TP_HANDLE_BYTES);
+    memcpy(handle_out, &h, sizeof h);
+    uint64_t bytes = m->comm_bytes;
+    memcpy(handle_out + 128, &bytes, 8);
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_tp_import(ncm_model* m, const uint8_t* handles, int world, int rank) {
+    if (!m || !handles) return fail(NCM_EINVAL, "null argument");
+    if (world != m->world || rank != m->rank) return fail(NCM_EPEER, "world/rank do not match the shard plan");
+    CK(cudaSetDevice(m->device));
+    TpComm c{};
+    c.world = world;
+    c.rank = rank;
+    c.H = m->emb;
+    c.grid_max = num_sms();
+    c.timeout_ns = m->timeout_ns;
+    for (int d = 0; d < world; ++d) {
+        const uint8_t* hb = handles + (size_t)d * NCM_TP_HANDLE_BYTES;
+        uint64_t bytes;
+        memcpy(&bytes, hb + 128, 8);
+        if (bytes != m->comm_bytes) return fail(NCM_EPEER, "peer exchange area size differs (different model?)");
+        uint8_t* base;
+        if (d == rank) base = m->comm_base;
+        else {
+            cudaIpcMemHandle_t h;
+            memcpy(&h, hb, sizeof h);
+            void* p = nullptr;
+            cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess) return fail(NCM_EPEER, std::string("cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+            m->ipc_open.push_back(p);
+            base = (uint8_t*)p;
+        }
+        c.recv[d] = (float*)base;
+        c.flags[d] = (unsigned*)(base + m->off_flags);
+        c.hx[d] = (float2*)(base + m->off_hx);
+        c.hflags[d] = (unsigned*)(base + m->off_hflags);
+    }
+    m->comm = c;
+    m->tp_ready = true;
+    m->dirty = true;
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_nccl_unique_id(uint8_t* out) {
+    if (!out) return fail(NCM_EINVAL, "null argument");
+    if (!g_nccl.load()) return fail(NCM_EUNSUPPORTED, "libnccl.so.2 not found");
+    nccl_uid id;
+    if (g_nccl.GetUniqueId(&id) != 0) return fail(NCM_EPEER, "ncclGetUniqueId failed");
+    memcpy(out, &id, 128);
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_tp_nccl_init(ncm_model* m, const uint8_t* unique_id, int world, int rank) {
+    if (!m || !unique_id) return fail(NCM_EINVAL, "null argument");
+    if (world != m->world || rank != m->rank) return fail(NCM_EPEER, "world/rank do not match the shard plan");
+    if (!g_nccl.load()) return fail(NCM_EUNSUPPORTED, "libnccl.so.2 not found");
+    CK(cudaSetDevice(m->device));
+    nccl_uid id;
+    memcpy(&id, unique_id, 128);
+    if (g_nccl.CommInitRank(&m->nccl, world, id, rank) != 0) return fail(NCM_EPEER, "ncclCommInitRank failed");
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_tp_set_reducer(ncm_model* m, int mode) {
+    if (!m) return fail(NCM_EINVAL, "null model");
+    if (mode != NCM_REDUCE_FUSED_P2P && mode != NCM_REDUCE_NCCL) return fail(NCM_EINVAL, "unknown reducer");
+    if (mode == NCM_REDUCE_NCCL && m->world > 1 && !m->nccl) return fail(NCM_EINVAL, "NCCL communicator not initialised");
+    m->reduce_mode = mode;
+    m->dirty = true;
+    if (m->world > 1) m->tp_ready = (mode == NCM_REDUCE_NCCL) ? (m->nccl != nullptr) : (m->comm.world == m->world);
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_tp_set_timeout_ns(ncm_model* m, uint64_t ns) {
+    if (!m || ns == 0) return fail(NCM_EINVAL, "bad arguments");
+    m->timeout_ns = ns;
+    m->comm.timeout_ns = ns;
+    m->dirty = true;
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_test_peer_timeout(int device, uint64_t timeout_ns) {
+    CK(cudaSetDevice(device));
+    unsigned* flags = nullptr;
+    int* err = nullptr;
+    CK(cudaMalloc(&flags, 64));
+    CK(cudaMalloc(&err, 4));
+    CK(cudaMemset(flags, 0, 64));
+    CK(cudaMemset(err, 0, 4));
+    TpComm c{};
+    c.world = 2;
+    c.rank = 0;
+    c.flags[0] = flags;
+    c.flags[1] = flags + 8;
+    c.timeout_ns = timeout_ns;
+    int r = peer_timeout_test_launch(c, err, nullptr);
+    cudaError_t e = cudaDeviceSynchronize();
+    int h = 0;
+    cudaMemcpy(&h, err, 4, cudaMemcpyDeviceToHost);
+    cudaFree(flags);
+    cudaFree(err);
+    if (r != 0 || e != cudaSuccess) return fail(NCM_ECUDA, "peer timeout test launch failed");
+    if (h & NCM_DEVERR_PEER_TIMEOUT) return fail(NCM_ETIMEOUT, "peer wait timed out (expected)");
+    return NCM_OK;
+}
+
+// ------------------------------------------------------------------ kernel seams
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+extern "C" ncm_status ncm_quantize_f32_to_q8_0(const float* x, int n, int8_t* x_i8, float* x_scales, void* stream) {
+    if (n < 0 || n % 32) return fail(NCM_EINVAL, "n must be a multiple of 32");
+    if (n && (!x || !x_i8 || !x_scales)) return fail(NCM_EINVAL, "null pointer");
+    CKL(quantize_launch(x, n, x_i8, x_scales, (cudaStream_t)stream));
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_matmul_quantized(int qtype, const void* w, int64_t rows, int cols, const int8_t* x_i8,
+                                          const float* x_scales, float* out, void* stream) {
+    if (!gemv_type_ok(qtype)) return fail(NCM_EUNSUPPORTED, "quant type outside Q4_0/Q8_0/Q4_K");
+    if (rows < 0 || cols <= 0 || cols % 64 || cols % ncm_type_block_elems(qtype) || cols / 64 > 512)
+        return fail(NCM_EINVAL, "cols must be a positive multiple of 64 (256 for Q4_K), at most 32768");
+    if (rows == 0) return NCM_OK;
+    if (!w || !x_i8 || !x_scales || !out) return fail(NCM_EINVAL, "null pointer");
+    if (!aligned16(x_i8) || ((uintptr_t)w & 3)) return fail(NCM_EINVAL, "x_i8 must be 16-byte and w 4-byte aligned");
+    const int rb = row_bytes(qtype, cols);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (rb % 16 == 0 && aligned16(w) && rows < (1ll << 31)) {
+        GemvParams p;
+        memset(&p, 0, sizeof p);
+        p.nseg = 1;
+        p.seg[0] = {(const uint8_t*)w, nullptr, out, (int)rows, 0, SEG_OUT};
+        p.total_rows = (int)rows;
+        p.pitch = rb;
+        p.xq = x_i8;
+        p.xs = x_scales;
+        p.tp.world = 1;
+        int grid;
+        size_t smem;
+        gemv_plan(qtype, cols, (int)rows, false, false, 0, p, grid, smem);
+        CKL(gemv_launch(qtype, IN_Q8, EPI_PLAIN, p, grid, s, false));
+    } else {
+        CKL(gemv_batch_launch(qtype, (const uint8_t*)w, rows, cols, rb, 1, x_i8, x_scales, out, s));
+    }
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_matmul_quantized_batch(int qtype, const void* w, int64_t rows, int cols, int ntok,
+                                                const int8_t* x_i8, const float* x_scales, float* out, void* stream) {
+    if (!gemv_type_ok(qtype)) return fail(NCM_EUNSUPPORTED, "quant type outside Q4_0/Q8_0/Q4_K");
+    if (ntok < 1 || ntok > 8) return fail(NCM_EINVAL, "1 <= ntok <= 8");
+    if (rows < 0 || cols <= 0 || cols % 64 || cols % ncm_type_block_elems(qtype))
+        return fail(NCM_EINVAL, "cols must be a positive multiple of 64 (256 for Q4_K)");
+    if (rows == 0) return NCM_OK;
+    if (!w || !x_i8 || !x_scales || !out) return fail(NCM_EINVAL, "null pointer");
+    if (((uintptr_t)x_i8 & 3) || ((uintptr_t)w & 3)) return fail(NCM_EINVAL, "w and x_i8 must be 4-byte aligned");
+    CKL(gemv_batch_launch(qtype, (const uint8_t*)w, rows, cols, row_bytes(qtype, cols), ntok, x_i8, x_scales, out,
+                          (cudaStream_t)stream));
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_block_dots(int qtype, const void* w, int64_t rows, int cols, const int8_t* x_i8,
+                                    int32_t* out, void* stream) {
+    if (!gemv_type_ok(qtype)) return fail(NCM_EUNSUPPORTED, "quant type outside Q4_0/Q8_0/Q4_K");
+    if (rows < 0 || cols <= 0 || cols % 64 || cols % ncm_type_block_elems(qtype)) return fail(NCM_EINVAL, "bad shape");
+    if (rows == 0) return NCM_OK;
+    if (!w || !x_i8 || !out) return fail(NCM_EINVAL, "null pointer");
+    if (((uintptr_t)x_i8 & 3) || ((uintptr_t)w & 3)) return fail(NCM_EINVAL, "w and x_i8 must be 4-byte aligned");
+    CKL(block_dots_launch(qtype, (const uint8_t*)w, rows, cols, x_i8, out, (cudaStream_t)stream));
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_rms_norm(float* out, const float* x, const float* weight, int n, float eps, void* stream) {
+    if (!out || !x || !weight || n <= 0 || n > 65536) return fail(NCM_EINVAL, "bad arguments");
+    CKL(rms_norm_launch(out, x, weight, n, eps, (cudaStream_t)stream));
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_fused_silu_mul(float* out, const float* gate, const float* up, int n, void* stream) {
+    if (n < 0 || (n && (!out || !gate || !up))) return fail(NCM_EINVAL, "bad arguments");
+    CKL(silu_mul_launch(out, gate, up, n, (cudaStream_t)stream));
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_attention(float* out, const float* q, const float* k_cache, const float* v_cache, int pos,
+                                   int heads, int kv_heads, int head_dim, void* stream) {
+    if (!out || !q || !k_cache || !v_cache || pos < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads ||
+        heads / kv_heads > 8 || head_dim % 32 || head_dim > 256)
+        return fail(NCM_EINVAL, "bad attention arguments");
+    cudaStream_t s = (cudaStream_t)stream;
+    // Scratch for this one call: position word, split partials and counters.
+    const int nsplit = 4;
+    const int max_per = (pos + 1 + nsplit - 1) / nsplit;
+    int* state = nullptr;
+    float* part = nullptr;
+    unsigned* cnt = nullptr;
+    CK(cudaMallocAsync((void**)&state, 4 * ST_COUNT, s));
+    CK(cudaMallocAsync((void**)&part, 4 * (size_t)heads * nsplit * (head_dim + 2), s));
+    CK(cudaMallocAsync((void**)&cnt, 4 * (size_t)kv_heads, s));
+    int st[ST_COUNT] = {pos, 0, 0, 0, 0, 0, 0, 0};
+    CK(cudaMemcpyAsync(state, st, sizeof st, cudaMemcpyHostToDevice, s));
+    CK(cudaMemsetAsync(cnt, 0, 4 * (size_t)kv_heads, s));
+    AttnParams a;
+    a.q = q; a.kc = k_cache; a.vc = v_cache; a.out = out; a.part = part; a.counter = cnt; a.state = state;
+    a.heads = heads; a.kv_heads = kv_heads; a.hd = head_dim; a.kvw = kv_heads * head_dim; a.nsplit = nsplit;
+    a.max_per = max_per < 1 ? 1 : max_per;
+    a.scale = 1.0f / sqrtf((float)head_dim);
+    int r = attention_launch(a, s, false);
+    cudaFreeAsync(state, s);
+    cudaFreeAsync(part, s);
+    cudaFreeAsync(cnt, s);
+    CK(cudaStreamSynchronize(s));
+    if (r) return fail(NCM_ECUDA, "attention launch failed");
+    return NCM_OK;
+}

@@ -1,0 +1,122 @@
+// Internal structures shared by kernels.cu (device code + launchers) and engine.cu
+// (model, decode graph, tensor parallel plumbing).  Not part of the C ABI.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ncm {
+
+constexpr int kThreads = 256;   // GEMV CTA size (8 warps)
+constexpr int kMaxSeg = 3;      // weight matrices fused into one GEMV launch (wq, wk, wv)
+constexpr int kMaxWorld = 8;    // GPUs of one NVSwitch box
+
+// Input modes of the GEMV prologue.
+enum InMode { IN_F32 = 0, IN_F32_RMS = 1, IN_Q8 = 2 };
+// Epilogue modes.
+enum EpiMode {
+    EPI_PLAIN = 0,   // out[row] = sum
+    EPI_RESID = 1,   // hidden[row] += sum              (wo / w2, one GPU)
+    EPI_QKV = 2,     // RoPE on q,k; k,v into the KV cache at pos
+    EPI_SILU = 3,    // dual matrices: out[row] = silu(g) * u  (w1 / w3)
+    EPI_ARGMAX = 4,  // logits + greedy argmax, token appended, position advanced
+    EPI_TP_RESID = 5 // partial rows stored into every peer, rank-ordered sum + residual
+};
+// Per-segment epilogue kinds inside EPI_QKV.
+enum SegKind { SEG_Q = 0, SEG_K = 1, SEG_V = 2, SEG_OUT = 3 };
+
+// Device decode state (one int array per model).
+enum StateIdx { ST_POS = 0, ST_STEP = 1, ST_NPROMPT = 2, ST_LAST_TOKEN = 3, ST_COUNT = 8 };
+
+struct Seg {
+    const uint8_t* w;   // raw blocks, rows x pitch bytes
+    const uint8_t* w2;  // EPI_SILU: the up matrix (same shape)
+    float* out;         // destination of this segment's rows
+    int rows;
+    int row_begin;      // first row of the segment in the fused row space
+    int kind;           // SegKind
+};
+
+// Peer-memory view of the tensor-parallel exchange buffers (identical layout on all ranks).
+struct TpComm {
+    int world, rank;
+    float* recv[kMaxWorld];       // recv[dst] -> rank dst's receive area (this rank's pointer to it)
+    unsigned* flags[kMaxWorld];   // flags[dst] -> rank dst's flag area
+    float2* hx[kMaxWorld];        // head argmax exchange slots (val, idx-as-float-bits) per rank
+    unsigned* hflags[kMaxWorld];
+    int H;                        // hidden size (rows of the reduced vectors)
+    int grid_max;                 // CTA slots per reduction slot
+    uint64_t timeout_ns;
+};
+
+struct GemvParams {
+    Seg seg[kMaxSeg];
+    int nseg;
+    int total_rows;
+    int cols, pitch, units;       // units = cols / 64
+    int pp, groups, nparts;       // threads per row-group (pow2), row groups, partial sums per row
+    int tile_rows;                // rows per pipeline stage
+    int stage_bytes, nstages;
+    int part_off, stage_off;      // shared-memory offsets
+    // input
+    const float* x;               // IN_F32 / IN_F32_RMS, per token stride = cols
+    const float* norm_w;
+    float eps;
+    const float* ssq_tok;         // layer 0: sequential sum of squares per vocab row (or null)
+    const int8_t* xq;             // IN_Q8
+    const float* xs;
+    // epilogue context
+    float* hidden;                // EPI_RESID / EPI_TP_RESID target
+    int* state;                   // StateIdx array
+    const float2* rope;           // [ctx][rope_half] (sin, cos)
+    int rope_half, head_dim;
+    float* kcache; float* vcache; // this layer's [ctx][kv_width] caches
+    int kv_width;
+    int* tokens;                  // token history [ctx]
+    float2* amax_part;            // [grid] (val, idx bits)
+    unsigned* counter;
+    int head_row0;                // global vocab row of this shard's first head row
+    float2* head_out;             // NCCL baseline: local (logit, token) only, no state update
+    int ctx;
+    TpComm tp;
+    int tp_slot;                  // layer*2 + phase
+    int* err;
+};
+
+struct AttnParams {
+    const float* q;          // [heads_local * hd] roped
+    const float* kc;         // layer cache [ctx][kvw]
+    const float* vc;
+    float* out;              // [heads_local * hd]
+    float* part;             // [heads_local][nsplit][hd + 2]
+    unsigned* counter;       // [kv_heads_local]
+    const int* state;
+    int heads, kv_heads, hd, kvw, nsplit, max_per;
+    float scale;
+};
+
+// Launchers (kernels.cu).
+int gemv_launch(int qtype, int in_mode, int epi, GemvParams p, int grid, cudaStream_t s, bool pdl);
+void gemv_plan(int qtype, int cols, int rows_hint, bool dual, bool need_even, int world_grid, GemvParams& p, int& grid,
+               size_t& smem);
+int embed_ssq_launch(int type, const uint8_t* table, int64_t pitch, int emb, int vocab, float* out, cudaStream_t s);
+int attention_launch(const AttnParams& a, cudaStream_t s, bool pdl);
+int embed_launch(int type, const uint8_t* table, int64_t pitch, int emb, const int* tokens, const int* state,
+                 float* hidden, cudaStream_t s, bool pdl);
+int resid_add_launch(float* hidden, const float* part, int n, cudaStream_t s, bool pdl);
+int argmax_merge_launch(const float2* gathered, int world, int* tokens, int* state, int ctx, cudaStream_t s, bool pdl);
+int advance_launch(int* state, cudaStream_t s, bool pdl);
+int quantize_launch(const float* x, int n, int8_t* xq, float* xs, cudaStream_t s);
+int block_dots_launch(int qtype, const uint8_t* w, int64_t rows, int cols, const int8_t* xq, int32_t* out,
+                      cudaStream_t s);
+int gemv_batch_launch(int qtype, const uint8_t* w, int64_t rows, int cols, int pitch, int ntok, const int8_t* xq,
+                      const float* xs, float* out, cudaStream_t s);
+int rms_norm_launch(float* out, const float* x, const float* w, int n, float eps, cudaStream_t s);
+int silu_mul_launch(float* out, const float* g, const float* u, int n, cudaStream_t s);
+int synth_launch(int type, uint64_t key, int64_t r0, int64_t nrows, int64_t c0, int64_t ncols, int64_t full_cols,
+                 uint8_t* out, int64_t pitch, cudaStream_t s);
+int requant_q4_0_launch(int src_type, const uint8_t* src, int64_t rows, int cols, int64_t src_pitch, uint8_t* dst,
+                        int64_t dst_pitch, cudaStream_t s);
+int peer_timeout_test_launch(TpComm c, int* err, cudaStream_t s);
+int num_sms();
+
+}  // namespace ncm

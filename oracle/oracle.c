@@ -1,0 +1,971 @@
+/*
+ * CPU ORACLE -- TEST INFRASTRUCTURE ONLY.
+ *
+ * A plain-C restatement of NanoCamelid's x86 portable (scalar) decode path.  It is
+ * the checker the GPU product is compared against and the timed CPU baseline; it
+ * is never linked into, called by, or shipped with the product library.  Only
+ * tests/, __graft_entry__.smoke() and bench.py's CPU arms load it.
+ *
+ * The reference is Rust and cannot be built here (no cargo/rustc, no network), so
+ * this file restates the algorithm function by function.  Every function names
+ * the reference file:line it follows.  Numerics mirrored exactly:
+ *   - f32 arithmetic in the reference's operation order, no FMA contraction
+ *     (built with -ffp-contract=off), sequential left-to-right sums;
+ *   - Rust f32::round == C roundf (half away from zero); `as i8`/`as i32`
+ *     saturate and map NaN to 0 (sat_i32 below);
+ *   - transcendentals (powf, sinf, cosf, expf, sqrtf) from the same glibc libm
+ *     that Rust's std calls on Linux.
+ * Parity pins: tests/test_oracle_kat.py checks this file against every known-answer
+ * test the reference's q8.rs / inference.rs hold for the path.
+ */
+#define _GNU_SOURCE
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#define QK 32
+#define QKK 256
+enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12 };
+
+/* ------------------------------------------------------------------ f16 */
+/* q8.rs:3599-3622 f16_bits_to_f32 (exact, subnormals normalised). */
+static float bits_f32(uint32_t b) { float f; memcpy(&f, &b, 4); return f; }
+static uint32_t f32_bits(float f) { uint32_t b; memcpy(&b, &f, 4); return b; }
+
+float orc_f16_to_f32(uint16_t bits) {
+    uint32_t sign = (uint32_t)(bits & 0x8000) << 16;
+    uint32_t exponent = (bits >> 10) & 0x1f;
+    uint32_t fraction = bits & 0x03ff;
+    if (exponent == 0) {
+        if (fraction == 0) return bits_f32(sign);
+        int32_t e = -14;
+        uint32_t m = fraction;
+        while ((m & 0x0400) == 0) { m <<= 1; e -= 1; }
+        m &= 0x03ff;
+        return bits_f32(sign | ((uint32_t)(e + 127) << 23) | (m << 13));
+    }
+    if (exponent == 0x1f) return bits_f32(sign | 0x7f800000u | (fraction << 13));
+    return bits_f32(sign | ((exponent + 112) << 23) | (fraction << 13));
+}
+
+/* q8.rs:3644-3673 fast_f32_to_f16: TRUNCATES the mantissa, flushes f32 denormals. */
+uint16_t orc_f32_to_f16(float value) {
+    uint32_t bits = f32_bits(value);
+    uint16_t sign = (uint16_t)((bits >> 16) & 0x8000);
+    int32_t exponent = (int32_t)((bits >> 23) & 0xff);
+    uint32_t fraction = bits & 0x007fffff;
+    if (exponent == 0) return sign;
+    if (exponent == 0xff) {
+        if (fraction == 0) return sign | 0x7c00;
+        return (uint16_t)(sign | 0x7c00 | (fraction >> 13) | 1);
+    }
+    int32_t he = exponent - 127 + 15;
+    if (he >= 0x1f) return sign | 0x7c00;
+    if (he <= 0) {
+        if (he < -10) return sign;
+        uint32_t mant = (fraction | 0x00800000u) >> (14 - he);
+        return (uint16_t)(sign | mant);
+    }
+    return (uint16_t)(sign | ((uint16_t)he << 10) | (fraction >> 13));
+}
+
+/* Rust `f as i32`: saturating, NaN -> 0. */
+static int32_t sat_i32(float f) {
+    if (f != f) return 0;
+    if (f >= 2147483647.0f) return 2147483647;
+    if (f <= -2147483648.0f) return (-2147483647 - 1);
+    return (int32_t)f;
+}
+static float rd16(const uint8_t* p) { return orc_f16_to_f32((uint16_t)(p[0] | (p[1] << 8))); }
+
+/* ------------------------------------------------------------------ block formats */
+size_t orc_block_bytes(int t) { return t == T_Q4_0 ? 18 : t == T_Q8_0 ? 34 : t == T_Q4_K ? 144 : t == T_F32 ? 4 : t == T_F16 ? 2 : 0; }
+size_t orc_block_elems(int t) { return t == T_Q4_K ? QKK : (t == T_Q4_0 || t == T_Q8_0) ? QK : 1; }
+
+/* q8.rs:539-546 Q4_0Block::unpack_values: low nibble -> j, high nibble -> j+16, minus 8. */
+void orc_q4_0_unpack(const uint8_t* blk, int8_t out[32]) {
+    for (int j = 0; j < 16; ++j) {
+        out[j] = (int8_t)((blk[2 + j] & 0x0f) - 8);
+        out[j + 16] = (int8_t)((blk[2 + j] >> 4) - 8);
+    }
+}
+
+/* q8.rs:3376-3382 dot_i8_scalar. */
+int32_t orc_dot_i8(const int8_t* a, const int8_t* b, int n) {
+    int32_t s = 0;
+    for (int i = 0; i < n; ++i) s += (int32_t)a[i] * (int32_t)b[i];
+    return s;
+}
+
+/* q8.rs:2699-2702 dot_q4_0_q8_0_scalar / Q8_0Block::dot_i32 (q8.rs:505). */
+int32_t orc_block_dot(int t, const uint8_t* blk, const int8_t* x) {
+    if (t == T_Q4_0) { int8_t w[32]; orc_q4_0_unpack(blk, w); return orc_dot_i8(w, x, 32); }
+    return orc_dot_i8((const int8_t*)(blk + 2), x, 32);
+}
+
+/* q8.rs:2009-2018 q4_k_scale_min. */
+void orc_q4_k_scale_min(int idx, const uint8_t* sc, uint8_t* s, uint8_t* m) {
+    if (idx < 4) { *s = sc[idx] & 63; *m = sc[idx + 4] & 63; }
+    else {
+        *s = (uint8_t)((sc[idx + 4] & 0x0f) | ((sc[idx - 4] >> 6) << 4));
+        *m = (uint8_t)((sc[idx + 4] >> 4) | ((sc[idx] >> 6) << 4));
+    }
+}
+
+/* Integer half of q8.rs:1338-1376 dot_q8_scaled_preloaded: per 32-sub-block
+ * weighted sum Σ q·x (q in 0..15) and activation sum Σ x, sub-block order 0..7. */
+void orc_q4_k_int_sums(const uint8_t* blk, const int8_t* x, int32_t wsum[8], int32_t asum[8]) {
+    const uint8_t* v = blk + 16;
+    for (int p = 0; p < 4; ++p) {
+        int32_t lw = 0, la = 0, hw = 0, ha = 0;
+        for (int l = 0; l < 32; ++l) {
+            uint8_t byte = v[p * 32 + l];
+            int32_t lx = x[p * 64 + l], hx = x[p * 64 + 32 + l];
+            lw += (int32_t)(byte & 0x0f) * lx; la += lx;
+            hw += (int32_t)(byte >> 4) * hx; ha += hx;
+        }
+        wsum[2 * p] = lw; asum[2 * p] = la; wsum[2 * p + 1] = hw; asum[2 * p + 1] = ha;
+    }
+}
+
+/* q8.rs:1249-1269 unpack + q8.rs:1338-1376 dot_q8_scaled_preloaded (f32 combine). */
+float orc_q4_k_dot(const uint8_t* blk, const int8_t* x, const float* xs) {
+    float d = rd16(blk), dmin = rd16(blk + 2);
+    float scales[8], mins[8];
+    for (int p = 0; p < 4; ++p) {
+        uint8_t ls, lm, hs, hm;
+        orc_q4_k_scale_min(2 * p, blk + 4, &ls, &lm);
+        orc_q4_k_scale_min(2 * p + 1, blk + 4, &hs, &hm);
+        scales[2 * p] = d * (float)ls; scales[2 * p + 1] = d * (float)hs;
+        mins[2 * p] = dmin * (float)lm; mins[2 * p + 1] = dmin * (float)hm;
+    }
+    int32_t ws[8], as[8];
+    orc_q4_k_int_sums(blk, x, ws, as);
+    float sum = 0.0f;
+    for (int j = 0; j < 8; ++j) sum += xs[j] * (scales[j] * (float)ws[j] - mins[j] * (float)as[j]);
+    return sum;
+}
+
+/* q8.rs:1240-1269 Q4KBlock::dequantize. */
+void orc_q4_k_dequant(const uint8_t* blk, float out[256]) {
+    float d = rd16(blk), dmin = rd16(blk + 2);
+    for (int p = 0; p < 4; ++p) {
+        uint8_t ls, lm, hs, hm;
+        orc_q4_k_scale_min(2 * p, blk + 4, &ls, &lm);
+        orc_q4_k_scale_min(2 * p + 1, blk + 4, &hs, &hm);
+        float lsc = d * (float)ls, hsc = d * (float)hs, lmn = dmin * (float)lm, hmn = dmin * (float)hm;
+        for (int l = 0; l < 32; ++l) {
+            uint8_t byte = blk[16 + p * 32 + l];
+            out[p * 64 + l] = lsc * (float)(byte & 0x0f) - lmn;
+            out[p * 64 + 32 + l] = hsc * (float)(byte >> 4) - hmn;
+        }
+    }
+}
+
+/* model.rs:1109-1132 load_f32_or_f16 for Q8_0 / Q4_0 / Q4_K / F32 / F16 rows. */
+void orc_dequant_row(int t, const uint8_t* row, int cols, float* out) {
+    if (t == T_F32) { memcpy(out, row, (size_t)cols * 4); return; }
+    if (t == T_F16) { for (int i = 0; i < cols; ++i) out[i] = rd16(row + 2 * i); return; }
+    if (t == T_Q4_K) { for (int b = 0; b < cols / QKK; ++b) orc_q4_k_dequant(row + (size_t)b * 144, out + b * QKK); return; }
+    int nb = cols / QK;
+    for (int b = 0; b < nb; ++b) {
+        const uint8_t* blk = row + (size_t)b * orc_block_bytes(t);
+        float scale = rd16(blk);
+        if (t == T_Q4_0) {
+            int8_t v[32]; orc_q4_0_unpack(blk, v);
+            for (int i = 0; i < 32; ++i) out[b * 32 + i] = (float)v[i] * scale;
+        } else {
+            const int8_t* v = (const int8_t*)(blk + 2);
+            for (int i = 0; i < 32; ++i) out[b * 32 + i] = (float)v[i] * scale;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------ quantizers */
+/* inference.rs:991-1029 quantize_f32_to_q8_0_scalar (x86 path). Scale stored as f32. */
+void orc_quantize_q8_0(const float* x, int n, int8_t* xq, float* xs) {
+    for (int b = 0; b < n / 32; ++b) {
+        const float* c = x + b * 32;
+        float max_abs = 0.0f;
+        for (int i = 0; i < 32; ++i) { float a = fabsf(c[i]); if (a > max_abs) max_abs = a; }
+        float scale = max_abs / 127.0f;
+        xs[b] = scale;
+        if (scale > 0.0f) {
+            float inv = 1.0f / scale;
+            for (int i = 0; i < 32; ++i) {
+                float q = roundf(c[i] * inv);
+                if (q < -127.0f) q = -127.0f;
+                if (q > 127.0f) q = 127.0f;
+                xq[b * 32 + i] = (int8_t)q;
+            }
+        } else {
+            memset(xq + b * 32, 0, 32);
+        }
+    }
+}
+
+/* q8.rs:2389-2440 quantize_f32_matrix_to_q8_0_blocks (f16-truncated scale). */
+void orc_quantize_matrix_q8_0(const float* v, long rows, int cols, uint8_t* out) {
+    int nb = cols / 32;
+    #pragma omp parallel for schedule(static) if (rows >= 128)
+    for (long r = 0; r < rows; ++r) {
+        for (int b = 0; b < nb; ++b) {
+            const float* c = v + r * cols + b * 32;
+            uint8_t* o = out + ((size_t)r * nb + b) * 34;
+            float max_abs = 0.0f;
+            for (int i = 0; i < 32; ++i) { float a = fabsf(c[i]); if (a > max_abs) max_abs = a; }
+            float scale = max_abs / 127.0f;
+            int8_t q[32]; memset(q, 0, 32);
+            if (scale > 0.0f) {
+                float inv = 1.0f / scale;
+                for (int i = 0; i < 32; ++i) {
+                    float t = roundf(c[i] * inv);
+                    if (t < -127.0f) t = -127.0f;
+                    if (t > 127.0f) t = 127.0f;
+                    q[i] = (int8_t)t;
+                }
+            }
+            uint16_t sb = orc_f32_to_f16(scale);
+            o[0] = sb & 0xff; o[1] = sb >> 8; memcpy(o + 2, q, 32);
+        }
+    }
+}
+
+/* q8.rs:2442-2488 quantize_f32_matrix_to_q4_0_blocks: d = signed-max/-8, q = trunc(x*id + 8.5). */
+void orc_quantize_block_q4_0(const float* c, uint8_t* o) {
+    float amax = 0.0f, mx = 0.0f;
+    for (int i = 0; i < 32; ++i) { float a = fabsf(c[i]); if (a > amax) { amax = a; mx = c[i]; } }
+    float d = mx / -8.0f;
+    float id = d != 0.0f ? 1.0f / d : 0.0f;
+    for (int j = 0; j < 16; ++j) {
+        float x0 = c[j] * id + 8.5f;
+        float x1 = c[j + 16] * id + 8.5f;
+        int32_t q0 = sat_i32(x0), q1 = sat_i32(x1);
+        q0 = q0 < 0 ? 0 : q0 > 15 ? 15 : q0;
+        q1 = q1 < 0 ? 0 : q1 > 15 ? 15 : q1;
+        o[2 + j] = (uint8_t)(q0 | (q1 << 4));
+    }
+    uint16_t sb = orc_f32_to_f16(d);
+    o[0] = sb & 0xff; o[1] = sb >> 8;
+}
+void orc_quantize_matrix_q4_0(const float* v, long rows, int cols, uint8_t* out) {
+    int nb = cols / 32;
+    #pragma omp parallel for schedule(static) if (rows >= 128)
+    for (long r = 0; r < rows; ++r)
+        for (int b = 0; b < nb; ++b) orc_quantize_block_q4_0(v + r * cols + b * 32, out + ((size_t)r * nb + b) * 18);
+}
+
+/* ------------------------------------------------------------------ GEMV */
+/* One output row, reference order.  Q4_0 / Q8_0: inference.rs:1146-1199 (matmul_q8_0),
+ * 2641-2667 (matmul_q4_0), 2886-2935 (1x4 swizzled chunk; same per-row formula):
+ *   sum += w_scale * x_scale * (float)dot   sequentially in block order.
+ * Q4_K: inference.rs:3089-3135: sum += dot_q8_scaled_preloaded(block) per super-block. */
+static float row_dot(int t, const uint8_t* row, int cols, const int8_t* xq, const float* xs) {
+    float sum = 0.0f;
+    if (t == T_Q4_K) {
+        for (int b = 0; b < cols / QKK; ++b) sum += orc_q4_k_dot(row + (size_t)b * 144, xq + b * QKK, xs + b * 8);
+        return sum;
+    }
+    size_t bb = orc_block_bytes(t);
+    for (int b = 0; b < cols / QK; ++b) {
+        const uint8_t* blk = row + b * bb;
+        int32_t d = orc_block_dot(t, blk, xq + b * 32);
+        sum += rd16(blk) * xs[b] * (float)d;
+    }
+    return sum;
+}
+
+size_t orc_row_bytes(int t, int cols) { return (size_t)cols / orc_block_elems(t) * orc_block_bytes(t); }
+
+/* inference.rs:1201-1244 matmul_quantized: out fully overwritten; rows in parallel
+ * (inference.rs:34-50: rayon only when rows >= 128; per-row order unchanged). */
+void orc_matmul_quantized(int t, const uint8_t* w, long rows, int cols, const int8_t* xq, const float* xs, float* out) {
+    size_t rb = orc_row_bytes(t, cols);
+    #pragma omp parallel for schedule(static) if (rows >= 128)
+    for (long r = 0; r < rows; ++r) out[r] = row_dot(t, w + r * rb, cols, xq, xs);
+}
+
+/* inference.rs:1246-1303,1343-1418,2006-2132 matmul_quantized_batch: out[token][row];
+ * each token's row uses the single-token formula. */
+void orc_matmul_quantized_batch(int t, const uint8_t* w, long rows, int cols, int ntok, const int8_t* xq, const float* xs, float* out) {
+    size_t rb = orc_row_bytes(t, cols);
+    int nbs = cols / 32;
+    #pragma omp parallel for schedule(static) if (rows >= 128)
+    for (long r = 0; r < rows; ++r)
+        for (int k = 0; k < ntok; ++k) out[(size_t)k * rows + r] = row_dot(t, w + r * rb, cols, xq + (size_t)k * cols, xs + (size_t)k * nbs);
+}
+
+/* Per-block integer dot dump (the bit-exact gate): Q4_0/Q8_0 -> rows x (cols/32) i32;
+ * Q4_K -> rows x (cols/32) x {wsum, asum}. */
+void orc_block_dots(int t, const uint8_t* w, long rows, int cols, const int8_t* xq, int32_t* out) {
+    size_t rb = orc_row_bytes(t, cols);
+    int nb = cols / 32;
+    for (long r = 0; r < rows; ++r) {
+        const uint8_t* row = w + r * rb;
+        if (t == T_Q4_K) {
+            for (int s = 0; s < cols / QKK; ++s) {
+                int32_t ws[8], as[8];
+                orc_q4_k_int_sums(row + (size_t)s * 144, xq + s * QKK, ws, as);
+                for (int j = 0; j < 8; ++j) {
+                    out[((size_t)r * nb + s * 8 + j) * 2] = ws[j];
+                    out[((size_t)r * nb + s * 8 + j) * 2 + 1] = as[j];
+                }
+            }
+        } else {
+            for (int b = 0; b < nb; ++b) out[(size_t)r * nb + b] = orc_block_dot(t, row + b * orc_block_bytes(t), xq + b * 32);
+        }
+    }
+}
+
+/* ------------------------------------------------------------------ elementwise */
+/* inference.rs:697-706 rms_norm. */
+void orc_rms_norm(float* out, const float* x, const float* w, int n, float eps) {
+    float sum = 0.0f;
+    for (int i = 0; i < n; ++i) sum += x[i] * x[i];
+    float scale = 1.0f / sqrtf(sum / (float)n + eps);
+    for (int i = 0; i < n; ++i) out[i] = x[i] * scale * w[i];
+}
+
+/* inference.rs:860-900 cached_rope_angles (no rope-scaling keys): (sin, cos) per pair. */
+void orc_rope_angles(int pos, int rope_dim, float base, float* sin_out, float* cos_out) {
+    for (int i = 0; i < rope_dim / 2; ++i) {
+        float theta = powf(base, -((float)(i * 2)) / (float)rope_dim);
+        float angle = (float)pos * theta;
+        sin_out[i] = sinf(angle);
+        cos_out[i] = cosf(angle);
+    }
+}
+
+/* inference.rs:904-933 apply_rope_cached, NORM style (interleaved pairs 2i, 2i+1). */
+void orc_apply_rope(float* data, int pos, int heads, int hd, int rope_dim, float base) {
+    float s[512], c[512];
+    orc_rope_angles(pos, rope_dim, base, s, c);
+    for (int h = 0; h < heads; ++h)
+        for (int i = 0; i < rope_dim / 2; ++i) {
+            float* d = data + h * hd + 2 * i;
+            float x0 = d[0], x1 = d[1];
+            d[0] = x0 * c[i] - x1 * s[i];
+            d[1] = x0 * s[i] + x1 * c[i];
+        }
+}
+
+/* inference.rs:3367-3390 fused_silu_mul: g * (1/(1+exp(-g))) * u. */
+void orc_silu_mul(float* out, const float* g, const float* u, int n) {
+    for (int i = 0; i < n; ++i) {
+        float sig = 1.0f / (1.0f + expf(-g[i]));
+        out[i] = g[i] * sig * u[i];
+    }
+}
+
+/* inference.rs:3522-3540 softmax. */
+static void softmax(float* x, int n) {
+    float mx = -INFINITY;
+    for (int i = 0; i < n; ++i) if (x[i] > mx) mx = x[i];
+    float sum = 0.0f;
+    for (int i = 0; i < n; ++i) { x[i] = expf(x[i] - mx); sum += x[i]; }
+    float inv = 1.0f / sum;
+    for (int i = 0; i < n; ++i) x[i] *= inv;
+}
+
+/* inference.rs:4242-4292 apply_attention_head (f32 cache, x86 path): scores via
+ * dot_f32_scalar (3570-3573), softmax, then out += score * v (add_weighted_f32_scalar
+ * 3619-3623) over p = 0..pos.  `out` must be zeroed by the caller (4660). */
+void orc_attention(float* out, const float* q, const float* kc, const float* vc, int pos,
+                   int heads, int kv_heads, int hd, int kv_width) {
+    int kv_mul = heads / kv_heads;
+    float scale = 1.0f / sqrtf((float)hd);
+    float* scores = (float*)malloc(sizeof(float) * (size_t)(pos + 1));
+    for (int h = 0; h < heads; ++h) {
+        int kvh = h / kv_mul;
+        const float* qh = q + h * hd;
+        for (int p = 0; p <= pos; ++p) {
+            const float* k = kc + (size_t)p * kv_width + kvh * hd;
+            float s = 0.0f;
+            for (int d = 0; d < hd; ++d) s += qh[d] * k[d];
+            scores[p] = s * scale;
+        }
+        softmax(scores, pos + 1);
+        float* o = out + h * hd;
+        for (int p = 0; p <= pos; ++p) {
+            const float* v = vc + (size_t)p * kv_width + kvh * hd;
+            for (int d = 0; d < hd; ++d) o[d] += scores[p] * v[d];
+        }
+    }
+    free(scores);
+}
+
+/* inference.rs:4834-4845 sample_logits(temperature 0): first max, strict >. */
+int orc_argmax(const float* x, long n) {
+    float mv = x[0]; long mi = 0;
+    for (long i = 0; i < n; ++i) if (x[i] > mv) { mv = x[i]; mi = i; }
+    return (int)mi;
+}
+
+/* ------------------------------------------------------------------ GGUF reader */
+/* gguf.rs:454-551 read_file: v2/v3 header, metadata, tensor table, aligned data. */
+typedef struct { char name[96]; int type; int ndim; uint64_t dims[4]; uint64_t off; } orc_tensor;
+typedef struct {
+    const uint8_t* map; size_t size; int fd;
+    orc_tensor* tensors; int ntensors;
+    uint64_t data_start, alignment;
+    /* llama hparams (model.rs:48-185) */
+    uint32_t ctx, emb, layers, ffn, heads, kv_heads, vocab, head_dim, rope_dim;
+    float rope_base, eps;
+    char arch[32];
+} orc_gguf;
+
+typedef struct { const uint8_t* p; const uint8_t* end; int err; } rd_t;
+static uint64_t rd_u(rd_t* r, int n) {
+    if (r->p + n > r->end) { r->err = 1; return 0; }
+    uint64_t v = 0; for (int i = 0; i < n; ++i) v |= (uint64_t)r->p[i] << (8 * i);
+    r->p += n; return v;
+}
+static int value_size(int t) { switch (t) { case 0: case 1: case 7: return 1; case 2: case 3: return 2; case 4: case 5: case 6: return 4; case 10: case 11: case 12: return 8; default: return -1; } }
+static void skip_value(rd_t* r, int t) {
+    if (t == 8) { uint64_t n = rd_u(r, 8); r->p += n; return; }
+    if (t == 9) { int et = (int)rd_u(r, 4); uint64_t n = rd_u(r, 8); for (uint64_t i = 0; i < n && !r->err; ++i) skip_value(r, et); return; }
+    int s = value_size(t); if (s < 0) { r->err = 1; return; } r->p += s;
+}
+
+static orc_tensor* find_tensor(orc_gguf* g, const char* name) {
+    for (int i = 0; i < g->ntensors; ++i) if (!strcmp(g->tensors[i].name, name)) return &g->tensors[i];
+    return NULL;
+}
+
+orc_gguf* orc_gguf_open(const char* path) {
+    int fd = open(path, O_RDONLY);
+    if (fd < 0) return NULL;
+    struct stat st; fstat(fd, &st);
+    const uint8_t* map = (const uint8_t*)mmap(NULL, (size_t)st.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
+    if (map == MAP_FAILED) { close(fd); return NULL; }
+    orc_gguf* g = (orc_gguf*)calloc(1, sizeof(orc_gguf));
+    g->map = map; g->size = (size_t)st.st_size; g->fd = fd; g->alignment = 32;
+    g->rope_base = 10000.0f; g->eps = 1e-5f;
+    rd_t r = { map, map + st.st_size, 0 };
+    if (memcmp(map, "GGUF", 4)) goto fail;
+    r.p += 4;
+    uint32_t ver = (uint32_t)rd_u(&r, 4);
+    if (ver < 2 || ver > 3) goto fail;
+    uint64_t nt = rd_u(&r, 8), nkv = rd_u(&r, 8);
+    for (uint64_t i = 0; i < nkv && !r.err; ++i) {
+        uint64_t kl = rd_u(&r, 8);
+        char key[128] = {0}; memcpy(key, r.p, kl < 127 ? kl : 127); r.p += kl;
+        int t = (int)rd_u(&r, 4);
+        const uint8_t* vp = r.p;
+        if (!strcmp(key, "general.architecture") && t == 8) {
+            uint64_t n = rd_u(&r, 8); memcpy(g->arch, r.p, n < 31 ? n : 31); r.p += n; continue;
+        }
+        skip_value(&r, t);
+        uint64_t u = 0; float f = 0;
+        if (t == 4 || t == 5) u = vp[0] | (vp[1] << 8) | (vp[2] << 16) | ((uint32_t)vp[3] << 24);
+        if (t == 10) memcpy(&u, vp, 8);
+        if (t == 6) memcpy(&f, vp, 4);
+        const char* k = strchr(key, '.'); k = k ? k + 1 : key;
+        if (!strcmp(key, "general.alignment")) g->alignment = u;
+        else if (!strncmp(key, "llama.", 6)) {
+            if (!strcmp(k, "context_length")) g->ctx = (uint32_t)u;
+            else if (!strcmp(k, "embedding_length")) g->emb = (uint32_t)u;
+            else if (!strcmp(k, "block_count")) g->layers = (uint32_t)u;
+            else if (!strcmp(k, "feed_forward_length")) g->ffn = (uint32_t)u;
+            else if (!strcmp(k, "attention.head_count")) g->heads = (uint32_t)u;
+            else if (!strcmp(k, "attention.head_count_kv")) g->kv_heads = (uint32_t)u;
+            else if (!strcmp(k, "vocab_size")) g->vocab = (uint32_t)u;
+            else if (!strcmp(k, "attention.key_length")) g->head_dim = (uint32_t)u;
+            else if (!strcmp(k, "rope.dimension_count")) g->rope_dim = (uint32_t)u;
+            else if (!strcmp(k, "rope.freq_base")) g->rope_base = f;
+            else if (!strcmp(k, "attention.layer_norm_rms_epsilon")) g->eps = f;
+        }
+    }
+    g->tensors = (orc_tensor*)calloc(nt ? nt : 1, sizeof(orc_tensor));
+    g->ntensors = (int)nt;
+    for (uint64_t i = 0; i < nt && !r.err; ++i) {
+        uint64_t nl = rd_u(&r, 8);
+        memcpy(g->tensors[i].name, r.p, nl < 95 ? nl : 95); r.p += nl;
+        g->tensors[i].ndim = (int)rd_u(&r, 4);
+        for (int d = 0; d < g->tensors[i].ndim && d < 4; ++d) g->tensors[i].dims[d] = rd_u(&r, 8);
+        g->tensors[i].type = (int)rd_u(&r, 4);
+        g->tensors[i].off = rd_u(&r, 8);
+    }
+    if (r.err) goto fail;
+    uint64_t pos = (uint64_t)(r.p - map);
+    g->data_start = (pos + g->alignment - 1) / g->alignment * g->alignment;
+    if (g->kv_heads == 0) g->kv_heads = g->heads;
+    if (g->heads == 0 || g->emb % g->heads) goto fail;
+    if (g->head_dim == 0) g->head_dim = g->emb / g->heads;
+    if (g->rope_dim == 0) g->rope_dim = g->head_dim;
+    if (g->vocab == 0) {
+        orc_tensor* te = find_tensor(g, "token_embd.weight");
+        if (!te) goto fail;
+        g->vocab = (uint32_t)(te->dims[0] == g->emb ? te->dims[1] : te->dims[0]);
+    }
+    return g;
+fail:
+    munmap((void*)map, (size_t)st.st_size); close(fd); free(g->tensors); free(g);
+    return NULL;
+}
+
+static const uint8_t* tensor_data(orc_gguf* g, orc_tensor* t) { return g->map + g->data_start + t->off; }
+
+/* ------------------------------------------------------------------ model */
+typedef struct { int type; long rows; int cols; const uint8_t* data; uint8_t* owned; } qmat;
+typedef struct {
+    float* attn_norm; float* ffn_norm;
+    qmat wq, wk, wv, wo, w1, w2, w3;
+} orc_layer;
+
+typedef struct {
+    orc_gguf* g;
+    int emb, layers, ffn, heads, kv_heads, hd, vocab, rope_dim, ctx, qw, kvw;
+    float eps, base;
+    int embd_type; const uint8_t* embd;      /* token_embd raw rows, dequantised on demand */
+    float* out_norm;
+    qmat head;                                 /* untied output.weight or tied Q4_0 requant */
+    orc_layer* L;
+    float *kc, *vc;                            /* [layer][ctx][kv_width] f32, inference.rs:505-547 */
+    /* workspace (inference.rs:601-695) */
+    float *hidden, *residual, *norm_x, *q, *k, *v, *att, *gate, *up, *gu, *logits;
+    int8_t* xq; float* xs;
+} orc_model;
+
+static float* load_f32(orc_gguf* g, const char* name, long n) {
+    orc_tensor* t = find_tensor(g, name);
+    if (!t) return NULL;
+    float* out = (float*)malloc(sizeof(float) * (size_t)n);
+    orc_dequant_row(t->type, tensor_data(g, t), (int)n, out);
+    return out;
+}
+static int load_q(orc_gguf* g, const char* name, qmat* m) {
+    orc_tensor* t = find_tensor(g, name);
+    if (!t || t->ndim != 2) return -1;
+    m->type = t->type; m->cols = (int)t->dims[0]; m->rows = (long)t->dims[1];
+    m->data = tensor_data(g, t); m->owned = NULL;
+    return 0;
+}
+
+void orc_embed_row(const orc_model* m, int token, float* out) {
+    orc_dequant_row(m->embd_type, m->embd + (size_t)token * orc_row_bytes(m->embd_type, m->emb), m->emb, out);
+}
+
+/* model.rs:461-545 LlamaWeights::load.  Tied head (model.rs:471-532, default
+ * NANOCAMELID_Q4_HEAD=on via model.rs:1429-1442): Q4_0 re-quantisation of the
+ * dequantised f32 token_embd table, block by block. */
+orc_model* orc_model_load(const char* path, int ctx_limit) {
+    orc_gguf* g = orc_gguf_open(path);
+    if (!g) return NULL;
+    orc_model* m = (orc_model*)calloc(1, sizeof(orc_model));
+    m->g = g; m->emb = g->emb; m->layers = g->layers; m->ffn = g->ffn; m->heads = g->heads;
+    m->kv_heads = g->kv_heads; m->hd = g->head_dim; m->vocab = g->vocab; m->rope_dim = g->rope_dim;
+    m->eps = g->eps; m->base = g->rope_base;
+    m->ctx = (ctx_limit > 0 && ctx_limit < (int)g->ctx) ? ctx_limit : (int)g->ctx;
+    m->qw = m->heads * m->hd; m->kvw = m->kv_heads * m->hd;
+    orc_tensor* te = find_tensor(g, "token_embd.weight");
+    if (!te) return NULL;
+    m->embd_type = te->type; m->embd = tensor_data(g, te);
+    m->out_norm = load_f32(g, "output_norm.weight", m->emb);
+    if (load_q(g, "output.weight", &m->head) != 0) {
+        long V = m->vocab; int H = m->emb, nb = H / 32;
+        m->head.type = T_Q4_0; m->head.rows = V; m->head.cols = H;
+        m->head.owned = (uint8_t*)malloc((size_t)V * nb * 18);
+        m->head.data = m->head.owned;
+        #pragma omp parallel
+        {
+            float* row = (float*)malloc(sizeof(float) * H);
+            #pragma omp for schedule(static)
+            for (long r = 0; r < V; ++r) {
+                orc_embed_row(m, (int)r, row);
+                for (int b = 0; b < nb; ++b) orc_quantize_block_q4_0(row + b * 32, m->head.owned + ((size_t)r * nb + b) * 18);
+            }
+            free(row);
+        }
+    }
+    m->L = (orc_layer*)calloc(m->layers, sizeof(orc_layer));
+    char nm[128];
+    for (int i = 0; i < m->layers; ++i) {
+        orc_layer* l = &m->L[i];
+#define LQ(field, s) snprintf(nm, sizeof nm, "blk.%d." s ".weight", i); if (load_q(g, nm, &l->field)) return NULL;
+        snprintf(nm, sizeof nm, "blk.%d.attn_norm.weight", i); l->attn_norm = load_f32(g, nm, m->emb);
+        snprintf(nm, sizeof nm, "blk.%d.ffn_norm.weight", i); l->ffn_norm = load_f32(g, nm, m->emb);
+        LQ(wq, "attn_q") LQ(wk, "attn_k") LQ(wv, "attn_v") LQ(wo, "attn_output")
+        LQ(w1, "ffn_gate") LQ(w3, "ffn_up") LQ(w2, "ffn_down")
+#undef LQ
+    }
+    size_t kvn = (size_t)m->layers * m->ctx * m->kvw;
+    m->kc = (float*)calloc(kvn, 4); m->vc = (float*)calloc(kvn, 4);
+    int mx = m->emb > m->qw ? m->emb : m->qw; if (m->ffn > mx) mx = m->ffn;
+    m->hidden = calloc(m->emb, 4); m->residual = calloc(m->emb, 4); m->norm_x = calloc(m->emb, 4);
+    m->q = calloc(m->qw, 4); m->k = calloc(m->kvw, 4); m->v = calloc(m->kvw, 4); m->att = calloc(m->qw, 4);
+    m->gate = calloc(m->ffn, 4); m->up = calloc(m->ffn, 4); m->gu = calloc(m->ffn, 4);
+    m->logits = calloc(m->vocab, 4); m->xq = calloc(mx, 1); m->xs = calloc(mx / 32 + 1, 4);
+    return m;
+}
+
+int orc_model_info(const orc_model* m, int* out) {
+    out[0] = m->emb; out[1] = m->layers; out[2] = m->ffn; out[3] = m->heads; out[4] = m->kv_heads;
+    out[5] = m->hd; out[6] = m->vocab; out[7] = m->rope_dim; out[8] = m->ctx; out[9] = m->head.type;
+    return 10;
+}
+void orc_model_reset(orc_model* m) {
+    size_t kvn = (size_t)m->layers * m->ctx * m->kvw;
+    memset(m->kc, 0, kvn * 4); memset(m->vc, 0, kvn * 4);
+}
+const uint8_t* orc_model_head_blocks(const orc_model* m) { return m->head.data; }
+float* orc_model_hidden(orc_model* m) { return m->hidden; }
+
+static void mm(const qmat* w, const int8_t* xq, const float* xs, float* out) {
+    orc_matmul_quantized(w->type, w->data, w->rows, w->cols, xq, xs, out);
+}
+
+/* inference.rs:4505-4781 run_layer_range (dense FFN) for one token at `pos`. */
+static void run_layers(orc_model* m, int pos) {
+    for (int li = 0; li < m->layers; ++li) {
+        orc_layer* l = &m->L[li];
+        memcpy(m->residual, m->hidden, 4 * (size_t)m->emb);
+        orc_rms_norm(m->norm_x, m->hidden, l->attn_norm, m->emb, m->eps);
+        orc_quantize_q8_0(m->norm_x, m->emb, m->xq, m->xs);
+        mm(&l->wq, m->xq, m->xs, m->q);
+        mm(&l->wk, m->xq, m->xs, m->k);
+        mm(&l->wv, m->xq, m->xs, m->v);
+        orc_apply_rope(m->q, pos, m->heads, m->hd, m->rope_dim, m->base);
+        orc_apply_rope(m->k, pos, m->kv_heads, m->hd, m->rope_dim, m->base);
+        size_t lo = (size_t)li * m->ctx * m->kvw;
+        memcpy(m->kc + lo + (size_t)pos * m->kvw, m->k, 4 * (size_t)m->kvw);
+        memcpy(m->vc + lo + (size_t)pos * m->kvw, m->v, 4 * (size_t)m->kvw);
+        memset(m->att, 0, 4 * (size_t)m->qw);
+        orc_attention(m->att, m->q, m->kc + lo, m->vc + lo, pos, m->heads, m->kv_heads, m->hd, m->kvw);
+        orc_quantize_q8_0(m->att, m->qw, m->xq, m->xs);
+        mm(&l->wo, m->xq, m->xs, m->hidden);
+        for (int i = 0; i < m->emb; ++i) m->hidden[i] += m->residual[i];
+        memcpy(m->residual, m->hidden, 4 * (size_t)m->emb);
+        orc_rms_norm(m->norm_x, m->hidden, l->ffn_norm, m->emb, m->eps);
+        orc_quantize_q8_0(m->norm_x, m->emb, m->xq, m->xs);
+        mm(&l->w1, m->xq, m->xs, m->gate);
+        mm(&l->w3, m->xq, m->xs, m->up);
+        orc_silu_mul(m->gu, m->gate, m->up, m->ffn);
+        orc_quantize_q8_0(m->gu, m->ffn, m->xq, m->xs);
+        mm(&l->w2, m->xq, m->xs, m->hidden);
+        for (int i = 0; i < m->emb; ++i) m->hidden[i] += m->residual[i];
+    }
+}
+
+/* inference.rs:4783-4832 compute_logits_from_hidden (quantised head). */
+void orc_compute_logits(orc_model* m, const float* hidden, float* logits) {
+    float* nx = (float*)malloc(4 * (size_t)m->emb);
+    int8_t* xq = (int8_t*)malloc(m->emb); float* xs = (float*)malloc(4 * (size_t)(m->emb / 32));
+    orc_rms_norm(nx, hidden, m->out_norm, m->emb, m->eps);
+    orc_quantize_q8_0(nx, m->emb, xq, xs);
+    mm(&m->head, xq, xs, logits);
+    free(nx); free(xq); free(xs);
+}
+
+/* inference.rs:3649-3670 forward_pass -> 4460-4492 forward_pass_inner.  Returns the
+ * greedy token (sample_logits temperature 0); logits copied out when non-NULL. */
+int orc_forward_pass(orc_model* m, int token, int pos, float* logits_out) {
+    orc_embed_row(m, token, m->hidden);
+    run_layers(m, pos);
+    orc_compute_logits(m, m->hidden, m->logits);
+    if (logits_out) memcpy(logits_out, m->logits, 4 * (size_t)m->vocab);
+    return orc_argmax(m->logits, m->vocab);
+}
+
+/* bin/cluster_tp_node.rs:808-875 run_reference: prompt token by token, then greedy
+ * decode of n_gen tokens (each generated token is fed back). */
+int orc_generate(orc_model* m, const int* prompt, int n_prompt, int n_gen, int* out, float* last_logits) {
+    int pos = 0, next = 0;
+    for (int i = 0; i < n_prompt; ++i) next = orc_forward_pass(m, prompt[i], pos++, NULL);
+    for (int g = 0; g < n_gen && pos < m->ctx; ++g) {
+        out[g] = next;
+        next = orc_forward_pass(m, next, pos++, (g + 1 == n_gen) ? last_logits : NULL);
+    }
+    return next;
+}
+
+/* inference.rs:3695-3744 prefill_pass_batch + 3747-4111 run_layer_range_batch: per
+ * token the single-token formulas, KV stored for the whole batch before attention.
+ * Writes the final hidden of each token into hidden_out[n][emb]. */
+void orc_prefill_batch(orc_model* m, const int* tokens, int n, int start_pos, float* hidden_out) {
+    int H = m->emb, F = m->ffn, QW = m->qw, KW = m->kvw;
+    float* hid = malloc(4 * (size_t)n * H); float* res = malloc(4 * (size_t)n * H);
+    float* nx = malloc(4 * (size_t)n * H); float* q = malloc(4 * (size_t)n * QW);
+    float* k = malloc(4 * (size_t)n * KW); float* v = malloc(4 * (size_t)n * KW);
+    float* att = malloc(4 * (size_t)n * QW); float* g = malloc(4 * (size_t)n * F);
+    float* u = malloc(4 * (size_t)n * F); float* gu = malloc(4 * (size_t)n * F);
+    int mx = F > QW ? F : QW; if (H > mx) mx = H;
+    int8_t* xq = malloc((size_t)n * mx); float* xs = malloc(4 * (size_t)n * (mx / 32));
+    for (int t = 0; t < n; ++t) orc_embed_row(m, tokens[t], hid + (size_t)t * H);
+    for (int li = 0; li < m->layers; ++li) {
+        orc_layer* l = &m->L[li];
+        memcpy(res, hid, 4 * (size_t)n * H);
+        for (int t = 0; t < n; ++t) {
+            orc_rms_norm(nx + (size_t)t * H, hid + (size_t)t * H, l->attn_norm, H, m->eps);
+            orc_quantize_q8_0(nx + (size_t)t * H, H, xq + (size_t)t * H, xs + (size_t)t * (H / 32));
+        }
+        orc_matmul_quantized_batch(l->wq.type, l->wq.data, l->wq.rows, H, n, xq, xs, q);
+        orc_matmul_quantized_batch(l->wk.type, l->wk.data, l->wk.rows, H, n, xq, xs, k);
+        orc_matmul_quantized_batch(l->wv.type, l->wv.data, l->wv.rows, H, n, xq, xs, v);
+        size_t lo = (size_t)li * m->ctx * KW;
+        for (int t = 0; t < n; ++t) {
+            int pos = start_pos + t;
+            orc_apply_rope(q + (size_t)t * QW, pos, m->heads, m->hd, m->rope_dim, m->base);
+            orc_apply_rope(k + (size_t)t * KW, pos, m->kv_heads, m->hd, m->rope_dim, m->base);
+            memcpy(m->kc + lo + (size_t)pos * KW, k + (size_t)t * KW, 4 * (size_t)KW);
+            memcpy(m->vc + lo + (size_t)pos * KW, v + (size_t)t * KW, 4 * (size_t)KW);
+        }
+        memset(att, 0, 4 * (size_t)n * QW);
+        for (int t = 0; t < n; ++t)
+            orc_attention(att + (size_t)t * QW, q + (size_t)t * QW, m->kc + lo, m->vc + lo, start_pos + t, m->heads, m->kv_heads, m->hd, KW);
+        for (int t = 0; t < n; ++t) orc_quantize_q8_0(att + (size_t)t * QW, QW, xq + (size_t)t * QW, xs + (size_t)t * (QW / 32));
+        orc_matmul_quantized_batch(l->wo.type, l->wo.data, H, QW, n, xq, xs, hid);
+        for (size_t i = 0; i < (size_t)n * H; ++i) hid[i] += res[i];
+        memcpy(res, hid, 4 * (size_t)n * H);
+        for (int t = 0; t < n; ++t) {
+            orc_rms_norm(nx + (size_t)t * H, hid + (size_t)t * H, l->ffn_norm, H, m->eps);
+            orc_quantize_q8_0(nx + (size_t)t * H, H, xq + (size_t)t * H, xs + (size_t)t * (H / 32));
+        }
+        orc_matmul_quantized_batch(l->w1.type, l->w1.data, F, H, n, xq, xs, g);
+        orc_matmul_quantized_batch(l->w3.type, l->w3.data, F, H, n, xq, xs, u);
+        orc_silu_mul(gu, g, u, n * F);
+        for (int t = 0; t < n; ++t) orc_quantize_q8_0(gu + (size_t)t * F, F, xq + (size_t)t * F, xs + (size_t)t * (F / 32));
+        orc_matmul_quantized_batch(l->w2.type, l->w2.data, H, F, n, xq, xs, hid);
+        for (size_t i = 0; i < (size_t)n * H; ++i) hid[i] += res[i];
+    }
+    memcpy(hidden_out, hid, 4 * (size_t)n * H);
+    free(hid); free(res); free(nx); free(q); free(k); free(v); free(att); free(g); free(u); free(gu); free(xq); free(xs);
+}
+
+/* speculative.rs:299-494 speculative_decoding_step (greedy, no stop tokens).
+ * `tlogit_tok` / `dlogit_tok` carry the argmax of the target/draft logits left by
+ * the previous pass.  Appends accepted tokens to out; returns the count and
+ * updates *pos, the argmaxes and stats[0..1] (drafted, accepted). */
+static int spec_step(orc_model* tgt, orc_model* dr, int* pos, int* tlogit_tok, int* dlogit_tok, int k, int* out, int* stats) {
+    int start = *pos;
+    int maxd = k;
+    if (tgt->ctx - (start + 1) < maxd) maxd = tgt->ctx - (start + 1);
+    if (dr->ctx - (start + 1) < maxd) maxd = dr->ctx - (start + 1);
+    if (maxd <= 0) return 0;
+    int drafted[64]; int nd = 0, cur = start;
+    while (nd < maxd) {
+        int t = *dlogit_tok;
+        drafted[nd++] = t;
+        *dlogit_tok = orc_forward_pass(dr, t, cur, NULL);
+        cur++;
+    }
+    float* hb = malloc(4 * (size_t)nd * tgt->emb);
+    orc_prefill_batch(tgt, drafted, nd, start, hb);
+    float* lg = malloc(4 * (size_t)tgt->vocab);
+    int nacc = 0, rejected = 0;
+    stats[0] += nd;
+    for (int i = 0; i < nd; ++i) {
+        int tt;
+        if (i == 0) tt = *tlogit_tok;
+        else { orc_compute_logits(tgt, hb + (size_t)(i - 1) * tgt->emb, lg); tt = orc_argmax(lg, tgt->vocab); }
+        if (drafted[i] == tt) { out[nacc++] = tt; stats[1]++; }
+        else {
+            rejected = 1; out[nacc++] = tt;
+            *tlogit_tok = orc_forward_pass(tgt, tt, start + i, NULL);
+            *dlogit_tok = orc_forward_pass(dr, tt, start + i, NULL);
+            *pos = start + i + 1;
+            break;
+        }
+    }
+    if (!rejected) {
+        orc_compute_logits(tgt, hb + (size_t)(nd - 1) * tgt->emb, lg);
+        int tr = orc_argmax(lg, tgt->vocab);
+        out[nacc++] = tr;
+        *tlogit_tok = orc_forward_pass(tgt, tr, start + nd, NULL);
+        *dlogit_tok = orc_forward_pass(dr, tr, start + nd, NULL);
+        *pos = start + nd + 1;
+    }
+    free(hb); free(lg);
+    return nacc;
+}
+
+/* main.rs:9604-9830 speculative chat loop shape: prompt through both models token by
+ * token, then speculative steps until n_gen tokens.  Returns tokens produced. */
+int orc_spec_generate(orc_model* tgt, orc_model* dr, const int* prompt, int n_prompt, int n_gen, int k, int* out, int* stats) {
+    int pos = 0, tt = 0, dt = 0, n = 0;
+    stats[0] = stats[1] = 0;
+    for (int i = 0; i < n_prompt; ++i) { tt = orc_forward_pass(tgt, prompt[i], pos, NULL); dt = orc_forward_pass(dr, prompt[i], pos, NULL); pos++; }
+    int buf[80];
+    while (n < n_gen) {
+        int c = spec_step(tgt, dr, &pos, &tt, &dt, k, buf, stats);
+        if (c == 0) break;
+        for (int i = 0; i < c && n < n_gen; ++i) out[n++] = buf[i];
+    }
+    return n;
+}
+
+/* ------------------------------------------------------------------ tensor parallel */
+/* tp.rs:641-660 validate_shares + tp.rs:662-701 shard_geometry.
+ * out: q_start q_heads kv_start kv_heads ffn_start ffn_len head_row_start head_rows. */
+int orc_shard_geometry(int heads, int kv_total, int ffn, int vocab, const int* shares, int n, int idx, int* out) {
+    int sum = 0;
+    for (int i = 0; i < n; ++i) { sum += shares[i]; if (shares[i] == 0) return -2; }
+    if (sum != kv_total) return -1;
+    for (int i = 0; i < n; ++i) if (((long)ffn * shares[i]) % ((long)kv_total * 32)) return -3;
+    if (idx < 0 || idx >= n) return -4;
+    int qpk = heads / kv_total, kv_start = 0;
+    for (int i = 0; i < idx; ++i) kv_start += shares[i];
+    int unit = ffn / kv_total;
+    long acc = 0, hs = 0, he = 0;
+    for (int i = 0; i < n; ++i) {
+        if (i == idx) hs = acc;
+        acc += ((long)vocab * shares[i] / kv_total) & ~3L;
+        if (i == idx) he = acc;
+    }
+    out[0] = kv_start * qpk; out[1] = shares[idx] * qpk; out[2] = kv_start; out[3] = shares[idx];
+    out[4] = kv_start * unit; out[5] = shares[idx] * unit;
+    out[6] = (int)hs; out[7] = (idx + 1 == n) ? (int)(vocab - hs) : (int)(he - hs);
+    return 0;
+}
+
+typedef struct {
+    int q0, qh, k0, kh, f0, fl, h0, hr;
+    qmat *wq, *wk, *wv, *wo, *w1, *w3, *w2;   /* per layer */
+    float *kc, *vc;
+    qmat head;
+} orc_shard;
+typedef struct { orc_model* m; int n; orc_shard* s; } orc_tp;
+
+/* tp.rs:41-49 slice_rows / row_run. */
+static qmat slice_rows(const qmat* w, long r0, long r1) {
+    qmat o = *w; size_t rb = orc_row_bytes(w->type, w->cols);
+    o.rows = r1 - r0; o.owned = malloc(rb * (size_t)o.rows);
+    memcpy(o.owned, w->data + rb * r0, rb * (size_t)o.rows); o.data = o.owned; return o;
+}
+/* tp.rs:61-118 slice_cols / col_gather (block-aligned column slices). */
+static qmat slice_cols(const qmat* w, int c0, int c1) {
+    qmat o = *w; int be = (int)orc_block_elems(w->type); size_t bb = orc_block_bytes(w->type);
+    size_t rb = orc_row_bytes(w->type, w->cols), nrb = (size_t)(c1 - c0) / be * bb;
+    o.cols = c1 - c0; o.owned = malloc(nrb * (size_t)w->rows);
+    for (long r = 0; r < w->rows; ++r) memcpy(o.owned + nrb * r, w->data + rb * r + (size_t)c0 / be * bb, nrb);
+    o.data = o.owned; return o;
+}
+
+/* tp.rs:125-199 build_tp_shards + tp.rs:541-570 build_tp_head_shards (tied and untied
+ * heads both become row slices of the same head blocks; per-block requantisation makes
+ * the tied slices identical to slicing the full requantised head). */
+orc_tp* orc_tp_build(orc_model* m, const int* shares, int n) {
+    orc_tp* tp = calloc(1, sizeof(orc_tp)); tp->m = m; tp->n = n; tp->s = calloc(n, sizeof(orc_shard));
+    for (int i = 0; i < n; ++i) {
+        int geo[8];
+        if (orc_shard_geometry(m->heads, m->kv_heads, m->ffn, m->vocab, shares, n, i, geo)) return NULL;
+        orc_shard* s = &tp->s[i];
+        s->q0 = geo[0]; s->qh = geo[1]; s->k0 = geo[2]; s->kh = geo[3]; s->f0 = geo[4]; s->fl = geo[5];
+        s->h0 = geo[6]; s->hr = geo[7];
+        s->wq = calloc(m->layers, sizeof(qmat)); s->wk = calloc(m->layers, sizeof(qmat)); s->wv = calloc(m->layers, sizeof(qmat));
+        s->wo = calloc(m->layers, sizeof(qmat)); s->w1 = calloc(m->layers, sizeof(qmat)); s->w3 = calloc(m->layers, sizeof(qmat));
+        s->w2 = calloc(m->layers, sizeof(qmat));
+        int hd = m->hd;
+        for (int l = 0; l < m->layers; ++l) {
+            orc_layer* L = &m->L[l];
+            s->wq[l] = slice_rows(&L->wq, (long)s->q0 * hd, (long)(s->q0 + s->qh) * hd);
+            s->wk[l] = slice_rows(&L->wk, (long)s->k0 * hd, (long)(s->k0 + s->kh) * hd);
+            s->wv[l] = slice_rows(&L->wv, (long)s->k0 * hd, (long)(s->k0 + s->kh) * hd);
+            s->wo[l] = slice_cols(&L->wo, s->q0 * hd, (s->q0 + s->qh) * hd);
+            s->w1[l] = slice_rows(&L->w1, s->f0, s->f0 + s->fl);
+            s->w3[l] = slice_rows(&L->w3, s->f0, s->f0 + s->fl);
+            s->w2[l] = slice_cols(&L->w2, s->f0, s->f0 + s->fl);
+        }
+        size_t kvn = (size_t)m->layers * m->ctx * s->kh * hd;
+        s->kc = calloc(kvn, 4); s->vc = calloc(kvn, 4);
+        s->head = slice_rows(&m->head, s->h0, s->h0 + s->hr);
+    }
+    return tp;
+}
+void orc_tp_reset(orc_tp* tp) {
+    for (int i = 0; i < tp->n; ++i) {
+        size_t kvn = (size_t)tp->m->layers * tp->m->ctx * tp->s[i].kh * tp->m->hd;
+        memset(tp->s[i].kc, 0, kvn * 4); memset(tp->s[i].vc, 0, kvn * 4);
+    }
+}
+
+/* tp.rs:226-428 tp_forward_token_reduced with the fixed-order reducer of
+ * cluster_tp_node.rs:1154-1180: hidden = ((0 + p0) + p1) + ... then + residual.
+ * Then head_shard_argmax (tp.rs:576-611) on every shard and the strict->, lowest
+ * row_start merge (cluster_tp_node.rs:1185-1204).  Returns the greedy token. */
+int orc_tp_forward(orc_tp* tp, int token, int pos, float* logits_out) {
+    orc_model* m = tp->m; int H = m->emb, hd = m->hd;
+    float* part = malloc(4 * (size_t)H);
+    orc_embed_row(m, token, m->hidden);
+    for (int li = 0; li < m->layers; ++li) {
+        orc_layer* L = &m->L[li];
+        memcpy(m->residual, m->hidden, 4 * (size_t)H);
+        orc_rms_norm(m->norm_x, m->hidden, L->attn_norm, H, m->eps);
+        for (int i = 0; i < H; ++i) m->hidden[i] = 0.0f;
+        for (int si = 0; si < tp->n; ++si) {
+            orc_shard* s = &tp->s[si];
+            int qw = s->qh * hd, kw = s->kh * hd;
+            orc_quantize_q8_0(m->norm_x, H, m->xq, m->xs);
+            mm(&s->wq[li], m->xq, m->xs, m->q);
+            mm(&s->wk[li], m->xq, m->xs, m->k);
+            mm(&s->wv[li], m->xq, m->xs, m->v);
+            orc_apply_rope(m->q, pos, s->qh, hd, m->rope_dim, m->base);
+            orc_apply_rope(m->k, pos, s->kh, hd, m->rope_dim, m->base);
+            size_t lo = (size_t)li * m->ctx * kw;
+            memcpy(s->kc + lo + (size_t)pos * kw, m->k, 4 * (size_t)kw);
+            memcpy(s->vc + lo + (size_t)pos * kw, m->v, 4 * (size_t)kw);
+            memset(m->att, 0, 4 * (size_t)qw);
+            orc_attention(m->att, m->q, s->kc + lo, s->vc + lo, pos, s->qh, s->kh, hd, kw);
+            orc_quantize_q8_0(m->att, qw, m->xq, m->xs);
+            mm(&s->wo[li], m->xq, m->xs, part);
+            for (int i = 0; i < H; ++i) m->hidden[i] += part[i];
+        }
+        for (int i = 0; i < H; ++i) m->hidden[i] += m->residual[i];
+        memcpy(m->residual, m->hidden, 4 * (size_t)H);
+        orc_rms_norm(m->norm_x, m->hidden, L->ffn_norm, H, m->eps);
+        for (int i = 0; i < H; ++i) m->hidden[i] = 0.0f;
+        for (int si = 0; si < tp->n; ++si) {
+            orc_shard* s = &tp->s[si];
+            orc_quantize_q8_0(m->norm_x, H, m->xq, m->xs);
+            mm(&s->w1[li], m->xq, m->xs, m->gate);
+            mm(&s->w3[li], m->xq, m->xs, m->up);
+            orc_silu_mul(m->gu, m->gate, m->up, s->fl);
+            orc_quantize_q8_0(m->gu, s->fl, m->xq, m->xs);
+            mm(&s->w2[li], m->xq, m->xs, part);
+            for (int i = 0; i < H; ++i) m->hidden[i] += part[i];
+        }
+        for (int i = 0; i < H; ++i) m->hidden[i] += m->residual[i];
+    }
+    float* nx = malloc(4 * (size_t)H); int8_t* xq = malloc(H); float* xs = malloc(4 * (size_t)(H / 32));
+    orc_rms_norm(nx, m->hidden, m->out_norm, H, m->eps);
+    orc_quantize_q8_0(nx, H, xq, xs);
+    int best = 0; float bv = 0.0f;
+    for (int si = 0; si < tp->n; ++si) {
+        orc_shard* s = &tp->s[si];
+        float* lg = logits_out ? logits_out + s->h0 : malloc(4 * (size_t)s->hr);
+        mm(&s->head, xq, xs, lg);
+        int loc = orc_argmax(lg, s->hr);
+        if (si == 0 || lg[loc] > bv) { bv = lg[loc]; best = s->h0 + loc; }
+        if (!logits_out) free(lg);
+    }
+    free(nx); free(xq); free(xs); free(part);
+    return best;
+}
+
+int orc_tp_generate(orc_tp* tp, const int* prompt, int n_prompt, int n_gen, int* out) {
+    int pos = 0, next = 0;
+    for (int i = 0; i < n_prompt; ++i) next = orc_tp_forward(tp, prompt[i], pos++, NULL);
+    for (int g = 0; g < n_gen && pos < tp->m->ctx; ++g) { out[g] = next; next = orc_tp_forward(tp, next, pos++, NULL); }
+    return next;
+}
+
+/* Debug view of the workspace (same `which` codes as the product's ncm_debug_read). */
+float* orc_model_buf(orc_model* m, int which, int layer) {
+    size_t lo = (size_t)layer * m->ctx * m->kvw;
+    switch (which) {
+        case 0: return m->hidden;
+        case 1: return m->q;
+        case 2: return m->att;
+        case 3: return m->gu;
+        case 4: return m->kc + lo;
+        case 5: return m->vc + lo;
+        case 6: return m->logits;
+        default: return NULL;
+    }
+}

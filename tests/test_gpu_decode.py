@@ -1,0 +1,114 @@
+"""End-to-end decode on the GPU vs the CPU oracle.
+
+Gates (the reference's own parity rule, README.md:107-115): greedy tokens identical to
+the single-node reference path; logits within 1e-3 relative (max |diff| <= 1e-3 *
+max |logit|)."""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import TINY
+
+pytestmark = pytest.mark.gpu
+
+
+def tiny_spec(ncm, **kw):
+    d = dict(TINY)
+    d.update(kw)
+    return ncm.spec(d["emb"], d["layers"], d["heads"], d["kv_heads"], d["head_dim"], d["ffn"], vocab=d["vocab"],
+                    ctx=d["ctx"], tied=d.get("tied", True), t_embd=d.get("t_embd", ncm.Q4_0),
+                    t_attn=d.get("t_attn", ncm.Q4_0), t_ffn=d.get("t_ffn", ncm.Q4_0), t_out=d.get("t_out", ncm.Q4_0),
+                    seed=d.get("seed", 7))
+
+
+def prompt_ids(n, vocab, seed=0):
+    rng = np.random.default_rng(seed)
+    return [int(v) for v in rng.integers(0, vocab, size=n)]
+
+
+VARIANTS = {
+    "q4_0_tied": {},
+    "q8_0_untied": dict(tied=False, t_embd=8, t_attn=8, t_ffn=8, t_out=8),
+    "mixed_q8attn_q4kffn": dict(tied=False, t_embd=8, t_attn=8, t_ffn=12, t_out=8, emb=512, ffn=1024),
+    "q4_0_untied_hd128": dict(tied=False, heads=4, kv_heads=1, head_dim=128, emb=512, ffn=768),
+}
+
+
+@pytest.mark.parametrize("variant", list(VARIANTS))
+def test_greedy_decode_matches_oracle(ncm, orc, cuda, tmp_path, variant):
+    sp = tiny_spec(ncm, **VARIANTS[variant])
+    path = tmp_path / "m.gguf"
+    ncm.write_synthetic_gguf(path, sp)
+    ref = orc.OracleModel(path)
+    prompt = prompt_ids(6, sp.vocab, seed=1)
+    n_gen = 24
+    ref_tokens, ref_logits = ref.generate(prompt, n_gen, want_last_logits=True)
+    m = ncm.Model.load(path, device=0)
+    got = m.generate(prompt, n_gen)
+    assert got == ref_tokens
+    # logits of one more forward pass at the next position
+    pos = len(prompt) + n_gen - 1
+    t_ref, lg_ref = ref.forward_pass(ref_tokens[-1], pos, want_logits=True)
+    t_got, lg_got = m.forward_pass(ref_tokens[-1], pos, want_logits=True)
+    assert t_got == t_ref
+    assert float(np.max(np.abs(lg_got - lg_ref))) <= 1e-3 * float(np.max(np.abs(lg_ref)))
+    m.close()
+
+
+def test_device_synthetic_equals_gguf_file(ncm, orc, cuda, tmp_path):
+    """On-device random init == GGUF writer + load (same blocks), checked through decode."""
+    sp = tiny_spec(ncm, tied=False, t_embd=8, t_attn=8, t_ffn=12, t_out=2, emb=512, ffn=1024)
+    path = tmp_path / "m.gguf"
+    ncm.write_synthetic_gguf(path, sp)
+    a = ncm.Model.load(path, device=0)
+    b = ncm.Model.synthetic(sp, device=0)
+    prompt = prompt_ids(5, sp.vocab, seed=2)
+    assert a.generate(prompt, 12) == b.generate(prompt, 12)
+    _, la = a.forward_pass(3, 20, want_logits=True)
+    _, lb = b.forward_pass(3, 20, want_logits=True)
+    assert np.array_equal(la, lb)
+
+
+def test_forward_pass_host_seam_and_reset(ncm, orc, cuda, tmp_path):
+    sp = tiny_spec(ncm)
+    path = tmp_path / "m.gguf"
+    ncm.write_synthetic_gguf(path, sp)
+    ref = orc.OracleModel(path)
+    m = ncm.Model.load(path, device=0)
+    toks = prompt_ids(10, sp.vocab, seed=5)
+    for pos, t in enumerate(toks):
+        r, lr = ref.forward_pass(t, pos, want_logits=True)
+        g, lg = m.forward_pass(t, pos, want_logits=True)
+        assert g == r
+        assert float(np.max(np.abs(lg - lr))) <= 1e-3 * float(np.max(np.abs(lr)))
+    m.reset()
+    ref.reset()
+    assert m.generate(toks[:3], 8) == ref.generate(toks[:3], 8)[0]
+
+
+def test_bad_arguments_fail_loudly(ncm, cuda, tmp_path):
+    sp = tiny_spec(ncm)
+    m = ncm.Model.synthetic(sp, device=0)
+    with pytest.raises(ncm.NcmError):
+        m.forward_pass(sp.vocab + 5, 0)
+    with pytest.raises(ncm.NcmError):
+        m.generate([1, 2, 3], sp.ctx)
+    with pytest.raises(ncm.NcmError):
+        ncm.Model.load(tmp_path / "missing.gguf")
+
+
+@pytest.mark.slow
+def test_config1_full_size_token_parity(ncm, orc, cuda, tmp_path):
+    """Llama-3.2-1B shape, Q4_0, tied head, 16-token prompt, 32 greedy tokens."""
+    sp = ncm.CONFIGS["cfg1_1b_q4_0"]
+    path = tmp_path / "cfg1.gguf"
+    ncm.write_synthetic_gguf(path, sp)
+    prompt = prompt_ids(16, sp.vocab, seed=0)
+    ref = orc.OracleModel(path, ctx_limit=64)
+    ref_tokens, ref_logits = ref.generate(prompt, 32, want_last_logits=True)
+    m = ncm.Model.load(path, ctx_limit=64, device=0)
+    got = m.generate(prompt, 32)
+    assert got == ref_tokens
+    _, lg = m.forward_pass(ref_tokens[-1], 16 + 31, want_logits=True)
+    assert float(np.max(np.abs(lg - ref_logits))) <= 1e-3 * float(np.max(np.abs(ref_logits)))
