@@ -5,6 +5,7 @@
 #include <dlfcn.h>
 #include <math.h>
 #include <string.h>
+#include <initializer_list>
 #include <string>
 #include <vector>
 #include "../../include/ncm.h"
@@ -88,13 +89,13 @@ struct ncm_model {
     float* out_norm = nullptr;
     std::vector<Layer> L;
     float *hidden = nullptr, *q = nullptr, *att = nullptr, *act = nullptr, *logits = nullptr, *kc = nullptr,
-          *vc = nullptr, *attn_part = nullptr, *part = nullptr;
-    unsigned *attn_cnt = nullptr, *amax_cnt = nullptr;
+          *vc = nullptr, *scores = nullptr, *part = nullptr;
+    unsigned* amax_cnt = nullptr;
     float2 *amax_part = nullptr, *rope = nullptr, *head_out = nullptr, *gather = nullptr;
     float* embd_ssq = nullptr;   // per vocab row: sequential f32 sum of squares of the embedding
     int *state = nullptr, *tokens = nullptr, *err = nullptr;
     int* h_stage = nullptr;   // pinned staging for small transfers
-    int nsplit = 1, max_per = 1;
+    int dsplit = 1;   // attention value-accumulation CTAs per kv head
     std::vector<void*> allocs;
     cudaGraphExec_t g_full = nullptr, g_nohead = nullptr;
     bool dirty = true;
@@ -201,12 +202,9 @@ static ncm_status setup_buffers(ncm_model* m, const int* shares, int nshards, in
     DALLOC(m->part, 4 * m->emb);
     DALLOC(m->kc, 4 * (size_t)m->layers * m->ctx * kw);
     DALLOC(m->vc, 4 * (size_t)m->layers * m->ctx * kw);
-    m->nsplit = num_sms() / m->kh;
-    if (m->nsplit < 1) m->nsplit = 1;
-    if (m->nsplit > m->ctx) m->nsplit = m->ctx;
-    m->max_per = (m->ctx + m->nsplit - 1) / m->nsplit;
-    DALLOC(m->attn_part, 4 * (size_t)m->qh * m->nsplit * (m->hd + 2));
-    DALLOC(m->attn_cnt, 4 * m->kh);
+    m->dsplit = 1;
+    while (m->dsplit * 2 * m->kh <= num_sms() && m->hd / (m->dsplit * 2) >= 4) m->dsplit *= 2;
+    DALLOC(m->scores, 4 * (size_t)m->qh * m->ctx);
     DALLOC(m->amax_part, 8 * num_sms());
     DALLOC(m->amax_cnt, 4);
     DALLOC(m->head_out, 8);
@@ -214,7 +212,6 @@ static ncm_status setup_buffers(ncm_model* m, const int* shares, int nshards, in
     DALLOC(m->state, 4 * ST_COUNT);
     DALLOC(m->tokens, 4 * (size_t)m->ctx);
     DALLOC(m->err, 4);
-    CK(cudaMemset(m->attn_cnt, 0, 4 * m->kh));
     CK(cudaMemset(m->amax_cnt, 0, 4));
     CK(cudaMemset(m->state, 0, 4 * ST_COUNT));
     CK(cudaMemset(m->tokens, 0, 4 * (size_t)m->ctx));
@@ -483,13 +480,23 @@ static GemvParams base_params(ncm_model* m) {
     return p;
 }
 
-static int launch_gemv(ncm_model* m, const DevMat& w, int in_mode, int epi, GemvParams& p, bool dual,
-                       cudaStream_t s) {
-    p.pitch = w.pitch;
-    int grid;
-    size_t smem;
-    gemv_plan(w.type, w.cols, p.total_rows, dual, epi == EPI_QKV, 0, p, grid, smem);
-    return gemv_launch(w.type, in_mode, epi, p, grid, s, true);
+// Plans the launch, encodes one TMA tensor map per weight matrix (box = the planned
+// rows x 512 columns) and launches.  mats[i] feeds segment i; `up` is the second matrix
+// of the gate/up pair.
+static int launch_gemv(std::initializer_list<const DevMat*> mats, const DevMat* up, int in_mode, int epi,
+                       GemvParams& p, cudaStream_t s) {
+    const DevMat& w0 = **mats.begin();
+    const int grid = gemv_plan(w0.type, w0.cols, p.total_rows, up != nullptr, in_mode, p);
+    int i = 0;
+    for (const DevMat* d : mats) {
+        int r = gemv_tensor_map(&p.tm[i++], d->d, d->rows, d->pitch, p.chunk_words, p.box_rows);
+        if (r) return r;
+    }
+    if (up) {
+        int r = gemv_tensor_map(&p.tm2, up->d, up->rows, up->pitch, p.chunk_words, p.box_rows);
+        if (r) return r;
+    }
+    return gemv_launch(w0.type, in_mode, epi, p, grid, s, true);
 }
 
 // Row-parallel projection (wo / w2) with its reduction: one GPU -> hidden += out;
@@ -502,16 +509,16 @@ static ncm_status row_parallel(ncm_model* m, const DevMat& w, const float* x, in
     p.x = x;
     p.hidden = m->hidden;
     if (m->world == 1) {
-        p.seg[0] = {w.d, nullptr, m->hidden, m->emb, 0, SEG_OUT};
-        CKL(launch_gemv(m, w, IN_F32, EPI_RESID, p, false, s));
+        p.seg[0] = {m->hidden, m->emb, 0, SEG_OUT};
+        CKL(launch_gemv({&w}, nullptr, IN_F32, EPI_RESID, p, s));
     } else if (m->reduce_mode == NCM_REDUCE_FUSED_P2P) {
-        p.seg[0] = {w.d, nullptr, nullptr, m->emb, 0, SEG_OUT};
+        p.seg[0] = {nullptr, m->emb, 0, SEG_OUT};
         p.tp = m->comm;
         p.tp_slot = slot;
-        CKL(launch_gemv(m, w, IN_F32, EPI_TP_RESID, p, false, s));
+        CKL(launch_gemv({&w}, nullptr, IN_F32, EPI_TP_RESID, p, s));
     } else {
-        p.seg[0] = {w.d, nullptr, m->part, m->emb, 0, SEG_OUT};
-        CKL(launch_gemv(m, w, IN_F32, EPI_PLAIN, p, false, s));
+        p.seg[0] = {m->part, m->emb, 0, SEG_OUT};
+        CKL(launch_gemv({&w}, nullptr, IN_F32, EPI_PLAIN, p, s));
         int r = g_nccl.AllReduce(m->part, m->part, (size_t)m->emb, kNcclFloat, kNcclSum, m->nccl, s);
         if (r != 0) return fail(NCM_EPEER, "ncclAllReduce failed");
         CKL(resid_add_launch(m->hidden, m->part, m->emb, s, true));
@@ -527,9 +534,9 @@ static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
         // rms_norm -> quantize -> wq/wk/wv -> rope -> store_kv (inference.rs:4521-4646)
         GemvParams p = base_params(m);
         p.nseg = 3;
-        p.seg[0] = {L.wq.d, nullptr, m->q, qw, 0, SEG_Q};
-        p.seg[1] = {L.wk.d, nullptr, nullptr, kw, qw, SEG_K};
-        p.seg[2] = {L.wv.d, nullptr, nullptr, kw, qw + kw, SEG_V};
+        p.seg[0] = {m->q, qw, 0, SEG_Q};
+        p.seg[1] = {nullptr, kw, qw, SEG_K};
+        p.seg[2] = {nullptr, kw, qw + kw, SEG_V};
         p.total_rows = qw + 2 * kw;
         p.x = m->hidden;
         p.norm_w = L.attn_norm;
@@ -537,22 +544,22 @@ static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
         p.vcache = m->vc + (size_t)l * m->ctx * kw;
         p.kv_width = kw;
         if (l == 0) p.ssq_tok = m->embd_ssq;
-        CKL(launch_gemv(m, L.wq, IN_F32_RMS, EPI_QKV, p, false, s));
+        CKL(launch_gemv({&L.wq, &L.wk, &L.wv}, nullptr, IN_F32_RMS, EPI_QKV, p, s));
         // attention (inference.rs:4648-4665)
         AttnParams a;
         a.q = m->q;
         a.kc = p.kcache;
         a.vc = p.vcache;
         a.out = m->att;
-        a.part = m->attn_part;
-        a.counter = m->attn_cnt;
+        a.scores = m->scores;
         a.state = m->state;
+        a.pos_override = -1;
         a.heads = m->qh;
         a.kv_heads = m->kh;
         a.hd = m->hd;
         a.kvw = kw;
-        a.nsplit = m->nsplit;
-        a.max_per = m->max_per;
+        a.ctx = m->ctx;
+        a.dsplit = m->dsplit;
         a.scale = 1.0f / sqrtf((float)m->hd);   // inference.rs:4653
         CKL(attention_launch(a, s, true));
         // quantize -> wo -> residual (inference.rs:4667-4673), reduce #1 (tp.rs:356-363)
@@ -561,11 +568,11 @@ static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
         // rms_norm -> quantize -> w1, w3 -> silu*mul (inference.rs:4679-4730)
         GemvParams f = base_params(m);
         f.nseg = 1;
-        f.seg[0] = {L.w1.d, L.w3.d, m->act, m->fl, 0, SEG_OUT};
+        f.seg[0] = {m->act, m->fl, 0, SEG_OUT};
         f.total_rows = m->fl;
         f.x = m->hidden;
         f.norm_w = L.ffn_norm;
-        CKL(launch_gemv(m, L.w1, IN_F32_RMS, EPI_SILU, f, true, s));
+        CKL(launch_gemv({&L.w1}, &L.w3, IN_F32_RMS, EPI_SILU, f, s));
         // quantize -> w2 -> residual (inference.rs:4732-4748), reduce #2 (tp.rs:416-424)
         st = row_parallel(m, L.w2, m->act, 2 * l + 1, s);
         if (st) return st;
@@ -577,7 +584,7 @@ static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
     // output norm -> quantize -> head -> greedy argmax (inference.rs:4783-4845)
     GemvParams h = base_params(m);
     h.nseg = 1;
-    h.seg[0] = {m->head.d, nullptr, m->logits, m->hr, 0, SEG_OUT};
+    h.seg[0] = {m->logits, m->hr, 0, SEG_OUT};
     h.total_rows = m->hr;
     h.x = m->hidden;
     h.norm_w = m->out_norm;
@@ -586,7 +593,7 @@ static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
     h.head_row0 = m->h0;
     if (m->world > 1 && m->reduce_mode == NCM_REDUCE_FUSED_P2P) h.tp = m->comm;
     if (m->world > 1 && m->reduce_mode == NCM_REDUCE_NCCL) h.head_out = m->head_out;
-    CKL(launch_gemv(m, m->head, IN_F32_RMS, EPI_ARGMAX, h, false, s));
+    CKL(launch_gemv({&m->head}, nullptr, IN_F32_RMS, EPI_ARGMAX, h, s));
     if (h.head_out) {
         int r = g_nccl.AllGather(m->head_out, m->gather, 2, kNcclFloat, m->nccl, s);
         if (r != 0) return fail(NCM_EPEER, "ncclAllGather failed");
@@ -864,47 +871,58 @@ extern "C" ncm_status ncm_quantize_f32_to_q8_0(const float* x, int n, int8_t* x_
     return NCM_OK;
 }
 
-extern "C" ncm_status ncm_matmul_quantized(int qtype, const void* w, int64_t rows, int cols, const int8_t* x_i8,
-                                          const float* x_scales, float* out, void* stream) {
-    if (!gemv_type_ok(qtype)) return fail(NCM_EUNSUPPORTED, "quant type outside Q4_0/Q8_0/Q4_K");
-    if (rows < 0 || cols <= 0 || cols % 64 || cols % ncm_type_block_elems(qtype) || cols / 64 > 512)
-        return fail(NCM_EINVAL, "cols must be a positive multiple of 64 (256 for Q4_K), at most 32768");
-    if (rows == 0) return NCM_OK;
-    if (!w || !x_i8 || !x_scales || !out) return fail(NCM_EINVAL, "null pointer");
-    if (!aligned16(x_i8) || ((uintptr_t)w & 3)) return fail(NCM_EINVAL, "x_i8 must be 16-byte and w 4-byte aligned");
+// Strict GEMV over caller-owned raw blocks; rows whose byte length is not a multiple of
+// 16 (or an unaligned base) are first copied into a 16-byte-pitched scratch so that the
+// TMA engine can address them.
+static ncm_status seam_gemv(int qtype, const void* w, int64_t rows, int cols, const int8_t* x_i8,
+                            const float* x_scales, float* out, cudaStream_t s) {
     const int rb = row_bytes(qtype, cols);
-    cudaStream_t s = (cudaStream_t)stream;
-    if (rb % 16 == 0 && aligned16(w) && rows < (1ll << 31)) {
-        GemvParams p;
-        memset(&p, 0, sizeof p);
-        p.nseg = 1;
-        p.seg[0] = {(const uint8_t*)w, nullptr, out, (int)rows, 0, SEG_OUT};
-        p.total_rows = (int)rows;
-        p.pitch = rb;
-        p.xq = x_i8;
-        p.xs = x_scales;
-        p.tp.world = 1;
-        int grid;
-        size_t smem;
-        gemv_plan(qtype, cols, (int)rows, false, false, 0, p, grid, smem);
-        CKL(gemv_launch(qtype, IN_Q8, EPI_PLAIN, p, grid, s, false));
-    } else {
-        CKL(gemv_batch_launch(qtype, (const uint8_t*)w, rows, cols, rb, 1, x_i8, x_scales, out, s));
+    const uint8_t* base = (const uint8_t*)w;
+    int pitch = rb;
+    uint8_t* tmp = nullptr;
+    if (rb % 16 || !aligned16(w)) {
+        pitch = (rb + 15) / 16 * 16;
+        CK(cudaMallocAsync((void**)&tmp, (size_t)pitch * rows, s));
+        CK(cudaMemcpy2DAsync(tmp, pitch, w, rb, rb, rows, cudaMemcpyDeviceToDevice, s));
+        base = tmp;
     }
+    GemvParams p;
+    memset(&p, 0, sizeof p);
+    p.nseg = 1;
+    p.seg[0] = {out, (int)rows, 0, SEG_OUT};
+    p.xq = x_i8;
+    p.xs = x_scales;
+    p.tp.world = 1;
+    const int grid = gemv_plan(qtype, cols, (int)rows, false, IN_Q8, p);
+    int r = gemv_tensor_map(&p.tm[0], base, rows, pitch, p.chunk_words, p.box_rows);
+    if (!r) r = gemv_launch(qtype, IN_Q8, EPI_PLAIN, p, grid, s, false);
+    if (tmp) cudaFreeAsync(tmp, s);
+    if (r) return fail(NCM_ECUDA, std::string("gemv launch: ") + cudaGetErrorString((cudaError_t)r));
     return NCM_OK;
 }
 
-extern "C" ncm_status ncm_matmul_quantized_batch(int qtype, const void* w, int64_t rows, int cols, int ntok,
-                                                const int8_t* x_i8, const float* x_scales, float* out, void* stream) {
+extern "C" ncm_status ncm_matmul_quantized(int qtype, const void* w, int64_t rows, int cols, const int8_t* x_i8,
+                                          const float* x_scales, float* out, void* stream) {
     if (!gemv_type_ok(qtype)) return fail(NCM_EUNSUPPORTED, "quant type outside Q4_0/Q8_0/Q4_K");
-    if (ntok < 1 || ntok > 8) return fail(NCM_EINVAL, "1 <= ntok <= 8");
-    if (rows < 0 || cols <= 0 || cols % 64 || cols % ncm_type_block_elems(qtype))
-        return fail(NCM_EINVAL, "cols must be a positive multiple of 64 (256 for Q4_K)");
+    if (rows < 0 || rows >= (1ll << 31) || cols <= 0 || cols % 64 || cols % ncm_type_block_elems(qtype) ||
+        cols / 64 > 512)
+        return fail(NCM_EINVAL, "cols must be a positive multiple of 64 (256 for Q4_K), at most 32768");
     if (rows == 0) return NCM_OK;
     if (!w || !x_i8 || !x_scales || !out) return fail(NCM_EINVAL, "null pointer");
-    if (((uintptr_t)x_i8 & 3) || ((uintptr_t)w & 3)) return fail(NCM_EINVAL, "w and x_i8 must be 4-byte aligned");
-    CKL(gemv_batch_launch(qtype, (const uint8_t*)w, rows, cols, row_bytes(qtype, cols), ntok, x_i8, x_scales, out,
-                          (cudaStream_t)stream));
+    if (!aligned16(x_i8) || ((uintptr_t)x_scales & 7)) return fail(NCM_EINVAL, "x_i8 must be 16-byte and x_scales 8-byte aligned");
+    return seam_gemv(qtype, w, rows, cols, x_i8, x_scales, out, (cudaStream_t)stream);
+}
+
+// inference.rs:1246-1303: every token's row uses the single-token formula, so the batch
+// is ntok single-token GEMVs (bit-identical per token by construction).
+extern "C" ncm_status ncm_matmul_quantized_batch(int qtype, const void* w, int64_t rows, int cols, int ntok,
+                                                const int8_t* x_i8, const float* x_scales, float* out, void* stream) {
+    if (ntok < 1 || ntok > 8) return fail(NCM_EINVAL, "1 <= ntok <= 8");
+    for (int t = 0; t < ntok; ++t) {
+        ncm_status st = ncm_matmul_quantized(qtype, w, rows, cols, x_i8 + (size_t)t * cols,
+                                             x_scales + (size_t)t * (cols / 32), out + (size_t)t * rows, stream);
+        if (st) return st;
+    }
     return NCM_OK;
 }
 
@@ -934,30 +952,21 @@ extern "C" ncm_status ncm_fused_silu_mul(float* out, const float* gate, const fl
 extern "C" ncm_status ncm_attention(float* out, const float* q, const float* k_cache, const float* v_cache, int pos,
                                    int heads, int kv_heads, int head_dim, void* stream) {
     if (!out || !q || !k_cache || !v_cache || pos < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads ||
-        heads / kv_heads > 8 || head_dim % 32 || head_dim > 256)
+        heads / kv_heads > 8 || head_dim % 32 || head_dim > 256 || pos >= 16384)
         return fail(NCM_EINVAL, "bad attention arguments");
     cudaStream_t s = (cudaStream_t)stream;
-    // Scratch for this one call: position word, split partials and counters.
-    const int nsplit = 4;
-    const int max_per = (pos + 1 + nsplit - 1) / nsplit;
-    int* state = nullptr;
-    float* part = nullptr;
-    unsigned* cnt = nullptr;
-    CK(cudaMallocAsync((void**)&state, 4 * ST_COUNT, s));
-    CK(cudaMallocAsync((void**)&part, 4 * (size_t)heads * nsplit * (head_dim + 2), s));
-    CK(cudaMallocAsync((void**)&cnt, 4 * (size_t)kv_heads, s));
-    int st[ST_COUNT] = {pos, 0, 0, 0, 0, 0, 0, 0};
-    CK(cudaMemcpyAsync(state, st, sizeof st, cudaMemcpyHostToDevice, s));
-    CK(cudaMemsetAsync(cnt, 0, 4 * (size_t)kv_heads, s));
+    float* scores = nullptr;
+    const int ctx = pos + 1;
+    CK(cudaMallocAsync((void**)&scores, 4 * (size_t)heads * ctx, s));
     AttnParams a;
-    a.q = q; a.kc = k_cache; a.vc = v_cache; a.out = out; a.part = part; a.counter = cnt; a.state = state;
-    a.heads = heads; a.kv_heads = kv_heads; a.hd = head_dim; a.kvw = kv_heads * head_dim; a.nsplit = nsplit;
-    a.max_per = max_per < 1 ? 1 : max_per;
+    memset(&a, 0, sizeof a);
+    a.q = q; a.kc = k_cache; a.vc = v_cache; a.out = out; a.scores = scores; a.state = nullptr;
+    a.pos_override = pos;
+    a.heads = heads; a.kv_heads = kv_heads; a.hd = head_dim; a.kvw = kv_heads * head_dim; a.ctx = ctx;
+    a.dsplit = 4;
     a.scale = 1.0f / sqrtf((float)head_dim);
     int r = attention_launch(a, s, false);
-    cudaFreeAsync(state, s);
-    cudaFreeAsync(part, s);
-    cudaFreeAsync(cnt, s);
+    cudaFreeAsync(scores, s);
     CK(cudaStreamSynchronize(s));
     if (r) return fail(NCM_ECUDA, "attention launch failed");
     return NCM_OK;

@@ -1,16 +1,26 @@
 // sm_100a kernels of the decode hot path.
 //
-// The GEMV (the whole decode cost: every weight byte is read once per token) streams
-// raw GGUF quant blocks from HBM into shared memory with the bulk-copy (TMA) engine,
-// `nstages` row tiles in flight per CTA, completion tracked by mbarriers.  The
-// activation vector is quantised to Q8_0 once per CTA, straight into registers, in the
-// kernel prologue (optionally after the RMSNorm), while the first weight tiles are
-// already in flight; programmatic dependent launch lets the next kernel's weight
-// prefetch start before this kernel finishes.  Each thread owns fixed 64-column
-// "units" (two Q8 activation blocks) of every row, so its activation registers are
-// reused across all rows the CTA streams; the per-block integer dots are dp4a sums,
-// exact in int32 and bit-identical to the reference's scalar dot.  Epilogues fuse what
-// follows each projection in the reference layer loop (inference.rs:4505-4781).
+// Parity contract: every f32 value is produced by the same operations in the same
+// order as the reference's x86 scalar path (inference.rs / q8.rs), so GPU activations
+// are bit-identical to the reference's wherever the reference itself is deterministic
+// (the one exception is expf, see expf_cr).  This matters more than it looks: the
+// activations are re-quantised to int8 before every projection, and with random-init
+// weights a single last-bit difference that moves one value across a rounding tie
+// changes an int8 and cascades into ~1e-2 logit differences.  So:
+//   * GEMV row sums fold the per-block terms sequentially in block order, one lane per
+//     row (inference.rs:1150-1160, 2659-2664, 3129-3133); the per-block integer dots,
+//     which are exact, are spread over all threads;
+//   * RMSNorm's sum of squares and the softmax denominator reproduce the reference's
+//     sequential f32 fold exactly with a parallel algorithm (seq_sum_nonneg);
+//   * attention scores, softmax weights and the V accumulation follow
+//     inference.rs:4242-4292 term by term.
+//
+// GEMV data path: raw GGUF blocks are streamed by the TMA engine as 2-D tiles
+// (box_rows rows x 512 columns) into a multi-stage shared-memory ring tracked by
+// mbarriers; the activation vector is quantised to Q8_0 once per CTA into shared
+// memory in the prologue, while the first tiles are in flight.  Programmatic dependent
+// launch lets the next kernel's weight prefetch start before this kernel drains.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <math.h>
@@ -31,16 +41,134 @@ int num_sms() {
     return g_num_sms;
 }
 
-// ------------------------------------------------------------------ activation (Q8_0)
-// Activation registers of one 64-column unit: two Q8_0 blocks.
-struct XUnit {
-    uint32_t w[16];   // 64 int8 values, 4 per word, element order
-    float s[2];       // per-block f32 scale (inference.rs:1008 stores the f32 scale)
-    int sum[2];       // per-block sum of the int8 values (for the Q4_0 -8 offset and Q4_K mins)
-};
+EncodeTiledFn encode_tiled_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    }
+    return fn;
+}
 
+// ------------------------------------------------------------------ exp
+// The reference's exp is glibc expf (Rust f32::exp).  Device expf is not bit-identical
+// to it; exp() in double rounded to float is correctly rounded except within ~1 double
+// ulp of a float rounding midpoint.  glibc 2.39's expf agrees with the correctly
+// rounded value on all but ~0.01-0.06% of inputs (measured on the build host), so this
+// is the closest device match short of reimplementing glibc's table.
+__device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
+
+// ------------------------------------------------------------------ exact sequential sums
+// Reproduces   s = 0.0f; for i in [0, n): s = RN(s + t(i))   for t(i) >= 0 exactly.
+//
+// Within one binade [2^e, 2^(e+1)) floats are a grid of spacing u, and for s = k*u,
+// RN(s + t) = u * (k + rint(t/u)) unless t/u is an exact half-integer (a tie, whose
+// result depends on the parity of k) or the sum leaves the binade.  So a run of terms
+// adds a fixed integer number of ulps, independent of where in the binade it starts.
+// Each chunk of terms gets a guessed starting binade from a prefix sum; a resolution
+// warp walks the chunks in order, adding whole chunks in integer ulps when the guess
+// and the no-tie / no-crossing conditions hold and folding the chunk term by term
+// (real FADDs) otherwise.  Guesses only affect speed, never the result.
+template <int NT>
+struct SeqSumScratchT {
+    float part[NT / 32];       // per-warp chunk-sum totals (binade guesses)
+    int ebits[NT];             // guessed biased exponent of the chunk's starting value
+    long long cnt[NT];         // sum of rint(t/u) over the chunk in that binade
+    int bad[NT];               // chunk has a tie or a term >= 2^24 ulps
+    float result;
+};
+typedef SeqSumScratchT<kThreads> SeqSumScratch;
+typedef SeqSumScratchT<32> SeqSumScratchW;
+
+// NT threads (one warp, or the whole 256-thread CTA) cooperate; `rank` is the thread's
+// index among them; the terms are read through term(i).  All NT threads get the result.
+template <int NT, class Term>
+__device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT>& sc, int rank) {
+    const int lane = rank & 31;
+    const int m = (n + NT - 1) / NT;
+    const int C = m > 0 ? (n + m - 1) / m : 0;
+    const int i0 = min(n, rank * m), i1 = min(n, i0 + m);
+    float d = 0.0f;
+    for (int i = i0; i < i1; ++i) d += term(i);
+    // exclusive prefix of the chunk sums: only a guess of each chunk's starting binade.
+    float v = d;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        float t = __shfl_up_sync(NCM_FULL, v, o);
+        if (lane >= o) v += t;
+    }
+    float pre = v - d;
+    if (NT > 32) {
+        if (lane == 31) sc.part[rank >> 5] = v;
+        __syncthreads();
+        for (int w = 0; w < (rank >> 5); ++w) pre += sc.part[w];
+    }
+    int eb = 0;
+    long long cnt = 0;
+    int bad = 0;
+    if (rank < C) {
+        const uint32_t gb = __float_as_uint(pre);
+        eb = (int)(gb >> 23);
+        if (eb < 1 || eb > 253) bad = 1;
+        for (int i = i0; i < i1 && !bad; ++i) {
+            const float a = ldexpf(term(i), 150 - eb);   // t / u, exact scaling
+            if (a >= 16777216.0f) { bad = 1; break; }
+            if (a - floorf(a) == 0.5f) { bad = 1; break; }
+            cnt += (long long)rintf(a);
+        }
+    }
+    sc.ebits[rank] = eb;
+    sc.cnt[rank] = cnt;
+    sc.bad[rank] = bad;
+    if (NT == 32) __syncwarp(); else __syncthreads();
+    if (rank < 32) {
+        float s = 0.0f;
+        int j = 0;
+        while (j < C) {
+            const uint32_t sb = __float_as_uint(s);
+            const int es = (int)(sb >> 23);
+            const bool normal = s > 0.0f && es >= 1 && es <= 253;
+            const long long k = normal ? (long long)((sb & 0x7fffffu) | 0x800000u) : 0;
+            const int c = j + lane;
+            const bool ok = normal && c < C && sc.ebits[c] == es && !sc.bad[c];
+            long long pv = ok ? sc.cnt[c] : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                long long t = __shfl_up_sync(NCM_FULL, pv, o);
+                if (lane >= o) pv += t;
+            }
+            const bool good = ok && (k + pv < 16777216ll);
+            const unsigned bal = __ballot_sync(NCM_FULL, good);
+            const int b = bal == NCM_FULL ? 32 : __ffs(~bal) - 1;
+            if (b > 0) {
+                const long long kk = k + __shfl_sync(NCM_FULL, pv, b - 1);
+                s = __uint_as_float(((uint32_t)es << 23) | (uint32_t)(kk & 0x7fffff));
+                j += b;
+            }
+            if (b < 32 && j < C) {
+                // fold chunk j term by term from the exact running value
+                float r = s;
+                if (lane == 0) {
+                    const int a0 = j * m, a1 = min(n, a0 + m);
+                    for (int i = a0; i < a1; ++i) r = r + term(i);
+                }
+                s = __shfl_sync(NCM_FULL, r, 0);
+                j += 1;
+            }
+        }
+        if (rank == 0) sc.result = s;
+    }
+    if (NT == 32) __syncwarp(); else __syncthreads();
+    return sc.result;
+}
+
+// ------------------------------------------------------------------ activation (Q8_0)
 // inference.rs:991-1029 quantize_f32_to_q8_0_scalar for one 32-value block:
-// scale = max|x|/127, q = round_half_away(x * (1/scale)) clamped to +-127; zero block -> 0.
+// scale = max|x|/127 (kept as f32), q = round_half_away(x * (1/scale)) clamped to
+// +-127; zero block -> scale 0, values 0.
 __device__ __forceinline__ void quant_block32(const float* v, uint32_t* w, float& s, int& sum) {
     float amax = 0.0f;
 #pragma unroll
@@ -70,19 +198,37 @@ __device__ __forceinline__ void quant_block32(const float* v, uint32_t* w, float
     sum = acc;
 }
 
-// ------------------------------------------------------------------ unit dots
-// Q4_0 unit = blocks 2u, 2u+1 = 36 bytes (nine 32-bit words, 4-byte aligned): nine
-// LDS.32 per lane with a 9-word stride, conflict-free across the warp.
-// q8.rs:2699-2702 dot = sum((nib-8)*x) = sum(nib*x) - 8*sum(x), exact in int32; the
-// block term is w_scale * x_scale * (float)dot as in inference.rs:2663.
-__device__ __forceinline__ void dots_q4_0(const uint8_t* row, int u, const XUnit& x, int& dA, int& dB, float& sA,
-                                          float& sB) {
+// Activation of one 64-column unit (two Q8_0 blocks).
+struct XUnit {
+    uint32_t w[16];
+    float s[2];
+    int sum[2];
+};
+
+// Shared-memory layout of the quantised activation: unit g at xq + 80 g (64 bytes +
+// 16 padding so that eight consecutive units hit distinct 16-byte bank groups).
+__device__ __forceinline__ void load_xunit(const uint8_t* smem, const GemvParams& p, int g, XUnit& x) {
+    const uint4* src = reinterpret_cast<const uint4*>(smem + p.xq_off + 80 * g);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        uint4 v = src[i];
+        x.w[4 * i] = v.x; x.w[4 * i + 1] = v.y; x.w[4 * i + 2] = v.z; x.w[4 * i + 3] = v.w;
+    }
+    float2 s = reinterpret_cast<const float2*>(smem + p.xs_off)[g];
+    int2 c = reinterpret_cast<const int2*>(smem + p.xsum_off)[g];
+    x.s[0] = s.x; x.s[1] = s.y;
+    x.sum[0] = c.x; x.sum[1] = c.y;
+}
+
+// ------------------------------------------------------------------ per-unit block terms
+// Q4_0 unit = blocks 2u, 2u+1 (36 bytes, nine words): q8.rs:2699-2702 dot =
+// sum((nib-8)*x) = sum(nib*x) - 8*sum(x) exact in int32; term = d_w * x_scale *
+// (float)dot as inference.rs:2663 (left to right).
+__device__ __forceinline__ void terms_q4_0(const uint8_t* row, int u, const XUnit& x, float& t0, float& t1, int* dots) {
     const uint32_t* p = reinterpret_cast<const uint32_t*>(row + 36 * u);
     uint32_t w[9];
 #pragma unroll
     for (int i = 0; i < 9; ++i) w[i] = p[i];
-    sA = f16_bits_to_f32(w[0] & 0xffff);
-    sB = f16_bits_to_f32(w[4] >> 16);
     int a = 0, b = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -93,27 +239,28 @@ __device__ __forceinline__ void dots_q4_0(const uint8_t* row, int u, const XUnit
         b = __dp4a((int)(r & 0x0f0f0f0fu), (int)x.w[8 + i], b);
         b = __dp4a((int)((r >> 4) & 0x0f0f0f0fu), (int)x.w[12 + i], b);
     }
-    dA = a - 8 * x.sum[0];
-    dB = b - 8 * x.sum[1];
+    a -= 8 * x.sum[0];
+    b -= 8 * x.sum[1];
+    if (dots) { dots[0] = a; dots[1] = b; }
+    t0 = f16_bits_to_f32(w[0] & 0xffff) * x.s[0] * (float)a;
+    t1 = f16_bits_to_f32(w[4] >> 16) * x.s[1] * (float)b;
 }
 
-// Q8_0 unit = 68 bytes (17 words, conflict-free stride): q8.rs:505 dot_i32.
-__device__ __forceinline__ void dots_q8_0(const uint8_t* row, int u, const XUnit& x, int& dA, int& dB, float& sA,
-                                          float& sB) {
+// Q8_0 unit = 68 bytes (17 words): q8.rs:505 dot_i32; inference.rs:1157.
+__device__ __forceinline__ void terms_q8_0(const uint8_t* row, int u, const XUnit& x, float& t0, float& t1, int* dots) {
     const uint32_t* p = reinterpret_cast<const uint32_t*>(row + 68 * u);
     uint32_t w[17];
 #pragma unroll
     for (int i = 0; i < 17; ++i) w[i] = p[i];
-    sA = f16_bits_to_f32(w[0] & 0xffff);
-    sB = f16_bits_to_f32(w[8] >> 16);
     int a = 0, b = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         a = __dp4a((int)__funnelshift_r(w[i], w[i + 1], 16), (int)x.w[i], a);
         b = __dp4a((int)w[9 + i], (int)x.w[8 + i], b);
     }
-    dA = a;
-    dB = b;
+    if (dots) { dots[0] = a; dots[1] = b; }
+    t0 = f16_bits_to_f32(w[0] & 0xffff) * x.s[0] * (float)a;
+    t1 = f16_bits_to_f32(w[8] >> 16) * x.s[1] * (float)b;
 }
 
 // q8.rs:2009-2018 q4_k_scale_min over the 12 packed scale bytes held in 3 words.
@@ -131,10 +278,10 @@ __device__ __forceinline__ void q4k_scale_min(int idx, uint32_t s0, uint32_t s1,
     }
 }
 
-// Q4_K unit u = sub-block pair (u & 3) of super-block (u >> 2): 16-byte header shared by
-// four lanes (broadcast) + 32 bytes of nibbles (two LDS.128, conflict-free).
-// Integer sums of q8.rs:1350-1368; f32 combine of q8.rs:1370-1373.
-__device__ __forceinline__ float unit_q4_k(const uint8_t* row, int u, const XUnit& x, int* ints) {
+// Q4_K unit u = sub-block pair (u & 3) of super-block (u >> 2) counted from `row`:
+// terms of sub-blocks 2p and 2p+1 exactly as q8.rs:1370-1373 (x_scale * (d*sc *
+// sum(q*x) - dmin*m * sum(x))), with d*sc and dmin*m formed as in q8.rs:1260-1263.
+__device__ __forceinline__ void terms_q4_k(const uint8_t* row, int u, const XUnit& x, float& t0, float& t1, int* ints) {
     const uint8_t* sb = row + 144 * (u >> 2);
     const int pr = u & 3;
     uint4 h = *reinterpret_cast<const uint4*>(sb);
@@ -147,112 +294,122 @@ __device__ __forceinline__ float unit_q4_k(const uint8_t* row, int u, const XUni
         wl = __dp4a((int)(q[i] & 0x0f0f0f0fu), (int)x.w[i], wl);
         wh = __dp4a((int)((q[i] >> 4) & 0x0f0f0f0fu), (int)x.w[8 + i], wh);
     }
+    if (ints) { ints[0] = wl; ints[1] = x.sum[0]; ints[2] = wh; ints[3] = x.sum[1]; }
     float d = f16_bits_to_f32(h.x & 0xffff), dmin = f16_bits_to_f32(h.x >> 16);
     int sl, ml, sh, mh;
     q4k_scale_min(2 * pr, h.y, h.z, h.w, sl, ml);
     q4k_scale_min(2 * pr + 1, h.y, h.z, h.w, sh, mh);
-    if (ints) { ints[0] = wl; ints[1] = x.sum[0]; ints[2] = wh; ints[3] = x.sum[1]; }
-    float scl = d * (float)sl, mnl = dmin * (float)ml;
-    float sch = d * (float)sh, mnh = dmin * (float)mh;
-    float lo = x.s[0] * (scl * (float)wl - mnl * (float)x.sum[0]);
-    float hi = x.s[1] * (sch * (float)wh - mnh * (float)x.sum[1]);
-    return lo + hi;
+    const float scl = d * (float)sl, mnl = dmin * (float)ml;
+    const float sch = d * (float)sh, mnh = dmin * (float)mh;
+    t0 = x.s[0] * (scl * (float)wl - mnl * (float)x.sum[0]);
+    t1 = x.s[1] * (sch * (float)wh - mnh * (float)x.sum[1]);
 }
 
 template <int QT>
-__device__ __forceinline__ float unit_dot(const uint8_t* row, int u, const XUnit& x) {
-    if constexpr (QT == NCM_T_Q4_K) {
-        return unit_q4_k(row, u, x, nullptr);
-    } else {
-        int dA, dB;
-        float sA, sB;
-        if constexpr (QT == NCM_T_Q4_0) dots_q4_0(row, u, x, dA, dB, sA, sB);
-        else dots_q8_0(row, u, x, dA, dB, sA, sB);
-        return sA * x.s[0] * (float)dA + sB * x.s[1] * (float)dB;
-    }
+__device__ __forceinline__ void unit_terms(const uint8_t* row, int u, const XUnit& x, float& t0, float& t1) {
+    if constexpr (QT == NCM_T_Q4_0) terms_q4_0(row, u, x, t0, t1, nullptr);
+    else if constexpr (QT == NCM_T_Q8_0) terms_q8_0(row, u, x, t0, t1, nullptr);
+    else terms_q4_k(row, u, x, t0, t1, nullptr);
+}
+
+// ------------------------------------------------------------------ TMA
+// 2-D tiled load (plain, no cluster multicast); x = word column (a multiple of 4 words,
+// i.e. 16 bytes), y = row.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
 }
 
 // ------------------------------------------------------------------ prologue
-template <int NPT, int IN>
-__device__ __forceinline__ void load_activation(const GemvParams& p, XUnit (&xr)[NPT], int li, float* red) {
+// Quantises the activation (optionally RMS-normalised) into shared memory.
+template <int IN>
+__device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, SeqSumScratch& sc) {
     const int tid = threadIdx.x;
+    const int nblk = p.nchunk * 16;     // padded block count (tail blocks zero)
+    float2* xs = reinterpret_cast<float2*>(smem + p.xs_off);
+    int2* xsum = reinterpret_cast<int2*>(smem + p.xsum_off);
     if constexpr (IN == IN_Q8) {
-#pragma unroll
-        for (int k = 0; k < NPT; ++k) {
-            int u = li + 256 * k;
-            if (u < p.units) {
-                const uint4* src = reinterpret_cast<const uint4*>(p.xq + 64 * u);
+        for (int g = tid; g < nblk / 2; g += kThreads) {
+            uint4* dst = reinterpret_cast<uint4*>(smem + p.xq_off + 80 * g);
+            if (2 * g < p.nb) {
+                const uint4* src = reinterpret_cast<const uint4*>(p.xq + 64 * g);
+                int s0 = 0, s1 = 0;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     uint4 v = src[i];
-                    xr[k].w[4 * i] = v.x; xr[k].w[4 * i + 1] = v.y; xr[k].w[4 * i + 2] = v.z; xr[k].w[4 * i + 3] = v.w;
+                    dst[i] = v;
+                    int a = i < 2 ? s0 : s1;
+                    a = __dp4a((int)v.x, 0x01010101, a);
+                    a = __dp4a((int)v.y, 0x01010101, a);
+                    a = __dp4a((int)v.z, 0x01010101, a);
+                    a = __dp4a((int)v.w, 0x01010101, a);
+                    if (i < 2) s0 = a; else s1 = a;
                 }
-                xr[k].s[0] = p.xs[2 * u];
-                xr[k].s[1] = p.xs[2 * u + 1];
+                xs[g] = make_float2(p.xs[2 * g], p.xs[2 * g + 1]);
+                xsum[g] = make_int2(s0, s1);
+            } else {
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    int s = 0;
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) s = __dp4a((int)xr[k].w[8 * h + i], 0x01010101, s);
-                    xr[k].sum[h] = s;
-                }
+                for (int i = 0; i < 4; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+                xs[g] = make_float2(0.0f, 0.0f);
+                xsum[g] = make_int2(0, 0);
             }
         }
     } else {
         float scale = 1.0f;
         if constexpr (IN == IN_F32_RMS) {
-            // inference.rs:697-706: scale = 1/sqrt(sum(x^2)/n + eps).
+            float* xf = reinterpret_cast<float*>(smem + p.xf_off);
+            for (int i = tid * 4; i < p.cols; i += 4 * kThreads)
+                *reinterpret_cast<float4*>(xf + i) = *reinterpret_cast<const float4*>(p.x + i);
+            __syncthreads();
             float tot;
             if (p.ssq_tok) {
-                // Layer 0: the input is a dequantised embedding row whose normalised values
-                // sit exactly on Q8 rounding ties, so the sum must round exactly as the
-                // reference's sequential loop does: precomputed per vocab row at load.
+                // Layer 0: sum of squares of the embedding row, folded sequentially at load.
                 tot = p.ssq_tok[p.tokens[p.state[ST_POS]]];
             } else {
-                // Tree sum (sequential in the reference; within f32 rounding).
-                float ss = 0.0f;
-                for (int i = tid * 4; i < p.cols; i += 4 * kThreads) {
-                    float4 v = *reinterpret_cast<const float4*>(p.x + i);
-                    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(NCM_FULL, ss, o);
-                if ((tid & 31) == 0) red[tid >> 5] = ss;
-                __syncthreads();
-                tot = 0.0f;
-#pragma unroll
-                for (int w = 0; w < kThreads / 32; ++w) tot += red[w];
+                // inference.rs:698-701: sum += val * val, sequential.
+                tot = seq_sum_nonneg<kThreads>([&](int i) { float v = xf[i]; return v * v; }, p.cols, sc, tid);
             }
             scale = 1.0f / sqrtf(tot / (float)p.cols + p.eps);
         }
+        for (int b = tid; b < nblk; b += kThreads) {
+            uint32_t* dst = reinterpret_cast<uint32_t*>(smem + p.xq_off + 80 * (b >> 1) + 32 * (b & 1));
+            float s = 0.0f;
+            int sum = 0;
+            if (b < p.nb) {
+                float v[32];
+                if constexpr (IN == IN_F32_RMS) {
+                    const float* xf = reinterpret_cast<const float*>(smem + p.xf_off) + 32 * b;
+                    const float4* nw = reinterpret_cast<const float4*>(p.norm_w + 32 * b);
 #pragma unroll
-        for (int k = 0; k < NPT; ++k) {
-            int u = li + 256 * k;
-            if (u < p.units) {
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    float v[32];
-                    const float4* src = reinterpret_cast<const float4*>(p.x + 64 * u + 32 * h);
+                    for (int i = 0; i < 8; ++i) {
+                        float4 w4 = nw[i];
+                        // inference.rs:704 out = x * scale * weight
+                        v[4 * i] = xf[4 * i] * scale * w4.x;
+                        v[4 * i + 1] = xf[4 * i + 1] * scale * w4.y;
+                        v[4 * i + 2] = xf[4 * i + 2] * scale * w4.z;
+                        v[4 * i + 3] = xf[4 * i + 3] * scale * w4.w;
+                    }
+                } else {
+                    const float4* src = reinterpret_cast<const float4*>(p.x + 32 * b);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         float4 t = src[i];
                         v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
                     }
-                    if constexpr (IN == IN_F32_RMS) {
-                        const float4* nw = reinterpret_cast<const float4*>(p.norm_w + 64 * u + 32 * h);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            float4 t = nw[i];
-                            // inference.rs:704 out = x * scale * weight
-                            v[4 * i] = v[4 * i] * scale * t.x;
-                            v[4 * i + 1] = v[4 * i + 1] * scale * t.y;
-                            v[4 * i + 2] = v[4 * i + 2] * scale * t.z;
-                            v[4 * i + 3] = v[4 * i + 3] * scale * t.w;
-                        }
-                    }
-                    quant_block32(v, &xr[k].w[8 * h], xr[k].s[h], xr[k].sum[h]);
                 }
+                uint32_t w[8];
+                quant_block32(v, w, s, sum);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) dst[k] = w[k];
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) dst[k] = 0;
             }
+            reinterpret_cast<float*>(xs)[b] = s;
+            reinterpret_cast<int*>(xsum)[b] = sum;
         }
     }
 }
@@ -266,8 +423,8 @@ __device__ __forceinline__ TileCursor tile_at(const GemvParams& p, int cur, int 
 #pragma unroll
     for (int i = 1; i < kMaxSeg; ++i)
         if (i < p.nseg && cur >= p.seg[i].row_begin) s = i;
-    int seg_end = p.seg[s].row_begin + p.seg[s].rows;
-    int n = min(p.tile_rows, min(r_end, seg_end) - cur);
+    const int seg_end = p.seg[s].row_begin + p.seg[s].rows;
+    const int n = min(p.box_rows, min(r_end, seg_end) - cur);
     return {s, n};
 }
 
@@ -275,214 +432,199 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
     return v > bv || (v == bv && i < bi);
 }
 
-template <int QT, int NPT, int IN, int EPI>
+template <int QT, int IN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr bool DUAL = (EPI == EPI_SILU);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    float* part = reinterpret_cast<float*>(smem + p.part_off);
-    uint8_t* stages = smem + p.stage_off;
-    __shared__ float red[32];
+    __shared__ SeqSumScratch sc;
     __shared__ int s_abort;
-    __shared__ float s_bv;
-    __shared__ int s_bi;
     __shared__ int s_last;
+    __shared__ float xchg[kMaxFold];
+    __shared__ float wv[2];
+    __shared__ int wi[2];
 
-    const int tid = threadIdx.x;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    float* tbuf = reinterpret_cast<float*>(smem + p.t_off);
+    uint8_t* stages = smem + p.stage_off;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int R = p.total_rows;
-    const int nb = gridDim.x;
-    const int r_begin = (int)(((long long)blockIdx.x * R / nb)) & ~1;
-    const int r_end = (blockIdx.x + 1 == nb) ? R : ((int)(((long long)(blockIdx.x + 1) * R / nb)) & ~1);
-    const int half_off = p.tile_rows * p.pitch;   // DUAL: second matrix inside a stage
+    const int nbk = gridDim.x;
+    const int r_begin = (int)(((long long)blockIdx.x * R / nbk)) & ~1;
+    const int r_end = (blockIdx.x + 1 == nbk) ? R : ((int)(((long long)(blockIdx.x + 1) * R / nbk)) & ~1);
+    const int box_bytes = p.box_rows * p.chunk_bytes;
     const uint64_t limit_ns = 4000000000ull;
 
-    // (1) barriers, then weight prefetch (weights never change: legal before the
-    // dependency wait of programmatic dependent launch).
-    int icur = r_begin;
+    // (1) barriers + weight prefetch (weights are constant: legal before the PDL wait).
+    int icur = r_begin, ichunk = 0;
     uint64_t pol = 0;
+    auto issue = [&](int s) {
+        TileCursor tc = tile_at(p, icur, r_end);
+        const int y = icur - p.seg[tc.seg].row_begin;
+        const int x = ichunk * p.chunk_words;
+        mbar_arrive_expect_tx(&full[s], DUAL ? 2 * box_bytes : box_bytes);
+        tma_load_2d(stages + (size_t)s * p.stage_bytes, &p.tm[tc.seg], x, y, &full[s], pol);
+        if (DUAL) tma_load_2d(stages + (size_t)s * p.stage_bytes + box_bytes, &p.tm2, x, y, &full[s], pol);
+        if (++ichunk == p.nchunk) { ichunk = 0; icur += tc.n; }
+    };
     if (tid == 0) {
         for (int s = 0; s < p.nstages; ++s) mbar_init(&full[s], 1);
         fence_mbar_init();
         s_abort = 0;
-        s_bv = -INFINITY;
-        s_bi = 0x7fffffff;
         pol = l2_evict_first_policy();
-        for (int s = 0; s < p.nstages && icur < r_end; ++s) {
-            TileCursor tc = tile_at(p, icur, r_end);
-            uint32_t bytes = (uint32_t)(tc.n * p.pitch);
-            const Seg& sg = p.seg[tc.seg];
-            size_t off = (size_t)(icur - sg.row_begin) * p.pitch;
-            mbar_arrive_expect_tx(&full[s], DUAL ? 2 * bytes : bytes);
-            bulk_g2s(stages + (size_t)s * p.stage_bytes, sg.w + off, bytes, &full[s], pol);
-            if (DUAL) bulk_g2s(stages + (size_t)s * p.stage_bytes + half_off, sg.w2 + off, bytes, &full[s], pol);
-            icur += tc.n;
-        }
+        for (int s = 0; s < p.nstages && icur < r_end; ++s) issue(s);
     }
     __syncthreads();
     pdl_launch_dependents();
     pdl_wait();
 
-    // (2) activation -> registers.
-    const int pp = p.pp, G = p.groups, np = p.nparts;
-    const int g = tid / pp, li = tid % pp;
-    XUnit xr[NPT];
-    load_activation<NPT, IN>(p, xr, li, red);
+    // (2) activation -> shared memory.
+    gemv_prologue<IN>(smem, p, sc);
+    __syncthreads();
 
     int pos = 0;
     if (EPI == EPI_QKV || EPI == EPI_ARGMAX) pos = p.state[ST_POS];
-
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
+    const int nsb = p.nb / 8;   // Q4_K super-blocks per row
 
-    // (3) stream the CTA's rows.
+    // (3) stream the CTA's rows: tiles of box_rows rows x nchunk chunks.
     int cur = r_begin, t = 0;
     while (cur < r_end) {
-        TileCursor tc = tile_at(p, cur, r_end);
-        const int s = t % p.nstages;
-        const uint32_t par = (uint32_t)((t / p.nstages) & 1);
-        if (!mbar_wait(&full[s], par, limit_ns)) {
-            s_abort = 1;
-            set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
-        }
-        const uint8_t* sb = stages + (size_t)s * p.stage_bytes;
-        float* pb = part + (t & 1) * (p.tile_rows * np * (DUAL ? 2 : 1));
-        const int iters = (tc.n + G - 1) / G;
-        for (int j = 0; j < iters; ++j) {
-            const int rho = g + j * G;
-            const bool valid = rho < tc.n;
-            const uint8_t* rowp = sb + (size_t)(valid ? rho : 0) * p.pitch;
-            float acc = 0.0f, acc2 = 0.0f;
-            if (valid) {
+        const TileCursor tc = tile_at(p, cur, r_end);
+        const int n = tc.n;
+        const int nfold = DUAL ? 2 * p.box_rows : n;   // fold lane f <-> term row f
+        float acc = 0.0f;
+        for (int c = 0; c < p.nchunk; ++c, ++t) {
+            const int s = t % p.nstages;
+            if (!mbar_wait(&full[s], (uint32_t)((t / p.nstages) & 1), limit_ns)) {
+                s_abort = 1;
+                set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+            }
+            const uint8_t* sb = stages + (size_t)s * p.stage_bytes;
+            float* T = tbuf + (t & 1) * (kMaxFold * kTStride);
+            const int per_mat = n * kUnits;
+            const int items = DUAL ? 2 * per_mat : per_mat;
+            for (int it = tid; it < items; it += kThreads) {
+                const int mat = DUAL ? (it >= per_mat) : 0;
+                const int rem = it - mat * per_mat;
+                const int r = rem >> 3, u = rem & 7;
+                const uint8_t* row = sb + mat * box_bytes + r * p.chunk_bytes;
+                XUnit x;
+                load_xunit(smem, p, c * kUnits + u, x);
+                float t0, t1;
+                unit_terms<QT>(row, u, x, t0, t1);
+                float* trow = T + (mat * p.box_rows + r) * kTStride;
+                trow[2 * u] = t0;
+                trow[2 * u + 1] = t1;
+            }
+            __syncthreads();
+            if (s_abort) break;
+            if (tid == 0 && icur < r_end) issue(s);
+            // sequential fold of this chunk's terms, one lane per row, block order.
+            if (tid < nfold) {
+                const bool live = DUAL ? ((tid % p.box_rows) < n) : true;
+                if (live) {
+                    const float* trow = T + tid * kTStride;
+                    if constexpr (QT == NCM_T_Q4_K) {
+                        const int nsbc = min(2, nsb - 2 * c);
+                        for (int q = 0; q < nsbc; ++q) {
+                            float ssum = 0.0f;   // q8.rs:1342 sum starts at 0 per super-block
 #pragma unroll
-                for (int k = 0; k < NPT; ++k) {
-                    int u = li + 256 * k;
-                    if (u < p.units) {
-                        acc += unit_dot<QT>(rowp, u, xr[k]);
-                        if constexpr (DUAL) acc2 += unit_dot<QT>(rowp + half_off, u, xr[k]);
+                            for (int j = 0; j < 8; ++j) ssum += trow[8 * q + j];
+                            acc += ssum;           // inference.rs:3129 row sum += block result
+                        }
+                    } else {
+                        const int nbc = min(16, p.nb - 16 * c);
+                        for (int j = 0; j < nbc; ++j) acc += trow[j];
                     }
                 }
             }
-            if (pp <= 32) {
-                for (int o = pp >> 1; o > 0; o >>= 1) {
-                    acc += __shfl_xor_sync(NCM_FULL, acc, o);
-                    if constexpr (DUAL) acc2 += __shfl_xor_sync(NCM_FULL, acc2, o);
-                }
-                if (li == 0 && valid) {
-                    pb[rho * np] = acc;
-                    if constexpr (DUAL) pb[(p.tile_rows + rho) * np] = acc2;
-                }
-            } else {
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    acc += __shfl_xor_sync(NCM_FULL, acc, o);
-                    if constexpr (DUAL) acc2 += __shfl_xor_sync(NCM_FULL, acc2, o);
-                }
-                if ((tid & 31) == 0 && valid) {
-                    pb[rho * np + (li >> 5)] = acc;
-                    if constexpr (DUAL) pb[(p.tile_rows + rho) * np + (li >> 5)] = acc2;
-                }
-            }
         }
-        __syncthreads();
         if (s_abort) break;
-        // stage s is free: refill it with the next pending tile.
-        if (tid == 0 && icur < r_end) {
-            TileCursor nc = tile_at(p, icur, r_end);
-            uint32_t bytes = (uint32_t)(nc.n * p.pitch);
-            const Seg& sg = p.seg[nc.seg];
-            size_t off = (size_t)(icur - sg.row_begin) * p.pitch;
-            mbar_arrive_expect_tx(&full[s], DUAL ? 2 * bytes : bytes);
-            bulk_g2s(stages + (size_t)s * p.stage_bytes, sg.w + off, bytes, &full[s], pol);
-            if (DUAL) bulk_g2s(stages + (size_t)s * p.stage_bytes + half_off, sg.w2 + off, bytes, &full[s], pol);
-            icur += nc.n;
-        }
 
-        // (4) epilogue for this tile.
+        // (4) tile epilogue on the fold lanes (rows cur .. cur+n-1 of segment tc.seg).
         const Seg& sg = p.seg[tc.seg];
-        const int lrow0 = cur - sg.row_begin;   // segment-local first row
+        const int lrow0 = cur - sg.row_begin;
         if constexpr (EPI == EPI_QKV) {
-            const int npairs = tc.n >> 1;
-            for (int pr = tid; pr < npairs; pr += kThreads) {
-                const int rho = 2 * pr;
-                float v0 = 0.0f, v1 = 0.0f;
-                for (int k = 0; k < np; ++k) { v0 += pb[rho * np + k]; v1 += pb[(rho + 1) * np + k]; }
-                const int lr = lrow0 + rho;
-                if (sg.kind != SEG_V) {
-                    // inference.rs:904-933 apply_rope_cached, NORM pairs (2i, 2i+1).
-                    const int i = (lr % p.head_dim) >> 1;
-                    if (i < p.rope_half) {
-                        float2 sc = p.rope[(size_t)pos * p.rope_half + i];
-                        float x0 = v0, x1 = v1;
-                        v0 = x0 * sc.y - x1 * sc.x;
-                        v1 = x0 * sc.x + x1 * sc.y;
+            if (tid < 64) {   // two full warps so the pair shuffle is well defined
+                const float other = __shfl_xor_sync(NCM_FULL, acc, 1);
+                if (tid < n) {
+                    const int lr = lrow0 + tid;
+                    float v = acc;
+                    if (sg.kind != SEG_V) {
+                        // inference.rs:904-933 apply_rope_cached, NORM pairs (2i, 2i+1).
+                        const int i = (lr % p.head_dim) >> 1;
+                        if (i < p.rope_half) {
+                            const float2 scs = p.rope[(size_t)pos * p.rope_half + i];
+                            const float x0 = (tid & 1) ? other : acc;
+                            const float x1 = (tid & 1) ? acc : other;
+                            v = (tid & 1) ? (x0 * scs.x + x1 * scs.y) : (x0 * scs.y - x1 * scs.x);
+                        }
                     }
-                }
-                if (sg.kind == SEG_Q) {
-                    sg.out[lr] = v0; sg.out[lr + 1] = v1;
-                } else {
-                    float* c = (sg.kind == SEG_K ? p.kcache : p.vcache) + (size_t)pos * p.kv_width;
-                    c[lr] = v0; c[lr + 1] = v1;
+                    if (sg.kind == SEG_Q) sg.out[lr] = v;
+                    else ((sg.kind == SEG_K ? p.kcache : p.vcache) + (size_t)pos * p.kv_width)[lr] = v;
                 }
             }
+        } else if constexpr (EPI == EPI_SILU) {
+            if (tid >= p.box_rows && tid < p.box_rows + n) xchg[tid - p.box_rows] = acc;
+            if (tid < 64) asm volatile("bar.sync 1, 64;" ::: "memory");
+            if (tid < n) {
+                const float g = acc, u = xchg[tid];
+                // inference.rs:3385-3388: sigmoid = 1/(1+exp(-g)); g * sigmoid * u
+                const float sig = 1.0f / (1.0f + expf_cr(-g));
+                sg.out[lrow0 + tid] = g * sig * u;
+            }
+            if (tid < 64) asm volatile("bar.sync 1, 64;" ::: "memory");
         } else {
-            for (int rho = tid; rho < tc.n; rho += kThreads) {
-                float v = 0.0f;
-                for (int k = 0; k < np; ++k) v += pb[rho * np + k];
-                const int lr = lrow0 + rho;
+            if (tid < n) {
+                const int lr = lrow0 + tid;
                 if constexpr (EPI == EPI_PLAIN) {
-                    sg.out[lr] = v;
+                    sg.out[lr] = acc;
                 } else if constexpr (EPI == EPI_RESID) {
-                    sg.out[lr] += v;   // inference.rs:4670-4672 hidden[i] += residual[i]
-                } else if constexpr (EPI == EPI_SILU) {
-                    float u = 0.0f;
-                    for (int k = 0; k < np; ++k) u += pb[(p.tile_rows + rho) * np + k];
-                    // inference.rs:3385-3388 g * (1/(1+exp(-g))) * u
-                    float sig = 1.0f / (1.0f + expf(-v));
-                    sg.out[lr] = v * sig * u;
+                    sg.out[lr] += acc;   // inference.rs:4670-4672 / 4744-4746
                 } else if constexpr (EPI == EPI_ARGMAX) {
-                    if (sg.out) sg.out[lr] = v;
-                    if (better(v, lr, best_v, best_i)) { best_v = v; best_i = lr; }
+                    if (sg.out) sg.out[lr] = acc;
+                    if (better(acc, lr, best_v, best_i)) { best_v = acc; best_i = lr; }
                 } else if constexpr (EPI == EPI_TP_RESID) {
                     // Partial row into slot [rank] of every GPU's receive area (NVLink
-                    // stores for peers), tp.rs:357-359 "all-reduce #1/#2" summand.
+                    // stores for peers): the summands of tp.rs:357-359 / 418-420.
                     const size_t idx = ((size_t)p.tp_slot * p.tp.world + p.tp.rank) * p.tp.H + lr;
-                    for (int d = 0; d < p.tp.world; ++d) p.tp.recv[d][idx] = v;
+                    for (int d = 0; d < p.tp.world; ++d) p.tp.recv[d][idx] = acc;
                 }
             }
         }
-        cur += tc.n;
-        ++t;
+        cur += n;
     }
 
     if constexpr (EPI == EPI_ARGMAX) {
-        // CTA-local first-max, then the last CTA merges all CTAs (rows ascend with the
-        // CTA index, so "larger value, ties to the lower row" == inference.rs:4838-4843).
+        // CTA first-max over its rows, then the last CTA merges every CTA (rows ascend
+        // with the CTA index, so "larger value, ties to the lower row" reproduces the
+        // strict '>' scan of inference.rs:4838-4843).
+        if (tid < 64) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            float ov = __shfl_xor_sync(NCM_FULL, best_v, o);
-            int oi = __shfl_xor_sync(NCM_FULL, best_i, o);
-            if (better(ov, oi, best_v, best_i)) { best_v = ov; best_i = oi; }
+            for (int o = 16; o > 0; o >>= 1) {
+                float ov = __shfl_xor_sync(NCM_FULL, best_v, o);
+                int oi = __shfl_xor_sync(NCM_FULL, best_i, o);
+                if (better(ov, oi, best_v, best_i)) { best_v = ov; best_i = oi; }
+            }
+            if (lane == 0) { wv[warp] = best_v; wi[warp] = best_i; }
         }
-        __shared__ float wv[kThreads / 32];
-        __shared__ int wi[kThreads / 32];
-        if ((tid & 31) == 0) { wv[tid >> 5] = best_v; wi[tid >> 5] = best_i; }
         __syncthreads();
         if (tid == 0) {
             float bv = wv[0];
             int bi = wi[0];
-            for (int w = 1; w < kThreads / 32; ++w)
-                if (better(wv[w], wi[w], bv, bi)) { bv = wv[w]; bi = wi[w]; }
+            if (better(wv[1], wi[1], bv, bi)) { bv = wv[1]; bi = wi[1]; }
             p.amax_part[blockIdx.x] = make_float2(bv, __int_as_float(bi));
             __threadfence();
             unsigned prev = atomicAdd(p.counter, 1u);
-            s_last = (prev == (unsigned)nb - 1);
+            s_last = (prev == (unsigned)nbk - 1);
         }
         __syncthreads();
         if (s_last && tid == 0) {
             __threadfence();
             float bv = -INFINITY;
             int bi = 0x7fffffff;
-            for (int c = 0; c < nb; ++c) {
+            for (int c = 0; c < nbk; ++c) {
                 float2 e = __ldcg(&p.amax_part[c]);
                 int ei = __float_as_int(e.y);
                 if (better(e.x, ei, bv, bi)) { bv = e.x; bi = ei; }
@@ -504,12 +646,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
                 for (int d = 0; d < W; ++d) st_release_sys(&p.tp.hflags[d][me], epoch);
                 uint64_t t0 = global_timer_ns();
                 bool ok = true;
-                for (int src = 0; src < W; ++src) {
+                for (int src = 0; src < W && ok; ++src) {
                     while (ld_acquire_sys(&p.tp.hflags[me][src]) < epoch) {
                         if (global_timer_ns() - t0 > p.tp.timeout_ns) { ok = false; break; }
                         __nanosleep(64);
                     }
-                    if (!ok) break;
                 }
                 if (!ok) set_dev_error(p.err, NCM_DEVERR_PEER_TIMEOUT);
                 float mv = 0.0f;
@@ -531,9 +672,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
 
     if constexpr (EPI == EPI_TP_RESID) {
         // Fused row-parallel reduction over NVLink (replaces the TCP star reducer,
-        // cluster_tp_node.rs:1154-1180): publish, wait for every rank's slice of the
-        // same rows, then sum in rank order on every GPU so all ranks hold identical
-        // bits: hidden = ((0 + p0) + p1) + ... then += residual (tp.rs:349-363).
+        // cluster_tp_node.rs:1154-1180): publish, wait for every rank's slice of the same
+        // rows, then sum in rank order on every GPU so all ranks hold identical bits:
+        // hidden = ((0 + p0) + p1) + ... then += residual (tp.rs:349-363).
         __syncthreads();
         const int W = p.tp.world, me = p.tp.rank;
         const unsigned epoch = (unsigned)p.state[ST_STEP] + 1u;
@@ -563,57 +704,72 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
 }
 
 // ------------------------------------------------------------------ GEMV planning / launch
-void gemv_plan(int qtype, int cols, int rows_hint, bool dual, bool need_even, int world_grid, GemvParams& p, int& grid,
-               size_t& smem) {
-    const int units = cols / 64;
-    p.units = units;
-    p.cols = cols;
-    if (units <= 256) {
-        int pp = 1;
-        while (pp < units) pp <<= 1;
-        p.pp = pp;
-        p.groups = kThreads / pp;
-    } else {
-        p.pp = kThreads;
-        p.groups = 1;
-    }
-    p.nparts = p.pp > 32 ? p.pp / 32 : 1;
-    const int row_bytes = p.pitch * (dual ? 2 : 1);
-    const int target = 24 * 1024;
-    int tr = target / row_bytes;
-    if (tr < p.groups) tr = p.groups;          // groups is a power of two (may be 1)
-    else tr = tr / p.groups * p.groups;
-    if (tr > 256) tr = 256;
-    if (need_even && (tr & 1)) tr += 1;        // RoPE pairs must share a tile
-    p.tile_rows = tr;
-    p.stage_bytes = (tr * row_bytes + 127) / 128 * 128;
-    // 4 stages (~96 KB) keeps two CTAs per SM; very wide rows drop to 2-3 stages.
-    int ns = (112 * 1024) / p.stage_bytes;
-    p.nstages = ns > 4 ? 4 : (ns < 2 ? 2 : ns);
-    p.part_off = 128;
-    const int part_bytes = 2 * tr * p.nparts * (dual ? 2 : 1) * 4;
-    p.stage_off = (p.part_off + part_bytes + 127) / 128 * 128;
-    smem = (size_t)p.stage_off + (size_t)p.nstages * p.stage_bytes;
-    int g = world_grid > 0 ? world_grid : num_sms();
-    int maxg = (rows_hint + 1) / 2;
-    if (maxg < 1) maxg = 1;
-    grid = g < maxg ? g : maxg;
-    (void)qtype;
+int gemv_tensor_map(CUtensorMap* tm, const void* base, int64_t rows, int pitch, int chunk_words, int box_rows) {
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return (int)cudaErrorNotSupported;
+    cuuint64_t gdim[2] = {(cuuint64_t)(pitch / 4), (cuuint64_t)rows};
+    cuuint64_t gstride[1] = {(cuuint64_t)pitch};
+    cuuint32_t box[2] = {(cuuint32_t)chunk_words, (cuuint32_t)box_rows};
+    cuuint32_t estride[2] = {1, 1};
+    CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
 }
 
-template <int QT, int NPT, int IN, int EPI>
+int gemv_plan(int qtype, int cols, int rows, bool dual, int in_mode, GemvParams& p) {
+    p.cols = cols;
+    p.nb = cols / 32;
+    p.nchunk = (cols + kChunkCols - 1) / kChunkCols;
+    p.chunk_bytes = qtype == NCM_T_Q8_0 ? 16 * 34 : 288;
+    p.chunk_words = p.chunk_bytes / 4;
+    p.total_rows = rows;
+    int grid = num_sms();
+    int maxg = (rows + 1) / 2;
+    if (maxg < 1) maxg = 1;
+    if (grid > maxg) grid = maxg;
+    const int per_cta = (rows + grid - 1) / grid;
+    int maxr = dual ? 32 : (qtype == NCM_T_Q8_0 ? 32 : 64);
+    int br = (per_cta + 1) & ~1;
+    if (br > maxr) br = maxr;
+    if (br < 2) br = 2;
+    p.box_rows = br;
+    p.stage_bytes = (br * p.chunk_bytes * (dual ? 2 : 1) + 127) / 128 * 128;
+    const int units = p.nchunk * kUnits;
+    int off = 128;
+    p.xq_off = off;
+    off += units * 80;
+    p.xs_off = off;
+    off += units * 8;
+    p.xsum_off = off;
+    off += units * 8;
+    off = (off + 127) / 128 * 128;
+    // The f32 staging of the RMS input and the term buffers are live at different times.
+    p.xf_off = off;
+    p.t_off = off;
+    int shared_region = 2 * kMaxFold * kTStride * 4;
+    if (in_mode == IN_F32_RMS && cols * 4 > shared_region) shared_region = cols * 4;
+    off += (shared_region + 127) / 128 * 128;
+    p.stage_off = off;
+    int ns = 4;
+    while (ns > 2 && off + ns * p.stage_bytes > 200 * 1024) --ns;
+    p.nstages = ns;
+    p.smem_bytes = off + ns * p.stage_bytes;
+    return grid;
+}
+
+template <int QT, int IN, int EPI>
 static int launch_t(const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
     static bool configured = false;
-    const size_t smem = (size_t)p.stage_off + (size_t)p.nstages * p.stage_bytes;
-    auto kern = gemv_kernel<QT, NPT, IN, EPI>;
+    auto kern = gemv_kernel<QT, IN, EPI>;
     if (!configured) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024);
         configured = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = p.smem_bytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -623,157 +779,136 @@ static int launch_t(const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
     return (int)cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-template <int QT, int NPT>
+template <int QT>
 static int launch_mode(int in_mode, int epi, const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
-    if (in_mode == IN_F32_RMS && epi == EPI_QKV) return launch_t<QT, NPT, IN_F32_RMS, EPI_QKV>(p, grid, s, pdl);
-    if (in_mode == IN_F32_RMS && epi == EPI_SILU) return launch_t<QT, NPT, IN_F32_RMS, EPI_SILU>(p, grid, s, pdl);
-    if (in_mode == IN_F32_RMS && epi == EPI_ARGMAX) return launch_t<QT, NPT, IN_F32_RMS, EPI_ARGMAX>(p, grid, s, pdl);
-    if (in_mode == IN_F32 && epi == EPI_RESID) return launch_t<QT, NPT, IN_F32, EPI_RESID>(p, grid, s, pdl);
-    if (in_mode == IN_F32 && epi == EPI_TP_RESID) return launch_t<QT, NPT, IN_F32, EPI_TP_RESID>(p, grid, s, pdl);
-    if (in_mode == IN_F32 && epi == EPI_PLAIN) return launch_t<QT, NPT, IN_F32, EPI_PLAIN>(p, grid, s, pdl);
-    if (in_mode == IN_Q8 && epi == EPI_PLAIN) return launch_t<QT, NPT, IN_Q8, EPI_PLAIN>(p, grid, s, pdl);
+    if (in_mode == IN_F32_RMS && epi == EPI_QKV) return launch_t<QT, IN_F32_RMS, EPI_QKV>(p, grid, s, pdl);
+    if (in_mode == IN_F32_RMS && epi == EPI_SILU) return launch_t<QT, IN_F32_RMS, EPI_SILU>(p, grid, s, pdl);
+    if (in_mode == IN_F32_RMS && epi == EPI_ARGMAX) return launch_t<QT, IN_F32_RMS, EPI_ARGMAX>(p, grid, s, pdl);
+    if (in_mode == IN_F32 && epi == EPI_RESID) return launch_t<QT, IN_F32, EPI_RESID>(p, grid, s, pdl);
+    if (in_mode == IN_F32 && epi == EPI_TP_RESID) return launch_t<QT, IN_F32, EPI_TP_RESID>(p, grid, s, pdl);
+    if (in_mode == IN_F32 && epi == EPI_PLAIN) return launch_t<QT, IN_F32, EPI_PLAIN>(p, grid, s, pdl);
+    if (in_mode == IN_Q8 && epi == EPI_PLAIN) return launch_t<QT, IN_Q8, EPI_PLAIN>(p, grid, s, pdl);
     return (int)cudaErrorInvalidValue;
 }
 
-int gemv_launch(int qtype, int in_mode, int epi, GemvParams p, int grid, cudaStream_t s, bool pdl) {
-    const int npt = p.units <= 256 ? 1 : (p.units + 255) / 256;
-    if (npt > 2) return (int)cudaErrorInvalidValue;
-    if (qtype == NCM_T_Q4_0) return npt == 1 ? launch_mode<NCM_T_Q4_0, 1>(in_mode, epi, p, grid, s, pdl)
-                                             : launch_mode<NCM_T_Q4_0, 2>(in_mode, epi, p, grid, s, pdl);
-    if (qtype == NCM_T_Q8_0) return npt == 1 ? launch_mode<NCM_T_Q8_0, 1>(in_mode, epi, p, grid, s, pdl)
-                                             : launch_mode<NCM_T_Q8_0, 2>(in_mode, epi, p, grid, s, pdl);
-    if (qtype == NCM_T_Q4_K) return npt == 1 ? launch_mode<NCM_T_Q4_K, 1>(in_mode, epi, p, grid, s, pdl)
-                                             : launch_mode<NCM_T_Q4_K, 2>(in_mode, epi, p, grid, s, pdl);
+int gemv_launch(int qtype, int in_mode, int epi, const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
+    if (qtype == NCM_T_Q4_0) return launch_mode<NCM_T_Q4_0>(in_mode, epi, p, grid, s, pdl);
+    if (qtype == NCM_T_Q8_0) return launch_mode<NCM_T_Q8_0>(in_mode, epi, p, grid, s, pdl);
+    if (qtype == NCM_T_Q4_K) return launch_mode<NCM_T_Q4_K>(in_mode, epi, p, grid, s, pdl);
     return (int)cudaErrorInvalidValue;
 }
 
 // ------------------------------------------------------------------ attention
-// Decode attention over the f32 KV cache (inference.rs:4242-4292), split over
-// positions: CTA (kv head, split) scores its positions for the head group, keeps
-// softmax stats, accumulates V; the last CTA of a kv head merges the splits.
-__global__ void __launch_bounds__(256) attn_kernel(const __grid_constant__ AttnParams a) {
-    extern __shared__ __align__(16) float sh[];
-    __shared__ float m_s[8], l_s[8];
-    __shared__ int s_last;
+// inference.rs:4242-4292 apply_attention_head, f32 cache, term by term.
+// Stage 1 (attn_scores_kernel): scores[h][p] = dot_f32(q_h, k_p) * scale with the dot a
+// sequential sum over head_dim (inference.rs:3570-3573, 4256); grid (kv head, 32
+// positions), warp = query head of the group, lane = position.
+__global__ void __launch_bounds__(256) attn_scores_kernel(const __grid_constant__ AttnParams a) {
+    __shared__ float qs[8 * 256];
+    __shared__ float ks[32 * 257];
     pdl_launch_dependents();
     pdl_wait();
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int kvh = blockIdx.x, split = blockIdx.y;
-    const int pos = a.state[ST_POS];
+    const int pos = a.pos_override >= 0 ? a.pos_override : a.state[ST_POS];
     const int n = pos + 1;
-    const int per = (n + a.nsplit - 1) / a.nsplit;
-    const int p0 = split * per;
-    const int p1 = min(n, p0 + per);
-    const int np = max(0, p1 - p0);
-    const int g = a.heads / a.kv_heads, hd = a.hd;
-    float* qs = sh;                       // [g][hd]
-    float* sc = sh + g * hd;              // [g][max_per]
-    float* rd = sc + g * a.max_per;       // [256 / hd][g][hd]
+    const int p0 = blockIdx.y * 32;
+    if (p0 >= n) return;
+    const int kvh = blockIdx.x, g = a.heads / a.kv_heads, hd = a.hd;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     for (int i = tid; i < g * hd; i += 256) qs[i] = a.q[(size_t)kvh * g * hd + i];
-    __syncthreads();
-    const int dpl = hd / 32;
-    for (int pi = warp; pi < np; pi += 8) {
-        const float* kr = a.kc + (size_t)(p0 + pi) * a.kvw + (size_t)kvh * hd + lane * dpl;
-        float kv[8];
-        for (int j = 0; j < dpl; ++j) kv[j] = kr[j];
-        for (int h = 0; h < g; ++h) {
-            float d = 0.0f;
-            for (int j = 0; j < dpl; ++j) d += qs[h * hd + lane * dpl + j] * kv[j];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(NCM_FULL, d, o);
-            if (lane == 0) sc[h * a.max_per + pi] = d * a.scale;   // inference.rs:4256
-        }
+    const int np = min(32, n - p0);
+    for (int i = tid; i < np * hd; i += 256) {
+        const int pl = i / hd, d = i % hd;
+        ks[pl * (hd + 1) + d] = a.kc[(size_t)(p0 + pl) * a.kvw + (size_t)kvh * hd + d];
     }
     __syncthreads();
+    for (int h = warp; h < g; h += 8) {
+        if (lane < np) {
+            const float* q = qs + h * hd;
+            const float* k = ks + lane * (hd + 1);
+            float s = 0.0f;
+            for (int d = 0; d < hd; ++d) s += q[d] * k[d];
+            a.scores[(size_t)(kvh * g + h) * a.ctx + p0 + lane] = s * a.scale;
+        }
+    }
+}
+
+// Stage 2 (attn_softmax_v_kernel): grid (kv head, dim split).  softmax
+// (inference.rs:3522-3540: max, exp(x - max), sequential sum, *= 1/sum) per query head
+// by one warp each, then out[d] = sum_p w_p * v_p[d] sequential over p per (head, dim)
+// (attn_output zeroed, add_weighted_f32_scalar inference.rs:3619-3623).
+__global__ void __launch_bounds__(256) attn_softmax_v_kernel(const __grid_constant__ AttnParams a) {
+    extern __shared__ __align__(16) float w[];   // [g][n] softmax weights
+    __shared__ SeqSumScratchW scr[8];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int pos = a.pos_override >= 0 ? a.pos_override : a.state[ST_POS];
+    const int n = pos + 1;
+    const int kvh = blockIdx.x, g = a.heads / a.kv_heads, hd = a.hd;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (warp < g) {
-        float m = -INFINITY;
-        for (int pi = lane; pi < np; pi += 32) m = fmaxf(m, sc[warp * a.max_per + pi]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(NCM_FULL, m, o));
-        float l = 0.0f;
-        for (int pi = lane; pi < np; pi += 32) {
-            float e = expf(sc[warp * a.max_per + pi] - m);
-            sc[warp * a.max_per + pi] = e;
-            l += e;
+        const int h = kvh * g + warp;
+        const float* srow = a.scores + (size_t)h * a.ctx;
+        float* wr = w + warp * n;
+        float mx = -INFINITY;
+        for (int p = lane; p < n; p += 32) {
+            float v = srow[p];
+            wr[p] = v;
+            mx = fmaxf(mx, v);   // max is order independent (no NaNs)
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(NCM_FULL, l, o);
-        if (lane == 0) { m_s[warp] = m; l_s[warp] = l; }
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(NCM_FULL, mx, o));
+        for (int p = lane; p < n; p += 32) wr[p] = expf_cr(wr[p] - mx);
+        __syncwarp();
+        const float sum = seq_sum_nonneg<32>([&](int i) { return wr[i]; }, n, scr[warp], lane);
+        const float inv = 1.0f / sum;
+        for (int p = lane; p < n; p += 32) wr[p] = wr[p] * inv;
     }
     __syncthreads();
-    const int nsub = 256 / hd, d = tid % hd, sub = tid / hd;
-    float acc[8];
-#pragma unroll
-    for (int h = 0; h < 8; ++h) acc[h] = 0.0f;
-    for (int pi = sub; pi < np; pi += nsub) {
-        float v = a.vc[(size_t)(p0 + pi) * a.kvw + (size_t)kvh * hd + d];
-#pragma unroll
-        for (int h = 0; h < 8; ++h)
-            if (h < g) acc[h] += sc[h * a.max_per + pi] * v;
-    }
-#pragma unroll
-    for (int h = 0; h < 8; ++h)
-        if (h < g) rd[(sub * g + h) * hd + d] = acc[h];
-    __syncthreads();
-    const int stride = hd + 2;
-    for (int i = tid; i < g * hd; i += 256) {
-        int h = i / hd, dd = i % hd;
-        float s = 0.0f;
-        for (int k = 0; k < nsub; ++k) s += rd[(k * g + h) * hd + dd];
-        a.part[((size_t)(kvh * g + h) * a.nsplit + split) * stride + 2 + dd] = s;
-    }
-    if (tid < g) {
-        float* pr = a.part + ((size_t)(kvh * g + tid) * a.nsplit + split) * stride;
-        pr[0] = np > 0 ? m_s[tid] : -INFINITY;
-        pr[1] = np > 0 ? l_s[tid] : 0.0f;
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = atomicAdd(&a.counter[kvh], 1u) == (unsigned)a.nsplit - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    for (int i = tid; i < g * hd; i += 256) {
-        int h = i / hd, dd = i % hd;
-        const float* base = a.part + (size_t)(kvh * g + h) * a.nsplit * stride;
-        float M = -INFINITY;
-        for (int c = 0; c < a.nsplit; ++c) M = fmaxf(M, __ldcg(base + (size_t)c * stride));
-        float L = 0.0f, o = 0.0f;
-        for (int c = 0; c < a.nsplit; ++c) {
-            float mc = __ldcg(base + (size_t)c * stride);
-            float f = expf(mc - M);
-            L += __ldcg(base + (size_t)c * stride + 1) * f;
-            o += __ldcg(base + (size_t)c * stride + 2 + dd) * f;
+    const int dw = hd / a.dsplit;
+    const int d0 = blockIdx.y * dw;
+    for (int item = tid; item < g * dw; item += 256) {
+        const int h = item / dw, d = d0 + item % dw;
+        const float* wr = w + h * n;
+        const float* vp = a.vc + (size_t)kvh * hd + d;
+        float acc = 0.0f;
+        int p = 0;
+        for (; p + 4 <= n; p += 4) {
+            const float v0 = vp[(size_t)p * a.kvw], v1 = vp[(size_t)(p + 1) * a.kvw];
+            const float v2 = vp[(size_t)(p + 2) * a.kvw], v3 = vp[(size_t)(p + 3) * a.kvw];
+            acc += wr[p] * v0;
+            acc += wr[p + 1] * v1;
+            acc += wr[p + 2] * v2;
+            acc += wr[p + 3] * v3;
         }
-        a.out[(size_t)(kvh * g + h) * hd + dd] = o / L;
+        for (; p < n; ++p) acc += wr[p] * vp[(size_t)p * a.kvw];
+        a.out[(size_t)(kvh * g + h) * hd + d] = acc;
     }
-    if (tid == 0) a.counter[kvh] = 0u;
 }
 
 int attention_launch(const AttnParams& a, cudaStream_t s, bool pdl) {
-    const int g = a.heads / a.kv_heads;
-    const size_t smem = (size_t)(g * a.hd + g * a.max_per + 256 * g) * sizeof(float);
     static bool configured = false;
     if (!configured) {
-        cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(attn_softmax_v_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         configured = true;
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.kv_heads, a.nsplit);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
+    const int g = a.heads / a.kv_heads;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return (int)cudaLaunchKernelEx(&cfg, attn_kernel, a);
+    cfg.gridDim = dim3(a.kv_heads, (a.ctx + 31) / 32);
+    int r = (int)cudaLaunchKernelEx(&cfg, attn_scores_kernel, a);
+    if (r) return r;
+    cfg.gridDim = dim3(a.kv_heads, a.dsplit);
+    cfg.dynamicSmemBytes = (size_t)g * a.ctx * sizeof(float);
+    return (int)cudaLaunchKernelEx(&cfg, attn_softmax_v_kernel, a);
 }
 
 // ------------------------------------------------------------------ small kernels
-// inference.rs:4494-4503 embed_token: one row of the dequantised token_embd table
-// (model.rs:1109-1132 dequantisation, done on demand for the current token).
 // One element of a dequantised row (model.rs:1109-1132 load_f32_or_f16 semantics).
 __device__ __forceinline__ float dequant_elem(int type, const uint8_t* row, int i) {
     if (type == NCM_T_F32) return reinterpret_cast<const float*>(row)[i];
@@ -799,6 +934,8 @@ __device__ __forceinline__ float dequant_elem(int type, const uint8_t* row, int 
     return (float)q * d;
 }
 
+// inference.rs:4494-4503 embed_token: one row of the dequantised token_embd table,
+// dequantised on demand for the current token.
 __global__ void embed_kernel(int type, const uint8_t* table, int64_t pitch, int emb, const int* tokens,
                              const int* state, float* hidden) {
     pdl_launch_dependents();
@@ -932,18 +1069,18 @@ __global__ void block_dots_kernel(int qtype, const uint8_t* w, int64_t rows, int
     }
     const uint8_t* row = w + r * pitch;
     const int nb = cols / 32;
+    float t0, t1;
     if (qtype == NCM_T_Q4_K) {
         int ints[4];
-        unit_q4_k(row, u, x, ints);
+        terms_q4_k(row, u, x, t0, t1, ints);
         int32_t* o = out + (r * nb + 2 * u) * 2;
         o[0] = ints[0]; o[1] = ints[1]; o[2] = ints[2]; o[3] = ints[3];
     } else {
-        int dA, dB;
-        float sA, sB;
-        if (qtype == NCM_T_Q4_0) dots_q4_0(row, u, x, dA, dB, sA, sB);
-        else dots_q8_0(row, u, x, dA, dB, sA, sB);
-        out[r * nb + 2 * u] = dA;
-        out[r * nb + 2 * u + 1] = dB;
+        int d[2];
+        if (qtype == NCM_T_Q4_0) terms_q4_0(row, u, x, t0, t1, d);
+        else terms_q8_0(row, u, x, t0, t1, d);
+        out[r * nb + 2 * u] = d[0];
+        out[r * nb + 2 * u + 1] = d[1];
     }
 }
 int block_dots_launch(int qtype, const uint8_t* w, int64_t rows, int cols, const int8_t* xq, int32_t* out,
@@ -955,74 +1092,21 @@ int block_dots_launch(int qtype, const uint8_t* w, int64_t rows, int cols, const
     return (int)cudaGetLastError();
 }
 
-// Multi-token GEMV (matmul_quantized_batch seam, speculative verify): one warp per row,
-// each lane a set of units, every token's activation read from global (L1/L2 resident).
-template <int QT>
-__global__ void __launch_bounds__(256) gemv_batch_kernel(const uint8_t* w, int64_t rows, int cols, int64_t pitch,
-                                                         int ntok, const int8_t* xq, const float* xs, float* out) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int units = cols / 64;
-    for (int64_t r = (int64_t)blockIdx.x * 8 + warp; r < rows; r += (int64_t)gridDim.x * 8) {
-        const uint8_t* row = w + r * pitch;
-        float acc[8];
-        for (int t = 0; t < 8; ++t) acc[t] = 0.0f;
-        for (int u = lane; u < units; u += 32) {
-            for (int t = 0; t < ntok; ++t) {
-                XUnit x;
-                const uint32_t* src = reinterpret_cast<const uint32_t*>(xq + (size_t)t * cols + 64 * u);
-                for (int i = 0; i < 16; ++i) x.w[i] = src[i];
-                x.s[0] = xs[(size_t)t * (cols / 32) + 2 * u];
-                x.s[1] = xs[(size_t)t * (cols / 32) + 2 * u + 1];
-                for (int h = 0; h < 2; ++h) {
-                    int s = 0;
-                    for (int i = 0; i < 8; ++i) s = __dp4a((int)x.w[8 * h + i], 0x01010101, s);
-                    x.sum[h] = s;
-                }
-                acc[t] += unit_dot<QT>(row, u, x);
-            }
-        }
-        for (int t = 0; t < ntok; ++t) {
-            float v = acc[t];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(NCM_FULL, v, o);
-            if (lane == 0) out[(size_t)t * rows + r] = v;
-        }
-    }
-}
-int gemv_batch_launch(int qtype, const uint8_t* w, int64_t rows, int cols, int pitch, int ntok, const int8_t* xq,
-                      const float* xs, float* out, cudaStream_t s) {
-    if (rows == 0) return 0;
-    int grid = (int)((rows + 7) / 8);
-    int cap = num_sms() * 8;
-    if (grid > cap) grid = cap;
-    if (qtype == NCM_T_Q4_0) gemv_batch_kernel<NCM_T_Q4_0><<<grid, 256, 0, s>>>(w, rows, cols, pitch, ntok, xq, xs, out);
-    else if (qtype == NCM_T_Q8_0) gemv_batch_kernel<NCM_T_Q8_0><<<grid, 256, 0, s>>>(w, rows, cols, pitch, ntok, xq, xs, out);
-    else if (qtype == NCM_T_Q4_K) gemv_batch_kernel<NCM_T_Q4_K><<<grid, 256, 0, s>>>(w, rows, cols, pitch, ntok, xq, xs, out);
-    else return (int)cudaErrorInvalidValue;
-    return (int)cudaGetLastError();
-}
-
-// inference.rs:697-706 rms_norm (one CTA; tree sum of squares).
+// inference.rs:697-706 rms_norm (one CTA): sequential-order sum of squares.
 __global__ void rms_norm_kernel(float* out, const float* x, const float* w, int n, float eps) {
-    __shared__ float red[32];
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss += x[i] * x[i];
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(NCM_FULL, ss, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    float tot = 0.0f;
-    for (int k = 0; k < (int)(blockDim.x / 32); ++k) tot += red[k];
-    float scale = 1.0f / sqrtf(tot / (float)n + eps);
+    __shared__ SeqSumScratch sc;
+    const float tot = seq_sum_nonneg<kThreads>([&](int i) { float v = x[i]; return v * v; }, n, sc, threadIdx.x);
+    const float scale = 1.0f / sqrtf(tot / (float)n + eps);
     for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = x[i] * scale * w[i];
 }
 int rms_norm_launch(float* out, const float* x, const float* w, int n, float eps, cudaStream_t s) {
-    rms_norm_kernel<<<1, 1024, 0, s>>>(out, x, w, n, eps);
+    rms_norm_kernel<<<1, kThreads, 0, s>>>(out, x, w, n, eps);
     return (int)cudaGetLastError();
 }
 
 __global__ void silu_mul_kernel(float* out, const float* g, const float* u, int n) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        float sig = 1.0f / (1.0f + expf(-g[i]));
+        float sig = 1.0f / (1.0f + expf_cr(-g[i]));
         out[i] = g[i] * sig * u[i];
     }
 }
@@ -1063,33 +1147,7 @@ __global__ void requant_q4_0_kernel(int src_type, const uint8_t* src, int64_t ro
     int b = (int)(idx % nb);
     float v[32];
     const uint8_t* row = src + r * src_pitch;
-    if (src_type == NCM_T_Q4_K) {
-        const uint8_t* sb = row + (size_t)(b / 8) * 144;
-        int j = b % 8, pr = j / 2, hi = j % 2;
-        uint32_t s0 = *reinterpret_cast<const uint32_t*>(sb + 4), s1 = *reinterpret_cast<const uint32_t*>(sb + 8),
-                 s2 = *reinterpret_cast<const uint32_t*>(sb + 12);
-        int sc, m;
-        q4k_scale_min(j, s0, s1, s2, sc, m);
-        float d = f16_bits_to_f32(sb[0] | (sb[1] << 8)), dmin = f16_bits_to_f32(sb[2] | (sb[3] << 8));
-        float scl = d * (float)sc, mn = dmin * (float)m;
-        for (int l = 0; l < 32; ++l) {
-            uint8_t byte = sb[16 + pr * 32 + l];
-            v[l] = scl * (float)(hi ? (byte >> 4) : (byte & 0x0f)) - mn;
-        }
-    } else if (src_type == NCM_T_F32) {
-        for (int l = 0; l < 32; ++l) v[l] = reinterpret_cast<const float*>(row)[32 * b + l];
-    } else if (src_type == NCM_T_F16) {
-        for (int l = 0; l < 32; ++l) v[l] = f16_bits_to_f32(row[2 * (32 * b + l)] | (row[2 * (32 * b + l) + 1] << 8));
-    } else {
-        const int bb = ncm_type_block_bytes(src_type);
-        const uint8_t* blk = row + (size_t)b * bb;
-        float d = f16_bits_to_f32(blk[0] | (blk[1] << 8));
-        for (int l = 0; l < 32; ++l) {
-            int q = src_type == NCM_T_Q4_0 ? (l < 16 ? (blk[2 + l] & 0x0f) : (blk[2 + l - 16] >> 4)) - 8
-                                           : (int)(int8_t)blk[2 + l];
-            v[l] = (float)q * d;
-        }
-    }
+    for (int l = 0; l < 32; ++l) v[l] = dequant_elem(src_type, row, 32 * b + l);
     ncm_encode_q4_0(v, dst + r * dst_pitch + (size_t)b * 18);
 }
 int requant_q4_0_launch(int src_type, const uint8_t* src, int64_t rows, int cols, int64_t src_pitch, uint8_t* dst,

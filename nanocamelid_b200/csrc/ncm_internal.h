@@ -1,6 +1,7 @@
 // Internal structures shared by kernels.cu (device code + launchers) and engine.cu
 // (model, decode graph, tensor parallel plumbing).  Not part of the C ABI.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -9,6 +10,10 @@ namespace ncm {
 constexpr int kThreads = 256;   // GEMV CTA size (8 warps)
 constexpr int kMaxSeg = 3;      // weight matrices fused into one GEMV launch (wq, wk, wv)
 constexpr int kMaxWorld = 8;    // GPUs of one NVSwitch box
+constexpr int kChunkCols = 512; // columns per TMA chunk: 16 Q4_0/Q8_0 blocks or 2 Q4_K super-blocks
+constexpr int kUnits = 8;       // 64-column units per chunk
+constexpr int kTStride = 17;    // per-row stride (floats) of the per-block term buffer (conflict-free)
+constexpr int kMaxFold = 64;    // fold lanes (rows) per tile
 
 // Input modes of the GEMV prologue.
 enum InMode { IN_F32 = 0, IN_F32_RMS = 1, IN_Q8 = 2 };
@@ -28,8 +33,6 @@ enum SegKind { SEG_Q = 0, SEG_K = 1, SEG_V = 2, SEG_OUT = 3 };
 enum StateIdx { ST_POS = 0, ST_STEP = 1, ST_NPROMPT = 2, ST_LAST_TOKEN = 3, ST_COUNT = 8 };
 
 struct Seg {
-    const uint8_t* w;   // raw blocks, rows x pitch bytes
-    const uint8_t* w2;  // EPI_SILU: the up matrix (same shape)
     float* out;         // destination of this segment's rows
     int rows;
     int row_begin;      // first row of the segment in the fused row space
@@ -48,24 +51,26 @@ struct TpComm {
     uint64_t timeout_ns;
 };
 
-struct GemvParams {
+struct alignas(64) GemvParams {
+    CUtensorMap tm[kMaxSeg];      // weights: dims {pitch/4 words, rows}, box {chunk_words, box_rows}
+    CUtensorMap tm2;              // EPI_SILU: the up matrix (same shape as tm[0])
     Seg seg[kMaxSeg];
     int nseg;
     int total_rows;
-    int cols, pitch, units;       // units = cols / 64
-    int pp, groups, nparts;       // threads per row-group (pow2), row groups, partial sums per row
-    int tile_rows;                // rows per pipeline stage
+    int cols, nb, nchunk;         // columns, 32-column blocks per row, 512-column chunks per row
+    int chunk_words, chunk_bytes; // TMA box inner extent per row
+    int box_rows;                 // rows per tile (TMA box outer extent)
     int stage_bytes, nstages;
-    int part_off, stage_off;      // shared-memory offsets
+    int xq_off, xs_off, xsum_off, xf_off, t_off, stage_off, smem_bytes;
     // input
-    const float* x;               // IN_F32 / IN_F32_RMS, per token stride = cols
+    const float* x;               // IN_F32 / IN_F32_RMS
     const float* norm_w;
     float eps;
     const float* ssq_tok;         // layer 0: sequential sum of squares per vocab row (or null)
     const int8_t* xq;             // IN_Q8
     const float* xs;
     // epilogue context
-    float* hidden;                // EPI_RESID / EPI_TP_RESID target
+    float* hidden;                // EPI_TP_RESID target
     int* state;                   // StateIdx array
     const float2* rope;           // [ctx][rope_half] (sin, cos)
     int rope_half, head_dim;
@@ -86,20 +91,25 @@ struct AttnParams {
     const float* q;          // [heads_local * hd] roped
     const float* kc;         // layer cache [ctx][kvw]
     const float* vc;
+    float* scores;           // [heads_local][ctx] scratch
     float* out;              // [heads_local * hd]
-    float* part;             // [heads_local][nsplit][hd + 2]
-    unsigned* counter;       // [kv_heads_local]
     const int* state;
-    int heads, kv_heads, hd, kvw, nsplit, max_per;
+    int pos_override;        // >= 0: use instead of state[ST_POS]
+    int heads, kv_heads, hd, kvw, ctx, dsplit;
     float scale;
 };
 
 // Launchers (kernels.cu).
-int gemv_launch(int qtype, int in_mode, int epi, GemvParams p, int grid, cudaStream_t s, bool pdl);
-void gemv_plan(int qtype, int cols, int rows_hint, bool dual, bool need_even, int world_grid, GemvParams& p, int& grid,
-               size_t& smem);
-int embed_ssq_launch(int type, const uint8_t* table, int64_t pitch, int emb, int vocab, float* out, cudaStream_t s);
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled_fn();
+// Fills the layout fields of p for a (qtype, cols) matrix set with `rows` total rows; returns the grid.
+int gemv_plan(int qtype, int cols, int rows, bool dual, int in_mode, GemvParams& p);
+int gemv_tensor_map(CUtensorMap* tm, const void* base, int64_t rows, int pitch, int chunk_words, int box_rows);
+int gemv_launch(int qtype, int in_mode, int epi, const GemvParams& p, int grid, cudaStream_t s, bool pdl);
 int attention_launch(const AttnParams& a, cudaStream_t s, bool pdl);
+int embed_ssq_launch(int type, const uint8_t* table, int64_t pitch, int emb, int vocab, float* out, cudaStream_t s);
 int embed_launch(int type, const uint8_t* table, int64_t pitch, int emb, const int* tokens, const int* state,
                  float* hidden, cudaStream_t s, bool pdl);
 int resid_add_launch(float* hidden, const float* part, int n, cudaStream_t s, bool pdl);
@@ -108,8 +118,6 @@ int advance_launch(int* state, cudaStream_t s, bool pdl);
 int quantize_launch(const float* x, int n, int8_t* xq, float* xs, cudaStream_t s);
 int block_dots_launch(int qtype, const uint8_t* w, int64_t rows, int cols, const int8_t* xq, int32_t* out,
                       cudaStream_t s);
-int gemv_batch_launch(int qtype, const uint8_t* w, int64_t rows, int cols, int pitch, int ntok, const int8_t* xq,
-                      const float* xs, float* out, cudaStream_t s);
 int rms_norm_launch(float* out, const float* x, const float* w, int n, float eps, cudaStream_t s);
 int silu_mul_launch(float* out, const float* g, const float* u, int n, cudaStream_t s);
 int synth_launch(int type, uint64_t key, int64_t r0, int64_t nrows, int64_t c0, int64_t ncols, int64_t full_cols,
