@@ -17,7 +17,7 @@ LIB = os.path.join(HERE, "libncm.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CU_SOURCES = ["kernels.cu", "engine.cu"]
-CPP_SOURCES = ["gguf.cpp"]
+CPP_SOURCES = ["gguf.cpp", "libm_table.cpp"]
 
 
 def _headers():

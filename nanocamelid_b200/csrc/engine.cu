@@ -6,6 +6,8 @@
 #include <math.h>
 #include <string.h>
 #include <initializer_list>
+#include <mutex>
+#include <thread>
 #include <string>
 #include <vector>
 #include "../../include/ncm.h"
@@ -174,7 +176,34 @@ extern "C" ncm_status ncm_shard_geometry(int heads, int kv_heads, int ffn, int v
 
 // Common set-up once the global config is known: shard geometry, activation buffers,
 // KV cache, rope table, state.
+// The exp exception table (libm_table.cpp) is built once per process and uploaded once
+// per device; every kernel that evaluates exp on that device then matches glibc's expf.
+static ncm_status ensure_expf_table(int device) {
+    static std::mutex mu;
+    static std::vector<uint32_t> host_tab;
+    static uint32_t mask = 0;
+    static std::vector<int> done;
+    std::lock_guard<std::mutex> lk(mu);
+    for (int d : done)
+        if (d == device) return NCM_OK;
+    if (host_tab.empty()) {
+        size_t count = 0;
+        unsigned hc = std::thread::hardware_concurrency();
+        host_tab = build_expf_exceptions(hc ? (int)hc : 8, &mask, &count);
+    }
+    uint32_t* dtab = nullptr;
+    CK(cudaMalloc(&dtab, host_tab.size() * 4));   // process lifetime (one per device)
+    CK(cudaMemcpy(dtab, host_tab.data(), host_tab.size() * 4, cudaMemcpyHostToDevice));
+    CKL(expf_table_install(dtab, mask));
+    done.push_back(device);
+    return NCM_OK;
+}
+
 static ncm_status setup_buffers(ncm_model* m, const int* shares, int nshards, int shard) {
+    {
+        ncm_status s = ensure_expf_table(m->device);
+        if (s) return s;
+    }
     if (m->heads % m->kv_heads) return fail(NCM_EINVAL, "heads must be a multiple of kv heads");
     if (m->emb % 256) return fail(NCM_EUNSUPPORTED, "embedding length must be a multiple of 256");
     if (m->hd % 32 || m->hd > 256 || m->heads / m->kv_heads > 8)
@@ -945,6 +974,12 @@ extern "C" ncm_status ncm_rms_norm(float* out, const float* x, const float* weig
 
 extern "C" ncm_status ncm_fused_silu_mul(float* out, const float* gate, const float* up, int n, void* stream) {
     if (n < 0 || (n && (!out || !gate || !up))) return fail(NCM_EINVAL, "bad arguments");
+    {
+        int dev = 0;
+        CK(cudaGetDevice(&dev));
+        ncm_status st = ensure_expf_table(dev);
+        if (st) return st;
+    }
     CKL(silu_mul_launch(out, gate, up, n, (cudaStream_t)stream));
     return NCM_OK;
 }
@@ -955,6 +990,12 @@ extern "C" ncm_status ncm_attention(float* out, const float* q, const float* k_c
         heads / kv_heads > 8 || head_dim % 32 || head_dim > 256 || pos >= 16384)
         return fail(NCM_EINVAL, "bad attention arguments");
     cudaStream_t s = (cudaStream_t)stream;
+    {
+        int dev = 0;
+        CK(cudaGetDevice(&dev));
+        ncm_status st = ensure_expf_table(dev);
+        if (st) return st;
+    }
     float* scores = nullptr;
     const int ctx = pos + 1;
     CK(cudaMallocAsync((void**)&scores, 4 * (size_t)heads * ctx, s));

@@ -54,12 +54,43 @@ EncodeTiledFn encode_tiled_fn() {
 }
 
 // ------------------------------------------------------------------ exp
-// The reference's exp is glibc expf (Rust f32::exp).  Device expf is not bit-identical
-// to it; exp() in double rounded to float is correctly rounded except within ~1 double
-// ulp of a float rounding midpoint.  glibc 2.39's expf agrees with the correctly
-// rounded value on all but ~0.01-0.06% of inputs (measured on the build host), so this
-// is the closest device match short of reimplementing glibc's table.
-__device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
+// The reference's exp is the host glibc expf (Rust f32::exp).  glibc's expf is not
+// correctly rounded, so a device exp must reproduce its exceptions: exp() in double
+// rounded to float is the correctly rounded value (up to CUDA's double exp landing
+// within one double ulp of a float midpoint), and the inputs where glibc differs from
+// it -- all of them lie within 2^-7 ulp of a float rounding midpoint -- are patched from
+// an exception hash built on the host from this process's glibc (libm_table.cpp).
+// Only values that close to a midpoint (~0.4% of inputs) probe the table.
+__device__ const uint32_t* g_expf_tab = nullptr;
+__device__ uint32_t g_expf_mask = 0;
+
+__device__ __forceinline__ float expf_cr(float x) {
+    const double yd = exp((double)x);
+    const float y = (float)yd;
+    const uint32_t* tab = g_expf_tab;
+    if (tab != nullptr && y != 0.0f && !isinf(y)) {
+        const double yy = (double)y;
+        const double half = (yd >= yy ? ((double)nextafterf(y, INFINITY) - yy) : (yy - (double)nextafterf(y, 0.0f))) * 0.5;
+        const double dist = fabs(yd - yy);
+        if (half - dist <= half * 0x1p-6) {
+            const uint32_t key = __float_as_uint(x), mask = g_expf_mask;
+            uint32_t h = (key * 2654435761u) & mask;
+            for (int probe = 0; probe < 64; ++probe) {
+                const uint2 e = reinterpret_cast<const uint2*>(tab)[h];
+                if (e.x == key) return __uint_as_float(e.y);
+                if (e.x == 0xffffffffu) break;
+                h = (h + 1) & mask;
+            }
+        }
+    }
+    return y;
+}
+
+int expf_table_install(const uint32_t* dev_tab, uint32_t mask) {
+    cudaError_t e = cudaMemcpyToSymbol(g_expf_tab, &dev_tab, sizeof(dev_tab));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_expf_mask, &mask, sizeof(mask));
+    return (int)e;
+}
 
 // ------------------------------------------------------------------ exact sequential sums
 // Reproduces   s = 0.0f; for i in [0, n): s = RN(s + t(i))   for t(i) >= 0 exactly.
@@ -452,6 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     const int r_begin = (int)(((long long)blockIdx.x * R / nbk)) & ~1;
     const int r_end = (blockIdx.x + 1 == nbk) ? R : ((int)(((long long)(blockIdx.x + 1) * R / nbk)) & ~1);
     const int box_bytes = p.box_rows * p.chunk_bytes;
+    const int box2_off = (box_bytes + 127) & ~127;   // tensor-TMA destinations are 128-byte aligned
     const uint64_t limit_ns = 4000000000ull;
 
     // (1) barriers + weight prefetch (weights are constant: legal before the PDL wait).
@@ -463,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         const int x = ichunk * p.chunk_words;
         mbar_arrive_expect_tx(&full[s], DUAL ? 2 * box_bytes : box_bytes);
         tma_load_2d(stages + (size_t)s * p.stage_bytes, &p.tm[tc.seg], x, y, &full[s], pol);
-        if (DUAL) tma_load_2d(stages + (size_t)s * p.stage_bytes + box_bytes, &p.tm2, x, y, &full[s], pol);
+        if (DUAL) tma_load_2d(stages + (size_t)s * p.stage_bytes + box2_off, &p.tm2, x, y, &full[s], pol);
         if (++ichunk == p.nchunk) { ichunk = 0; icur += tc.n; }
     };
     if (tid == 0) {
@@ -508,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
                 const int mat = DUAL ? (it >= per_mat) : 0;
                 const int rem = it - mat * per_mat;
                 const int r = rem >> 3, u = rem & 7;
-                const uint8_t* row = sb + mat * box_bytes + r * p.chunk_bytes;
+                const uint8_t* row = sb + mat * box2_off + r * p.chunk_bytes;
                 XUnit x;
                 load_xunit(smem, p, c * kUnits + u, x);
                 float t0, t1;
@@ -734,7 +766,7 @@ int gemv_plan(int qtype, int cols, int rows, bool dual, int in_mode, GemvParams&
     if (br > maxr) br = maxr;
     if (br < 2) br = 2;
     p.box_rows = br;
-    p.stage_bytes = (br * p.chunk_bytes * (dual ? 2 : 1) + 127) / 128 * 128;
+    p.stage_bytes = (br * p.chunk_bytes + 127) / 128 * 128 * (dual ? 2 : 1);
     const int units = p.nchunk * kUnits;
     int off = 128;
     p.xq_off = off;

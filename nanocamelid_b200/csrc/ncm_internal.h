@@ -126,5 +126,11 @@ int requant_q4_0_launch(int src_type, const uint8_t* src, int64_t rows, int cols
                         int64_t dst_pitch, cudaStream_t s);
 int peer_timeout_test_launch(TpComm c, int* err, cudaStream_t s);
 int num_sms();
+int expf_table_install(const uint32_t* dev_tab, uint32_t mask);
+// libm_table.cpp
+}  // namespace ncm
+#include <vector>
+namespace ncm {
+std::vector<uint32_t> build_expf_exceptions(int threads, uint32_t* mask, size_t* count);
 
 }  // namespace ncm
