@@ -79,6 +79,23 @@ ncm_status ncm_fused_silu_mul(float* out, const float* gate, const float* up, in
 ncm_status ncm_attention(float* out, const float* q, const float* k_cache, const float* v_cache, int pos,
                          int heads, int kv_heads, int head_dim, void* stream);
 
+/* No counterpart in the reference.  The same computation as ncm_attention, for callers
+ * that must not allocate device memory on the call path: code running inside a CUDA
+ * graph capture or a latency-critical loop where cudaMalloc would stall, and hosts that
+ * run under a fixed memory budget with allocation forbidden after start-up.  The
+ * softmax-score scratch is a fixed 1 MiB array (262144 floats) compiled into the
+ * library, held by every GPU that loads it until the process exits; calls with
+ * heads * (pos + 1) > 262144 are rejected with NCM_EINVAL.  The first call on a device
+ * looks up that device's copy of the array (cudaGetSymbolAddress), so make it once on
+ * each device before any stream capture.  All calls on a device share the one array:
+ * calls that can overlap on the GPU race, so serialise them (one stream, or events).
+ * Nothing in it needs clearing, because each call writes every score it reads.  The
+ * launch is stream ordered and does not synchronise.  exp matches the host glibc bit
+ * for bit only after an allocating call (a model load, ncm_attention or
+ * ncm_fused_silu_mul) has set up the exp table on this device. */
+ncm_status ncm_attention_noalloc(float* out, const float* q, const float* k_cache, const float* v_cache, int pos,
+                                 int heads, int kv_heads, int head_dim, void* stream);
+
 /* ---------------------------------------------------------------- fixtures
  * Random-init model spec (the five BASELINE configs are random-init shapes). */
 typedef struct {

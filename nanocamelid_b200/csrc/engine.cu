@@ -1012,3 +1012,52 @@ extern "C" ncm_status ncm_attention(float* out, const float* q, const float* k_c
     if (r) return fail(NCM_ECUDA, "attention launch failed");
     return NCM_OK;
 }
+
+// ------------------------------------------------------------------ allocation-free attention
+// Scores scratch for ncm_attention_noalloc: a fixed array that lives in every GPU that
+// loads this library until the process exits (1 MiB per device).
+static constexpr int64_t kNoAllocScores = 262144;   // floats: heads * (pos + 1) at most
+static __device__ __align__(256) float g_noalloc_scores[kNoAllocScores];
+
+// Host code cannot use g_noalloc_scores directly (the host symbol is only a stand-in for
+// the device array); its device address is looked up once per device, with that device
+// current, and cached here.
+static float* noalloc_scores_ptr(int device, cudaError_t* err) {
+    static std::mutex mu;
+    static float* ptrs[64] = {nullptr};
+    *err = cudaSuccess;
+    if (device < 0 || device >= 64) { *err = cudaErrorInvalidDevice; return nullptr; }
+    std::lock_guard<std::mutex> lk(mu);
+    if (!ptrs[device]) {
+        void* p = nullptr;
+        *err = cudaGetSymbolAddress(&p, g_noalloc_scores);
+        if (*err != cudaSuccess) return nullptr;
+        ptrs[device] = (float*)p;
+    }
+    return ptrs[device];
+}
+
+extern "C" ncm_status ncm_attention_noalloc(float* out, const float* q, const float* k_cache, const float* v_cache,
+                                           int pos, int heads, int kv_heads, int head_dim, void* stream) {
+    if (!out || !q || !k_cache || !v_cache || pos < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads ||
+        heads / kv_heads > 8 || head_dim % 32 || head_dim > 256)
+        return fail(NCM_EINVAL, "bad attention arguments");
+    if ((int64_t)heads * (pos + 1) > kNoAllocScores)
+        return fail(NCM_EINVAL, "ncm_attention_noalloc: heads * (pos + 1) = " + std::to_string((int64_t)heads * (pos + 1)) +
+                                    " exceeds the fixed scratch of " + std::to_string(kNoAllocScores) +
+                                    " floats; use ncm_attention");
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    cudaError_t e;
+    float* scores = noalloc_scores_ptr(dev, &e);
+    if (!scores) return fail(NCM_ECUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    AttnParams a;
+    memset(&a, 0, sizeof a);
+    a.q = q; a.kc = k_cache; a.vc = v_cache; a.out = out; a.scores = scores; a.state = nullptr;
+    a.pos_override = pos;
+    a.heads = heads; a.kv_heads = kv_heads; a.hd = head_dim; a.kvw = kv_heads * head_dim; a.ctx = pos + 1;
+    a.dsplit = 4;
+    a.scale = 1.0f / sqrtf((float)head_dim);
+    CKL(attention_launch(a, (cudaStream_t)stream, false));
+    return NCM_OK;
+}
