@@ -119,9 +119,10 @@ typedef SeqSumScratchT<32> SeqSumScratchW;
 template <int NT, class Term>
 __device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT>& sc, int rank) {
     const int lane = rank & 31;
+    const bool member = rank < NT;   // threads beyond NT only take part in the barriers
     const int m = (n + NT - 1) / NT;
     const int C = m > 0 ? (n + m - 1) / m : 0;
-    const int i0 = min(n, rank * m), i1 = min(n, i0 + m);
+    const int i0 = member ? min(n, rank * m) : n, i1 = member ? min(n, i0 + m) : n;
     float d = 0.0f;
     for (int i = i0; i < i1; ++i) d += term(i);
     // exclusive prefix of the chunk sums: only a guess of each chunk's starting binade.
@@ -133,14 +134,15 @@ __device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT>& sc,
     }
     float pre = v - d;
     if (NT > 32) {
-        if (lane == 31) sc.part[rank >> 5] = v;
+        if (member && lane == 31) sc.part[rank >> 5] = v;
         __syncthreads();
-        for (int w = 0; w < (rank >> 5); ++w) pre += sc.part[w];
+        if (member)
+            for (int w = 0; w < (rank >> 5); ++w) pre += sc.part[w];
     }
     int eb = 0;
     long long cnt = 0;
     int bad = 0;
-    if (rank < C) {
+    if (member && rank < C) {
         const uint32_t gb = __float_as_uint(pre);
         eb = (int)(gb >> 23);
         if (eb < 1 || eb > 253) bad = 1;
@@ -151,9 +153,11 @@ __device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT>& sc,
             cnt += (long long)rintf(a);
         }
     }
-    sc.ebits[rank] = eb;
-    sc.cnt[rank] = cnt;
-    sc.bad[rank] = bad;
+    if (member) {
+        sc.ebits[rank] = eb;
+        sc.cnt[rank] = cnt;
+        sc.bad[rank] = bad;
+    }
     if (NT == 32) __syncwarp(); else __syncthreads();
     if (rank < 32) {
         float s = 0.0f;
@@ -363,7 +367,7 @@ __device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, SeqSumScratch&
     float2* xs = reinterpret_cast<float2*>(smem + p.xs_off);
     int2* xsum = reinterpret_cast<int2*>(smem + p.xsum_off);
     if constexpr (IN == IN_Q8) {
-        for (int g = tid; g < nblk / 2; g += kThreads) {
+        for (int g = tid; g < nblk / 2; g += blockDim.x) {
             uint4* dst = reinterpret_cast<uint4*>(smem + p.xq_off + 80 * g);
             if (2 * g < p.nb) {
                 const uint4* src = reinterpret_cast<const uint4*>(p.xq + 64 * g);
@@ -392,7 +396,7 @@ __device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, SeqSumScratch&
         float scale = 1.0f;
         if constexpr (IN == IN_F32_RMS) {
             float* xf = reinterpret_cast<float*>(smem + p.xf_off);
-            for (int i = tid * 4; i < p.cols; i += 4 * kThreads)
+            for (int i = tid * 4; i < p.cols; i += 4 * blockDim.x)
                 *reinterpret_cast<float4*>(xf + i) = *reinterpret_cast<const float4*>(p.x + i);
             __syncthreads();
             float tot;
@@ -405,7 +409,7 @@ __device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, SeqSumScratch&
             }
             scale = 1.0f / sqrtf(tot / (float)p.cols + p.eps);
         }
-        for (int b = tid; b < nblk; b += kThreads) {
+        for (int b = tid; b < nblk; b += blockDim.x) {
             uint32_t* dst = reinterpret_cast<uint32_t*>(smem + p.xq_off + 80 * (b >> 1) + 32 * (b & 1));
             float s = 0.0f;
             int sum = 0;
@@ -463,33 +467,62 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
     return v > bv || (v == bv && i < bi);
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Warp roles: warps 0-7 compute per-block terms, warps 8-9 fold them row by row (and run
+// the epilogue), warp 10 issues the TMA loads.  Hand-offs use mbarriers only:
+//   full[s]  (TMA -> compute)      empty[s]  (compute -> producer: stage s reusable)
+//   tfull[k] (compute -> fold)     tempty[k] (fold -> compute: term slot k reusable)
+constexpr int kComputeThreads = 256;
+constexpr int kFoldBase = 256;      // first fold thread
+constexpr int kProducer = 320;      // producer thread
+constexpr int kGemvThreads = 352;
+
 template <int QT, int IN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr bool DUAL = (EPI == EPI_SILU);
     __shared__ SeqSumScratch sc;
-    __shared__ int s_abort;
+    __shared__ __align__(8) uint64_t tfull[8], tempty[8];
     __shared__ int s_last;
     __shared__ float xchg[kMaxFold];
     __shared__ float wv[2];
     __shared__ int wi[2];
 
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + 8;
     float* tbuf = reinterpret_cast<float*>(smem + p.t_off);
     uint8_t* stages = smem + p.stage_off;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31;
     const int R = p.total_rows;
     const int nbk = gridDim.x;
     const int r_begin = (int)(((long long)blockIdx.x * R / nbk)) & ~1;
     const int r_end = (blockIdx.x + 1 == nbk) ? R : ((int)(((long long)(blockIdx.x + 1) * R / nbk)) & ~1);
     const int box_bytes = p.box_rows * p.chunk_bytes;
     const int box2_off = (box_bytes + 127) & ~127;   // tensor-TMA destinations are 128-byte aligned
+    const int ns = p.nstages;
     const uint64_t limit_ns = 4000000000ull;
 
-    // (1) barriers + weight prefetch (weights are constant: legal before the PDL wait).
-    int icur = r_begin, ichunk = 0;
+    if (tid == 0) {
+        for (int s = 0; s < ns; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kComputeThreads / 32);
+            mbar_init(&tfull[s], kComputeThreads / 32);
+            mbar_init(&tempty[s], 2);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    // (1) producer: first stages before the PDL wait (weights are constant).
+    int icur = r_begin, ichunk = 0, tprod = 0;
     uint64_t pol = 0;
-    auto issue = [&](int s) {
+    auto issue = [&]() {
+        const int s = tprod % ns;
+        if (tprod >= ns && !mbar_wait(&empty[s], (uint32_t)(((tprod / ns) & 1) ^ 1), limit_ns))
+            set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
         TileCursor tc = tile_at(p, icur, r_end);
         const int y = icur - p.seg[tc.seg].row_begin;
         const int x = ichunk * p.chunk_words;
@@ -497,66 +530,74 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         tma_load_2d(stages + (size_t)s * p.stage_bytes, &p.tm[tc.seg], x, y, &full[s], pol);
         if (DUAL) tma_load_2d(stages + (size_t)s * p.stage_bytes + box2_off, &p.tm2, x, y, &full[s], pol);
         if (++ichunk == p.nchunk) { ichunk = 0; icur += tc.n; }
+        ++tprod;
     };
-    if (tid == 0) {
-        for (int s = 0; s < p.nstages; ++s) mbar_init(&full[s], 1);
-        fence_mbar_init();
-        s_abort = 0;
+    if (tid == kProducer) {
         pol = l2_evict_first_policy();
-        for (int s = 0; s < p.nstages && icur < r_end; ++s) issue(s);
+        while (tprod < ns && icur < r_end) issue();
     }
-    __syncthreads();
     pdl_launch_dependents();
     pdl_wait();
 
-    // (2) activation -> shared memory.
+    // (2) activation -> shared memory (all threads).
     gemv_prologue<IN>(smem, p, sc);
     __syncthreads();
 
-    int pos = 0;
-    if (EPI == EPI_QKV || EPI == EPI_ARGMAX) pos = p.state[ST_POS];
-    float best_v = -INFINITY;
-    int best_i = 0x7fffffff;
-    const int nsb = p.nb / 8;   // Q4_K super-blocks per row
-
-    // (3) stream the CTA's rows: tiles of box_rows rows x nchunk chunks.
-    int cur = r_begin, t = 0;
-    while (cur < r_end) {
-        const TileCursor tc = tile_at(p, cur, r_end);
-        const int n = tc.n;
-        const int nfold = DUAL ? 2 * p.box_rows : n;   // fold lane f <-> term row f
-        float acc = 0.0f;
-        for (int c = 0; c < p.nchunk; ++c, ++t) {
-            const int s = t % p.nstages;
-            if (!mbar_wait(&full[s], (uint32_t)((t / p.nstages) & 1), limit_ns)) {
-                s_abort = 1;
-                set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
-            }
-            const uint8_t* sb = stages + (size_t)s * p.stage_bytes;
-            float* T = tbuf + (t & 1) * (kMaxFold * kTStride);
-            const int per_mat = n * kUnits;
-            const int items = DUAL ? 2 * per_mat : per_mat;
-            for (int it = tid; it < items; it += kThreads) {
-                const int mat = DUAL ? (it >= per_mat) : 0;
-                const int rem = it - mat * per_mat;
-                const int r = rem >> 3, u = rem & 7;
-                const uint8_t* row = sb + mat * box2_off + r * p.chunk_bytes;
+    if (tid == kProducer) {
+        while (icur < r_end) issue();
+    } else if (tid < kComputeThreads) {
+        // (3a) compute warps: per-block terms of every (row, unit) of each stage.
+        const int u = tid & 7, r0 = tid >> 3;
+        int t = 0;
+        for (int cur = r_begin; cur < r_end;) {
+            const int n = tile_at(p, cur, r_end).n;
+            const int vrows = DUAL ? 2 * p.box_rows : n;
+            for (int c = 0; c < p.nchunk; ++c, ++t) {
+                const int s = t % ns;
+                if (!mbar_wait(&full[s], (uint32_t)((t / ns) & 1), limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+                if (!mbar_wait(&tempty[s], (uint32_t)(((t / ns) & 1) ^ 1), limit_ns))
+                    set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+                const uint8_t* sb = stages + (size_t)s * p.stage_bytes;
+                float* T = tbuf + s * (kMaxFold * kTStride);
                 XUnit x;
                 load_xunit(smem, p, c * kUnits + u, x);
-                float t0, t1;
-                unit_terms<QT>(row, u, x, t0, t1);
-                float* trow = T + (mat * p.box_rows + r) * kTStride;
-                trow[2 * u] = t0;
-                trow[2 * u + 1] = t1;
+                for (int vr = r0; vr < vrows; vr += 32) {
+                    const int mat = DUAL ? (vr >= p.box_rows) : 0;
+                    const int r = vr - mat * p.box_rows;
+                    if (r >= n) continue;
+                    float t0, t1;
+                    unit_terms<QT>(sb + mat * box2_off + r * p.chunk_bytes, u, x, t0, t1);
+                    float* trow = T + vr * kTStride;
+                    trow[2 * u] = t0;
+                    trow[2 * u + 1] = t1;
+                }
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&empty[s]);
+                    mbar_arrive(&tfull[s]);
+                }
             }
-            __syncthreads();
-            if (s_abort) break;
-            if (tid == 0 && icur < r_end) issue(s);
-            // sequential fold of this chunk's terms, one lane per row, block order.
-            if (tid < nfold) {
-                const bool live = DUAL ? ((tid % p.box_rows) < n) : true;
+            cur += n;
+        }
+    } else if (tid < kProducer) {
+        // (3b) fold warps: sequential per-row sums in block order, then the epilogue.
+        const int f = tid - kFoldBase;
+        int pos = 0;
+        if (EPI == EPI_QKV || EPI == EPI_ARGMAX) pos = p.state[ST_POS];
+        float best_v = -INFINITY;
+        int best_i = 0x7fffffff;
+        const int nsb = p.nb / 8;
+        int t = 0;
+        for (int cur = r_begin; cur < r_end;) {
+            const TileCursor tc = tile_at(p, cur, r_end);
+            const int n = tc.n;
+            const bool live = DUAL ? (f < 2 * p.box_rows && (f % p.box_rows) < n) : (f < n);
+            float acc = 0.0f;
+            for (int c = 0; c < p.nchunk; ++c, ++t) {
+                const int s = t % ns;
+                if (!mbar_wait(&tfull[s], (uint32_t)((t / ns) & 1), limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
                 if (live) {
-                    const float* trow = T + tid * kTStride;
+                    const float* trow = tbuf + s * (kMaxFold * kTStride) + f * kTStride;
                     if constexpr (QT == NCM_T_Q4_K) {
                         const int nsbc = min(2, nsb - 2 * c);
                         for (int q = 0; q < nsbc; ++q) {
@@ -570,78 +611,77 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
                         for (int j = 0; j < nbc; ++j) acc += trow[j];
                     }
                 }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[s]);
             }
-        }
-        if (s_abort) break;
 
-        // (4) tile epilogue on the fold lanes (rows cur .. cur+n-1 of segment tc.seg).
-        const Seg& sg = p.seg[tc.seg];
-        const int lrow0 = cur - sg.row_begin;
-        if constexpr (EPI == EPI_QKV) {
-            if (tid < 64) {   // two full warps so the pair shuffle is well defined
+            // tile epilogue (rows cur .. cur+n-1 of segment tc.seg)
+            const Seg& sg = p.seg[tc.seg];
+            const int lrow0 = cur - sg.row_begin;
+            if constexpr (EPI == EPI_QKV) {
                 const float other = __shfl_xor_sync(NCM_FULL, acc, 1);
-                if (tid < n) {
-                    const int lr = lrow0 + tid;
+                if (f < n) {
+                    const int lr = lrow0 + f;
                     float v = acc;
                     if (sg.kind != SEG_V) {
                         // inference.rs:904-933 apply_rope_cached, NORM pairs (2i, 2i+1).
                         const int i = (lr % p.head_dim) >> 1;
                         if (i < p.rope_half) {
                             const float2 scs = p.rope[(size_t)pos * p.rope_half + i];
-                            const float x0 = (tid & 1) ? other : acc;
-                            const float x1 = (tid & 1) ? acc : other;
-                            v = (tid & 1) ? (x0 * scs.x + x1 * scs.y) : (x0 * scs.y - x1 * scs.x);
+                            const float x0 = (f & 1) ? other : acc;
+                            const float x1 = (f & 1) ? acc : other;
+                            v = (f & 1) ? (x0 * scs.x + x1 * scs.y) : (x0 * scs.y - x1 * scs.x);
                         }
                     }
                     if (sg.kind == SEG_Q) sg.out[lr] = v;
                     else ((sg.kind == SEG_K ? p.kcache : p.vcache) + (size_t)pos * p.kv_width)[lr] = v;
                 }
-            }
-        } else if constexpr (EPI == EPI_SILU) {
-            if (tid >= p.box_rows && tid < p.box_rows + n) xchg[tid - p.box_rows] = acc;
-            if (tid < 64) asm volatile("bar.sync 1, 64;" ::: "memory");
-            if (tid < n) {
-                const float g = acc, u = xchg[tid];
-                // inference.rs:3385-3388: sigmoid = 1/(1+exp(-g)); g * sigmoid * u
-                const float sig = 1.0f / (1.0f + expf_cr(-g));
-                sg.out[lrow0 + tid] = g * sig * u;
-            }
-            if (tid < 64) asm volatile("bar.sync 1, 64;" ::: "memory");
-        } else {
-            if (tid < n) {
-                const int lr = lrow0 + tid;
-                if constexpr (EPI == EPI_PLAIN) {
-                    sg.out[lr] = acc;
-                } else if constexpr (EPI == EPI_RESID) {
-                    sg.out[lr] += acc;   // inference.rs:4670-4672 / 4744-4746
-                } else if constexpr (EPI == EPI_ARGMAX) {
-                    if (sg.out) sg.out[lr] = acc;
-                    if (better(acc, lr, best_v, best_i)) { best_v = acc; best_i = lr; }
-                } else if constexpr (EPI == EPI_TP_RESID) {
-                    // Partial row into slot [rank] of every GPU's receive area (NVLink
-                    // stores for peers): the summands of tp.rs:357-359 / 418-420.
-                    const size_t idx = ((size_t)p.tp_slot * p.tp.world + p.tp.rank) * p.tp.H + lr;
-                    for (int d = 0; d < p.tp.world; ++d) p.tp.recv[d][idx] = acc;
+            } else if constexpr (EPI == EPI_SILU) {
+                if (f >= p.box_rows && f < p.box_rows + n) xchg[f - p.box_rows] = acc;
+                asm volatile("bar.sync 1, 64;" ::: "memory");
+                if (f < n) {
+                    const float g = acc, uu = xchg[f];
+                    // inference.rs:3385-3388: sigmoid = 1/(1+exp(-g)); g * sigmoid * u
+                    const float sig = 1.0f / (1.0f + expf_cr(-g));
+                    sg.out[lrow0 + f] = g * sig * uu;
+                }
+                asm volatile("bar.sync 1, 64;" ::: "memory");
+            } else {
+                if (f < n) {
+                    const int lr = lrow0 + f;
+                    if constexpr (EPI == EPI_PLAIN) {
+                        sg.out[lr] = acc;
+                    } else if constexpr (EPI == EPI_RESID) {
+                        sg.out[lr] += acc;   // inference.rs:4670-4672 / 4744-4746
+                    } else if constexpr (EPI == EPI_ARGMAX) {
+                        if (sg.out) sg.out[lr] = acc;
+                        if (better(acc, lr, best_v, best_i)) { best_v = acc; best_i = lr; }
+                    } else if constexpr (EPI == EPI_TP_RESID) {
+                        // Partial row into slot [rank] of every GPU's receive area (NVLink
+                        // stores for peers): the summands of tp.rs:357-359 / 418-420.
+                        const size_t idx = ((size_t)p.tp_slot * p.tp.world + p.tp.rank) * p.tp.H + lr;
+                        for (int d = 0; d < p.tp.world; ++d) p.tp.recv[d][idx] = acc;
+                    }
                 }
             }
+            cur += n;
         }
-        cur += n;
-    }
-
-    if constexpr (EPI == EPI_ARGMAX) {
-        // CTA first-max over its rows, then the last CTA merges every CTA (rows ascend
-        // with the CTA index, so "larger value, ties to the lower row" reproduces the
-        // strict '>' scan of inference.rs:4838-4843).
-        if (tid < 64) {
+        if constexpr (EPI == EPI_ARGMAX) {
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
                 float ov = __shfl_xor_sync(NCM_FULL, best_v, o);
                 int oi = __shfl_xor_sync(NCM_FULL, best_i, o);
                 if (better(ov, oi, best_v, best_i)) { best_v = ov; best_i = oi; }
             }
-            if (lane == 0) { wv[warp] = best_v; wi[warp] = best_i; }
+            if (lane == 0) { wv[f >> 5] = best_v; wi[f >> 5] = best_i; }
         }
-        __syncthreads();
+    }
+    __syncthreads();
+
+    if constexpr (EPI == EPI_ARGMAX) {
+        // CTA first-max over its rows, then the last CTA merges every CTA (rows ascend
+        // with the CTA index, so "larger value, ties to the lower row" reproduces the
+        // strict '>' scan of inference.rs:4838-4843).
         if (tid == 0) {
             float bv = wv[0];
             int bi = wi[0];
@@ -707,7 +747,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         // cluster_tp_node.rs:1154-1180): publish, wait for every rank's slice of the same
         // rows, then sum in rank order on every GPU so all ranks hold identical bits:
         // hidden = ((0 + p0) + p1) + ... then += residual (tp.rs:349-363).
-        __syncthreads();
         const int W = p.tp.world, me = p.tp.rank;
         const unsigned epoch = (unsigned)p.state[ST_STEP] + 1u;
         const size_t fslot = ((size_t)p.tp_slot * p.tp.grid_max + blockIdx.x) * W;
@@ -727,7 +766,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         }
         __syncthreads();
         const float* base = p.tp.recv[me] + (size_t)p.tp_slot * W * p.tp.H;
-        for (int r = r_begin + tid; r < r_end; r += kThreads) {
+        for (int r = r_begin + tid; r < r_end; r += blockDim.x) {
             float s = 0.0f;
             for (int src = 0; src < W; ++src) s += __ldcg(base + (size_t)src * p.tp.H + r);
             p.hidden[r] += s;
@@ -777,13 +816,14 @@ int gemv_plan(int qtype, int cols, int rows, bool dual, int in_mode, GemvParams&
     off += units * 8;
     off = (off + 127) / 128 * 128;
     // The f32 staging of the RMS input and the term buffers are live at different times.
+    int ns = (112 * 1024) / p.stage_bytes;
+    ns = ns > 8 ? 8 : (ns < 2 ? 2 : ns);
     p.xf_off = off;
     p.t_off = off;
-    int shared_region = 2 * kMaxFold * kTStride * 4;
+    int shared_region = ns * kMaxFold * kTStride * 4;
     if (in_mode == IN_F32_RMS && cols * 4 > shared_region) shared_region = cols * 4;
     off += (shared_region + 127) / 128 * 128;
     p.stage_off = off;
-    int ns = 4;
     while (ns > 2 && off + ns * p.stage_bytes > 200 * 1024) --ns;
     p.nstages = ns;
     p.smem_bytes = off + ns * p.stage_bytes;
@@ -800,7 +840,7 @@ static int launch_t(const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(kGemvThreads);
     cfg.dynamicSmemBytes = p.smem_bytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
