@@ -188,7 +188,14 @@ __device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT>& sc,
                 float r = s;
                 if (lane == 0) {
                     const int a0 = j * m, a1 = min(n, a0 + m);
-                    for (int i = a0; i < a1; ++i) r = r + term(i);
+                    for (int i = a0; i < a1; i += 8) {
+                        float tv[8];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) tv[q] = (i + q < a1) ? term(i + q) : 0.0f;
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            if (i + q < a1) r = r + tv[q];
+                    }
                 }
                 s = __shfl_sync(NCM_FULL, r, 0);
                 j += 1;
@@ -597,18 +604,27 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                 const int s = t % ns;
                 if (!mbar_wait(&tfull[s], (uint32_t)((t / ns) & 1), limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
                 if (live) {
+                    // all 16 terms into registers first, then the in-order adds
                     const float* trow = tbuf + s * (kMaxFold * kTStride) + f * kTStride;
+                    float tv[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) tv[j] = trow[j];
                     if constexpr (QT == NCM_T_Q4_K) {
                         const int nsbc = min(2, nsb - 2 * c);
-                        for (int q = 0; q < nsbc; ++q) {
-                            float ssum = 0.0f;   // q8.rs:1342 sum starts at 0 per super-block
 #pragma unroll
-                            for (int j = 0; j < 8; ++j) ssum += trow[8 * q + j];
-                            acc += ssum;           // inference.rs:3129 row sum += block result
+                        for (int q = 0; q < 2; ++q) {
+                            if (q < nsbc) {
+                                float ssum = 0.0f;   // q8.rs:1342 sum starts at 0 per super-block
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) ssum += tv[8 * q + j];
+                                acc += ssum;         // inference.rs:3129 row sum += block result
+                            }
                         }
                     } else {
                         const int nbc = min(16, p.nb - 16 * c);
-                        for (int j = 0; j < nbc; ++j) acc += trow[j];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (j < nbc) acc += tv[j];
                     }
                 }
                 __syncwarp();
