@@ -98,112 +98,180 @@ int expf_table_install(const uint32_t* dev_tab, uint32_t mask) {
 // Within one binade [2^e, 2^(e+1)) floats are a grid of spacing u, and for s = k*u,
 // RN(s + t) = u * (k + rint(t/u)) unless t/u is an exact half-integer (a tie, whose
 // result depends on the parity of k) or the sum leaves the binade.  So a run of terms
-// adds a fixed integer number of ulps, independent of where in the binade it starts.
-// Each chunk of terms gets a guessed starting binade from a prefix sum; a resolution
-// warp walks the chunks in order, adding whole chunks in integer ulps when the guess
-// and the no-tie / no-crossing conditions hold and folding the chunk term by term
-// (real FADDs) otherwise.  Guesses only affect speed, never the result.
+// adds a fixed integer number of ulps -- to the bit pattern of s -- independent of
+// where in the binade it starts.
+//
+// The terms are cut into groups of 32, one thread per group.  From an approximate
+// (reassociated) prefix sum each group gets a guessed binade for the running value; a
+// group whose guess holds across the group and that has no tie gets its integer ulp
+// count in that binade.  One warp then walks the groups with the exact running value,
+// 32 groups per step: the leading groups whose guess equals the true binade and whose
+// counts keep the sum inside it are one integer add on the bit pattern; the first
+// group that fails is folded term by term with real FADDs.  Folds happen about once
+// per binade crossing.  Guesses only affect speed, never the result.
+//
+// Counts are capped at 2^23 per group (a capped group can never stay in its binade)
+// and their prefix is kept modulo 2^32: along a step the sum grows by at most 2^23 per
+// lane, so the first lane that leaves the binade sees no wrap-around, and the walk
+// never looks past it.
+constexpr int kSeqHead = 4;   // groups folded outright at the start of a sum
+
 template <int NT>
 struct SeqSumScratchT {
-    float part[NT / 32];       // per-warp chunk-sum totals (binade guesses)
-    int ebits[NT];             // guessed biased exponent of the chunk's starting value
-    long long cnt[NT];         // sum of rint(t/u) over the chunk in that binade
-    int bad[NT];               // chunk has a tie or a term >= 2^24 ulps
+    static constexpr int kGroups = NT;        // groups (of 32 terms) per segment
+    uint32_t key[kGroups];                    // guessed biased exponent, ~0 if unusable
+    uint32_t pre[kGroups];                    // inclusive prefix of the ulp counts
+    float wsum[NT / 32];                      // per-warp totals for the block scans
+    uint32_t wcnt[NT / 32];
     float result;
 };
 typedef SeqSumScratchT<kThreads> SeqSumScratch;
 typedef SeqSumScratchT<32> SeqSumScratchW;
 
-// NT threads (one warp, or the whole 256-thread CTA) cooperate; `rank` is the thread's
-// index among them; the terms are read through term(i).  All NT threads get the result.
-template <int NT, class Term>
-__device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT>& sc, int rank) {
-    const int lane = rank & 31;
-    const bool member = rank < NT;   // threads beyond NT only take part in the barriers
-    const int m = (n + NT - 1) / NT;
-    const int C = m > 0 ? (n + m - 1) / m : 0;
-    const int i0 = member ? min(n, rank * m) : n, i1 = member ? min(n, i0 + m) : n;
-    float d = 0.0f;
-    for (int i = i0; i < i1; ++i) d += term(i);
-    // exclusive prefix of the chunk sums: only a guess of each chunk's starting binade.
-    float v = d;
+// 1/u for the binade with biased exponent e (24 <= e <= 253): 2^(150 - e), exact.
+__device__ __forceinline__ float seq_inv_ulp(int e) { return __uint_as_float((uint32_t)(277 - e) << 23); }
+
+// a = t / u (exact scaling) rounded to the nearest integer, with FADDs only: below 2^23,
+// a + 2^23 lands in [2^23, 2^24) where the float grid is the integers, so the add rounds
+// a half-even and the bit pattern holds the integer; from 2^23 on, a is an integer.
+// False for a tie (|rint(a) - a| = 1/2, the subtraction is exact), for a >= 2^24 and NaN.
+__device__ __forceinline__ bool seq_units(float a, uint32_t& c) {
+    const float y = a + 8388608.0f;
+    const bool lo = a < 8388608.0f;
+    const float r = y - 8388608.0f;
+    c = lo ? __float_as_uint(y) - 0x4b000000u : __float_as_uint(a) - 0x4a800000u;
+    const bool ok = a < 16777216.0f && (!lo || fabsf(r - a) != 0.5f);
+    if (!ok) c = 0;
+    return ok;
+}
+
+// Adds the terms a0 .. a0+m-1 (m <= 32) to x in order with real FADDs.  All loads are
+// issued before the first add.
+template <class Term>
+__device__ __forceinline__ float seq_fold32(const Term& term, int a0, int m, float x) {
+    float tv[32];
+#pragma unroll
+    for (int q = 0; q < 32; ++q) tv[q] = q < m ? term(a0 + q) : 0.0f;
+    asm volatile("" ::: "memory");
+#pragma unroll
+    for (int q = 0; q < 32; ++q) x = x + tv[q];   // + 0.0f is exact
+    return x;
+}
+
+// An entry {key, count} applies to the bit pattern sb iff sb lies in binade `key` and
+// stays there after the add.
+__device__ __forceinline__ bool seq_applies(uint32_t sb, uint32_t key, uint32_t cnt) {
+    return (sb >> 23) == key && ((sb + cnt) >> 23) == key;
+}
+
+template <class T>
+__device__ __forceinline__ T warp_incl_scan(T v, int lane) {
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-        float t = __shfl_up_sync(NCM_FULL, v, o);
+        const T t = __shfl_up_sync(NCM_FULL, v, o);
         if (lane >= o) v += t;
     }
-    float pre = v - d;
-    if (NT > 32) {
-        if (member && lane == 31) sc.part[rank >> 5] = v;
-        __syncthreads();
-        if (member)
-            for (int w = 0; w < (rank >> 5); ++w) pre += sc.part[w];
-    }
-    int eb = 0;
-    long long cnt = 0;
-    int bad = 0;
-    if (member && rank < C) {
-        const uint32_t gb = __float_as_uint(pre);
-        eb = (int)(gb >> 23);
-        if (eb < 1 || eb > 253) bad = 1;
-        for (int i = i0; i < i1 && !bad; ++i) {
-            const float a = ldexpf(term(i), 150 - eb);   // t / u, exact scaling
-            if (a >= 16777216.0f) { bad = 1; break; }
-            if (a - floorf(a) == 0.5f) { bad = 1; break; }
-            cnt += (long long)rintf(a);
+    return v;
+}
+
+// NT threads (one warp, or the whole 256-thread CTA) cooperate; `rank` is the thread's
+// index among them; the terms are read through term(i).  All NT threads get the result;
+// with NT > 32 every thread of the CTA must call (threads beyond NT only take part in
+// the barriers).
+template <int NT, class Term>
+__device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT>& sc, int rank) {
+    constexpr int NW = NT / 32;
+    constexpr int SEG = 32 * NT;            // terms per segment: one group per thread
+    if (n <= 0) return 0.0f;
+    const int lane = rank & 31, warp = rank >> 5;
+    const bool member = rank < NT;
+    for (int seg0 = 0; seg0 < n; seg0 += SEG) {
+        const int segn = min(n - seg0, SEG);
+        const int G = (segn + 31) >> 5;
+        const float carry = seg0 == 0 ? 0.0f : sc.result;
+        const int g = rank;
+        const bool mine = member && g < G;
+        // (1) this thread's group, read in rotated order (bank-conflict free)
+        float v[32];
+        float acc4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const int gb = 32 * g, m = mine ? min(32, segn - gb) : 0;
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+            const int idx = (q + lane) & 31;
+            v[q] = idx < m ? term(seg0 + gb + idx) : 0.0f;
+            acc4[q & 3] += v[q];
         }
-    }
-    if (member) {
-        sc.ebits[rank] = eb;
-        sc.cnt[rank] = cnt;
-        sc.bad[rank] = bad;
-    }
-    if (NT == 32) __syncwarp(); else __syncthreads();
-    if (rank < 32) {
-        float s = 0.0f;
-        int j = 0;
-        while (j < C) {
-            const uint32_t sb = __float_as_uint(s);
-            const int es = (int)(sb >> 23);
-            const bool normal = s > 0.0f && es >= 1 && es <= 253;
-            const long long k = normal ? (long long)((sb & 0x7fffffu) | 0x800000u) : 0;
-            const int c = j + lane;
-            const bool ok = normal && c < C && sc.ebits[c] == es && !sc.bad[c];
-            long long pv = ok ? sc.cnt[c] : 0;
+        const float acc = (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
+        float incl = warp_incl_scan(acc, lane);
+        if (NT > 32) {
+            if (member && lane == 31) sc.wsum[warp] = incl;
+            __syncthreads();
+            if (member)
+                for (int w = 0; w < warp; ++w) incl += sc.wsum[w];
+        }
+        // (2) guessed binade and ulp count
+        const float start = carry + (incl - acc), end = carry + incl;
+        const int e = (int)(__float_as_uint(start) >> 23);
+        bool ok = e >= 24 && e <= 253 && (int)(__float_as_uint(end) >> 23) == e;
+        const float inv = seq_inv_ulp(ok ? e : 150);
+        uint32_t cnt = 0;
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                long long t = __shfl_up_sync(NCM_FULL, pv, o);
-                if (lane >= o) pv += t;
+        for (int q = 0; q < 32; ++q) {
+            uint32_t c;
+            ok = seq_units(v[q] * inv, c) && ok;
+            cnt += c;
+        }
+        cnt = ok ? min(cnt, 1u << 23) : (1u << 23);
+        uint32_t cp = warp_incl_scan(cnt, lane);
+        if (NT > 32) {
+            if (member && lane == 31) sc.wcnt[warp] = cp;
+            __syncthreads();
+            if (member)
+                for (int w = 0; w < warp; ++w) cp += sc.wcnt[w];
+        }
+        if (mine) {
+            sc.key[g] = ok ? (uint32_t)e : ~0u;
+            sc.pre[g] = cp;
+        }
+        if (NT == 32) __syncwarp(); else __syncthreads();
+        // (3) the walk, by warp 0 in lockstep
+        if (rank < 32) {
+            uint32_t sb = __float_as_uint(carry);
+            int j = 0;
+            if (seg0 == 0) {
+                // the running value crosses binades every few terms at first: fold the
+                // first groups outright
+                const int m0 = min(segn, 32 * kSeqHead);
+                float x = 0.0f;
+                for (int i = 0; i < m0; i += 32) x = seq_fold32(term, i, min(32, m0 - i), x);
+                sb = __float_as_uint(x);
+                j = (m0 + 31) >> 5;
             }
-            const bool good = ok && (k + pv < 16777216ll);
-            const unsigned bal = __ballot_sync(NCM_FULL, good);
-            const int b = bal == NCM_FULL ? 32 : __ffs(~bal) - 1;
-            if (b > 0) {
-                const long long kk = k + __shfl_sync(NCM_FULL, pv, b - 1);
-                s = __uint_as_float(((uint32_t)es << 23) | (uint32_t)(kk & 0x7fffff));
-                j += b;
-            }
-            if (b < 32 && j < C) {
-                // fold chunk j term by term from the exact running value
-                float r = s;
-                if (lane == 0) {
-                    const int a0 = j * m, a1 = min(n, a0 + m);
-                    for (int i = a0; i < a1; i += 8) {
-                        float tv[8];
-#pragma unroll
-                        for (int q = 0; q < 8; ++q) tv[q] = (i + q < a1) ? term(i + q) : 0.0f;
-#pragma unroll
-                        for (int q = 0; q < 8; ++q)
-                            if (i + q < a1) r = r + tv[q];
-                    }
+            while (j < G) {
+                const int gi = j + lane;
+                const uint32_t base = j > 0 ? sc.pre[j - 1] : 0u;
+                const uint32_t p = gi < G ? sc.pre[gi] - base : 0u;
+                const bool good = gi >= G || seq_applies(sb, sc.key[gi], p);
+                const uint32_t bad = __ballot_sync(NCM_FULL, !good);
+                const int f = bad ? __ffs(bad) - 1 : 32;
+                const uint32_t add = __shfl_sync(NCM_FULL, p, (f - 1) & 31);
+                if (f == 32) {
+                    // all 32 (or all remaining) groups apply; lanes past G carry p = 0,
+                    // so read the count of the last real group
+                    sb += __shfl_sync(NCM_FULL, p, min(31, G - 1 - j));
+                    j += 32;
+                    continue;
                 }
-                s = __shfl_sync(NCM_FULL, r, 0);
-                j += 1;
+                if (f > 0) sb += add;
+                const int a0 = seg0 + 32 * (j + f);
+                const float x = seq_fold32(term, a0, min(32, n - a0), __uint_as_float(sb));
+                sb = __float_as_uint(x);
+                j += f + 1;
             }
+            if (rank == 0) sc.result = __uint_as_float(sb);
         }
-        if (rank == 0) sc.result = s;
+        if (NT == 32) __syncwarp(); else __syncthreads();
     }
-    if (NT == 32) __syncwarp(); else __syncthreads();
     return sc.result;
 }
 
@@ -1180,15 +1248,31 @@ int block_dots_launch(int qtype, const uint8_t* w, int64_t rows, int cols, const
     return (int)cudaGetLastError();
 }
 
-// inference.rs:697-706 rms_norm (one CTA): sequential-order sum of squares.
-__global__ void rms_norm_kernel(float* out, const float* x, const float* w, int n, float eps) {
+// inference.rs:697-706 rms_norm (one CTA): sequential-order sum of squares.  x is staged
+// in shared memory when it fits (the exact sum reads each term up to three times).
+__global__ void rms_norm_kernel(float* out, const float* x, const float* w, int n, float eps, int staged) {
+    extern __shared__ __align__(16) float xs[];
     __shared__ SeqSumScratch sc;
-    const float tot = seq_sum_nonneg<kThreads>([&](int i) { float v = x[i]; return v * v; }, n, sc, threadIdx.x);
+    float tot;
+    if (staged) {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = x[i];
+        __syncthreads();
+        tot = seq_sum_nonneg<kThreads>([&](int i) { float v = xs[i]; return v * v; }, n, sc, threadIdx.x);
+    } else {
+        tot = seq_sum_nonneg<kThreads>([&](int i) { float v = x[i]; return v * v; }, n, sc, threadIdx.x);
+    }
     const float scale = 1.0f / sqrtf(tot / (float)n + eps);
     for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = x[i] * scale * w[i];
 }
 int rms_norm_launch(float* out, const float* x, const float* w, int n, float eps, cudaStream_t s) {
-    rms_norm_kernel<<<1, kThreads, 0, s>>>(out, x, w, n, eps);
+    constexpr int kMaxStaged = 48 * 1024;   // floats (192 KB)
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxStaged * 4);
+        configured = true;
+    }
+    const int staged = n <= kMaxStaged;
+    rms_norm_kernel<<<1, kThreads, staged ? (size_t)n * 4 : 0, s>>>(out, x, w, n, eps, staged);
     return (int)cudaGetLastError();
 }
 

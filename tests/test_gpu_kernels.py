@@ -198,3 +198,66 @@ def test_peer_wait_times_out_cleanly(ncm, cuda):
     assert dt < 5.0
     x = cuda.ones(4, device="cuda")
     assert float(x.sum()) == 4.0
+
+
+def _rms_cases(rng):
+    yield "normal", rng.standard_normal(3072).astype(np.float32)
+    yield "normal_8192", rng.standard_normal(8192).astype(np.float32)
+    yield "normal_odd", rng.standard_normal(3001).astype(np.float32)
+    yield "segmented", rng.standard_normal(20011).astype(np.float32)
+    yield "one", np.array([3.0], dtype=np.float32)
+    yield "short", rng.standard_normal(33).astype(np.float32)
+    yield "ints_ties", rng.integers(-4096, 4096, size=8192).astype(np.float32)
+    yield "small_ints", rng.integers(-7, 8, size=4096).astype(np.float32)
+    yield "powers_of_two", np.ldexp(1.0, rng.integers(-30, 20, size=4096)).astype(np.float32)
+    yield "wide_range", (10.0 ** rng.uniform(-20, 5, size=4096) * rng.choice([-1, 1], size=4096)).astype(np.float32)
+    x = np.zeros(4096, dtype=np.float32)
+    x[1000::997] = 1.5
+    yield "sparse", x
+    x = rng.standard_normal(4096).astype(np.float32)
+    x[:2000] = 1e-30
+    yield "tiny_prefix", x
+    x = rng.standard_normal(2048).astype(np.float32) * 1e-3
+    x[0] = 1e4
+    yield "big_first", x
+    yield "quantised", (np.round(rng.standard_normal(3072) * 40) / 64).astype(np.float32)
+
+
+def test_rms_norm_bit_exact_sequential_sum(ncm, orc, cuda):
+    """The device sum of squares reproduces the reference's sequential f32 fold bit for bit
+    (inference.rs:697-706) on adversarial inputs: exact ties, binade crossings, zeros,
+    tiny and huge terms, lengths that are not multiples of 32 and beyond one segment."""
+    torch = cuda
+    L = orc.lib()
+    rng = np.random.default_rng(17)
+    for name, x in _rms_cases(rng):
+        n = x.size
+        w = (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+        ref = np.zeros(n, dtype=np.float32)
+        L.orc_rms_norm(orc.ptr(ref), orc.ptr(x), orc.ptr(w), n, np.float32(1e-5))
+        out = torch.zeros(n, dtype=torch.float32, device="cuda")
+        xd, wd = dev(torch, x), dev(torch, w)
+        ncm.rms_norm(out.data_ptr(), xd.data_ptr(), wd.data_ptr(), n, 1e-5)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), name
+
+
+def test_attention_bit_exact(ncm, orc, cuda):
+    """Scores, softmax (sequential denominator, glibc-exact exp) and the V accumulation
+    follow inference.rs:4242-4292 term by term: outputs equal the oracle's bit for bit."""
+    torch = cuda
+    L = orc.lib()
+    rng = np.random.default_rng(23)
+    for heads, kvh, hd, pos in [(4, 2, 64, 0), (32, 8, 64, 47), (24, 8, 128, 200), (32, 8, 128, 2500)]:
+        kvw = kvh * hd
+        q = rng.standard_normal(heads * hd).astype(np.float32)
+        kc = rng.standard_normal((pos + 1) * kvw).astype(np.float32) * 0.3
+        vc = rng.standard_normal((pos + 1) * kvw).astype(np.float32)
+        ref = np.zeros(heads * hd, dtype=np.float32)
+        L.orc_attention(orc.ptr(ref), orc.ptr(q), orc.ptr(kc), orc.ptr(vc), pos, heads, kvh, hd, kvw)
+        o = torch.zeros(heads * hd, dtype=torch.float32, device="cuda")
+        qd, kd, vd = dev(torch, q), dev(torch, kc), dev(torch, vc)
+        ncm.attention(o.data_ptr(), qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), pos, heads, kvh, hd)
+        torch.cuda.synchronize()
+        assert np.array_equal(o.cpu().numpy().view(np.uint32), ref.view(np.uint32)), (heads, kvh, hd, pos)
