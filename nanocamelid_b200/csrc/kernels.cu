@@ -24,6 +24,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <math.h>
+#include <algorithm>
 #include "ncm_internal.h"
 #include "common.cuh"
 #include "synth.h"
@@ -114,19 +115,20 @@ int expf_table_install(const uint32_t* dev_tab, uint32_t mask) {
 // and their prefix is kept modulo 2^32: along a step the sum grows by at most 2^23 per
 // lane, so the first lane that leaves the binade sees no wrap-around, and the walk
 // never looks past it.
-constexpr int kSeqHead = 4;   // groups folded outright at the start of a sum
+constexpr int kSeqHead = 128;     // terms folded outright at the start of a sum
+constexpr int kSeqSerial = 256;   // one-warp sums of at most this many terms: plain fold
 
-template <int NT>
+template <int NT, int GS>
 struct SeqSumScratchT {
-    static constexpr int kGroups = NT;        // groups (of 32 terms) per segment
+    static constexpr int kGroups = NT;        // groups (of GS terms) per segment
     uint32_t key[kGroups];                    // guessed biased exponent, ~0 if unusable
     uint32_t pre[kGroups];                    // inclusive prefix of the ulp counts
     float wsum[NT / 32];                      // per-warp totals for the block scans
     uint32_t wcnt[NT / 32];
     float result;
 };
-typedef SeqSumScratchT<kThreads> SeqSumScratch;
-typedef SeqSumScratchT<32> SeqSumScratchW;
+typedef SeqSumScratchT<kThreads, 16> SeqSumScratch;
+typedef SeqSumScratchT<32, 32> SeqSumScratchW;
 
 // 1/u for the binade with biased exponent e (24 <= e <= 253): 2^(150 - e), exact.
 __device__ __forceinline__ float seq_inv_ulp(int e) { return __uint_as_float((uint32_t)(277 - e) << 23); }
@@ -145,16 +147,16 @@ __device__ __forceinline__ bool seq_units(float a, uint32_t& c) {
     return ok;
 }
 
-// Adds the terms a0 .. a0+m-1 (m <= 32) to x in order with real FADDs.  All loads are
+// Adds the terms a0 .. a0+m-1 (m <= GS) to x in order with real FADDs.  All loads are
 // issued before the first add.
-template <class Term>
-__device__ __forceinline__ float seq_fold32(const Term& term, int a0, int m, float x) {
-    float tv[32];
+template <int GS, class Term>
+__device__ __forceinline__ float seq_fold(const Term& term, int a0, int m, float x) {
+    float tv[GS];
 #pragma unroll
-    for (int q = 0; q < 32; ++q) tv[q] = q < m ? term(a0 + q) : 0.0f;
+    for (int q = 0; q < GS; ++q) tv[q] = q < m ? term(a0 + q) : 0.0f;
     asm volatile("" ::: "memory");
 #pragma unroll
-    for (int q = 0; q < 32; ++q) x = x + tv[q];   // + 0.0f is exact
+    for (int q = 0; q < GS; ++q) x = x + tv[q];   // + 0.0f is exact
     return x;
 }
 
@@ -178,26 +180,32 @@ __device__ __forceinline__ T warp_incl_scan(T v, int lane) {
 // index among them; the terms are read through term(i).  All NT threads get the result;
 // with NT > 32 every thread of the CTA must call (threads beyond NT only take part in
 // the barriers).
-template <int NT, class Term>
-__device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT>& sc, int rank) {
-    constexpr int NW = NT / 32;
-    constexpr int SEG = 32 * NT;            // terms per segment: one group per thread
+template <int NT, int GS, class Term>
+__device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT, GS>& sc, int rank) {
+    static_assert(GS == 16 || GS == 32, "group size");
+    constexpr int SEG = GS * NT;            // terms per segment: one group per thread
     if (n <= 0) return 0.0f;
     const int lane = rank & 31, warp = rank >> 5;
     const bool member = rank < NT;
+    if (NT == 32 && n <= kSeqSerial) {
+        float x = 0.0f;
+        for (int i = 0; i < n; i += 32) x = seq_fold<32>(term, i, min(32, n - i), x);
+        return x;
+    }
     for (int seg0 = 0; seg0 < n; seg0 += SEG) {
         const int segn = min(n - seg0, SEG);
-        const int G = (segn + 31) >> 5;
+        const int G = (segn + GS - 1) / GS;
         const float carry = seg0 == 0 ? 0.0f : sc.result;
         const int g = rank;
         const bool mine = member && g < G;
         // (1) this thread's group, read in rotated order (bank-conflict free)
-        float v[32];
+        float v[GS];
         float acc4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        const int gb = 32 * g, m = mine ? min(32, segn - gb) : 0;
+        const int gb = GS * g, m = mine ? min(GS, segn - gb) : 0;
+        const int rot = GS == 32 ? lane : (lane >> 1);
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
-            const int idx = (q + lane) & 31;
+        for (int q = 0; q < GS; ++q) {
+            const int idx = (q + rot) & (GS - 1);
             v[q] = idx < m ? term(seg0 + gb + idx) : 0.0f;
             acc4[q & 3] += v[q];
         }
@@ -216,7 +224,7 @@ __device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT>& sc,
         const float inv = seq_inv_ulp(ok ? e : 150);
         uint32_t cnt = 0;
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
+        for (int q = 0; q < GS; ++q) {
             uint32_t c;
             ok = seq_units(v[q] * inv, c) && ok;
             cnt += c;
@@ -240,12 +248,12 @@ __device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT>& sc,
             int j = 0;
             if (seg0 == 0) {
                 // the running value crosses binades every few terms at first: fold the
-                // first groups outright
-                const int m0 = min(segn, 32 * kSeqHead);
+                // first terms outright
+                const int m0 = min(segn, kSeqHead);
                 float x = 0.0f;
-                for (int i = 0; i < m0; i += 32) x = seq_fold32(term, i, min(32, m0 - i), x);
+                for (int i = 0; i < m0; i += 32) x = seq_fold<32>(term, i, min(32, m0 - i), x);
                 sb = __float_as_uint(x);
-                j = (m0 + 31) >> 5;
+                j = (m0 + GS - 1) / GS;
             }
             while (j < G) {
                 const int gi = j + lane;
@@ -263,8 +271,8 @@ __device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT>& sc,
                     continue;
                 }
                 if (f > 0) sb += add;
-                const int a0 = seg0 + 32 * (j + f);
-                const float x = seq_fold32(term, a0, min(32, n - a0), __uint_as_float(sb));
+                const int a0 = seg0 + GS * (j + f);
+                const float x = seq_fold<GS>(term, a0, min(GS, n - a0), __uint_as_float(sb));
                 sb = __float_as_uint(x);
                 j += f + 1;
             }
@@ -433,6 +441,25 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, in
         : "memory");
 }
 
+// Copies n floats (n a multiple of 4, both pointers 16-byte aligned) from global to
+// shared memory with up to eight float4 loads per thread in flight.
+__device__ __forceinline__ void stage_f32(float* dst, const float* src, int n, int tid, int nthreads) {
+    const int n4 = n >> 2;
+    for (int base = 0; base < n4; base += 8 * nthreads) {
+        float4 r[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int i = base + k * nthreads + tid;
+            if (i < n4) r[k] = reinterpret_cast<const float4*>(src)[i];
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int i = base + k * nthreads + tid;
+            if (i < n4) reinterpret_cast<float4*>(dst)[i] = r[k];
+        }
+    }
+}
+
 // ------------------------------------------------------------------ prologue
 // Quantises the activation (optionally RMS-normalised) into shared memory.
 template <int IN>
@@ -469,18 +496,18 @@ __device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, SeqSumScratch&
         }
     } else {
         float scale = 1.0f;
+        // the input vector, staged with coalesced loads
+        float* xf = reinterpret_cast<float*>(smem + p.xf_off);
+        stage_f32(xf, p.x, p.cols, tid, blockDim.x);
+        __syncthreads();
         if constexpr (IN == IN_F32_RMS) {
-            float* xf = reinterpret_cast<float*>(smem + p.xf_off);
-            for (int i = tid * 4; i < p.cols; i += 4 * blockDim.x)
-                *reinterpret_cast<float4*>(xf + i) = *reinterpret_cast<const float4*>(p.x + i);
-            __syncthreads();
             float tot;
             if (p.ssq_tok) {
                 // Layer 0: sum of squares of the embedding row, folded sequentially at load.
                 tot = p.ssq_tok[p.tokens[p.state[ST_POS]]];
             } else {
                 // inference.rs:698-701: sum += val * val, sequential.
-                tot = seq_sum_nonneg<kThreads>([&](int i) { float v = xf[i]; return v * v; }, p.cols, sc, tid);
+                tot = seq_sum_nonneg<kThreads, 16>([&](int i) { float v = xf[i]; return v * v; }, p.cols, sc, tid);
             }
             scale = 1.0f / sqrtf(tot / (float)p.cols + p.eps);
         }
@@ -489,31 +516,31 @@ __device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, SeqSumScratch&
             float s = 0.0f;
             int sum = 0;
             if (b < p.nb) {
+                // The block's eight float4 groups are read starting at group (b & 7), so
+                // the eight lanes of a shared-memory phase hit distinct banks; amax and
+                // the sum are order free and each group quantises into its own word.
                 float v[32];
-                if constexpr (IN == IN_F32_RMS) {
-                    const float* xf = reinterpret_cast<const float*>(smem + p.xf_off) + 32 * b;
-                    const float4* nw = reinterpret_cast<const float4*>(p.norm_w + 32 * b);
+                const float4* xb = reinterpret_cast<const float4*>(xf) + 8 * b;
+                const int rot = b & 7;
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        float4 w4 = nw[i];
+                for (int i = 0; i < 8; ++i) {
+                    const int j = (i + rot) & 7;
+                    const float4 x4 = xb[j];
+                    if constexpr (IN == IN_F32_RMS) {
+                        const float4 w4 = reinterpret_cast<const float4*>(smem + p.nw_off)[8 * b + j];
                         // inference.rs:704 out = x * scale * weight
-                        v[4 * i] = xf[4 * i] * scale * w4.x;
-                        v[4 * i + 1] = xf[4 * i + 1] * scale * w4.y;
-                        v[4 * i + 2] = xf[4 * i + 2] * scale * w4.z;
-                        v[4 * i + 3] = xf[4 * i + 3] * scale * w4.w;
-                    }
-                } else {
-                    const float4* src = reinterpret_cast<const float4*>(p.x + 32 * b);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        float4 t = src[i];
-                        v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+                        v[4 * i] = x4.x * scale * w4.x;
+                        v[4 * i + 1] = x4.y * scale * w4.y;
+                        v[4 * i + 2] = x4.z * scale * w4.z;
+                        v[4 * i + 3] = x4.w * scale * w4.w;
+                    } else {
+                        v[4 * i] = x4.x; v[4 * i + 1] = x4.y; v[4 * i + 2] = x4.z; v[4 * i + 3] = x4.w;
                     }
                 }
                 uint32_t w[8];
                 quant_block32(v, w, s, sum);
 #pragma unroll
-                for (int k = 0; k < 8; ++k) dst[k] = w[k];
+                for (int i = 0; i < 8; ++i) dst[(i + rot) & 7] = w[i];
             } else {
 #pragma unroll
                 for (int k = 0; k < 8; ++k) dst[k] = 0;
@@ -610,6 +637,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     if (tid == kProducer) {
         pol = l2_evict_first_policy();
         while (tprod < ns && icur < r_end) issue();
+    }
+    if constexpr (IN == IN_F32_RMS) {
+        // norm weights are constant: stage them before waiting for the previous kernel
+        stage_f32(reinterpret_cast<float*>(smem + p.nw_off), p.norm_w, p.cols, tid, blockDim.x);
     }
     pdl_launch_dependents();
     pdl_wait();
@@ -905,8 +936,10 @@ int gemv_plan(int qtype, int cols, int rows, bool dual, int in_mode, GemvParams&
     p.xf_off = off;
     p.t_off = off;
     int shared_region = ns * kMaxFold * kTStride * 4;
-    if (in_mode == IN_F32_RMS && cols * 4 > shared_region) shared_region = cols * 4;
+    if (in_mode != IN_Q8 && cols * 4 > shared_region) shared_region = cols * 4;
     off += (shared_region + 127) / 128 * 128;
+    p.nw_off = off;
+    if (in_mode == IN_F32_RMS) off += (cols * 4 + 127) / 128 * 128;
     p.stage_off = off;
     while (ns > 2 && off + ns * p.stage_bytes > 200 * 1024) --ns;
     p.nstages = ns;
@@ -956,11 +989,24 @@ int gemv_launch(int qtype, int in_mode, int epi, const GemvParams& p, int grid, 
 
 // ------------------------------------------------------------------ attention
 // inference.rs:4242-4292 apply_attention_head, f32 cache, term by term.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// 16-byte vector access is used when every base pointer is 16-byte aligned (rows of
+// q / K / V start at multiples of head_dim, a multiple of 32 floats).
+__device__ __forceinline__ bool attn_vec_ok(const AttnParams& a) {
+    return (((uintptr_t)a.q | (uintptr_t)a.kc | (uintptr_t)a.vc) & 15) == 0 && (a.kvw & 3) == 0;
+}
+
 // Stage 1 (attn_scores_kernel): scores[h][p] = dot_f32(q_h, k_p) * scale with the dot a
 // sequential sum over head_dim (inference.rs:3570-3573, 4256); grid (kv head, 32
-// positions), warp = query head of the group, lane = position.
+// positions), warp = query head of the group, lane = position.  The K tile is loaded
+// with all its loads in flight at once, then transposed into a padded shared array.
 __global__ void __launch_bounds__(256) attn_scores_kernel(const __grid_constant__ AttnParams a) {
-    __shared__ float qs[8 * 256];
+    __shared__ __align__(16) float qs[8 * 256];
     __shared__ float ks[32 * 257];
     pdl_launch_dependents();
     pdl_wait();
@@ -970,11 +1016,38 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const __grid_constant_
     if (p0 >= n) return;
     const int kvh = blockIdx.x, g = a.heads / a.kv_heads, hd = a.hd;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int i = tid; i < g * hd; i += 256) qs[i] = a.q[(size_t)kvh * g * hd + i];
     const int np = min(32, n - p0);
-    for (int i = tid; i < np * hd; i += 256) {
-        const int pl = i / hd, d = i % hd;
-        ks[pl * (hd + 1) + d] = a.kc[(size_t)(p0 + pl) * a.kvw + (size_t)kvh * hd + d];
+    const float* qsrc = a.q + (size_t)kvh * g * hd;
+    const float* ksrc = a.kc + (size_t)p0 * a.kvw + (size_t)kvh * hd;
+    if (attn_vec_ok(a)) {
+        const int per = hd >> 2;                 // float4 per row
+        float4 qv[2], kv[8];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int i = tid + 256 * k;
+            if (i < g * per) qv[k] = reinterpret_cast<const float4*>(qsrc)[i];
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int i = tid + 256 * k;
+            if (i < np * per) kv[k] = *reinterpret_cast<const float4*>(ksrc + (size_t)(i / per) * a.kvw + 4 * (i % per));
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int i = tid + 256 * k;
+            if (i < g * per) reinterpret_cast<float4*>(qs)[i] = qv[k];
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int i = tid + 256 * k;
+            if (i < np * per) {
+                float* d = ks + (i / per) * (hd + 1) + 4 * (i % per);
+                d[0] = kv[k].x; d[1] = kv[k].y; d[2] = kv[k].z; d[3] = kv[k].w;
+            }
+        }
+    } else {
+        for (int i = tid; i < g * hd; i += 256) qs[i] = qsrc[i];
+        for (int i = tid; i < np * hd; i += 256) ks[(i / hd) * (hd + 1) + i % hd] = ksrc[(size_t)(i / hd) * a.kvw + i % hd];
     }
     __syncthreads();
     for (int h = warp; h < g; h += 8) {
@@ -982,6 +1055,7 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const __grid_constant_
             const float* q = qs + h * hd;
             const float* k = ks + lane * (hd + 1);
             float s = 0.0f;
+#pragma unroll 8
             for (int d = 0; d < hd; ++d) s += q[d] * k[d];
             a.scores[(size_t)(kvh * g + h) * a.ctx + p0 + lane] = s * a.scale;
         }
@@ -991,9 +1065,11 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const __grid_constant_
 // Stage 2 (attn_softmax_v_kernel): grid (kv head, dim split).  softmax
 // (inference.rs:3522-3540: max, exp(x - max), sequential sum, *= 1/sum) per query head
 // by one warp each, then out[d] = sum_p w_p * v_p[d] sequential over p per (head, dim)
-// (attn_output zeroed, add_weighted_f32_scalar inference.rs:3619-3623).
+// (attn_output zeroed, add_weighted_f32_scalar inference.rs:3619-3623).  The CTA's V
+// columns are copied into shared memory by cp.async, the first chunk while the softmax
+// runs.
 __global__ void __launch_bounds__(256) attn_softmax_v_kernel(const __grid_constant__ AttnParams a) {
-    extern __shared__ __align__(16) float w[];   // [g][n] softmax weights
+    extern __shared__ __align__(16) float sm[];   // w[g][n] softmax weights, then V chunk
     __shared__ SeqSumScratchW scr[8];
     pdl_launch_dependents();
     pdl_wait();
@@ -1001,6 +1077,24 @@ __global__ void __launch_bounds__(256) attn_softmax_v_kernel(const __grid_consta
     const int n = pos + 1;
     const int kvh = blockIdx.x, g = a.heads / a.kv_heads, hd = a.hd;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int dw = hd / a.dsplit;
+    const int d0 = blockIdx.y * dw;
+    float* w = sm;
+    float* vs = sm + ((g * a.ctx + 3) & ~3);
+    const bool vec = attn_vec_ok(a) && (dw & 3) == 0;
+    const float* vsrc = a.vc + (size_t)kvh * hd + d0;
+    auto stage = [&](int c0) {
+        const int np = min(a.vchunk, n - c0);
+        if (vec) {
+            const int per = dw >> 2;
+            for (int i = tid; i < np * per; i += 256)
+                cp_async16(vs + 4 * i, vsrc + (size_t)(c0 + i / per) * a.kvw + 4 * (i % per));
+            cp_async_commit();
+        } else {
+            for (int i = tid; i < np * dw; i += 256) vs[i] = vsrc[(size_t)(c0 + i / dw) * a.kvw + i % dw];
+        }
+    };
+    stage(0);
     if (warp < g) {
         const int h = kvh * g + warp;
         const float* srow = a.scores + (size_t)h * a.ctx;
@@ -1015,39 +1109,55 @@ __global__ void __launch_bounds__(256) attn_softmax_v_kernel(const __grid_consta
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(NCM_FULL, mx, o));
         for (int p = lane; p < n; p += 32) wr[p] = expf_cr(wr[p] - mx);
         __syncwarp();
-        const float sum = seq_sum_nonneg<32>([&](int i) { return wr[i]; }, n, scr[warp], lane);
+        const float sum = seq_sum_nonneg<32, 32>([&](int i) { return wr[i]; }, n, scr[warp], lane);
         const float inv = 1.0f / sum;
         for (int p = lane; p < n; p += 32) wr[p] = wr[p] * inv;
     }
-    __syncthreads();
-    const int dw = hd / a.dsplit;
-    const int d0 = blockIdx.y * dw;
-    for (int item = tid; item < g * dw; item += 256) {
-        const int h = item / dw, d = d0 + item % dw;
-        const float* wr = w + h * n;
-        const float* vp = a.vc + (size_t)kvh * hd + d;
-        float acc = 0.0f;
-        int p = 0;
-        for (; p + 4 <= n; p += 4) {
-            const float v0 = vp[(size_t)p * a.kvw], v1 = vp[(size_t)(p + 1) * a.kvw];
-            const float v2 = vp[(size_t)(p + 2) * a.kvw], v3 = vp[(size_t)(p + 3) * a.kvw];
-            acc += wr[p] * v0;
-            acc += wr[p + 1] * v1;
-            acc += wr[p + 2] * v2;
-            acc += wr[p + 3] * v3;
+    const int item = tid, h = item / dw, d = item % dw;
+    const bool live = item < g * dw;
+    const float* wr = w + h * n;
+    float acc = 0.0f;
+    for (int c0 = 0; c0 < n; c0 += a.vchunk) {
+        if (c0 > 0) {
+            __syncthreads();   // every thread is done with the previous chunk
+            stage(c0);
         }
-        for (; p < n; ++p) acc += wr[p] * vp[(size_t)p * a.kvw];
-        a.out[(size_t)(kvh * g + h) * hd + d] = acc;
+        if (vec) cp_async_wait_all();
+        __syncthreads();
+        if (live) {
+            const int np = min(a.vchunk, n - c0);
+            const float* wp = wr + c0;
+            const float* vp = vs + d;
+            int p = 0;
+            for (; p + 4 <= np; p += 4) {
+                const float w0 = wp[p], w1 = wp[p + 1], w2 = wp[p + 2], w3 = wp[p + 3];
+                const float v0 = vp[p * dw], v1 = vp[(p + 1) * dw], v2 = vp[(p + 2) * dw], v3 = vp[(p + 3) * dw];
+                acc += w0 * v0;
+                acc += w1 * v1;
+                acc += w2 * v2;
+                acc += w3 * v3;
+            }
+            for (; p < np; ++p) acc += wp[p] * vp[p * dw];
+        }
     }
+    if (live) a.out[(size_t)(kvh * g + h) * hd + d0 + d] = acc;
 }
 
-int attention_launch(const AttnParams& a, cudaStream_t s, bool pdl) {
+int attention_launch(const AttnParams& a0, cudaStream_t s, bool pdl) {
     static bool configured = false;
+    constexpr int kMaxSmem = 200 * 1024;
     if (!configured) {
-        cudaFuncSetAttribute(attn_softmax_v_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(attn_softmax_v_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
         configured = true;
     }
-    const int g = a.heads / a.kv_heads;
+    AttnParams a = a0;
+    const int g = a.heads / a.kv_heads, dw = a.hd / a.dsplit;
+    const size_t wbytes = (size_t)((g * a.ctx + 3) & ~3) * sizeof(float);
+    if (wbytes + 32 * dw * sizeof(float) > (size_t)kMaxSmem || g * dw > 256) return (int)cudaErrorInvalidValue;
+    int vchunk = (int)std::min<size_t>((kMaxSmem - wbytes) / (dw * sizeof(float)), 32768 / (dw * sizeof(float)) * 4);
+    vchunk = std::min(vchunk, (a.ctx + 31) & ~31);
+    vchunk = std::max(32, vchunk & ~31);
+    a.vchunk = vchunk;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -1060,7 +1170,7 @@ int attention_launch(const AttnParams& a, cudaStream_t s, bool pdl) {
     int r = (int)cudaLaunchKernelEx(&cfg, attn_scores_kernel, a);
     if (r) return r;
     cfg.gridDim = dim3(a.kv_heads, a.dsplit);
-    cfg.dynamicSmemBytes = (size_t)g * a.ctx * sizeof(float);
+    cfg.dynamicSmemBytes = wbytes + (size_t)vchunk * dw * sizeof(float);
     return (int)cudaLaunchKernelEx(&cfg, attn_softmax_v_kernel, a);
 }
 
@@ -1257,9 +1367,9 @@ __global__ void rms_norm_kernel(float* out, const float* x, const float* w, int 
     if (staged) {
         for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = x[i];
         __syncthreads();
-        tot = seq_sum_nonneg<kThreads>([&](int i) { float v = xs[i]; return v * v; }, n, sc, threadIdx.x);
+        tot = seq_sum_nonneg<kThreads, 16>([&](int i) { float v = xs[i]; return v * v; }, n, sc, threadIdx.x);
     } else {
-        tot = seq_sum_nonneg<kThreads>([&](int i) { float v = x[i]; return v * v; }, n, sc, threadIdx.x);
+        tot = seq_sum_nonneg<kThreads, 16>([&](int i) { float v = x[i]; return v * v; }, n, sc, threadIdx.x);
     }
     const float scale = 1.0f / sqrtf(tot / (float)n + eps);
     for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = x[i] * scale * w[i];

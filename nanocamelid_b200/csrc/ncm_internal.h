@@ -61,7 +61,7 @@ struct alignas(64) GemvParams {
     int chunk_words, chunk_bytes; // TMA box inner extent per row
     int box_rows;                 // rows per tile (TMA box outer extent)
     int stage_bytes, nstages;
-    int xq_off, xs_off, xsum_off, xf_off, t_off, stage_off, smem_bytes;
+    int xq_off, xs_off, xsum_off, xf_off, nw_off, t_off, stage_off, smem_bytes;
     // input
     const float* x;               // IN_F32 / IN_F32_RMS
     const float* norm_w;
@@ -96,6 +96,7 @@ struct AttnParams {
     const int* state;
     int pos_override;        // >= 0: use instead of state[ST_POS]
     int heads, kv_heads, hd, kvw, ctx, dsplit;
+    int vchunk;              // positions of V staged in shared memory at a time (set by attention_launch)
     float scale;
 };
 
