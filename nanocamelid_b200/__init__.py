@@ -72,13 +72,15 @@ _lib = None
 
 
 def lib():
-    """Loads libncm.so (fails loudly if it has not been built)."""
+    """Loads libncm.so (fails loudly if it has not been built).  NCM_LIBRARY, when set,
+    names another build of the same library to load instead."""
     global _lib
     if _lib is not None:
         return _lib
-    if not os.path.exists(LIB_PATH):
-        raise ImportError(f"{LIB_PATH} missing: run `python -m nanocamelid_b200.build` (or __graft_entry__.build())")
-    L = ctypes.CDLL(LIB_PATH)
+    path = os.environ.get("NCM_LIBRARY") or LIB_PATH
+    if not os.path.exists(path):
+        raise ImportError(f"{path} missing: run `python -m nanocamelid_b200.build` (or __graft_entry__.build())")
+    L = ctypes.CDLL(os.path.abspath(path))
     c_int, c_i64, c_p, c_f, c_u64 = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_float, ctypes.c_uint64
     pint = ctypes.POINTER(ctypes.c_int)
     pu8 = ctypes.POINTER(ctypes.c_uint8)

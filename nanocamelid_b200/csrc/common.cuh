@@ -53,6 +53,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
     }
 }
 
+// CTA-scope flags in shared memory: release store / acquire load, and a bounded wait for
+// a flag to reach a value (false after limit_ns).
+__device__ __forceinline__ uint32_t ld_acquire_cta(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_cta(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ bool flag_wait_geq(const uint32_t* p, uint32_t v, uint64_t limit_ns) {
+    if (ld_acquire_cta(p) >= v) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (ld_acquire_cta(p) >= v) return true;
+        if ((i & 1023) == 0 && global_timer_ns() - t0 > limit_ns) return false;
+    }
+}
+
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     uint64_t pol;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));

@@ -516,6 +516,7 @@ static int launch_gemv(std::initializer_list<const DevMat*> mats, const DevMat* 
                        GemvParams& p, cudaStream_t s) {
     const DevMat& w0 = **mats.begin();
     const int grid = gemv_plan(w0.type, w0.cols, p.total_rows, up != nullptr, in_mode, p);
+    if (grid < 0) return (int)cudaErrorInvalidValue;
     int i = 0;
     for (const DevMat* d : mats) {
         int r = gemv_tensor_map(&p.tm[i++], d->d, d->rows, d->pitch, p.chunk_words, p.box_rows);
@@ -923,7 +924,7 @@ static ncm_status seam_gemv(int qtype, const void* w, int64_t rows, int cols, co
     p.xs = x_scales;
     p.tp.world = 1;
     const int grid = gemv_plan(qtype, cols, (int)rows, false, IN_Q8, p);
-    int r = gemv_tensor_map(&p.tm[0], base, rows, pitch, p.chunk_words, p.box_rows);
+    int r = grid < 0 ? (int)cudaErrorInvalidValue : gemv_tensor_map(&p.tm[0], base, rows, pitch, p.chunk_words, p.box_rows);
     if (!r) r = gemv_launch(qtype, IN_Q8, EPI_PLAIN, p, grid, s, false);
     if (tmp) cudaFreeAsync(tmp, s);
     if (r) return fail(NCM_ECUDA, std::string("gemv launch: ") + cudaGetErrorString((cudaError_t)r));

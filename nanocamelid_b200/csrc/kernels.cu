@@ -99,36 +99,43 @@ int expf_table_install(const uint32_t* dev_tab, uint32_t mask) {
 // Within one binade [2^e, 2^(e+1)) floats are a grid of spacing u, and for s = k*u,
 // RN(s + t) = u * (k + rint(t/u)) unless t/u is an exact half-integer (a tie, whose
 // result depends on the parity of k) or the sum leaves the binade.  So a run of terms
-// adds a fixed integer number of ulps -- to the bit pattern of s -- independent of
-// where in the binade it starts.
+// that keeps the running value inside one binade adds a fixed integer number of ulps
+// -- to the bit pattern of s -- independent of where in the binade it starts.
 //
-// The terms are cut into groups of 32, one thread per group.  From an approximate
-// (reassociated) prefix sum each group gets a guessed binade for the running value; a
-// group whose guess holds across the group and that has no tie gets its integer ulp
-// count in that binade.  One warp then walks the groups with the exact running value,
-// 32 groups per step: the leading groups whose guess equals the true binade and whose
-// counts keep the sum inside it are one integer add on the bit pattern; the first
-// group that fails is folded term by term with real FADDs.  Folds happen about once
-// per binade crossing.  Guesses only affect speed, never the result.
+// Which binade the running value S(i) is in is certified from an approximate prefix
+// A(i) computed in parallel: for nonnegative terms the sequential fold satisfies
+// |S(i) - R(i)| <= gamma_i R(i), and any summation tree in which every term goes
+// through at most d additions satisfies |A(i) - R(i)| <= gamma_d R(i), where R is the
+// exact sum and gamma_k = k u / (1 - k u), u = 2^-24 (Higham, "Accuracy and Stability
+// of Numerical Algorithms", 2nd ed., section 4.2).  A term is "certain" when
+// A(i-1)(1 - mg) and A(i)(1 + mg) lie in the same binade, mg = 4 u (i + 128) covering
+// both bounds (here d < 90) and the rounding of the two products; S(i-1) and S(i) are
+// then provably in that binade and, barring a tie, the term adds rint(t/u) ulps.  The
+// other terms ("uncertain": binade crossings, ties, the first terms) are listed in
+// order; one thread walks the list, adding the ulp count of the certain run before
+// each listed term to the bit pattern and the listed term itself with a real FADD --
+// about one integer add and one FADD per binade crossing.
 //
-// Counts are capped at 2^23 per group (a capped group can never stay in its binade)
-// and their prefix is kept modulo 2^32: along a step the sum grows by at most 2^23 per
-// lane, so the first lane that leaves the binade sees no wrap-around, and the walk
-// never looks past it.
-constexpr int kSeqHead = 128;     // terms folded outright at the start of a sum
+// Each thread owns a chunk of KM consecutive terms (KM odd, so a warp's reads hit
+// distinct banks) held in registers; every per-term step is unrolled so that the
+// terms' latencies overlap.  A list that would overflow falls back to a plain
+// sequential fold.  Counts are kept modulo 2^32: only differences between consecutive
+// list entries are used, each below 2^24.
 constexpr int kSeqSerial = 256;   // one-warp sums of at most this many terms: plain fold
 
-template <int NT, int GS>
+template <int NT>
 struct SeqSumScratchT {
-    static constexpr int kGroups = NT;        // groups (of GS terms) per segment
-    uint32_t key[kGroups];                    // guessed biased exponent, ~0 if unusable
-    uint32_t pre[kGroups];                    // inclusive prefix of the ulp counts
-    float wsum[NT / 32];                      // per-warp totals for the block scans
-    uint32_t wcnt[NT / 32];
+    static constexpr int kList = NT > 32 ? 512 : 128;   // uncertain terms per segment
+    float lt[kList];                    // the uncertain terms, in order
+    uint32_t lc[kList];                 // certain-term ulp count before each (mod 2^32)
+    float wsum[NT / 32];                // per-warp totals for the block scans
+    uint32_t wcnt[NT / 32], wunc[NT / 32];
+    uint32_t tail;                      // certain-term ulp count of the whole segment
+    int nlist;
     float result;
 };
-typedef SeqSumScratchT<kThreads, 16> SeqSumScratch;
-typedef SeqSumScratchT<32, 32> SeqSumScratchW;
+typedef SeqSumScratchT<kThreads> SeqSumScratch;
+typedef SeqSumScratchT<32> SeqSumScratchW;
 
 // 1/u for the binade with biased exponent e (24 <= e <= 253): 2^(150 - e), exact.
 __device__ __forceinline__ float seq_inv_ulp(int e) { return __uint_as_float((uint32_t)(277 - e) << 23); }
@@ -142,8 +149,26 @@ __device__ __forceinline__ bool seq_units(float a, uint32_t& c) {
     const bool lo = a < 8388608.0f;
     const float r = y - 8388608.0f;
     c = lo ? __float_as_uint(y) - 0x4b000000u : __float_as_uint(a) - 0x4a800000u;
-    const bool ok = a < 16777216.0f && (!lo || fabsf(r - a) != 0.5f);
-    if (!ok) c = 0;
+    const bool ok = (a < 16777216.0f) & (!lo | (fabsf(r - a) != 0.5f));
+    c = ok ? c : 0u;
+    return ok;
+}
+
+// Term t at global index i, added to a running value whose approximate prefix is ae
+// before and ai after the add: true when the running value provably stays in one
+// binade and t is no tie there; c = t in ulps of that binade (0 otherwise).  With
+// mg = (i + 128) 2^-22, "ae (1 - mg) and ai (1 + mg) in the binade of ae" is checked
+// on the significand bits: frac(ae) >= mg and frac(ai) <= 1 - 2 mg with frac the
+// fraction field in units of 2^-23, mg 2^23 = 2 (i + 128), plus one unit for the
+// roundings of the comparison itself.
+__device__ __forceinline__ bool seq_certain(float t, float ae, float ai, int i, uint32_t& c) {
+    const uint32_t be = __float_as_uint(ae), bi = __float_as_uint(ai);
+    const int e = (int)(be >> 23);
+    const uint32_t m = 2u * (uint32_t)(i + 128) + 1u;
+    const bool in = (e >= 24) & (e <= 253) & ((int)(bi >> 23) == e) & ((be & 0x7fffffu) >= m) &
+                    ((bi & 0x7fffffu) + 2u * m <= 0x7fffffu);
+    const bool ok = seq_units(t * seq_inv_ulp(in ? e : 150), c) & in;
+    c = ok ? c : 0u;
     return ok;
 }
 
@@ -160,12 +185,6 @@ __device__ __forceinline__ float seq_fold(const Term& term, int a0, int m, float
     return x;
 }
 
-// An entry {key, count} applies to the bit pattern sb iff sb lies in binade `key` and
-// stays there after the add.
-__device__ __forceinline__ bool seq_applies(uint32_t sb, uint32_t key, uint32_t cnt) {
-    return (sb >> 23) == key && ((sb + cnt) >> 23) == key;
-}
-
 template <class T>
 __device__ __forceinline__ T warp_incl_scan(T v, int lane) {
 #pragma unroll
@@ -176,111 +195,147 @@ __device__ __forceinline__ T warp_incl_scan(T v, int lane) {
     return v;
 }
 
+// One segment (at most KM * NT terms) continuing from the exact value carry.
+template <int NT, int KM, class Term>
+__device__ float seq_sum_segment(const Term& term, int seg0, int segn, float carry, SeqSumScratchT<NT>& sc,
+                                 int rank) {
+    constexpr int kList = SeqSumScratchT<NT>::kList;
+    const int lane = rank & 31, warp = rank >> 5;
+    const bool member = rank < NT;
+    const int i0 = member ? rank * KM : segn;
+    // (1) the chunk into registers; approximate exclusive prefix of the chunk
+    float v[KM];
+#pragma unroll
+    for (int q = 0; q < KM; ++q) v[q] = i0 + q < segn ? term(seg0 + i0 + q) : 0.0f;
+    float loc[KM];
+    float tot = 0.0f;
+#pragma unroll
+    for (int q = 0; q < KM; ++q) { tot = tot + v[q]; loc[q] = tot; }
+    const float incl = warp_incl_scan(tot, lane);
+    float excl = __shfl_up_sync(NCM_FULL, incl, 1);
+    if (lane == 0) excl = 0.0f;
+    float base = 0.0f;
+    if (NT > 32) {
+        if (member && lane == 31) sc.wsum[warp] = incl;
+        __syncthreads();
+        if (member)
+            for (int w = 0; w < warp; ++w) base += sc.wsum[w];
+    }
+    const float off = base + excl;
+    // (2) certify each term.  Fast path: the chunk's two ends certify one binade for
+    // the whole chunk (S is monotone), then a term is uncertain only if it is a tie.
+    uint32_t c[KM];
+    uint64_t umask = 0;   // KM may exceed 32
+    uint32_t cnt = 0;
+    const int nq = min(KM, max(0, segn - i0));
+    bool chunk_ok = false;
+    int ec = 150;
+    if (nq > 0) {
+        const float a0 = carry + off, a1 = carry + (off + loc[KM - 1]);
+        const float mg = (float)(seg0 + i0 + KM + 128) * 0x1p-22f;
+        ec = (int)(__float_as_uint(a0) >> 23);
+        chunk_ok = (ec >= 24) & (ec <= 253) & ((int)(__float_as_uint(a0 * (1.0f - mg)) >> 23) == ec) &
+                   ((int)(__float_as_uint(a1 * (1.0f + mg)) >> 23) == ec);
+    }
+    if (chunk_ok) {
+        const float inv = seq_inv_ulp(ec);
+#pragma unroll
+        for (int q = 0; q < KM; ++q) {
+            uint32_t cq;
+            const bool ok = seq_units(v[q] * inv, cq);   // padding terms are 0: ok, count 0
+            c[q] = cq;
+            umask |= ok ? 0ull : (1ull << q);
+            cnt += cq;
+        }
+    } else {
+#pragma unroll
+        for (int q = 0; q < KM; ++q) {
+            const float ae = carry + (q ? off + loc[q - 1] : off);
+            const float ai = carry + (off + loc[q]);
+            const bool valid = q < nq;
+            uint32_t cq;
+            const bool cert = seq_certain(v[q], ae, ai, seg0 + i0 + q, cq);
+            c[q] = valid ? cq : 0u;
+            umask |= (valid & !cert) ? (1ull << q) : 0ull;
+            cnt += c[q];
+        }
+    }
+    const uint32_t nunc = __popcll(umask);
+    // (3) list positions and count offsets (block scans of integers: exact)
+    const uint32_t ci = warp_incl_scan(cnt, lane), ui = warp_incl_scan(nunc, lane);
+    uint32_t cb = 0, ub = 0;
+    if (NT > 32) {
+        if (member && lane == 31) { sc.wcnt[warp] = ci; sc.wunc[warp] = ui; }
+        __syncthreads();
+        if (member)
+            for (int w = 0; w < warp; ++w) { cb += sc.wcnt[w]; ub += sc.wunc[w]; }
+    }
+    if (rank == NT - 1) { sc.tail = cb + ci; sc.nlist = (int)(ub + ui); }
+    uint32_t k = ub + ui - nunc, cr = cb + ci - cnt;
+    int ovf = member && k + nunc > (uint32_t)kList;
+    if (member && !ovf && umask) {
+#pragma unroll
+        for (int q = 0; q < KM; ++q) {
+            if (umask & (1ull << q)) { sc.lt[k] = v[q]; sc.lc[k] = cr; ++k; }
+            cr += c[q];
+        }
+    }
+    if (NT > 32) ovf = __syncthreads_or(ovf); else ovf = __any_sync(NCM_FULL, ovf);
+    // (4) the walk, by warp 0 in lockstep
+    if (rank < 32) {
+        float x = carry;
+        if (ovf) {
+            for (int i = 0; i < segn; i += 32) x = seq_fold<32>(term, seg0 + i, min(32, segn - i), x);
+        } else {
+            const int nlist = sc.nlist;
+            uint32_t bits = __float_as_uint(x), prev = 0;
+            int j = 0;
+            for (; j + 8 <= nlist; j += 8) {
+                float tk[8];
+                uint32_t ck[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) { tk[q] = sc.lt[j + q]; ck[q] = sc.lc[j + q]; }
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    bits += ck[q] - prev;
+                    prev = ck[q];
+                    bits = __float_as_uint(__uint_as_float(bits) + tk[q]);
+                }
+            }
+            for (; j < nlist; ++j) {
+                const uint32_t cj = sc.lc[j];
+                bits += cj - prev;
+                prev = cj;
+                bits = __float_as_uint(__uint_as_float(bits) + sc.lt[j]);
+            }
+            bits += sc.tail - prev;
+            x = __uint_as_float(bits);
+        }
+        if (rank == 0) sc.result = x;
+    }
+    if (NT == 32) __syncwarp(); else __syncthreads();
+    return sc.result;
+}
+
 // NT threads (one warp, or the whole 256-thread CTA) cooperate; `rank` is the thread's
 // index among them; the terms are read through term(i).  All NT threads get the result;
 // with NT > 32 every thread of the CTA must call (threads beyond NT only take part in
 // the barriers).
-template <int NT, int GS, class Term>
-__device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT, GS>& sc, int rank) {
-    static_assert(GS == 16 || GS == 32, "group size");
-    constexpr int SEG = GS * NT;            // terms per segment: one group per thread
+template <int NT, class Term>
+__device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT>& sc, int rank) {
     if (n <= 0) return 0.0f;
-    const int lane = rank & 31, warp = rank >> 5;
-    const bool member = rank < NT;
     if (NT == 32 && n <= kSeqSerial) {
         float x = 0.0f;
         for (int i = 0; i < n; i += 32) x = seq_fold<32>(term, i, min(32, n - i), x);
         return x;
     }
-    for (int seg0 = 0; seg0 < n; seg0 += SEG) {
-        const int segn = min(n - seg0, SEG);
-        const int G = (segn + GS - 1) / GS;
-        const float carry = seg0 == 0 ? 0.0f : sc.result;
-        const int g = rank;
-        const bool mine = member && g < G;
-        // (1) this thread's group, read in rotated order (bank-conflict free)
-        float v[GS];
-        float acc4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        const int gb = GS * g, m = mine ? min(GS, segn - gb) : 0;
-        const int rot = GS == 32 ? lane : (lane >> 1);
-#pragma unroll
-        for (int q = 0; q < GS; ++q) {
-            const int idx = (q + rot) & (GS - 1);
-            v[q] = idx < m ? term(seg0 + gb + idx) : 0.0f;
-            acc4[q & 3] += v[q];
-        }
-        const float acc = (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
-        float incl = warp_incl_scan(acc, lane);
-        if (NT > 32) {
-            if (member && lane == 31) sc.wsum[warp] = incl;
-            __syncthreads();
-            if (member)
-                for (int w = 0; w < warp; ++w) incl += sc.wsum[w];
-        }
-        // (2) guessed binade and ulp count
-        const float start = carry + (incl - acc), end = carry + incl;
-        const int e = (int)(__float_as_uint(start) >> 23);
-        bool ok = e >= 24 && e <= 253 && (int)(__float_as_uint(end) >> 23) == e;
-        const float inv = seq_inv_ulp(ok ? e : 150);
-        uint32_t cnt = 0;
-#pragma unroll
-        for (int q = 0; q < GS; ++q) {
-            uint32_t c;
-            ok = seq_units(v[q] * inv, c) && ok;
-            cnt += c;
-        }
-        cnt = ok ? min(cnt, 1u << 23) : (1u << 23);
-        uint32_t cp = warp_incl_scan(cnt, lane);
-        if (NT > 32) {
-            if (member && lane == 31) sc.wcnt[warp] = cp;
-            __syncthreads();
-            if (member)
-                for (int w = 0; w < warp; ++w) cp += sc.wcnt[w];
-        }
-        if (mine) {
-            sc.key[g] = ok ? (uint32_t)e : ~0u;
-            sc.pre[g] = cp;
-        }
-        if (NT == 32) __syncwarp(); else __syncthreads();
-        // (3) the walk, by warp 0 in lockstep
-        if (rank < 32) {
-            uint32_t sb = __float_as_uint(carry);
-            int j = 0;
-            if (seg0 == 0) {
-                // the running value crosses binades every few terms at first: fold the
-                // first terms outright
-                const int m0 = min(segn, kSeqHead);
-                float x = 0.0f;
-                for (int i = 0; i < m0; i += 32) x = seq_fold<32>(term, i, min(32, m0 - i), x);
-                sb = __float_as_uint(x);
-                j = (m0 + GS - 1) / GS;
-            }
-            while (j < G) {
-                const int gi = j + lane;
-                const uint32_t base = j > 0 ? sc.pre[j - 1] : 0u;
-                const uint32_t p = gi < G ? sc.pre[gi] - base : 0u;
-                const bool good = gi >= G || seq_applies(sb, sc.key[gi], p);
-                const uint32_t bad = __ballot_sync(NCM_FULL, !good);
-                const int f = bad ? __ffs(bad) - 1 : 32;
-                const uint32_t add = __shfl_sync(NCM_FULL, p, (f - 1) & 31);
-                if (f == 32) {
-                    // all 32 (or all remaining) groups apply; lanes past G carry p = 0,
-                    // so read the count of the last real group
-                    sb += __shfl_sync(NCM_FULL, p, min(31, G - 1 - j));
-                    j += 32;
-                    continue;
-                }
-                if (f > 0) sb += add;
-                const int a0 = seg0 + GS * (j + f);
-                const float x = seq_fold<GS>(term, a0, min(GS, n - a0), __uint_as_float(sb));
-                sb = __float_as_uint(x);
-                j += f + 1;
-            }
-            if (rank == 0) sc.result = __uint_as_float(sb);
-        }
-        if (NT == 32) __syncwarp(); else __syncthreads();
-    }
-    return sc.result;
+    if (n <= 9 * NT) return seq_sum_segment<NT, 9>(term, 0, n, 0.0f, sc, rank);
+    if (n <= 13 * NT) return seq_sum_segment<NT, 13>(term, 0, n, 0.0f, sc, rank);
+    if (n <= 17 * NT) return seq_sum_segment<NT, 17>(term, 0, n, 0.0f, sc, rank);
+    float x = 0.0f;
+    for (int seg0 = 0; seg0 < n; seg0 += 33 * NT)
+        x = seq_sum_segment<NT, 33>(term, seg0, min(n - seg0, 33 * NT), x, sc, rank);
+    return x;
 }
 
 // ------------------------------------------------------------------ activation (Q8_0)
@@ -460,10 +515,17 @@ __device__ __forceinline__ void stage_f32(float* dst, const float* src, int n, i
     }
 }
 
+// GEMV block: warps 0-7 compute, 8-9 fold, 10 produces (see gemv_kernel).
+constexpr int kComputeThreads = 256;
+constexpr int kFoldBase = 256;      // first fold thread
+constexpr int kProducer = 320;      // producer thread
+constexpr int kGemvThreads = 352;
+typedef SeqSumScratchT<kGemvThreads> GemvSeqScratch;
+
 // ------------------------------------------------------------------ prologue
 // Quantises the activation (optionally RMS-normalised) into shared memory.
 template <int IN>
-__device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, SeqSumScratch& sc) {
+__device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, GemvSeqScratch& sc) {
     const int tid = threadIdx.x;
     const int nblk = p.nchunk * 16;     // padded block count (tail blocks zero)
     float2* xs = reinterpret_cast<float2*>(smem + p.xs_off);
@@ -507,7 +569,7 @@ __device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, SeqSumScratch&
                 tot = p.ssq_tok[p.tokens[p.state[ST_POS]]];
             } else {
                 // inference.rs:698-701: sum += val * val, sequential.
-                tot = seq_sum_nonneg<kThreads, 16>([&](int i) { float v = xf[i]; return v * v; }, p.cols, sc, tid);
+                tot = seq_sum_nonneg<kGemvThreads>([&](int i) { float v = xf[i]; return v * v; }, p.cols, sc, tid);
             }
             scale = 1.0f / sqrtf(tot / (float)p.cols + p.eps);
         }
@@ -576,18 +638,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 // Warp roles: warps 0-7 compute per-block terms, warps 8-9 fold them row by row (and run
 // the epilogue), warp 10 issues the TMA loads.  Hand-offs use mbarriers only:
 //   full[s]  (TMA -> compute)      empty[s]  (compute -> producer: stage s reusable)
-//   tfull[k] (compute -> fold)     tempty[k] (fold -> compute: term slot k reusable)
-constexpr int kComputeThreads = 256;
-constexpr int kFoldBase = 256;      // first fold thread
-constexpr int kProducer = 320;      // producer thread
-constexpr int kGemvThreads = 352;
+// and the term slots are handed over with shared-memory flags (release / acquire):
+//   tflag[k]    (compute -> fold: uses of slot k whose terms are written)
+//   eflag[w][k] (fold warp w -> compute: uses of slot k folded)
 
 template <int QT, int IN, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr bool DUAL = (EPI == EPI_SILU);
-    __shared__ SeqSumScratch sc;
-    __shared__ __align__(8) uint64_t tfull[8], tempty[8];
+    __shared__ GemvSeqScratch sc;
+    __shared__ uint32_t tflag[kMaxStages], eflag[2][kMaxStages];
     __shared__ int s_last;
     __shared__ float xchg[kMaxFold];
     __shared__ float wv[2];
@@ -610,9 +670,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     if (tid == 0) {
         for (int s = 0; s < ns; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kComputeThreads / 32);
-            mbar_init(&tfull[s], kComputeThreads / 32);
-            mbar_init(&tempty[s], 2);
+            mbar_init(&empty[s], 1);
+            tflag[s] = 0;
+            eflag[0][s] = 0;
+            eflag[1][s] = 0;
         }
         fence_mbar_init();
     }
@@ -652,38 +713,50 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     if (tid == kProducer) {
         while (icur < r_end) issue();
     } else if (tid < kComputeThreads) {
-        // (3a) compute warps: per-block terms of every (row, unit) of each stage.
-        const int u = tid & 7, r0 = tid >> 3;
-        int t = 0;
-        for (int cur = r_begin; cur < r_end;) {
-            const int n = tile_at(p, cur, r_end).n;
-            const int vrows = DUAL ? 2 * p.box_rows : n;
-            for (int c = 0; c < p.nchunk; ++c, ++t) {
-                const int s = t % ns;
-                if (!mbar_wait(&full[s], (uint32_t)((t / ns) & 1), limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
-                if (!mbar_wait(&tempty[s], (uint32_t)(((t / ns) & 1) ^ 1), limit_ns))
-                    set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
-                const uint8_t* sb = stages + (size_t)s * p.stage_bytes;
-                float* T = tbuf + s * (kMaxFold * kTStride);
-                XUnit x;
-                load_xunit(smem, p, c * kUnits + u, x);
-                for (int vr = r0; vr < vrows; vr += 32) {
-                    const int mat = DUAL ? (vr >= p.box_rows) : 0;
-                    const int r = vr - mat * p.box_rows;
-                    if (r >= n) continue;
-                    float t0, t1;
-                    unit_terms<QT>(sb + mat * box2_off + r * p.chunk_bytes, u, x, t0, t1);
-                    float* trow = T + vr * kTStride;
-                    trow[2 * u] = t0;
-                    trow[2 * u + 1] = t1;
+        // (3a) compute warps: warp w owns ring slot w and computes every ns-th stage in
+        // full, so up to ns stages are in compute at once.  A lane keeps one 64-column
+        // unit (lane & 7) and walks the rows (lane >> 3) + 4k.
+        const int w = tid >> 5, u = lane & 7;
+        if (w < ns) {
+            int t = 0;
+            for (int cur = r_begin; cur < r_end;) {
+                const int n = tile_at(p, cur, r_end).n;
+                const int vrows = DUAL ? 2 * p.box_rows : n;
+                for (int c = 0; c < p.nchunk; ++c, ++t) {
+                    if (t % ns != w) continue;
+                    const uint32_t ph = (uint32_t)((t / ns) & 1);
+                    if (!mbar_wait(&full[w], ph, limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+                    const uint32_t use = (uint32_t)(t / ns);
+                    if (!flag_wait_geq(&eflag[0][w], use, limit_ns) || !flag_wait_geq(&eflag[1][w], use, limit_ns))
+                        set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+                    const uint8_t* sb = stages + (size_t)w * p.stage_bytes;
+                    float* T = tbuf + w * (kMaxFold * kTStride);
+                    XUnit x;
+                    load_xunit(smem, p, c * kUnits + u, x);
+                    const int v0 = lane >> 3, nk = (vrows - v0 + 3) >> 2;
+                    for (int k0 = 0; k0 < nk; k0 += 4) {
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk) {
+                            const int vr = v0 + 4 * (k0 + kk);
+                            const int mat = DUAL ? (vr >= p.box_rows) : 0;
+                            const int r = vr - mat * p.box_rows;
+                            if (k0 + kk < nk && r < n) {
+                                float t0, t1;
+                                unit_terms<QT>(sb + mat * box2_off + r * p.chunk_bytes, u, x, t0, t1);
+                                float* trow = T + vr * kTStride;
+                                trow[2 * u] = t0;
+                                trow[2 * u + 1] = t1;
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&empty[w]);
+                        st_release_cta(&tflag[w], use + 1);
+                    }
                 }
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&empty[s]);
-                    mbar_arrive(&tfull[s]);
-                }
+                cur += n;
             }
-            cur += n;
         }
     } else if (tid < kProducer) {
         // (3b) fold warps: sequential per-row sums in block order, then the epilogue.
@@ -693,21 +766,23 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         float best_v = -INFINITY;
         int best_i = 0x7fffffff;
         const int nsb = p.nb / 8;
-        int t = 0;
+        int s = 0;
+        uint32_t use = 0;   // ring slot of the next stage and how often it was used before
         for (int cur = r_begin; cur < r_end;) {
             const TileCursor tc = tile_at(p, cur, r_end);
             const int n = tc.n;
             const bool live = DUAL ? (f < 2 * p.box_rows && (f % p.box_rows) < n) : (f < n);
             float acc = 0.0f;
-            for (int c = 0; c < p.nchunk; ++c, ++t) {
-                const int s = t % ns;
-                if (!mbar_wait(&tfull[s], (uint32_t)((t / ns) & 1), limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+            const float* trow0 = tbuf + f * kTStride;
+            for (int c = 0; c < p.nchunk; ++c) {
+                if (!flag_wait_geq(&tflag[s], use + 1, limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
                 if (live) {
                     // all 16 terms into registers first, then the in-order adds
-                    const float* trow = tbuf + s * (kMaxFold * kTStride) + f * kTStride;
+                    const float* trow = trow0 + s * (kMaxFold * kTStride);
                     float tv[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) tv[j] = trow[j];
+                    asm volatile("" ::: "memory");
                     if constexpr (QT == NCM_T_Q4_K) {
                         const int nsbc = min(2, nsb - 2 * c);
 #pragma unroll
@@ -721,13 +796,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                         }
                     } else {
                         const int nbc = min(16, p.nb - 16 * c);
+                        if (nbc == 16) {
 #pragma unroll
-                        for (int j = 0; j < 16; ++j)
-                            if (j < nbc) acc += tv[j];
+                            for (int j = 0; j < 16; ++j) acc += tv[j];
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                if (j < nbc) acc += tv[j];
+                        }
                     }
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[s]);
+                if (lane == 0) st_release_cta(&eflag[(tid >> 5) - (kFoldBase >> 5)][s], use + 1);
+                if (++s == ns) { s = 0; ++use; }
             }
 
             // tile epilogue (rows cur .. cur+n-1 of segment tc.seg)
@@ -903,6 +984,8 @@ int gemv_tensor_map(CUtensorMap* tm, const void* base, int64_t rows, int pitch, 
     return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
 }
 
+constexpr int kGemvSmemLimit = 220 * 1024;
+
 int gemv_plan(int qtype, int cols, int rows, bool dual, int in_mode, GemvParams& p) {
     p.cols = cols;
     p.nb = cols / 32;
@@ -915,7 +998,10 @@ int gemv_plan(int qtype, int cols, int rows, bool dual, int in_mode, GemvParams&
     if (maxg < 1) maxg = 1;
     if (grid > maxg) grid = maxg;
     const int per_cta = (rows + grid - 1) / grid;
-    int maxr = dual ? 32 : (qtype == NCM_T_Q8_0 ? 32 : 64);
+    // rows per tile: a stage (one tile x 512 columns) stays near 18 KB so that eight
+    // stages fit beside the activation
+    int maxr = qtype == NCM_T_Q8_0 ? 32 : 64;
+    if (dual) maxr /= 2;
     int br = (per_cta + 1) & ~1;
     if (br > maxr) br = maxr;
     if (br < 2) br = 2;
@@ -930,20 +1016,20 @@ int gemv_plan(int qtype, int cols, int rows, bool dual, int in_mode, GemvParams&
     p.xsum_off = off;
     off += units * 8;
     off = (off + 127) / 128 * 128;
-    // The f32 staging of the RMS input and the term buffers are live at different times.
-    int ns = (112 * 1024) / p.stage_bytes;
-    ns = ns > 8 ? 8 : (ns < 2 ? 2 : ns);
+    // The f32 staging of the input and the term buffers are live at different times.
     p.xf_off = off;
     p.t_off = off;
-    int shared_region = ns * kMaxFold * kTStride * 4;
+    int shared_region = kMaxStages * kMaxFold * kTStride * 4;
     if (in_mode != IN_Q8 && cols * 4 > shared_region) shared_region = cols * 4;
     off += (shared_region + 127) / 128 * 128;
     p.nw_off = off;
     if (in_mode == IN_F32_RMS) off += (cols * 4 + 127) / 128 * 128;
     p.stage_off = off;
-    while (ns > 2 && off + ns * p.stage_bytes > 200 * 1024) --ns;
+    int ns = kMaxStages;
+    while (ns > 2 && off + ns * p.stage_bytes > kGemvSmemLimit) --ns;
     p.nstages = ns;
     p.smem_bytes = off + ns * p.stage_bytes;
+    if (p.smem_bytes > kGemvSmemLimit) return -1;
     return grid;
 }
 
@@ -952,7 +1038,7 @@ static int launch_t(const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
     static bool configured = false;
     auto kern = gemv_kernel<QT, IN, EPI>;
     if (!configured) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmemLimit);
         configured = true;
     }
     cudaLaunchConfig_t cfg = {};
@@ -1109,7 +1195,7 @@ __global__ void __launch_bounds__(256) attn_softmax_v_kernel(const __grid_consta
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(NCM_FULL, mx, o));
         for (int p = lane; p < n; p += 32) wr[p] = expf_cr(wr[p] - mx);
         __syncwarp();
-        const float sum = seq_sum_nonneg<32, 32>([&](int i) { return wr[i]; }, n, scr[warp], lane);
+        const float sum = seq_sum_nonneg<32>([&](int i) { return wr[i]; }, n, scr[warp], lane);
         const float inv = 1.0f / sum;
         for (int p = lane; p < n; p += 32) wr[p] = wr[p] * inv;
     }
@@ -1367,9 +1453,9 @@ __global__ void rms_norm_kernel(float* out, const float* x, const float* w, int 
     if (staged) {
         for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = x[i];
         __syncthreads();
-        tot = seq_sum_nonneg<kThreads, 16>([&](int i) { float v = xs[i]; return v * v; }, n, sc, threadIdx.x);
+        tot = seq_sum_nonneg<kThreads>([&](int i) { float v = xs[i]; return v * v; }, n, sc, threadIdx.x);
     } else {
-        tot = seq_sum_nonneg<kThreads, 16>([&](int i) { float v = x[i]; return v * v; }, n, sc, threadIdx.x);
+        tot = seq_sum_nonneg<kThreads>([&](int i) { float v = x[i]; return v * v; }, n, sc, threadIdx.x);
     }
     const float scale = 1.0f / sqrtf(tot / (float)n + eps);
     for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = x[i] * scale * w[i];

@@ -14,6 +14,7 @@ constexpr int kChunkCols = 512; // columns per TMA chunk: 16 Q4_0/Q8_0 blocks or
 constexpr int kUnits = 8;       // 64-column units per chunk
 constexpr int kTStride = 17;    // per-row stride (floats) of the per-block term buffer (conflict-free)
 constexpr int kMaxFold = 64;    // fold lanes (rows) per tile
+constexpr int kMaxStages = 8;   // GEMV ring stages (one per compute warp)
 
 // Input modes of the GEMV prologue.
 enum InMode { IN_F32 = 0, IN_F32_RMS = 1, IN_Q8 = 2 };
