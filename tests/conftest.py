@@ -12,6 +12,7 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA B200 (sm_100a) device")
     config.addinivalue_line("markers", "multigpu: needs two or more CUDA devices")
     config.addinivalue_line("markers", "slow: full-size configuration, minutes of CPU oracle time")
+    config.addinivalue_line("markers", "cpu: runs without a GPU (oracle, host logic, C-ABI surface)")
 
 
 @pytest.fixture(scope="session")

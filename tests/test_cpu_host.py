@@ -1,0 +1,202 @@
+"""Host-side checks that need no GPU: the C-ABI surface, the tensor-parallel plan, the
+synthetic GGUF writer against the oracle's loader, and the oracle's own tensor-parallel
+and speculative paths (tp.rs, speculative.rs semantics)."""
+import os
+import re
+import struct
+
+import numpy as np
+import pytest
+
+from conftest import ROOT, TINY
+
+pytestmark = pytest.mark.cpu
+
+
+def test_library_exports_every_declared_symbol(ncm):
+    """Every function include/ncm.h declares is exported by libncm.so."""
+    text = open(os.path.join(ROOT, "include", "ncm.h")).read()
+    names = sorted(set(re.findall(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_ \*]*?\b(ncm_[a-z0-9_]+)\s*\(", text, re.M)))
+    assert len(names) >= 30
+    L = ncm.lib()
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+
+
+SHAPES = [(32, 8, 14336, 128256), (24, 8, 8192, 128256), (32, 8, 8192, 128256), (64, 8, 28672, 128256)]
+SHARES = [[8], [4, 4], [2, 3, 3], [1] * 8, [2, 2, 2, 2]]
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("shares", SHARES)
+def test_shard_geometry_matches_oracle_and_covers(ncm, orc, shape, shares):
+    """tp.rs:641-701: q_start = kv_start*(Hq/Hkv), ffn_start = kv_start*F/Hkv, head rows
+    (V*s/Hkv) & !3 with the remainder on the last shard; shards tile every range."""
+    heads, kvh, ffn, vocab = shape
+    sh = np.asarray(shares, dtype=np.int32)
+    ends = {"q": 0, "kv": 0, "ffn": 0, "head": 0}
+    for i in range(len(shares)):
+        g = ncm.shard_geometry(heads, kvh, ffn, vocab, shares, i)
+        ref = np.zeros(8, dtype=np.int32)
+        assert orc.lib().orc_shard_geometry(heads, kvh, ffn, vocab, orc.ptr(sh), len(sh), i, orc.ptr(ref)) == 0
+        assert list(g.values()) == [int(v) for v in ref]
+        assert g["q_start"] == ends["q"] and g["kv_start"] == ends["kv"] and g["ffn_start"] == ends["ffn"]
+        assert g["head_row_start"] == ends["head"] and g["head_row_start"] % 4 == 0
+        ends["q"] += g["q_heads"]; ends["kv"] += g["kv_heads"]
+        ends["ffn"] += g["ffn_len"]; ends["head"] += g["head_rows"]
+    assert (ends["q"], ends["kv"], ends["ffn"], ends["head"]) == (heads, kvh, ffn, vocab)
+
+
+@pytest.mark.parametrize("shares", [[3, 3], [0, 8], [1, 1, 1]])
+def test_shard_geometry_rejects_bad_shares(ncm, shares):
+    """tp.rs:641-660 validate_shares: sum must equal the KV heads, no empty shard."""
+    with pytest.raises(ncm.NcmError):
+        ncm.shard_geometry(32, 8, 14336, 128256, shares, 0)
+
+
+def test_even_shares():
+    from nanocamelid_b200 import tp
+    assert tp.even_shares(8, 4) == [2, 2, 2, 2]
+    with pytest.raises(ValueError):
+        tp.even_shares(8, 3)
+
+
+# ---------------------------------------------------------------- GGUF
+GGUF_SCALAR = {0: 1, 1: 1, 2: 2, 3: 2, 4: 4, 5: 4, 6: 4, 7: 1, 10: 8, 11: 8, 12: 8}
+
+
+def _gguf_value(f, t):
+    if t in GGUF_SCALAR:
+        f.read(GGUF_SCALAR[t])
+    elif t == 8:
+        (n,) = struct.unpack("<Q", f.read(8))
+        f.read(n)
+    elif t == 9:
+        et, n = struct.unpack("<IQ", f.read(12))
+        for _ in range(n):
+            _gguf_value(f, et)
+    else:
+        raise ValueError(f"GGUF value type {t}")
+
+
+def read_gguf_tensors(path):
+    """Minimal GGUF v3 reader (gguf.rs:454-551): {name: (type, dims, data offset)}."""
+    with open(path, "rb") as f:
+        assert f.read(4) == b"GGUF"
+        ver, nt, nkv = struct.unpack("<IQQ", f.read(20))
+        align = 32
+        for _ in range(nkv):
+            (kl,) = struct.unpack("<Q", f.read(8))
+            key = f.read(kl).decode()
+            (t,) = struct.unpack("<I", f.read(4))
+            if key == "general.alignment" and t == 4:
+                (align,) = struct.unpack("<I", f.read(4))
+            else:
+                _gguf_value(f, t)
+        infos = {}
+        for _ in range(nt):
+            (nl,) = struct.unpack("<Q", f.read(8))
+            name = f.read(nl).decode()
+            (nd,) = struct.unpack("<I", f.read(4))
+            dims = struct.unpack("<" + "Q" * nd, f.read(8 * nd))
+            t, off = struct.unpack("<IQ", f.read(12))
+            infos[name] = (t, dims, off)
+        base = (f.tell() + align - 1) // align * align
+    return {k: (t, d, base + o) for k, (t, d, o) in infos.items()}
+
+
+def tiny(ncm, **kw):
+    d = dict(TINY)
+    d.update(kw)
+    return ncm.spec(d["emb"], d["layers"], d["heads"], d["kv_heads"], d["head_dim"], d["ffn"], vocab=d["vocab"],
+                    ctx=d["ctx"], tied=d.get("tied", True), t_embd=d.get("t_embd", ncm.Q4_0),
+                    t_attn=d.get("t_attn", ncm.Q4_0), t_ffn=d.get("t_ffn", ncm.Q4_0), t_out=d.get("t_out", ncm.Q4_0),
+                    seed=d.get("seed", 7))
+
+
+def test_gguf_writer_blocks_equal_host_generator(ncm, tmp_path):
+    """The synthetic GGUF's tensor bytes equal ncm_synth_tensor_host (the same generator
+    the on-device initialiser runs), including column slices."""
+    sp = tiny(ncm, tied=False, t_embd=ncm.Q8_0, t_attn=ncm.Q8_0, t_ffn=ncm.Q4_K, t_out=ncm.Q4_0, emb=512, ffn=1024)
+    path = tmp_path / "m.gguf"
+    ncm.write_synthetic_gguf(path, sp)
+    tens = read_gguf_tensors(path)
+    raw = open(path, "rb").read()
+    bb = {ncm.Q4_0: (18, 32), ncm.Q8_0: (34, 32), ncm.Q4_K: (144, 256)}
+    for name in ["blk.0.attn_q.weight", "blk.1.ffn_down.weight", "blk.0.ffn_gate.weight", "output.weight"]:
+        t, dims, off = tens[name]
+        cols, rows = dims[0], dims[1]
+        b, e = bb[t]
+        row_bytes = cols // e * b
+        want = ncm.synth_tensor_bytes(sp, name, t, 0, rows, 0, cols, cols)
+        assert raw[off:off + rows * row_bytes] == want, name
+        c0, c1 = e, 3 * e
+        part = ncm.synth_tensor_bytes(sp, name, t, 1, 3, c0, c1, cols)
+        exp = b"".join(raw[off + r * row_bytes + c0 // e * b: off + r * row_bytes + c1 // e * b] for r in (1, 2))
+        assert part == exp, name
+
+
+def test_gguf_writer_is_deterministic_and_loads(ncm, orc, tmp_path):
+    sp = tiny(ncm)
+    a, b = tmp_path / "a.gguf", tmp_path / "b.gguf"
+    ncm.write_synthetic_gguf(a, sp, threads=1)
+    ncm.write_synthetic_gguf(b, sp, threads=4)
+    assert open(a, "rb").read() == open(b, "rb").read()
+    m = orc.OracleModel(a)
+    assert (m.emb, m.layers, m.heads, m.kv_heads, m.head_dim, m.ffn, m.vocab) == (
+        TINY["emb"], TINY["layers"], TINY["heads"], TINY["kv_heads"], TINY["head_dim"], TINY["ffn"], TINY["vocab"])
+
+
+# ---------------------------------------------------------------- oracle TP / speculative
+def _prompt(n, vocab, seed):
+    return [int(v) for v in np.random.default_rng(seed).integers(0, vocab, size=n)]
+
+
+@pytest.mark.parametrize("kvh,heads,shares", [(2, 4, [1, 1]), (8, 8, [2, 3, 3]), (8, 8, [1] * 8)])
+def test_oracle_tp_matches_single_node(ncm, orc, tmp_path, kvh, heads, shares):
+    """bin/cluster_tp_split_smoke.rs:101-165 semantics: TP greedy tokens identical to the
+    single-node path, logits within 1e-3 relative."""
+    hd = TINY["emb"] // heads
+    sp = tiny(ncm, kv_heads=kvh, heads=heads, head_dim=hd, ffn=2048 if kvh == 8 else 512)
+    path = tmp_path / "m.gguf"
+    ncm.write_synthetic_gguf(path, sp)
+    full = orc.OracleModel(path)
+    tp = orc.OracleTP(orc.OracleModel(path), shares)
+    prompt = _prompt(5, sp.vocab, 3)
+    ref = full.generate(prompt, 12)[0]
+    assert tp.generate(prompt, 12) == ref
+    full.reset()
+    tp = orc.OracleTP(orc.OracleModel(path), shares)
+    for pos, t in enumerate(prompt):
+        _, la = full.forward_pass(t, pos, want_logits=True)
+        _, lb = tp.forward_pass(t, pos, want_logits=True)
+        assert float(np.max(np.abs(la - lb))) <= 1e-3 * float(np.max(np.abs(la)))
+
+
+def test_oracle_speculative_equals_greedy(ncm, orc, tmp_path):
+    """speculative.rs:299-494: greedy speculative decoding emits the target's greedy tokens."""
+    tgt_spec = tiny(ncm, seed=11)
+    draft_spec = tiny(ncm, seed=12, layers=1)
+    pt, pd = tmp_path / "t.gguf", tmp_path / "d.gguf"
+    ncm.write_synthetic_gguf(pt, tgt_spec)
+    ncm.write_synthetic_gguf(pd, draft_spec)
+    prompt = _prompt(6, tgt_spec.vocab, 4)
+    greedy = orc.OracleModel(pt).generate(prompt, 16)[0]
+    for k in (1, 4):
+        toks, stats = orc.spec_generate(orc.OracleModel(pt), orc.OracleModel(pd), prompt, 16, k)
+        assert toks == greedy, k
+
+
+def test_oracle_regression_fixture(ncm, orc, tmp_path):
+    """tests/golden/tiny_oracle.json (made by tests/golden/make_golden.py): greedy tokens and
+    a logit checksum of the oracle on a tiny synthetic model -- pins the writer + oracle
+    against silent drift."""
+    import json
+    g = json.load(open(os.path.join(ROOT, "tests", "golden", "tiny_oracle.json")))
+    sp = tiny(ncm, **g["spec_overrides"])
+    path = tmp_path / "m.gguf"
+    ncm.write_synthetic_gguf(path, sp)
+    m = orc.OracleModel(path)
+    toks, lg = m.generate(g["prompt"], g["n_gen"], want_last_logits=True)
+    assert toks == g["tokens"]
+    assert lg.view(np.uint32)[: len(g["logit_bits_head"])].tolist() == g["logit_bits_head"]
