@@ -37,6 +37,8 @@ def parse():
     ap.add_argument("--prompt", type=int, default=64)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--gemv-only", action="store_true",
+                    help="only the roofline GEMV (head-shaped Q4_0 matrix): the small case for ncu captures")
     return ap.parse_args()
 
 
@@ -282,7 +284,11 @@ def main():
     import nanocamelid_b200 as ncm
     sp = ncm.CONFIGS[args.config]
     rank = int(os.environ.get("RANK", "0"))
-    if args.impl == "reference":
+    if args.gemv_only:
+        import torch
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        print(json.dumps({"roofline": gemv_roofline(torch, ncm, sp, peaks["hbm_gbs"])}))
+    elif args.impl == "reference":
         run_reference(args, sp, rank)
     else:
         run_b200(args, sp)
