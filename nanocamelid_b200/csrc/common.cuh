@@ -96,10 +96,26 @@ __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepc
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void st_relaxed_sys(unsigned* p, unsigned v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+// Spins (no sleep: the waiting CTA has nothing else to do) until *p >= v; false once
+// limit_ns has passed, the clock being read every 256 polls.
+__device__ __forceinline__ bool wait_flag_sys(const unsigned* p, unsigned v, uint64_t limit_ns);
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     unsigned v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
+}
+
+__device__ __forceinline__ bool wait_flag_sys(const unsigned* p, unsigned v, uint64_t limit_ns) {
+    if (ld_acquire_sys(p) >= v) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (ld_acquire_sys(p) >= v) return true;
+        if ((i & 255u) == 0 && global_timer_ns() - t0 > limit_ns) return false;
+    }
 }
 
 __device__ __forceinline__ void set_dev_error(int* err, int bits) {

@@ -910,16 +910,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                 // strict '>' so the lowest row range wins ties.
                 const int W = p.tp.world, me = p.tp.rank;
                 for (int d = 0; d < W; ++d) p.tp.hx[d][me] = make_float2(bv, __int_as_float(tok));
-                __threadfence_system();
-                for (int d = 0; d < W; ++d) st_release_sys(&p.tp.hflags[d][me], epoch);
-                uint64_t t0 = global_timer_ns();
+                fence_acq_rel_sys();
+                for (int d = 0; d < W; ++d) st_relaxed_sys(&p.tp.hflags[d][me], epoch);
                 bool ok = true;
-                for (int src = 0; src < W && ok; ++src) {
-                    while (ld_acquire_sys(&p.tp.hflags[me][src]) < epoch) {
-                        if (global_timer_ns() - t0 > p.tp.timeout_ns) { ok = false; break; }
-                        __nanosleep(64);
-                    }
-                }
+                for (int src = 0; src < W && ok; ++src) ok = wait_flag_sys(&p.tp.hflags[me][src], epoch, p.tp.timeout_ns);
                 if (!ok) set_dev_error(p.err, NCM_DEVERR_PEER_TIMEOUT);
                 float mv = 0.0f;
                 int mt = 0;
@@ -947,19 +941,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         const unsigned epoch = (unsigned)p.state[ST_STEP] + 1u;
         const size_t fslot = ((size_t)p.tp_slot * p.tp.grid_max + blockIdx.x) * W;
         if (tid == 0) {
-            __threadfence_system();
-            for (int d = 0; d < W; ++d) st_release_sys(&p.tp.flags[d][fslot + me], epoch);
+            // the CTA's peer stores are ordered before this fence by the barrier above
+            fence_acq_rel_sys();
+            for (int d = 0; d < W; ++d) st_relaxed_sys(&p.tp.flags[d][fslot + me], epoch);
         }
-        if (tid < W) {
-            uint64_t t0 = global_timer_ns();
-            while (ld_acquire_sys(&p.tp.flags[me][fslot + tid]) < epoch) {
-                if (global_timer_ns() - t0 > p.tp.timeout_ns) {
-                    set_dev_error(p.err, NCM_DEVERR_PEER_TIMEOUT);
-                    break;
-                }
-                __nanosleep(32);
-            }
-        }
+        if (tid < W && !wait_flag_sys(&p.tp.flags[me][fslot + tid], epoch, p.tp.timeout_ns))
+            set_dev_error(p.err, NCM_DEVERR_PEER_TIMEOUT);
         __syncthreads();
         const float* base = p.tp.recv[me] + (size_t)p.tp_slot * W * p.tp.H;
         for (int r = r_begin + tid; r < r_end; r += blockDim.x) {
