@@ -37,6 +37,9 @@ def parse():
     ap.add_argument("--prompt", type=int, default=64)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--spec", action="store_true",
+                    help="BASELINE config 5: greedy speculative decoding, draft = config 1, target = config-3 "
+                         "shape all Q4_0, k = 4, 128-token prompt, 256 tokens (one GPU)")
     ap.add_argument("--gemv-only", action="store_true",
                     help="only the roofline GEMV (head-shaped Q4_0 matrix): the small case for ncu captures")
     return ap.parse_args()
@@ -279,12 +282,49 @@ def run_b200(args, sp):
         dist.destroy_process_group()
 
 
+def run_spec(args, ncm):
+    """Config 5 on one GPU: tokens emitted per second by ncm_spec_generate (host-driven
+    draft/verify loop, synchronous), next to the target's plain greedy decode."""
+    import numpy as np
+    import torch
+    target_sp, draft_sp = ncm.CONFIGS["cfg5_target_q4_0"], ncm.CONFIGS["cfg1_1b_q4_0"]
+    n_prompt, n_gen, k = 128, 256, 4
+    ctx = n_prompt + n_gen + 2 * k + 2
+    prompt = [int(v) for v in np.random.default_rng(0).integers(0, target_sp.vocab, n_prompt)]
+    target = ncm.Model.synthetic(target_sp, ctx_limit=ctx, device=0)
+    draft = ncm.Model.synthetic(draft_sp, ctx_limit=ctx, device=0)
+    target.spec_generate(draft, prompt, 8, k=k)                     # warm-up (graphs, buffers)
+    target.reset(); draft.reset()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    toks, (drafted, accepted) = target.spec_generate(draft, prompt, n_gen, k=k)
+    torch.cuda.synchronize()
+    dt_spec = time.perf_counter() - t0
+    ref = ncm.Model.synthetic(target_sp, ctx_limit=ctx, device=0)
+    ref.generate(prompt, 8)
+    ref.reset()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    greedy = ref.generate(prompt, n_gen)
+    torch.cuda.synchronize()
+    dt_greedy = time.perf_counter() - t0
+    print(json.dumps({"metric": "bs1 speculative decode tok/s", "value": round(n_gen / dt_spec, 2), "unit": "tok/s",
+                      "n_gpus": 1, "higher_is_better": True, "data": "synthetic",
+                      "config": {"workload": "cfg5: draft cfg1_1b_q4_0, target cfg5_target_q4_0 (8B shape, Q4_0)",
+                                 "k": k, "prompt": n_prompt, "tokens": n_gen},
+                      "acceptance": round(accepted / max(1, drafted), 4), "drafted": drafted, "accepted": accepted,
+                      "target_greedy_tok_s": round(n_gen / dt_greedy, 2), "tokens_equal_greedy": toks == greedy,
+                      "timing": "wall clock around the call (prefill included), synchronous"}))
+
+
 def main():
     args = parse()
     import nanocamelid_b200 as ncm
     sp = ncm.CONFIGS[args.config]
     rank = int(os.environ.get("RANK", "0"))
-    if args.gemv_only:
+    if args.spec:
+        run_spec(args, ncm)
+    elif args.gemv_only:
         import torch
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
         print(json.dumps({"roofline": gemv_roofline(torch, ncm, sp, peaks["hbm_gbs"])}))

@@ -55,8 +55,10 @@ ncm_status ncm_matmul_quantized(int qtype, const void* w, int64_t rows, int cols
                                 const float* x_scales, float* out, void* stream);
 
 /* inference.rs:1246-1303 matmul_quantized_batch(out, x_i8, x_scales, w, shape{batch,rows,cols}, _):
- * ntok activation rows (x_i8[ntok][cols], x_scales[ntok][cols/32]) -> out[ntok][rows].
- * 1 <= ntok <= 8. */
+ * ntok activation rows (x_i8[ntok][cols], x_scales[ntok][cols/32]) -> out[ntok][rows],
+ * 1 <= ntok <= 8, every row bit-identical to ncm_matmul_quantized of that row.  The
+ * block dots run on int8 tensor-core MMA; w and x_i8 16-byte aligned, raw row pitch a
+ * multiple of 16 bytes. */
 ncm_status ncm_matmul_quantized_batch(int qtype, const void* w, int64_t rows, int cols, int ntok,
                                       const int8_t* x_i8, const float* x_scales, float* out, void* stream);
 
@@ -171,6 +173,22 @@ ncm_status ncm_get_hidden(ncm_model* m, float* hidden);
  * which: 0 hidden, 1 q (roped, last layer), 2 attention output, 3 silu(gate)*up,
  * 4 / 5 K / V cache of `layer` ([ctx][local kv width]), 6 logits (local head rows). */
 ncm_status ncm_debug_read(ncm_model* m, int which, int layer, float* out, int64_t n);
+
+/* ---------------------------------------------------------------- speculative decoding
+ * speculative.rs:381-389 prefill_pass_batch + compute_logits_from_hidden +
+ * sample_logits(_, 0.0) per row: tokens[ntok] (1 <= ntok <= 8) at positions
+ * pos0 .. pos0+ntok-1 through the target in one multi-row pass (each weight tile read
+ * once for all rows; int8 tensor-core block dots), K/V stored at those positions;
+ * argmax_out[t] = greedy token after row t.  Each row equals the one-token step at its
+ * position bit for bit.  The model's decode position is not changed.  One GPU. */
+ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok, int pos0, int* argmax_out);
+
+/* speculative.rs:299-494 speculative_decoding_step at temperature 0, from a prompt:
+ * the draft proposes k (<= 8) tokens, the target verifies them with ncm_verify_batch,
+ * the agreeing prefix plus the target's next token are emitted.  out_tokens[n_gen]
+ * equals the target's greedy decode; stats[2] = {drafted, accepted} (may be NULL). */
+ncm_status ncm_spec_generate(ncm_model* target, ncm_model* draft, const int* prompt, int n_prompt, int n_gen, int k,
+                             int* out_tokens, int* stats);
 
 /* ---------------------------------------------------------------- multi-GPU (one process per GPU)
  * Replaces the TCP star reducer (bin/cluster_tp_node.rs:505-550, 1042-1056, 1154-1180)

@@ -117,6 +117,8 @@ def lib():
         "ncm_tp_nccl_init": (c_int, [c_p, pu8, c_int, c_int]),
         "ncm_tp_set_reducer": (c_int, [c_p, c_int]),
         "ncm_tp_set_timeout_ns": (c_int, [c_p, c_u64]),
+        "ncm_verify_batch": (c_int, [c_p, pint, c_int, c_int, pint]),
+        "ncm_spec_generate": (c_int, [c_p, c_p, pint, c_int, c_int, c_int, pint, pint]),
         "ncm_test_peer_timeout": (c_int, [c_int, c_u64]),
     }
     for name, (res, args) in sigs.items():
@@ -296,6 +298,20 @@ class Model:
         out = np.empty(n, dtype=np.float32)
         _ck(lib().ncm_debug_read(self._h, which, layer, out.ctypes.data_as(ctypes.c_void_p), n))
         return out
+
+    def verify_batch(self, tokens, pos0):
+        """speculative.rs:381 prefill_pass_batch + per-row greedy argmax (one pass)."""
+        out = (ctypes.c_int * len(tokens))()
+        _ck(lib().ncm_verify_batch(self._h, _ints(tokens), len(tokens), pos0, out))
+        return list(out)
+
+    def spec_generate(self, draft, prompt, n_gen, k=4):
+        """speculative.rs:299-494 greedy speculative decoding with `draft`; returns
+        (tokens, (drafted, accepted))."""
+        out = (ctypes.c_int * max(1, n_gen))()
+        stats = (ctypes.c_int * 2)()
+        _ck(lib().ncm_spec_generate(self._h, draft._h, _ints(prompt), len(prompt), n_gen, k, out, stats))
+        return list(out)[:n_gen], (stats[0], stats[1])
 
     # tensor parallel
     def tp_export(self):

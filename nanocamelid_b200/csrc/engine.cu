@@ -5,6 +5,7 @@
 #include <dlfcn.h>
 #include <math.h>
 #include <string.h>
+#include <algorithm>
 #include <initializer_list>
 #include <mutex>
 #include <thread>
@@ -101,6 +102,13 @@ struct ncm_model {
     std::vector<void*> allocs;
     cudaGraphExec_t g_full = nullptr, g_nohead = nullptr;
     bool dirty = true;
+    // multi-row verify buffers (allocated on first use): [kMaxBatch][...]
+    float *b_hidden = nullptr, *b_q = nullptr, *b_att = nullptr, *b_act = nullptr;
+    int8_t* b_xq = nullptr;
+    float* b_xs = nullptr;
+    float2* b_amax = nullptr;
+    unsigned* b_cnt = nullptr;
+    int *b_tok = nullptr, *b_arg = nullptr;
     // tensor parallel
     int world = 1, rank = 0, reduce_mode = NCM_REDUCE_FUSED_P2P;
     bool tp_ready = false;
@@ -777,6 +785,208 @@ extern "C" ncm_status ncm_get_hidden(ncm_model* m, float* hidden) {
     return NCM_OK;
 }
 
+// ------------------------------------------------------------------ multi-row verify
+static ncm_status ensure_batch_buffers(ncm_model* m) {
+    if (m->b_hidden) return NCM_OK;
+    const size_t qw = (size_t)m->qh * m->hd;
+    const size_t wmax = std::max((size_t)m->emb, std::max(qw, (size_t)m->fl));
+    DALLOC(m->b_hidden, 4 * (size_t)kMaxBatch * m->emb);
+    DALLOC(m->b_q, 4 * (size_t)kMaxBatch * qw);
+    DALLOC(m->b_att, 4 * (size_t)kMaxBatch * qw);
+    DALLOC(m->b_act, 4 * (size_t)kMaxBatch * m->fl);
+    DALLOC(m->b_xq, (size_t)kMaxBatch * wmax);
+    DALLOC(m->b_xs, 4 * (size_t)kMaxBatch * (wmax / 32));
+    DALLOC(m->b_amax, sizeof(float2) * kMaxBatch * num_sms());
+    DALLOC(m->b_cnt, 4);
+    DALLOC(m->b_tok, 4 * kMaxBatch);
+    DALLOC(m->b_arg, 4 * kMaxBatch);
+    CK(cudaMemset(m->b_cnt, 0, 4));
+    return NCM_OK;
+}
+
+static BatchParams batch_base(ncm_model* m, int ntok) {
+    BatchParams p;
+    memset(&p, 0, sizeof p);
+    p.ntok = ntok;
+    p.rope = m->rope;
+    p.rope_half = m->rope_dim / 2;
+    p.head_dim = m->hd;
+    p.err = m->err;
+    p.xq = m->b_xq;
+    p.xs = m->b_xs;
+    return p;
+}
+
+static int launch_batch(std::initializer_list<const DevMat*> mats, const DevMat* up, int epi, BatchParams& p,
+                        cudaStream_t s) {
+    const DevMat& w0 = **mats.begin();
+    const int grid = batch_plan(w0.type, w0.cols, p.total_rows, up != nullptr, p.ntok, p);
+    if (grid < 0) return (int)cudaErrorInvalidValue;
+    int i = 0;
+    for (const DevMat* d : mats) {
+        int r = gemv_tensor_map(&p.tm[i++], d->d, d->rows, d->pitch, p.chunk_words, p.box_rows);
+        if (r) return r;
+    }
+    if (up) {
+        int r = gemv_tensor_map(&p.tm2, up->d, up->rows, up->pitch, p.chunk_words, p.box_rows);
+        if (r) return r;
+    }
+    return batch_gemv_launch(w0.type, epi, p, grid, s, true);
+}
+
+// speculative.rs:381-389 prefill_pass_batch (inference.rs:3695-4111) followed by
+// compute_logits_from_hidden + sample_logits(_, 0.0) for every row: ntok tokens at
+// positions pos0 .. pos0+ntok-1 through the whole model at once (each weight tile read
+// once for all rows), K/V stored at their positions, greedy argmax of every row out.
+// Every row's result is bit-identical to the one-token step at that position.
+extern "C" ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok, int pos0, int* argmax_out) {
+    if (!m || !tokens || !argmax_out || ntok < 1 || ntok > kMaxBatch || pos0 < 0 || pos0 + ntok > m->ctx)
+        return fail(NCM_EINVAL, "bad verify batch");
+    if (m->world > 1) return fail(NCM_EUNSUPPORTED, "multi-row verify runs on one GPU");
+    for (int i = 0; i < ntok; ++i)
+        if (tokens[i] < 0 || tokens[i] >= m->vocab) return fail(NCM_EINVAL, "token id out of range");
+    CK(cudaSetDevice(m->device));
+    ncm_status st = ensure_batch_buffers(m);
+    if (st) return st;
+    cudaStream_t s = m->stream;
+    const int qw = m->qh * m->hd, kw = m->kh * m->hd;
+    memcpy(m->h_stage + 4, tokens, 4 * (size_t)ntok);
+    CK(cudaMemcpyAsync(m->b_tok, m->h_stage + 4, 4 * (size_t)ntok, cudaMemcpyHostToDevice, s));
+    CKL(embed_rows_launch(m->embd.type, m->embd.d, m->embd.pitch, m->emb, m->b_tok, ntok, m->b_hidden, s, true));
+    for (int l = 0; l < m->layers; ++l) {
+        const Layer& L = m->L[l];
+        CKL(batch_prep_launch(m->b_hidden, m->emb, m->emb, ntok, L.attn_norm, m->eps, l == 0 ? m->embd_ssq : nullptr,
+                              m->b_tok, m->b_xq, m->b_xs, s, true));
+        BatchParams p = batch_base(m, ntok);
+        p.nseg = 3;
+        p.seg[0] = {m->b_q, qw, 0, SEG_Q};
+        p.seg[1] = {nullptr, kw, qw, SEG_K};
+        p.seg[2] = {nullptr, kw, qw + kw, SEG_V};
+        p.total_rows = qw + 2 * kw;
+        p.out_stride = qw;
+        p.pos0 = pos0;
+        p.kcache = m->kc + (size_t)l * m->ctx * kw;
+        p.vcache = m->vc + (size_t)l * m->ctx * kw;
+        p.kv_width = kw;
+        CKL(launch_batch({&L.wq, &L.wk, &L.wv}, nullptr, EPI_QKV, p, s));
+        for (int t = 0; t < ntok; ++t) {
+            AttnParams a;
+            memset(&a, 0, sizeof a);
+            a.q = m->b_q + (size_t)t * qw;
+            a.kc = p.kcache;
+            a.vc = p.vcache;
+            a.out = m->b_att + (size_t)t * qw;
+            a.scores = m->scores;
+            a.state = m->state;
+            a.pos_override = pos0 + t;
+            a.heads = m->qh;
+            a.kv_heads = m->kh;
+            a.hd = m->hd;
+            a.kvw = kw;
+            a.ctx = m->ctx;
+            a.dsplit = m->dsplit;
+            a.scale = 1.0f / sqrtf((float)m->hd);
+            CKL(attention_launch(a, s, true));
+        }
+        CKL(batch_prep_launch(m->b_att, qw, qw, ntok, nullptr, m->eps, nullptr, nullptr, m->b_xq, m->b_xs, s, true));
+        BatchParams o = batch_base(m, ntok);
+        o.nseg = 1;
+        o.seg[0] = {nullptr, m->emb, 0, SEG_OUT};
+        o.total_rows = m->emb;
+        o.hidden = m->b_hidden;
+        o.hidden_stride = m->emb;
+        CKL(launch_batch({&L.wo}, nullptr, EPI_RESID, o, s));
+        CKL(batch_prep_launch(m->b_hidden, m->emb, m->emb, ntok, L.ffn_norm, m->eps, nullptr, nullptr, m->b_xq,
+                              m->b_xs, s, true));
+        BatchParams f = batch_base(m, ntok);
+        f.nseg = 1;
+        f.seg[0] = {m->b_act, m->fl, 0, SEG_OUT};
+        f.total_rows = m->fl;
+        f.out_stride = m->fl;
+        CKL(launch_batch({&L.w1}, &L.w3, EPI_SILU, f, s));
+        CKL(batch_prep_launch(m->b_act, m->fl, m->fl, ntok, nullptr, m->eps, nullptr, nullptr, m->b_xq, m->b_xs, s,
+                              true));
+        BatchParams d = batch_base(m, ntok);
+        d.nseg = 1;
+        d.seg[0] = {nullptr, m->emb, 0, SEG_OUT};
+        d.total_rows = m->emb;
+        d.hidden = m->b_hidden;
+        d.hidden_stride = m->emb;
+        CKL(launch_batch({&L.w2}, nullptr, EPI_RESID, d, s));
+    }
+    CKL(batch_prep_launch(m->b_hidden, m->emb, m->emb, ntok, m->out_norm, m->eps, nullptr, nullptr, m->b_xq, m->b_xs,
+                          s, true));
+    BatchParams h = batch_base(m, ntok);
+    h.nseg = 1;
+    h.seg[0] = {nullptr, m->hr, 0, SEG_OUT};
+    h.total_rows = m->hr;
+    h.amax_part = m->b_amax;
+    h.counter = m->b_cnt;
+    h.argmax_out = m->b_arg;
+    h.head_row0 = m->h0;
+    CKL(launch_batch({&m->head}, nullptr, EPI_ARGMAX, h, s));
+    CK(cudaMemcpyAsync(m->h_stage + 4, m->b_arg, 4 * (size_t)ntok, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    if ((st = check_err(m))) return st;
+    memcpy(argmax_out, m->h_stage + 4, 4 * (size_t)ntok);
+    return NCM_OK;
+}
+
+// speculative.rs:299-494 speculative_decoding_step at temperature 0, repeated: the
+// draft proposes k tokens greedily (its device-resident decode graph), the target
+// verifies them in one multi-row pass, the agreeing prefix is accepted, then the
+// target's own token at the first disagreement (or the trailing token) is emitted and
+// run one token at a time through both models.  The output equals the target's greedy
+// decode.  stats[0] = drafted, stats[1] = accepted.
+extern "C" ncm_status ncm_spec_generate(ncm_model* target, ncm_model* draft, const int* prompt, int n_prompt,
+                                       int n_gen, int k, int* out_tokens, int* stats) {
+    if (!target || !draft || !prompt || !out_tokens || n_prompt < 1 || n_gen < 0 || k < 1 || k > kMaxBatch)
+        return fail(NCM_EINVAL, "bad speculative arguments");
+    if (target->vocab != draft->vocab) return fail(NCM_EINVAL, "draft and target vocabularies differ");
+    if (n_prompt + n_gen + k + 1 > std::min(target->ctx, draft->ctx))
+        return fail(NCM_EINVAL, "prompt + generation + draft window exceeds a context");
+    if (stats) stats[0] = stats[1] = 0;
+    ncm_status st = ncm_prefill_tokens(target, prompt, n_prompt, nullptr);
+    if (!st) st = ncm_prefill_tokens(draft, prompt, n_prompt, nullptr);
+    if (st) return st;
+    int tt = 0, dt = 0, pos = n_prompt, n = 0;
+    {
+        int p0 = 0;
+        if ((st = ncm_sync_tokens(target, nullptr, 0, &p0))) return st;
+        CK(cudaSetDevice(target->device));
+        CK(cudaMemcpy(&tt, target->state + ST_LAST_TOKEN, 4, cudaMemcpyDeviceToHost));
+        if ((st = ncm_sync_tokens(draft, nullptr, 0, &p0))) return st;
+        CK(cudaSetDevice(draft->device));
+        CK(cudaMemcpy(&dt, draft->state + ST_LAST_TOKEN, 4, cudaMemcpyDeviceToHost));
+    }
+    std::vector<int> hist(std::min(target->ctx, draft->ctx));
+    while (n < n_gen) {
+        // draft: k greedy tokens from its current state (token dt at pos)
+        if ((st = ncm_decode_steps(draft, k, nullptr))) return st;
+        if ((st = ncm_sync_tokens(draft, hist.data(), pos + k, nullptr))) return st;
+        int drafted[kMaxBatch], rows[kMaxBatch];
+        for (int i = 0; i < k; ++i) drafted[i] = hist[pos + i];
+        if (stats) stats[0] += k;
+        // target: every drafted token through one multi-row pass
+        if ((st = ncm_verify_batch(target, drafted, k, pos, rows))) return st;
+        int i = 0, next = tt;
+        while (i < k && drafted[i] == next) {
+            if (n < n_gen) out_tokens[n++] = drafted[i];
+            if (stats) stats[1] += 1;
+            next = rows[i];
+            ++i;
+        }
+        // `next`: the target's token after the accepted prefix (the correction, or the
+        // trailing token when all k were accepted); run it through both models
+        if (n < n_gen) out_tokens[n++] = next;
+        const int at = pos + i;
+        if ((st = ncm_forward_pass(target, next, at, nullptr, &tt))) return st;
+        if ((st = ncm_forward_pass(draft, next, at, nullptr, &dt))) return st;
+        pos = at + 1;
+    }
+    return NCM_OK;
+}
+
 // ------------------------------------------------------------------ tensor parallel
 extern "C" ncm_status ncm_tp_export(ncm_model* m, uint8_t* handle_out) {
     if (!m || !handle_out) return fail(NCM_EINVAL, "null argument");
@@ -947,12 +1157,35 @@ extern "C" ncm_status ncm_matmul_quantized(int qtype, const void* w, int64_t row
 // is ntok single-token GEMVs (bit-identical per token by construction).
 extern "C" ncm_status ncm_matmul_quantized_batch(int qtype, const void* w, int64_t rows, int cols, int ntok,
                                                 const int8_t* x_i8, const float* x_scales, float* out, void* stream) {
-    if (ntok < 1 || ntok > 8) return fail(NCM_EINVAL, "1 <= ntok <= 8");
-    for (int t = 0; t < ntok; ++t) {
-        ncm_status st = ncm_matmul_quantized(qtype, w, rows, cols, x_i8 + (size_t)t * cols,
-                                             x_scales + (size_t)t * (cols / 32), out + (size_t)t * rows, stream);
-        if (st) return st;
-    }
+    if (ntok < 1 || ntok > kMaxBatch) return fail(NCM_EINVAL, "1 <= ntok <= 8");
+    if (!gemv_type_ok(qtype)) return fail(NCM_EUNSUPPORTED, "quant type outside Q4_0/Q8_0/Q4_K");
+    if (rows <= 0 || rows > (1 << 30) || cols <= 0 || cols % ncm_type_block_elems(qtype) || cols % 32)
+        return fail(NCM_EINVAL, "bad shape");
+    if (!w || !x_i8 || !x_scales || !out) return fail(NCM_EINVAL, "null pointer");
+    if (((uintptr_t)x_i8 & 15) || ((uintptr_t)w & 15) || (cols % 16))
+        return fail(NCM_EINVAL, "w and x_i8 must be 16-byte aligned");
+    const int pitch = row_bytes(qtype, cols);
+    if (pitch % 16) return fail(NCM_EINVAL, "row pitch must be a multiple of 16 bytes");
+    BatchParams p;
+    memset(&p, 0, sizeof p);
+    p.nseg = 1;
+    p.seg[0] = {out, (int)rows, 0, SEG_OUT};
+    p.total_rows = (int)rows;
+    p.out_stride = (int)rows;
+    p.xq = x_i8;
+    p.xs = x_scales;
+    const int grid = batch_plan(qtype, cols, (int)rows, false, ntok, p);
+    if (grid < 0) return fail(NCM_EUNSUPPORTED, "activation rows do not fit in shared memory");
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    int* err = nullptr;
+    CK(cudaMallocAsync((void**)&err, 4, (cudaStream_t)stream));
+    CK(cudaMemsetAsync(err, 0, 4, (cudaStream_t)stream));
+    p.err = err;
+    int r = gemv_tensor_map(&p.tm[0], w, rows, pitch, p.chunk_words, p.box_rows);
+    if (!r) r = batch_gemv_launch(qtype, EPI_PLAIN, p, grid, (cudaStream_t)stream, false);
+    cudaFreeAsync(err, (cudaStream_t)stream);
+    if (r) return fail(NCM_ECUDA, std::string("batch gemv launch: ") + cudaGetErrorString((cudaError_t)r));
     return NCM_OK;
 }
 

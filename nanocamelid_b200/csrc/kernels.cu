@@ -1531,4 +1531,475 @@ int peer_timeout_test_launch(TpComm c, int* err, cudaStream_t s) {
     return (int)cudaGetLastError();
 }
 
+
+// ================================================================== multi-row GEMV (verify)
+// speculative.rs:381-389 prefill_pass_batch -> inference.rs:1246-1303
+// matmul_quantized_batch: each of ntok <= 8 activation rows against the same weights,
+// every row's result bit-identical to the one-row GEMV (inference.rs:6866-6913).
+// The block dots come from int8 tensor-core MMA (mma.sync m16n8k32 s8): A = 16 weight
+// rows x one 32-column block straight from the raw GGUF bytes in shared memory (Q4_0
+// nibbles - 8, Q8_0 bytes, Q4_K unsigned nibbles), B = the block of 8 token rows.  Lane
+// (g, t) of a warp then holds the exact integer dots of rows g, g+8 and tokens 2t, 2t+1
+// and folds them into its four row sums in block order, with the one-row path's term
+// formulas -- no separate fold stage.
+constexpr int kBatchThreads = 288;   // warps 0-7 compute 16-row slabs, warp 8 produces
+constexpr int kBatchProducer = 256;
+
+__device__ __forceinline__ void mma_s8_16x8x32(int32_t c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// 4 bytes at a 2-byte aligned shared-memory address.
+__device__ __forceinline__ uint32_t ld_u32_a2(const uint8_t* p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    if ((a & 3) == 0) return *reinterpret_cast<const uint32_t*>(p);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(p - 2);
+    return __funnelshift_r(w[0], w[1], 16);
+}
+
+__device__ __forceinline__ TileCursor batch_tile_at(const BatchParams& p, int cur, int r_end) {
+    int s = 0;
+#pragma unroll
+    for (int i = 1; i < kMaxSeg; ++i)
+        if (i < p.nseg && cur >= p.seg[i].row_begin) s = i;
+    const int seg_end = p.seg[s].row_begin + p.seg[s].rows;
+    return {s, min(p.box_rows, min(r_end, seg_end) - cur)};
+}
+
+// Folds one 512-column chunk of one matrix (tile rows ra, rb = ra + 8) into acc[4]
+// (acc[0] = (ra, tok 2t), [1] = (ra, 2t+1), [2] = (rb, 2t), [3] = (rb, 2t+1)).
+template <int QT>
+__device__ __forceinline__ void batch_chunk(const uint8_t* tile, int cb, int ra, int g, int t, int c, const uint8_t* xq,
+                                            int xq_pitch, const float* xs, const int* xsum, int nb, int ntok,
+                                            float acc[4]) {
+    const uint8_t* rowa = tile + ra * cb;
+    const uint8_t* rowb = rowa + 8 * cb;
+    const bool tg = g < ntok;
+    const uint8_t* xrow = xq + g * xq_pitch;
+    const int ta = 2 * t, tb = 2 * t + 1;
+    const bool va = ta < ntok, vb = tb < ntok;
+    if constexpr (QT == NCM_T_Q4_0 || QT == NCM_T_Q8_0) {
+        constexpr int BB = QT == NCM_T_Q4_0 ? 18 : 34;
+#pragma unroll 4
+        for (int bl = 0; bl < 16; ++bl) {
+            const int bg = 16 * c + bl;
+            if (bg >= nb) break;
+            uint32_t a0, a1, a2, a3;
+            if constexpr (QT == NCM_T_Q4_0) {
+                const uint32_t wa = ld_u32_a2(rowa + BB * bl + 2 + 4 * t), wb = ld_u32_a2(rowb + BB * bl + 2 + 4 * t);
+                a0 = __vsub4(wa & 0x0f0f0f0fu, 0x08080808u);
+                a2 = __vsub4((wa >> 4) & 0x0f0f0f0fu, 0x08080808u);
+                a1 = __vsub4(wb & 0x0f0f0f0fu, 0x08080808u);
+                a3 = __vsub4((wb >> 4) & 0x0f0f0f0fu, 0x08080808u);
+            } else {
+                a0 = ld_u32_a2(rowa + BB * bl + 2 + 4 * t);
+                a2 = ld_u32_a2(rowa + BB * bl + 18 + 4 * t);
+                a1 = ld_u32_a2(rowb + BB * bl + 2 + 4 * t);
+                a3 = ld_u32_a2(rowb + BB * bl + 18 + 4 * t);
+            }
+            uint32_t b0 = 0, b1 = 0;
+            if (tg) {
+                b0 = *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 4 * t);
+                b1 = *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 16 + 4 * t);
+            }
+            int32_t d4[4] = {0, 0, 0, 0};
+            mma_s8_16x8x32(d4, a0, a1, a2, a3, b0, b1);
+            const float da = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rowa + BB * bl));
+            const float db = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rowb + BB * bl));
+            const float sa = va ? xs[ta * nb + bg] : 0.0f, sb = vb ? xs[tb * nb + bg] : 0.0f;
+            // inference.rs:2663 / 1157: d_w * x_scale * (dot as f32), row sum in block order
+            acc[0] += da * sa * (float)d4[0];
+            acc[1] += da * sb * (float)d4[1];
+            acc[2] += db * sa * (float)d4[2];
+            acc[3] += db * sb * (float)d4[3];
+        }
+    } else {
+        // Q4_K: two 256-column super-blocks per chunk; sub-block terms summed from 0 per
+        // super-block (q8.rs:1342), then added to the row sum (inference.rs:3129).
+#pragma unroll 1
+        for (int sbi = 0; sbi < 2; ++sbi) {
+            if (2 * c + sbi >= nb / 8) break;
+            const uint8_t* sa_ = rowa + 144 * sbi;
+            const uint8_t* sb_ = rowb + 144 * sbi;
+            const uint4 ha = *reinterpret_cast<const uint4*>(sa_), hb = *reinterpret_cast<const uint4*>(sb_);
+            const float dA = f16_bits_to_f32(ha.x & 0xffff), mA = f16_bits_to_f32(ha.x >> 16);
+            const float dB = f16_bits_to_f32(hb.x & 0xffff), mB = f16_bits_to_f32(hb.x >> 16);
+            float ss[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int pr = 0; pr < 4; ++pr) {
+                const uint32_t wa0 = *reinterpret_cast<const uint32_t*>(sa_ + 16 + 32 * pr + 4 * t);
+                const uint32_t wa1 = *reinterpret_cast<const uint32_t*>(sa_ + 32 + 32 * pr + 4 * t);
+                const uint32_t wb0 = *reinterpret_cast<const uint32_t*>(sb_ + 16 + 32 * pr + 4 * t);
+                const uint32_t wb1 = *reinterpret_cast<const uint32_t*>(sb_ + 32 + 32 * pr + 4 * t);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int j = 2 * pr + h, bg = 16 * c + 8 * sbi + j;
+                    const uint32_t a0 = (wa0 >> (4 * h)) & 0x0f0f0f0fu, a2 = (wa1 >> (4 * h)) & 0x0f0f0f0fu;
+                    const uint32_t a1 = (wb0 >> (4 * h)) & 0x0f0f0f0fu, a3 = (wb1 >> (4 * h)) & 0x0f0f0f0fu;
+                    uint32_t b0 = 0, b1 = 0;
+                    if (tg) {
+                        b0 = *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 4 * t);
+                        b1 = *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 16 + 4 * t);
+                    }
+                    int32_t d4[4] = {0, 0, 0, 0};
+                    mma_s8_16x8x32(d4, a0, a1, a2, a3, b0, b1);
+                    int scA, mnA, scB, mnB;
+                    q4k_scale_min(j, ha.y, ha.z, ha.w, scA, mnA);
+                    q4k_scale_min(j, hb.y, hb.z, hb.w, scB, mnB);
+                    const float sclA = dA * (float)scA, mnlA = mA * (float)mnA;
+                    const float sclB = dB * (float)scB, mnlB = mB * (float)mnB;
+                    const float sa = va ? xs[ta * nb + bg] : 0.0f, sb = vb ? xs[tb * nb + bg] : 0.0f;
+                    const float xa = va ? (float)xsum[ta * nb + bg] : 0.0f, xb = vb ? (float)xsum[tb * nb + bg] : 0.0f;
+                    // q8.rs:1370-1373: x_scale * (d*sc * sum(q*x) - dmin*m * sum(x))
+                    ss[0] += sa * (sclA * (float)d4[0] - mnlA * xa);
+                    ss[1] += sb * (sclA * (float)d4[1] - mnlA * xb);
+                    ss[2] += sa * (sclB * (float)d4[2] - mnlB * xa);
+                    ss[3] += sb * (sclB * (float)d4[3] - mnlB * xb);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[i] += ss[i];
+        }
+    }
+}
+
+template <int QT, int EPI>
+__global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(const __grid_constant__ BatchParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr bool DUAL = (EPI == EPI_SILU);
+    __shared__ float wv[8][kMaxBatch];
+    __shared__ int wi[8][kMaxBatch];
+    __shared__ int s_last;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + 8;
+    uint8_t* stages = smem + p.stage_off;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int R = p.total_rows, nbk = gridDim.x;
+    const int r_begin = (int)(((long long)blockIdx.x * R / nbk)) & ~1;
+    const int r_end = (blockIdx.x + 1 == nbk) ? R : ((int)(((long long)(blockIdx.x + 1) * R / nbk)) & ~1);
+    const int box_bytes = p.box_rows * p.chunk_bytes;
+    const int box2_off = (box_bytes + 127) & ~127;
+    const int ns = p.nstages;
+    const uint64_t limit_ns = 4000000000ull;
+    if (tid == 0) {
+        for (int s = 0; s < ns; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 8);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    int icur = r_begin, ichunk = 0, tprod = 0;
+    uint64_t pol = 0;
+    auto issue = [&]() {
+        const int s = tprod % ns;
+        if (tprod >= ns && !mbar_wait(&empty[s], (uint32_t)(((tprod / ns) & 1) ^ 1), limit_ns))
+            set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+        const TileCursor tc = batch_tile_at(p, icur, r_end);
+        const int y = icur - p.seg[tc.seg].row_begin;
+        const int x = ichunk * p.chunk_words;
+        mbar_arrive_expect_tx(&full[s], DUAL ? 2 * box_bytes : box_bytes);
+        tma_load_2d(stages + (size_t)s * p.stage_bytes, &p.tm[tc.seg], x, y, &full[s], pol);
+        if (DUAL) tma_load_2d(stages + (size_t)s * p.stage_bytes + box2_off, &p.tm2, x, y, &full[s], pol);
+        if (++ichunk == p.nchunk) { ichunk = 0; icur += tc.n; }
+        ++tprod;
+    };
+    if (tid == kBatchProducer) {
+        pol = l2_evict_first_policy();
+        while (tprod < ns && icur < r_end) issue();
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    // quantised rows, their scales and per-block sums into shared memory
+    uint8_t* xq = smem + p.xq_off;
+    float* xs = reinterpret_cast<float*>(smem + p.xs_off);
+    int* xsum = reinterpret_cast<int*>(smem + p.xsum_off);
+    {
+        const int n16 = p.cols / 16;
+        for (int i = tid; i < p.ntok * n16; i += blockDim.x) {
+            const int tk = i / n16, k = i % n16;
+            *reinterpret_cast<uint4*>(xq + tk * p.xq_pitch + 16 * k) =
+                *reinterpret_cast<const uint4*>(p.xq + (size_t)tk * p.cols + 16 * k);
+        }
+        for (int i = tid; i < p.ntok * p.nb; i += blockDim.x) {
+            const int tk = i / p.nb, b = i % p.nb;
+            xs[i] = p.xs[(size_t)tk * p.nb + b];
+            const uint4* src = reinterpret_cast<const uint4*>(p.xq + (size_t)tk * p.cols + 32 * b);
+            int sum = 0;
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const uint4 v = src[k];
+                sum = __dp4a((int)v.x, 0x01010101, sum);
+                sum = __dp4a((int)v.y, 0x01010101, sum);
+                sum = __dp4a((int)v.z, 0x01010101, sum);
+                sum = __dp4a((int)v.w, 0x01010101, sum);
+            }
+            xsum[i] = sum;
+        }
+    }
+    __syncthreads();
+    float best_v[2] = {-INFINITY, -INFINITY};
+    int best_i[2] = {0x7fffffff, 0x7fffffff};
+    if (tid == kBatchProducer) {
+        while (icur < r_end) issue();
+    } else if (warp < 8) {
+        const int g = lane >> 2, t = lane & 3;
+        const int ra = 16 * warp + g, rb = ra + 8;
+        int tc_ = 0;
+        for (int cur = r_begin; cur < r_end;) {
+            const TileCursor tc = batch_tile_at(p, cur, r_end);
+            const int n = tc.n;
+            const bool active = 16 * warp < n;
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, acc2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int c = 0; c < p.nchunk; ++c, ++tc_) {
+                const int s = tc_ % ns;
+                if (!mbar_wait(&full[s], (uint32_t)((tc_ / ns) & 1), limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+                if (active) {
+                    const uint8_t* tile = stages + (size_t)s * p.stage_bytes;
+                    batch_chunk<QT>(tile, p.chunk_bytes, ra, g, t, c, xq, p.xq_pitch, xs, xsum, p.nb, p.ntok, acc);
+                    if (DUAL)
+                        batch_chunk<QT>(tile + box2_off, p.chunk_bytes, ra, g, t, c, xq, p.xq_pitch, xs, xsum, p.nb,
+                                        p.ntok, acc2);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+            }
+            // tile epilogue: rows ra / rb (tile-local), tokens 2t / 2t+1
+            const Seg& sg = p.seg[tc.seg];
+            const int lrow0 = cur - sg.row_begin;
+            float part[4];
+            if (EPI == EPI_QKV) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) part[i] = __shfl_xor_sync(NCM_FULL, acc[i], 4);   // row ^ 1
+            }
+            if (active) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int r = (i < 2) ? ra : rb, tk = 2 * t + (i & 1);
+                    if (r >= n || tk >= p.ntok) continue;
+                    const int lr = lrow0 + r;
+                    const float v = acc[i];
+                    if constexpr (EPI == EPI_PLAIN) {
+                        sg.out[(size_t)tk * p.out_stride + lr] = v;
+                    } else if constexpr (EPI == EPI_RESID) {
+                        p.hidden[(size_t)tk * p.hidden_stride + lr] += v;   // inference.rs:4670-4672
+                    } else if constexpr (EPI == EPI_QKV) {
+                        float o = v;
+                        if (sg.kind != SEG_V) {
+                            // inference.rs:904-933 apply_rope_cached at this token's position
+                            const int ri = (lr % p.head_dim) >> 1;
+                            if (ri < p.rope_half) {
+                                const float2 scs = p.rope[(size_t)(p.pos0 + tk) * p.rope_half + ri];
+                                const float x0 = (lr & 1) ? part[i] : v;
+                                const float x1 = (lr & 1) ? v : part[i];
+                                o = (lr & 1) ? (x0 * scs.x + x1 * scs.y) : (x0 * scs.y - x1 * scs.x);
+                            }
+                        }
+                        if (sg.kind == SEG_Q) sg.out[(size_t)tk * p.out_stride + lr] = o;
+                        else ((sg.kind == SEG_K ? p.kcache : p.vcache) + (size_t)(p.pos0 + tk) * p.kv_width)[lr] = o;
+                    } else if constexpr (EPI == EPI_SILU) {
+                        const float gg = v, uu = acc2[i];
+                        const float sig = 1.0f / (1.0f + expf_cr(-gg));   // inference.rs:3385-3388
+                        sg.out[(size_t)tk * p.out_stride + lr] = gg * sig * uu;
+                    } else if constexpr (EPI == EPI_ARGMAX) {
+                        if (sg.out) sg.out[(size_t)tk * p.out_stride + lr] = v;
+                        const int k = i & 1;
+                        if (better(v, lr, best_v[k], best_i[k])) { best_v[k] = v; best_i[k] = lr; }
+                    }
+                }
+            }
+            cur += n;
+        }
+        if constexpr (EPI == EPI_ARGMAX) {
+            // lanes with the same t hold the same two tokens: reduce over g (lane bits 2-4)
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) {
+                    const float ov = __shfl_xor_sync(NCM_FULL, best_v[k], o);
+                    const int oi = __shfl_xor_sync(NCM_FULL, best_i[k], o);
+                    if (better(ov, oi, best_v[k], best_i[k])) { best_v[k] = ov; best_i[k] = oi; }
+                }
+            }
+            if (lane < 4) {
+                wv[warp][2 * lane] = best_v[0]; wi[warp][2 * lane] = best_i[0];
+                wv[warp][2 * lane + 1] = best_v[1]; wi[warp][2 * lane + 1] = best_i[1];
+            }
+        }
+    }
+    __syncthreads();
+    if constexpr (EPI == EPI_ARGMAX) {
+        if (tid < p.ntok) {
+            float bv = wv[0][tid];
+            int bi = wi[0][tid];
+            for (int w = 1; w < 8; ++w)
+                if (better(wv[w][tid], wi[w][tid], bv, bi)) { bv = wv[w][tid]; bi = wi[w][tid]; }
+            p.amax_part[(size_t)blockIdx.x * kMaxBatch + tid] = make_float2(bv, __int_as_float(bi));
+        }
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) s_last = atomicAdd(p.counter, 1u) == (unsigned)nbk - 1;
+        __syncthreads();
+        if (s_last && tid < p.ntok) {
+            __threadfence();
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
+            for (int c = 0; c < nbk; ++c) {
+                const float2 e = __ldcg(&p.amax_part[(size_t)c * kMaxBatch + tid]);
+                const int ei = __float_as_int(e.y);
+                if (better(e.x, ei, bv, bi)) { bv = e.x; bi = ei; }
+            }
+            p.argmax_out[tid] = p.head_row0 + bi;
+        }
+        __syncthreads();
+        if (s_last && tid == 0) *p.counter = 0u;
+    }
+}
+
+constexpr int kBatchSmemLimit = 220 * 1024;
+
+int batch_plan(int qtype, int cols, int rows, bool dual, int ntok, BatchParams& p) {
+    if (ntok < 1 || ntok > kMaxBatch || cols % 32) return -1;
+    p.ntok = ntok;
+    p.cols = cols;
+    p.nb = cols / 32;
+    p.nchunk = (cols + kChunkCols - 1) / kChunkCols;
+    p.chunk_bytes = qtype == NCM_T_Q8_0 ? 16 * 34 : 288;
+    p.chunk_words = p.chunk_bytes / 4;
+    p.total_rows = rows;
+    int grid = num_sms();
+    const int maxg = (rows + 15) / 16;
+    if (grid > maxg) grid = maxg > 0 ? maxg : 1;
+    const int per_cta = (rows + grid - 1) / grid;
+    int cap = qtype == NCM_T_Q8_0 ? 64 : 128;
+    if (dual) cap /= 2;
+    int br = (per_cta + 15) & ~15;
+    if (br > cap) br = cap;
+    if (br < 16) br = 16;
+    p.box_rows = br;
+    p.stage_bytes = (br * p.chunk_bytes + 127) / 128 * 128 * (dual ? 2 : 1);
+    p.xq_pitch = cols + 16;   // distinct banks for the eight token rows of a fragment
+    int off = 128;
+    p.xq_off = off;
+    off += (ntok * p.xq_pitch + 127) / 128 * 128;
+    p.xs_off = off;
+    off += (ntok * p.nb * 4 + 127) / 128 * 128;
+    p.xsum_off = off;
+    off += (ntok * p.nb * 4 + 127) / 128 * 128;
+    p.stage_off = off;
+    int ns = kMaxStages;
+    while (ns > 2 && off + ns * p.stage_bytes > kBatchSmemLimit) --ns;
+    p.nstages = ns;
+    p.smem_bytes = off + ns * p.stage_bytes;
+    if (p.smem_bytes > kBatchSmemLimit) return -1;
+    return grid;
+}
+
+template <int QT, int EPI>
+static int batch_launch_t(const BatchParams& p, int grid, cudaStream_t s, bool pdl) {
+    static bool configured = false;
+    auto kern = gemv_batch_kernel<QT, EPI>;
+    if (!configured) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBatchSmemLimit);
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kBatchThreads);
+    cfg.dynamicSmemBytes = p.smem_bytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return (int)cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+template <int QT>
+static int batch_launch_q(int epi, const BatchParams& p, int grid, cudaStream_t s, bool pdl) {
+    switch (epi) {
+        case EPI_PLAIN: return batch_launch_t<QT, EPI_PLAIN>(p, grid, s, pdl);
+        case EPI_RESID: return batch_launch_t<QT, EPI_RESID>(p, grid, s, pdl);
+        case EPI_QKV: return batch_launch_t<QT, EPI_QKV>(p, grid, s, pdl);
+        case EPI_SILU: return batch_launch_t<QT, EPI_SILU>(p, grid, s, pdl);
+        case EPI_ARGMAX: return batch_launch_t<QT, EPI_ARGMAX>(p, grid, s, pdl);
+        default: return (int)cudaErrorInvalidValue;
+    }
+}
+
+int batch_gemv_launch(int qtype, int epi, const BatchParams& p, int grid, cudaStream_t s, bool pdl) {
+    if (qtype == NCM_T_Q4_0) return batch_launch_q<NCM_T_Q4_0>(epi, p, grid, s, pdl);
+    if (qtype == NCM_T_Q8_0) return batch_launch_q<NCM_T_Q8_0>(epi, p, grid, s, pdl);
+    if (qtype == NCM_T_Q4_K) return batch_launch_q<NCM_T_Q4_K>(epi, p, grid, s, pdl);
+    return (int)cudaErrorInvalidValue;
+}
+
+// Per token row: optional rms_norm (inference.rs:697-706; layer 0 reads the embedding
+// row's sequential sum of squares) then quantize_f32_to_q8_0 (inference.rs:991-1029).
+__global__ void __launch_bounds__(kThreads) batch_prep_kernel(const float* x, int x_stride, int n, const float* norm_w,
+                                                              float eps, const float* ssq_tab, const int* toks,
+                                                              int8_t* xq, float* xs) {
+    extern __shared__ __align__(16) float xr[];
+    __shared__ SeqSumScratch sc;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tk = blockIdx.x, tid = threadIdx.x;
+    stage_f32(xr, x + (size_t)tk * x_stride, n, tid, blockDim.x);
+    __syncthreads();
+    float scale = 1.0f;
+    if (norm_w) {
+        const float tot = ssq_tab ? ssq_tab[toks[tk]]
+                                  : seq_sum_nonneg<kThreads>([&](int i) { float v = xr[i]; return v * v; }, n, sc, tid);
+        scale = 1.0f / sqrtf(tot / (float)n + eps);
+    }
+    for (int b = tid; b < n / 32; b += blockDim.x) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = norm_w ? xr[32 * b + i] * scale * norm_w[32 * b + i] : xr[32 * b + i];
+        uint32_t w[8];
+        float s = 0.0f;
+        int sum = 0;
+        quant_block32(v, w, s, sum);
+        uint4* dst = reinterpret_cast<uint4*>(xq + (size_t)tk * n + 32 * b);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        xs[(size_t)tk * (n / 32) + b] = s;
+    }
+}
+
+int batch_prep_launch(const float* x, int x_stride, int n, int ntok, const float* norm_w, float eps,
+                      const float* ssq_tab, const int* toks, int8_t* xq, float* xs, cudaStream_t s, bool pdl) {
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(batch_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
+        configured = true;
+    }
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = small_cfg(dim3(ntok), dim3(kThreads), s, pdl, attr);
+    cfg.dynamicSmemBytes = (size_t)n * 4;
+    return (int)cudaLaunchKernelEx(&cfg, batch_prep_kernel, x, x_stride, n, norm_w, eps, ssq_tab, toks, xq, xs);
+}
+
+__global__ void embed_rows_kernel(int type, const uint8_t* table, int64_t pitch, int emb, const int* toks,
+                                  float* hidden) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tk = blockIdx.y;
+    const uint8_t* row = table + (size_t)toks[tk] * pitch;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < emb; i += gridDim.x * blockDim.x)
+        hidden[(size_t)tk * emb + i] = dequant_elem(type, row, i);
+}
+
+int embed_rows_launch(int type, const uint8_t* table, int64_t pitch, int emb, const int* toks, int ntok,
+                      float* hidden, cudaStream_t s, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = small_cfg(dim3((emb + 255) / 256, ntok), dim3(256), s, pdl, attr);
+    return (int)cudaLaunchKernelEx(&cfg, embed_rows_kernel, type, table, pitch, emb, toks, hidden);
+}
+
 }  // namespace ncm

@@ -101,6 +101,35 @@ struct AttnParams {
     float scale;
 };
 
+// Multi-row (speculative verify) GEMV: ntok activation rows share every weight tile;
+// int8 tensor-core MMA forms the block dots (16 weight rows x 8 token rows per
+// instruction), each (row, token) chain is folded in block order as in the one-row GEMV.
+constexpr int kMaxBatch = 8;
+struct alignas(64) BatchParams {
+    CUtensorMap tm[kMaxSeg];
+    CUtensorMap tm2;              // EPI_SILU: the up matrix
+    Seg seg[kMaxSeg];             // seg.out: token 0's destination (token t at + t * out_stride)
+    int nseg, total_rows;
+    int cols, nb, nchunk, chunk_words, chunk_bytes, box_rows, stage_bytes, nstages;
+    int xq_off, xs_off, xsum_off, stage_off, smem_bytes, xq_pitch;
+    int ntok;
+    const int8_t* xq;             // [ntok][cols] quantised rows
+    const float* xs;              // [ntok][cols / 32]
+    int out_stride;
+    float* hidden;                // EPI_RESID: hidden[t * hidden_stride + row] += sum
+    int hidden_stride;
+    int pos0;                     // EPI_QKV: position of token 0 (token t at pos0 + t)
+    const float2* rope;
+    int rope_half, head_dim;
+    float* kcache; float* vcache;
+    int kv_width;
+    float2* amax_part;            // EPI_ARGMAX: [grid][kMaxBatch]
+    unsigned* counter;
+    int* argmax_out;              // [ntok] global vocab rows
+    int head_row0;
+    int* err;
+};
+
 // Launchers (kernels.cu).
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -127,6 +156,12 @@ int synth_launch(int type, uint64_t key, int64_t r0, int64_t nrows, int64_t c0, 
 int requant_q4_0_launch(int src_type, const uint8_t* src, int64_t rows, int cols, int64_t src_pitch, uint8_t* dst,
                         int64_t dst_pitch, cudaStream_t s);
 int peer_timeout_test_launch(TpComm c, int* err, cudaStream_t s);
+int batch_plan(int qtype, int cols, int rows, bool dual, int ntok, BatchParams& p);
+int batch_gemv_launch(int qtype, int epi, const BatchParams& p, int grid, cudaStream_t s, bool pdl);
+int batch_prep_launch(const float* x, int x_stride, int n, int ntok, const float* norm_w, float eps,
+                      const float* ssq_tab, const int* toks, int8_t* xq, float* xs, cudaStream_t s, bool pdl);
+int embed_rows_launch(int type, const uint8_t* table, int64_t pitch, int emb, const int* toks, int ntok,
+                      float* hidden, cudaStream_t s, bool pdl);
 int num_sms();
 int expf_table_install(const uint32_t* dev_tab, uint32_t mask);
 // libm_table.cpp
