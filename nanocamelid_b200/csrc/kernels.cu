@@ -573,42 +573,68 @@ __device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, GemvSeqScratch
             }
             scale = 1.0f / sqrtf(tot / (float)p.cols + p.eps);
         }
-        for (int b = tid; b < nblk; b += blockDim.x) {
+        // Four lanes per 32-value block (quantize_f32_to_q8_0, inference.rs:991-1029):
+        // lane li takes elements 8c .. 8c+7 with c = (li + b) & 3 (bank rotation); the
+        // block max and the value sum are reduced inside the quad (both order free),
+        // every element is rounded exactly as in the one-thread quantiser.
+        const int li = tid & 3;
+        const unsigned qmask = 0xFu << (tid & 28);
+        for (int b = tid >> 2; b < nblk; b += blockDim.x >> 2) {
             uint32_t* dst = reinterpret_cast<uint32_t*>(smem + p.xq_off + 80 * (b >> 1) + 32 * (b & 1));
-            float s = 0.0f;
-            int sum = 0;
+            const int c = (li + b) & 3;
             if (b < p.nb) {
-                // The block's eight float4 groups are read starting at group (b & 7), so
-                // the eight lanes of a shared-memory phase hit distinct banks; amax and
-                // the sum are order free and each group quantises into its own word.
-                float v[32];
-                const float4* xb = reinterpret_cast<const float4*>(xf) + 8 * b;
-                const int rot = b & 7;
+                float v[8];
+                const float4* xb = reinterpret_cast<const float4*>(xf) + 8 * b + 2 * c;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int j = (i + rot) & 7;
-                    const float4 x4 = xb[j];
+                for (int h = 0; h < 2; ++h) {
+                    const float4 x4 = xb[h];
                     if constexpr (IN == IN_F32_RMS) {
-                        const float4 w4 = reinterpret_cast<const float4*>(smem + p.nw_off)[8 * b + j];
+                        const float4 w4 = reinterpret_cast<const float4*>(smem + p.nw_off)[8 * b + 2 * c + h];
                         // inference.rs:704 out = x * scale * weight
-                        v[4 * i] = x4.x * scale * w4.x;
-                        v[4 * i + 1] = x4.y * scale * w4.y;
-                        v[4 * i + 2] = x4.z * scale * w4.z;
-                        v[4 * i + 3] = x4.w * scale * w4.w;
+                        v[4 * h] = x4.x * scale * w4.x;
+                        v[4 * h + 1] = x4.y * scale * w4.y;
+                        v[4 * h + 2] = x4.z * scale * w4.z;
+                        v[4 * h + 3] = x4.w * scale * w4.w;
                     } else {
-                        v[4 * i] = x4.x; v[4 * i + 1] = x4.y; v[4 * i + 2] = x4.z; v[4 * i + 3] = x4.w;
+                        v[4 * h] = x4.x; v[4 * h + 1] = x4.y; v[4 * h + 2] = x4.z; v[4 * h + 3] = x4.w;
                     }
                 }
-                uint32_t w[8];
-                quant_block32(v, w, s, sum);
+                float amax = 0.0f;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) dst[(i + rot) & 7] = w[i];
+                for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+                amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 1));
+                amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 2));
+                const float scale_b = amax / 127.0f;
+                uint32_t w0 = 0, w1 = 0;
+                int sum = 0;
+                if (scale_b > 0.0f) {
+                    const float inv = 1.0f / scale_b;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        float q = roundf(v[i] * inv);
+                        q = fminf(fmaxf(q, -127.0f), 127.0f);
+                        const int qi = (int)q;
+                        sum += qi;
+                        const uint32_t byte = (uint32_t)(qi & 0xff) << (8 * (i & 3));
+                        if (i < 4) w0 |= byte; else w1 |= byte;
+                    }
+                }
+                sum += __shfl_xor_sync(qmask, sum, 1);
+                sum += __shfl_xor_sync(qmask, sum, 2);
+                dst[2 * c] = w0;
+                dst[2 * c + 1] = w1;
+                if (li == 0) {
+                    reinterpret_cast<float*>(xs)[b] = scale_b;
+                    reinterpret_cast<int*>(xsum)[b] = sum;
+                }
             } else {
-#pragma unroll
-                for (int k = 0; k < 8; ++k) dst[k] = 0;
+                dst[2 * c] = 0;
+                dst[2 * c + 1] = 0;
+                if (li == 0) {
+                    reinterpret_cast<float*>(xs)[b] = 0.0f;
+                    reinterpret_cast<int*>(xsum)[b] = 0;
+                }
             }
-            reinterpret_cast<float*>(xs)[b] = s;
-            reinterpret_cast<int*>(xsum)[b] = sum;
         }
     }
 }
