@@ -108,7 +108,9 @@ struct ncm_model {
     float* b_xs = nullptr;
     float2* b_amax = nullptr;
     unsigned* b_cnt = nullptr;
-    int *b_tok = nullptr, *b_arg = nullptr;
+    int *b_tok = nullptr, *b_arg = nullptr, *b_pos = nullptr;
+    float* b_scores = nullptr;
+    cudaGraphExec_t b_graph[kMaxBatch + 1] = {};
     // tensor parallel
     int world = 1, rank = 0, reduce_mode = NCM_REDUCE_FUSED_P2P;
     bool tp_ready = false;
@@ -141,6 +143,8 @@ static void free_model(ncm_model* m) {
     cudaSetDevice(m->device);
     if (m->g_full) cudaGraphExecDestroy(m->g_full);
     if (m->g_nohead) cudaGraphExecDestroy(m->g_nohead);
+    for (auto& gx : m->b_graph)
+        if (gx) cudaGraphExecDestroy(gx);
     for (void* p : m->ipc_open) cudaIpcCloseMemHandle(p);
     if (m->nccl && g_nccl.CommDestroy) g_nccl.CommDestroy(m->nccl);
     for (void* p : m->allocs) cudaFree(p);
@@ -585,6 +589,7 @@ static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
         CKL(launch_gemv({&L.wq, &L.wk, &L.wv}, nullptr, IN_F32_RMS, EPI_QKV, p, s));
         // attention (inference.rs:4648-4665)
         AttnParams a;
+        memset(&a, 0, sizeof a);
         a.q = m->q;
         a.kc = p.kcache;
         a.vc = p.vcache;
@@ -800,6 +805,8 @@ static ncm_status ensure_batch_buffers(ncm_model* m) {
     DALLOC(m->b_cnt, 4);
     DALLOC(m->b_tok, 4 * kMaxBatch);
     DALLOC(m->b_arg, 4 * kMaxBatch);
+    DALLOC(m->b_pos, 4);
+    DALLOC(m->b_scores, 4 * (size_t)kMaxBatch * m->qh * m->ctx);
     CK(cudaMemset(m->b_cnt, 0, 4));
     return NCM_OK;
 }
@@ -834,24 +841,12 @@ static int launch_batch(std::initializer_list<const DevMat*> mats, const DevMat*
     return batch_gemv_launch(w0.type, epi, p, grid, s, true);
 }
 
-// speculative.rs:381-389 prefill_pass_batch (inference.rs:3695-4111) followed by
-// compute_logits_from_hidden + sample_logits(_, 0.0) for every row: ntok tokens at
-// positions pos0 .. pos0+ntok-1 through the whole model at once (each weight tile read
-// once for all rows), K/V stored at their positions, greedy argmax of every row out.
-// Every row's result is bit-identical to the one-token step at that position.
-extern "C" ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok, int pos0, int* argmax_out) {
-    if (!m || !tokens || !argmax_out || ntok < 1 || ntok > kMaxBatch || pos0 < 0 || pos0 + ntok > m->ctx)
-        return fail(NCM_EINVAL, "bad verify batch");
-    if (m->world > 1) return fail(NCM_EUNSUPPORTED, "multi-row verify runs on one GPU");
-    for (int i = 0; i < ntok; ++i)
-        if (tokens[i] < 0 || tokens[i] >= m->vocab) return fail(NCM_EINVAL, "token id out of range");
-    CK(cudaSetDevice(m->device));
-    ncm_status st = ensure_batch_buffers(m);
-    if (st) return st;
-    cudaStream_t s = m->stream;
+// The multi-row pass (speculative.rs:381-389 prefill_pass_batch, inference.rs:3695-4111,
+// then compute_logits_from_hidden + sample_logits(_, 0.0) per row) for tokens b_tok at
+// positions *b_pos + t: each weight tile read once for all rows, K/V stored at their
+// positions, greedy argmax of every row into b_arg.  Captured once per row count.
+static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s) {
     const int qw = m->qh * m->hd, kw = m->kh * m->hd;
-    memcpy(m->h_stage + 4, tokens, 4 * (size_t)ntok);
-    CK(cudaMemcpyAsync(m->b_tok, m->h_stage + 4, 4 * (size_t)ntok, cudaMemcpyHostToDevice, s));
     CKL(embed_rows_launch(m->embd.type, m->embd.d, m->embd.pitch, m->emb, m->b_tok, ntok, m->b_hidden, s, true));
     for (int l = 0; l < m->layers; ++l) {
         const Layer& L = m->L[l];
@@ -864,30 +859,30 @@ extern "C" ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok
         p.seg[2] = {nullptr, kw, qw + kw, SEG_V};
         p.total_rows = qw + 2 * kw;
         p.out_stride = qw;
-        p.pos0 = pos0;
+        p.pos_dev = m->b_pos;
         p.kcache = m->kc + (size_t)l * m->ctx * kw;
         p.vcache = m->vc + (size_t)l * m->ctx * kw;
         p.kv_width = kw;
         CKL(launch_batch({&L.wq, &L.wk, &L.wv}, nullptr, EPI_QKV, p, s));
-        for (int t = 0; t < ntok; ++t) {
-            AttnParams a;
-            memset(&a, 0, sizeof a);
-            a.q = m->b_q + (size_t)t * qw;
-            a.kc = p.kcache;
-            a.vc = p.vcache;
-            a.out = m->b_att + (size_t)t * qw;
-            a.scores = m->scores;
-            a.state = m->state;
-            a.pos_override = pos0 + t;
-            a.heads = m->qh;
-            a.kv_heads = m->kh;
-            a.hd = m->hd;
-            a.kvw = kw;
-            a.ctx = m->ctx;
-            a.dsplit = m->dsplit;
-            a.scale = 1.0f / sqrtf((float)m->hd);
-            CKL(attention_launch(a, s, true));
-        }
+        AttnParams a;
+        memset(&a, 0, sizeof a);
+        a.q = m->b_q;
+        a.kc = p.kcache;
+        a.vc = p.vcache;
+        a.out = m->b_att;
+        a.scores = m->b_scores;
+        a.state = m->b_pos;   // b_pos[0] plays ST_POS (= 0): token z at *b_pos + z
+        a.pos_override = -1;
+        a.heads = m->qh;
+        a.kv_heads = m->kh;
+        a.hd = m->hd;
+        a.kvw = kw;
+        a.ctx = m->ctx;
+        a.dsplit = m->dsplit;
+        a.scale = 1.0f / sqrtf((float)m->hd);
+        a.ntok = ntok;
+        a.tok_stride = qw;
+        CKL(attention_launch(a, s, true));
         CKL(batch_prep_launch(m->b_att, qw, qw, ntok, nullptr, m->eps, nullptr, nullptr, m->b_xq, m->b_xs, s, true));
         BatchParams o = batch_base(m, ntok);
         o.nseg = 1;
@@ -925,10 +920,47 @@ extern "C" ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok
     h.argmax_out = m->b_arg;
     h.head_row0 = m->h0;
     CKL(launch_batch({&m->head}, nullptr, EPI_ARGMAX, h, s));
-    CK(cudaMemcpyAsync(m->h_stage + 4, m->b_arg, 4 * (size_t)ntok, cudaMemcpyDeviceToHost, s));
+    return NCM_OK;
+}
+
+// Every row's greedy token equals the one-token step at that position bit for bit.
+extern "C" ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok, int pos0, int* argmax_out) {
+    if (!m || !tokens || !argmax_out || ntok < 1 || ntok > kMaxBatch || pos0 < 0 || pos0 + ntok > m->ctx)
+        return fail(NCM_EINVAL, "bad verify batch");
+    if (m->world > 1) return fail(NCM_EUNSUPPORTED, "multi-row verify runs on one GPU");
+    for (int i = 0; i < ntok; ++i)
+        if (tokens[i] < 0 || tokens[i] >= m->vocab) return fail(NCM_EINVAL, "token id out of range");
+    CK(cudaSetDevice(m->device));
+    ncm_status st = ensure_batch_buffers(m);
+    if (st) return st;
+    cudaStream_t s = m->stream;
+    m->h_stage[4] = pos0;
+    memcpy(m->h_stage + 5, tokens, 4 * (size_t)ntok);
+    CK(cudaMemcpyAsync(m->b_pos, m->h_stage + 4, 4, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(m->b_tok, m->h_stage + 5, 4 * (size_t)ntok, cudaMemcpyHostToDevice, s));
+    if (m->b_graph[ntok]) {
+        CK(cudaGraphLaunch(m->b_graph[ntok], s));
+    } else {
+        // first use of this row count: run eagerly (configures the kernels), then capture
+        if ((st = enqueue_verify(m, ntok, s))) return st;
+        CK(cudaStreamSynchronize(s));
+        cudaGraph_t graph;
+        CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        st = enqueue_verify(m, ntok, s);
+        cudaError_t e = cudaStreamEndCapture(s, &graph);
+        if (st) {
+            if (e == cudaSuccess) cudaGraphDestroy(graph);
+            return st;
+        }
+        CK(e);
+        e = cudaGraphInstantiate(&m->b_graph[ntok], graph, 0);
+        cudaGraphDestroy(graph);
+        CK(e);
+    }
+    CK(cudaMemcpyAsync(m->h_stage + 16, m->b_arg, 4 * (size_t)ntok, cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
     if ((st = check_err(m))) return st;
-    memcpy(argmax_out, m->h_stage + 4, 4 * (size_t)ntok);
+    memcpy(argmax_out, m->h_stage + 16, 4 * (size_t)ntok);
     return NCM_OK;
 }
 

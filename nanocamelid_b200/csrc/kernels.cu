@@ -1109,14 +1109,16 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const __grid_constant_
     __shared__ float ks[32 * 257];
     pdl_launch_dependents();
     pdl_wait();
-    const int pos = a.pos_override >= 0 ? a.pos_override : a.state[ST_POS];
+    const int tz = blockIdx.z;
+    const int pos = (a.pos_override >= 0 ? a.pos_override : a.state[ST_POS]) + tz;
     const int n = pos + 1;
     const int p0 = blockIdx.y * 32;
     if (p0 >= n) return;
     const int kvh = blockIdx.x, g = a.heads / a.kv_heads, hd = a.hd;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int np = min(32, n - p0);
-    const float* qsrc = a.q + (size_t)kvh * g * hd;
+    const float* qsrc = a.q + (size_t)tz * a.tok_stride + (size_t)kvh * g * hd;
+    float* scores = a.scores + (size_t)tz * a.heads * a.ctx;
     const float* ksrc = a.kc + (size_t)p0 * a.kvw + (size_t)kvh * hd;
     if (attn_vec_ok(a)) {
         const int per = hd >> 2;                 // float4 per row
@@ -1156,7 +1158,7 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const __grid_constant_
             float s = 0.0f;
 #pragma unroll 8
             for (int d = 0; d < hd; ++d) s += q[d] * k[d];
-            a.scores[(size_t)(kvh * g + h) * a.ctx + p0 + lane] = s * a.scale;
+            scores[(size_t)(kvh * g + h) * a.ctx + p0 + lane] = s * a.scale;
         }
     }
 }
@@ -1172,7 +1174,8 @@ __global__ void __launch_bounds__(256) attn_softmax_v_kernel(const __grid_consta
     __shared__ SeqSumScratchW scr[8];
     pdl_launch_dependents();
     pdl_wait();
-    const int pos = a.pos_override >= 0 ? a.pos_override : a.state[ST_POS];
+    const int tz = blockIdx.z;
+    const int pos = (a.pos_override >= 0 ? a.pos_override : a.state[ST_POS]) + tz;
     const int n = pos + 1;
     const int kvh = blockIdx.x, g = a.heads / a.kv_heads, hd = a.hd;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1196,7 +1199,7 @@ __global__ void __launch_bounds__(256) attn_softmax_v_kernel(const __grid_consta
     stage(0);
     if (warp < g) {
         const int h = kvh * g + warp;
-        const float* srow = a.scores + (size_t)h * a.ctx;
+        const float* srow = a.scores + (size_t)tz * a.heads * a.ctx + (size_t)h * a.ctx;
         float* wr = w + warp * n;
         float mx = -INFINITY;
         for (int p = lane; p < n; p += 32) {
@@ -1239,7 +1242,7 @@ __global__ void __launch_bounds__(256) attn_softmax_v_kernel(const __grid_consta
             for (; p < np; ++p) acc += wp[p] * vp[p * dw];
         }
     }
-    if (live) a.out[(size_t)(kvh * g + h) * hd + d0 + d] = acc;
+    if (live) a.out[(size_t)tz * a.tok_stride + (size_t)(kvh * g + h) * hd + d0 + d] = acc;
 }
 
 int attention_launch(const AttnParams& a0, cudaStream_t s, bool pdl) {
@@ -1265,10 +1268,11 @@ int attention_launch(const AttnParams& a0, cudaStream_t s, bool pdl) {
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    cfg.gridDim = dim3(a.kv_heads, (a.ctx + 31) / 32);
+    const int nz = a.ntok > 1 ? a.ntok : 1;
+    cfg.gridDim = dim3(a.kv_heads, (a.ctx + 31) / 32, nz);
     int r = (int)cudaLaunchKernelEx(&cfg, attn_scores_kernel, a);
     if (r) return r;
-    cfg.gridDim = dim3(a.kv_heads, a.dsplit);
+    cfg.gridDim = dim3(a.kv_heads, a.dsplit, nz);
     cfg.dynamicSmemBytes = wbytes + (size_t)vchunk * dw * sizeof(float);
     return (int)cudaLaunchKernelEx(&cfg, attn_softmax_v_kernel, a);
 }
@@ -1573,7 +1577,7 @@ constexpr int kBatchProducer = 256;
 
 __device__ __forceinline__ void mma_s8_16x8x32(int32_t c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -1610,38 +1614,51 @@ __device__ __forceinline__ void batch_chunk(const uint8_t* tile, int cb, int ra,
     const bool va = ta < ntok, vb = tb < ntok;
     if constexpr (QT == NCM_T_Q4_0 || QT == NCM_T_Q8_0) {
         constexpr int BB = QT == NCM_T_Q4_0 ? 18 : 34;
-#pragma unroll 4
-        for (int bl = 0; bl < 16; ++bl) {
-            const int bg = 16 * c + bl;
-            if (bg >= nb) break;
-            uint32_t a0, a1, a2, a3;
-            if constexpr (QT == NCM_T_Q4_0) {
-                const uint32_t wa = ld_u32_a2(rowa + BB * bl + 2 + 4 * t), wb = ld_u32_a2(rowb + BB * bl + 2 + 4 * t);
-                a0 = __vsub4(wa & 0x0f0f0f0fu, 0x08080808u);
-                a2 = __vsub4((wa >> 4) & 0x0f0f0f0fu, 0x08080808u);
-                a1 = __vsub4(wb & 0x0f0f0f0fu, 0x08080808u);
-                a3 = __vsub4((wb >> 4) & 0x0f0f0f0fu, 0x08080808u);
-            } else {
-                a0 = ld_u32_a2(rowa + BB * bl + 2 + 4 * t);
-                a2 = ld_u32_a2(rowa + BB * bl + 18 + 4 * t);
-                a1 = ld_u32_a2(rowb + BB * bl + 2 + 4 * t);
-                a3 = ld_u32_a2(rowb + BB * bl + 18 + 4 * t);
+        // eight blocks at a time: every fragment load, then the eight MMAs, then the
+        // in-order adds, so that loads and MMAs of different blocks overlap
+#pragma unroll 1
+        for (int b0 = 0; b0 < 16; b0 += 8) {
+            if (16 * c + b0 >= nb) break;
+            uint32_t a[8][4], bf[8][2];
+            float da[8], db[8], sa[8], sb[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const int bl = b0 + q, bg = min(16 * c + bl, nb - 1);
+                if constexpr (QT == NCM_T_Q4_0) {
+                    const uint32_t wa = ld_u32_a2(rowa + BB * bl + 2 + 4 * t), wb = ld_u32_a2(rowb + BB * bl + 2 + 4 * t);
+                    a[q][0] = __vsub4(wa & 0x0f0f0f0fu, 0x08080808u);
+                    a[q][2] = __vsub4((wa >> 4) & 0x0f0f0f0fu, 0x08080808u);
+                    a[q][1] = __vsub4(wb & 0x0f0f0f0fu, 0x08080808u);
+                    a[q][3] = __vsub4((wb >> 4) & 0x0f0f0f0fu, 0x08080808u);
+                } else {
+                    a[q][0] = ld_u32_a2(rowa + BB * bl + 2 + 4 * t);
+                    a[q][2] = ld_u32_a2(rowa + BB * bl + 18 + 4 * t);
+                    a[q][1] = ld_u32_a2(rowb + BB * bl + 2 + 4 * t);
+                    a[q][3] = ld_u32_a2(rowb + BB * bl + 18 + 4 * t);
+                }
+                bf[q][0] = tg ? *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 4 * t) : 0u;
+                bf[q][1] = tg ? *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 16 + 4 * t) : 0u;
+                da[q] = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rowa + BB * bl));
+                db[q] = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rowb + BB * bl));
+                sa[q] = va ? xs[ta * nb + bg] : 0.0f;
+                sb[q] = vb ? xs[tb * nb + bg] : 0.0f;
             }
-            uint32_t b0 = 0, b1 = 0;
-            if (tg) {
-                b0 = *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 4 * t);
-                b1 = *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 16 + 4 * t);
+            int32_t d[8][4];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0;
+                mma_s8_16x8x32(d[q], a[q][0], a[q][1], a[q][2], a[q][3], bf[q][0], bf[q][1]);
             }
-            int32_t d4[4] = {0, 0, 0, 0};
-            mma_s8_16x8x32(d4, a0, a1, a2, a3, b0, b1);
-            const float da = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rowa + BB * bl));
-            const float db = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rowb + BB * bl));
-            const float sa = va ? xs[ta * nb + bg] : 0.0f, sb = vb ? xs[tb * nb + bg] : 0.0f;
-            // inference.rs:2663 / 1157: d_w * x_scale * (dot as f32), row sum in block order
-            acc[0] += da * sa * (float)d4[0];
-            acc[1] += da * sb * (float)d4[1];
-            acc[2] += db * sa * (float)d4[2];
-            acc[3] += db * sb * (float)d4[3];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                if (16 * c + b0 + q < nb) {
+                    // inference.rs:2663 / 1157: d_w * x_scale * (dot as f32), row sum in block order
+                    acc[0] += da[q] * sa[q] * (float)d[q][0];
+                    acc[1] += da[q] * sb[q] * (float)d[q][1];
+                    acc[2] += db[q] * sa[q] * (float)d[q][2];
+                    acc[3] += db[q] * sb[q] * (float)d[q][3];
+                }
+            }
         }
     } else {
         // Q4_K: two 256-column super-blocks per chunk; sub-block terms summed from 0 per
@@ -1768,6 +1785,7 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(const __gr
         }
     }
     __syncthreads();
+    const int pos0 = p.pos_dev ? *p.pos_dev : p.pos0;
     float best_v[2] = {-INFINITY, -INFINITY};
     int best_i[2] = {0x7fffffff, 0x7fffffff};
     if (tid == kBatchProducer) {
@@ -1819,14 +1837,14 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(const __gr
                             // inference.rs:904-933 apply_rope_cached at this token's position
                             const int ri = (lr % p.head_dim) >> 1;
                             if (ri < p.rope_half) {
-                                const float2 scs = p.rope[(size_t)(p.pos0 + tk) * p.rope_half + ri];
+                                const float2 scs = p.rope[(size_t)(pos0 + tk) * p.rope_half + ri];
                                 const float x0 = (lr & 1) ? part[i] : v;
                                 const float x1 = (lr & 1) ? v : part[i];
                                 o = (lr & 1) ? (x0 * scs.x + x1 * scs.y) : (x0 * scs.y - x1 * scs.x);
                             }
                         }
                         if (sg.kind == SEG_Q) sg.out[(size_t)tk * p.out_stride + lr] = o;
-                        else ((sg.kind == SEG_K ? p.kcache : p.vcache) + (size_t)(p.pos0 + tk) * p.kv_width)[lr] = o;
+                        else ((sg.kind == SEG_K ? p.kcache : p.vcache) + (size_t)(pos0 + tk) * p.kv_width)[lr] = o;
                     } else if constexpr (EPI == EPI_SILU) {
                         const float gg = v, uu = acc2[i];
                         const float sig = 1.0f / (1.0f + expf_cr(-gg));   // inference.rs:3385-3388
@@ -1897,8 +1915,9 @@ int batch_plan(int qtype, int cols, int rows, bool dual, int ntok, BatchParams& 
     p.chunk_bytes = qtype == NCM_T_Q8_0 ? 16 * 34 : 288;
     p.chunk_words = p.chunk_bytes / 4;
     p.total_rows = rows;
+    // at least 64 rows (four 16-row slabs) per CTA, so that half the compute warps work
     int grid = num_sms();
-    const int maxg = (rows + 15) / 16;
+    const int maxg = (rows + 63) / 64;
     if (grid > maxg) grid = maxg > 0 ? maxg : 1;
     const int per_cta = (rows + grid - 1) / grid;
     int cap = qtype == NCM_T_Q8_0 ? 64 : 128;
@@ -1967,6 +1986,9 @@ int batch_gemv_launch(int qtype, int epi, const BatchParams& p, int grid, cudaSt
 
 // Per token row: optional rms_norm (inference.rs:697-706; layer 0 reads the embedding
 // row's sequential sum of squares) then quantize_f32_to_q8_0 (inference.rs:991-1029).
+// Grid (token, split): every CTA of a token forms the same exact norm scale and
+// quantises its share of the 32-value blocks, four lanes per block.
+constexpr int kPrepSplit = 16;
 __global__ void __launch_bounds__(kThreads) batch_prep_kernel(const float* x, int x_stride, int n, const float* norm_w,
                                                               float eps, const float* ssq_tab, const int* toks,
                                                               int8_t* xq, float* xs) {
@@ -1975,26 +1997,58 @@ __global__ void __launch_bounds__(kThreads) batch_prep_kernel(const float* x, in
     pdl_launch_dependents();
     pdl_wait();
     const int tk = blockIdx.x, tid = threadIdx.x;
-    stage_f32(xr, x + (size_t)tk * x_stride, n, tid, blockDim.x);
-    __syncthreads();
+    const int nblk = n / 32;
+    const int per = (nblk + gridDim.y - 1) / gridDim.y;
+    const int b0 = blockIdx.y * per, b1 = min(nblk, b0 + per);
+    const float* src = x + (size_t)tk * x_stride;
     float scale = 1.0f;
     if (norm_w) {
-        const float tot = ssq_tab ? ssq_tab[toks[tk]]
-                                  : seq_sum_nonneg<kThreads>([&](int i) { float v = xr[i]; return v * v; }, n, sc, tid);
-        scale = 1.0f / sqrtf(tot / (float)n + eps);
+        if (ssq_tab) {
+            scale = 1.0f / sqrtf(ssq_tab[toks[tk]] / (float)n + eps);
+        } else {
+            stage_f32(xr, src, n, tid, blockDim.x);
+            __syncthreads();
+            const float tot = seq_sum_nonneg<kThreads>([&](int i) { float v = xr[i]; return v * v; }, n, sc, tid);
+            scale = 1.0f / sqrtf(tot / (float)n + eps);
+        }
     }
-    for (int b = tid; b < n / 32; b += blockDim.x) {
-        float v[32];
+    const int li = tid & 3;
+    const unsigned qmask = 0xFu << (tid & 28);
+    for (int b = b0 + (tid >> 2); b < b1; b += blockDim.x >> 2) {
+        const int c = li;
+        float v[8];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = norm_w ? xr[32 * b + i] * scale * norm_w[32 * b + i] : xr[32 * b + i];
-        uint32_t w[8];
-        float s = 0.0f;
-        int sum = 0;
-        quant_block32(v, w, s, sum);
-        uint4* dst = reinterpret_cast<uint4*>(xq + (size_t)tk * n + 32 * b);
-        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        xs[(size_t)tk * (n / 32) + b] = s;
+        for (int h = 0; h < 2; ++h) {
+            const float4 x4 = reinterpret_cast<const float4*>(src)[8 * b + 2 * c + h];
+            if (norm_w) {
+                const float4 w4 = reinterpret_cast<const float4*>(norm_w)[8 * b + 2 * c + h];
+                v[4 * h] = x4.x * scale * w4.x;
+                v[4 * h + 1] = x4.y * scale * w4.y;
+                v[4 * h + 2] = x4.z * scale * w4.z;
+                v[4 * h + 3] = x4.w * scale * w4.w;
+            } else {
+                v[4 * h] = x4.x; v[4 * h + 1] = x4.y; v[4 * h + 2] = x4.z; v[4 * h + 3] = x4.w;
+            }
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 2));
+        const float sb = amax / 127.0f;
+        uint32_t w0 = 0, w1 = 0;
+        if (sb > 0.0f) {
+            const float inv = 1.0f / sb;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                float q = roundf(v[i] * inv);
+                q = fminf(fmaxf(q, -127.0f), 127.0f);
+                const uint32_t byte = (uint32_t)((int)q & 0xff) << (8 * (i & 3));
+                if (i < 4) w0 |= byte; else w1 |= byte;
+            }
+        }
+        *reinterpret_cast<uint2*>(xq + (size_t)tk * n + 32 * b + 8 * c) = make_uint2(w0, w1);
+        if (li == 0) xs[(size_t)tk * nblk + b] = sb;
     }
 }
 
@@ -2006,8 +2060,9 @@ int batch_prep_launch(const float* x, int x_stride, int n, int ntok, const float
         configured = true;
     }
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = small_cfg(dim3(ntok), dim3(kThreads), s, pdl, attr);
-    cfg.dynamicSmemBytes = (size_t)n * 4;
+    const int split = std::min(kPrepSplit, std::max(1, n / 32 / 64));
+    cudaLaunchConfig_t cfg = small_cfg(dim3(ntok, split), dim3(kThreads), s, pdl, attr);
+    cfg.dynamicSmemBytes = (norm_w && !ssq_tab) ? (size_t)n * 4 : 0;
     return (int)cudaLaunchKernelEx(&cfg, batch_prep_kernel, x, x_stride, n, norm_w, eps, ssq_tab, toks, xq, xs);
 }
 

@@ -99,6 +99,8 @@ struct AttnParams {
     int heads, kv_heads, hd, kvw, ctx, dsplit;
     int vchunk;              // positions of V staged in shared memory at a time (set by attention_launch)
     float scale;
+    int ntok;                // rows in one launch (grid z): token z at position pos + z, q / out at
+    int tok_stride;          //   + z * tok_stride floats, scores at + z * heads * ctx
 };
 
 // Multi-row (speculative verify) GEMV: ntok activation rows share every weight tile;
@@ -118,7 +120,8 @@ struct alignas(64) BatchParams {
     int out_stride;
     float* hidden;                // EPI_RESID: hidden[t * hidden_stride + row] += sum
     int hidden_stride;
-    int pos0;                     // EPI_QKV: position of token 0 (token t at pos0 + t)
+    int pos0;                     // EPI_QKV: position of token 0 (token t at pos0 + t) ...
+    const int* pos_dev;           // ... or read from device memory when set (graph replay)
     const float2* rope;
     int rope_half, head_dim;
     float* kcache; float* vcache;
