@@ -1029,20 +1029,25 @@ int gemv_plan(int qtype, int cols, int rows, bool dual, int in_mode, GemvParams&
     p.xsum_off = off;
     off += units * 8;
     off = (off + 127) / 128 * 128;
-    // The f32 staging of the input and the term buffers are live at different times.
+    // The f32 staging of the input and the term buffers (one slot per stage) are live
+    // at different times.  The stage count is the largest that fits the budget.
     p.xf_off = off;
     p.t_off = off;
-    int shared_region = kMaxStages * kMaxFold * kTStride * 4;
-    if (in_mode != IN_Q8 && cols * 4 > shared_region) shared_region = cols * 4;
-    off += (shared_region + 127) / 128 * 128;
-    p.nw_off = off;
-    if (in_mode == IN_F32_RMS) off += (cols * 4 + 127) / 128 * 128;
-    p.stage_off = off;
+    const int base = off;
     int ns = kMaxStages;
-    while (ns > 2 && off + ns * p.stage_bytes > kGemvSmemLimit) --ns;
+    for (; ns >= 2; --ns) {
+        int o = base;
+        int shared_region = ns * kMaxFold * kTStride * 4;
+        if (in_mode != IN_Q8 && cols * 4 > shared_region) shared_region = cols * 4;
+        o += (shared_region + 127) / 128 * 128;
+        p.nw_off = o;
+        if (in_mode == IN_F32_RMS) o += (cols * 4 + 127) / 128 * 128;
+        p.stage_off = o;
+        if (o + ns * p.stage_bytes <= kGemvSmemLimit) break;
+    }
+    if (ns < 2) return -1;
     p.nstages = ns;
-    p.smem_bytes = off + ns * p.stage_bytes;
-    if (p.smem_bytes > kGemvSmemLimit) return -1;
+    p.smem_bytes = p.stage_off + ns * p.stage_bytes;
     return grid;
 }
 
