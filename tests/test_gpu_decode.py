@@ -32,6 +32,7 @@ VARIANTS = {
     "q8_0_untied": dict(tied=False, t_embd=8, t_attn=8, t_ffn=8, t_out=8),
     "mixed_q8attn_q4kffn": dict(tied=False, t_embd=8, t_attn=8, t_ffn=12, t_out=8, emb=512, ffn=1024),
     "q4_0_untied_hd128": dict(tied=False, heads=4, kv_heads=1, head_dim=128, emb=512, ffn=768),
+    "q4_0_hd32_mha": dict(heads=8, kv_heads=8, head_dim=32, ffn=2048),
 }
 
 
