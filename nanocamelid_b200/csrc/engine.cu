@@ -217,7 +217,7 @@ static ncm_status setup_buffers(ncm_model* m, const int* shares, int nshards, in
         if (s) return s;
     }
     if (m->heads % m->kv_heads) return fail(NCM_EINVAL, "heads must be a multiple of kv heads");
-    if (m->emb % 256) return fail(NCM_EUNSUPPORTED, "embedding length must be a multiple of 256");
+    if (m->emb % 32) return fail(NCM_EUNSUPPORTED, "embedding length must be a multiple of 32");
     if (m->hd % 32 || m->hd > 256 || m->heads / m->kv_heads > 8)
         return fail(NCM_EUNSUPPORTED, "head_dim must be a multiple of 32 (<= 256), group size <= 8");
     if (nshards > 1) {
@@ -233,7 +233,7 @@ static ncm_status setup_buffers(ncm_model* m, const int* shares, int nshards, in
     m->shard = nshards > 1 ? shard : 0;
     m->world = m->nshards;
     m->rank = m->shard;
-    if ((m->qh * m->hd) % 64 || m->fl % 64) return fail(NCM_EUNSUPPORTED, "shard widths must be multiples of 64");
+    if (m->fl % 32) return fail(NCM_EUNSUPPORTED, "FFN shard width must be a multiple of 32");
     const int qw = m->qh * m->hd, kw = m->kh * m->hd;
     DALLOC(m->hidden, 4 * m->emb);
     DALLOC(m->q, 4 * qw);
@@ -296,8 +296,8 @@ static ncm_status setup_buffers(ncm_model* m, const int* shares, int nshards, in
 
 static ncm_status check_matrix_shape(const DevMat& d, const char* what) {
     if (!gemv_type_ok(d.type)) return fail(NCM_EUNSUPPORTED, std::string(what) + ": tensor type outside Q4_0/Q8_0/Q4_K");
-    if (d.cols % 64 || d.cols % ncm_type_block_elems(d.type)) return fail(NCM_EUNSUPPORTED, std::string(what) + ": columns not block aligned");
-    if (d.cols / 64 > 512) return fail(NCM_EUNSUPPORTED, std::string(what) + ": more than 32768 columns");
+    if (d.cols % 32 || d.cols % ncm_type_block_elems(d.type)) return fail(NCM_EUNSUPPORTED, std::string(what) + ": columns not block aligned");
+    if (d.cols > 32768) return fail(NCM_EUNSUPPORTED, std::string(what) + ": more than 32768 columns");
     return NCM_OK;
 }
 
@@ -1176,9 +1176,9 @@ static ncm_status seam_gemv(int qtype, const void* w, int64_t rows, int cols, co
 extern "C" ncm_status ncm_matmul_quantized(int qtype, const void* w, int64_t rows, int cols, const int8_t* x_i8,
                                           const float* x_scales, float* out, void* stream) {
     if (!gemv_type_ok(qtype)) return fail(NCM_EUNSUPPORTED, "quant type outside Q4_0/Q8_0/Q4_K");
-    if (rows < 0 || rows >= (1ll << 31) || cols <= 0 || cols % 64 || cols % ncm_type_block_elems(qtype) ||
-        cols / 64 > 512)
-        return fail(NCM_EINVAL, "cols must be a positive multiple of 64 (256 for Q4_K), at most 32768");
+    if (rows < 0 || rows >= (1ll << 31) || cols <= 0 || cols % 32 || cols % ncm_type_block_elems(qtype) ||
+        cols > 32768)
+        return fail(NCM_EINVAL, "cols must be a positive multiple of 32 (256 for Q4_K), at most 32768");
     if (rows == 0) return NCM_OK;
     if (!w || !x_i8 || !x_scales || !out) return fail(NCM_EINVAL, "null pointer");
     if (!aligned16(x_i8) || ((uintptr_t)x_scales & 7)) return fail(NCM_EINVAL, "x_i8 must be 16-byte and x_scales 8-byte aligned");
@@ -1224,7 +1224,7 @@ extern "C" ncm_status ncm_matmul_quantized_batch(int qtype, const void* w, int64
 extern "C" ncm_status ncm_block_dots(int qtype, const void* w, int64_t rows, int cols, const int8_t* x_i8,
                                     int32_t* out, void* stream) {
     if (!gemv_type_ok(qtype)) return fail(NCM_EUNSUPPORTED, "quant type outside Q4_0/Q8_0/Q4_K");
-    if (rows < 0 || cols <= 0 || cols % 64 || cols % ncm_type_block_elems(qtype)) return fail(NCM_EINVAL, "bad shape");
+    if (rows < 0 || cols <= 0 || cols % 32 || cols % ncm_type_block_elems(qtype)) return fail(NCM_EINVAL, "bad shape");
     if (rows == 0) return NCM_OK;
     if (!w || !x_i8 || !out) return fail(NCM_EINVAL, "null pointer");
     if (((uintptr_t)x_i8 & 3) || ((uintptr_t)w & 3)) return fail(NCM_EINVAL, "w and x_i8 must be 4-byte aligned");

@@ -221,8 +221,10 @@ static void kv_f32(FILE* f, const char* k, float v) { put_str(f, k); put_u32(f, 
 extern "C" ncm_status ncm_gguf_write_synthetic(const char* path, const ncm_synth_spec* spec, int threads) {
     if (!path || !spec) return NCM_EINVAL;
     const ncm_synth_spec& s = *spec;
-    if (s.emb % 256 || s.ffn % 256 || s.heads <= 0 || s.kv_heads <= 0 || s.heads % s.kv_heads) return NCM_EINVAL;
+    if (s.emb % 32 || s.ffn % 32 || s.heads <= 0 || s.kv_heads <= 0 || s.heads % s.kv_heads) return NCM_EINVAL;
     auto list = synth_tensor_list(s);
+    for (auto& t : list)   // every row is whole blocks of its type (256 columns for Q4_K)
+        if (t.cols % ncm_type_block_elems(t.type)) return NCM_EINVAL;
     FILE* f = fopen(path, "wb");
     if (!f) return NCM_EIO;
     fwrite("GGUF", 1, 4, f);

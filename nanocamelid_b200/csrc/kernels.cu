@@ -534,11 +534,13 @@ __device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, GemvSeqScratch
         for (int g = tid; g < nblk / 2; g += blockDim.x) {
             uint4* dst = reinterpret_cast<uint4*>(smem + p.xq_off + 80 * g);
             if (2 * g < p.nb) {
+                // an odd block count leaves the second block of the last unit empty
+                const bool two = 2 * g + 1 < p.nb;
                 const uint4* src = reinterpret_cast<const uint4*>(p.xq + 64 * g);
                 int s0 = 0, s1 = 0;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    uint4 v = src[i];
+                    uint4 v = (i < 2 || two) ? src[i] : make_uint4(0, 0, 0, 0);
                     dst[i] = v;
                     int a = i < 2 ? s0 : s1;
                     a = __dp4a((int)v.x, 0x01010101, a);
@@ -547,7 +549,7 @@ __device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, GemvSeqScratch
                     a = __dp4a((int)v.w, 0x01010101, a);
                     if (i < 2) s0 = a; else s1 = a;
                 }
-                xs[g] = make_float2(p.xs[2 * g], p.xs[2 * g + 1]);
+                xs[g] = make_float2(p.xs[2 * g], two ? p.xs[2 * g + 1] : 0.0f);
                 xsum[g] = make_int2(s0, s1);
             } else {
 #pragma unroll
@@ -1427,14 +1429,15 @@ int quantize_launch(const float* x, int n, int8_t* xq, float* xs, cudaStream_t s
 // unit code as the GEMV.
 __global__ void block_dots_kernel(int qtype, const uint8_t* w, int64_t rows, int cols, int64_t pitch,
                                   const int8_t* xq, int32_t* out) {
-    const int units = cols / 64;
+    const int nb = cols / 32, units = (nb + 1) / 2;
     int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= rows * units) return;
     int64_t r = idx / units;
     int u = (int)(idx % units);
+    const bool two = 2 * u + 1 < nb;   // the last unit of an odd block count holds one block
     XUnit x;
     const uint32_t* src = reinterpret_cast<const uint32_t*>(xq + 64 * u);
-    for (int i = 0; i < 16; ++i) x.w[i] = src[i];
+    for (int i = 0; i < 16; ++i) x.w[i] = (i < 8 || two) ? src[i] : 0u;
     x.s[0] = x.s[1] = 1.0f;
     for (int h = 0; h < 2; ++h) {
         int s = 0;
@@ -1442,7 +1445,6 @@ __global__ void block_dots_kernel(int qtype, const uint8_t* w, int64_t rows, int
         x.sum[h] = s;
     }
     const uint8_t* row = w + r * pitch;
-    const int nb = cols / 32;
     float t0, t1;
     if (qtype == NCM_T_Q4_K) {
         int ints[4];
@@ -1454,13 +1456,13 @@ __global__ void block_dots_kernel(int qtype, const uint8_t* w, int64_t rows, int
         if (qtype == NCM_T_Q4_0) terms_q4_0(row, u, x, t0, t1, d);
         else terms_q8_0(row, u, x, t0, t1, d);
         out[r * nb + 2 * u] = d[0];
-        out[r * nb + 2 * u + 1] = d[1];
+        if (two) out[r * nb + 2 * u + 1] = d[1];
     }
 }
 int block_dots_launch(int qtype, const uint8_t* w, int64_t rows, int cols, const int8_t* xq, int32_t* out,
                       cudaStream_t s) {
     int64_t pitch = (int64_t)cols / ncm_type_block_elems(qtype) * ncm_type_block_bytes(qtype);
-    int64_t n = rows * (cols / 64);
+    int64_t n = rows * ((cols / 32 + 1) / 2);
     if (n == 0) return 0;
     block_dots_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(qtype, w, rows, cols, pitch, xq, out);
     return (int)cudaGetLastError();

@@ -33,6 +33,9 @@ VARIANTS = {
     "mixed_q8attn_q4kffn": dict(tied=False, t_embd=8, t_attn=8, t_ffn=12, t_out=8, emb=512, ffn=1024),
     "q4_0_untied_hd128": dict(tied=False, heads=4, kv_heads=1, head_dim=128, emb=512, ffn=768),
     "q4_0_hd32_mha": dict(heads=8, kv_heads=8, head_dim=32, ffn=2048),
+    # widths with an odd number of 32-value blocks (emb 288 = 9 blocks, ffn 800 = 25)
+    "q8_0_odd_blocks": dict(tied=False, t_embd=8, t_attn=8, t_ffn=8, t_out=2, heads=9, kv_heads=3,
+                            head_dim=32, emb=288, ffn=800),
 }
 
 

@@ -51,7 +51,7 @@ def test_quantizer_bit_exact(ncm, orc, cuda):
 
 
 @pytest.mark.parametrize("qtype", [2, 8, 12])
-@pytest.mark.parametrize("rows,cols", [(5, 256), (64, 2048), (33, 14336), (9, 28672)])
+@pytest.mark.parametrize("rows,cols", [(5, 256), (64, 2048), (33, 14336), (9, 28672), (7, 96), (3, 32)])
 def test_block_dots_bit_exact(ncm, orc, cuda, qtype, rows, cols):
     torch = cuda
     w = random_blocks(qtype, rows, cols, seed=rows * 7 + qtype)
@@ -65,7 +65,7 @@ def test_block_dots_bit_exact(ncm, orc, cuda, qtype, rows, cols):
     assert np.array_equal(out.cpu().numpy(), ref)
 
 
-SHAPES = [(3, 64), (7, 256), (64, 2048), (2048, 2048), (4097, 3072), (1024, 4096), (512, 8192), (200, 14336),
+SHAPES = [(3, 64), (7, 256), (5, 32), (300, 96), (2049, 160), (64, 2080), (64, 2048), (2048, 2048), (4097, 3072), (1024, 4096), (512, 8192), (200, 14336),
           (96, 28672), (1, 8192)]
 
 

@@ -26,10 +26,12 @@ def random_blocks(qtype, rows, cols, seed):
 
 
 @pytest.mark.parametrize("qtype", [2, 8, 12])
-@pytest.mark.parametrize("rows,cols", [(300, 4096), (37, 512), (2100, 3072), (64, 14336)])
+@pytest.mark.parametrize("rows,cols", [(300, 4096), (37, 512), (2100, 3072), (64, 14336), (45, 96), (130, 288)])
 @pytest.mark.parametrize("ntok", [1, 5, 8])
 def test_batch_rows_bit_equal_single_rows(ncm, orc, cuda, qtype, rows, cols, ntok):
     torch = cuda
+    if cols % BE[qtype]:
+        pytest.skip("Q4_K needs 256-aligned columns")
     w = random_blocks(qtype, rows, cols, seed=rows + cols + qtype)
     x = np.random.default_rng(ntok + rows).standard_normal((ntok, cols)).astype(np.float32)
     qs = [orc.quantize_q8_0(x[t]) for t in range(ntok)]
@@ -63,6 +65,8 @@ VARIANTS = {
     "q4_0_tied": {},
     "mixed_q8attn_q4kffn": dict(tied=False, t_embd=8, t_attn=8, t_ffn=12, t_out=8, emb=512, ffn=1024),
     "q4_0_hd128": dict(tied=False, heads=4, kv_heads=1, head_dim=128, emb=512, ffn=768),
+    "q8_0_odd_blocks": dict(tied=False, t_embd=8, t_attn=8, t_ffn=8, t_out=2, heads=9, kv_heads=3, head_dim=32,
+                            emb=288, ffn=800),
 }
 
 
