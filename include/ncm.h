@@ -57,8 +57,8 @@ ncm_status ncm_matmul_quantized(int qtype, const void* w, int64_t rows, int cols
 /* inference.rs:1246-1303 matmul_quantized_batch(out, x_i8, x_scales, w, shape{batch,rows,cols}, _):
  * ntok activation rows (x_i8[ntok][cols], x_scales[ntok][cols/32]) -> out[ntok][rows],
  * 1 <= ntok <= 8, every row bit-identical to ncm_matmul_quantized of that row.  The
- * block dots run on int8 tensor-core MMA; w and x_i8 16-byte aligned, raw row pitch a
- * multiple of 16 bytes. */
+ * block dots run on int8 tensor-core MMA; x_i8 16-byte aligned; rows whose byte length
+ * is not a multiple of 16 are re-pitched into a scratch first. */
 ncm_status ncm_matmul_quantized_batch(int qtype, const void* w, int64_t rows, int cols, int ntok,
                                       const int8_t* x_i8, const float* x_scales, float* out, void* stream);
 

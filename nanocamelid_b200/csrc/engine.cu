@@ -1194,10 +1194,20 @@ extern "C" ncm_status ncm_matmul_quantized_batch(int qtype, const void* w, int64
     if (rows <= 0 || rows > (1 << 30) || cols <= 0 || cols % ncm_type_block_elems(qtype) || cols % 32)
         return fail(NCM_EINVAL, "bad shape");
     if (!w || !x_i8 || !x_scales || !out) return fail(NCM_EINVAL, "null pointer");
-    if (((uintptr_t)x_i8 & 15) || ((uintptr_t)w & 15) || (cols % 16))
-        return fail(NCM_EINVAL, "w and x_i8 must be 16-byte aligned");
-    const int pitch = row_bytes(qtype, cols);
-    if (pitch % 16) return fail(NCM_EINVAL, "row pitch must be a multiple of 16 bytes");
+    if ((uintptr_t)x_i8 & 15) return fail(NCM_EINVAL, "x_i8 must be 16-byte aligned");
+    // rows whose byte length is not a multiple of 16 (or an unaligned base) are copied
+    // into a 16-byte-pitched scratch so that the TMA engine can address them
+    cudaStream_t st = (cudaStream_t)stream;
+    const int rb = row_bytes(qtype, cols);
+    const uint8_t* base = (const uint8_t*)w;
+    int pitch = rb;
+    uint8_t* tmp = nullptr;
+    if (rb % 16 || !aligned16(w)) {
+        pitch = (rb + 15) / 16 * 16;
+        CK(cudaMallocAsync((void**)&tmp, (size_t)pitch * rows, st));
+        CK(cudaMemcpy2DAsync(tmp, pitch, w, rb, rb, rows, cudaMemcpyDeviceToDevice, st));
+        base = tmp;
+    }
     BatchParams p;
     memset(&p, 0, sizeof p);
     p.nseg = 1;
@@ -1207,16 +1217,18 @@ extern "C" ncm_status ncm_matmul_quantized_batch(int qtype, const void* w, int64
     p.xq = x_i8;
     p.xs = x_scales;
     const int grid = batch_plan(qtype, cols, (int)rows, false, ntok, p);
-    if (grid < 0) return fail(NCM_EUNSUPPORTED, "activation rows do not fit in shared memory");
-    int dev = 0;
-    CK(cudaGetDevice(&dev));
+    if (grid < 0) {
+        if (tmp) cudaFreeAsync(tmp, st);
+        return fail(NCM_EUNSUPPORTED, "activation rows do not fit in shared memory");
+    }
     int* err = nullptr;
-    CK(cudaMallocAsync((void**)&err, 4, (cudaStream_t)stream));
-    CK(cudaMemsetAsync(err, 0, 4, (cudaStream_t)stream));
+    CK(cudaMallocAsync((void**)&err, 4, st));
+    CK(cudaMemsetAsync(err, 0, 4, st));
     p.err = err;
-    int r = gemv_tensor_map(&p.tm[0], w, rows, pitch, p.chunk_words, p.box_rows);
-    if (!r) r = batch_gemv_launch(qtype, EPI_PLAIN, p, grid, (cudaStream_t)stream, false);
-    cudaFreeAsync(err, (cudaStream_t)stream);
+    int r = gemv_tensor_map(&p.tm[0], base, rows, pitch, p.chunk_words, p.box_rows);
+    if (!r) r = batch_gemv_launch(qtype, EPI_PLAIN, p, grid, st, false);
+    cudaFreeAsync(err, st);
+    if (tmp) cudaFreeAsync(tmp, st);
     if (r) return fail(NCM_ECUDA, std::string("batch gemv launch: ") + cudaGetErrorString((cudaError_t)r));
     return NCM_OK;
 }
@@ -1228,7 +1240,22 @@ extern "C" ncm_status ncm_block_dots(int qtype, const void* w, int64_t rows, int
     if (rows == 0) return NCM_OK;
     if (!w || !x_i8 || !out) return fail(NCM_EINVAL, "null pointer");
     if (((uintptr_t)x_i8 & 3) || ((uintptr_t)w & 3)) return fail(NCM_EINVAL, "w and x_i8 must be 4-byte aligned");
-    CKL(block_dots_launch(qtype, (const uint8_t*)w, rows, cols, x_i8, out, (cudaStream_t)stream));
+    // The unit code loads 32-bit words: rows of an odd block count (Q4_0 / Q8_0 rows of
+    // 18 / 34 bytes per block) are re-pitched to 16 bytes first, as in the GEMV seam.
+    cudaStream_t s = (cudaStream_t)stream;
+    const int rb = row_bytes(qtype, cols);
+    const uint8_t* base = (const uint8_t*)w;
+    int64_t pitch = rb;
+    uint8_t* tmp = nullptr;
+    if (rb % 4) {
+        pitch = (rb + 15) / 16 * 16;
+        CK(cudaMallocAsync((void**)&tmp, (size_t)pitch * rows, s));
+        CK(cudaMemcpy2DAsync(tmp, pitch, w, rb, rb, rows, cudaMemcpyDeviceToDevice, s));
+        base = tmp;
+    }
+    const int r = block_dots_launch(qtype, base, rows, cols, pitch, x_i8, out, s);
+    if (tmp) cudaFreeAsync(tmp, s);
+    if (r) return fail(NCM_ECUDA, std::string("block dots launch: ") + cudaGetErrorString((cudaError_t)r));
     return NCM_OK;
 }
 

@@ -1459,9 +1459,8 @@ __global__ void block_dots_kernel(int qtype, const uint8_t* w, int64_t rows, int
         if (two) out[r * nb + 2 * u + 1] = d[1];
     }
 }
-int block_dots_launch(int qtype, const uint8_t* w, int64_t rows, int cols, const int8_t* xq, int32_t* out,
-                      cudaStream_t s) {
-    int64_t pitch = (int64_t)cols / ncm_type_block_elems(qtype) * ncm_type_block_bytes(qtype);
+int block_dots_launch(int qtype, const uint8_t* w, int64_t rows, int cols, int64_t pitch, const int8_t* xq,
+                      int32_t* out, cudaStream_t s) {
     int64_t n = rows * ((cols / 32 + 1) / 2);
     if (n == 0) return 0;
     block_dots_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(qtype, w, rows, cols, pitch, xq, out);

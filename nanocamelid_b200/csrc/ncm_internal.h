@@ -150,8 +150,8 @@ int resid_add_launch(float* hidden, const float* part, int n, cudaStream_t s, bo
 int argmax_merge_launch(const float2* gathered, int world, int* tokens, int* state, int ctx, cudaStream_t s, bool pdl);
 int advance_launch(int* state, cudaStream_t s, bool pdl);
 int quantize_launch(const float* x, int n, int8_t* xq, float* xs, cudaStream_t s);
-int block_dots_launch(int qtype, const uint8_t* w, int64_t rows, int cols, const int8_t* xq, int32_t* out,
-                      cudaStream_t s);
+int block_dots_launch(int qtype, const uint8_t* w, int64_t rows, int cols, int64_t pitch, const int8_t* xq,
+                      int32_t* out, cudaStream_t s);
 int rms_norm_launch(float* out, const float* x, const float* w, int n, float eps, cudaStream_t s);
 int silu_mul_launch(float* out, const float* g, const float* u, int n, cudaStream_t s);
 int synth_launch(int type, uint64_t key, int64_t r0, int64_t nrows, int64_t c0, int64_t ncols, int64_t full_cols,
