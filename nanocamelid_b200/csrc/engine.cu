@@ -1181,7 +1181,7 @@ extern "C" ncm_status ncm_matmul_quantized(int qtype, const void* w, int64_t row
         return fail(NCM_EINVAL, "cols must be a positive multiple of 32 (256 for Q4_K), at most 32768");
     if (rows == 0) return NCM_OK;
     if (!w || !x_i8 || !x_scales || !out) return fail(NCM_EINVAL, "null pointer");
-    if (!aligned16(x_i8) || ((uintptr_t)x_scales & 7)) return fail(NCM_EINVAL, "x_i8 must be 16-byte and x_scales 8-byte aligned");
+    if (!aligned16(x_i8) || ((uintptr_t)x_scales & 3)) return fail(NCM_EINVAL, "x_i8 must be 16-byte and x_scales 4-byte aligned");
     return seam_gemv(qtype, w, rows, cols, x_i8, x_scales, out, (cudaStream_t)stream);
 }
 

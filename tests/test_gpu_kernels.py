@@ -54,6 +54,8 @@ def test_quantizer_bit_exact(ncm, orc, cuda):
 @pytest.mark.parametrize("rows,cols", [(5, 256), (64, 2048), (33, 14336), (9, 28672), (7, 96), (3, 32)])
 def test_block_dots_bit_exact(ncm, orc, cuda, qtype, rows, cols):
     torch = cuda
+    if cols % BE[qtype]:
+        pytest.skip("Q4_K needs 256-aligned columns")
     w = random_blocks(qtype, rows, cols, seed=rows * 7 + qtype)
     x = np.random.default_rng(cols).standard_normal(cols).astype(np.float32)
     xq, xs = orc.quantize_q8_0(x)
