@@ -966,10 +966,42 @@ extern "C" ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok
 
 // speculative.rs:299-494 speculative_decoding_step at temperature 0, repeated: the
 // draft proposes k tokens greedily (its device-resident decode graph), the target
-// verifies them in one multi-row pass, the agreeing prefix is accepted, then the
-// target's own token at the first disagreement (or the trailing token) is emitted and
-// run one token at a time through both models.  The output equals the target's greedy
-// decode.  stats[0] = drafted, stats[1] = accepted.
+// verifies them in one multi-row pass, the agreeing prefix is accepted and the target's
+// own token at the first disagreement (or the trailing token) is emitted.  The output
+// equals the target's greedy decode.  stats[0] = drafted, stats[1] = accepted.
+//
+// The reference runs that last token through both models one token at a time
+// (speculative.rs:421-443, 459-484).  Here it stays pending instead and becomes row 0 of
+// the next verify and the draft's first step: row 0 gives the target prediction the
+// reference takes from its logits, the draft's step gives its first proposal, so every
+// accept decision, token and count is the reference's, and a cycle costs k draft steps
+// plus one (k+1)-row verify.  When every draft was accepted the draft ingests its last
+// proposal (the reference's draft loop already did).  k + 1 > 8 rows falls back to the
+// reference's cycle shape.
+static ncm_status spec_cycle_reference_shape(ncm_model* target, ncm_model* draft, int k, int n_gen, int* out_tokens,
+                                             int* stats, int& n, int& pos, int& tt, int& dt, std::vector<int>& hist) {
+    ncm_status st;
+    if ((st = ncm_decode_steps(draft, k, nullptr))) return st;
+    if ((st = ncm_sync_tokens(draft, hist.data(), pos + k, nullptr))) return st;
+    int drafted[kMaxBatch], rows[kMaxBatch];
+    for (int i = 0; i < k; ++i) drafted[i] = hist[pos + i];
+    if (stats) stats[0] += k;
+    if ((st = ncm_verify_batch(target, drafted, k, pos, rows))) return st;
+    int i = 0, next = tt;
+    while (i < k && drafted[i] == next) {
+        if (n < n_gen) out_tokens[n++] = drafted[i];
+        if (stats) stats[1] += 1;
+        next = rows[i];
+        ++i;
+    }
+    if (n < n_gen) out_tokens[n++] = next;
+    const int at = pos + i;
+    if ((st = ncm_forward_pass(target, next, at, nullptr, &tt))) return st;
+    if ((st = ncm_forward_pass(draft, next, at, nullptr, &dt))) return st;
+    pos = at + 1;
+    return NCM_OK;
+}
+
 extern "C" ncm_status ncm_spec_generate(ncm_model* target, ncm_model* draft, const int* prompt, int n_prompt,
                                        int n_gen, int k, int* out_tokens, int* stats) {
     if (!target || !draft || !prompt || !out_tokens || n_prompt < 1 || n_gen < 0 || k < 1 || k > kMaxBatch)
@@ -977,46 +1009,72 @@ extern "C" ncm_status ncm_spec_generate(ncm_model* target, ncm_model* draft, con
     if (target->vocab != draft->vocab) return fail(NCM_EINVAL, "draft and target vocabularies differ");
     if (n_prompt + n_gen + k + 1 > std::min(target->ctx, draft->ctx))
         return fail(NCM_EINVAL, "prompt + generation + draft window exceeds a context");
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= target->vocab) return fail(NCM_EINVAL, "token id out of range");
     if (stats) stats[0] = stats[1] = 0;
-    ncm_status st = ncm_prefill_tokens(target, prompt, n_prompt, nullptr);
-    if (!st) st = ncm_prefill_tokens(draft, prompt, n_prompt, nullptr);
-    if (st) return st;
-    int tt = 0, dt = 0, pos = n_prompt, n = 0;
-    {
-        int p0 = 0;
+    std::vector<int> hist(std::min(target->ctx, draft->ctx));
+    ncm_status st;
+    int n = 0;
+    if (k + 1 > kMaxBatch) {
+        if ((st = ncm_prefill_tokens(target, prompt, n_prompt, nullptr))) return st;
+        if ((st = ncm_prefill_tokens(draft, prompt, n_prompt, nullptr))) return st;
+        int tt = 0, dt = 0, pos = n_prompt, p0 = 0;
         if ((st = ncm_sync_tokens(target, nullptr, 0, &p0))) return st;
         CK(cudaSetDevice(target->device));
         CK(cudaMemcpy(&tt, target->state + ST_LAST_TOKEN, 4, cudaMemcpyDeviceToHost));
         if ((st = ncm_sync_tokens(draft, nullptr, 0, &p0))) return st;
         CK(cudaSetDevice(draft->device));
         CK(cudaMemcpy(&dt, draft->state + ST_LAST_TOKEN, 4, cudaMemcpyDeviceToHost));
+        while (n < n_gen)
+            if ((st = spec_cycle_reference_shape(target, draft, k, n_gen, out_tokens, stats, n, pos, tt, dt, hist)))
+                return st;
+        return NCM_OK;
     }
-    std::vector<int> hist(std::min(target->ctx, draft->ctx));
+    // all prompt tokens but the last through both models; the last one is pending
+    if (n_prompt > 1) {
+        if ((st = ncm_prefill_tokens(target, prompt, n_prompt - 1, nullptr))) return st;
+        if ((st = ncm_prefill_tokens(draft, prompt, n_prompt - 1, nullptr))) return st;
+    }
+    int cur = prompt[n_prompt - 1], q = n_prompt - 1;   // pending token and its position
     while (n < n_gen) {
-        // draft: k greedy tokens from its current state (token dt at pos)
+        // draft: ingest the pending token at q, then propose d0 .. d(k-1) at q+1 .. q+k
+        CK(cudaSetDevice(draft->device));
+        draft->h_stage[2] = cur;
+        CK(cudaMemcpyAsync(draft->tokens + q, &draft->h_stage[2], 4, cudaMemcpyHostToDevice, draft->stream));
+        if ((st = set_pos(draft, q, q + 1, draft->stream))) return st;
         if ((st = ncm_decode_steps(draft, k, nullptr))) return st;
-        if ((st = ncm_sync_tokens(draft, hist.data(), pos + k, nullptr))) return st;
-        int drafted[kMaxBatch], rows[kMaxBatch];
-        for (int i = 0; i < k; ++i) drafted[i] = hist[pos + i];
+        if ((st = ncm_sync_tokens(draft, hist.data(), q + k + 1, nullptr))) return st;
+        int rows_in[kMaxBatch], g[kMaxBatch];
+        rows_in[0] = cur;
+        for (int i = 0; i < k; ++i) rows_in[i + 1] = hist[q + 1 + i];
         if (stats) stats[0] += k;
-        // target: every drafted token through one multi-row pass
-        if ((st = ncm_verify_batch(target, drafted, k, pos, rows))) return st;
-        int i = 0, next = tt;
-        while (i < k && drafted[i] == next) {
-            if (n < n_gen) out_tokens[n++] = drafted[i];
+        // target: the pending token and every proposal in one (k+1)-row pass; row i
+        // predicts position q+i+1
+        if ((st = ncm_verify_batch(target, rows_in, k + 1, q, g))) return st;
+        int i = 0;
+        while (i < k && rows_in[i + 1] == g[i]) {
+            if (n < n_gen) out_tokens[n++] = rows_in[i + 1];
             if (stats) stats[1] += 1;
-            next = rows[i];
             ++i;
         }
-        // `next`: the target's token after the accepted prefix (the correction, or the
-        // trailing token when all k were accepted); run it through both models
+        const int next = g[i];   // correction, or the trailing token when all k agreed
         if (n < n_gen) out_tokens[n++] = next;
-        const int at = pos + i;
-        if ((st = ncm_forward_pass(target, next, at, nullptr, &tt))) return st;
-        if ((st = ncm_forward_pass(draft, next, at, nullptr, &dt))) return st;
-        pos = at + 1;
+        if (i == k) {
+            // the draft fed d0 .. d(k-2); its cache also needs d(k-1) at q+k
+            CK(cudaSetDevice(draft->device));
+            draft->h_stage[2] = rows_in[k];
+            CK(cudaMemcpyAsync(draft->tokens + q + k, &draft->h_stage[2], 4, cudaMemcpyHostToDevice, draft->stream));
+            if ((st = set_pos(draft, q + k, q + k + 1, draft->stream))) return st;
+            if ((st = ncm_decode_steps(draft, 1, nullptr))) return st;
+            // the pinned staging words are rewritten by the next cycle
+            CK(cudaStreamSynchronize(draft->stream));
+        }
+        cur = next;
+        q += i + 1;
     }
-    return NCM_OK;
+    CK(cudaSetDevice(draft->device));
+    CK(cudaStreamSynchronize(draft->stream));
+    return check_err(draft);
 }
 
 // ------------------------------------------------------------------ tensor parallel

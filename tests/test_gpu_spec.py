@@ -108,8 +108,9 @@ def test_spec_generate_equals_target_greedy(ncm, orc, cuda, tmp_path, k):
     pt, pd = tmp_path / "t.gguf", tmp_path / "d.gguf"
     ncm.write_synthetic_gguf(pt, tsp)
     ncm.write_synthetic_gguf(pd, dsp)
-    ref, _ = orc.spec_generate(orc.OracleModel(pt), orc.OracleModel(pd), prompt, n_gen, k)
+    ref, ref_stats = orc.spec_generate(orc.OracleModel(pt), orc.OracleModel(pd), prompt, n_gen, k)
     assert toks == ref
+    assert (drafted, accepted) == tuple(ref_stats)
 
 
 def test_spec_self_draft_accepts_everything(ncm, cuda):
