@@ -40,6 +40,9 @@ def parse():
     ap.add_argument("--spec", action="store_true",
                     help="BASELINE config 5: greedy speculative decoding, draft = config 1, target = config-3 "
                          "shape all Q4_0, k = 4, 128-token prompt, 256 tokens (one GPU)")
+    ap.add_argument("--verify-only", action="store_true",
+                    help="config 5 target: time the multi-row verify pass (1/4/5/8 rows) and one graphed step")
+    ap.add_argument("--verify-rows", default="1,4,5,8")
     ap.add_argument("--gemv-only", action="store_true",
                     help="only the roofline GEMV (head-shaped Q4_0 matrix): the small case for ncu captures")
     return ap.parse_args()
@@ -308,13 +311,52 @@ def run_spec(args, ncm):
     greedy = ref.generate(prompt, n_gen)
     torch.cuda.synchronize()
     dt_greedy = time.perf_counter() - t0
+    vms, step_ms = verify_times(ncm, target, n_prompt)
     print(json.dumps({"metric": "bs1 speculative decode tok/s", "value": round(n_gen / dt_spec, 2), "unit": "tok/s",
                       "n_gpus": 1, "higher_is_better": True, "data": "synthetic",
                       "config": {"workload": "cfg5: draft cfg1_1b_q4_0, target cfg5_target_q4_0 (8B shape, Q4_0)",
                                  "k": k, "prompt": n_prompt, "tokens": n_gen},
                       "acceptance": round(accepted / max(1, drafted), 4), "drafted": drafted, "accepted": accepted,
                       "target_greedy_tok_s": round(n_gen / dt_greedy, 2), "tokens_equal_greedy": toks == greedy,
+                      "verify_ms_by_rows": vms, "target_step_ms": step_ms,
                       "timing": "wall clock around the call (prefill included), synchronous"}))
+
+
+def verify_times(ncm, target, n_prompt, reps=10, rows=(1, 4, 5, 8)):
+    """Wall time of one synchronous ncm_verify_batch call per row count, and of one
+    graphed single-token step, at position n_prompt (the verify graphs are warm)."""
+    import torch
+    out = {}
+    for ntok in rows:
+        toks = [5 + i for i in range(ntok)]
+        for _ in range(3):
+            target.verify_batch(toks, n_prompt)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            target.verify_batch(toks, n_prompt)
+        out[str(ntok)] = round((time.perf_counter() - t0) / reps * 1e3, 3)
+    for i in range(3):
+        target.forward_pass(7, n_prompt + i)
+    t0 = time.perf_counter()
+    for i in range(reps):
+        target.forward_pass(7, n_prompt + i)
+    return out, round((time.perf_counter() - t0) / reps * 1e3, 3)
+
+
+def run_verify(args, ncm):
+    """The config-5 target's multi-row verify pass alone (a small, repeatable command
+    for launch lists and captures)."""
+    import numpy as np
+    sp = ncm.CONFIGS["cfg5_target_q4_0"]
+    n_prompt = args.prompt
+    prompt = [int(v) for v in np.random.default_rng(0).integers(0, sp.vocab, n_prompt)]
+    target = ncm.Model.synthetic(sp, ctx_limit=n_prompt + 32, device=0)
+    target.generate(prompt, 1)
+    rows = tuple(int(v) for v in args.verify_rows.split(","))
+    vms, step_ms = verify_times(ncm, target, n_prompt, reps=max(1, args.steps), rows=rows)
+    print(json.dumps({"workload": f"cfg5_target_q4_0 verify pass at position {n_prompt}", "verify_ms_by_rows": vms,
+                      "single_step_ms": step_ms, "timing": "wall clock per synchronous call"}))
 
 
 def main():
@@ -324,6 +366,8 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     if args.spec:
         run_spec(args, ncm)
+    elif args.verify_only:
+        run_verify(args, ncm)
     elif args.gemv_only:
         import torch
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
