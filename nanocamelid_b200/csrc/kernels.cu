@@ -1573,13 +1573,20 @@ int peer_timeout_test_launch(TpComm c, int* err, cudaStream_t s) {
 // matmul_quantized_batch: each of ntok <= 8 activation rows against the same weights,
 // every row's result bit-identical to the one-row GEMV (inference.rs:6866-6913).
 // The block dots come from int8 tensor-core MMA (mma.sync m16n8k32 s8): A = 16 weight
-// rows x one 32-column block straight from the raw GGUF bytes in shared memory (Q4_0
-// nibbles - 8, Q8_0 bytes, Q4_K unsigned nibbles), B = the block of 8 token rows.  Lane
-// (g, t) of a warp then holds the exact integer dots of rows g, g+8 and tokens 2t, 2t+1
-// and folds them into its four row sums in block order, with the one-row path's term
-// formulas -- no separate fold stage.
-constexpr int kBatchThreads = 288;   // warps 0-7 compute 16-row slabs, warp 8 produces
-constexpr int kBatchProducer = 256;
+// rows (a slab) x one 32-column block straight from the raw GGUF bytes in shared memory
+// (Q4_0 nibbles - 8, Q8_0 bytes, Q4_K unsigned nibbles), B = the block of 8 token rows.
+// Lane (g, t) of an MMA holds the exact integer dots of slab rows g, g+8 and tokens 2t,
+// 2t+1.  Warp roles per 512-column stage:
+//   warps 0-7  split the stage's slabs x 16 blocks, turn each dot into its f32 term with
+//              the one-row path's formula and store the lane's four terms (float4);
+//   warps 8-9  fold warp f owns slab f: the terms in block order into the four row sums
+//              (same lane layout), then the epilogue;
+//   thread 320 issues the TMA loads.
+// Hand-offs are mbarriers: full (TMA -> compute), empty (compute -> producer), tfull
+// (compute -> fold), tempty (fold -> compute: term slot reusable).
+constexpr int kBatchThreads = 352;
+constexpr int kBatchFoldWarps = 2;
+constexpr int kBatchProducer = 320;
 
 __device__ __forceinline__ void mma_s8_16x8x32(int32_t c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
@@ -1606,12 +1613,13 @@ __device__ __forceinline__ TileCursor batch_tile_at(const BatchParams& p, int cu
     return {s, min(p.box_rows, min(r_end, seg_end) - cur)};
 }
 
-// Folds one 512-column chunk of one matrix (tile rows ra, rb = ra + 8) into acc[4]
-// (acc[0] = (ra, tok 2t), [1] = (ra, 2t+1), [2] = (rb, 2t), [3] = (rb, 2t+1)).
-template <int QT>
-__device__ __forceinline__ void batch_chunk(const uint8_t* tile, int cb, int ra, int g, int t, int c, const uint8_t* xq,
-                                            int xq_pitch, const float* xs, const int* xsum, int nb, int ntok,
-                                            float acc[4]) {
+// Terms of blocks bl0 .. bl0+NB-1 of chunk c for slab rows ra, rb = ra + 8 of one
+// matrix tile.  T points at this lane's float4 of block 0 (block bl at T[32 * bl]):
+// {(ra, tok 2t), (ra, 2t+1), (rb, 2t), (rb, 2t+1)}.
+template <int QT, int NB>
+__device__ __forceinline__ void batch_terms(const uint8_t* tile, int cb, int ra, int g, int t, int c, int bl0,
+                                            const uint8_t* xq, int xq_pitch, const float* xs, const int* xsum,
+                                            int nb, int ntok, float4* T) {
     const uint8_t* rowa = tile + ra * cb;
     const uint8_t* rowb = rowa + 8 * cb;
     const bool tg = g < ntok;
@@ -1620,98 +1628,114 @@ __device__ __forceinline__ void batch_chunk(const uint8_t* tile, int cb, int ra,
     const bool va = ta < ntok, vb = tb < ntok;
     if constexpr (QT == NCM_T_Q4_0 || QT == NCM_T_Q8_0) {
         constexpr int BB = QT == NCM_T_Q4_0 ? 18 : 34;
-        // eight blocks at a time: every fragment load, then the eight MMAs, then the
-        // in-order adds, so that loads and MMAs of different blocks overlap
-#pragma unroll 1
-        for (int b0 = 0; b0 < 16; b0 += 8) {
-            if (16 * c + b0 >= nb) break;
-            uint32_t a[8][4], bf[8][2];
-            float da[8], db[8], sa[8], sb[8];
+        // every fragment load first, then the MMAs, so that loads of different blocks overlap
+        uint32_t a[NB][4], bf[NB][2];
+        float da[NB], db[NB], sa[NB], sb[NB];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const int bl = b0 + q, bg = min(16 * c + bl, nb - 1);
-                if constexpr (QT == NCM_T_Q4_0) {
-                    const uint32_t wa = ld_u32_a2(rowa + BB * bl + 2 + 4 * t), wb = ld_u32_a2(rowb + BB * bl + 2 + 4 * t);
-                    a[q][0] = __vsub4(wa & 0x0f0f0f0fu, 0x08080808u);
-                    a[q][2] = __vsub4((wa >> 4) & 0x0f0f0f0fu, 0x08080808u);
-                    a[q][1] = __vsub4(wb & 0x0f0f0f0fu, 0x08080808u);
-                    a[q][3] = __vsub4((wb >> 4) & 0x0f0f0f0fu, 0x08080808u);
-                } else {
-                    a[q][0] = ld_u32_a2(rowa + BB * bl + 2 + 4 * t);
-                    a[q][2] = ld_u32_a2(rowa + BB * bl + 18 + 4 * t);
-                    a[q][1] = ld_u32_a2(rowb + BB * bl + 2 + 4 * t);
-                    a[q][3] = ld_u32_a2(rowb + BB * bl + 18 + 4 * t);
-                }
-                bf[q][0] = tg ? *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 4 * t) : 0u;
-                bf[q][1] = tg ? *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 16 + 4 * t) : 0u;
-                da[q] = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rowa + BB * bl));
-                db[q] = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rowb + BB * bl));
-                sa[q] = va ? xs[ta * nb + bg] : 0.0f;
-                sb[q] = vb ? xs[tb * nb + bg] : 0.0f;
+        for (int q = 0; q < NB; ++q) {
+            const int bl = bl0 + q, bg = min(16 * c + bl, nb - 1);   // blocks past nb: terms unused
+            if constexpr (QT == NCM_T_Q4_0) {
+                const uint32_t wa = ld_u32_a2(rowa + BB * bl + 2 + 4 * t), wb = ld_u32_a2(rowb + BB * bl + 2 + 4 * t);
+                a[q][0] = __vsub4(wa & 0x0f0f0f0fu, 0x08080808u);
+                a[q][2] = __vsub4((wa >> 4) & 0x0f0f0f0fu, 0x08080808u);
+                a[q][1] = __vsub4(wb & 0x0f0f0f0fu, 0x08080808u);
+                a[q][3] = __vsub4((wb >> 4) & 0x0f0f0f0fu, 0x08080808u);
+            } else {
+                a[q][0] = ld_u32_a2(rowa + BB * bl + 2 + 4 * t);
+                a[q][2] = ld_u32_a2(rowa + BB * bl + 18 + 4 * t);
+                a[q][1] = ld_u32_a2(rowb + BB * bl + 2 + 4 * t);
+                a[q][3] = ld_u32_a2(rowb + BB * bl + 18 + 4 * t);
             }
-            int32_t d[8][4];
+            bf[q][0] = tg ? *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 4 * t) : 0u;
+            bf[q][1] = tg ? *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 16 + 4 * t) : 0u;
+            da[q] = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rowa + BB * bl));
+            db[q] = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rowb + BB * bl));
+            sa[q] = va ? xs[ta * nb + bg] : 0.0f;
+            sb[q] = vb ? xs[tb * nb + bg] : 0.0f;
+        }
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0;
-                mma_s8_16x8x32(d[q], a[q][0], a[q][1], a[q][2], a[q][3], bf[q][0], bf[q][1]);
-            }
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                if (16 * c + b0 + q < nb) {
-                    // inference.rs:2663 / 1157: d_w * x_scale * (dot as f32), row sum in block order
-                    acc[0] += da[q] * sa[q] * (float)d[q][0];
-                    acc[1] += da[q] * sb[q] * (float)d[q][1];
-                    acc[2] += db[q] * sa[q] * (float)d[q][2];
-                    acc[3] += db[q] * sb[q] * (float)d[q][3];
-                }
-            }
+        for (int q = 0; q < NB; ++q) {
+            int32_t d[4] = {0, 0, 0, 0};
+            mma_s8_16x8x32(d, a[q][0], a[q][1], a[q][2], a[q][3], bf[q][0], bf[q][1]);
+            // inference.rs:2663 / 1157: d_w * x_scale * (dot as f32)
+            T[32 * (bl0 + q)] = make_float4(da[q] * sa[q] * (float)d[0], da[q] * sb[q] * (float)d[1],
+                                            db[q] * sa[q] * (float)d[2], db[q] * sb[q] * (float)d[3]);
         }
     } else {
-        // Q4_K: two 256-column super-blocks per chunk; sub-block terms summed from 0 per
-        // super-block (q8.rs:1342), then added to the row sum (inference.rs:3129).
-#pragma unroll 1
-        for (int sbi = 0; sbi < 2; ++sbi) {
-            if (2 * c + sbi >= nb / 8) break;
+        // Q4_K: block bl is sub-block j = bl % 8 of super-block bl / 8 (two per chunk)
+#pragma unroll
+        for (int q = 0; q < NB; ++q) {
+            const int bl = bl0 + q, sbi = bl >> 3, j = bl & 7, pr = j >> 1, h = j & 1;
+            if (2 * c + sbi >= nb / 8) continue;   // chunk tail: the fold skips these terms
+            const int bg = 16 * c + bl;
             const uint8_t* sa_ = rowa + 144 * sbi;
             const uint8_t* sb_ = rowb + 144 * sbi;
             const uint4 ha = *reinterpret_cast<const uint4*>(sa_), hb = *reinterpret_cast<const uint4*>(sb_);
             const float dA = f16_bits_to_f32(ha.x & 0xffff), mA = f16_bits_to_f32(ha.x >> 16);
             const float dB = f16_bits_to_f32(hb.x & 0xffff), mB = f16_bits_to_f32(hb.x >> 16);
-            float ss[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-            for (int pr = 0; pr < 4; ++pr) {
-                const uint32_t wa0 = *reinterpret_cast<const uint32_t*>(sa_ + 16 + 32 * pr + 4 * t);
-                const uint32_t wa1 = *reinterpret_cast<const uint32_t*>(sa_ + 32 + 32 * pr + 4 * t);
-                const uint32_t wb0 = *reinterpret_cast<const uint32_t*>(sb_ + 16 + 32 * pr + 4 * t);
-                const uint32_t wb1 = *reinterpret_cast<const uint32_t*>(sb_ + 32 + 32 * pr + 4 * t);
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int j = 2 * pr + h, bg = 16 * c + 8 * sbi + j;
-                    const uint32_t a0 = (wa0 >> (4 * h)) & 0x0f0f0f0fu, a2 = (wa1 >> (4 * h)) & 0x0f0f0f0fu;
-                    const uint32_t a1 = (wb0 >> (4 * h)) & 0x0f0f0f0fu, a3 = (wb1 >> (4 * h)) & 0x0f0f0f0fu;
-                    uint32_t b0 = 0, b1 = 0;
-                    if (tg) {
-                        b0 = *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 4 * t);
-                        b1 = *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 16 + 4 * t);
-                    }
-                    int32_t d4[4] = {0, 0, 0, 0};
-                    mma_s8_16x8x32(d4, a0, a1, a2, a3, b0, b1);
-                    int scA, mnA, scB, mnB;
-                    q4k_scale_min(j, ha.y, ha.z, ha.w, scA, mnA);
-                    q4k_scale_min(j, hb.y, hb.z, hb.w, scB, mnB);
-                    const float sclA = dA * (float)scA, mnlA = mA * (float)mnA;
-                    const float sclB = dB * (float)scB, mnlB = mB * (float)mnB;
-                    const float sa = va ? xs[ta * nb + bg] : 0.0f, sb = vb ? xs[tb * nb + bg] : 0.0f;
-                    const float xa = va ? (float)xsum[ta * nb + bg] : 0.0f, xb = vb ? (float)xsum[tb * nb + bg] : 0.0f;
-                    // q8.rs:1370-1373: x_scale * (d*sc * sum(q*x) - dmin*m * sum(x))
-                    ss[0] += sa * (sclA * (float)d4[0] - mnlA * xa);
-                    ss[1] += sb * (sclA * (float)d4[1] - mnlA * xb);
-                    ss[2] += sa * (sclB * (float)d4[2] - mnlB * xa);
-                    ss[3] += sb * (sclB * (float)d4[3] - mnlB * xb);
-                }
+            const uint32_t wa0 = *reinterpret_cast<const uint32_t*>(sa_ + 16 + 32 * pr + 4 * t);
+            const uint32_t wa1 = *reinterpret_cast<const uint32_t*>(sa_ + 32 + 32 * pr + 4 * t);
+            const uint32_t wb0 = *reinterpret_cast<const uint32_t*>(sb_ + 16 + 32 * pr + 4 * t);
+            const uint32_t wb1 = *reinterpret_cast<const uint32_t*>(sb_ + 32 + 32 * pr + 4 * t);
+            const uint32_t a0 = (wa0 >> (4 * h)) & 0x0f0f0f0fu, a2 = (wa1 >> (4 * h)) & 0x0f0f0f0fu;
+            const uint32_t a1 = (wb0 >> (4 * h)) & 0x0f0f0f0fu, a3 = (wb1 >> (4 * h)) & 0x0f0f0f0fu;
+            uint32_t b0 = 0, b1 = 0;
+            if (tg) {
+                b0 = *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 4 * t);
+                b1 = *reinterpret_cast<const uint32_t*>(xrow + 32 * bg + 16 + 4 * t);
             }
+            int32_t d4[4] = {0, 0, 0, 0};
+            mma_s8_16x8x32(d4, a0, a1, a2, a3, b0, b1);
+            int scA, mnA, scB, mnB;
+            q4k_scale_min(j, ha.y, ha.z, ha.w, scA, mnA);
+            q4k_scale_min(j, hb.y, hb.z, hb.w, scB, mnB);
+            const float sclA = dA * (float)scA, mnlA = mA * (float)mnA;
+            const float sclB = dB * (float)scB, mnlB = mB * (float)mnB;
+            const float sa = va ? xs[ta * nb + bg] : 0.0f, sb = vb ? xs[tb * nb + bg] : 0.0f;
+            const float xa = va ? (float)xsum[ta * nb + bg] : 0.0f, xb = vb ? (float)xsum[tb * nb + bg] : 0.0f;
+            // q8.rs:1370-1373: x_scale * (d*sc * sum(q*x) - dmin*m * sum(x))
+            T[32 * bl] = make_float4(sa * (sclA * (float)d4[0] - mnlA * xa), sb * (sclA * (float)d4[1] - mnlA * xb),
+                                     sa * (sclB * (float)d4[2] - mnlB * xa), sb * (sclB * (float)d4[3] - mnlB * xb));
+        }
+    }
+}
+
+// Folds one chunk's 16 terms (T as in batch_terms) into acc[4] in block order: Q4_0 /
+// Q8_0 term by term (inference.rs row sum += block result); Q4_K per super-block from 0
+// (q8.rs:1342) and then into the row sum (inference.rs:3129).
+template <int QT>
+__device__ __forceinline__ void batch_fold(const float4* T, int c, int nb, float acc[4]) {
+    float4 tv[16];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) acc[i] += ss[i];
+    for (int j = 0; j < 16; ++j) tv[j] = T[32 * j];
+    asm volatile("" ::: "memory");
+    if constexpr (QT == NCM_T_Q4_K) {
+        const int nsbc = min(2, nb / 8 - 2 * c);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            if (q < nsbc) {
+                float ss[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    ss[0] += tv[8 * q + j].x;
+                    ss[1] += tv[8 * q + j].y;
+                    ss[2] += tv[8 * q + j].z;
+                    ss[3] += tv[8 * q + j].w;
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[i] += ss[i];
+            }
+        }
+    } else {
+        const int nbc = min(16, nb - 16 * c);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if (j < nbc) {
+                acc[0] += tv[j].x;
+                acc[1] += tv[j].y;
+                acc[2] += tv[j].z;
+                acc[3] += tv[j].w;
+            }
         }
     }
 }
@@ -1720,24 +1744,31 @@ template <int QT, int EPI>
 __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(const __grid_constant__ BatchParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr bool DUAL = (EPI == EPI_SILU);
-    __shared__ float wv[8][kMaxBatch];
-    __shared__ int wi[8][kMaxBatch];
+    constexpr int NM = DUAL ? 2 : 1;
+    __shared__ float wv[kBatchFoldWarps][kMaxBatch];
+    __shared__ int wi[kBatchFoldWarps][kMaxBatch];
     __shared__ int s_last;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + 8;
+    uint64_t* tfull = full + 16;
+    uint64_t* tempty = full + 24;
     uint8_t* stages = smem + p.stage_off;
+    float4* tbase = reinterpret_cast<float4*>(smem + p.t_off);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int R = p.total_rows, nbk = gridDim.x;
     const int r_begin = (int)(((long long)blockIdx.x * R / nbk)) & ~1;
     const int r_end = (blockIdx.x + 1 == nbk) ? R : ((int)(((long long)(blockIdx.x + 1) * R / nbk)) & ~1);
     const int box_bytes = p.box_rows * p.chunk_bytes;
     const int box2_off = (box_bytes + 127) & ~127;
-    const int ns = p.nstages;
+    const int ns = p.nstages, S = p.nslab;
+    const int tslot = NM * S * 16 * 32;   // float4 per term slot
     const uint64_t limit_ns = 4000000000ull;
     if (tid == 0) {
         for (int s = 0; s < ns; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 8);
+            mbar_init(&tfull[s], 8);
+            mbar_init(&tempty[s], kBatchFoldWarps);
         }
         fence_mbar_init();
     }
@@ -1797,28 +1828,68 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(const __gr
     if (tid == kBatchProducer) {
         while (icur < r_end) issue();
     } else if (warp < 8) {
+        // compute: warp -> slab warp % S, blocks bl0 .. bl0 + 16 S / 8 - 1 of every stage
         const int g = lane >> 2, t = lane & 3;
-        const int ra = 16 * warp + g, rb = ra + 8;
+        const int sl = warp % S, nbw = 2 * S, bl0 = (warp / S) * nbw;
+        const int ra = 16 * sl + g;
+        int tc_ = 0;
+        for (int cur = r_begin; cur < r_end;) {
+            const int n = batch_tile_at(p, cur, r_end).n;
+            const bool active = 16 * sl < n;
+            for (int c = 0; c < p.nchunk; ++c, ++tc_) {
+                const int s = tc_ % ns;
+                const uint32_t u = (uint32_t)(tc_ / ns);
+                if (!mbar_wait(&full[s], u & 1, limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+                if (u > 0 && !mbar_wait(&tempty[s], (u - 1) & 1, limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+                if (active) {
+                    const uint8_t* tile = stages + (size_t)s * p.stage_bytes;
+                    float4* T = tbase + (size_t)s * tslot + sl * 16 * 32 + lane;
+                    if (nbw == 2)
+                        batch_terms<QT, 2>(tile, p.chunk_bytes, ra, g, t, c, bl0, xq, p.xq_pitch, xs, xsum, p.nb, p.ntok, T);
+                    else
+                        batch_terms<QT, 4>(tile, p.chunk_bytes, ra, g, t, c, bl0, xq, p.xq_pitch, xs, xsum, p.nb, p.ntok, T);
+                    if (DUAL) {
+                        float4* T2 = T + S * 16 * 32;
+                        if (nbw == 2)
+                            batch_terms<QT, 2>(tile + box2_off, p.chunk_bytes, ra, g, t, c, bl0, xq, p.xq_pitch, xs, xsum,
+                                               p.nb, p.ntok, T2);
+                        else
+                            batch_terms<QT, 4>(tile + box2_off, p.chunk_bytes, ra, g, t, c, bl0, xq, p.xq_pitch, xs, xsum,
+                                               p.nb, p.ntok, T2);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&empty[s]);
+                    mbar_arrive(&tfull[s]);
+                }
+            }
+            cur += n;
+        }
+    } else if (warp < 8 + kBatchFoldWarps) {
+        // fold warp f: slab f's rows ra / rb (tile-local) for tokens 2t / 2t+1
+        const int f = warp - 8;
+        const int g = lane >> 2, t = lane & 3;
+        const int ra = 16 * f + g, rb = ra + 8;
         int tc_ = 0;
         for (int cur = r_begin; cur < r_end;) {
             const TileCursor tc = batch_tile_at(p, cur, r_end);
             const int n = tc.n;
-            const bool active = 16 * warp < n;
+            const bool active = f < S && 16 * f < n;
             float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, acc2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             for (int c = 0; c < p.nchunk; ++c, ++tc_) {
                 const int s = tc_ % ns;
-                if (!mbar_wait(&full[s], (uint32_t)((tc_ / ns) & 1), limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+                const uint32_t u = (uint32_t)(tc_ / ns);
+                if (!mbar_wait(&tfull[s], u & 1, limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
                 if (active) {
-                    const uint8_t* tile = stages + (size_t)s * p.stage_bytes;
-                    batch_chunk<QT>(tile, p.chunk_bytes, ra, g, t, c, xq, p.xq_pitch, xs, xsum, p.nb, p.ntok, acc);
-                    if (DUAL)
-                        batch_chunk<QT>(tile + box2_off, p.chunk_bytes, ra, g, t, c, xq, p.xq_pitch, xs, xsum, p.nb,
-                                        p.ntok, acc2);
+                    const float4* T = tbase + (size_t)s * tslot + f * 16 * 32 + lane;
+                    batch_fold<QT>(T, c, p.nb, acc);
+                    if (DUAL) batch_fold<QT>(T + S * 16 * 32, c, p.nb, acc2);
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
+                if (lane == 0) mbar_arrive(&tempty[s]);
             }
-            // tile epilogue: rows ra / rb (tile-local), tokens 2t / 2t+1
+            // tile epilogue
             const Seg& sg = p.seg[tc.seg];
             const int lrow0 = cur - sg.row_begin;
             float part[4];
@@ -1876,8 +1947,8 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(const __gr
                 }
             }
             if (lane < 4) {
-                wv[warp][2 * lane] = best_v[0]; wi[warp][2 * lane] = best_i[0];
-                wv[warp][2 * lane + 1] = best_v[1]; wi[warp][2 * lane + 1] = best_i[1];
+                wv[f][2 * lane] = best_v[0]; wi[f][2 * lane] = best_i[0];
+                wv[f][2 * lane + 1] = best_v[1]; wi[f][2 * lane + 1] = best_i[1];
             }
         }
     }
@@ -1886,7 +1957,7 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(const __gr
         if (tid < p.ntok) {
             float bv = wv[0][tid];
             int bi = wi[0][tid];
-            for (int w = 1; w < 8; ++w)
+            for (int w = 1; w < kBatchFoldWarps; ++w)
                 if (better(wv[w][tid], wi[w][tid], bv, bi)) { bv = wv[w][tid]; bi = wi[w][tid]; }
             p.amax_part[(size_t)blockIdx.x * kMaxBatch + tid] = make_float2(bv, __int_as_float(bi));
         }
@@ -1921,20 +1992,13 @@ int batch_plan(int qtype, int cols, int rows, bool dual, int ntok, BatchParams& 
     p.chunk_bytes = qtype == NCM_T_Q8_0 ? 16 * 34 : 288;
     p.chunk_words = p.chunk_bytes / 4;
     p.total_rows = rows;
-    // at least 64 rows (four 16-row slabs) per CTA, so that half the compute warps work
+    // one CTA per SM while every CTA keeps at least one 16-row slab
     int grid = num_sms();
-    const int maxg = (rows + 63) / 64;
+    const int maxg = (rows + 15) / 16;
     if (grid > maxg) grid = maxg > 0 ? maxg : 1;
     const int per_cta = (rows + grid - 1) / grid;
-    int cap = qtype == NCM_T_Q8_0 ? 64 : 128;
-    if (dual) cap /= 2;
-    int br = (per_cta + 15) & ~15;
-    if (br > cap) br = cap;
-    if (br < 16) br = 16;
-    p.box_rows = br;
-    p.stage_bytes = (br * p.chunk_bytes + 127) / 128 * 128 * (dual ? 2 : 1);
     p.xq_pitch = cols + 16;   // distinct banks for the eight token rows of a fragment
-    int off = 128;
+    int off = 256;            // full / empty / tfull / tempty mbarriers
     p.xq_off = off;
     off += (ntok * p.xq_pitch + 127) / 128 * 128;
     p.xs_off = off;
@@ -1942,12 +2006,23 @@ int batch_plan(int qtype, int cols, int rows, bool dual, int ntok, BatchParams& 
     p.xsum_off = off;
     off += (ntok * p.nb * 4 + 127) / 128 * 128;
     p.stage_off = off;
-    int ns = kMaxStages;
-    while (ns > 2 && off + ns * p.stage_bytes > kBatchSmemLimit) --ns;
-    p.nstages = ns;
-    p.smem_bytes = off + ns * p.stage_bytes;
-    if (p.smem_bytes > kBatchSmemLimit) return -1;
-    return grid;
+    // slabs per tile: two (one per fold warp) unless the CTA's rows or the budget say one
+    for (int S = std::min(dual ? 1 : 2, (per_cta + 15) / 16); S >= 1; --S) {
+        const int br = 16 * S;
+        const int stage_bytes = (br * p.chunk_bytes + 127) / 128 * 128 * (dual ? 2 : 1);
+        const int t_bytes = (dual ? 2 : 1) * S * 16 * 32 * 16;
+        int ns = kMaxStages;
+        while (ns > 2 && off + ns * (stage_bytes + t_bytes) > kBatchSmemLimit) --ns;
+        if (off + ns * (stage_bytes + t_bytes) > kBatchSmemLimit) continue;
+        p.nslab = S;
+        p.box_rows = br;
+        p.stage_bytes = stage_bytes;
+        p.nstages = ns;
+        p.t_off = off + ns * stage_bytes;
+        p.smem_bytes = p.t_off + ns * t_bytes;
+        return grid;
+    }
+    return -1;
 }
 
 template <int QT, int EPI>

@@ -114,6 +114,8 @@ struct alignas(64) BatchParams {
     int nseg, total_rows;
     int cols, nb, nchunk, chunk_words, chunk_bytes, box_rows, stage_bytes, nstages;
     int xq_off, xs_off, xsum_off, stage_off, smem_bytes, xq_pitch;
+    int nslab;                    // 16-row slabs per tile (one fold warp each)
+    int t_off;                    // term ring (one slot per stage)
     int ntok;
     const int8_t* xq;             // [ntok][cols] quantised rows
     const float* xs;              // [ntok][cols / 32]
