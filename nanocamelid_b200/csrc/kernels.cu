@@ -2070,11 +2070,13 @@ int batch_gemv_launch(int qtype, int epi, const BatchParams& p, int grid, cudaSt
 // Grid (token, split): every CTA of a token forms the same exact norm scale and
 // quantises its share of the 32-value blocks, four lanes per block.
 constexpr int kPrepSplit = 16;
-__global__ void __launch_bounds__(kThreads) batch_prep_kernel(const float* x, int x_stride, int n, const float* norm_w,
-                                                              float eps, const float* ssq_tab, const int* toks,
-                                                              int8_t* xq, float* xs) {
+// NT threads: 512 when the CTA folds an RMS sum (short per-thread chunks), else 256.
+template <int NT>
+__global__ void __launch_bounds__(NT) batch_prep_kernel(const float* x, int x_stride, int n, const float* norm_w,
+                                                        float eps, const float* ssq_tab, const int* toks,
+                                                        int8_t* xq, float* xs) {
     extern __shared__ __align__(16) float xr[];
-    __shared__ SeqSumScratch sc;
+    __shared__ SeqSumScratchT<NT> sc;
     pdl_launch_dependents();
     pdl_wait();
     const int tk = blockIdx.x, tid = threadIdx.x;
@@ -2089,7 +2091,7 @@ __global__ void __launch_bounds__(kThreads) batch_prep_kernel(const float* x, in
         } else {
             stage_f32(xr, src, n, tid, blockDim.x);
             __syncthreads();
-            const float tot = seq_sum_nonneg<kThreads>([&](int i) { float v = xr[i]; return v * v; }, n, sc, tid);
+            const float tot = seq_sum_nonneg<NT>([&](int i) { float v = xr[i]; return v * v; }, n, sc, tid);
             scale = 1.0f / sqrtf(tot / (float)n + eps);
         }
     }
@@ -2137,14 +2139,18 @@ int batch_prep_launch(const float* x, int x_stride, int n, int ntok, const float
                       const float* ssq_tab, const int* toks, int8_t* xq, float* xs, cudaStream_t s, bool pdl) {
     static bool configured = false;
     if (!configured) {
-        cudaFuncSetAttribute(batch_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
+        cudaFuncSetAttribute(batch_prep_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
+        cudaFuncSetAttribute(batch_prep_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
         configured = true;
     }
     cudaLaunchAttribute attr[1];
     const int split = std::min(kPrepSplit, std::max(1, n / 32 / 64));
-    cudaLaunchConfig_t cfg = small_cfg(dim3(ntok, split), dim3(kThreads), s, pdl, attr);
-    cfg.dynamicSmemBytes = (norm_w && !ssq_tab) ? (size_t)n * 4 : 0;
-    return (int)cudaLaunchKernelEx(&cfg, batch_prep_kernel, x, x_stride, n, norm_w, eps, ssq_tab, toks, xq, xs);
+    const bool folds = norm_w && !ssq_tab;
+    cudaLaunchConfig_t cfg = small_cfg(dim3(ntok, split), dim3(folds ? 512 : 256), s, pdl, attr);
+    cfg.dynamicSmemBytes = folds ? (size_t)n * 4 : 0;
+    if (folds)
+        return (int)cudaLaunchKernelEx(&cfg, batch_prep_kernel<512>, x, x_stride, n, norm_w, eps, ssq_tab, toks, xq, xs);
+    return (int)cudaLaunchKernelEx(&cfg, batch_prep_kernel<256>, x, x_stride, n, norm_w, eps, ssq_tab, toks, xq, xs);
 }
 
 __global__ void embed_rows_kernel(int type, const uint8_t* table, int64_t pitch, int emb, const int* toks,
