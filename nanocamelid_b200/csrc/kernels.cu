@@ -2007,7 +2007,7 @@ int batch_plan(int qtype, int cols, int rows, bool dual, int ntok, BatchParams& 
     off += (ntok * p.nb * 4 + 127) / 128 * 128;
     p.stage_off = off;
     // slabs per tile: two (one per fold warp) unless the CTA's rows or the budget say one
-    for (int S = std::min(dual ? 1 : 2, (per_cta + 15) / 16); S >= 1; --S) {
+    for (int S = std::min(2, (per_cta + 15) / 16); S >= 1; --S) {
         const int br = 16 * S;
         const int stage_bytes = (br * p.chunk_bytes + 127) / 128 * 128 * (dual ? 2 : 1);
         const int t_bytes = (dual ? 2 : 1) * S * 16 * 32 * 16;
