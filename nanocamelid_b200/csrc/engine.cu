@@ -883,8 +883,9 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s) {
         a.ntok = ntok;
         a.tok_stride = qw;
         CKL(attention_launch(a, s, true));
-        CKL(batch_prep_launch(m->b_att, qw, qw, ntok, nullptr, m->eps, nullptr, nullptr, m->b_xq, m->b_xs, s, true));
         BatchParams o = batch_base(m, ntok);
+        o.xf = m->b_att;
+        o.xf_stride = qw;
         o.nseg = 1;
         o.seg[0] = {nullptr, m->emb, 0, SEG_OUT};
         o.total_rows = m->emb;
@@ -899,9 +900,9 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s) {
         f.total_rows = m->fl;
         f.out_stride = m->fl;
         CKL(launch_batch({&L.w1}, &L.w3, EPI_SILU, f, s));
-        CKL(batch_prep_launch(m->b_act, m->fl, m->fl, ntok, nullptr, m->eps, nullptr, nullptr, m->b_xq, m->b_xs, s,
-                              true));
         BatchParams d = batch_base(m, ntok);
+        d.xf = m->b_act;
+        d.xf_stride = m->fl;
         d.nseg = 1;
         d.seg[0] = {nullptr, m->emb, 0, SEG_OUT};
         d.total_rows = m->emb;

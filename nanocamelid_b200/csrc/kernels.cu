@@ -1798,7 +1798,46 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(const __gr
     uint8_t* xq = smem + p.xq_off;
     float* xs = reinterpret_cast<float*>(smem + p.xs_off);
     int* xsum = reinterpret_cast<int*>(smem + p.xsum_off);
-    {
+    if (p.xf) {
+        // f32 rows: quantize_f32_to_q8_0 (inference.rs:991-1029) here, four lanes per
+        // 32-value block (quad max and sum reductions), every element rounded as in the
+        // one-thread quantiser
+        const int li = tid & 3;
+        const unsigned qmask = 0xFu << (tid & 28);
+        for (int i = tid >> 2; i < p.ntok * p.nb; i += blockDim.x >> 2) {
+            const int tk = i / p.nb, b = i % p.nb;
+            const float4* src = reinterpret_cast<const float4*>(p.xf + (size_t)tk * p.xf_stride) + 8 * b + 2 * li;
+            const float4 x0 = src[0], x1 = src[1];
+            const float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            float amax = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(v[k]));
+            amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 2));
+            const float sb = amax / 127.0f;
+            uint32_t w0 = 0, w1 = 0;
+            int sum = 0;
+            if (sb > 0.0f) {
+                const float inv = 1.0f / sb;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    float q = roundf(v[k] * inv);
+                    q = fminf(fmaxf(q, -127.0f), 127.0f);
+                    const int qi = (int)q;
+                    sum += qi;
+                    const uint32_t byte = (uint32_t)(qi & 0xff) << (8 * (k & 3));
+                    if (k < 4) w0 |= byte; else w1 |= byte;
+                }
+            }
+            sum += __shfl_xor_sync(qmask, sum, 1);
+            sum += __shfl_xor_sync(qmask, sum, 2);
+            *reinterpret_cast<uint2*>(xq + tk * p.xq_pitch + 32 * b + 8 * li) = make_uint2(w0, w1);
+            if (li == 0) {
+                xs[i] = sb;
+                xsum[i] = sum;
+            }
+        }
+    } else {
         const int n16 = p.cols / 16;
         for (int i = tid; i < p.ntok * n16; i += blockDim.x) {
             const int tk = i / n16, k = i % n16;

@@ -119,6 +119,8 @@ struct alignas(64) BatchParams {
     int ntok;
     const int8_t* xq;             // [ntok][cols] quantised rows
     const float* xs;              // [ntok][cols / 32]
+    const float* xf;              // when set: f32 rows [ntok][xf_stride], quantised in the prologue
+    int xf_stride;
     int out_stride;
     float* hidden;                // EPI_RESID: hidden[t * hidden_stride + row] += sum
     int hidden_stride;
