@@ -841,6 +841,10 @@ static int launch_batch(std::initializer_list<const DevMat*> mats, const DevMat*
     return batch_gemv_launch(w0.type, epi, p, grid, s, true);
 }
 
+// Every GEMV CTA quantises the whole f32 input itself when it is small (saves a launch);
+// larger inputs go through one prep launch whose CTAs split the work.
+static bool prologue_quant(int ntok, int cols) { return (int64_t)ntok * cols <= 5 * 4096; }
+
 // The multi-row pass (speculative.rs:381-389 prefill_pass_batch, inference.rs:3695-4111,
 // then compute_logits_from_hidden + sample_logits(_, 0.0) per row) for tokens b_tok at
 // positions *b_pos + t: each weight tile read once for all rows, K/V stored at their
@@ -884,8 +888,12 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s) {
         a.tok_stride = qw;
         CKL(attention_launch(a, s, true));
         BatchParams o = batch_base(m, ntok);
-        o.xf = m->b_att;
-        o.xf_stride = qw;
+        if (prologue_quant(ntok, qw)) {
+            o.xf = m->b_att;
+            o.xf_stride = qw;
+        } else {
+            CKL(batch_prep_launch(m->b_att, qw, qw, ntok, nullptr, m->eps, nullptr, nullptr, m->b_xq, m->b_xs, s, true));
+        }
         o.nseg = 1;
         o.seg[0] = {nullptr, m->emb, 0, SEG_OUT};
         o.total_rows = m->emb;
@@ -901,8 +909,13 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s) {
         f.out_stride = m->fl;
         CKL(launch_batch({&L.w1}, &L.w3, EPI_SILU, f, s));
         BatchParams d = batch_base(m, ntok);
-        d.xf = m->b_act;
-        d.xf_stride = m->fl;
+        if (prologue_quant(ntok, m->fl)) {
+            d.xf = m->b_act;
+            d.xf_stride = m->fl;
+        } else {
+            CKL(batch_prep_launch(m->b_act, m->fl, m->fl, ntok, nullptr, m->eps, nullptr, nullptr, m->b_xq, m->b_xs, s,
+                                  true));
+        }
         d.nseg = 1;
         d.seg[0] = {nullptr, m->emb, 0, SEG_OUT};
         d.total_rows = m->emb;
