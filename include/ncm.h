@@ -198,9 +198,26 @@ ncm_status ncm_spec_generate(ncm_model* target, ncm_model* draft, const int* pro
  * 3) ncm_tp_import: opens every peer's buffers;  mode selects the reducer:
  *    NCM_REDUCE_FUSED_P2P -- partial rows written into every peer's slot by NVLink
  *        stores from the o_proj / down GEMV epilogue, rank-ordered sum on each GPU;
- *    NCM_REDUCE_NCCL -- ncclAllReduce(sum) between GEMV and residual (baseline). */
+ *    NCM_REDUCE_NCCL -- ncclAllReduce(sum) between GEMV and residual (baseline);
+ *    NCM_REDUCE_HOST_CALLBACK -- the reference's `reduce` closure (tp.rs:226-236):
+ *        the partial row goes to a host function registered with
+ *        ncm_tp_set_host_reducer, which leaves the global sum in place (any transport:
+ *        the reference's TCP star, a host collective, a test harness); steps run
+ *        eagerly, synchronously, on the calling thread. */
 #define NCM_REDUCE_FUSED_P2P 0
 #define NCM_REDUCE_NCCL 1
+#define NCM_REDUCE_HOST_CALLBACK 2
+/* Phases passed to the host reducer: tp.rs:203-206 ReducePhase::{Attention, Ffn}
+ * (buf = n = emb floats, this rank's partial; leave the sum over ranks, added in rank
+ * order from 0.0f), and the head merge (buf = 2 floats {logit, token bits} of this
+ * shard's first maximum; leave the merged pair: strict '>' in rank order,
+ * cluster_tp_node.rs:1185-1204).  Return 0, or non-zero for the closure's Err ->
+ * NCM_EPEER from the step. */
+#define NCM_REDUCE_PHASE_ATTENTION 0
+#define NCM_REDUCE_PHASE_FFN 1
+#define NCM_REDUCE_PHASE_HEAD 2
+typedef int (*ncm_host_reduce_fn)(float* buf, int n, int layer, int phase, void* user);
+ncm_status ncm_tp_set_host_reducer(ncm_model* m, ncm_host_reduce_fn fn, void* user);
 #define NCM_TP_HANDLE_BYTES 256
 ncm_status ncm_tp_export(ncm_model* m, uint8_t* handle_out /* NCM_TP_HANDLE_BYTES */);
 ncm_status ncm_tp_import(ncm_model* m, const uint8_t* handles /* world x NCM_TP_HANDLE_BYTES */, int world,

@@ -18,7 +18,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libncm.so")
 
 Q4_0, Q8_0, Q4_K, F32, F16 = 2, 8, 12, 0, 1
-REDUCE_FUSED_P2P, REDUCE_NCCL = 0, 1
+REDUCE_FUSED_P2P, REDUCE_NCCL, REDUCE_HOST_CALLBACK = 0, 1, 2
+PHASE_ATTENTION, PHASE_FFN, PHASE_HEAD = 0, 1, 2   # tp.rs:203-206 ReducePhase, + the head merge
+HOST_REDUCE_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.POINTER(ctypes.c_float), ctypes.c_int, ctypes.c_int,
+                                  ctypes.c_int, ctypes.c_void_p)
 TP_HANDLE_BYTES = 256
 
 STATUS = {0: "OK", 1: "EINVAL", 2: "ECUDA", 3: "ETIMEOUT", 4: "EPEER", 5: "EIO", 6: "EUNSUPPORTED"}
@@ -116,6 +119,7 @@ def lib():
         "ncm_nccl_unique_id": (c_int, [pu8]),
         "ncm_tp_nccl_init": (c_int, [c_p, pu8, c_int, c_int]),
         "ncm_tp_set_reducer": (c_int, [c_p, c_int]),
+        "ncm_tp_set_host_reducer": (c_int, [c_p, HOST_REDUCE_FN, c_p]),
         "ncm_tp_set_timeout_ns": (c_int, [c_p, c_u64]),
         "ncm_verify_batch": (c_int, [c_p, pint, c_int, c_int, pint]),
         "ncm_spec_generate": (c_int, [c_p, c_p, pint, c_int, c_int, c_int, pint, pint]),
@@ -330,6 +334,24 @@ class Model:
 
     def tp_set_reducer(self, mode):
         _ck(lib().ncm_tp_set_reducer(self._h, mode))
+
+    def tp_set_host_reducer(self, fn):
+        """Registers fn(buf, layer, phase) -> int (0 = ok) as this rank's reduce closure
+        (tp.rs:226-236).  buf is a float32 numpy view of the partial row (PHASE_ATTENTION /
+        PHASE_FFN) or of {logit, token bits} (PHASE_HEAD); fn leaves the global value in
+        it.  Then tp_set_reducer(REDUCE_HOST_CALLBACK)."""
+        import numpy as np
+
+        def tramp(ptr, n, layer, phase, _user):
+            try:
+                buf = np.ctypeslib.as_array(ptr, shape=(n,))
+                rc = fn(buf, layer, phase)
+                return int(rc or 0)
+            except Exception:   # an exception is the closure's Err
+                return -1
+
+        self._host_reducer = HOST_REDUCE_FN(tramp)   # kept alive with the model
+        _ck(lib().ncm_tp_set_host_reducer(self._h, self._host_reducer, None))
 
     def tp_set_timeout_ns(self, ns):
         _ck(lib().ncm_tp_set_timeout_ns(self._h, int(ns)))

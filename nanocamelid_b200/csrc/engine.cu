@@ -120,6 +120,9 @@ struct ncm_model {
     std::vector<void*> ipc_open;
     nccl_comm nccl = nullptr;
     uint64_t timeout_ns = 10000000000ull;
+    ncm_host_reduce_fn host_fn = nullptr;   // NCM_REDUCE_HOST_CALLBACK
+    void* host_user = nullptr;
+    float* h_red = nullptr;                 // pinned: the partial row / head pair handed to host_fn
 };
 
 static ncm_status dalloc(ncm_model* m, void** p, size_t bytes) {
@@ -149,6 +152,7 @@ static void free_model(ncm_model* m) {
     if (m->nccl && g_nccl.CommDestroy) g_nccl.CommDestroy(m->nccl);
     for (void* p : m->allocs) cudaFree(p);
     if (m->h_stage) cudaFreeHost(m->h_stage);
+    if (m->h_red) cudaFreeHost(m->h_red);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
 }
@@ -541,9 +545,28 @@ static int launch_gemv(std::initializer_list<const DevMat*> mats, const DevMat* 
     return gemv_launch(w0.type, in_mode, epi, p, grid, s, true);
 }
 
+static ncm_status check_err(ncm_model* m);
+static bool host_mode(const ncm_model* m) { return m->world > 1 && m->reduce_mode == NCM_REDUCE_HOST_CALLBACK; }
+
+// The reference's reduce closure (tp.rs:226-236): n floats of `dev` go to the host
+// function, which leaves the global value in place; a non-zero return is the closure's
+// Err.  Runs eagerly on the calling thread (synchronous).
+static ncm_status host_reduce(ncm_model* m, void* dev, int n, int layer, int phase, cudaStream_t s) {
+    CK(cudaMemcpyAsync(m->h_red, dev, 4 * (size_t)n, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    ncm_status st = check_err(m);
+    if (st) return st;
+    const int rc = m->host_fn(m->h_red, n, layer, phase, m->host_user);
+    if (rc != 0)
+        return fail(NCM_EPEER, "host reducer returned " + std::to_string(rc) + " at layer " + std::to_string(layer) +
+                                   ", phase " + std::to_string(phase));
+    CK(cudaMemcpyAsync(dev, m->h_red, 4 * (size_t)n, cudaMemcpyHostToDevice, s));
+    return NCM_OK;
+}
+
 // Row-parallel projection (wo / w2) with its reduction: one GPU -> hidden += out;
 // fused P2P -> NVLink stores + rank-ordered sum in the epilogue; NCCL -> partial,
-// ncclAllReduce, residual add.
+// ncclAllReduce, residual add; host callback -> partial, host_fn, residual add.
 static ncm_status row_parallel(ncm_model* m, const DevMat& w, const float* x, int slot, cudaStream_t s) {
     GemvParams p = base_params(m);
     p.nseg = 1;
@@ -558,6 +581,12 @@ static ncm_status row_parallel(ncm_model* m, const DevMat& w, const float* x, in
         p.tp = m->comm;
         p.tp_slot = slot;
         CKL(launch_gemv({&w}, nullptr, IN_F32, EPI_TP_RESID, p, s));
+    } else if (m->reduce_mode == NCM_REDUCE_HOST_CALLBACK) {
+        p.seg[0] = {m->part, m->emb, 0, SEG_OUT};
+        CKL(launch_gemv({&w}, nullptr, IN_F32, EPI_PLAIN, p, s));
+        ncm_status st = host_reduce(m, m->part, m->emb, slot / 2, slot % 2, s);
+        if (st) return st;
+        CKL(resid_add_launch(m->hidden, m->part, m->emb, s, true));
     } else {
         p.seg[0] = {m->part, m->emb, 0, SEG_OUT};
         CKL(launch_gemv({&w}, nullptr, IN_F32, EPI_PLAIN, p, s));
@@ -635,9 +664,15 @@ static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
     h.counter = m->amax_cnt;
     h.head_row0 = m->h0;
     if (m->world > 1 && m->reduce_mode == NCM_REDUCE_FUSED_P2P) h.tp = m->comm;
-    if (m->world > 1 && m->reduce_mode == NCM_REDUCE_NCCL) h.head_out = m->head_out;
+    if (m->world > 1 && m->reduce_mode != NCM_REDUCE_FUSED_P2P) h.head_out = m->head_out;
     CKL(launch_gemv({&m->head}, nullptr, IN_F32_RMS, EPI_ARGMAX, h, s));
-    if (h.head_out) {
+    if (h.head_out && host_mode(m)) {
+        // this shard's (logit, token); the host merges every shard's pair (strict '>' in
+        // rank order, cluster_tp_node.rs:1185-1204) and the merged pair advances the state
+        ncm_status st = host_reduce(m, m->head_out, 2, m->layers, NCM_REDUCE_PHASE_HEAD, s);
+        if (st) return st;
+        CKL(argmax_merge_launch(m->head_out, 1, m->tokens, m->state, m->ctx, s, true));
+    } else if (h.head_out) {
         int r = g_nccl.AllGather(m->head_out, m->gather, 2, kNcclFloat, m->nccl, s);
         if (r != 0) return fail(NCM_EPEER, "ncclAllGather failed");
         CKL(argmax_merge_launch(m->gather, m->world, m->tokens, m->state, m->ctx, s, true));
@@ -663,6 +698,7 @@ static ncm_status capture(ncm_model* m, bool with_head, cudaGraphExec_t* exec) {
 
 static ncm_status ensure_graphs(ncm_model* m) {
     if (m->world > 1 && !m->tp_ready) return fail(NCM_EINVAL, "tensor-parallel peers not set up (ncm_tp_import / ncm_tp_nccl_init)");
+    if (host_mode(m)) return NCM_OK;   // eager steps: the host reducer runs between kernels
     if (!m->dirty && m->g_full) return NCM_OK;
     if (m->g_full) { cudaGraphExecDestroy(m->g_full); m->g_full = nullptr; }
     if (m->g_nohead) { cudaGraphExecDestroy(m->g_nohead); m->g_nohead = nullptr; }
@@ -685,6 +721,13 @@ static ncm_status check_err(ncm_model* m) {
     return NCM_OK;
 }
 
+// One decode step: the captured graph, or eagerly when a host reducer takes part.
+static ncm_status run_step(ncm_model* m, bool with_head, cudaStream_t s) {
+    if (host_mode(m)) return enqueue_step(m, with_head, s);
+    CK(cudaGraphLaunch(with_head ? m->g_full : m->g_nohead, s));
+    return NCM_OK;
+}
+
 static ncm_status set_pos(ncm_model* m, int pos, int nprompt, cudaStream_t s) {
     m->h_stage[0] = pos;
     m->h_stage[1] = nprompt;
@@ -704,9 +747,9 @@ extern "C" ncm_status ncm_prefill_tokens(ncm_model* m, const int* prompt, int n_
     CK(cudaStreamSynchronize(st));
     CK(cudaMemcpyAsync(m->tokens, prompt, 4 * (size_t)n_prompt, cudaMemcpyHostToDevice, st));
     if ((s = set_pos(m, 0, n_prompt, st))) return s;
-    for (int i = 0; i + 1 < n_prompt; ++i) CK(cudaGraphLaunch(m->g_nohead, st));
-    CK(cudaGraphLaunch(m->g_full, st));
-    return NCM_OK;
+    for (int i = 0; i + 1 < n_prompt; ++i)
+        if ((s = run_step(m, false, st))) return s;
+    return run_step(m, true, st);
 }
 
 extern "C" ncm_status ncm_decode_steps(ncm_model* m, int n, void* stream) {
@@ -715,7 +758,8 @@ extern "C" ncm_status ncm_decode_steps(ncm_model* m, int n, void* stream) {
     ncm_status s = ensure_graphs(m);
     if (s) return s;
     cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
-    for (int i = 0; i < n; ++i) CK(cudaGraphLaunch(m->g_full, st));
+    for (int i = 0; i < n; ++i)
+        if ((s = run_step(m, true, st))) return s;
     return NCM_OK;
 }
 
@@ -751,7 +795,7 @@ extern "C" ncm_status ncm_forward_pass(ncm_model* m, int token, int pos, float* 
     m->h_stage[2] = token;
     CK(cudaMemcpyAsync(m->tokens + pos, &m->h_stage[2], 4, cudaMemcpyHostToDevice, st));
     if ((s = set_pos(m, pos, pos + 1, st))) return s;
-    CK(cudaGraphLaunch(m->g_full, st));
+    if ((s = run_step(m, true, st))) return s;
     CK(cudaMemcpyAsync(&m->h_stage[3], m->state + ST_LAST_TOKEN, 4, cudaMemcpyDeviceToHost, st));
     if (logits) CK(cudaMemcpyAsync(logits, m->logits, 4 * (size_t)m->hr, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
@@ -1164,11 +1208,26 @@ extern "C" ncm_status ncm_tp_nccl_init(ncm_model* m, const uint8_t* unique_id, i
 
 extern "C" ncm_status ncm_tp_set_reducer(ncm_model* m, int mode) {
     if (!m) return fail(NCM_EINVAL, "null model");
-    if (mode != NCM_REDUCE_FUSED_P2P && mode != NCM_REDUCE_NCCL) return fail(NCM_EINVAL, "unknown reducer");
+    if (mode != NCM_REDUCE_FUSED_P2P && mode != NCM_REDUCE_NCCL && mode != NCM_REDUCE_HOST_CALLBACK)
+        return fail(NCM_EINVAL, "unknown reducer");
     if (mode == NCM_REDUCE_NCCL && m->world > 1 && !m->nccl) return fail(NCM_EINVAL, "NCCL communicator not initialised");
+    if (mode == NCM_REDUCE_HOST_CALLBACK && !m->host_fn) return fail(NCM_EINVAL, "no host reducer registered");
     m->reduce_mode = mode;
     m->dirty = true;
-    if (m->world > 1) m->tp_ready = (mode == NCM_REDUCE_NCCL) ? (m->nccl != nullptr) : (m->comm.world == m->world);
+    if (m->world > 1)
+        m->tp_ready = mode == NCM_REDUCE_NCCL ? m->nccl != nullptr
+                      : mode == NCM_REDUCE_HOST_CALLBACK ? true
+                                                          : m->comm.world == m->world;
+    return NCM_OK;
+}
+
+extern "C" ncm_status ncm_tp_set_host_reducer(ncm_model* m, ncm_host_reduce_fn fn, void* user) {
+    if (!m || !fn) return fail(NCM_EINVAL, "null argument");
+    CK(cudaSetDevice(m->device));
+    CK(cudaStreamSynchronize(m->stream));
+    if (!m->h_red) CK(cudaMallocHost((void**)&m->h_red, 4 * (size_t)std::max(m->emb, 2)));
+    m->host_fn = fn;
+    m->host_user = user;
     return NCM_OK;
 }
 

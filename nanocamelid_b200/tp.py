@@ -9,7 +9,8 @@ For the NCCL baseline reducer, rank 0's ncclUniqueId is broadcast the same way.
 """
 import torch.distributed as dist
 
-from . import REDUCE_FUSED_P2P, REDUCE_NCCL, Model, nccl_unique_id, shard_geometry
+from . import (PHASE_HEAD, REDUCE_FUSED_P2P, REDUCE_HOST_CALLBACK, REDUCE_NCCL, Model, nccl_unique_id,
+               shard_geometry)
 
 
 def even_shares(kv_heads, world):
@@ -41,9 +42,49 @@ def check_plan(spec_, shares, world, rank, group=None):
     return plans
 
 
+def rank_ordered(parts, phase):
+    """The global value from every rank's buffer, in rank order: the f32 sum from 0.0f
+    (tp.rs:349-363, the master's fixed-order sum in cluster_tp_node.rs:1154-1180), or for
+    the head the first maximum by strict '>' (cluster_tp_node.rs:1185-1204; the token
+    slot is copied, never computed on)."""
+    import numpy as np
+    if phase == PHASE_HEAD:
+        best = parts[0]
+        for p in parts[1:]:
+            if p[0] > best[0]:
+                best = p
+        return np.array(best, dtype=np.float32, copy=True)
+    acc = np.zeros(len(parts[0]), dtype=np.float32)
+    for p in parts:
+        acc = acc + p
+    return acc
+
+
+def host_reducer(world, group=None):
+    """A reduce closure (tp.rs:226-236) over a torch.distributed group of CPU ranks
+    (gloo or any backend): all-gathers this rank's buffer and leaves rank_ordered() of
+    all of them in place.  For Model.tp_set_host_reducer."""
+    import numpy as np
+    import torch
+
+    def fn(buf, layer, phase):
+        mine = torch.from_numpy(np.array(buf, dtype=np.float32, copy=True))
+        outs = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(outs, mine, group=group)
+        buf[:] = rank_ordered([o.numpy() for o in outs], phase)
+        return 0
+
+    return fn
+
+
 def connect(model: Model, rank, world, reducer=REDUCE_FUSED_P2P, group=None):
-    """Exchanges peer handles (and an NCCL id for the baseline) and selects the reducer."""
+    """Exchanges peer handles (and an NCCL id for the baseline) and selects the reducer.
+    REDUCE_HOST_CALLBACK uses host_reducer over `group` (no device buffers are shared)."""
     if world <= 1:
+        return
+    if reducer == REDUCE_HOST_CALLBACK:
+        model.tp_set_host_reducer(host_reducer(world, group))
+        model.tp_set_reducer(reducer)
         return
     handles = exchange(model.tp_export(), world, group)
     model.tp_import(handles, world, rank)

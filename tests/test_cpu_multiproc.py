@@ -67,3 +67,41 @@ def test_two_rank_plan_mismatch_is_rejected(tmp_path):
     mp.spawn(_bad_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
     for r in range(2):
         assert open(tmp_path / f"r{r}").read().startswith("rejected"), r
+
+
+def _reducer_worker(rank, world, port, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import numpy as np
+        import nanocamelid_b200 as ncm
+        from nanocamelid_b200 import tp
+        fn = tp.host_reducer(world)
+        rng = np.random.default_rng(rank)
+        part = (rng.standard_normal(300) * 10.0 ** rng.integers(-3, 3, 300)).astype(np.float32)
+        buf = part.copy()
+        assert fn(buf, 3, ncm.PHASE_FFN) == 0
+        np.save(os.path.join(result_dir, f"p{rank}.npy"), part)
+        np.save(os.path.join(result_dir, f"s{rank}.npy"), buf)
+        # head pairs: equal logits on both ranks -> rank 0's token (strict '>')
+        tok = np.array([0.0, 0.0], dtype=np.float32)
+        tok.view(np.int32)[1] = 1000 + rank
+        tok[0] = 2.5
+        assert fn(tok, 3, ncm.PHASE_HEAD) == 0
+        np.save(os.path.join(result_dir, f"h{rank}.npy"), tok)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_host_reducer_rank_ordered_sum_and_head_merge(tmp_path):
+    """tp.host_reducer over gloo: both ranks hold ((0 + p0) + p1) in f32 and the same
+    merged head pair (rank 0 wins a tie)."""
+    import numpy as np
+    mp.spawn(_reducer_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    p = [np.load(tmp_path / f"p{r}.npy") for r in range(2)]
+    want = (np.float32(0.0) + p[0]).astype(np.float32) + p[1]
+    for r in range(2):
+        got = np.load(tmp_path / f"s{r}.npy")
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), r
+        h = np.load(tmp_path / f"h{r}.npy")
+        assert h[0] == 2.5 and h.view(np.int32)[1] == 1000, r

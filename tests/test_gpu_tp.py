@@ -1,4 +1,4 @@
-"""Tensor parallel on 2+ GPUs (one process per GPU).
+"""Tensor parallel on 2+ GPUs (one process per GPU), and the host-callback reducer.
 
 The reference's TP path (tp.rs:226-428 with the fixed-order reducer,
 cluster_tp_node.rs:1154-1180) is restated by the oracle's TP (OracleTP).  The fused NVLink
@@ -12,13 +12,14 @@ memory stays mapped) and only skips the step."""
 import json
 import os
 import socket
+import threading
 
 import numpy as np
 import pytest
 
 from conftest import TINY
 
-pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+pytestmark = [pytest.mark.gpu]
 
 
 def _free_port():
@@ -48,7 +49,8 @@ def _worker(rank, world, port, path, shares, reducer, prompt, n_gen, out_dir):
         import nanocamelid_b200 as ncm
         from nanocamelid_b200 import tp
         m = ncm.Model.load(path, device=rank, shares=shares, shard=rank)
-        tp.connect(m, rank, world, ncm.REDUCE_NCCL if reducer == "nccl" else ncm.REDUCE_FUSED_P2P)
+        mode = {"p2p": ncm.REDUCE_FUSED_P2P, "nccl": ncm.REDUCE_NCCL, "host": ncm.REDUCE_HOST_CALLBACK}[reducer]
+        tp.connect(m, rank, world, mode)
         lgs = [m.forward_pass(t, pos, want_logits=True)[1] for pos, t in enumerate(prompt)]
         np.save(os.path.join(out_dir, f"lg{rank}.npy"), np.stack(lgs))
         m.reset()
@@ -60,7 +62,8 @@ def _worker(rank, world, port, path, shares, reducer, prompt, n_gen, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("reducer", ["p2p", "nccl"])
+@pytest.mark.multigpu
+@pytest.mark.parametrize("reducer", ["p2p", "nccl", "host"])
 @pytest.mark.parametrize("kvh,heads,shares", [(2, 4, [1, 1]), (4, 4, [1, 3]), (8, 8, [4, 4]), (8, 8, [2, 3, 3])])
 def test_tp_decode_matches_oracle_tp(ncm, orc, tmp_path, reducer, kvh, heads, shares):
     world = len(shares)
@@ -82,7 +85,7 @@ def test_tp_decode_matches_oracle_tp(ncm, orc, tmp_path, reducer, kvh, heads, sh
     assert lg.shape == ref_lg.shape
     gap = float(np.max(np.abs(lg - ref_lg))) / float(np.max(np.abs(ref_lg)))
     assert all(t == toks[0] for t in toks), toks
-    if reducer == "p2p":
+    if reducer in ("p2p", "host"):   # both sum in rank order from 0.0f
         assert toks[0] == ref_tokens and gap <= 1e-5, (toks[0], ref_tokens, gap)
     else:
         assert gap <= 1e-3, gap
@@ -114,6 +117,7 @@ def _silent_worker(rank, world, port, path, out_dir):
         dist.destroy_process_group()
 
 
+@pytest.mark.multigpu
 def test_tp_missing_rank_times_out(ncm, tmp_path):
     if _ngpus() < 2:
         pytest.skip("needs 2 GPUs")
@@ -124,3 +128,88 @@ def test_tp_missing_rank_times_out(ncm, tmp_path):
     mp.spawn(_silent_worker, args=(2, _free_port(), path, str(tmp_path)), nprocs=2, join=True)
     r0 = json.load(open(tmp_path / "s0.json"))["result"]
     assert r0.startswith("error") and "TIMEOUT" in r0.upper(), r0
+
+
+def _thread_reducers(world, fail_at=None):
+    """One reduce closure per shard for shards driven by threads of one process: each
+    publishes its buffer, waits for the others, and takes the rank-ordered value
+    (tp.rank_ordered).  fail_at = (layer, phase): every closure returns an error there."""
+    from nanocamelid_b200 import tp
+    slots = [None] * world
+    bar = threading.Barrier(world)
+
+    def make(rank):
+        def fn(buf, layer, phase):
+            if fail_at == (layer, phase):
+                return 7
+            slots[rank] = buf.copy()
+            bar.wait(timeout=30)
+            out = tp.rank_ordered(slots, phase)
+            bar.wait(timeout=30)   # every shard has read the slots before they are reused
+            buf[:] = out
+            return 0
+        return fn
+    return [make(r) for r in range(world)]
+
+
+def _run_shards(models, fn):
+    res = [None] * len(models)
+
+    def go(r):
+        try:
+            res[r] = fn(r, models[r])
+        except Exception as e:   # reported to the test thread
+            res[r] = e
+    th = [threading.Thread(target=go, args=(r,)) for r in range(len(models))]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join(timeout=300)
+    return res
+
+
+def test_tp_host_callback_reducer_on_one_gpu(ncm, orc, cuda, tmp_path):
+    """NCM_REDUCE_HOST_CALLBACK (the reference's reduce closure, tp.rs:226-236): two
+    shards of one model on one GPU, driven by two threads, reduced on the host; greedy
+    tokens equal the oracle's TP restatement and the logits agree to 1e-5.  Then every
+    closure fails at layer 1 (tp.rs's Err path): each step returns NCM_EPEER, and the
+    same models decode correctly afterwards."""
+    sp = _spec(ncm, 2, 4)
+    path = str(tmp_path / "m.gguf")
+    ncm.write_synthetic_gguf(path, sp)
+    shares = [1, 1]
+    prompt = [int(v) for v in np.random.default_rng(2).integers(0, sp.vocab, size=6)]
+    n_gen = 16
+    ref_tokens = orc.OracleTP(orc.OracleModel(path), shares).generate(prompt, n_gen)
+    rtp = orc.OracleTP(orc.OracleModel(path), shares)
+    ref_lg = np.stack([rtp.forward_pass(t, pos, want_logits=True)[1] for pos, t in enumerate(prompt)])
+    models = [ncm.Model.load(path, device=0, shares=shares, shard=r) for r in range(2)]
+    try:
+        for m, fn in zip(models, _thread_reducers(2)):
+            m.tp_set_host_reducer(fn)
+            m.tp_set_reducer(ncm.REDUCE_HOST_CALLBACK)
+        lgs = _run_shards(models, lambda r, m: np.stack(
+            [m.forward_pass(t, pos, want_logits=True)[1] for pos, t in enumerate(prompt)]))
+        assert not any(isinstance(x, Exception) for x in lgs), lgs
+        lg = np.concatenate(lgs, axis=1)
+        gap = float(np.max(np.abs(lg - ref_lg))) / float(np.max(np.abs(ref_lg)))
+        assert gap <= 1e-5, gap
+        for m in models:
+            m.reset()
+        toks = _run_shards(models, lambda r, m: m.generate(prompt, n_gen))
+        assert toks[0] == toks[1] == ref_tokens, (toks, ref_tokens)
+
+        # the closure's Err at layer 1, FFN phase: a step error, no device wait involved
+        for m, fn in zip(models, _thread_reducers(2, fail_at=(1, ncm.PHASE_FFN))):
+            m.tp_set_host_reducer(fn)
+        errs = _run_shards(models, lambda r, m: m.forward_pass(prompt[0], 0))
+        for e in errs:
+            assert isinstance(e, ncm.NcmError) and e.status == 4 and "layer 1" in str(e), errs
+        for m, fn in zip(models, _thread_reducers(2)):
+            m.tp_set_host_reducer(fn)
+            m.reset()
+        toks = _run_shards(models, lambda r, m: m.generate(prompt, n_gen))
+        assert toks[0] == toks[1] == ref_tokens, (toks, ref_tokens)
+    finally:
+        for m in models:
+            m.close()
