@@ -351,10 +351,11 @@ def run_verify(args, ncm):
     sp = ncm.CONFIGS["cfg5_target_q4_0"]
     n_prompt = args.prompt
     prompt = [int(v) for v in np.random.default_rng(0).integers(0, sp.vocab, n_prompt)]
-    target = ncm.Model.synthetic(sp, ctx_limit=n_prompt + 32, device=0)
+    reps = max(1, args.steps)
+    target = ncm.Model.synthetic(sp, ctx_limit=n_prompt + 16 + reps, device=0)   # verify rows + timed steps
     target.generate(prompt, 1)
     rows = tuple(int(v) for v in args.verify_rows.split(","))
-    vms, step_ms = verify_times(ncm, target, n_prompt, reps=max(1, args.steps), rows=rows)
+    vms, step_ms = verify_times(ncm, target, n_prompt, reps=reps, rows=rows)
     print(json.dumps({"workload": f"cfg5_target_q4_0 verify pass at position {n_prompt}", "verify_ms_by_rows": vms,
                       "single_step_ms": step_ms, "timing": "wall clock per synchronous call"}))
 
