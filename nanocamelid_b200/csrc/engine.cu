@@ -110,6 +110,8 @@ struct ncm_model {
     unsigned* b_cnt = nullptr;
     int *b_tok = nullptr, *b_arg = nullptr, *b_pos = nullptr;
     float* b_scores = nullptr;
+    float* b_part = nullptr;      // tensor parallel: [kMaxBatch][emb] partial rows
+    float2* b_pairs = nullptr;    // tensor parallel: [kMaxBatch] head pairs of this shard
     cudaGraphExec_t b_graph[kMaxBatch + 1] = {};
     // tensor parallel
     int world = 1, rank = 0, reduce_mode = NCM_REDUCE_FUSED_P2P;
@@ -851,6 +853,8 @@ static ncm_status ensure_batch_buffers(ncm_model* m) {
     DALLOC(m->b_arg, 4 * kMaxBatch);
     DALLOC(m->b_pos, 4);
     DALLOC(m->b_scores, 4 * (size_t)kMaxBatch * m->qh * m->ctx);
+    DALLOC(m->b_part, 4 * (size_t)kMaxBatch * m->emb);
+    DALLOC(m->b_pairs, sizeof(float2) * kMaxBatch);
     CK(cudaMemset(m->b_cnt, 0, 4));
     return NCM_OK;
 }
@@ -883,6 +887,24 @@ static int launch_batch(std::initializer_list<const DevMat*> mats, const DevMat*
         if (r) return r;
     }
     return batch_gemv_launch(w0.type, epi, p, grid, s, true);
+}
+
+// Row-parallel wo / w2 of the multi-row pass: one GPU -> hidden rows += out; tensor
+// parallel (host-callback reducer) -> partial rows, the host's rank-ordered sum over all
+// ntok rows at once (tp.rs:349-363 per row), residual add.
+static ncm_status batch_row_parallel(ncm_model* m, const DevMat& w, BatchParams& p, int ntok, int layer, int phase,
+                                     cudaStream_t s) {
+    if (!host_mode(m)) {
+        CKL(launch_batch({&w}, nullptr, EPI_RESID, p, s));
+        return NCM_OK;
+    }
+    p.seg[0] = {m->b_part, m->emb, 0, SEG_OUT};
+    p.out_stride = m->emb;
+    CKL(launch_batch({&w}, nullptr, EPI_PLAIN, p, s));
+    ncm_status st = host_reduce(m, m->b_part, ntok * m->emb, layer, phase, s);
+    if (st) return st;
+    CKL(resid_add_launch(m->b_hidden, m->b_part, ntok * m->emb, s, true));
+    return NCM_OK;
 }
 
 // Every GEMV CTA quantises the whole f32 input itself when it is small (saves a launch);
@@ -943,7 +965,8 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s) {
         o.total_rows = m->emb;
         o.hidden = m->b_hidden;
         o.hidden_stride = m->emb;
-        CKL(launch_batch({&L.wo}, nullptr, EPI_RESID, o, s));
+        ncm_status st = batch_row_parallel(m, L.wo, o, ntok, l, NCM_REDUCE_PHASE_ATTENTION, s);
+        if (st) return st;
         CKL(batch_prep_launch(m->b_hidden, m->emb, m->emb, ntok, L.ffn_norm, m->eps, nullptr, nullptr, m->b_xq,
                               m->b_xs, s, true));
         BatchParams f = batch_base(m, ntok);
@@ -965,7 +988,8 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s) {
         d.total_rows = m->emb;
         d.hidden = m->b_hidden;
         d.hidden_stride = m->emb;
-        CKL(launch_batch({&L.w2}, nullptr, EPI_RESID, d, s));
+        st = batch_row_parallel(m, L.w2, d, ntok, l, NCM_REDUCE_PHASE_FFN, s);
+        if (st) return st;
     }
     CKL(batch_prep_launch(m->b_hidden, m->emb, m->emb, ntok, m->out_norm, m->eps, nullptr, nullptr, m->b_xq, m->b_xs,
                           s, true));
@@ -977,6 +1001,16 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s) {
     h.counter = m->b_cnt;
     h.argmax_out = m->b_arg;
     h.head_row0 = m->h0;
+    if (host_mode(m)) {
+        // each row's (logit, token) of this vocab shard; the host merges them per row in
+        // rank order (cluster_tp_node.rs:1185-1204) and the merged tokens are the result
+        h.pair_out = m->b_pairs;
+        CKL(launch_batch({&m->head}, nullptr, EPI_ARGMAX, h, s));
+        ncm_status st = host_reduce(m, m->b_pairs, 2 * ntok, m->layers, NCM_REDUCE_PHASE_HEAD, s);
+        if (st) return st;
+        for (int t = 0; t < ntok; ++t) memcpy(m->h_stage + 16 + t, m->h_red + 2 * t + 1, 4);
+        return NCM_OK;
+    }
     CKL(launch_batch({&m->head}, nullptr, EPI_ARGMAX, h, s));
     return NCM_OK;
 }
@@ -985,7 +1019,8 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s) {
 extern "C" ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok, int pos0, int* argmax_out) {
     if (!m || !tokens || !argmax_out || ntok < 1 || ntok > kMaxBatch || pos0 < 0 || pos0 + ntok > m->ctx)
         return fail(NCM_EINVAL, "bad verify batch");
-    if (m->world > 1) return fail(NCM_EUNSUPPORTED, "multi-row verify runs on one GPU");
+    if (m->world > 1 && !host_mode(m))
+        return fail(NCM_EUNSUPPORTED, "multi-row verify under tensor parallelism runs with the host-callback reducer");
     for (int i = 0; i < ntok; ++i)
         if (tokens[i] < 0 || tokens[i] >= m->vocab) return fail(NCM_EINVAL, "token id out of range");
     CK(cudaSetDevice(m->device));
@@ -996,6 +1031,14 @@ extern "C" ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok
     memcpy(m->h_stage + 5, tokens, 4 * (size_t)ntok);
     CK(cudaMemcpyAsync(m->b_pos, m->h_stage + 4, 4, cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(m->b_tok, m->h_stage + 5, 4 * (size_t)ntok, cudaMemcpyHostToDevice, s));
+    if (host_mode(m)) {
+        // eager: the host reducer runs between the kernels; the merged tokens are in h_stage
+        if ((st = enqueue_verify(m, ntok, s))) return st;
+        CK(cudaStreamSynchronize(s));
+        if ((st = check_err(m))) return st;
+        memcpy(argmax_out, m->h_stage + 16, 4 * (size_t)ntok);
+        return NCM_OK;
+    }
     if (m->b_graph[ntok]) {
         CK(cudaGraphLaunch(m->b_graph[ntok], s));
     } else {
@@ -1225,7 +1268,7 @@ extern "C" ncm_status ncm_tp_set_host_reducer(ncm_model* m, ncm_host_reduce_fn f
     if (!m || !fn) return fail(NCM_EINVAL, "null argument");
     CK(cudaSetDevice(m->device));
     CK(cudaStreamSynchronize(m->stream));
-    if (!m->h_red) CK(cudaMallocHost((void**)&m->h_red, 4 * (size_t)std::max(m->emb, 2)));
+    if (!m->h_red) CK(cudaMallocHost((void**)&m->h_red, 4 * (size_t)kMaxBatch * std::max(m->emb, 2)));
     m->host_fn = fn;
     m->host_user = user;
     return NCM_OK;

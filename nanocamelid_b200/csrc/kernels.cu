@@ -2013,7 +2013,8 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(const __gr
                 const int ei = __float_as_int(e.y);
                 if (better(e.x, ei, bv, bi)) { bv = e.x; bi = ei; }
             }
-            p.argmax_out[tid] = p.head_row0 + bi;
+            if (p.pair_out) p.pair_out[tid] = make_float2(bv, __int_as_float(p.head_row0 + bi));   // shard's pair
+            else p.argmax_out[tid] = p.head_row0 + bi;
         }
         __syncthreads();
         if (s_last && tid == 0) *p.counter = 0u;

@@ -133,6 +133,7 @@ struct alignas(64) BatchParams {
     float2* amax_part;            // EPI_ARGMAX: [grid][kMaxBatch]
     unsigned* counter;
     int* argmax_out;              // [ntok] global vocab rows
+    float2* pair_out;             // or, when set: [ntok] (logit, token bits) of this vocab shard
     int head_row0;
     int* err;
 };

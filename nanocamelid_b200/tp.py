@@ -45,15 +45,17 @@ def check_plan(spec_, shares, world, rank, group=None):
 def rank_ordered(parts, phase):
     """The global value from every rank's buffer, in rank order: the f32 sum from 0.0f
     (tp.rs:349-363, the master's fixed-order sum in cluster_tp_node.rs:1154-1180), or for
-    the head the first maximum by strict '>' (cluster_tp_node.rs:1185-1204; the token
-    slot is copied, never computed on)."""
+    the head the first maximum of every row's pair by strict '>'
+    (cluster_tp_node.rs:1185-1204; the token slot is copied, never computed on)."""
     import numpy as np
     if phase == PHASE_HEAD:
-        best = parts[0]
+        # one (logit, token bits) pair per row: merged row by row
+        best = np.array(parts[0], dtype=np.float32, copy=True).reshape(-1, 2)
         for p in parts[1:]:
-            if p[0] > best[0]:
-                best = p
-        return np.array(best, dtype=np.float32, copy=True)
+            p = np.asarray(p, dtype=np.float32).reshape(-1, 2)
+            take = p[:, 0] > best[:, 0]
+            best[take] = p[take]
+        return best.reshape(-1)
     acc = np.zeros(len(parts[0]), dtype=np.float32)
     for p in parts:
         acc = acc + p

@@ -200,3 +200,25 @@ def test_oracle_regression_fixture(ncm, orc, tmp_path):
     toks, lg = m.generate(g["prompt"], g["n_gen"], want_last_logits=True)
     assert toks == g["tokens"]
     assert lg.view(np.uint32)[: len(g["logit_bits_head"])].tolist() == g["logit_bits_head"]
+
+
+def test_rank_ordered_sum_and_per_row_head_merge():
+    """tp.rank_ordered: f32 sum from 0.0f in rank order (tp.rs:349-363); head pairs
+    merged per row by strict '>' in rank order, token bits copied unchanged."""
+    from nanocamelid_b200 import PHASE_FFN, PHASE_HEAD
+    from nanocamelid_b200 import tp
+    rng = np.random.default_rng(5)
+    parts = [(rng.standard_normal(64) * 10.0 ** rng.integers(-4, 4, 64)).astype(np.float32) for _ in range(3)]
+    want = np.float32(0.0) + parts[0]
+    want = (want + parts[1]).astype(np.float32)
+    want = (want + parts[2]).astype(np.float32)
+    assert np.array_equal(tp.rank_ordered(parts, PHASE_FFN).view(np.uint32), want.view(np.uint32))
+    pairs = []
+    for r, logits in enumerate(([1.0, 5.0, 2.0], [3.0, 5.0, 2.0], [3.0, 4.0, 9.0])):
+        a = np.zeros(6, dtype=np.float32)
+        a[0::2] = logits
+        a.view(np.int32)[1::2] = [100 * r + 1, 100 * r + 2, 100 * r + 3]   # denormal bit patterns
+        pairs.append(a)
+    got = tp.rank_ordered(pairs, PHASE_HEAD)
+    assert got[0::2].tolist() == [3.0, 5.0, 9.0]
+    assert got.view(np.int32)[1::2].tolist() == [101, 2, 203]

@@ -213,3 +213,35 @@ def test_tp_host_callback_reducer_on_one_gpu(ncm, orc, cuda, tmp_path):
     finally:
         for m in models:
             m.close()
+
+
+@pytest.mark.parametrize("k", [4, 8])
+def test_tp_speculative_with_host_reducer_on_one_gpu(ncm, orc, cuda, tmp_path, k):
+    """Config 5 with a tensor-parallel target (two shards of one GPU, threads, host
+    reducer): every rank runs the same speculative loop with its own full draft; the
+    multi-row verify reduces all rows through the host closure and merges each row's
+    head pair.  The output equals the oracle TP's greedy decode (k = 4: the pending-token
+    cycle with 5-row verifies; k = 8: the reference-shaped cycle)."""
+    sp = _spec(ncm, 2, 4)
+    d = dict(TINY)
+    dsp = ncm.spec(d["emb"], 1, 4, 2, d["emb"] // 4, 512, vocab=d["vocab"], ctx=d["ctx"], tied=True, seed=12)
+    path = str(tmp_path / "m.gguf")
+    ncm.write_synthetic_gguf(path, sp)
+    shares = [1, 1]
+    prompt = [int(v) for v in np.random.default_rng(4).integers(0, sp.vocab, size=7)]
+    n_gen = 24
+    ref = orc.OracleTP(orc.OracleModel(path), shares).generate(prompt, n_gen)
+    models = [ncm.Model.load(path, device=0, shares=shares, shard=r) for r in range(2)]
+    drafts = [ncm.Model.synthetic(dsp, device=0) for _ in range(2)]
+    try:
+        for m, fn in zip(models, _thread_reducers(2)):
+            m.tp_set_host_reducer(fn)
+            m.tp_set_reducer(ncm.REDUCE_HOST_CALLBACK)
+        out = _run_shards(models, lambda r, m: m.spec_generate(drafts[r], prompt, n_gen, k=k))
+        assert not any(isinstance(x, Exception) for x in out), out
+        (t0, s0), (t1, s1) = out
+        assert t0 == t1 == ref, (t0, t1, ref)
+        assert s0 == s1
+    finally:
+        for m in models + drafts:
+            m.close()
