@@ -112,7 +112,7 @@ struct ncm_model {
     float* b_scores = nullptr;
     float* b_part = nullptr;      // tensor parallel: [kMaxBatch][emb] partial rows
     float2* b_pairs = nullptr;    // tensor parallel: [kMaxBatch] head pairs of this shard
-    cudaGraphExec_t b_graph[kMaxBatch + 1] = {};
+    cudaGraphExec_t b_graph[2][kMaxBatch + 1] = {};   // [with head][rows]
     // tensor parallel
     int world = 1, rank = 0, reduce_mode = NCM_REDUCE_FUSED_P2P;
     bool tp_ready = false;
@@ -148,8 +148,9 @@ static void free_model(ncm_model* m) {
     cudaSetDevice(m->device);
     if (m->g_full) cudaGraphExecDestroy(m->g_full);
     if (m->g_nohead) cudaGraphExecDestroy(m->g_nohead);
-    for (auto& gx : m->b_graph)
-        if (gx) cudaGraphExecDestroy(gx);
+    for (auto& row : m->b_graph)
+        for (auto& gx : row)
+            if (gx) cudaGraphExecDestroy(gx);
     for (void* p : m->ipc_open) cudaIpcCloseMemHandle(p);
     if (m->nccl && g_nccl.CommDestroy) g_nccl.CommDestroy(m->nccl);
     for (void* p : m->allocs) cudaFree(p);
@@ -548,6 +549,7 @@ static int launch_gemv(std::initializer_list<const DevMat*> mats, const DevMat* 
 }
 
 static ncm_status check_err(ncm_model* m);
+static ncm_status run_rows(ncm_model* m, const int* tokens, int ntok, int pos0, bool with_head, int* argmax_out);
 static bool host_mode(const ncm_model* m) { return m->world > 1 && m->reduce_mode == NCM_REDUCE_HOST_CALLBACK; }
 
 // The reference's reduce closure (tp.rs:226-236): n floats of `dev` go to the host
@@ -747,6 +749,25 @@ extern "C" ncm_status ncm_prefill_tokens(ncm_model* m, const int* prompt, int n_
     if (s) return s;
     cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
     CK(cudaStreamSynchronize(st));
+    if (n_prompt > 1 && (m->world == 1 || host_mode(m))) {
+        // Eight prompt tokens per multi-row pass: every row's K/V and greedy token equal
+        // the token-by-token prefill's bit for bit, so the state below is the one that
+        // prefill leaves (tokens, position, prompt length, last token).
+        int last = 0;
+        for (int c0 = 0; c0 < n_prompt; c0 += kMaxBatch) {
+            const int nt = std::min(kMaxBatch, n_prompt - c0);
+            const bool fin = c0 + nt == n_prompt;
+            int out[kMaxBatch];
+            if ((s = run_rows(m, prompt + c0, nt, c0, fin, out))) return s;
+            if (fin) last = out[nt - 1];
+        }
+        CK(cudaMemcpy(m->tokens, prompt, 4 * (size_t)n_prompt, cudaMemcpyHostToDevice));
+        if (n_prompt < m->ctx) CK(cudaMemcpy(m->tokens + n_prompt, &last, 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(m->state + ST_POS, &n_prompt, 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(m->state + ST_NPROMPT, &n_prompt, 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(m->state + ST_LAST_TOKEN, &last, 4, cudaMemcpyHostToDevice));
+        return NCM_OK;
+    }
     CK(cudaMemcpyAsync(m->tokens, prompt, 4 * (size_t)n_prompt, cudaMemcpyHostToDevice, st));
     if ((s = set_pos(m, 0, n_prompt, st))) return s;
     for (int i = 0; i + 1 < n_prompt; ++i)
@@ -915,7 +936,7 @@ static bool prologue_quant(int ntok, int cols) { return (int64_t)ntok * cols <= 
 // then compute_logits_from_hidden + sample_logits(_, 0.0) per row) for tokens b_tok at
 // positions *b_pos + t: each weight tile read once for all rows, K/V stored at their
 // positions, greedy argmax of every row into b_arg.  Captured once per row count.
-static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s) {
+static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s, bool with_head) {
     const int qw = m->qh * m->hd, kw = m->kh * m->hd;
     CKL(embed_rows_launch(m->embd.type, m->embd.d, m->embd.pitch, m->emb, m->b_tok, ntok, m->b_hidden, s, true));
     for (int l = 0; l < m->layers; ++l) {
@@ -991,6 +1012,7 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s) {
         st = batch_row_parallel(m, L.w2, d, ntok, l, NCM_REDUCE_PHASE_FFN, s);
         if (st) return st;
     }
+    if (!with_head) return NCM_OK;   // prompt rows before the last: K/V only
     CKL(batch_prep_launch(m->b_hidden, m->emb, m->emb, ntok, m->out_norm, m->eps, nullptr, nullptr, m->b_xq, m->b_xs,
                           s, true));
     BatchParams h = batch_base(m, ntok);
@@ -1015,14 +1037,10 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s) {
     return NCM_OK;
 }
 
-// Every row's greedy token equals the one-token step at that position bit for bit.
-extern "C" ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok, int pos0, int* argmax_out) {
-    if (!m || !tokens || !argmax_out || ntok < 1 || ntok > kMaxBatch || pos0 < 0 || pos0 + ntok > m->ctx)
-        return fail(NCM_EINVAL, "bad verify batch");
-    if (m->world > 1 && !host_mode(m))
-        return fail(NCM_EUNSUPPORTED, "multi-row verify under tensor parallelism runs with the host-callback reducer");
-    for (int i = 0; i < ntok; ++i)
-        if (tokens[i] < 0 || tokens[i] >= m->vocab) return fail(NCM_EINVAL, "token id out of range");
+// One multi-row pass over tokens[0..ntok) at positions pos0 .. pos0+ntok-1 (K/V stored),
+// with the head (greedy token of every row into argmax_out) or without it.  Graph per
+// (head, rows), captured on first use; eager under the host reducer.
+static ncm_status run_rows(ncm_model* m, const int* tokens, int ntok, int pos0, bool with_head, int* argmax_out) {
     CK(cudaSetDevice(m->device));
     ncm_status st = ensure_batch_buffers(m);
     if (st) return st;
@@ -1033,36 +1051,48 @@ extern "C" ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok
     CK(cudaMemcpyAsync(m->b_tok, m->h_stage + 5, 4 * (size_t)ntok, cudaMemcpyHostToDevice, s));
     if (host_mode(m)) {
         // eager: the host reducer runs between the kernels; the merged tokens are in h_stage
-        if ((st = enqueue_verify(m, ntok, s))) return st;
+        if ((st = enqueue_verify(m, ntok, s, with_head))) return st;
         CK(cudaStreamSynchronize(s));
         if ((st = check_err(m))) return st;
-        memcpy(argmax_out, m->h_stage + 16, 4 * (size_t)ntok);
+        if (with_head) memcpy(argmax_out, m->h_stage + 16, 4 * (size_t)ntok);
         return NCM_OK;
     }
-    if (m->b_graph[ntok]) {
-        CK(cudaGraphLaunch(m->b_graph[ntok], s));
+    cudaGraphExec_t& gx = m->b_graph[with_head ? 1 : 0][ntok];
+    if (gx) {
+        CK(cudaGraphLaunch(gx, s));
     } else {
-        // first use of this row count: run eagerly (configures the kernels), then capture
-        if ((st = enqueue_verify(m, ntok, s))) return st;
+        // first use of this shape: run eagerly (configures the kernels), then capture
+        if ((st = enqueue_verify(m, ntok, s, with_head))) return st;
         CK(cudaStreamSynchronize(s));
         cudaGraph_t graph;
         CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-        st = enqueue_verify(m, ntok, s);
+        st = enqueue_verify(m, ntok, s, with_head);
         cudaError_t e = cudaStreamEndCapture(s, &graph);
         if (st) {
             if (e == cudaSuccess) cudaGraphDestroy(graph);
             return st;
         }
         CK(e);
-        e = cudaGraphInstantiate(&m->b_graph[ntok], graph, 0);
+        e = cudaGraphInstantiate(&gx, graph, 0);
         cudaGraphDestroy(graph);
         CK(e);
     }
-    CK(cudaMemcpyAsync(m->h_stage + 16, m->b_arg, 4 * (size_t)ntok, cudaMemcpyDeviceToHost, s));
+    if (with_head) CK(cudaMemcpyAsync(m->h_stage + 16, m->b_arg, 4 * (size_t)ntok, cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
     if ((st = check_err(m))) return st;
-    memcpy(argmax_out, m->h_stage + 16, 4 * (size_t)ntok);
+    if (with_head) memcpy(argmax_out, m->h_stage + 16, 4 * (size_t)ntok);
     return NCM_OK;
+}
+
+// Every row's greedy token equals the one-token step at that position bit for bit.
+extern "C" ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok, int pos0, int* argmax_out) {
+    if (!m || !tokens || !argmax_out || ntok < 1 || ntok > kMaxBatch || pos0 < 0 || pos0 + ntok > m->ctx)
+        return fail(NCM_EINVAL, "bad verify batch");
+    if (m->world > 1 && !host_mode(m))
+        return fail(NCM_EUNSUPPORTED, "multi-row verify under tensor parallelism runs with the host-callback reducer");
+    for (int i = 0; i < ntok; ++i)
+        if (tokens[i] < 0 || tokens[i] >= m->vocab) return fail(NCM_EINVAL, "token id out of range");
+    return run_rows(m, tokens, ntok, pos0, true, argmax_out);
 }
 
 // speculative.rs:299-494 speculative_decoding_step at temperature 0, repeated: the

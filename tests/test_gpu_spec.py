@@ -122,3 +122,26 @@ def test_spec_self_draft_accepts_everything(ncm, cuda):
     toks, (drafted, accepted) = target.spec_generate(draft, prompt, 25, k=4)
     assert toks == ncm.Model.synthetic(sp, device=0).generate(prompt, 25)
     assert accepted == drafted
+
+
+@pytest.mark.parametrize("variant", list(VARIANTS))
+def test_batched_prefill_equals_token_by_token(ncm, cuda, variant):
+    """The prompt is ingested eight rows per multi-row pass (the verify kernels): the K/V
+    of every prompt position, the first generated token and the decode after it equal a
+    token-by-token ingestion (one-token steps) bit for bit."""
+    sp = tiny(ncm, **VARIANTS[variant])
+    prompt = [int(v) for v in np.random.default_rng(8).integers(0, sp.vocab, size=19)]   # 8 + 8 + 3 rows
+    a = ncm.Model.synthetic(sp, device=0)
+    b = ncm.Model.synthetic(sp, device=0)
+    ga = a.generate(prompt, 6)
+    for pos, t in enumerate(prompt):
+        nxt = b.forward_pass(t, pos)[0]
+    assert ga[0] == nxt
+    kw = sp.kv_heads * sp.head_dim
+    for layer in range(sp.layers):
+        for which in (4, 5):
+            ka = a.debug_read(which, len(prompt) * kw, layer)
+            kb = b.debug_read(which, len(prompt) * kw, layer)
+            assert np.array_equal(ka.view(np.uint32), kb.view(np.uint32)), (layer, which)
+    for i in range(1, len(ga)):   # the decode after the prompt continues identically
+        assert b.forward_pass(ga[i - 1], len(prompt) + i - 1)[0] == ga[i], i
