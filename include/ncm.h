@@ -190,6 +190,19 @@ ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok, int pos0,
 ncm_status ncm_spec_generate(ncm_model* target, ncm_model* draft, const int* prompt, int n_prompt, int n_gen, int k,
                              int* out_tokens, int* stats);
 
+/* speculative.rs:80-105 NGramDrafter::draft, host only (no GPU): up to max_tokens
+ * tokens that followed the most recent earlier occurrence of the longest suffix
+ * n-gram of history[0..len) (n from max_ngram down to min_ngram; the reference's
+ * defaults are 4 and 3).  Returns the count written to out. */
+int ncm_ngram_draft(const int* history, int len, int max_tokens, int max_ngram, int min_ngram, int* out);
+
+/* speculative.rs:122-297 ngram_speculative_step at temperature 0, repeated as
+ * main.rs:9720-9760 (prompt-lookup speculation, the reference's default draft source):
+ * n_gen tokens into out_tokens, equal to the greedy decode; stats = {drafted,
+ * accepted}.  Up to 7 drafts per multi-row pass (row 0 = the target's own token). */
+ncm_status ncm_ngram_generate(ncm_model* m, const int* prompt, int n_prompt, int n_gen, int k, int max_ngram,
+                              int min_ngram, int* out_tokens, int* stats);
+
 /* ---------------------------------------------------------------- multi-GPU (one process per GPU)
  * Replaces the TCP star reducer (bin/cluster_tp_node.rs:505-550, 1042-1056, 1154-1180)
  * feeding tp.rs:226-428 tp_forward_token_reduced.

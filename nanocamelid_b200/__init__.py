@@ -123,6 +123,8 @@ def lib():
         "ncm_tp_set_timeout_ns": (c_int, [c_p, c_u64]),
         "ncm_verify_batch": (c_int, [c_p, pint, c_int, c_int, pint]),
         "ncm_spec_generate": (c_int, [c_p, c_p, pint, c_int, c_int, c_int, pint, pint]),
+        "ncm_ngram_draft": (c_int, [pint, c_int, c_int, c_int, c_int, pint]),
+        "ncm_ngram_generate": (c_int, [c_p, pint, c_int, c_int, c_int, c_int, c_int, pint, pint]),
         "ncm_test_peer_timeout": (c_int, [c_int, c_u64]),
     }
     for name, (res, args) in sigs.items():
@@ -317,6 +319,14 @@ class Model:
         _ck(lib().ncm_spec_generate(self._h, draft._h, _ints(prompt), len(prompt), n_gen, k, out, stats))
         return list(out)[:n_gen], (stats[0], stats[1])
 
+    def ngram_generate(self, prompt, n_gen, k=4, max_ngram=4, min_ngram=3):
+        """speculative.rs:122-297 prompt-lookup (n-gram) speculative decoding; returns
+        (tokens, (drafted, accepted))."""
+        out = (ctypes.c_int * max(1, n_gen))()
+        stats = (ctypes.c_int * 2)()
+        _ck(lib().ncm_ngram_generate(self._h, _ints(prompt), len(prompt), n_gen, k, max_ngram, min_ngram, out, stats))
+        return list(out)[:n_gen], (stats[0], stats[1])
+
     # tensor parallel
     def tp_export(self):
         buf = (ctypes.c_uint8 * TP_HANDLE_BYTES)()
@@ -355,6 +365,13 @@ class Model:
 
     def tp_set_timeout_ns(self, ns):
         _ck(lib().ncm_tp_set_timeout_ns(self._h, int(ns)))
+
+
+def ngram_draft(history, max_tokens, max_ngram=4, min_ngram=3):
+    """speculative.rs:80-105 NGramDrafter::draft (host only)."""
+    out = (ctypes.c_int * max(1, max_tokens))()
+    n = lib().ncm_ngram_draft(_ints(history), len(history), max_tokens, max_ngram, min_ngram, out)
+    return list(out)[:n]
 
 
 def nccl_unique_id():

@@ -1208,6 +1208,84 @@ extern "C" ncm_status ncm_spec_generate(ncm_model* target, ncm_model* draft, con
     return check_err(draft);
 }
 
+// ------------------------------------------------------------------ n-gram speculation
+// speculative.rs:80-105 NGramDrafter::draft (host only): the longest suffix n-gram of
+// the history (max_ngram down to min_ngram) that occurred earlier, its most recent
+// occurrence; the tokens that followed it (up to max_tokens, inside the history).
+extern "C" int ncm_ngram_draft(const int* history, int len, int max_tokens, int max_ngram, int min_ngram, int* out) {
+    if (!history || !out || len < 0 || max_tokens <= 0 || min_ngram <= 0 || len <= min_ngram) return 0;
+    const int max_n = std::min(max_ngram, len - 1);
+    for (int n = max_n; n >= min_ngram; --n) {
+        const int* pat = history + len - n;
+        for (int start = len - n - 1; start >= 0; --start) {
+            if (!std::equal(pat, pat + n, history + start)) continue;
+            const int cs = start + n, ce = std::min(cs + max_tokens, len);
+            if (cs >= ce) break;
+            std::copy(history + cs, history + ce, out);
+            return ce - cs;
+        }
+    }
+    return 0;
+}
+
+// speculative.rs:122-297 ngram_speculative_step at temperature 0, driven as
+// main.rs:9720-9760 (k per step = min(k, remaining - 1)): the target's own token t0
+// plus the drafts from the history go through one multi-row pass (t0 is row 0); the
+// agreeing drafts are emitted, the first disagreement emits the target's token and
+// runs the corrective one-token step.  Output = the target's greedy decode.
+extern "C" ncm_status ncm_ngram_generate(ncm_model* m, const int* prompt, int n_prompt, int n_gen, int k, int max_ngram,
+                                        int min_ngram, int* out_tokens, int* stats) {
+    if (!m || !prompt || !out_tokens || n_prompt < 1 || n_gen < 0 || k < 0)
+        return fail(NCM_EINVAL, "bad n-gram speculative arguments");
+    if (n_prompt + n_gen > m->ctx) return fail(NCM_EINVAL, "prompt + generation exceeds the context");
+    if (k > 0 && m->world > 1 && !host_mode(m))
+        return fail(NCM_EUNSUPPORTED, "multi-row verify under tensor parallelism runs with the host-callback reducer");
+    if (stats) stats[0] = stats[1] = 0;
+    ncm_status st = ncm_prefill_tokens(m, prompt, n_prompt, nullptr);
+    if (st) return st;
+    int pred = 0, p0 = 0;
+    if ((st = ncm_sync_tokens(m, nullptr, 0, &p0))) return st;
+    CK(cudaMemcpy(&pred, m->state + ST_LAST_TOKEN, 4, cudaMemcpyDeviceToHost));
+    std::vector<int> hist(prompt, prompt + n_prompt), drafts(std::max(k, 1));
+    int pos = n_prompt, n = 0;
+    while (n < n_gen && pos < m->ctx) {
+        const int cur_k = std::min(k, n_gen - n - 1);
+        const int t0 = pred;
+        hist.push_back(t0);   // the draft sees the history plus t0
+        int nd = cur_k > 0 ? ncm_ngram_draft(hist.data(), (int)hist.size(), cur_k, max_ngram, min_ngram, drafts.data()) : 0;
+        nd = std::min(nd, std::min(kMaxBatch - 1, m->ctx - (pos + 1)));
+        out_tokens[n++] = t0;
+        if (nd <= 0) {
+            if ((st = ncm_forward_pass(m, t0, pos, nullptr, &pred))) return st;
+            pos += 1;
+            continue;
+        }
+        if (stats) stats[0] += nd;
+        int rows[kMaxBatch], g[kMaxBatch];
+        rows[0] = t0;
+        for (int i = 0; i < nd; ++i) rows[i + 1] = drafts[i];
+        if ((st = ncm_verify_batch(m, rows, nd + 1, pos, g))) return st;
+        int i = 0;
+        for (; i < nd; ++i) {
+            const int tt = g[i];
+            if (drafts[i] == tt && stats) stats[1] += 1;
+            if (n < n_gen) out_tokens[n++] = tt;
+            hist.push_back(tt);
+            if (drafts[i] != tt) {
+                // corrective step: replaces the rejected draft's K/V, predicts the next position
+                if ((st = ncm_forward_pass(m, tt, pos + i + 1, nullptr, &pred))) return st;
+                pos += i + 2;
+                break;
+            }
+        }
+        if (i == nd) {
+            pred = g[nd];
+            pos += nd + 1;
+        }
+    }
+    return NCM_OK;
+}
+
 // ------------------------------------------------------------------ tensor parallel
 extern "C" ncm_status ncm_tp_export(ncm_model* m, uint8_t* handle_out) {
     if (!m || !handle_out) return fail(NCM_EINVAL, "null argument");

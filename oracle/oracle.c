@@ -800,6 +800,77 @@ int orc_spec_generate(orc_model* tgt, orc_model* dr, const int* prompt, int n_pr
     return n;
 }
 
+/* speculative.rs:80-105 NGramDrafter::draft: the longest suffix n-gram of history
+ * (max_ngram down to min_ngram) with an earlier occurrence, the most recent one; its
+ * continuation (up to max_tokens, inside history) is the draft. */
+int orc_ngram_draft(const int* h, int len, int max_tokens, int max_ngram, int min_ngram, int* out) {
+    if (max_tokens <= 0 || min_ngram <= 0 || len <= min_ngram) return 0;
+    int max_n = max_ngram < len - 1 ? max_ngram : len - 1;
+    for (int n = max_n; n >= min_ngram; --n) {
+        const int* pat = h + len - n;
+        for (int start = len - n - 1; start >= 0; --start) {
+            if (memcmp(h + start, pat, sizeof(int) * (size_t)n) == 0) {
+                int cs = start + n, ce = cs + max_tokens < len ? cs + max_tokens : len;
+                if (cs < ce) {
+                    memcpy(out, h + cs, sizeof(int) * (size_t)(ce - cs));
+                    return ce - cs;
+                }
+                break;
+            }
+        }
+    }
+    return 0;
+}
+
+/* speculative.rs:122-297 ngram_speculative_step at temperature 0 (no stop tokens),
+ * driven as main.rs:9720-9760: k per step = min(k, remaining - 1); drafts bounded by
+ * max_batch - 1 and the context; t0 and the drafts verified as batch rows (each row =
+ * a one-token forward pass at its position), a corrective pass on the first mismatch. */
+int orc_ngram_generate(orc_model* m, const int* prompt, int n_prompt, int n_gen, int k, int max_ngram, int min_ngram,
+                       int max_batch, int* out, int* stats) {
+    stats[0] = stats[1] = 0;
+    int* hist = malloc(sizeof(int) * (size_t)(n_prompt + n_gen + 2));
+    int* drafts = malloc(sizeof(int) * (size_t)(k + 1));
+    int len = 0, pos = 0, pred = 0, n = 0;
+    for (int i = 0; i < n_prompt; ++i) { pred = orc_forward_pass(m, prompt[i], pos++, NULL); hist[len++] = prompt[i]; }
+    while (n < n_gen && pos < m->ctx) {
+        int cur_k = k < n_gen - n - 1 ? k : n_gen - n - 1;
+        int t0 = pred;
+        hist[len] = t0;
+        int nd = cur_k > 0 ? orc_ngram_draft(hist, len + 1, cur_k, max_ngram, min_ngram, drafts) : 0;
+        if (nd > max_batch - 1) nd = max_batch - 1;
+        if (nd > m->ctx - (pos + 1)) nd = m->ctx - (pos + 1);
+        if (nd <= 0) {
+            out[n++] = t0; hist[len++] = t0;
+            pred = orc_forward_pass(m, t0, pos, NULL);
+            pos += 1;
+            continue;
+        }
+        stats[0] += nd;
+        int g[65];
+        g[0] = orc_forward_pass(m, t0, pos, NULL);
+        for (int i = 0; i < nd; ++i) g[i + 1] = orc_forward_pass(m, drafts[i], pos + 1 + i, NULL);
+        out[n++] = t0; hist[len++] = t0;
+        int all = 1;
+        for (int i = 0; i < nd; ++i) {
+            int tt = g[i];
+            if (drafts[i] == tt) {
+                stats[1]++;
+                out[n++] = tt; hist[len++] = tt;
+            } else {
+                out[n++] = tt; hist[len++] = tt;
+                pred = orc_forward_pass(m, tt, pos + i + 1, NULL);
+                pos = pos + i + 2;
+                all = 0;
+                break;
+            }
+        }
+        if (all) { pred = g[nd]; pos = pos + nd + 1; }
+    }
+    free(hist); free(drafts);
+    return n;
+}
+
 /* ------------------------------------------------------------------ tensor parallel */
 /* tp.rs:641-660 validate_shares + tp.rs:662-701 shard_geometry.
  * out: q_start q_heads kv_start kv_heads ffn_start ffn_len head_row_start head_rows. */

@@ -58,6 +58,8 @@ def lib():
         "orc_prefill_batch": (None, [P, P, I, I, P]),
         "orc_compute_logits": (None, [P, P, P]),
         "orc_spec_generate": (I, [P, P, P, I, I, I, P, P]),
+        "orc_ngram_draft": (I, [P, I, I, I, I, P]),
+        "orc_ngram_generate": (I, [P, P, I, I, I, I, I, I, P, P]),
         "orc_model_buf": (P, [P, I, I]),
         "orc_shard_geometry": (I, [I, I, I, I, P, I, I, P]),
         "orc_tp_build": (P, [P, P, I]),
@@ -146,6 +148,22 @@ def spec_generate(target, draft, prompt, n_gen, k):
     out = np.zeros(n_gen, dtype=np.int32)
     stats = np.zeros(2, dtype=np.int32)
     n = lib().orc_spec_generate(target.h, draft.h, ptr(p), len(p), n_gen, k, ptr(out), ptr(stats))
+    return [int(v) for v in out[:n]], (int(stats[0]), int(stats[1]))
+
+
+def ngram_draft(history, max_tokens, max_ngram=4, min_ngram=3):
+    h = np.asarray(history, dtype=np.int32)
+    out = np.zeros(max(1, max_tokens), dtype=np.int32)
+    n = lib().orc_ngram_draft(ptr(h), len(h), max_tokens, max_ngram, min_ngram, ptr(out))
+    return [int(v) for v in out[:n]]
+
+
+def ngram_generate(target, prompt, n_gen, k=4, max_ngram=4, min_ngram=3, max_batch=8):
+    p = np.asarray(prompt, dtype=np.int32)
+    out = np.zeros(max(1, n_gen), dtype=np.int32)
+    stats = np.zeros(2, dtype=np.int32)
+    n = lib().orc_ngram_generate(target.h, ptr(p), len(p), n_gen, k, max_ngram, min_ngram, max_batch, ptr(out),
+                                 ptr(stats))
     return [int(v) for v in out[:n]], (int(stats[0]), int(stats[1]))
 
 

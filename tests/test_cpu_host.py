@@ -222,3 +222,47 @@ def test_rank_ordered_sum_and_per_row_head_merge():
     got = tp.rank_ordered(pairs, PHASE_HEAD)
     assert got[0::2].tolist() == [3.0, 5.0, 9.0]
     assert got.view(np.int32)[1::2].tolist() == [101, 2, 203]
+
+
+# ---------------------------------------------------------------- n-gram drafter
+NGRAM_KATS = [   # speculative.rs:561-595: (history, max_tokens, max_ngram, min_ngram, draft)
+    ([1, 2, 3, 4, 5, 6, 9, 9, 1, 2, 3, 4], 3, 4, 3, [5, 6, 9]),
+    ([3, 4, 7, 0, 3, 4, 8, 0, 3, 4], 2, 4, 3, [8, 0]),
+    ([1, 2, 3, 4, 5], 4, 4, 3, []),
+    ([1, 2], 4, 4, 3, []),
+    ([], 4, 4, 3, []),
+    ([1, 2, 9, 8, 7, 6, 1, 2], 2, 3, 2, [9, 8]),
+    ([1, 2, 9, 8, 7, 6, 1, 2], 10, 3, 2, [9, 8, 7, 6, 1, 2]),
+]
+
+
+@pytest.mark.parametrize("kat", NGRAM_KATS)
+def test_ngram_draft_reference_vectors(ncm, orc, kat):
+    """NGramDrafter::draft (speculative.rs:80-105) on the reference's own test vectors,
+    for the library's host drafter and the oracle's restatement."""
+    history, max_tokens, max_n, min_n, want = kat
+    assert ncm.ngram_draft(history, max_tokens, max_n, min_n) == want
+    assert orc.ngram_draft(history, max_tokens, max_n, min_n) == want
+
+
+def test_ngram_draft_matches_oracle_on_random_histories(ncm, orc):
+    rng = np.random.default_rng(11)
+    for trial in range(400):
+        h = [int(v) for v in rng.integers(0, int(rng.integers(2, 6)), size=int(rng.integers(0, 40)))]
+        max_tokens, max_n = int(rng.integers(1, 9)), int(rng.integers(1, 6))
+        min_n = int(rng.integers(1, max_n + 1))
+        assert ncm.ngram_draft(h, max_tokens, max_n, min_n) == orc.ngram_draft(h, max_tokens, max_n, min_n), trial
+
+
+def test_oracle_ngram_generate_equals_greedy(ncm, orc, tmp_path):
+    """ngram_speculative_step (speculative.rs:122-297): the emitted stream is the plain
+    greedy loop's."""
+    sp = tiny(ncm, seed=13)
+    path = tmp_path / "m.gguf"
+    ncm.write_synthetic_gguf(path, sp)
+    prompt = [5, 9, 2, 7, 5, 9, 2, 7, 5, 9]
+    greedy = orc.OracleModel(path).generate(prompt, 20)[0]
+    for k in (1, 4):
+        toks, (drafted, accepted) = orc.ngram_generate(orc.OracleModel(path), prompt, 20, k)
+        assert toks == greedy, k
+        assert 0 <= accepted <= drafted

@@ -145,3 +145,22 @@ def test_batched_prefill_equals_token_by_token(ncm, cuda, variant):
             assert np.array_equal(ka.view(np.uint32), kb.view(np.uint32)), (layer, which)
     for i in range(1, len(ga)):   # the decode after the prompt continues identically
         assert b.forward_pass(ga[i - 1], len(prompt) + i - 1)[0] == ga[i], i
+
+
+@pytest.mark.parametrize("k", [1, 4, 8])
+def test_ngram_generate_equals_greedy_and_oracle(ncm, orc, cuda, tmp_path, k):
+    """Prompt-lookup speculation (speculative.rs:122-297, main.rs:9720-9760): t0 and the
+    history drafts verified in one multi-row pass; tokens equal the greedy decode, and
+    tokens and drafted / accepted counts equal the oracle's restatement."""
+    sp = tiny(ncm, seed=21)
+    prompt = [308, 799, 395, 620, 308, 799, 395, 620, 308, 799, 395, 620, 308]
+    n_gen = 40
+    greedy = ncm.Model.synthetic(sp, device=0).generate(prompt, n_gen)
+    toks, stats = ncm.Model.synthetic(sp, device=0).ngram_generate(prompt, n_gen, k=k)
+    assert toks == greedy
+    path = tmp_path / "m.gguf"
+    ncm.write_synthetic_gguf(path, sp)
+    ref, ref_stats = orc.ngram_generate(orc.OracleModel(path), prompt, n_gen, k)
+    assert toks == ref
+    assert stats == ref_stats
+    assert stats[0] > stats[1] > 0   # drafts accepted and one rejected (corrective step)
