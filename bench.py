@@ -311,6 +311,13 @@ def run_spec(args, ncm):
     greedy = ref.generate(prompt, n_gen)
     torch.cuda.synchronize()
     dt_greedy = time.perf_counter() - t0
+    # prompt-lookup drafting (the reference's default draft source) on the same target
+    target.reset()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ng_toks, (ng_drafted, ng_accepted) = target.ngram_generate(prompt, n_gen, k=k)
+    torch.cuda.synchronize()
+    dt_ngram = time.perf_counter() - t0
     vms, step_ms = verify_times(ncm, target, n_prompt)
     print(json.dumps({"metric": "bs1 speculative decode tok/s", "value": round(n_gen / dt_spec, 2), "unit": "tok/s",
                       "n_gpus": 1, "higher_is_better": True, "data": "synthetic",
@@ -319,6 +326,8 @@ def run_spec(args, ncm):
                       "acceptance": round(accepted / max(1, drafted), 4), "drafted": drafted, "accepted": accepted,
                       "target_greedy_tok_s": round(n_gen / dt_greedy, 2), "tokens_equal_greedy": toks == greedy,
                       "verify_ms_by_rows": vms, "target_step_ms": step_ms,
+                      "ngram": {"tok_s": round(n_gen / dt_ngram, 2), "drafted": ng_drafted, "accepted": ng_accepted,
+                                "tokens_equal_greedy": ng_toks == greedy},
                       "timing": "wall clock around the call (prefill included), synchronous"}))
 
 
