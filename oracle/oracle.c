@@ -31,7 +31,7 @@
 
 #define QK 32
 #define QKK 256
-enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12 };
+enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
 
 /* ------------------------------------------------------------------ f16 */
 /* q8.rs:3599-3622 f16_bits_to_f32 (exact, subnormals normalised). */
@@ -85,8 +85,10 @@ static int32_t sat_i32(float f) {
 static float rd16(const uint8_t* p) { return orc_f16_to_f32((uint16_t)(p[0] | (p[1] << 8))); }
 
 /* ------------------------------------------------------------------ block formats */
-size_t orc_block_bytes(int t) { return t == T_Q4_0 ? 18 : t == T_Q8_0 ? 34 : t == T_Q4_K ? 144 : t == T_F32 ? 4 : t == T_F16 ? 2 : 0; }
-size_t orc_block_elems(int t) { return t == T_Q4_K ? QKK : (t == T_Q4_0 || t == T_Q8_0) ? QK : 1; }
+size_t orc_block_bytes(int t) {
+    return t == T_Q4_0 ? 18 : t == T_Q8_0 ? 34 : t == T_Q4_K ? 144 : t == T_Q6_K ? 210 : t == T_F32 ? 4 : t == T_F16 ? 2 : 0;
+}
+size_t orc_block_elems(int t) { return (t == T_Q4_K || t == T_Q6_K) ? QKK : (t == T_Q4_0 || t == T_Q8_0) ? QK : 1; }
 
 /* q8.rs:539-546 Q4_0Block::unpack_values: low nibble -> j, high nibble -> j+16, minus 8. */
 void orc_q4_0_unpack(const uint8_t* blk, int8_t out[32]) {
@@ -168,11 +170,63 @@ void orc_q4_k_dequant(const uint8_t* blk, float out[256]) {
     }
 }
 
-/* model.rs:1109-1132 load_f32_or_f16 for Q8_0 / Q4_0 / Q4_K / F32 / F16 rows. */
+/* q8.rs:2026-2090 Q6KBlock: ql[128] | qh[64] | scales i8[16] | d f16.  Each 128-value
+ * half n holds four 32-lanes: q1 (ql low nibble, qh bits 0-1), q2 (ql+32 low, bits 2-3),
+ * q3 (ql high, bits 4-5), q4 (ql+32 high, bits 6-7), each minus 32; lane l of quarter
+ * j uses scale (n/128)*8 + j*2 + l/16. */
+static inline void q6k_quad(const uint8_t* blk, int half, int l, int q[4]) {
+    const uint8_t* ql = blk + half * 64;
+    const uint8_t qh = blk[128 + half * 32 + l];
+    q[0] = (int)(int8_t)((ql[l] & 0x0f) | ((qh & 0x03) << 4)) - 32;
+    q[1] = (int)(int8_t)((ql[l + 32] & 0x0f) | (((qh >> 2) & 0x03) << 4)) - 32;
+    q[2] = (int)(int8_t)((ql[l] >> 4) | (((qh >> 4) & 0x03) << 4)) - 32;
+    q[3] = (int)(int8_t)((ql[l + 32] >> 4) | (((qh >> 6) & 0x03) << 4)) - 32;
+}
+
+/* q8.rs:2056-2090 dequantize: out = d * scale * q (left to right). */
+void orc_q6_k_dequant(const uint8_t* blk, float out[256]) {
+    const float d = rd16(blk + 208);
+    const int8_t* sc = (const int8_t*)(blk + 192);
+    for (int half = 0; half < 2; ++half)
+        for (int l = 0; l < 32; ++l) {
+            int q[4]; q6k_quad(blk, half, l, q);
+            for (int j = 0; j < 4; ++j)
+                out[half * 128 + j * 32 + l] = d * (float)sc[half * 8 + l / 16 + 2 * j] * (float)q[j];
+        }
+}
+
+/* q8.rs:2092-2150 dot_q8_scaled (the x86 path of inference.rs:3074-3086): per
+ * 128-half, c[j][h] = (d * scale) * x_scale; then one f32 sum over the 256 products
+ * (c * q) * x in the order l = 0..15 (low scales) then 16..31 (high scales), and
+ * within each l the quarters q1..q4. */
+float orc_q6_k_dot(const uint8_t* blk, const int8_t* x, const float* xs) {
+    const float d = rd16(blk + 208);
+    const int8_t* sc = (const int8_t*)(blk + 192);
+    float ws[16];
+    for (int i = 0; i < 16; ++i) ws[i] = d * (float)sc[i];
+    float sum = 0.0f;
+    for (int half = 0; half < 2; ++half) {
+        const int n = half * 128, so = half * 8, xo = n / 32;
+        float c[4][2];
+        for (int j = 0; j < 4; ++j) {
+            c[j][0] = ws[so + 2 * j] * xs[xo + j];
+            c[j][1] = ws[so + 2 * j + 1] * xs[xo + j];
+        }
+        for (int l = 0; l < 32; ++l) {
+            int q[4]; q6k_quad(blk, half, l, q);
+            const int hi = l >= 16;
+            for (int j = 0; j < 4; ++j) sum += c[j][hi] * (float)q[j] * (float)x[n + j * 32 + l];
+        }
+    }
+    return sum;
+}
+
+/* model.rs:1109-1132 load_f32_or_f16 for Q8_0 / Q4_0 / Q4_K / Q6_K / F32 / F16 rows. */
 void orc_dequant_row(int t, const uint8_t* row, int cols, float* out) {
     if (t == T_F32) { memcpy(out, row, (size_t)cols * 4); return; }
     if (t == T_F16) { for (int i = 0; i < cols; ++i) out[i] = rd16(row + 2 * i); return; }
     if (t == T_Q4_K) { for (int b = 0; b < cols / QKK; ++b) orc_q4_k_dequant(row + (size_t)b * 144, out + b * QKK); return; }
+    if (t == T_Q6_K) { for (int b = 0; b < cols / QKK; ++b) orc_q6_k_dequant(row + (size_t)b * 210, out + b * QKK); return; }
     int nb = cols / QK;
     for (int b = 0; b < nb; ++b) {
         const uint8_t* blk = row + (size_t)b * orc_block_bytes(t);
@@ -270,6 +324,10 @@ static float row_dot(int t, const uint8_t* row, int cols, const int8_t* xq, cons
     float sum = 0.0f;
     if (t == T_Q4_K) {
         for (int b = 0; b < cols / QKK; ++b) sum += orc_q4_k_dot(row + (size_t)b * 144, xq + b * QKK, xs + b * 8);
+        return sum;
+    }
+    if (t == T_Q6_K) {   /* inference.rs:3074-3086 */
+        for (int b = 0; b < cols / QKK; ++b) sum += orc_q6_k_dot(row + (size_t)b * 210, xq + b * QKK, xs + b * 8);
         return sum;
     }
     size_t bb = orc_block_bytes(t);

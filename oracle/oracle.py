@@ -42,6 +42,8 @@ def lib():
         "orc_block_dots": (None, [I, P, L64, I, P, P]),
         "orc_block_dot": (ctypes.c_int32, [I, P, P]),
         "orc_q4_k_dot": (F, [P, P, P]),
+        "orc_q6_k_dot": (F, [P, P, P]),
+        "orc_q6_k_dequant": (None, [P, P]),
         "orc_q4_0_unpack": (None, [P, P]),
         "orc_dequant_row": (None, [I, P, I, P]),
         "orc_rms_norm": (None, [P, P, P, I, F]),
@@ -79,8 +81,8 @@ def ptr(a):
     return a.ctypes.data_as(ctypes.c_void_p)
 
 
-BLOCK_BYTES = {2: 18, 8: 34, 12: 144}
-BLOCK_ELEMS = {2: 32, 8: 32, 12: 256}
+BLOCK_BYTES = {2: 18, 8: 34, 12: 144, 14: 210}
+BLOCK_ELEMS = {2: 32, 8: 32, 12: 256, 14: 256}
 
 
 def quantize_q8_0(x):

@@ -226,3 +226,46 @@ def test_argmax_first_max(orc):
     """inference.rs:4834-4845: strict '>' scan keeps the first maximum."""
     x = np.array([1.0, 3.0, 2.0, 3.0, -1.0], dtype=np.float32)
     assert orc.lib().orc_argmax(orc.ptr(x), x.size) == 1
+
+
+# ---------------------------------------------------------------- Q6_K (oracle ahead of the GPU kernel)
+def _q6_k_block(scale_bits, seed):
+    """inference.rs:5589-5603 q6_k_block: ql[i] = (seed + 5i) mod 256, qh[i] = (seed + 7i)
+    mod 256, scales[i] = (seed + 3i) mod 15 - 7, d = scale_bits."""
+    i = np.arange(128)
+    ql = ((seed + i * 5) % 256).astype(np.uint8)
+    qh = ((seed + np.arange(64) * 7) % 256).astype(np.uint8)
+    sc = (((seed + np.arange(16) * 3) % 15) - 7).astype(np.int8)
+    return np.concatenate([ql, qh, sc.view(np.uint8), np.array([scale_bits & 0xFF, scale_bits >> 8], np.uint8)])
+
+
+def test_q6_k_dequant_layout(orc):
+    """q8.rs:4646-4666: ql[0] = 0x10, ql[32] = 0x02, qh[0] = 0b11_10_01_00, scales 1,
+    d = 1.0 -> values[0] = -32, [32] = -14, [64] = 1, [96] = 16."""
+    blk = np.zeros(210, dtype=np.uint8)
+    blk[0], blk[32], blk[128] = 0x10, 0x02, 0b11100100
+    blk[192:208] = 1
+    blk[208], blk[209] = 0x00, 0x3c
+    out = np.zeros(256, dtype=np.float32)
+    orc.lib().orc_q6_k_dequant(orc.ptr(blk), orc.ptr(out))
+    assert (out[0], out[32], out[64], out[96]) == (-32.0, -14.0, 1.0, 16.0)
+
+
+def test_q6_k_matmul_matches_dequantized(orc):
+    """inference.rs:6605-6640: rows 2, cols 512, x = (5i % 61) - 30, x scales 0.125 +
+    i/32; the row sums agree with the dequantized reference within 1e-4."""
+    rows, cols = 2, 512
+    w = np.concatenate([_q6_k_block(b, s) for b, s in ((0x3800, 1), (0x3c00, 2), (0x4000, 3), (0x4200, 4))])
+    x = ((np.arange(cols) * 5) % 61 - 30).astype(np.int8)
+    xs = (0.125 + np.arange(cols // 32) * 0.03125).astype(np.float32)
+    got = orc.matmul(14, w, rows, cols, x, xs)
+    for r in range(rows):
+        s = np.float32(0.0)
+        for b in range(2):
+            vals = np.zeros(256, dtype=np.float32)
+            orc.lib().orc_q6_k_dequant(orc.ptr(np.ascontiguousarray(w[(r * 2 + b) * 210:(r * 2 + b + 1) * 210])),
+                                       orc.ptr(vals))
+            for i in range(256):
+                xi = b * 256 + i
+                s = np.float32(s + np.float32(np.float32(vals[i] * np.float32(x[xi])) * xs[xi // 32]))
+        assert abs(float(got[r]) - float(s)) < 1e-4, (r, got[r], s)
