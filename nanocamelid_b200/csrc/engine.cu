@@ -50,6 +50,8 @@ struct Nccl {
     int (*AllGather)(const void*, void*, size_t, int, nccl_comm, cudaStream_t) = nullptr;
     int (*CommDestroy)(nccl_comm) = nullptr;
     bool load() {
+        static std::mutex mu;
+        std::lock_guard<std::mutex> lock(mu);
         if (h) return true;
         const char* names[] = {"libnccl.so.2", "libnccl.so"};
         for (auto n : names) {

@@ -25,32 +25,49 @@
 #include <stdint.h>
 #include <math.h>
 #include <algorithm>
+#include <mutex>
+#include <set>
+#include <utility>
 #include "ncm_internal.h"
 #include "common.cuh"
 #include "synth.h"
 
 namespace ncm {
 
-static int g_num_sms = 0;
 int num_sms() {
-    if (!g_num_sms) {
-        int dev = 0;
+    // every device of a B200 box has the same count; first call wins (thread-safe init)
+    static const int n = [] {
+        int dev = 0, v = 0;
         cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (g_num_sms <= 0) g_num_sms = 148;
-    }
-    return g_num_sms;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        return v > 0 ? v : 148;
+    }();
+    return n;
+}
+
+// Raises a kernel's dynamic shared-memory limit once per (kernel, device): the attribute
+// is per device, and several host threads (one per shard) may launch at once.
+static int set_smem_limit(const void* fn, int bytes) {
+    static std::mutex mu;
+    static std::set<std::pair<const void*, int>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count({fn, dev})) return 0;
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done.insert({fn, dev});
+    return (int)e;
 }
 
 EncodeTiledFn encode_tiled_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
+    static const EncodeTiledFn fn = [] {   // thread-safe one-time lookup
         void* p = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = (EncodeTiledFn)p;
-    }
+            return (EncodeTiledFn)p;
+        return (EncodeTiledFn) nullptr;
+    }();
     return fn;
 }
 
@@ -1055,12 +1072,8 @@ int gemv_plan(int qtype, int cols, int rows, bool dual, int in_mode, GemvParams&
 
 template <int QT, int IN, int EPI>
 static int launch_t(const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
-    static bool configured = false;
     auto kern = gemv_kernel<QT, IN, EPI>;
-    if (!configured) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmemLimit);
-        configured = true;
-    }
+    if (int r = set_smem_limit((const void*)kern, kGemvSmemLimit)) return r;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kGemvThreads);
@@ -1253,12 +1266,8 @@ __global__ void __launch_bounds__(256) attn_softmax_v_kernel(const __grid_consta
 }
 
 int attention_launch(const AttnParams& a0, cudaStream_t s, bool pdl) {
-    static bool configured = false;
     constexpr int kMaxSmem = 200 * 1024;
-    if (!configured) {
-        cudaFuncSetAttribute(attn_softmax_v_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
-        configured = true;
-    }
+    if (int r = set_smem_limit((const void*)attn_softmax_v_kernel, kMaxSmem)) return r;
     AttnParams a = a0;
     const int g = a.heads / a.kv_heads, dw = a.hd / a.dsplit;
     const size_t wbytes = (size_t)((g * a.ctx + 3) & ~3) * sizeof(float);
@@ -1485,11 +1494,7 @@ __global__ void rms_norm_kernel(float* out, const float* x, const float* w, int 
 }
 int rms_norm_launch(float* out, const float* x, const float* w, int n, float eps, cudaStream_t s) {
     constexpr int kMaxStaged = 48 * 1024;   // floats (192 KB)
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxStaged * 4);
-        configured = true;
-    }
+    if (int r = set_smem_limit((const void*)rms_norm_kernel, kMaxStaged * 4)) return r;
     const int staged = n <= kMaxStaged;
     rms_norm_kernel<<<1, kThreads, staged ? (size_t)n * 4 : 0, s>>>(out, x, w, n, eps, staged);
     return (int)cudaGetLastError();
@@ -2067,12 +2072,8 @@ int batch_plan(int qtype, int cols, int rows, bool dual, int ntok, BatchParams& 
 
 template <int QT, int EPI>
 static int batch_launch_t(const BatchParams& p, int grid, cudaStream_t s, bool pdl) {
-    static bool configured = false;
     auto kern = gemv_batch_kernel<QT, EPI>;
-    if (!configured) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBatchSmemLimit);
-        configured = true;
-    }
+    if (int r = set_smem_limit((const void*)kern, kBatchSmemLimit)) return r;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kBatchThreads);
@@ -2177,12 +2178,8 @@ __global__ void __launch_bounds__(NT) batch_prep_kernel(const float* x, int x_st
 
 int batch_prep_launch(const float* x, int x_stride, int n, int ntok, const float* norm_w, float eps,
                       const float* ssq_tab, const int* toks, int8_t* xq, float* xs, cudaStream_t s, bool pdl) {
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(batch_prep_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
-        cudaFuncSetAttribute(batch_prep_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
-        configured = true;
-    }
+    if (int r = set_smem_limit((const void*)batch_prep_kernel<256>, 128 * 1024)) return r;
+    if (int r = set_smem_limit((const void*)batch_prep_kernel<512>, 128 * 1024)) return r;
     cudaLaunchAttribute attr[1];
     const int split = std::min(kPrepSplit, std::max(1, n / 32 / 64));
     const bool folds = norm_w && !ssq_tab;
