@@ -160,8 +160,10 @@ ncm_status ncm_forward_pass(ncm_model* m, int token, int pos, float* logits, int
 ncm_status ncm_generate(ncm_model* m, const int* prompt, int n_prompt, int n_gen, int* out_tokens);
 
 /* Device-resident decode: run `n` more greedy steps from the current position on
- * `stream` without host synchronisation (bench path).  ncm_sync_tokens copies the
- * token history [0, count) to host and checks the device error word. */
+ * `stream` without host synchronisation (bench path).  ncm_sync_tokens waits for the
+ * model's stream and for the last caller stream given to prefill / decode (which must
+ * stay valid until then), copies the token history [0, count) to host and checks the
+ * device error word. */
 ncm_status ncm_decode_steps(ncm_model* m, int n, void* stream);
 ncm_status ncm_prefill_tokens(ncm_model* m, const int* prompt, int n_prompt, void* stream);
 ncm_status ncm_sync_tokens(ncm_model* m, int* tokens, int count, int* pos_out);

@@ -100,6 +100,7 @@ struct ncm_model {
     float* embd_ssq = nullptr;   // per vocab row: sequential f32 sum of squares of the embedding
     int *state = nullptr, *tokens = nullptr, *err = nullptr;
     int* h_stage = nullptr;   // pinned staging for small transfers
+    cudaStream_t ext_stream = nullptr;   // caller stream of the last prefill / decode, until synced
     int dsplit = 1;   // attention value-accumulation CTAs per kv head
     std::vector<void*> allocs;
     cudaGraphExec_t g_full = nullptr, g_nohead = nullptr;
@@ -750,6 +751,7 @@ extern "C" ncm_status ncm_prefill_tokens(ncm_model* m, const int* prompt, int n_
     ncm_status s = ensure_graphs(m);
     if (s) return s;
     cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
+    if (stream) m->ext_stream = st;
     CK(cudaStreamSynchronize(st));
     if (n_prompt > 1 && (m->world == 1 || host_mode(m))) {
         // Eight prompt tokens per multi-row pass: every row's K/V and greedy token equal
@@ -783,6 +785,7 @@ extern "C" ncm_status ncm_decode_steps(ncm_model* m, int n, void* stream) {
     ncm_status s = ensure_graphs(m);
     if (s) return s;
     cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
+    if (stream) m->ext_stream = st;
     for (int i = 0; i < n; ++i)
         if ((s = run_step(m, true, st))) return s;
     return NCM_OK;
@@ -791,7 +794,13 @@ extern "C" ncm_status ncm_decode_steps(ncm_model* m, int n, void* stream) {
 extern "C" ncm_status ncm_sync_tokens(ncm_model* m, int* tokens, int count, int* pos_out) {
     if (!m) return fail(NCM_EINVAL, "null model");
     CK(cudaSetDevice(m->device));
-    CK(cudaDeviceSynchronize());
+    // this model's streams only: a device-wide sync would also wait on (and fail during)
+    // another host thread's graph capture on the same GPU
+    CK(cudaStreamSynchronize(m->stream));
+    if (m->ext_stream) {
+        CK(cudaStreamSynchronize(m->ext_stream));
+        m->ext_stream = nullptr;
+    }
     ncm_status s = check_err(m);
     if (s) return s;
     if (tokens && count > 0) CK(cudaMemcpy(tokens, m->tokens, 4 * (size_t)(count < m->ctx ? count : m->ctx), cudaMemcpyDeviceToHost));

@@ -233,6 +233,10 @@ def test_tp_speculative_with_host_reducer_on_one_gpu(ncm, orc, cuda, tmp_path, k
     ref = orc.OracleTP(orc.OracleModel(path), shares).generate(prompt, n_gen)
     models = [ncm.Model.load(path, device=0, shares=shares, shard=r) for r in range(2)]
     drafts = [ncm.Model.synthetic(dsp, device=0) for _ in range(2)]
+    for dm in drafts:   # capture every graph the drafts use (decode; 6- and 7-row prefill) up front
+        dm.generate(prompt[:-1], 2)
+        dm.generate(prompt, 2)
+        dm.reset()
     try:
         for m, fn in zip(models, _thread_reducers(2)):
             m.tp_set_host_reducer(fn)
