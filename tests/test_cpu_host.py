@@ -266,3 +266,28 @@ def test_oracle_ngram_generate_equals_greedy(ncm, orc, tmp_path):
         toks, (drafted, accepted) = orc.ngram_generate(orc.OracleModel(path), prompt, 20, k)
         assert toks == greedy, k
         assert 0 <= accepted <= drafted
+
+
+def _header_prototypes():
+    """{name: parameter count} for every function include/ncm.h declares."""
+    text = open(os.path.join(ROOT, "include", "ncm.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    protos = {}
+    for m in re.finditer(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_ \*]*?\b(ncm_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text,
+                         re.M | re.S):
+        args = m.group(2).strip()
+        protos[m.group(1)] = 0 if args in ("", "void") else args.count(",") + 1
+    return protos
+
+
+def test_python_bindings_match_header_arity(ncm):
+    """The ctypes mirror declares every header function with the header's parameter
+    count (guards the C ABI against drift)."""
+    protos = _header_prototypes()
+    assert len(protos) >= 30
+    L = ncm.lib()
+    for name, n in protos.items():
+        fn = getattr(L, name)
+        if fn.argtypes is None:
+            continue   # not used from Python
+        assert len(fn.argtypes) == n, (name, len(fn.argtypes), n)
