@@ -1,6 +1,7 @@
 """Decode benchmark: bs1 greedy decode tok/s on BASELINE.json configs[1] (Llama-3.2-3B
 shape, Q4_0, tied head, random-init N(0, 0.02), 64-token seeded prompt) at N GPUs of one
-node (tensor parallel with even KV-head shares, fused NVLink reduction).
+node (tensor parallel over KV-head shares -- even, or --shares such as 2,3,3 -- with the
+fused NVLink reduction).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {b200,reference}]
                   [--reducer {p2p,nccl}] [--config NAME]
@@ -33,6 +34,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--reducer", default="p2p", choices=["p2p", "nccl"])
+    ap.add_argument("--shares", default="", help="KV-head shares per rank, e.g. 2,3,3 (default: even, remainder last)")
     ap.add_argument("--config", default="cfg2_3b_q4_0")
     ap.add_argument("--prompt", type=int, default=64)
     ap.add_argument("--no-e2e", action="store_true")
@@ -89,14 +91,16 @@ class ClockSampler:
                 "reasons": reasons}
 
 
-def weight_bytes(sp, world):
-    """Algorithmic weight bytes read per decoded token, per GPU (largest shard)."""
+def weight_bytes(sp, world, shares=None):
+    """Algorithmic weight bytes read per decoded token, per GPU (the largest shard: its
+    KV-head fraction of every sharded matrix and of the vocab rows)."""
     bpw = {2: 18 / 32, 8: 34 / 32, 12: 144 / 256}
     H, F, hd = sp.emb, sp.ffn, sp.head_dim
     qw, kw = sp.heads * hd, sp.kv_heads * hd
     layer = (qw * H + 2 * kw * H + H * qw) * bpw[sp.t_attn] + 3 * F * H * bpw[sp.t_ffn]
     head = sp.vocab * H * (bpw[2] if sp.tied else bpw[sp.t_out])
-    return sp.layers * layer / world + head / world
+    frac = max(shares) / sp.kv_heads if shares else 1.0 / world
+    return (sp.layers * layer + head) * frac
 
 
 class OracleRun:
@@ -208,7 +212,12 @@ def run_b200(args, sp):
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    shares = tp.even_shares(sp.kv_heads, world) if world > 1 else None
+    if world > 1:
+        shares = [int(v) for v in args.shares.split(",")] if args.shares else tp.default_shares(sp.kv_heads, world)
+        if len(shares) != world:
+            raise SystemExit(f"--shares lists {len(shares)} ranks for {world} processes")
+    else:
+        shares = None
     ctx = args.prompt + args.warmup + args.steps + 8
     m = ncm.Model.synthetic(sp, ctx_limit=ctx, device=local, shares=shares, shard=rank)
     if world > 1:
@@ -265,7 +274,7 @@ def run_b200(args, sp):
             os.path.join(ROOT, "MEASURED_PEAKS.json")) else {"hbm_gbs": 6650.0}
         peak = float(peaks.get("hbm_gbs", 6650.0))
         roof = gemv_roofline(torch, ncm, sp, peak)
-        bpt = weight_bytes(sp, world)
+        bpt = weight_bytes(sp, world, shares)
         whole = {"bytes_per_token_per_gpu": int(bpt), "achieved_gbs": round(bpt * tok_s / 1e9, 1),
                  "frac_of_measured_hbm": round(bpt * tok_s / 1e9 / peak, 4)}
         cpu = None if (args.no_cpu or world > 1) else cpu_sample(sp)
@@ -276,6 +285,7 @@ def run_b200(args, sp):
                 "config": {"workload": args.config, "prompt": args.prompt, "decode_positions":
                            f"{args.prompt + args.warmup}..{args.prompt + args.warmup + args.steps - 1}",
                            "parallelism": f"tp{world}", "reducer": args.reducer if world > 1 else None,
+                           "shares": shares,
                            "l2": "inputs larger than L2 (weights %.2f GB/token/GPU)" % (bpt / 1e9)},
                 "roofline": roof, "decode_roofline": whole, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": launches_per_step * args.steps, "clocks": clk.summary()}

@@ -19,6 +19,15 @@ def even_shares(kv_heads, world):
     return [kv_heads // world] * world
 
 
+def default_shares(kv_heads, world):
+    """Even KV-head shares where world divides the KV heads, else the remainder on the
+    last ranks (8 heads over 3 ranks -> [2, 3, 3], the reference's uneven plan)."""
+    if world < 1 or world > kv_heads:
+        raise ValueError(f"{world} ranks for {kv_heads} kv heads")
+    base, rem = divmod(kv_heads, world)
+    return [base + (1 if r >= world - rem else 0) for r in range(world)]
+
+
 def exchange(obj, world, group=None):
     """All-gather of one picklable object per rank, in rank order (handles, plans)."""
     out = [None] * world

@@ -61,6 +61,19 @@ def test_even_shares():
         tp.even_shares(8, 3)
 
 
+def test_default_shares_even_or_remainder_last(ncm):
+    from nanocamelid_b200 import tp
+    assert tp.default_shares(8, 3) == [2, 3, 3]
+    assert tp.default_shares(8, 8) == [1] * 8 and tp.default_shares(8, 2) == [4, 4]
+    assert tp.default_shares(8, 5) == [1, 1, 2, 2, 2]
+    for world in range(1, 9):   # every default plan is one validate_shares accepts
+        sh = tp.default_shares(8, world)
+        for i in range(world):
+            ncm.shard_geometry(32, 8, 14336, 128256, sh, i)
+    with pytest.raises(ValueError):
+        tp.default_shares(8, 9)
+
+
 # ---------------------------------------------------------------- GGUF
 GGUF_SCALAR = {0: 1, 1: 1, 2: 2, 3: 2, 4: 4, 5: 4, 6: 4, 7: 1, 10: 8, 11: 8, 12: 8}
 
