@@ -1436,21 +1436,39 @@ extern "C" ncm_status ncm_quantize_f32_to_q8_0(const float* x, int n, int8_t* x_
     return NCM_OK;
 }
 
-// Strict GEMV over caller-owned raw blocks; rows whose byte length is not a multiple of
-// 16 (or an unaligned base) are first copied into a 16-byte-pitched scratch so that the
-// TMA engine can address them.
+// Stream-ordered device scratch, freed (stream-ordered) when the scope ends, early
+// returns included.
+struct AsyncScratch {
+    uint8_t* p = nullptr;
+    cudaStream_t s = nullptr;
+    ~AsyncScratch() {
+        if (p) cudaFreeAsync(p, s);
+    }
+};
+
+// Caller-owned raw block rows as the kernels address them: rows whose byte length is not
+// a multiple of `align` (or an unaligned base) are copied into a 16-byte-pitched scratch.
+static ncm_status addressable_rows(const void* w, int64_t rows, int rb, int align, cudaStream_t s, AsyncScratch& tmp,
+                                   const uint8_t** base, int64_t* pitch) {
+    *base = (const uint8_t*)w;
+    *pitch = rb;
+    if (rb % align == 0 && ((uintptr_t)w % align) == 0) return NCM_OK;
+    *pitch = (rb + 15) / 16 * 16;
+    tmp.s = s;
+    CK(cudaMallocAsync((void**)&tmp.p, (size_t)*pitch * rows, s));
+    CK(cudaMemcpy2DAsync(tmp.p, (size_t)*pitch, w, rb, rb, rows, cudaMemcpyDeviceToDevice, s));
+    *base = tmp.p;
+    return NCM_OK;
+}
+
+// Strict GEMV over caller-owned raw blocks (TMA: 16-byte row pitch).
 static ncm_status seam_gemv(int qtype, const void* w, int64_t rows, int cols, const int8_t* x_i8,
                             const float* x_scales, float* out, cudaStream_t s) {
-    const int rb = row_bytes(qtype, cols);
-    const uint8_t* base = (const uint8_t*)w;
-    int pitch = rb;
-    uint8_t* tmp = nullptr;
-    if (rb % 16 || !aligned16(w)) {
-        pitch = (rb + 15) / 16 * 16;
-        CK(cudaMallocAsync((void**)&tmp, (size_t)pitch * rows, s));
-        CK(cudaMemcpy2DAsync(tmp, pitch, w, rb, rb, rows, cudaMemcpyDeviceToDevice, s));
-        base = tmp;
-    }
+    AsyncScratch tmp;
+    const uint8_t* base = nullptr;
+    int64_t pitch = 0;
+    ncm_status st = addressable_rows(w, rows, row_bytes(qtype, cols), 16, s, tmp, &base, &pitch);
+    if (st) return st;
     GemvParams p;
     memset(&p, 0, sizeof p);
     p.nseg = 1;
@@ -1459,9 +1477,9 @@ static ncm_status seam_gemv(int qtype, const void* w, int64_t rows, int cols, co
     p.xs = x_scales;
     p.tp.world = 1;
     const int grid = gemv_plan(qtype, cols, (int)rows, false, IN_Q8, p);
-    int r = grid < 0 ? (int)cudaErrorInvalidValue : gemv_tensor_map(&p.tm[0], base, rows, pitch, p.chunk_words, p.box_rows);
+    int r = grid < 0 ? (int)cudaErrorInvalidValue
+                     : gemv_tensor_map(&p.tm[0], base, rows, (int)pitch, p.chunk_words, p.box_rows);
     if (!r) r = gemv_launch(qtype, IN_Q8, EPI_PLAIN, p, grid, s, false);
-    if (tmp) cudaFreeAsync(tmp, s);
     if (r) return fail(NCM_ECUDA, std::string("gemv launch: ") + cudaGetErrorString((cudaError_t)r));
     return NCM_OK;
 }
@@ -1478,8 +1496,9 @@ extern "C" ncm_status ncm_matmul_quantized(int qtype, const void* w, int64_t row
     return seam_gemv(qtype, w, rows, cols, x_i8, x_scales, out, (cudaStream_t)stream);
 }
 
-// inference.rs:1246-1303: every token's row uses the single-token formula, so the batch
-// is ntok single-token GEMVs (bit-identical per token by construction).
+// inference.rs:1246-1303: every token's row uses the single-token formula; the int8
+// tensor-core kernel forms the same integer dots and f32 terms, folded in block order,
+// so every row is bit-identical to ncm_matmul_quantized of that row.
 extern "C" ncm_status ncm_matmul_quantized_batch(int qtype, const void* w, int64_t rows, int cols, int ntok,
                                                 const int8_t* x_i8, const float* x_scales, float* out, void* stream) {
     if (ntok < 1 || ntok > kMaxBatch) return fail(NCM_EINVAL, "1 <= ntok <= 8");
@@ -1488,19 +1507,12 @@ extern "C" ncm_status ncm_matmul_quantized_batch(int qtype, const void* w, int64
         return fail(NCM_EINVAL, "bad shape");
     if (!w || !x_i8 || !x_scales || !out) return fail(NCM_EINVAL, "null pointer");
     if ((uintptr_t)x_i8 & 15) return fail(NCM_EINVAL, "x_i8 must be 16-byte aligned");
-    // rows whose byte length is not a multiple of 16 (or an unaligned base) are copied
-    // into a 16-byte-pitched scratch so that the TMA engine can address them
     cudaStream_t st = (cudaStream_t)stream;
-    const int rb = row_bytes(qtype, cols);
-    const uint8_t* base = (const uint8_t*)w;
-    int pitch = rb;
-    uint8_t* tmp = nullptr;
-    if (rb % 16 || !aligned16(w)) {
-        pitch = (rb + 15) / 16 * 16;
-        CK(cudaMallocAsync((void**)&tmp, (size_t)pitch * rows, st));
-        CK(cudaMemcpy2DAsync(tmp, pitch, w, rb, rb, rows, cudaMemcpyDeviceToDevice, st));
-        base = tmp;
-    }
+    AsyncScratch tmp;
+    const uint8_t* base = nullptr;
+    int64_t pitch = 0;
+    ncm_status s = addressable_rows(w, rows, row_bytes(qtype, cols), 16, st, tmp, &base, &pitch);
+    if (s) return s;
     BatchParams p;
     memset(&p, 0, sizeof p);
     p.nseg = 1;
@@ -1510,18 +1522,9 @@ extern "C" ncm_status ncm_matmul_quantized_batch(int qtype, const void* w, int64
     p.xq = x_i8;
     p.xs = x_scales;
     const int grid = batch_plan(qtype, cols, (int)rows, false, ntok, p);
-    if (grid < 0) {
-        if (tmp) cudaFreeAsync(tmp, st);
-        return fail(NCM_EUNSUPPORTED, "activation rows do not fit in shared memory");
-    }
-    int* err = nullptr;
-    CK(cudaMallocAsync((void**)&err, 4, st));
-    CK(cudaMemsetAsync(err, 0, 4, st));
-    p.err = err;
-    int r = gemv_tensor_map(&p.tm[0], base, rows, pitch, p.chunk_words, p.box_rows);
+    if (grid < 0) return fail(NCM_EUNSUPPORTED, "activation rows do not fit in shared memory");
+    int r = gemv_tensor_map(&p.tm[0], base, rows, (int)pitch, p.chunk_words, p.box_rows);
     if (!r) r = batch_gemv_launch(qtype, EPI_PLAIN, p, grid, st, false);
-    cudaFreeAsync(err, st);
-    if (tmp) cudaFreeAsync(tmp, st);
     if (r) return fail(NCM_ECUDA, std::string("batch gemv launch: ") + cudaGetErrorString((cudaError_t)r));
     return NCM_OK;
 }
@@ -1536,18 +1539,12 @@ extern "C" ncm_status ncm_block_dots(int qtype, const void* w, int64_t rows, int
     // The unit code loads 32-bit words: rows of an odd block count (Q4_0 / Q8_0 rows of
     // 18 / 34 bytes per block) are re-pitched to 16 bytes first, as in the GEMV seam.
     cudaStream_t s = (cudaStream_t)stream;
-    const int rb = row_bytes(qtype, cols);
-    const uint8_t* base = (const uint8_t*)w;
-    int64_t pitch = rb;
-    uint8_t* tmp = nullptr;
-    if (rb % 4) {
-        pitch = (rb + 15) / 16 * 16;
-        CK(cudaMallocAsync((void**)&tmp, (size_t)pitch * rows, s));
-        CK(cudaMemcpy2DAsync(tmp, pitch, w, rb, rb, rows, cudaMemcpyDeviceToDevice, s));
-        base = tmp;
-    }
+    AsyncScratch tmp;
+    const uint8_t* base = nullptr;
+    int64_t pitch = 0;
+    ncm_status st = addressable_rows(w, rows, row_bytes(qtype, cols), 4, s, tmp, &base, &pitch);
+    if (st) return st;
     const int r = block_dots_launch(qtype, base, rows, cols, pitch, x_i8, out, s);
-    if (tmp) cudaFreeAsync(tmp, s);
     if (r) return fail(NCM_ECUDA, std::string("block dots launch: ") + cudaGetErrorString((cudaError_t)r));
     return NCM_OK;
 }
