@@ -21,8 +21,14 @@ struct Rd {
     const uint8_t* p;
     const uint8_t* end;
     bool err = false;
+    uint64_t left() const { return (uint64_t)(end - p); }
+    bool take(uint64_t n) {   // advance n bytes, or flag a truncated file
+        if (err || n > left()) { err = true; return false; }
+        p += n;
+        return true;
+    }
     uint64_t u(int n) {
-        if (p + n > end) { err = true; return 0; }
+        if (err || (uint64_t)n > left()) { err = true; return 0; }
         uint64_t v = 0;
         for (int i = 0; i < n; ++i) v |= (uint64_t)p[i] << (8 * i);
         p += n;
@@ -30,7 +36,7 @@ struct Rd {
     }
     std::string str() {
         uint64_t n = u(8);
-        if (p + n > end) { err = true; return {}; }
+        if (err || n > left()) { err = true; return {}; }
         std::string s((const char*)p, n);
         p += n;
         return s;
@@ -45,17 +51,26 @@ int vsize(int t) {
         default: return -1;
     }
 }
-void skip(Rd& r, int t) {
+// Skips one value of type t; arrays nest at most 4 deep and fixed-size element runs are
+// skipped in one bounds-checked step (a corrupt count cannot loop or recurse for long).
+void skip(Rd& r, int t, int depth = 0) {
     if (t == 8) { r.str(); return; }
     if (t == 9) {
         int et = (int)r.u(4);
         uint64_t n = r.u(8);
-        for (uint64_t i = 0; i < n && !r.err; ++i) skip(r, et);
+        if (r.err || depth >= 4) { r.err = true; return; }
+        const int es = vsize(et);
+        if (es > 0) {
+            if (n > r.left() / (uint64_t)es) { r.err = true; return; }
+            r.take(n * (uint64_t)es);
+            return;
+        }
+        for (uint64_t i = 0; i < n && !r.err; ++i) skip(r, et, depth + 1);
         return;
     }
     int s = vsize(t);
     if (s < 0) { r.err = true; return; }
-    r.p += s;
+    r.take((uint64_t)s);
 }
 }  // namespace
 
@@ -134,13 +149,21 @@ bool GgufFile::open(const char* path, std::string& err) {
         if (!te || te->dims.size() != 2) { err = "cannot infer vocab"; return false; }
         vocab = (int)(te->dims[0] == (uint64_t)emb ? te->dims[1] : te->dims[0]);
     }
+    if (data_start > size) { err = "truncated GGUF header"; return false; }
     for (auto& t : tensors) {
         int be = ncm_type_block_elems(t.type), bb = ncm_type_block_bytes(t.type);
         if (bb == 0) continue;
+        // overflow-safe: the sized types take at least half a byte per element, so no
+        // element count in the file exceeds 64 x its size
+        const uint64_t lim = (uint64_t)size * 64;
         uint64_t el = 1;
-        for (auto d : t.dims) el *= d;
-        t.nbytes = el / be * bb;
-        if (data_start + t.offset + t.nbytes > size) { err = "tensor " + t.name + " overruns file"; return false; }
+        for (auto d : t.dims) {
+            if (d == 0 || d > lim || el > lim / d) { err = "tensor " + t.name + " has bad dimensions"; return false; }
+            el *= d;
+        }
+        t.nbytes = el / (uint64_t)be * (uint64_t)bb;
+        const uint64_t room = size - data_start;
+        if (t.offset > room || t.nbytes > room - t.offset) { err = "tensor " + t.name + " overruns file"; return false; }
     }
     return true;
 }

@@ -304,3 +304,48 @@ def test_python_bindings_match_header_arity(ncm):
         if fn.argtypes is None:
             continue   # not used from Python
         assert len(fn.argtypes) == n, (name, len(fn.argtypes), n)
+
+
+_FUZZ = r'''
+import ctypes, sys
+import numpy as np
+import nanocamelid_b200 as ncm
+raw = open(sys.argv[1], "rb").read()
+L = ncm.lib()
+def load(b):
+    open(sys.argv[2], "wb").write(b)
+    h = ctypes.c_void_p()
+    # device -1: parsing runs in full, then device selection fails before any allocation
+    return L.ncm_model_load(sys.argv[2].encode(), 0, -1, None, 0, 0, ctypes.byref(h))
+rng = np.random.default_rng(0)
+hdr = int(sys.argv[3])
+bad = []
+for cut in sorted(set(int(v) for v in np.linspace(0, len(raw) - 1, 60)) | set(range(0, hdr, max(1, hdr // 40)))):
+    s = load(raw[:cut])
+    if s != 5:
+        bad.append(("truncated", cut, s))
+for trial in range(300):
+    b = bytearray(raw[:hdr + 64])
+    for _ in range(int(rng.integers(1, 6))):
+        b[int(rng.integers(0, hdr))] = int(rng.integers(0, 256))
+    s = load(bytes(b) + raw[hdr + 64:])
+    if s not in (0, 1, 2, 5, 6):
+        bad.append(("corrupt", trial, s))
+print("BAD", bad)
+'''
+
+
+def test_gguf_reader_rejects_truncated_and_corrupt_files(ncm, tmp_path):
+    """The GGUF reader (gguf.rs:454-551 semantics) on hostile files: every truncation is
+    NCM_EIO, and random byte corruption of the header and tensor table ends in a status
+    (parse error, or a parse that then stops at device selection), never a crash."""
+    import subprocess
+    import sys
+    sp = tiny(ncm)
+    path = tmp_path / "m.gguf"
+    ncm.write_synthetic_gguf(path, sp)
+    hdr = min(read_gguf_tensors(path).values(), key=lambda v: v[2])[2]   # first tensor's data offset
+    r = subprocess.run([sys.executable, "-c", _FUZZ, str(path), str(tmp_path / "x.gguf"), str(hdr)],
+                       capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, (r.returncode, r.stderr[-2000:])
+    assert "BAD []" in r.stdout, r.stdout[-2000:]
