@@ -458,6 +458,92 @@ void orc_attention(float* out, const float* q, const float* kc, const float* vc,
     free(scores);
 }
 
+/* inference.rs:4298-4317 quantize_row_to_q8_0_blocks (the Q8_0 KV-cache store): per 32
+ * values scale = max|x|/127, inv = 1/scale (0 for a zero block), q = clamp(round(x*inv)),
+ * the scale stored as f16 with the truncating encode (q8.rs fast_f32_to_f16). */
+void orc_kv_quantize_row_q8_0(const float* x, int n, uint8_t* out) {
+    for (int b = 0; b < n / 32; ++b) {
+        const float* c = x + b * 32;
+        uint8_t* o = out + (size_t)b * 34;
+        float mx = 0.0f;
+        for (int i = 0; i < 32; ++i) { float a = fabsf(c[i]); if (a > mx) mx = a; }
+        float scale = mx / 127.0f, inv = scale > 0.0f ? 1.0f / scale : 0.0f;
+        uint16_t sb = orc_f32_to_f16(scale);
+        o[0] = sb & 0xff; o[1] = sb >> 8;
+        for (int i = 0; i < 32; ++i) {
+            float q = roundf(c[i] * inv);
+            q = q < -127.0f ? -127.0f : q > 127.0f ? 127.0f : q;
+            o[2 + i] = (uint8_t)(int8_t)q;
+        }
+    }
+}
+
+/* inference.rs:539-568 store_kv for the F16 cache: truncating f16 encode per value. */
+void orc_kv_store_f16(const float* x, int n, uint16_t* out) {
+    for (int i = 0; i < n; ++i) out[i] = orc_f32_to_f16(x[i]);
+}
+
+/* inference.rs:4242-4458 apply_attention_head over an F16 (kind 1) or Q8_0 (kind 2)
+ * cache; kind 0 is the f32 cache of orc_attention.
+ *   F16: each K / V head row is decoded to f32, then the f32 path (dot_f32, softmax,
+ *        add_weighted).
+ *   Q8_0: q_head is quantised like the store; score = (sum over blocks of
+ *        (s_q * s_k) * dot_i32) * scale; V blocks decoded as q * s, then add_weighted.
+ * `out` must be zeroed by the caller. */
+void orc_attention_kv(int kind, float* out, const float* q, const void* kc, const void* vc, int pos, int heads,
+                      int kv_heads, int hd, int kv_width) {
+    if (kind == 0) { orc_attention(out, q, (const float*)kc, (const float*)vc, pos, heads, kv_heads, hd, kv_width); return; }
+    int kv_mul = heads / kv_heads;
+    float scale = 1.0f / sqrtf((float)hd);
+    float* scores = malloc(sizeof(float) * (size_t)(pos + 1));
+    float* row = malloc(sizeof(float) * (size_t)hd);
+    uint8_t* qb = malloc((size_t)(hd / 32) * 34);
+    const int bph = hd / 32, bpw = kv_width / 32;
+    for (int h = 0; h < heads; ++h) {
+        int kvh = h / kv_mul;
+        const float* qh = q + h * hd;
+        if (kind == 2) orc_kv_quantize_row_q8_0(qh, hd, qb);
+        for (int p = 0; p <= pos; ++p) {
+            float sc;
+            if (kind == 1) {
+                const uint16_t* k = (const uint16_t*)kc + (size_t)p * kv_width + kvh * hd;
+                for (int d = 0; d < hd; ++d) row[d] = orc_f16_to_f32(k[d]);
+                float s = 0.0f;
+                for (int d = 0; d < hd; ++d) s += qh[d] * row[d];
+                sc = s;
+            } else {
+                const uint8_t* k = (const uint8_t*)kc + ((size_t)p * bpw + (size_t)kvh * bph) * 34;
+                float acc = 0.0f;
+                for (int b = 0; b < bph; ++b) {
+                    const uint8_t* kb = k + (size_t)b * 34;
+                    const uint8_t* qq = qb + (size_t)b * 34;
+                    int32_t dot = 0;
+                    for (int i = 0; i < 32; ++i) dot += (int32_t)(int8_t)qq[2 + i] * (int32_t)(int8_t)kb[2 + i];
+                    acc += rd16(qq) * rd16(kb) * (float)dot;   /* q8.rs:509-511 scaled_dot_f32 */
+                }
+                sc = acc;
+            }
+            scores[p] = sc * scale;
+        }
+        softmax(scores, pos + 1);
+        float* o = out + h * hd;
+        for (int p = 0; p <= pos; ++p) {
+            if (kind == 1) {
+                const uint16_t* v = (const uint16_t*)vc + (size_t)p * kv_width + kvh * hd;
+                for (int d = 0; d < hd; ++d) row[d] = orc_f16_to_f32(v[d]);
+            } else {
+                const uint8_t* v = (const uint8_t*)vc + ((size_t)p * bpw + (size_t)kvh * bph) * 34;
+                for (int b = 0; b < bph; ++b) {
+                    float sb = rd16(v + (size_t)b * 34);
+                    for (int i = 0; i < 32; ++i) row[b * 32 + i] = (float)(int8_t)v[(size_t)b * 34 + 2 + i] * sb;
+                }
+            }
+            for (int d = 0; d < hd; ++d) o[d] += scores[p] * row[d];
+        }
+    }
+    free(scores); free(row); free(qb);
+}
+
 /* inference.rs:4834-4845 sample_logits(temperature 0): first max, strict >. */
 int orc_argmax(const float* x, long n) {
     float mv = x[0]; long mi = 0;

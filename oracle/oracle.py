@@ -50,6 +50,9 @@ def lib():
         "orc_apply_rope": (None, [P, I, I, I, I, F]),
         "orc_silu_mul": (None, [P, P, P, I]),
         "orc_attention": (None, [P, P, P, P, I, I, I, I, I]),
+        "orc_attention_kv": (None, [I, P, P, P, P, I, I, I, I, I]),
+        "orc_kv_quantize_row_q8_0": (None, [P, I, P]),
+        "orc_kv_store_f16": (None, [P, I, P]),
         "orc_argmax": (I, [P, L64]),
         "orc_model_load": (P, [ctypes.c_char_p, I]),
         "orc_model_info": (I, [P, P]),

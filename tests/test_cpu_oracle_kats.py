@@ -269,3 +269,57 @@ def test_q6_k_matmul_matches_dequantized(orc):
                 xi = b * 256 + i
                 s = np.float32(s + np.float32(np.float32(vals[i] * np.float32(x[xi])) * xs[xi // 32]))
         assert abs(float(got[r]) - float(s)) < 1e-4, (r, got[r], s)
+
+
+# ---------------------------------------------------------------- F16 / Q8_0 KV caches (oracle ahead of the GPU)
+def _kv_case(hd):
+    heads, kvh, ctx, pos = 4, 2, 5, 4
+    kvw = kvh * hd
+    q = (np.arange(heads * hd, dtype=np.float32) * np.float32(0.017) - np.float32(0.25)).astype(np.float32)
+    k = (np.float32(0.5) - np.arange(ctx * kvw, dtype=np.float32) * np.float32(0.009)).astype(np.float32)
+    v = (np.arange(ctx * kvw, dtype=np.float32) * np.float32(0.013) - np.float32(0.4)).astype(np.float32)
+    return heads, kvh, kvw, pos, q, k, v
+
+
+def _attn(orc, kind, q, kc, vc, pos, heads, kvh, hd, kvw):
+    out = np.zeros(heads * hd, dtype=np.float32)
+    orc.lib().orc_attention_kv(kind, orc.ptr(out), orc.ptr(q), orc.ptr(kc), orc.ptr(vc), pos, heads, kvh, hd, kvw)
+    return out
+
+
+def test_f16_kv_attention_matches_decoded_cache(orc):
+    """inference.rs:5812-5880: attention over an F16 cache equals the f32 path over the
+    explicitly decoded cache (within 1e-6)."""
+    hd = 8
+    heads, kvh, kvw, pos, q, k, v = _kv_case(hd)
+    k16, v16 = np.zeros(k.size, np.uint16), np.zeros(v.size, np.uint16)
+    orc.lib().orc_kv_store_f16(orc.ptr(k), k.size, orc.ptr(k16))
+    orc.lib().orc_kv_store_f16(orc.ptr(v), v.size, orc.ptr(v16))
+    kd = np.array([orc.lib().orc_f16_to_f32(int(b)) for b in k16], dtype=np.float32)
+    vd = np.array([orc.lib().orc_f16_to_f32(int(b)) for b in v16], dtype=np.float32)
+    got = _attn(orc, 1, q, k16, v16, pos, heads, kvh, hd, kvw)
+    want = _attn(orc, 0, q, kd, vd, pos, heads, kvh, hd, kvw)
+    assert float(np.max(np.abs(got - want))) < 1e-6
+
+
+def test_q8_0_kv_attention_matches_dequantized_cache(orc):
+    """inference.rs:5886-5983: attention over a Q8_0 cache against the f32 path over the
+    dequantised cache; q is quantised too, so within 5e-2."""
+    hd = 32
+    heads, kvh, kvw, pos, q, k, v = _kv_case(hd)
+    kq, vq = np.zeros(k.size // 32 * 34, np.uint8), np.zeros(v.size // 32 * 34, np.uint8)
+    orc.lib().orc_kv_quantize_row_q8_0(orc.ptr(k), k.size, orc.ptr(kq))
+    orc.lib().orc_kv_quantize_row_q8_0(orc.ptr(v), v.size, orc.ptr(vq))
+
+    def deq(blocks):
+        b = blocks.reshape(-1, 34)
+        s = np.array([orc.lib().orc_f16_to_f32(int(x[0]) | (int(x[1]) << 8)) for x in b], dtype=np.float32)
+        return (b[:, 2:].view(np.int8).astype(np.float32) * s[:, None]).reshape(-1).astype(np.float32)
+
+    got = _attn(orc, 2, q, kq, vq, pos, heads, kvh, hd, kvw)
+    want = _attn(orc, 0, q, deq(kq), deq(vq), pos, heads, kvh, hd, kvw)
+    assert float(np.max(np.abs(got - want))) < 5e-2
+    # the store keeps the truncating f16 scale and round-half-away values
+    blk = kq[:34]
+    s = np.float32(np.max(np.abs(k[:32])) / np.float32(127.0))
+    assert (int(blk[0]) | (int(blk[1]) << 8)) == orc.lib().orc_f32_to_f16(s)
