@@ -35,8 +35,10 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--reducer", default="p2p", choices=["p2p", "nccl"])
     ap.add_argument("--shares", default="", help="KV-head shares per rank, e.g. 2,3,3 (default: even, remainder last)")
-    ap.add_argument("--config", default="cfg2_3b_q4_0")
-    ap.add_argument("--prompt", type=int, default=64)
+    ap.add_argument("--config", default="cfg4_70b_q4_0")
+    ap.add_argument("--prompt", type=int, default=None, help="context length (default: the config's, BASELINE.json)")
+    ap.add_argument("--layers", type=int, default=0, help="small case for profiler captures: fewer layers")
+    ap.add_argument("--vocab", type=int, default=0, help="small case for profiler captures: smaller vocab")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--spec", action="store_true",
@@ -103,57 +105,76 @@ def weight_bytes(sp, world, shares=None):
     return (sp.layers * layer + head) * frac
 
 
+# BASELINE.json prompt (context) length per config
+PROMPTS = {"cfg1_1b_q4_0": 16, "cfg2_3b_q4_0": 64, "cfg3_8b_mixed": 512, "cfg4_70b_q4_0": 1024, "cfg5_target_q4_0": 128}
+
+
+def bench_config(args, world, shares):
+    """The `config` object both arms print (identical, so the two lines are comparable)."""
+    first = args.prompt + args.warmup
+    return {"workload": args.config, "prompt": args.prompt,
+            "decode_positions": f"{first}..{first + args.steps - 1}", "parallelism": f"tp{world}",
+            "reducer": args.reducer if world > 1 else None, "shares": shares}
+
+
 class OracleRun:
-    """The CPU restatement of the reference's portable path (oracle/) on the same model."""
+    """The CPU restatement of the reference's portable path (oracle/) on the same model,
+    built in host memory by the oracle's own generator (no product code is loaded).  The
+    K/V cache of the first `ctx_pos` positions is filled with seeded values instead of
+    being prefilled (a 1024-token prefill of the 70B shape is hours of CPU time), so a
+    step at position p does the reference's full per-token work at that position."""
 
-    def __init__(self, sp):
-        import numpy as np
-        import nanocamelid_b200 as ncm
+    def __init__(self, sp, ctx_pos, ctx_limit):
         from oracle import oracle as orc
-        self.tmp = tempfile.TemporaryDirectory()
-        path = os.path.join(self.tmp.name, "m.gguf")
-        ncm.write_synthetic_gguf(path, sp)
-        self.ref = orc.OracleModel(path, ctx_limit=64)
-        rng = np.random.default_rng(0)
-        self.pos, self.tok = 0, 0
-        for t in [int(v) for v in rng.integers(0, sp.vocab, 4)]:
-            self.step(t)
+        self.ref = orc.OracleModel(spec=sp, ctx_limit=ctx_limit)
+        self.ref.fill_kv(ctx_pos)
+        self.pos, self.tok = ctx_pos, 0
 
-    def step(self, tok=None):
-        self.tok, _ = self.ref.forward_pass(self.tok if tok is None else tok, self.pos)
+    def step(self):
+        self.tok, _ = self.ref.forward_pass(self.tok, self.pos)
         self.pos += 1
 
     def timed(self, n, budget_s):
         k, t0 = 0, time.perf_counter()
-        while k < n and time.perf_counter() - t0 < budget_s and self.pos < 63:
+        while k < n and time.perf_counter() - t0 < budget_s and self.pos < self.ref.ctx:
             self.step()
             k += 1
         return k, time.perf_counter() - t0
 
 
-def cpu_sample(sp, budget_s=20.0):
-    run = OracleRun(sp)
-    run.step()
-    n, dt = run.timed(32, budget_s)
-    return {"value": round(n / dt, 3), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{n} greedy decode tokens after a 4-token prompt on the same model: CPU restatement of the "
-                      f"reference x86 portable path (oracle/, OpenMP over {os.cpu_count()} threads)"}
+def oracle_sample(args, sp, warmup, n, budget_s):
+    """(tok/s, tokens timed, the sample's description): decode steps of the CPU oracle at
+    the GPU arm's timed positions, OpenMP over every host core."""
+    first = args.prompt + args.warmup
+    run = OracleRun(sp, first - warmup, first + args.steps + 8)
+    for _ in range(warmup):
+        run.step()
+    k, dt = run.timed(n, budget_s)
+    desc = (f"{k} greedy decode steps at positions {first}..{first + k - 1} of {args.config} ({warmup} untimed "
+            f"before them); K/V of the earlier positions seeded instead of prefilled; CPU restatement of the "
+            f"reference x86 portable path (oracle/), OpenMP over {os.cpu_count()} threads")
+    return k / dt, k, desc
+
+
+def cpu_sample(args, sp, budget_s=20.0):
+    v, _, desc = oracle_sample(args, sp, 1, args.steps, budget_s)
+    return {"value": round(v, 3), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port", "sample": desc}
 
 
 def run_reference(args, sp, rank):
     if rank != 0:
         return
-    run = OracleRun(sp)
-    for _ in range(min(args.warmup, 3)):
-        run.step()
-    n, dt = run.timed(args.steps, 30.0)
-    v = n / dt
-    cpu = {"value": round(v, 3), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-           "sample": f"{n} greedy decode tokens after a 4-token prompt (+{min(args.warmup, 3)} warm-up tokens), "
-                     f"CPU restatement of the reference x86 portable path, OpenMP over {os.cpu_count()} threads"}
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    shares = None
+    if world > 1:
+        from nanocamelid_b200 import tp
+        shares = [int(v) for v in args.shares.split(",")] if args.shares else tp.default_shares(sp.kv_heads, world)
+    w = min(args.warmup, 2)
+    v, n, desc = oracle_sample(args, sp, w, args.steps, 30.0)
+    cpu = {"value": round(v, 3), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port", "sample": desc}
     print(json.dumps({"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "tok/s",
-                      "n_gpus": args.gpus, "steps": n, "warmup": min(args.warmup, 3), "higher_is_better": True,
-                      "dtype": "int8 dot / f32", "data": "synthetic", "config": {"workload": args.config, "prompt": 4},
+                      "n_gpus": args.gpus, "steps": n, "warmup": w, "higher_is_better": True,
+                      "dtype": "int8 dot / f32", "data": "synthetic", "config": bench_config(args, world, shares),
                       "cpu_baseline": cpu, "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
                                                    "d2h_bytes_per_step": 0}}), flush=True)
 
@@ -188,15 +209,58 @@ def gemv_roofline(torch, ncm, sp, peak):
     algo = nbytes + cols + cols // 32 * 4 + rows * 4
     gbs = algo / sec / 1e9
     traffic = None
-    prof = os.path.join(ROOT, "profiles", "gemv_q4_0_head_3b.traffic.json")
+    prof = os.path.join(ROOT, "profiles", f"gemv_q4_0_head_{rows}x{cols}.traffic.json")
     if os.path.exists(prof):
         try:
             traffic = json.load(open(prof)).get("dram_bytes_per_launch")
         except Exception:
             traffic = None
-    return {"bound": "hbm", "kernel": "gemv_kernel<Q4_0,IN_Q8,PLAIN> (tied head 128256x3072)", "achieved": round(gbs, 1),
+    return {"bound": "hbm", "kernel": f"ncm_qgemv_kernel<Q4_0,IN_Q8,PLAIN> (head-shaped {rows}x{cols}, microbench)",
+            "achieved": round(gbs, 1),
             "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4), "traffic": traffic,
             "algorithmic_bytes_per_launch": algo, "launch_us": round(sec * 1e6, 2), "peak_source": "measured"}
+
+
+def step_kernel_roofline(torch, ncm, m, sp, kind, peak, stream, world=1):
+    """CUDA-event time of the decode step's own GEMV of `kind` (same kernel, same launch
+    parameters as inside the captured step, PDL included), one launch per layer in turn so
+    that every launch streams weights that are not in L2."""
+    bpw = {2: 18 / 32, 8: 34 / 32, 12: 144 / 256}
+    tn = {2: "Q4_0", 8: "Q8_0", 12: "Q4_K"}
+    H, F = sp.emb, sp.ffn // world
+    qw, kw = sp.heads * sp.head_dim // world, sp.kv_heads * sp.head_dim // world
+    if kind == ncm.STEP_W13:
+        name, wbytes = f"ncm_qgemv_kernel<{tn[sp.t_ffn]},IN_F32_RMS,EPI_SILU> (ffn_gate+ffn_up {F}x{H} x2)", 2 * F * H * bpw[sp.t_ffn]
+        io = H * 4 * 2 + F * 4
+    else:
+        name, wbytes = f"ncm_qgemv_kernel<{tn[sp.t_attn]},IN_F32_RMS,EPI_QKV> (attn_q/k/v {qw + 2 * kw}x{H})", (qw + 2 * kw) * H * bpw[sp.t_attn]
+        io = H * 4 * 2 + (qw + 2 * kw) * 4
+    n = max(8, min(sp.layers, 40))
+    for i in range(4):
+        m.launch_step_kernel(kind, i % sp.layers, stream.cuda_stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(n):
+        m.launch_step_kernel(kind, i % sp.layers, stream.cuda_stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / n
+    algo = int(wbytes + io)
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", f"{args_config_key(sp)}_w13.traffic.json")
+    if kind == ncm.STEP_W13 and os.path.exists(prof):
+        try:
+            traffic = json.load(open(prof)).get("dram_bytes_per_launch")
+        except Exception:
+            traffic = None
+    return {"bound": "hbm", "kernel": name, "achieved": round(algo / sec / 1e9, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(algo / sec / 1e9 / peak, 4), "traffic": traffic, "algorithmic_bytes_per_launch": algo,
+            "launch_us": round(sec * 1e6, 2), "launches_timed": n, "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)"}
+
+
+def args_config_key(sp):
+    return "gemv_q4_0_70b" if sp.emb == 8192 else f"gemv_emb{sp.emb}"
 
 
 def run_b200(args, sp):
@@ -221,7 +285,10 @@ def run_b200(args, sp):
     ctx = args.prompt + args.warmup + args.steps + 8
     m = ncm.Model.synthetic(sp, ctx_limit=ctx, device=local, shares=shares, shard=rank)
     if world > 1:
-        tp.connect(m, rank, world, ncm.REDUCE_NCCL if args.reducer == "nccl" else ncm.REDUCE_FUSED_P2P)
+        # peers' exchange areas and an NCCL communicator: the fused reducer is timed first,
+        # then the NCCL-allreduce baseline on the same shards
+        tp.connect(m, rank, world, ncm.REDUCE_NCCL)
+        m.tp_set_reducer(ncm.REDUCE_FUSED_P2P if args.reducer == "p2p" else ncm.REDUCE_NCCL)
     rng = np.random.default_rng(0)
     prompt = [int(v) for v in rng.integers(0, sp.vocab, args.prompt)]
     stream = torch.cuda.Stream()
@@ -230,22 +297,27 @@ def run_b200(args, sp):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+
+    def timed_steps(n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         e0.record(stream)
-        m.decode_steps(args.steps, stream.cuda_stream)
+        m.decode_steps(n, stream.cuda_stream)
         e1.record(stream)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        t = e0.elapsed_time(e1)
+        if world > 1:
+            tt = torch.tensor([t], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
+
+    with ClockSampler(local) as clk:
+        ms = timed_steps(args.steps)
     toks, pos = m.sync_tokens(ctx)
     tok_s = args.steps / (ms / 1e3)
     # end to end through the C-ABI forward_pass: host token in, argmax out, per step
@@ -269,26 +341,40 @@ def run_b200(args, sp):
             el = float(t.item())
         e2e = {"value": round(ne / el, 2), "unit": "tok/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4,
                "api": "ncm_forward_pass (host token -> device step -> host argmax, synchronous)"}
+    nccl = None
+    if world > 1 and args.reducer == "p2p":
+        # the NCCL-allreduce baseline of the same decode (same shards, positions rewritten)
+        m.tp_set_reducer(ncm.REDUCE_NCCL)
+        m.decode_steps(2, stream.cuda_stream)
+        torch.cuda.synchronize()
+        n_ms = timed_steps(args.steps)
+        nccl = {"value": round(args.steps / (n_ms / 1e3), 2), "unit": "tok/s", "ms_per_step": round(n_ms / args.steps, 4),
+                "reducer": "ncclAllReduce(sum) of the wo/w2 partial rows + residual add, ncclAllGather argmax merge"}
+        m.tp_set_reducer(ncm.REDUCE_FUSED_P2P)
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {"hbm_gbs": 6650.0}
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    # the decode step's dominant kernel, timed live (rank 0's shard under TP)
+    roof = step_kernel_roofline(torch, ncm, m, sp, ncm.STEP_W13, peak, stream, world=world)
+    if world > 1:
+        dist.barrier()
     if rank == 0:
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
-            os.path.join(ROOT, "MEASURED_PEAKS.json")) else {"hbm_gbs": 6650.0}
-        peak = float(peaks.get("hbm_gbs", 6650.0))
-        roof = gemv_roofline(torch, ncm, sp, peak)
+        head = gemv_roofline(torch, ncm, sp, peak)
         bpt = weight_bytes(sp, world, shares)
         whole = {"bytes_per_token_per_gpu": int(bpt), "achieved_gbs": round(bpt * tok_s / 1e9, 1),
                  "frac_of_measured_hbm": round(bpt * tok_s / 1e9 / peak, 4)}
-        cpu = None if (args.no_cpu or world > 1) else cpu_sample(sp)
+        cpu = None if (args.no_cpu or world > 1) else cpu_sample(args, sp)
         launches_per_step = 2 + 6 * sp.layers + (0 if world == 1 or args.reducer == "p2p" else 2 * sp.layers + 1)
+        cfg = bench_config(args, world, shares)
+        cfg["l2"] = "inputs larger than L2 (weights %.2f GB/token/GPU)" % (bpt / 1e9)
         line = {"metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "int8 dot / f32", "data": "synthetic",
-                "config": {"workload": args.config, "prompt": args.prompt, "decode_positions":
-                           f"{args.prompt + args.warmup}..{args.prompt + args.warmup + args.steps - 1}",
-                           "parallelism": f"tp{world}", "reducer": args.reducer if world > 1 else None,
-                           "shares": shares,
-                           "l2": "inputs larger than L2 (weights %.2f GB/token/GPU)" % (bpt / 1e9)},
-                "roofline": roof, "decode_roofline": whole, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_launches": launches_per_step * args.steps, "clocks": clk.summary()}
+                "config": cfg, "roofline": roof, "head_gemv_roofline": head, "decode_roofline": whole,
+                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+                "clocks": clk.summary()}
+        if nccl:
+            line["nccl_baseline"] = nccl
         print(json.dumps(line), flush=True)
     m.close()
     if world > 1:
@@ -383,6 +469,12 @@ def main():
     args = parse()
     import nanocamelid_b200 as ncm
     sp = ncm.CONFIGS[args.config]
+    if args.layers:
+        sp = sp.replace(layers=args.layers)
+    if args.vocab:
+        sp = sp.replace(vocab=args.vocab)
+    if args.prompt is None:
+        args.prompt = PROMPTS.get(args.config, 64)
     rank = int(os.environ.get("RANK", "0"))
     if args.spec:
         run_spec(args, ncm)

@@ -176,6 +176,14 @@ ncm_status ncm_get_hidden(ncm_model* m, float* hidden);
  * 4 / 5 K / V cache of `layer` ([ctx][local kv width]), 6 logits (local head rows). */
 ncm_status ncm_debug_read(ncm_model* m, int which, int layer, float* out, int64_t n);
 
+/* Measurement seam (no reference counterpart; the reference times whole tokens): one
+ * launch, on `stream`, of the decode step's GEMV kernel of kind NCM_STEP_* for `layer`,
+ * with the parameters the captured step uses, so that a caller can time the step's
+ * dominant kernel with events.  It overwrites the activations that kernel writes.
+ * NCM_STEP_WO / NCM_STEP_W2 run on unsharded models only. */
+enum { NCM_STEP_QKV = 0, NCM_STEP_W13 = 1, NCM_STEP_WO = 2, NCM_STEP_W2 = 3 };
+ncm_status ncm_launch_step_kernel(ncm_model* m, int kind, int layer, void* stream);
+
 /* ---------------------------------------------------------------- speculative decoding
  * speculative.rs:381-389 prefill_pass_batch + compute_logits_from_hidden +
  * sample_logits(_, 0.0) per row: tokens[ntok] (1 <= ntok <= 8) at positions

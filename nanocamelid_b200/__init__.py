@@ -19,6 +19,7 @@ LIB_PATH = os.path.join(HERE, "libncm.so")
 
 Q4_0, Q8_0, Q4_K, F32, F16 = 2, 8, 12, 0, 1
 REDUCE_FUSED_P2P, REDUCE_NCCL, REDUCE_HOST_CALLBACK = 0, 1, 2
+STEP_QKV, STEP_W13, STEP_WO, STEP_W2 = 0, 1, 2, 3
 PHASE_ATTENTION, PHASE_FFN, PHASE_HEAD = 0, 1, 2   # tp.rs:203-206 ReducePhase, + the head merge
 HOST_REDUCE_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.POINTER(ctypes.c_float), ctypes.c_int, ctypes.c_int,
                                   ctypes.c_int, ctypes.c_void_p)
@@ -114,6 +115,7 @@ def lib():
         "ncm_sync_tokens": (c_int, [c_p, pint, c_int, pint]),
         "ncm_get_hidden": (c_int, [c_p, c_p]),
         "ncm_debug_read": (c_int, [c_p, c_int, c_int, c_p, c_i64]),
+        "ncm_launch_step_kernel": (c_int, [c_p, c_int, c_int, c_p]),
         "ncm_tp_export": (c_int, [c_p, pu8]),
         "ncm_tp_import": (c_int, [c_p, pu8, c_int, c_int]),
         "ncm_nccl_unique_id": (c_int, [pu8]),
@@ -291,6 +293,10 @@ class Model:
         pos = ctypes.c_int()
         _ck(lib().ncm_sync_tokens(self._h, out, count, ctypes.byref(pos)))
         return list(out)[:count], pos.value
+
+    def launch_step_kernel(self, kind, layer, stream=0):
+        """One launch of the decode step's GEMV of `kind` (STEP_*) for `layer` (timing)."""
+        _ck(lib().ncm_launch_step_kernel(self._h, kind, layer, _stream(stream)))
 
     def hidden(self):
         import numpy as np

@@ -109,6 +109,7 @@ struct ncm_model {
     float *b_hidden = nullptr, *b_q = nullptr, *b_att = nullptr, *b_act = nullptr;
     int8_t* b_xq = nullptr;
     float* b_xs = nullptr;
+    int* b_xsum = nullptr;
     float2* b_amax = nullptr;
     unsigned* b_cnt = nullptr;
     int *b_tok = nullptr, *b_arg = nullptr, *b_pos = nullptr;
@@ -604,31 +605,49 @@ static ncm_status row_parallel(ncm_model* m, const DevMat& w, const float* x, in
     return NCM_OK;
 }
 
-static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
+// rms_norm -> quantize -> wq/wk/wv -> rope -> store_kv (inference.rs:4521-4646) of layer l.
+static int launch_qkv(ncm_model* m, int l, cudaStream_t s) {
+    const Layer& L = m->L[l];
     const int qw = m->qh * m->hd, kw = m->kh * m->hd;
+    GemvParams p = base_params(m);
+    p.nseg = 3;
+    p.seg[0] = {m->q, qw, 0, SEG_Q};
+    p.seg[1] = {nullptr, kw, qw, SEG_K};
+    p.seg[2] = {nullptr, kw, qw + kw, SEG_V};
+    p.total_rows = qw + 2 * kw;
+    p.x = m->hidden;
+    p.norm_w = L.attn_norm;
+    p.kcache = m->kc + (size_t)l * m->ctx * kw;
+    p.vcache = m->vc + (size_t)l * m->ctx * kw;
+    p.kv_width = kw;
+    if (l == 0) p.ssq_tok = m->embd_ssq;
+    return launch_gemv({&L.wq, &L.wk, &L.wv}, nullptr, IN_F32_RMS, EPI_QKV, p, s);
+}
+
+// rms_norm -> quantize -> w1, w3 -> silu*mul (inference.rs:4679-4730) of layer l.
+static int launch_w13(ncm_model* m, int l, cudaStream_t s) {
+    const Layer& L = m->L[l];
+    GemvParams f = base_params(m);
+    f.nseg = 1;
+    f.seg[0] = {m->act, m->fl, 0, SEG_OUT};
+    f.total_rows = m->fl;
+    f.x = m->hidden;
+    f.norm_w = L.ffn_norm;
+    return launch_gemv({&L.w1}, &L.w3, IN_F32_RMS, EPI_SILU, f, s);
+}
+
+static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
+    const int kw = m->kh * m->hd;
     CKL(embed_launch(m->embd.type, m->embd.d, m->embd.pitch, m->emb, m->tokens, m->state, m->hidden, s, true));
     for (int l = 0; l < m->layers; ++l) {
         const Layer& L = m->L[l];
-        // rms_norm -> quantize -> wq/wk/wv -> rope -> store_kv (inference.rs:4521-4646)
-        GemvParams p = base_params(m);
-        p.nseg = 3;
-        p.seg[0] = {m->q, qw, 0, SEG_Q};
-        p.seg[1] = {nullptr, kw, qw, SEG_K};
-        p.seg[2] = {nullptr, kw, qw + kw, SEG_V};
-        p.total_rows = qw + 2 * kw;
-        p.x = m->hidden;
-        p.norm_w = L.attn_norm;
-        p.kcache = m->kc + (size_t)l * m->ctx * kw;
-        p.vcache = m->vc + (size_t)l * m->ctx * kw;
-        p.kv_width = kw;
-        if (l == 0) p.ssq_tok = m->embd_ssq;
-        CKL(launch_gemv({&L.wq, &L.wk, &L.wv}, nullptr, IN_F32_RMS, EPI_QKV, p, s));
+        CKL(launch_qkv(m, l, s));
         // attention (inference.rs:4648-4665)
         AttnParams a;
         memset(&a, 0, sizeof a);
         a.q = m->q;
-        a.kc = p.kcache;
-        a.vc = p.vcache;
+        a.kc = m->kc + (size_t)l * m->ctx * kw;
+        a.vc = m->vc + (size_t)l * m->ctx * kw;
         a.out = m->att;
         a.scores = m->scores;
         a.state = m->state;
@@ -644,14 +663,7 @@ static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
         // quantize -> wo -> residual (inference.rs:4667-4673), reduce #1 (tp.rs:356-363)
         ncm_status st = row_parallel(m, L.wo, m->att, 2 * l, s);
         if (st) return st;
-        // rms_norm -> quantize -> w1, w3 -> silu*mul (inference.rs:4679-4730)
-        GemvParams f = base_params(m);
-        f.nseg = 1;
-        f.seg[0] = {m->act, m->fl, 0, SEG_OUT};
-        f.total_rows = m->fl;
-        f.x = m->hidden;
-        f.norm_w = L.ffn_norm;
-        CKL(launch_gemv({&L.w1}, &L.w3, IN_F32_RMS, EPI_SILU, f, s));
+        CKL(launch_w13(m, l, s));
         // quantize -> w2 -> residual (inference.rs:4732-4748), reduce #2 (tp.rs:416-424)
         st = row_parallel(m, L.w2, m->act, 2 * l + 1, s);
         if (st) return st;
@@ -868,6 +880,26 @@ extern "C" ncm_status ncm_get_hidden(ncm_model* m, float* hidden) {
     return NCM_OK;
 }
 
+// Measurement seam: one launch of a decode step's GEMV kernel for `layer`, with exactly
+// the parameters the captured step uses (so a caller can time the step's dominant kernel
+// with events on its own stream).  It overwrites the activations it writes (q and the
+// layer's K/V row at the current position, silu*up, or hidden for the row-parallel ones).
+extern "C" ncm_status ncm_launch_step_kernel(ncm_model* m, int kind, int layer, void* stream) {
+    if (!m || layer < 0 || layer >= m->layers) return fail(NCM_EINVAL, "bad layer");
+    CK(cudaSetDevice(m->device));
+    cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+    switch (kind) {
+        case NCM_STEP_QKV: CKL(launch_qkv(m, layer, s)); return NCM_OK;
+        case NCM_STEP_W13: CKL(launch_w13(m, layer, s)); return NCM_OK;
+        case NCM_STEP_WO:
+        case NCM_STEP_W2:
+            if (m->world > 1) return fail(NCM_EUNSUPPORTED, "row-parallel kernels of a shard wait on their peers");
+            return row_parallel(m, kind == NCM_STEP_WO ? m->L[layer].wo : m->L[layer].w2,
+                                kind == NCM_STEP_WO ? m->att : m->act, 0, s);
+        default: return fail(NCM_EINVAL, "unknown step kernel");
+    }
+}
+
 // ------------------------------------------------------------------ multi-row verify
 static ncm_status ensure_batch_buffers(ncm_model* m) {
     if (m->b_hidden) return NCM_OK;
@@ -879,6 +911,7 @@ static ncm_status ensure_batch_buffers(ncm_model* m) {
     DALLOC(m->b_act, 4 * (size_t)kMaxBatch * m->fl);
     DALLOC(m->b_xq, (size_t)kMaxBatch * wmax);
     DALLOC(m->b_xs, 4 * (size_t)kMaxBatch * (wmax / 32));
+    DALLOC(m->b_xsum, 4 * (size_t)kMaxBatch * (wmax / 32));
     DALLOC(m->b_amax, sizeof(float2) * kMaxBatch * num_sms());
     DALLOC(m->b_cnt, 4);
     DALLOC(m->b_tok, 4 * kMaxBatch);
@@ -901,6 +934,7 @@ static BatchParams batch_base(ncm_model* m, int ntok) {
     p.err = m->err;
     p.xq = m->b_xq;
     p.xs = m->b_xs;
+    p.xsum = m->b_xsum;
     return p;
 }
 
@@ -953,7 +987,7 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s, bool wi
     for (int l = 0; l < m->layers; ++l) {
         const Layer& L = m->L[l];
         CKL(batch_prep_launch(m->b_hidden, m->emb, m->emb, ntok, L.attn_norm, m->eps, l == 0 ? m->embd_ssq : nullptr,
-                              m->b_tok, m->b_xq, m->b_xs, s, true));
+                              m->b_tok, m->b_xq, m->b_xs, m->b_xsum, s, true));
         BatchParams p = batch_base(m, ntok);
         p.nseg = 3;
         p.seg[0] = {m->b_q, qw, 0, SEG_Q};
@@ -990,7 +1024,7 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s, bool wi
             o.xf = m->b_att;
             o.xf_stride = qw;
         } else {
-            CKL(batch_prep_launch(m->b_att, qw, qw, ntok, nullptr, m->eps, nullptr, nullptr, m->b_xq, m->b_xs, s, true));
+            CKL(batch_prep_launch(m->b_att, qw, qw, ntok, nullptr, m->eps, nullptr, nullptr, m->b_xq, m->b_xs, m->b_xsum, s, true));
         }
         o.nseg = 1;
         o.seg[0] = {nullptr, m->emb, 0, SEG_OUT};
@@ -1000,7 +1034,7 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s, bool wi
         ncm_status st = batch_row_parallel(m, L.wo, o, ntok, l, NCM_REDUCE_PHASE_ATTENTION, s);
         if (st) return st;
         CKL(batch_prep_launch(m->b_hidden, m->emb, m->emb, ntok, L.ffn_norm, m->eps, nullptr, nullptr, m->b_xq,
-                              m->b_xs, s, true));
+                              m->b_xs, m->b_xsum, s, true));
         BatchParams f = batch_base(m, ntok);
         f.nseg = 1;
         f.seg[0] = {m->b_act, m->fl, 0, SEG_OUT};
@@ -1012,8 +1046,8 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s, bool wi
             d.xf = m->b_act;
             d.xf_stride = m->fl;
         } else {
-            CKL(batch_prep_launch(m->b_act, m->fl, m->fl, ntok, nullptr, m->eps, nullptr, nullptr, m->b_xq, m->b_xs, s,
-                                  true));
+            CKL(batch_prep_launch(m->b_act, m->fl, m->fl, ntok, nullptr, m->eps, nullptr, nullptr, m->b_xq, m->b_xs,
+                                  m->b_xsum, s, true));
         }
         d.nseg = 1;
         d.seg[0] = {nullptr, m->emb, 0, SEG_OUT};
@@ -1025,7 +1059,7 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s, bool wi
     }
     if (!with_head) return NCM_OK;   // prompt rows before the last: K/V only
     CKL(batch_prep_launch(m->b_hidden, m->emb, m->emb, ntok, m->out_norm, m->eps, nullptr, nullptr, m->b_xq, m->b_xs,
-                          s, true));
+                          m->b_xsum, s, true));
     BatchParams h = batch_base(m, ntok);
     h.nseg = 1;
     h.seg[0] = {nullptr, m->hr, 0, SEG_OUT};
@@ -1522,7 +1556,16 @@ extern "C" ncm_status ncm_matmul_quantized_batch(int qtype, const void* w, int64
     p.xq = x_i8;
     p.xs = x_scales;
     const int grid = batch_plan(qtype, cols, (int)rows, false, ntok, p);
-    if (grid < 0) return fail(NCM_EUNSUPPORTED, "activation rows do not fit in shared memory");
+    if (grid < 0) return fail(NCM_EUNSUPPORTED, "no launch plan for this shape");
+    AsyncScratch sums;
+    if (p.x_global) {
+        // rows read in place: their per-block sums come from a small pass into scratch
+        const int64_t nblk = (int64_t)ntok * (cols / 32);
+        sums.s = st;
+        CK(cudaMallocAsync((void**)&sums.p, 4 * (size_t)nblk, st));
+        CKL(block_sums_launch(x_i8, nblk, (int*)sums.p, st));
+        p.xsum = (const int*)sums.p;
+    }
     int r = gemv_tensor_map(&p.tm[0], base, rows, (int)pitch, p.chunk_words, p.box_rows);
     if (!r) r = batch_gemv_launch(qtype, EPI_PLAIN, p, grid, st, false);
     if (r) return fail(NCM_ECUDA, std::string("batch gemv launch: ") + cudaGetErrorString((cudaError_t)r));

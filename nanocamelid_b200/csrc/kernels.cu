@@ -532,7 +532,7 @@ __device__ __forceinline__ void stage_f32(float* dst, const float* src, int n, i
     }
 }
 
-// GEMV block: warps 0-7 compute, 8-9 fold, 10 produces (see gemv_kernel).
+// GEMV block: warps 0-7 compute, 8-9 fold, 10 produces (see ncm_qgemv_kernel).
 constexpr int kComputeThreads = 256;
 constexpr int kFoldBase = 256;      // first fold thread
 constexpr int kProducer = 320;      // producer thread
@@ -688,7 +688,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 //   eflag[w][k] (fold warp w -> compute: uses of slot k folded)
 
 template <int QT, int IN, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr bool DUAL = (EPI == EPI_SILU);
     __shared__ GemvSeqScratch sc;
@@ -1072,7 +1072,7 @@ int gemv_plan(int qtype, int cols, int rows, bool dual, int in_mode, GemvParams&
 
 template <int QT, int IN, int EPI>
 static int launch_t(const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
-    auto kern = gemv_kernel<QT, IN, EPI>;
+    auto kern = ncm_qgemv_kernel<QT, IN, EPI>;
     if (int r = set_smem_limit((const void*)kern, kGemvSmemLimit)) return r;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -1746,7 +1746,7 @@ __device__ __forceinline__ void batch_fold(const float4* T, int c, int nb, float
 }
 
 template <int QT, int EPI>
-__global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(const __grid_constant__ BatchParams p) {
+__global__ void __launch_bounds__(kBatchThreads, 1) ncm_qgemm_verify_kernel(const __grid_constant__ BatchParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr bool DUAL = (EPI == EPI_SILU);
     constexpr int NM = DUAL ? 2 : 1;
@@ -1799,11 +1799,18 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(const __gr
     }
     pdl_launch_dependents();
     pdl_wait();
-    // quantised rows, their scales and per-block sums into shared memory
-    uint8_t* xq = smem + p.xq_off;
-    float* xs = reinterpret_cast<float*>(smem + p.xs_off);
-    int* xsum = reinterpret_cast<int*>(smem + p.xsum_off);
-    if (p.xf) {
+    // quantised rows, their scales and per-block sums into shared memory (or, for rows
+    // too wide for it, read in place from global memory, where they stay L2-resident)
+    const uint8_t* xq = p.x_global ? reinterpret_cast<const uint8_t*>(p.xq) : smem + p.xq_off;
+    const float* xs = p.x_global ? p.xs : reinterpret_cast<const float*>(smem + p.xs_off);
+    const int* xsum = p.x_global ? p.xsum : reinterpret_cast<const int*>(smem + p.xsum_off);
+    const int xq_pitch = p.x_global ? p.cols : p.xq_pitch;
+    if (p.x_global) {
+        // nothing to stage
+    } else if (p.xf) {
+        uint8_t* xq_s = smem + p.xq_off;
+        float* xs_s = reinterpret_cast<float*>(smem + p.xs_off);
+        int* xsum_s = reinterpret_cast<int*>(smem + p.xsum_off);
         // f32 rows: quantize_f32_to_q8_0 (inference.rs:991-1029) here, four lanes per
         // 32-value block (quad max and sum reductions), every element rounded as in the
         // one-thread quantiser
@@ -1836,22 +1843,25 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(const __gr
             }
             sum += __shfl_xor_sync(qmask, sum, 1);
             sum += __shfl_xor_sync(qmask, sum, 2);
-            *reinterpret_cast<uint2*>(xq + tk * p.xq_pitch + 32 * b + 8 * li) = make_uint2(w0, w1);
+            *reinterpret_cast<uint2*>(xq_s + tk * p.xq_pitch + 32 * b + 8 * li) = make_uint2(w0, w1);
             if (li == 0) {
-                xs[i] = sb;
-                xsum[i] = sum;
+                xs_s[i] = sb;
+                xsum_s[i] = sum;
             }
         }
     } else {
+        uint8_t* xq_s = smem + p.xq_off;
+        float* xs_s = reinterpret_cast<float*>(smem + p.xs_off);
+        int* xsum_s = reinterpret_cast<int*>(smem + p.xsum_off);
         const int n16 = p.cols / 16;
         for (int i = tid; i < p.ntok * n16; i += blockDim.x) {
             const int tk = i / n16, k = i % n16;
-            *reinterpret_cast<uint4*>(xq + tk * p.xq_pitch + 16 * k) =
+            *reinterpret_cast<uint4*>(xq_s + tk * p.xq_pitch + 16 * k) =
                 *reinterpret_cast<const uint4*>(p.xq + (size_t)tk * p.cols + 16 * k);
         }
         for (int i = tid; i < p.ntok * p.nb; i += blockDim.x) {
             const int tk = i / p.nb, b = i % p.nb;
-            xs[i] = p.xs[(size_t)tk * p.nb + b];
+            xs_s[i] = p.xs[(size_t)tk * p.nb + b];
             const uint4* src = reinterpret_cast<const uint4*>(p.xq + (size_t)tk * p.cols + 32 * b);
             int sum = 0;
 #pragma unroll
@@ -1862,7 +1872,7 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(const __gr
                 sum = __dp4a((int)v.z, 0x01010101, sum);
                 sum = __dp4a((int)v.w, 0x01010101, sum);
             }
-            xsum[i] = sum;
+            xsum_s[i] = sum;
         }
     }
     __syncthreads();
@@ -1889,16 +1899,16 @@ __global__ void __launch_bounds__(kBatchThreads, 1) gemv_batch_kernel(const __gr
                     const uint8_t* tile = stages + (size_t)s * p.stage_bytes;
                     float4* T = tbase + (size_t)s * tslot + sl * 16 * 32 + lane;
                     if (nbw == 2)
-                        batch_terms<QT, 2>(tile, p.chunk_bytes, ra, g, t, c, bl0, xq, p.xq_pitch, xs, xsum, p.nb, p.ntok, T);
+                        batch_terms<QT, 2>(tile, p.chunk_bytes, ra, g, t, c, bl0, xq, xq_pitch, xs, xsum, p.nb, p.ntok, T);
                     else
-                        batch_terms<QT, 4>(tile, p.chunk_bytes, ra, g, t, c, bl0, xq, p.xq_pitch, xs, xsum, p.nb, p.ntok, T);
+                        batch_terms<QT, 4>(tile, p.chunk_bytes, ra, g, t, c, bl0, xq, xq_pitch, xs, xsum, p.nb, p.ntok, T);
                     if (DUAL) {
                         float4* T2 = T + S * 16 * 32;
                         if (nbw == 2)
-                            batch_terms<QT, 2>(tile + box2_off, p.chunk_bytes, ra, g, t, c, bl0, xq, p.xq_pitch, xs, xsum,
+                            batch_terms<QT, 2>(tile + box2_off, p.chunk_bytes, ra, g, t, c, bl0, xq, xq_pitch, xs, xsum,
                                                p.nb, p.ntok, T2);
                         else
-                            batch_terms<QT, 4>(tile + box2_off, p.chunk_bytes, ra, g, t, c, bl0, xq, p.xq_pitch, xs, xsum,
+                            batch_terms<QT, 4>(tile + box2_off, p.chunk_bytes, ra, g, t, c, bl0, xq, xq_pitch, xs, xsum,
                                                p.nb, p.ntok, T2);
                     }
                 }
@@ -2043,36 +2053,47 @@ int batch_plan(int qtype, int cols, int rows, bool dual, int ntok, BatchParams& 
     if (grid > maxg) grid = maxg > 0 ? maxg : 1;
     const int per_cta = (rows + grid - 1) / grid;
     p.xq_pitch = cols + 16;   // distinct banks for the eight token rows of a fragment
-    int off = 256;            // full / empty / tfull / tempty mbarriers
-    p.xq_off = off;
-    off += (ntok * p.xq_pitch + 127) / 128 * 128;
-    p.xs_off = off;
-    off += (ntok * p.nb * 4 + 127) / 128 * 128;
-    p.xsum_off = off;
-    off += (ntok * p.nb * 4 + 127) / 128 * 128;
-    p.stage_off = off;
-    // slabs per tile: two (one per fold warp) unless the CTA's rows or the budget say one
-    for (int S = std::min(2, (per_cta + 15) / 16); S >= 1; --S) {
-        const int br = 16 * S;
-        const int stage_bytes = (br * p.chunk_bytes + 127) / 128 * 128 * (dual ? 2 : 1);
-        const int t_bytes = (dual ? 2 : 1) * S * 16 * 32 * 16;
-        int ns = kMaxStages;
-        while (ns > 2 && off + ns * (stage_bytes + t_bytes) > kBatchSmemLimit) --ns;
-        if (off + ns * (stage_bytes + t_bytes) > kBatchSmemLimit) continue;
-        p.nslab = S;
-        p.box_rows = br;
-        p.stage_bytes = stage_bytes;
-        p.nstages = ns;
-        p.t_off = off + ns * stage_bytes;
-        p.smem_bytes = p.t_off + ns * t_bytes;
-        return grid;
+    // Activation rows in shared memory when they fit beside a ring of at least four
+    // stages; otherwise (wide inputs: the 70B down projection has 28672 columns) they are
+    // read in place from global memory (x_global: xq / xs / xsum prepared by the caller).
+    for (int xg = 0; xg < 2; ++xg) {
+        int off = 256;            // full / empty / tfull / tempty mbarriers
+        if (!xg) {
+            p.xq_off = off;
+            off += (ntok * p.xq_pitch + 127) / 128 * 128;
+            p.xs_off = off;
+            off += (ntok * p.nb * 4 + 127) / 128 * 128;
+            p.xsum_off = off;
+            off += (ntok * p.nb * 4 + 127) / 128 * 128;
+        } else {
+            if (p.xf) return -1;   // f32 rows are quantised into shared memory only
+            p.xq_off = p.xs_off = p.xsum_off = off;
+        }
+        p.x_global = xg;
+        p.stage_off = off;
+        // slabs per tile: two (one per fold warp) unless the CTA's rows or the budget say one
+        for (int S = std::min(2, (per_cta + 15) / 16); S >= 1; --S) {
+            const int br = 16 * S;
+            const int stage_bytes = (br * p.chunk_bytes + 127) / 128 * 128 * (dual ? 2 : 1);
+            const int t_bytes = (dual ? 2 : 1) * S * 16 * 32 * 16;
+            int ns = kMaxStages;
+            while (ns > 2 && off + ns * (stage_bytes + t_bytes) > kBatchSmemLimit) --ns;
+            if (off + ns * (stage_bytes + t_bytes) > kBatchSmemLimit || (!xg && ns < 4)) continue;
+            p.nslab = S;
+            p.box_rows = br;
+            p.stage_bytes = stage_bytes;
+            p.nstages = ns;
+            p.t_off = off + ns * stage_bytes;
+            p.smem_bytes = p.t_off + ns * t_bytes;
+            return grid;
+        }
     }
     return -1;
 }
 
 template <int QT, int EPI>
 static int batch_launch_t(const BatchParams& p, int grid, cudaStream_t s, bool pdl) {
-    auto kern = gemv_batch_kernel<QT, EPI>;
+    auto kern = ncm_qgemm_verify_kernel<QT, EPI>;
     if (int r = set_smem_limit((const void*)kern, kBatchSmemLimit)) return r;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -2115,7 +2136,7 @@ constexpr int kPrepSplit = 16;
 template <int NT>
 __global__ void __launch_bounds__(NT) batch_prep_kernel(const float* x, int x_stride, int n, const float* norm_w,
                                                         float eps, const float* ssq_tab, const int* toks,
-                                                        int8_t* xq, float* xs) {
+                                                        int8_t* xq, float* xs, int* xsum) {
     extern __shared__ __align__(16) float xr[];
     __shared__ SeqSumScratchT<NT> sc;
     pdl_launch_dependents();
@@ -2161,23 +2182,31 @@ __global__ void __launch_bounds__(NT) batch_prep_kernel(const float* x, int x_st
         amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 2));
         const float sb = amax / 127.0f;
         uint32_t w0 = 0, w1 = 0;
+        int sum = 0;
         if (sb > 0.0f) {
             const float inv = 1.0f / sb;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 float q = roundf(v[i] * inv);
                 q = fminf(fmaxf(q, -127.0f), 127.0f);
+                sum += (int)q;
                 const uint32_t byte = (uint32_t)((int)q & 0xff) << (8 * (i & 3));
                 if (i < 4) w0 |= byte; else w1 |= byte;
             }
         }
+        sum += __shfl_xor_sync(qmask, sum, 1);
+        sum += __shfl_xor_sync(qmask, sum, 2);
         *reinterpret_cast<uint2*>(xq + (size_t)tk * n + 32 * b + 8 * c) = make_uint2(w0, w1);
-        if (li == 0) xs[(size_t)tk * nblk + b] = sb;
+        if (li == 0) {
+            xs[(size_t)tk * nblk + b] = sb;
+            if (xsum) xsum[(size_t)tk * nblk + b] = sum;
+        }
     }
 }
 
 int batch_prep_launch(const float* x, int x_stride, int n, int ntok, const float* norm_w, float eps,
-                      const float* ssq_tab, const int* toks, int8_t* xq, float* xs, cudaStream_t s, bool pdl) {
+                      const float* ssq_tab, const int* toks, int8_t* xq, float* xs, int* xsum, cudaStream_t s,
+                      bool pdl) {
     if (int r = set_smem_limit((const void*)batch_prep_kernel<256>, 128 * 1024)) return r;
     if (int r = set_smem_limit((const void*)batch_prep_kernel<512>, 128 * 1024)) return r;
     cudaLaunchAttribute attr[1];
@@ -2186,8 +2215,32 @@ int batch_prep_launch(const float* x, int x_stride, int n, int ntok, const float
     cudaLaunchConfig_t cfg = small_cfg(dim3(ntok, split), dim3(folds ? 512 : 256), s, pdl, attr);
     cfg.dynamicSmemBytes = folds ? (size_t)n * 4 : 0;
     if (folds)
-        return (int)cudaLaunchKernelEx(&cfg, batch_prep_kernel<512>, x, x_stride, n, norm_w, eps, ssq_tab, toks, xq, xs);
-    return (int)cudaLaunchKernelEx(&cfg, batch_prep_kernel<256>, x, x_stride, n, norm_w, eps, ssq_tab, toks, xq, xs);
+        return (int)cudaLaunchKernelEx(&cfg, batch_prep_kernel<512>, x, x_stride, n, norm_w, eps, ssq_tab, toks, xq, xs,
+                                       xsum);
+    return (int)cudaLaunchKernelEx(&cfg, batch_prep_kernel<256>, x, x_stride, n, norm_w, eps, ssq_tab, toks, xq, xs,
+                                   xsum);
+}
+
+// Per-block sums of quantised rows (the Q4_K min term needs sum(x) per 32-block).
+__global__ void block_sums_kernel(const int8_t* xq, int64_t nblocks, int* xsum) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nblocks) return;
+    const uint4* src = reinterpret_cast<const uint4*>(xq + 32 * b);
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const uint4 v = src[k];
+        sum = __dp4a((int)v.x, 0x01010101, sum);
+        sum = __dp4a((int)v.y, 0x01010101, sum);
+        sum = __dp4a((int)v.z, 0x01010101, sum);
+        sum = __dp4a((int)v.w, 0x01010101, sum);
+    }
+    xsum[b] = sum;
+}
+int block_sums_launch(const int8_t* xq, int64_t nblocks, int* xsum, cudaStream_t s) {
+    if (nblocks <= 0) return 0;
+    block_sums_kernel<<<(unsigned)((nblocks + 127) / 128), 128, 0, s>>>(xq, nblocks, xsum);
+    return (int)cudaGetLastError();
 }
 
 __global__ void embed_rows_kernel(int type, const uint8_t* table, int64_t pitch, int emb, const int* toks,

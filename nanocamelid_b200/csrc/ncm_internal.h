@@ -119,6 +119,8 @@ struct alignas(64) BatchParams {
     int ntok;
     const int8_t* xq;             // [ntok][cols] quantised rows
     const float* xs;              // [ntok][cols / 32]
+    const int* xsum;              // [ntok][cols / 32] per-block sums of xq (read when x_global)
+    int x_global;                 // 1: rows too wide for shared memory, read from xq / xs / xsum
     const float* xf;              // when set: f32 rows [ntok][xf_stride], quantised in the prologue
     int xf_stride;
     int out_stride;
@@ -167,7 +169,9 @@ int peer_timeout_test_launch(TpComm c, int* err, cudaStream_t s);
 int batch_plan(int qtype, int cols, int rows, bool dual, int ntok, BatchParams& p);
 int batch_gemv_launch(int qtype, int epi, const BatchParams& p, int grid, cudaStream_t s, bool pdl);
 int batch_prep_launch(const float* x, int x_stride, int n, int ntok, const float* norm_w, float eps,
-                      const float* ssq_tab, const int* toks, int8_t* xq, float* xs, cudaStream_t s, bool pdl);
+                      const float* ssq_tab, const int* toks, int8_t* xq, float* xs, int* xsum, cudaStream_t s,
+                      bool pdl);
+int block_sums_launch(const int8_t* xq, int64_t nblocks, int* xsum, cudaStream_t s);
 int embed_rows_launch(int type, const uint8_t* table, int64_t pitch, int emb, const int* toks, int ntok,
                       float* hidden, cudaStream_t s, bool pdl);
 int num_sms();

@@ -105,10 +105,23 @@ int32_t orc_dot_i8(const int8_t* a, const int8_t* b, int n) {
     return s;
 }
 
-/* q8.rs:2699-2702 dot_q4_0_q8_0_scalar / Q8_0Block::dot_i32 (q8.rs:505). */
+/* q8.rs:2699-2702 dot_q4_0_q8_0_scalar / Q8_0Block::dot_i32 (q8.rs:505).  The sums are
+ * exact in int32, so the loops are written to vectorise. */
+static inline int32_t q4_0_dot(const uint8_t* blk, const int8_t* x) {
+    int32_t s = 0;
+    for (int j = 0; j < 16; ++j) {
+        s += ((int32_t)(blk[2 + j] & 0x0f) - 8) * (int32_t)x[j];
+        s += ((int32_t)(blk[2 + j] >> 4) - 8) * (int32_t)x[j + 16];
+    }
+    return s;
+}
+static inline int32_t q8_0_dot(const uint8_t* blk, const int8_t* x) {
+    int32_t s = 0;
+    for (int j = 0; j < 32; ++j) s += (int32_t)(int8_t)blk[2 + j] * (int32_t)x[j];
+    return s;
+}
 int32_t orc_block_dot(int t, const uint8_t* blk, const int8_t* x) {
-    if (t == T_Q4_0) { int8_t w[32]; orc_q4_0_unpack(blk, w); return orc_dot_i8(w, x, 32); }
-    return orc_dot_i8((const int8_t*)(blk + 2), x, 32);
+    return t == T_Q4_0 ? q4_0_dot(blk, x) : q8_0_dot(blk, x);
 }
 
 /* q8.rs:2009-2018 q4_k_scale_min. */
@@ -264,31 +277,29 @@ void orc_quantize_q8_0(const float* x, int n, int8_t* xq, float* xs) {
     }
 }
 
-/* q8.rs:2389-2440 quantize_f32_matrix_to_q8_0_blocks (f16-truncated scale). */
+/* q8.rs:2389-2440 quantize_f32_matrix_to_q8_0_blocks (f16-truncated scale), one block. */
+void orc_quantize_block_q8_0(const float* c, uint8_t* o) {
+    float max_abs = 0.0f;
+    for (int i = 0; i < 32; ++i) { float a = fabsf(c[i]); if (a > max_abs) max_abs = a; }
+    float scale = max_abs / 127.0f;
+    int8_t q[32]; memset(q, 0, 32);
+    if (scale > 0.0f) {
+        float inv = 1.0f / scale;
+        for (int i = 0; i < 32; ++i) {
+            float t = roundf(c[i] * inv);
+            if (t < -127.0f) t = -127.0f;
+            if (t > 127.0f) t = 127.0f;
+            q[i] = (int8_t)t;
+        }
+    }
+    uint16_t sb = orc_f32_to_f16(scale);
+    o[0] = sb & 0xff; o[1] = sb >> 8; memcpy(o + 2, q, 32);
+}
 void orc_quantize_matrix_q8_0(const float* v, long rows, int cols, uint8_t* out) {
     int nb = cols / 32;
     #pragma omp parallel for schedule(static) if (rows >= 128)
-    for (long r = 0; r < rows; ++r) {
-        for (int b = 0; b < nb; ++b) {
-            const float* c = v + r * cols + b * 32;
-            uint8_t* o = out + ((size_t)r * nb + b) * 34;
-            float max_abs = 0.0f;
-            for (int i = 0; i < 32; ++i) { float a = fabsf(c[i]); if (a > max_abs) max_abs = a; }
-            float scale = max_abs / 127.0f;
-            int8_t q[32]; memset(q, 0, 32);
-            if (scale > 0.0f) {
-                float inv = 1.0f / scale;
-                for (int i = 0; i < 32; ++i) {
-                    float t = roundf(c[i] * inv);
-                    if (t < -127.0f) t = -127.0f;
-                    if (t > 127.0f) t = 127.0f;
-                    q[i] = (int8_t)t;
-                }
-            }
-            uint16_t sb = orc_f32_to_f16(scale);
-            o[0] = sb & 0xff; o[1] = sb >> 8; memcpy(o + 2, q, 32);
-        }
-    }
+    for (long r = 0; r < rows; ++r)
+        for (int b = 0; b < nb; ++b) orc_quantize_block_q8_0(v + r * cols + b * 32, out + ((size_t)r * nb + b) * 34);
 }
 
 /* q8.rs:2442-2488 quantize_f32_matrix_to_q4_0_blocks: d = signed-max/-8, q = trunc(x*id + 8.5). */
@@ -354,9 +365,39 @@ void orc_matmul_quantized(int t, const uint8_t* w, long rows, int cols, const in
 void orc_matmul_quantized_batch(int t, const uint8_t* w, long rows, int cols, int ntok, const int8_t* xq, const float* xs, float* out) {
     size_t rb = orc_row_bytes(t, cols);
     int nbs = cols / 32;
-    #pragma omp parallel for schedule(static) if (rows >= 128)
-    for (long r = 0; r < rows; ++r)
-        for (int k = 0; k < ntok; ++k) out[(size_t)k * rows + r] = row_dot(t, w + r * rb, cols, xq + (size_t)k * cols, xs + (size_t)k * nbs);
+    if (t != T_Q4_0 && t != T_Q8_0) {
+        #pragma omp parallel for schedule(static) if (rows >= 128)
+        for (long r = 0; r < rows; ++r)
+            for (int k = 0; k < ntok; ++k) out[(size_t)k * rows + r] = row_dot(t, w + r * rb, cols, xq + (size_t)k * cols, xs + (size_t)k * nbs);
+        return;
+    }
+    /* Q4_0 / Q8_0: the same per-token sums (block order, one f32 accumulator per token),
+     * walking each weight block once for all tokens. */
+    #pragma omp parallel
+    {
+        float* acc = (float*)malloc(sizeof(float) * (size_t)ntok);
+        size_t bb = orc_block_bytes(t);
+        #pragma omp for schedule(static)
+        for (long r = 0; r < rows; ++r) {
+            const uint8_t* row = w + r * rb;
+            for (int k = 0; k < ntok; ++k) acc[k] = 0.0f;
+            for (int b = 0; b < nbs; ++b) {
+                const uint8_t* blk = row + b * bb;
+                const float d = rd16(blk);
+                int8_t wv[32];
+                if (t == T_Q4_0) orc_q4_0_unpack(blk, wv);
+                else memcpy(wv, blk + 2, 32);
+                for (int k = 0; k < ntok; ++k) {
+                    const int8_t* x = xq + (size_t)k * cols + b * 32;
+                    int32_t dot = 0;
+                    for (int j = 0; j < 32; ++j) dot += (int32_t)wv[j] * (int32_t)x[j];
+                    acc[k] += d * xs[(size_t)k * nbs + b] * (float)dot;
+                }
+            }
+            for (int k = 0; k < ntok; ++k) out[(size_t)k * rows + r] = acc[k];
+        }
+        free(acc);
+    }
 }
 
 /* Per-block integer dot dump (the bit-exact gate): Q4_0/Q8_0 -> rows x (cols/32) i32;
@@ -696,6 +737,37 @@ void orc_embed_row(const orc_model* m, int token, float* out) {
     orc_dequant_row(m->embd_type, m->embd + (size_t)token * orc_row_bytes(m->embd_type, m->emb), m->emb, out);
 }
 
+/* model.rs:471-508: the tied head is the Q4_0 re-quantisation of the dequantised f32
+ * token_embd table, block by block (q8.rs:2442-2488). */
+static void tied_head(orc_model* m) {
+    long V = m->vocab; int H = m->emb, nb = H / 32;
+    m->head.type = T_Q4_0; m->head.rows = V; m->head.cols = H;
+    m->head.owned = (uint8_t*)malloc((size_t)V * nb * 18);
+    m->head.data = m->head.owned;
+    #pragma omp parallel
+    {
+        float* row = (float*)malloc(sizeof(float) * H);
+        #pragma omp for schedule(static)
+        for (long r = 0; r < V; ++r) {
+            orc_embed_row(m, (int)r, row);
+            for (int b = 0; b < nb; ++b) orc_quantize_block_q4_0(row + b * 32, m->head.owned + ((size_t)r * nb + b) * 18);
+        }
+        free(row);
+    }
+}
+
+/* KV cache [layer][ctx][kv_width] f32 (inference.rs:505-547) and the per-token workspace
+ * (inference.rs:601-695). */
+static void alloc_workspace(orc_model* m) {
+    size_t kvn = (size_t)m->layers * m->ctx * m->kvw;
+    m->kc = (float*)calloc(kvn, 4); m->vc = (float*)calloc(kvn, 4);
+    int mx = m->emb > m->qw ? m->emb : m->qw; if (m->ffn > mx) mx = m->ffn;
+    m->hidden = calloc(m->emb, 4); m->residual = calloc(m->emb, 4); m->norm_x = calloc(m->emb, 4);
+    m->q = calloc(m->qw, 4); m->k = calloc(m->kvw, 4); m->v = calloc(m->kvw, 4); m->att = calloc(m->qw, 4);
+    m->gate = calloc(m->ffn, 4); m->up = calloc(m->ffn, 4); m->gu = calloc(m->ffn, 4);
+    m->logits = calloc(m->vocab, 4); m->xq = calloc(mx, 1); m->xs = calloc(mx / 32 + 1, 4);
+}
+
 /* model.rs:461-545 LlamaWeights::load.  Tied head (model.rs:471-532, default
  * NANOCAMELID_Q4_HEAD=on via model.rs:1429-1442): Q4_0 re-quantisation of the
  * dequantised f32 token_embd table, block by block. */
@@ -712,22 +784,7 @@ orc_model* orc_model_load(const char* path, int ctx_limit) {
     if (!te) return NULL;
     m->embd_type = te->type; m->embd = tensor_data(g, te);
     m->out_norm = load_f32(g, "output_norm.weight", m->emb);
-    if (load_q(g, "output.weight", &m->head) != 0) {
-        long V = m->vocab; int H = m->emb, nb = H / 32;
-        m->head.type = T_Q4_0; m->head.rows = V; m->head.cols = H;
-        m->head.owned = (uint8_t*)malloc((size_t)V * nb * 18);
-        m->head.data = m->head.owned;
-        #pragma omp parallel
-        {
-            float* row = (float*)malloc(sizeof(float) * H);
-            #pragma omp for schedule(static)
-            for (long r = 0; r < V; ++r) {
-                orc_embed_row(m, (int)r, row);
-                for (int b = 0; b < nb; ++b) orc_quantize_block_q4_0(row + b * 32, m->head.owned + ((size_t)r * nb + b) * 18);
-            }
-            free(row);
-        }
-    }
+    if (load_q(g, "output.weight", &m->head) != 0) tied_head(m);
     m->L = (orc_layer*)calloc(m->layers, sizeof(orc_layer));
     char nm[128];
     for (int i = 0; i < m->layers; ++i) {
@@ -739,14 +796,175 @@ orc_model* orc_model_load(const char* path, int ctx_limit) {
         LQ(w1, "ffn_gate") LQ(w3, "ffn_up") LQ(w2, "ffn_down")
 #undef LQ
     }
-    size_t kvn = (size_t)m->layers * m->ctx * m->kvw;
-    m->kc = (float*)calloc(kvn, 4); m->vc = (float*)calloc(kvn, 4);
-    int mx = m->emb > m->qw ? m->emb : m->qw; if (m->ffn > mx) mx = m->ffn;
-    m->hidden = calloc(m->emb, 4); m->residual = calloc(m->emb, 4); m->norm_x = calloc(m->emb, 4);
-    m->q = calloc(m->qw, 4); m->k = calloc(m->kvw, 4); m->v = calloc(m->kvw, 4); m->att = calloc(m->qw, 4);
-    m->gate = calloc(m->ffn, 4); m->up = calloc(m->ffn, 4); m->gu = calloc(m->ffn, 4);
-    m->logits = calloc(m->vocab, 4); m->xq = calloc(mx, 1); m->xs = calloc(mx / 32 + 1, 4);
+    alloc_workspace(m);
     return m;
+}
+
+/* ------------------------------------------------------------------ synthetic models
+ * The BASELINE configs are random-init models (weights ~ N(0, 0.02), quantised; norms
+ * all ones; no checkpoint exists).  The generator that defines those weights is restated
+ * here independently of the product library, so that the CPU baseline builds its model in
+ * host memory without loading the product or writing a multi-GB GGUF file:
+ *   key(tensor)   = splitmix64(FNV-1a64(name) ^ splitmix64(seed))
+ *   value(key, i) = (sum of the four 16-bit lanes of splitmix64(key + i) - 131070) * C,
+ *                   C = 0.02 sqrt(3) / 65536 rounded to f32 (Irwin-Hall(4), integer only),
+ *   element i = row * cols + col of the full tensor;
+ * then each block goes through the reference's matrix quantisers (Q4_0 q8.rs:2442-2488,
+ * Q8_0 q8.rs:2389-2440).  The reference has no Q4_K encoder (it only decodes Q4_K,
+ * q8.rs:1193-1376); the Q4_K blocks are a min/max encoder with 6-bit scales packed the way
+ * q8.rs:2009-2018 reads them.  tests/test_cpu_host.py checks every block type against the
+ * product's host generator byte for byte. */
+typedef struct {
+    int32_t emb, layers, heads, kv_heads, head_dim, ffn, vocab, ctx;
+    float rope_base, eps;
+    int32_t tied, t_embd, t_attn, t_ffn, t_out;
+    uint64_t seed;
+} orc_synth_spec;
+
+static uint64_t syn_mix(uint64_t x) {   /* splitmix64 */
+    uint64_t z = x + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+static float syn_value(uint64_t key, uint64_t idx) {
+    uint64_t h = syn_mix(key + idx);
+    int s = (int)(h & 0xffff) + (int)((h >> 16) & 0xffff) + (int)((h >> 32) & 0xffff) + (int)(h >> 48);
+    return (float)(s - 131070) * 0x1.1bc77ap-21f;
+}
+uint64_t orc_synth_key(uint64_t seed, const char* name) {
+    uint64_t h = 0xcbf29ce484222325ull;
+    for (const char* p = name; *p; ++p) { h ^= (uint8_t)*p; h *= 0x100000001b3ull; }
+    return syn_mix(h ^ syn_mix(seed));
+}
+
+/* Q4_K: per 32-value sub-block j the range [min(0, lo), hi] on a 15-step grid; scales and
+ * mins as 6-bit multiples of d = max(scale)/63 and dmin = max(min)/63 (f16, truncated). */
+static void syn_encode_q4_k(const float* v, uint8_t* o) {
+    float scf[8], mnf[8], maxsc = 0.0f, maxmn = 0.0f;
+    for (int j = 0; j < 8; ++j) {
+        float lo = v[32 * j], hi = v[32 * j];
+        for (int l = 1; l < 32; ++l) { float x = v[32 * j + l]; if (x < lo) lo = x; if (x > hi) hi = x; }
+        if (lo > 0.0f) lo = 0.0f;
+        scf[j] = (hi - lo) / 15.0f;
+        mnf[j] = -lo;
+        if (scf[j] > maxsc) maxsc = scf[j];
+        if (mnf[j] > maxmn) maxmn = mnf[j];
+    }
+    uint16_t db = orc_f32_to_f16(maxsc / 63.0f), mb = orc_f32_to_f16(maxmn / 63.0f);
+    float dd = orc_f16_to_f32(db), dm = orc_f16_to_f32(mb);
+    int sc[8], mn[8];
+    for (int j = 0; j < 8; ++j) {
+        float a = dd > 0.0f ? roundf(scf[j] / dd) : 0.0f;
+        float b = dm > 0.0f ? roundf(mnf[j] / dm) : 0.0f;
+        sc[j] = a < 0.0f ? 0 : (a > 63.0f ? 63 : (int)a);
+        mn[j] = b < 0.0f ? 0 : (b > 63.0f ? 63 : (int)b);
+    }
+    o[0] = db & 0xff; o[1] = db >> 8; o[2] = mb & 0xff; o[3] = mb >> 8;
+    uint8_t* s = o + 4;
+    for (int j = 0; j < 4; ++j) {   /* the inverse of q8.rs:2009-2018 */
+        s[j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+        s[j + 4] = (uint8_t)((mn[j] & 63) | ((mn[j + 4] >> 4) << 6));
+        s[j + 8] = (uint8_t)((sc[j + 4] & 15) | ((mn[j + 4] & 15) << 4));
+    }
+    for (int p = 0; p < 4; ++p)
+        for (int l = 0; l < 32; ++l) {
+            int q[2];
+            for (int h = 0; h < 2; ++h) {
+                int j = 2 * p + h;
+                float ds = dd * (float)sc[j], dmv = dm * (float)mn[j];
+                float t = ds > 0.0f ? roundf((v[32 * j + l] + dmv) / ds) : 0.0f;
+                q[h] = t < 0.0f ? 0 : (t > 15.0f ? 15 : (int)t);
+            }
+            o[16 + 32 * p + l] = (uint8_t)(q[0] | (q[1] << 4));
+        }
+}
+
+/* Rows [r0, r0 + nrows) x columns [c0, c0 + ncols) of a synthetic tensor `cols` wide,
+ * raw blocks, row-major, no padding. */
+void orc_synth_tensor(int type, uint64_t key, long r0, long nrows, long c0, long ncols, long cols, uint8_t* out) {
+    int be = (int)orc_block_elems(type), bb = (int)orc_block_bytes(type);
+    long bpr = ncols / be;
+    size_t rb = (size_t)bpr * bb;
+    #pragma omp parallel for schedule(static)
+    for (long r = 0; r < nrows; ++r) {
+        float v[256];
+        for (long b = 0; b < bpr; ++b) {
+            uint64_t base = (uint64_t)(r0 + r) * (uint64_t)cols + (uint64_t)(c0 + b * be);
+            uint8_t* o = out + (size_t)r * rb + (size_t)b * bb;
+            for (int i = 0; i < be; ++i) v[i] = syn_value(key, base + i);
+            if (type == T_Q4_0) orc_quantize_block_q4_0(v, o);
+            else if (type == T_Q8_0) orc_quantize_block_q8_0(v, o);
+            else if (type == T_Q4_K) syn_encode_q4_k(v, o);
+            else if (type == T_F32) memcpy(o, &v[0], 4);
+            else { uint16_t h = orc_f32_to_f16(v[0]); o[0] = h & 0xff; o[1] = h >> 8; }
+        }
+    }
+}
+
+static uint8_t* syn_alloc_tensor(const orc_synth_spec* sp, const char* name, int type, long rows, long cols) {
+    uint8_t* d = (uint8_t*)malloc(orc_row_bytes(type, (int)cols) * (size_t)rows);
+    if (d) orc_synth_tensor(type, orc_synth_key(sp->seed, name), 0, rows, 0, cols, cols, d);
+    return d;
+}
+static int syn_mat(const orc_synth_spec* sp, const char* name, int type, long rows, int cols, qmat* m) {
+    m->type = type; m->rows = rows; m->cols = cols;
+    m->owned = syn_alloc_tensor(sp, name, type, rows, cols);
+    m->data = m->owned;
+    return m->owned ? 0 : -1;
+}
+static float* syn_ones(int n) {
+    float* v = (float*)malloc(4 * (size_t)n);
+    for (int i = 0; i < n; ++i) v[i] = 1.0f;
+    return v;
+}
+
+/* The synthetic model in host memory, exactly as orc_model_load would read it from the
+ * synthetic GGUF file of the same spec (rope_dim = head_dim; context = spec ctx). */
+orc_model* orc_model_create_synthetic(const orc_synth_spec* sp, int ctx_limit) {
+    orc_model* m = (orc_model*)calloc(1, sizeof(orc_model));
+    m->emb = sp->emb; m->layers = sp->layers; m->ffn = sp->ffn; m->heads = sp->heads; m->kv_heads = sp->kv_heads;
+    m->hd = sp->head_dim; m->vocab = sp->vocab; m->rope_dim = sp->head_dim; m->eps = sp->eps; m->base = sp->rope_base;
+    m->ctx = (ctx_limit > 0 && ctx_limit < sp->ctx) ? ctx_limit : sp->ctx;
+    m->qw = m->heads * m->hd; m->kvw = m->kv_heads * m->hd;
+    const int H = m->emb, F = m->ffn, QW = m->qw, KW = m->kvw;
+    m->embd_type = sp->t_embd;
+    m->embd = syn_alloc_tensor(sp, "token_embd.weight", sp->t_embd, m->vocab, H);
+    if (!m->embd) return NULL;
+    m->out_norm = syn_ones(H);
+    if (sp->tied) tied_head(m);
+    else if (syn_mat(sp, "output.weight", sp->t_out, m->vocab, H, &m->head)) return NULL;
+    m->L = (orc_layer*)calloc(m->layers, sizeof(orc_layer));
+    char nm[128];
+    for (int i = 0; i < m->layers; ++i) {
+        orc_layer* l = &m->L[i];
+        l->attn_norm = syn_ones(H);
+        l->ffn_norm = syn_ones(H);
+#define SQ(field, s, t, r, c) snprintf(nm, sizeof nm, "blk.%d." s ".weight", i); if (syn_mat(sp, nm, t, r, c, &l->field)) return NULL;
+        SQ(wq, "attn_q", sp->t_attn, QW, H) SQ(wk, "attn_k", sp->t_attn, KW, H) SQ(wv, "attn_v", sp->t_attn, KW, H)
+        SQ(wo, "attn_output", sp->t_attn, H, QW) SQ(w1, "ffn_gate", sp->t_ffn, F, H) SQ(w3, "ffn_up", sp->t_ffn, F, H)
+        SQ(w2, "ffn_down", sp->t_ffn, H, F)
+#undef SQ
+    }
+    alloc_workspace(m);
+    return m;
+}
+
+/* Fills K/V of positions [0, npos) of every layer with seeded values of the size the
+ * projections produce (|x| < 0.5), so that a decode step at position npos does the same
+ * attention work as after an npos-token prompt (the timed CPU sample of long contexts). */
+void orc_model_fill_kv(orc_model* m, int npos, uint64_t seed) {
+    if (npos > m->ctx) npos = m->ctx;
+    size_t per = (size_t)npos * m->kvw;
+    #pragma omp parallel for schedule(static)
+    for (int li = 0; li < m->layers; ++li) {
+        size_t lo = (size_t)li * m->ctx * m->kvw;
+        uint64_t kk = orc_synth_key(seed, "kv.k") + (uint64_t)li * per, kv = orc_synth_key(seed, "kv.v") + (uint64_t)li * per;
+        for (size_t i = 0; i < per; ++i) {
+            m->kc[lo + i] = syn_value(kk, i) * 16.0f;
+            m->vc[lo + i] = syn_value(kv, i) * 16.0f;
+        }
+    }
 }
 
 int orc_model_info(const orc_model* m, int* out) {
@@ -880,6 +1098,30 @@ void orc_prefill_batch(orc_model* m, const int* tokens, int n, int start_pos, fl
     }
     memcpy(hidden_out, hid, 4 * (size_t)n * H);
     free(hid); free(res); free(nx); free(q); free(k); free(v); free(att); free(g); free(u); free(gu); free(xq); free(xs);
+}
+
+/* orc_generate with the prompt ingested `chunk` rows per orc_prefill_batch pass (the
+ * reference's batched prefill; every row equals the one-token step, inference.rs:6866-6913),
+ * then the greedy loop of bin/cluster_tp_node.rs:808-875. */
+int orc_generate_batched(orc_model* m, const int* prompt, int n_prompt, int n_gen, int chunk, int* out, float* last_logits) {
+    if (chunk < 1) chunk = 1;
+    float* hid = (float*)malloc(4 * (size_t)chunk * m->emb);
+    int next = 0, pos = 0;
+    for (int c0 = 0; c0 < n_prompt; c0 += chunk) {
+        int n = n_prompt - c0 < chunk ? n_prompt - c0 : chunk;
+        orc_prefill_batch(m, prompt + c0, n, c0, hid);
+        if (c0 + n == n_prompt) {
+            orc_compute_logits(m, hid + (size_t)(n - 1) * m->emb, m->logits);
+            next = orc_argmax(m->logits, m->vocab);
+        }
+    }
+    free(hid);
+    pos = n_prompt;
+    for (int g = 0; g < n_gen && pos < m->ctx; ++g) {
+        out[g] = next;
+        next = orc_forward_pass(m, next, pos++, (g + 1 == n_gen) ? last_logits : NULL);
+    }
+    return next;
 }
 
 /* speculative.rs:299-494 speculative_decoding_step (greedy, no stop tokens).

@@ -15,6 +15,21 @@ LIB_PATH = os.path.join(HERE, "liboracle.so")
 _lib = None
 
 
+class SynthSpec(ctypes.Structure):
+    """orc_synth_spec: a random-init llama model (the BASELINE configs' weights)."""
+    _fields_ = [("emb", ctypes.c_int32), ("layers", ctypes.c_int32), ("heads", ctypes.c_int32),
+                ("kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("ffn", ctypes.c_int32),
+                ("vocab", ctypes.c_int32), ("ctx", ctypes.c_int32), ("rope_base", ctypes.c_float),
+                ("eps", ctypes.c_float), ("tied", ctypes.c_int32), ("t_embd", ctypes.c_int32),
+                ("t_attn", ctypes.c_int32), ("t_ffn", ctypes.c_int32), ("t_out", ctypes.c_int32),
+                ("seed", ctypes.c_uint64)]
+
+    @classmethod
+    def of(cls, spec):
+        """From any object with the same field names (e.g. the product's spec)."""
+        return cls(*[getattr(spec, k) for k, _ in cls._fields_])
+
+
 def build():
     r = subprocess.run(["make", "-C", HERE, "-s"], capture_output=True, text=True)
     if r.returncode != 0:
@@ -55,6 +70,11 @@ def lib():
         "orc_kv_store_f16": (None, [P, I, P]),
         "orc_argmax": (I, [P, L64]),
         "orc_model_load": (P, [ctypes.c_char_p, I]),
+        "orc_model_create_synthetic": (P, [ctypes.POINTER(SynthSpec), I]),
+        "orc_model_fill_kv": (None, [P, I, ctypes.c_uint64]),
+        "orc_synth_key": (ctypes.c_uint64, [ctypes.c_uint64, ctypes.c_char_p]),
+        "orc_synth_tensor": (None, [I, ctypes.c_uint64, L64, L64, L64, L64, L64, P]),
+        "orc_generate_batched": (I, [P, P, I, I, I, P, P]),
         "orc_model_info": (I, [P, P]),
         "orc_model_reset": (None, [P]),
         "orc_model_head_blocks": (P, [P]),
@@ -115,11 +135,29 @@ def block_dots(qtype, w, rows, cols, xq):
     return out
 
 
+def synth_tensor(spec, name, qtype, r0, r1, c0, c1, cols):
+    """Raw blocks of rows [r0, r1) x columns [c0, c1) of a synthetic tensor (the oracle's
+    own generator)."""
+    be = 256 if qtype == 12 else (32 if qtype in (2, 8) else 1)
+    bb = {2: 18, 8: 34, 12: 144, 0: 4, 1: 2}[qtype]
+    out = np.zeros((r1 - r0) * ((c1 - c0) // be) * bb, dtype=np.uint8)
+    sp = SynthSpec.of(spec)
+    key = lib().orc_synth_key(sp.seed, name.encode())
+    lib().orc_synth_tensor(qtype, key, r0, r1 - r0, c0, c1 - c0, cols, ptr(out))
+    return out.tobytes()
+
+
 class OracleModel:
-    def __init__(self, path, ctx_limit=0):
-        self.h = lib().orc_model_load(str(path).encode(), ctx_limit)
+    def __init__(self, path=None, ctx_limit=0, spec=None):
+        """From a GGUF file, or (spec=...) the synthetic model of that spec built in host
+        memory by the oracle's own generator."""
+        if spec is not None:
+            self._spec = SynthSpec.of(spec)
+            self.h = lib().orc_model_create_synthetic(ctypes.byref(self._spec), ctx_limit)
+        else:
+            self.h = lib().orc_model_load(str(path).encode(), ctx_limit)
         if not self.h:
-            raise RuntimeError(f"oracle could not load {path}")
+            raise RuntimeError(f"oracle could not build the model ({path or 'synthetic'})")
         info = np.zeros(10, dtype=np.int32)
         lib().orc_model_info(self.h, ptr(info))
         (self.emb, self.layers, self.ffn, self.heads, self.kv_heads, self.head_dim, self.vocab, self.rope_dim,
@@ -139,6 +177,18 @@ class OracleModel:
         lg = np.zeros(self.vocab, dtype=np.float32) if want_last_logits else None
         lib().orc_generate(self.h, ptr(p), len(p), n_gen, ptr(out), ptr(lg) if want_last_logits else None)
         return [int(v) for v in out[:n_gen]], lg
+
+    def generate_batched(self, prompt, n_gen, chunk=64, want_last_logits=False):
+        """orc_generate with the prompt ingested `chunk` rows per batched pass (bit-identical
+        to token-by-token, inference.rs:6866-6913)."""
+        p = np.asarray(prompt, dtype=np.int32)
+        out = np.zeros(max(1, n_gen), dtype=np.int32)
+        lg = np.zeros(self.vocab, dtype=np.float32) if want_last_logits else None
+        lib().orc_generate_batched(self.h, ptr(p), len(p), n_gen, chunk, ptr(out), ptr(lg) if want_last_logits else None)
+        return [int(v) for v in out[:n_gen]], lg
+
+    def fill_kv(self, npos, seed=0):
+        lib().orc_model_fill_kv(self.h, npos, seed)
 
     def buf(self, which, n, layer=0):
         p = lib().orc_model_buf(self.h, which, layer)

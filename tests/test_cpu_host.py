@@ -149,6 +149,36 @@ def test_gguf_writer_blocks_equal_host_generator(ncm, tmp_path):
         assert part == exp, name
 
 
+@pytest.mark.parametrize("qtype", ["Q4_0", "Q8_0", "Q4_K"])
+def test_oracle_generator_equals_product_generator(ncm, orc, qtype):
+    """The oracle's own restatement of the synthetic-weight generator (used by the CPU
+    baseline, which loads no product code) gives the product's bytes, slices included."""
+    t = getattr(ncm, qtype)
+    sp = tiny(ncm, emb=512, ffn=1024, seed=23)
+    for name, rows, cols in [("blk.0.ffn_gate.weight", 5, 512), ("blk.1.ffn_down.weight", 3, 1024)]:
+        assert orc.synth_tensor(sp, name, t, 0, rows, 0, cols, cols) == \
+            ncm.synth_tensor_bytes(sp, name, t, 0, rows, 0, cols, cols), name
+        e = 256 if t == ncm.Q4_K else 32
+        assert orc.synth_tensor(sp, name, t, 1, 3, e, 3 * e, cols) == \
+            ncm.synth_tensor_bytes(sp, name, t, 1, 3, e, 3 * e, cols), name
+
+
+@pytest.mark.parametrize("kw", [dict(tied=True), dict(tied=False, t_embd=8, t_attn=8, t_ffn=12, t_out=8, ffn=768)])
+def test_oracle_synthetic_model_equals_gguf_model(ncm, orc, tmp_path, kw):
+    """orc_model_create_synthetic builds in memory exactly the model orc_model_load reads
+    from the synthetic GGUF file; the batched prefill decodes like the token-by-token one."""
+    sp = tiny(ncm, **kw)
+    path = tmp_path / "m.gguf"
+    ncm.write_synthetic_gguf(path, sp)
+    prompt = _prompt(7, sp.vocab, 3)
+    a = orc.OracleModel(path).generate(prompt, 6, want_last_logits=True)
+    b = orc.OracleModel(spec=sp).generate(prompt, 6, want_last_logits=True)
+    c = orc.OracleModel(spec=sp).generate_batched(prompt, 6, chunk=3, want_last_logits=True)
+    assert a[0] == b[0] == c[0]
+    assert np.array_equal(a[1].view(np.uint32), b[1].view(np.uint32))
+    assert np.array_equal(a[1].view(np.uint32), c[1].view(np.uint32))
+
+
 def test_gguf_writer_is_deterministic_and_loads(ncm, orc, tmp_path):
     sp = tiny(ncm)
     a, b = tmp_path / "a.gguf", tmp_path / "b.gguf"
