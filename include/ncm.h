@@ -87,14 +87,15 @@ ncm_status ncm_attention(float* out, const float* q, const float* k_cache, const
  * run under a fixed memory budget with allocation forbidden after start-up.  The
  * softmax-score scratch is a fixed 1 MiB array (262144 floats) compiled into the
  * library, held by every GPU that loads it until the process exits; calls with
- * heads * (pos + 1) > 262144 are rejected with NCM_EINVAL.  The first call on a device
- * looks up that device's copy of the array (cudaGetSymbolAddress), so make it once on
- * each device before any stream capture.  All calls on a device share the one array:
- * calls that can overlap on the GPU race, so serialise them (one stream, or events).
- * Nothing in it needs clearing, because each call writes every score it reads.  The
- * launch is stream ordered and does not synchronise.  exp matches the host glibc bit
- * for bit only after an allocating call (a model load, ncm_attention or
- * ncm_fused_silu_mul) has set up the exp table on this device. */
+ * pos >= 16384 (the limit ncm_attention has too) or heads * (pos + 1) > 262144 are
+ * rejected with NCM_EINVAL.  The first call on a device does that device's set-up: it
+ * looks up the device's copy of the array (cudaGetSymbolAddress) and copies the glibc
+ * expf exception table (built on the host, once per process, about two seconds) into
+ * its own fixed in-library array, so that exp matches the host glibc bit for bit; make
+ * that first call once on each device before any stream capture.  All calls on a device
+ * share the one scratch array: calls that can overlap on the GPU race, so serialise them
+ * (one stream, or events).  Nothing in it needs clearing, because each call writes every
+ * score it reads.  The launch is stream ordered and does not synchronise. */
 ncm_status ncm_attention_noalloc(float* out, const float* q, const float* k_cache, const float* v_cache, int pos,
                                  int heads, int kv_heads, int head_dim, void* stream);
 

@@ -98,6 +98,12 @@ struct ncm_model {
     unsigned* amax_cnt = nullptr;
     float2 *amax_part = nullptr, *rope = nullptr, *head_out = nullptr, *gather = nullptr;
     float* embd_ssq = nullptr;   // per vocab row: sequential f32 sum of squares of the embedding
+    // the attention output and silu(gate)*up as Q8_0 blocks, written by their producing
+    // kernels, read by the row-parallel projections (wo, w2) of the decode step
+    int8_t *att_q = nullptr, *act_q = nullptr;
+    float *att_s = nullptr, *act_s = nullptr;
+    bool act_quantised = false;   // the gate/up plan allows the quantised hand-off (32-row tiles)
+    int64_t prefetch_bytes = 320 * 1024;   // per CTA: next kernel's weights streamed into L2
     int *state = nullptr, *tokens = nullptr, *err = nullptr;
     int* h_stage = nullptr;   // pinned staging for small transfers
     cudaStream_t ext_stream = nullptr;   // caller stream of the last prefill / decode, until synced
@@ -199,12 +205,14 @@ extern "C" ncm_status ncm_shard_geometry(int heads, int kv_heads, int ffn, int v
 
 // Common set-up once the global config is known: shard geometry, activation buffers,
 // KV cache, rope table, state.
-// The exp exception table (libm_table.cpp) is built once per process and uploaded once
-// per device; every kernel that evaluates exp on that device then matches glibc's expf.
+// The exp exception table (libm_table.cpp) is built once per process and copied once
+// per device into the library's fixed device array (no device allocation); every kernel
+// that evaluates exp on that device then matches glibc's expf.
 static ncm_status ensure_expf_table(int device) {
     static std::mutex mu;
     static std::vector<uint32_t> host_tab;
     static uint32_t mask = 0;
+    static int gate = 1;
     static std::vector<int> done;
     std::lock_guard<std::mutex> lk(mu);
     for (int d : done)
@@ -212,12 +220,12 @@ static ncm_status ensure_expf_table(int device) {
     if (host_tab.empty()) {
         size_t count = 0;
         unsigned hc = std::thread::hardware_concurrency();
-        host_tab = build_expf_exceptions(hc ? (int)hc : 8, &mask, &count);
+        host_tab = build_expf_exceptions(hc ? (int)hc : 8, kExpfTabEntries, &mask, &count, &gate);
+        if (host_tab.empty())
+            return fail(NCM_EUNSUPPORTED, "this libm's expf has " + std::to_string(count) +
+                                              " exceptions, more than the device table holds");
     }
-    uint32_t* dtab = nullptr;
-    CK(cudaMalloc(&dtab, host_tab.size() * 4));   // process lifetime (one per device)
-    CK(cudaMemcpy(dtab, host_tab.data(), host_tab.size() * 4, cudaMemcpyHostToDevice));
-    CKL(expf_table_install(dtab, mask));
+    CKL(expf_table_install(host_tab.data(), host_tab.size() / 2, mask, gate));
     done.push_back(device);
     return NCM_OK;
 }
@@ -252,6 +260,10 @@ static ncm_status setup_buffers(ncm_model* m, const int* shares, int nshards, in
     DALLOC(m->act, 4 * m->fl);
     DALLOC(m->logits, 4 * (size_t)m->hr);
     DALLOC(m->part, 4 * m->emb);
+    DALLOC(m->att_q, qw);
+    DALLOC(m->att_s, 4 * (qw / 32));
+    DALLOC(m->act_q, m->fl);
+    DALLOC(m->act_s, 4 * (m->fl / 32));
     DALLOC(m->kc, 4 * (size_t)m->layers * m->ctx * kw);
     DALLOC(m->vc, 4 * (size_t)m->layers * m->ctx * kw);
     m->dsplit = 1;
@@ -333,9 +345,50 @@ static ncm_status upload_slice(ncm_model* m, const GgufFile& g, const char* name
     return NCM_OK;
 }
 
-static ncm_status upload_f32(ncm_model* m, const GgufFile& g, const char* name, int n, float** out) {
+// A norm vector: one dimension of exactly n elements, F32 or F16 (the reader has checked
+// that the tensor's bytes lie inside the file).
+static ncm_status check_norm(const GgufFile& g, const char* name, int n) {
     const GgufTensor* t = g.find(name);
     if (!t) return fail(NCM_EIO, std::string("missing tensor ") + name);
+    if (t->type != NCM_T_F32 && t->type != NCM_T_F16)
+        return fail(NCM_EUNSUPPORTED, std::string("norm tensor must be F32/F16: ") + name);
+    if (t->dims.size() != 1 || t->dims[0] != (uint64_t)n || t->nbytes < (uint64_t)n * (t->type == NCM_T_F32 ? 4 : 2))
+        return fail(NCM_EIO, std::string("norm tensor is not ") + std::to_string(n) + " elements long: " + name);
+    return NCM_OK;
+}
+
+// Host-side check of every tensor the loader reads (names, ranks, shapes), before any
+// device work, so that a malformed file fails with NCM_EIO instead of being read past.
+static ncm_status check_llama_tensors(const GgufFile& g) {
+    const uint64_t H = (uint64_t)g.emb, QW = (uint64_t)g.heads * g.head_dim, KW = (uint64_t)g.kv_heads * g.head_dim,
+                   F = (uint64_t)g.ffn, V = (uint64_t)g.vocab;
+    auto mat = [&](const std::string& name, uint64_t rows, uint64_t cols, bool required) -> ncm_status {
+        const GgufTensor* t = g.find(name);
+        if (!t) return required ? fail(NCM_EIO, "missing tensor " + name) : NCM_OK;
+        if (t->dims.size() != 2 || t->dims[0] != cols || t->dims[1] != rows)
+            return fail(NCM_EIO, "unexpected shape for " + name);
+        return NCM_OK;
+    };
+    ncm_status s;
+    if ((s = mat("token_embd.weight", V, H, true))) return s;
+    if ((s = mat("output.weight", V, H, false))) return s;
+    if ((s = check_norm(g, "output_norm.weight", g.emb))) return s;
+    for (int i = 0; i < g.layers; ++i) {
+        const std::string b = "blk." + std::to_string(i) + ".";
+        if ((s = check_norm(g, (b + "attn_norm.weight").c_str(), g.emb))) return s;
+        if ((s = check_norm(g, (b + "ffn_norm.weight").c_str(), g.emb))) return s;
+        if ((s = mat(b + "attn_q.weight", QW, H, true)) || (s = mat(b + "attn_k.weight", KW, H, true)) ||
+            (s = mat(b + "attn_v.weight", KW, H, true)) || (s = mat(b + "attn_output.weight", H, QW, true)) ||
+            (s = mat(b + "ffn_gate.weight", F, H, true)) || (s = mat(b + "ffn_up.weight", F, H, true)) ||
+            (s = mat(b + "ffn_down.weight", H, F, true)))
+            return s;
+    }
+    return NCM_OK;
+}
+
+static ncm_status upload_f32(ncm_model* m, const GgufFile& g, const char* name, int n, float** out) {
+    if (ncm_status s = check_norm(g, name, n)) return s;
+    const GgufTensor* t = g.find(name);
     std::vector<float> v(n);
     const uint8_t* d = g.data(*t);
     if (t->type == NCM_T_F32) memcpy(v.data(), d, 4 * (size_t)n);
@@ -359,6 +412,8 @@ static ncm_status build_tied_head(ncm_model* m) {
     return NCM_OK;
 }
 
+static GemvParams base_params(ncm_model* m);
+
 static ncm_status check_all_shapes(ncm_model* m) {
     ncm_status s;
     DALLOC(m->embd_ssq, 4 * (size_t)m->vocab);
@@ -375,6 +430,11 @@ static ncm_status check_all_shapes(ncm_model* m) {
     int t = m->embd.type;
     if (!(t == NCM_T_Q4_0 || t == NCM_T_Q8_0 || t == NCM_T_Q4_K || t == NCM_T_F32 || t == NCM_T_F16))
         return fail(NCM_EUNSUPPORTED, "token_embd type");
+    // gate/up can hand w2 its input as Q8_0 blocks when every tile is one 32-row block
+    GemvParams w = base_params(m);
+    w.row_align = 32;
+    const int g = m->fl % 32 == 0 ? gemv_plan(m->L[0].w1.type, m->emb, m->fl, true, IN_F32_RMS, w) : -1;
+    m->act_quantised = g > 0 && w.box_rows == 32;
     return NCM_OK;
 }
 
@@ -395,6 +455,9 @@ extern "C" ncm_status ncm_model_load(const char* path, int ctx_limit, int device
     GgufFile g;
     std::string err;
     if (!g.open(path, err)) return fail(NCM_EIO, err);
+    if (g.emb <= 0 || g.layers <= 0 || g.heads <= 0 || g.kv_heads <= 0 || g.head_dim <= 0 || g.vocab <= 0)
+        return fail(NCM_EIO, "incomplete llama metadata");
+    if (ncm_status cs = check_llama_tensors(g)) return cs;
     ncm_model* m = nullptr;
     ncm_status s = new_model(device, &m);
     if (s) return s;
@@ -529,7 +592,25 @@ static GemvParams base_params(ncm_model* m) {
     p.err = m->err;
     p.tp.world = 1;
     p.tp.timeout_ns = m->timeout_ns;
+    p.row_align = 2;
     return p;
+}
+
+// The next GEMV's weights, for the L2 prefetch a kernel issues once its own loads are
+// out: mats share one fused row space (wq/wk/wv), or are a dual pair (w1/w3).
+static void set_prefetch(ncm_model* m, GemvParams& p, std::initializer_list<const DevMat*> mats, bool dual) {
+    p.pf_nmat = 0;
+    int rows = 0;
+    for (const DevMat* d : mats) {
+        p.pf_base[p.pf_nmat] = d->d;
+        p.pf_pitch[p.pf_nmat] = d->pitch;
+        p.pf_rows[p.pf_nmat] = d->rows;
+        rows = dual ? d->rows : rows + d->rows;
+        ++p.pf_nmat;
+    }
+    p.pf_dual = dual ? 1 : 0;
+    p.pf_grid = std::max(1, std::min(num_sms(), rows / 2));
+    p.pf_bytes = m->prefetch_bytes;
 }
 
 // Plans the launch, encodes one TMA tensor map per weight matrix (box = the planned
@@ -575,29 +656,41 @@ static ncm_status host_reduce(ncm_model* m, void* dev, int n, int layer, int pha
 // Row-parallel projection (wo / w2) with its reduction: one GPU -> hidden += out;
 // fused P2P -> NVLink stores + rank-ordered sum in the epilogue; NCCL -> partial,
 // ncclAllReduce, residual add; host callback -> partial, host_fn, residual add.
-static ncm_status row_parallel(ncm_model* m, const DevMat& w, const float* x, int slot, cudaStream_t s) {
+// The input is the f32 vector x, or (xq non-null) its Q8_0 blocks as the producing kernel
+// wrote them (bit-identical to quantising x here).  `next` is prefetched into L2.
+static ncm_status row_parallel(ncm_model* m, const DevMat& w, const float* x, const int8_t* xq, const float* xs,
+                               int slot, const GemvParams* next, cudaStream_t s) {
     GemvParams p = base_params(m);
     p.nseg = 1;
     p.total_rows = m->emb;
     p.x = x;
+    p.xq = xq;
+    p.xs = xs;
+    const int in = xq ? IN_Q8 : IN_F32;
+    if (next) {
+        memcpy(p.pf_base, next->pf_base, sizeof p.pf_base);
+        memcpy(p.pf_pitch, next->pf_pitch, sizeof p.pf_pitch);
+        memcpy(p.pf_rows, next->pf_rows, sizeof p.pf_rows);
+        p.pf_nmat = next->pf_nmat; p.pf_grid = next->pf_grid; p.pf_dual = next->pf_dual; p.pf_bytes = next->pf_bytes;
+    }
     p.hidden = m->hidden;
     if (m->world == 1) {
         p.seg[0] = {m->hidden, m->emb, 0, SEG_OUT};
-        CKL(launch_gemv({&w}, nullptr, IN_F32, EPI_RESID, p, s));
+        CKL(launch_gemv({&w}, nullptr, in, EPI_RESID, p, s));
     } else if (m->reduce_mode == NCM_REDUCE_FUSED_P2P) {
         p.seg[0] = {nullptr, m->emb, 0, SEG_OUT};
         p.tp = m->comm;
         p.tp_slot = slot;
-        CKL(launch_gemv({&w}, nullptr, IN_F32, EPI_TP_RESID, p, s));
+        CKL(launch_gemv({&w}, nullptr, in, EPI_TP_RESID, p, s));
     } else if (m->reduce_mode == NCM_REDUCE_HOST_CALLBACK) {
         p.seg[0] = {m->part, m->emb, 0, SEG_OUT};
-        CKL(launch_gemv({&w}, nullptr, IN_F32, EPI_PLAIN, p, s));
+        CKL(launch_gemv({&w}, nullptr, in, EPI_PLAIN, p, s));
         ncm_status st = host_reduce(m, m->part, m->emb, slot / 2, slot % 2, s);
         if (st) return st;
         CKL(resid_add_launch(m->hidden, m->part, m->emb, s, true));
     } else {
         p.seg[0] = {m->part, m->emb, 0, SEG_OUT};
-        CKL(launch_gemv({&w}, nullptr, IN_F32, EPI_PLAIN, p, s));
+        CKL(launch_gemv({&w}, nullptr, in, EPI_PLAIN, p, s));
         int r = g_nccl.AllReduce(m->part, m->part, (size_t)m->emb, kNcclFloat, kNcclSum, m->nccl, s);
         if (r != 0) return fail(NCM_EPEER, "ncclAllReduce failed");
         CKL(resid_add_launch(m->hidden, m->part, m->emb, s, true));
@@ -605,7 +698,28 @@ static ncm_status row_parallel(ncm_model* m, const DevMat& w, const float* x, in
     return NCM_OK;
 }
 
+// Prefetch descriptors of the step's GEMVs (which weights each kernel streams into L2
+// for its successor).
+static GemvParams pf_of(ncm_model* m, std::initializer_list<const DevMat*> mats, bool dual) {
+    GemvParams p;
+    memset(&p, 0, sizeof p);
+    set_prefetch(m, p, mats, dual);
+    return p;
+}
+static GemvParams pf_qkv(ncm_model* m, int l) { return pf_of(m, {&m->L[l].wq, &m->L[l].wk, &m->L[l].wv}, false); }
+static GemvParams pf_w13(ncm_model* m, int l) { return pf_of(m, {&m->L[l].w1, &m->L[l].w3}, true); }
+static GemvParams pf_next_after_w2(ncm_model* m, int l) {
+    return l + 1 < m->layers ? pf_qkv(m, l + 1) : pf_of(m, {&m->head}, false);
+}
+static void copy_pf(GemvParams& p, const GemvParams& n) {
+    memcpy(p.pf_base, n.pf_base, sizeof p.pf_base);
+    memcpy(p.pf_pitch, n.pf_pitch, sizeof p.pf_pitch);
+    memcpy(p.pf_rows, n.pf_rows, sizeof p.pf_rows);
+    p.pf_nmat = n.pf_nmat; p.pf_grid = n.pf_grid; p.pf_dual = n.pf_dual; p.pf_bytes = n.pf_bytes;
+}
+
 // rms_norm -> quantize -> wq/wk/wv -> rope -> store_kv (inference.rs:4521-4646) of layer l.
+// It streams wo of the layer into L2 for the output projection after attention.
 static int launch_qkv(ncm_model* m, int l, cudaStream_t s) {
     const Layer& L = m->L[l];
     const int qw = m->qh * m->hd, kw = m->kh * m->hd;
@@ -621,10 +735,12 @@ static int launch_qkv(ncm_model* m, int l, cudaStream_t s) {
     p.vcache = m->vc + (size_t)l * m->ctx * kw;
     p.kv_width = kw;
     if (l == 0) p.ssq_tok = m->embd_ssq;
+    copy_pf(p, pf_of(m, {&L.wo}, false));
     return launch_gemv({&L.wq, &L.wk, &L.wv}, nullptr, IN_F32_RMS, EPI_QKV, p, s);
 }
 
-// rms_norm -> quantize -> w1, w3 -> silu*mul (inference.rs:4679-4730) of layer l.
+// rms_norm -> quantize -> w1, w3 -> silu*mul (inference.rs:4679-4730) of layer l; the
+// result also as Q8_0 blocks for w2 when the plan has 32-row tiles.  Streams w2 into L2.
 static int launch_w13(ncm_model* m, int l, cudaStream_t s) {
     const Layer& L = m->L[l];
     GemvParams f = base_params(m);
@@ -633,39 +749,55 @@ static int launch_w13(ncm_model* m, int l, cudaStream_t s) {
     f.total_rows = m->fl;
     f.x = m->hidden;
     f.norm_w = L.ffn_norm;
+    if (m->act_quantised) {
+        f.row_align = 32;
+        f.qout = m->act_q;
+        f.qout_s = m->act_s;
+    }
+    copy_pf(f, pf_of(m, {&L.w2}, false));
     return launch_gemv({&L.w1}, &L.w3, IN_F32_RMS, EPI_SILU, f, s);
 }
 
-static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
+static void attn_params(ncm_model* m, int l, AttnParams& a) {
     const int kw = m->kh * m->hd;
+    memset(&a, 0, sizeof a);
+    a.q = m->q;
+    a.kc = m->kc + (size_t)l * m->ctx * kw;
+    a.vc = m->vc + (size_t)l * m->ctx * kw;
+    a.out = m->att;
+    a.scores = m->scores;
+    a.state = m->state;
+    a.pos_override = -1;
+    a.heads = m->qh;
+    a.kv_heads = m->kh;
+    a.hd = m->hd;
+    a.kvw = kw;
+    a.ctx = m->ctx;
+    // one 32-dimension slice per CTA, so each warp's output is one Q8_0 block for wo
+    a.dsplit = m->hd / 32;
+    a.out_q = m->att_q;
+    a.out_s = m->att_s;
+    a.scale = 1.0f / sqrtf((float)m->hd);   // inference.rs:4653
+}
+
+static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
     CKL(embed_launch(m->embd.type, m->embd.d, m->embd.pitch, m->emb, m->tokens, m->state, m->hidden, s, true));
     for (int l = 0; l < m->layers; ++l) {
         const Layer& L = m->L[l];
         CKL(launch_qkv(m, l, s));
         // attention (inference.rs:4648-4665)
         AttnParams a;
-        memset(&a, 0, sizeof a);
-        a.q = m->q;
-        a.kc = m->kc + (size_t)l * m->ctx * kw;
-        a.vc = m->vc + (size_t)l * m->ctx * kw;
-        a.out = m->att;
-        a.scores = m->scores;
-        a.state = m->state;
-        a.pos_override = -1;
-        a.heads = m->qh;
-        a.kv_heads = m->kh;
-        a.hd = m->hd;
-        a.kvw = kw;
-        a.ctx = m->ctx;
-        a.dsplit = m->dsplit;
-        a.scale = 1.0f / sqrtf((float)m->hd);   // inference.rs:4653
+        attn_params(m, l, a);
         CKL(attention_launch(a, s, true));
         // quantize -> wo -> residual (inference.rs:4667-4673), reduce #1 (tp.rs:356-363)
-        ncm_status st = row_parallel(m, L.wo, m->att, 2 * l, s);
+        const GemvParams n1 = pf_w13(m, l);
+        ncm_status st = row_parallel(m, L.wo, nullptr, m->att_q, m->att_s, 2 * l, &n1, s);
         if (st) return st;
         CKL(launch_w13(m, l, s));
         // quantize -> w2 -> residual (inference.rs:4732-4748), reduce #2 (tp.rs:416-424)
-        st = row_parallel(m, L.w2, m->act, 2 * l + 1, s);
+        const GemvParams n2 = pf_next_after_w2(m, l);
+        st = m->act_quantised ? row_parallel(m, L.w2, nullptr, m->act_q, m->act_s, 2 * l + 1, &n2, s)
+                              : row_parallel(m, L.w2, m->act, nullptr, nullptr, 2 * l + 1, &n2, s);
         if (st) return st;
     }
     if (!with_head) {
@@ -892,10 +1024,12 @@ extern "C" ncm_status ncm_launch_step_kernel(ncm_model* m, int kind, int layer, 
         case NCM_STEP_QKV: CKL(launch_qkv(m, layer, s)); return NCM_OK;
         case NCM_STEP_W13: CKL(launch_w13(m, layer, s)); return NCM_OK;
         case NCM_STEP_WO:
+            if (m->world > 1) return fail(NCM_EUNSUPPORTED, "row-parallel kernels of a shard wait on their peers");
+            return row_parallel(m, m->L[layer].wo, nullptr, m->att_q, m->att_s, 0, nullptr, s);
         case NCM_STEP_W2:
             if (m->world > 1) return fail(NCM_EUNSUPPORTED, "row-parallel kernels of a shard wait on their peers");
-            return row_parallel(m, kind == NCM_STEP_WO ? m->L[layer].wo : m->L[layer].w2,
-                                kind == NCM_STEP_WO ? m->att : m->act, 0, s);
+            return m->act_quantised ? row_parallel(m, m->L[layer].w2, nullptr, m->act_q, m->act_s, 0, nullptr, s)
+                                    : row_parallel(m, m->L[layer].w2, m->act, nullptr, nullptr, 0, nullptr, s);
         default: return fail(NCM_EINVAL, "unknown step kernel");
     }
 }
@@ -1666,7 +1800,7 @@ static float* noalloc_scores_ptr(int device, cudaError_t* err) {
 extern "C" ncm_status ncm_attention_noalloc(float* out, const float* q, const float* k_cache, const float* v_cache,
                                            int pos, int heads, int kv_heads, int head_dim, void* stream) {
     if (!out || !q || !k_cache || !v_cache || pos < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads ||
-        heads / kv_heads > 8 || head_dim % 32 || head_dim > 256)
+        heads / kv_heads > 8 || head_dim % 32 || head_dim > 256 || pos >= 16384)
         return fail(NCM_EINVAL, "bad attention arguments");
     if ((int64_t)heads * (pos + 1) > kNoAllocScores)
         return fail(NCM_EINVAL, "ncm_attention_noalloc: heads * (pos + 1) = " + std::to_string((int64_t)heads * (pos + 1)) +
@@ -1674,6 +1808,12 @@ extern "C" ncm_status ncm_attention_noalloc(float* out, const float* q, const fl
                                     " floats; use ncm_attention");
     int dev = 0;
     CK(cudaGetDevice(&dev));
+    {
+        // glibc-exact exp: the exception table is copied into its own fixed in-library
+        // array on the first call on this device (host work plus a copy, no allocation)
+        ncm_status st = ensure_expf_table(dev);
+        if (st) return st;
+    }
     cudaError_t e;
     float* scores = noalloc_scores_ptr(dev, &e);
     if (!scores) return fail(NCM_ECUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));

@@ -78,9 +78,14 @@ EncodeTiledFn encode_tiled_fn() {
 // within one double ulp of a float midpoint), and the inputs where glibc differs from
 // it -- all of them lie within 2^-7 ulp of a float rounding midpoint -- are patched from
 // an exception hash built on the host from this process's glibc (libm_table.cpp).
-// Only values that close to a midpoint (~0.4% of inputs) probe the table.
+// Only values that close to a midpoint (~0.4% of inputs) probe the table, unless the
+// host found an exception outside that window (another glibc): then every value probes.
+// The table lives in a fixed in-library array (no device allocation), filled once per
+// device; g_expf_tab stays null until then (correctly rounded exp without patches).
+__device__ uint2 g_expf_store[kExpfTabEntries];
 __device__ const uint32_t* g_expf_tab = nullptr;
 __device__ uint32_t g_expf_mask = 0;
+__device__ int g_expf_gate = 1;
 
 __device__ __forceinline__ float expf_cr(float x) {
     const double yd = exp((double)x);
@@ -90,7 +95,7 @@ __device__ __forceinline__ float expf_cr(float x) {
         const double yy = (double)y;
         const double half = (yd >= yy ? ((double)nextafterf(y, INFINITY) - yy) : (yy - (double)nextafterf(y, 0.0f))) * 0.5;
         const double dist = fabs(yd - yy);
-        if (half - dist <= half * 0x1p-6) {
+        if (!g_expf_gate || half - dist <= half * 0x1p-6) {
             const uint32_t key = __float_as_uint(x), mask = g_expf_mask;
             uint32_t h = (key * 2654435761u) & mask;
             for (int probe = 0; probe < 64; ++probe) {
@@ -104,9 +109,17 @@ __device__ __forceinline__ float expf_cr(float x) {
     return y;
 }
 
-int expf_table_install(const uint32_t* dev_tab, uint32_t mask) {
-    cudaError_t e = cudaMemcpyToSymbol(g_expf_tab, &dev_tab, sizeof(dev_tab));
+// Copies the host-built table (pairs {key, value}, power-of-two capacity <=
+// kExpfTabEntries) into the in-library array of the current device and publishes it.
+int expf_table_install(const uint32_t* host_tab, size_t entries, uint32_t mask, int gate) {
+    if (entries > kExpfTabEntries || entries != (size_t)mask + 1) return (int)cudaErrorInvalidValue;
+    cudaError_t e = cudaMemcpyToSymbol(g_expf_store, host_tab, entries * sizeof(uint2));
+    void* dev = nullptr;
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(&dev, g_expf_store);
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_expf_mask, &mask, sizeof(mask));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_expf_gate, &gate, sizeof(gate));
+    const uint32_t* p = (const uint32_t*)dev;
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_expf_tab, &p, sizeof(p));
     return (int)e;
 }
 
@@ -680,6 +693,43 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// L2 prefetch (cp.async.bulk.prefetch.L2) of up to pf_bytes of this CTA's share of the
+// next kernel's weight rows: the rows [b R / grid, (b+1) R / grid) of the next launch's
+// fused row space (both matrices of a dual pair).  Row pitches are multiples of 16 bytes.
+__device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__device__ __forceinline__ void prefetch_l2(const uint8_t* a, int64_t bytes) {
+    for (int64_t o = 0; o < bytes; o += 32768) {
+        const uint32_t n = (uint32_t)min64(32768, bytes - o);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a + o), "r"(n) : "memory");
+    }
+}
+__device__ void prefetch_next_weights(const GemvParams& p) {
+    if (p.pf_nmat == 0 || (int)blockIdx.x >= p.pf_grid) return;
+    const int b = blockIdx.x;
+    int64_t budget = p.pf_bytes;
+    if (p.pf_dual) {
+        const int R = p.pf_rows[0];
+        const int r0 = (int)((long long)b * R / p.pf_grid), r1 = (int)((long long)(b + 1) * R / p.pf_grid);
+        for (int m = 0; m < p.pf_nmat; ++m)
+            prefetch_l2(p.pf_base[m] + (int64_t)r0 * p.pf_pitch[m],
+                        min64((int64_t)(r1 - r0) * p.pf_pitch[m], budget / p.pf_nmat));
+        return;
+    }
+    int R = 0;
+    for (int m = 0; m < p.pf_nmat; ++m) R += p.pf_rows[m];
+    const int r0 = (int)((long long)b * R / p.pf_grid), r1 = (int)((long long)(b + 1) * R / p.pf_grid);
+    int seg0 = 0;
+    for (int m = 0; m < p.pf_nmat && budget > 0; ++m) {
+        const int lo = max(r0, seg0), hi = min(r1, seg0 + p.pf_rows[m]);
+        if (lo < hi) {
+            const int64_t n = min64((int64_t)(hi - lo) * p.pf_pitch[m], budget);
+            prefetch_l2(p.pf_base[m] + (int64_t)(lo - seg0) * p.pf_pitch[m], n);
+            budget -= n;
+        }
+        seg0 += p.pf_rows[m];
+    }
+}
+
 // Warp roles: warps 0-7 compute per-block terms, warps 8-9 fold them row by row (and run
 // the epilogue), warp 10 issues the TMA loads.  Hand-offs use mbarriers only:
 //   full[s]  (TMA -> compute)      empty[s]  (compute -> producer: stage s reusable)
@@ -705,8 +755,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
     const int tid = threadIdx.x, lane = tid & 31;
     const int R = p.total_rows;
     const int nbk = gridDim.x;
-    const int r_begin = (int)(((long long)blockIdx.x * R / nbk)) & ~1;
-    const int r_end = (blockIdx.x + 1 == nbk) ? R : ((int)(((long long)(blockIdx.x + 1) * R / nbk)) & ~1);
+    const int ralign = p.row_align;
+    const int r_begin = (int)(((long long)blockIdx.x * R / nbk)) & ~(ralign - 1);
+    const int r_end = (blockIdx.x + 1 == nbk) ? R : ((int)(((long long)(blockIdx.x + 1) * R / nbk)) & ~(ralign - 1));
     const int box_bytes = p.box_rows * p.chunk_bytes;
     const int box2_off = (box_bytes + 127) & ~127;   // tensor-TMA destinations are 128-byte aligned
     const int ns = p.nstages;
@@ -757,6 +808,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
 
     if (tid == kProducer) {
         while (icur < r_end) issue();
+        // Every load of this CTA is issued: HBM would idle through this kernel's tail, the
+        // kernel boundary and the next kernel's prologue, so stream the start of the next
+        // kernel's weights into L2 now (its first tiles then come from L2).
+        prefetch_next_weights(p);
     } else if (tid < kComputeThreads) {
         // (3a) compute warps: warp w owns ring slot w and computes every ns-th stage in
         // full, so up to ns stages are in compute at once.  A lane keeps one 64-column
@@ -880,11 +935,29 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
             } else if constexpr (EPI == EPI_SILU) {
                 if (f >= p.box_rows && f < p.box_rows + n) xchg[f - p.box_rows] = acc;
                 asm volatile("bar.sync 1, 64;" ::: "memory");
+                float o = 0.0f;
                 if (f < n) {
                     const float g = acc, uu = xchg[f];
                     // inference.rs:3385-3388: sigmoid = 1/(1+exp(-g)); g * sigmoid * u
                     const float sig = 1.0f / (1.0f + expf_cr(-g));
-                    sg.out[lrow0 + f] = g * sig * uu;
+                    o = g * sig * uu;
+                    sg.out[lrow0 + f] = o;
+                }
+                if (p.qout && f < 32) {
+                    // The tile is one 32-row block (box_rows == 32, 32-aligned row ranges):
+                    // fold warp 8 holds it and quantises it for the down projection
+                    // (quantize_f32_to_q8_0, inference.rs:991-1029).
+                    float amax = fabsf(o);
+#pragma unroll
+                    for (int k = 16; k > 0; k >>= 1) amax = fmaxf(amax, __shfl_xor_sync(NCM_FULL, amax, k));
+                    const float scale = amax / 127.0f;
+                    int q = 0;
+                    if (scale > 0.0f) {
+                        const float inv = 1.0f / scale;
+                        q = (int)fminf(fmaxf(roundf(o * inv), -127.0f), 127.0f);
+                    }
+                    p.qout[lrow0 + f] = (int8_t)q;
+                    if (f == 0) p.qout_s[(lrow0) >> 5] = scale;
                 }
                 asm volatile("bar.sync 1, 64;" ::: "memory");
             } else {
@@ -1026,7 +1099,8 @@ int gemv_plan(int qtype, int cols, int rows, bool dual, int in_mode, GemvParams&
     p.chunk_words = p.chunk_bytes / 4;
     p.total_rows = rows;
     int grid = num_sms();
-    int maxg = (rows + 1) / 2;
+    const int ra = p.row_align > 2 ? p.row_align : 2;
+    int maxg = (rows + ra - 1) / ra;
     if (maxg < 1) maxg = 1;
     if (grid > maxg) grid = maxg;
     const int per_cta = (rows + grid - 1) / grid;
@@ -1096,6 +1170,8 @@ static int launch_mode(int in_mode, int epi, const GemvParams& p, int grid, cuda
     if (in_mode == IN_F32 && epi == EPI_TP_RESID) return launch_t<QT, IN_F32, EPI_TP_RESID>(p, grid, s, pdl);
     if (in_mode == IN_F32 && epi == EPI_PLAIN) return launch_t<QT, IN_F32, EPI_PLAIN>(p, grid, s, pdl);
     if (in_mode == IN_Q8 && epi == EPI_PLAIN) return launch_t<QT, IN_Q8, EPI_PLAIN>(p, grid, s, pdl);
+    if (in_mode == IN_Q8 && epi == EPI_RESID) return launch_t<QT, IN_Q8, EPI_RESID>(p, grid, s, pdl);
+    if (in_mode == IN_Q8 && epi == EPI_TP_RESID) return launch_t<QT, IN_Q8, EPI_TP_RESID>(p, grid, s, pdl);
     return (int)cudaErrorInvalidValue;
 }
 
@@ -1263,6 +1339,22 @@ __global__ void __launch_bounds__(256) attn_softmax_v_kernel(const __grid_consta
         }
     }
     if (live) a.out[(size_t)tz * a.tok_stride + (size_t)(kvh * g + h) * hd + d0 + d] = acc;
+    if (a.out_q && warp < g) {
+        // dw == 32: warp h holds one 32-value block of head h; quantise it for the output
+        // projection (quantize_f32_to_q8_0, inference.rs:991-1029)
+        float amax = fabsf(acc);
+#pragma unroll
+        for (int k = 16; k > 0; k >>= 1) amax = fmaxf(amax, __shfl_xor_sync(NCM_FULL, amax, k));
+        const float scale = amax / 127.0f;
+        int q = 0;
+        if (scale > 0.0f) {
+            const float inv = 1.0f / scale;
+            q = (int)fminf(fmaxf(roundf(acc * inv), -127.0f), 127.0f);
+        }
+        const size_t o = (size_t)(kvh * g + h) * hd + d0;
+        a.out_q[o + d] = (int8_t)q;
+        if (d == 0) a.out_s[o >> 5] = scale;
+    }
 }
 
 int attention_launch(const AttnParams& a0, cudaStream_t s, bool pdl) {

@@ -11,6 +11,7 @@
 #include <stdint.h>
 #include <string.h>
 #include <algorithm>
+#include <cmath>
 #include <thread>
 #include <vector>
 
@@ -29,9 +30,25 @@ static void scan_range(uint32_t lo, uint32_t hi, std::vector<uint64_t>* out) {
     }
 }
 
+// True when the correctly rounded exp(x) is close enough to a float rounding midpoint
+// for the device to consult the table: the same test as expf_cr, here with the host's
+// double exp.
+static bool near_midpoint(float x) {
+    const double yd = exp((double)x);
+    const float y = (float)yd;
+    if (y == 0.0f || std::isinf(y)) return true;
+    const double yy = (double)y;
+    const double half = (yd >= yy ? ((double)nextafterf(y, INFINITY) - yy) : (yy - (double)nextafterf(y, 0.0f))) * 0.5;
+    const double dist = fabs(yd - yy);
+    // a margin of 2 over the device window covers the two libraries' double exp differing
+    return half - dist <= half * 0x1p-7;
+}
+
 // Builds the exception hash.  Returns the table (pairs of uint32 {key, value}, EMPTY key
-// 0xffffffff) with power-of-two capacity; *mask = capacity - 1.
-std::vector<uint32_t> build_expf_exceptions(int threads, uint32_t* mask, size_t* count) {
+// 0xffffffff) with power-of-two capacity (at most max_entries); *mask = capacity - 1.
+// Empty when even a half-full table of max_entries cannot hold them.
+std::vector<uint32_t> build_expf_exceptions(int threads, uint32_t max_entries, uint32_t* mask, size_t* count,
+                                            int* gate) {
     // x in (-104, 89): outside, expf is 0 / inf for both.
     const uint32_t pos_hi = f2u(89.0f);              // [+0, 89)
     const uint32_t neg_lo = 0x80000000u, neg_hi = f2u(-104.0f);   // [-0, -104)
@@ -48,9 +65,17 @@ std::vector<uint32_t> build_expf_exceptions(int threads, uint32_t* mask, size_t*
     }
     for (auto& t : th) t.join();
     size_t n = 0;
-    for (auto& p : parts) n += p.size();
+    *gate = 1;
+    for (auto& p : parts) {
+        n += p.size();
+        for (uint64_t e : p)
+            if (!near_midpoint(u2f((uint32_t)(e >> 32)))) *gate = 0;
+    }
+    *count = n;
     size_t cap = 1;
     while (cap < 4 * n + 16) cap <<= 1;
+    if (cap > max_entries) cap = max_entries;
+    if (cap < 2 * n + 16) return {};
     std::vector<uint32_t> tab(2 * cap, 0xffffffffu);
     for (auto& p : parts)
         for (uint64_t e : p) {
@@ -61,7 +86,6 @@ std::vector<uint32_t> build_expf_exceptions(int threads, uint32_t* mask, size_t*
             tab[2 * h + 1] = val;
         }
     *mask = (uint32_t)(cap - 1);
-    *count = n;
     return tab;
 }
 

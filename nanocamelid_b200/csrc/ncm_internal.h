@@ -86,6 +86,16 @@ struct alignas(64) GemvParams {
     TpComm tp;
     int tp_slot;                  // layer*2 + phase
     int* err;
+    int row_align;                // CTA row ranges start at multiples of this (2, or 32 with qout)
+    int8_t* qout;                 // EPI_SILU: the output rows also as Q8_0 blocks (box_rows == 32) ...
+    float* qout_s;                //   ... and their scales: the next projection's quantised input
+    // L2 prefetch of the next kernel's weights once this CTA has issued its own loads:
+    // up to pf_bytes of this CTA's share (rows [b*pf_rows/pf_grid, ...)) of each matrix.
+    const uint8_t* pf_base[kMaxSeg + 1];
+    int64_t pf_pitch[kMaxSeg + 1];
+    int pf_rows[kMaxSeg + 1];
+    int pf_nmat, pf_grid, pf_dual;
+    int64_t pf_bytes;
 };
 
 struct AttnParams {
@@ -101,6 +111,8 @@ struct AttnParams {
     float scale;
     int ntok;                // rows in one launch (grid z): token z at position pos + z, q / out at
     int tok_stride;          //   + z * tok_stride floats, scores at + z * heads * ctx
+    int8_t* out_q;           // when set (one row, head_dim / dsplit == 32): the output also as Q8_0
+    float* out_s;            //   blocks (quantize_f32_to_q8_0), the next projection's input
 };
 
 // Multi-row (speculative verify) GEMV: ntok activation rows share every weight tile;
@@ -175,11 +187,17 @@ int block_sums_launch(const int8_t* xq, int64_t nblocks, int* xsum, cudaStream_t
 int embed_rows_launch(int type, const uint8_t* table, int64_t pitch, int emb, const int* toks, int ntok,
                       float* hidden, cudaStream_t s, bool pdl);
 int num_sms();
-int expf_table_install(const uint32_t* dev_tab, uint32_t mask);
+// The glibc expf exception table: at most kExpfTabEntries {key, value} pairs, kept in a
+// fixed in-library device array.
+constexpr uint32_t kExpfTabEntries = 1u << 20;
+int expf_table_install(const uint32_t* host_tab, size_t entries, uint32_t mask, int gate);
 // libm_table.cpp
 }  // namespace ncm
 #include <vector>
 namespace ncm {
-std::vector<uint32_t> build_expf_exceptions(int threads, uint32_t* mask, size_t* count);
+// *gate = 0 when some exception lies outside the near-midpoint window the device checks
+// first (then the device probes the table for every value).
+std::vector<uint32_t> build_expf_exceptions(int threads, uint32_t max_entries, uint32_t* mask, size_t* count,
+                                            int* gate);
 
 }  // namespace ncm

@@ -92,6 +92,9 @@ def _gguf_value(f, t):
         raise ValueError(f"GGUF value type {t}")
 
 
+DIMS_AT = {}
+
+
 def read_gguf_tensors(path):
     """Minimal GGUF v3 reader (gguf.rs:454-551): {name: (type, dims, data offset)}."""
     with open(path, "rb") as f:
@@ -111,9 +114,11 @@ def read_gguf_tensors(path):
             (nl,) = struct.unpack("<Q", f.read(8))
             name = f.read(nl).decode()
             (nd,) = struct.unpack("<I", f.read(4))
+            dims_at = f.tell()
             dims = struct.unpack("<" + "Q" * nd, f.read(8 * nd))
             t, off = struct.unpack("<IQ", f.read(12))
             infos[name] = (t, dims, off)
+            DIMS_AT[(str(path), name)] = dims_at
         base = (f.tell() + align - 1) // align * align
     return {k: (t, d, base + o) for k, (t, d, o) in infos.items()}
 
@@ -379,3 +384,25 @@ def test_gguf_reader_rejects_truncated_and_corrupt_files(ncm, tmp_path):
                        capture_output=True, text=True, timeout=600, cwd=ROOT)
     assert r.returncode == 0, (r.returncode, r.stderr[-2000:])
     assert "BAD []" in r.stdout, r.stdout[-2000:]
+
+
+@pytest.mark.parametrize("name,dim", [("blk.1.attn_norm.weight", 224), ("output_norm.weight", 128),
+                                      ("blk.0.ffn_norm.weight", 512)])
+def test_model_load_rejects_misshapen_norm_tensors(ncm, tmp_path, name, dim):
+    """A norm tensor whose length is not the embedding width (shorter ones could read past
+    the mapped file) is rejected with NCM_EIO by the host-side tensor check, before any
+    device is touched (device -1 here)."""
+    import ctypes
+    sp = tiny(ncm)
+    path = tmp_path / "m.gguf"
+    ncm.write_synthetic_gguf(path, sp)
+    read_gguf_tensors(path)
+    raw = bytearray(open(path, "rb").read())
+    at = DIMS_AT[(str(path), name)]
+    raw[at:at + 8] = struct.pack("<Q", dim)
+    bad = tmp_path / "bad.gguf"
+    open(bad, "wb").write(bytes(raw))
+    h = ctypes.c_void_p()
+    st = ncm.lib().ncm_model_load(str(bad).encode(), 0, -1, None, 0, 0, ctypes.byref(h))
+    assert st == 5, (st, ncm.lib().ncm_last_error())
+    assert name.encode() in ncm.lib().ncm_last_error()
