@@ -37,6 +37,7 @@ typedef int ncm_status;
 #define NCM_TYPE_Q4_0 2
 #define NCM_TYPE_Q8_0 8
 #define NCM_TYPE_Q4_K 12
+#define NCM_TYPE_Q6_K 14
 
 const char* ncm_last_error(void);
 int ncm_version(void);
@@ -49,7 +50,8 @@ ncm_status ncm_quantize_f32_to_q8_0(const float* x, int n, int8_t* x_i8, float* 
 
 /* inference.rs:1201-1244 matmul_quantized(out, x_i8, x_scales, w, rows, cols, _):
  * out[r] = sum_b d_w[r,b] * s_x[b] * dot_b over the raw GGUF blocks of `w`
- * (row-major, rows x cols, type Q4_0 / Q8_0 / Q4_K, row pitch = raw row bytes).
+ * (row-major, rows x cols, type Q4_0 / Q8_0 / Q4_K / Q6_K, row pitch = raw row bytes);
+ * Q6_K is inference.rs:3045-3087 matmul_q6_k over q8.rs:2092-2150 dot_q8_scaled.
  * `out` is overwritten.  All pointers device. */
 ncm_status ncm_matmul_quantized(int qtype, const void* w, int64_t rows, int cols, const int8_t* x_i8,
                                 const float* x_scales, float* out, void* stream);
@@ -81,6 +83,14 @@ ncm_status ncm_fused_silu_mul(float* out, const float* gate, const float* up, in
 ncm_status ncm_attention(float* out, const float* q, const float* k_cache, const float* v_cache, int pos,
                          int heads, int kv_heads, int head_dim, void* stream);
 
+/* inference.rs:4319-4458 apply_attention_head_q8_0 / _f16: the same attention over an F16
+ * cache (kind 1: u16 [ctx][kv_heads*head_dim], exact decode then the f32 path) or a
+ * Q8_0 cache (kind 2: 34-byte blocks [ctx][kv_heads*head_dim/32]; q quantised like the
+ * store, scores from integer block dots scaled (s_q * s_k), V decoded as q * s).  Kind 0
+ * is ncm_attention.  Device pointers. */
+ncm_status ncm_attention_kv(int kind, float* out, const float* q, const void* k_cache, const void* v_cache, int pos,
+                            int heads, int kv_heads, int head_dim, void* stream);
+
 /* No counterpart in the reference.  The same computation as ncm_attention, for callers
  * that must not allocate device memory on the call path: code running inside a CUDA
  * graph capture or a latency-critical loop where cudaMalloc would stall, and hosts that
@@ -107,6 +117,7 @@ typedef struct {
     int32_t tied;                       /* 1: no output.weight (head = Q4_0 requant of token_embd) */
     int32_t t_embd, t_attn, t_ffn, t_out; /* GGUF type ids */
     uint64_t seed;
+    int32_t t_down;                     /* ffn_down type id (0: t_ffn) */
 } ncm_synth_spec;
 
 /* Writes a GGUF v3 file with llama metadata (keys read at model.rs:55-153) and the
@@ -148,6 +159,12 @@ ncm_status ncm_model_info(const ncm_model* m, int* out);
 
 /* Clears the KV cache and the decode position (new session, cluster_tp_node.rs:987-996). */
 ncm_status ncm_model_reset(ncm_model* m);
+
+/* inference.rs:505-531 LlamaKvCache::new storage selection (NANOCAMELID_KV_CACHE_F16 /
+ * NANOCAMELID_KV_CACHE_Q8): kind 0 f32, 1 F16 (truncating f32 -> f16 per value on store),
+ * 2 Q8_0 (quantize_row_to_q8_0_blocks on store, inference.rs:4298-4317).  Clears the
+ * cache and the position; call before prefill. */
+ncm_status ncm_model_set_kv_cache(ncm_model* m, int kind);
 
 /* inference.rs:3649-3670 forward_pass + 4834-4845 sample_logits(_, 0.0) for ONE token
  * at `pos`, host buffers: copies the token in, runs the step, copies the greedy

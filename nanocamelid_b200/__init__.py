@@ -17,7 +17,7 @@ from dataclasses import dataclass, field
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libncm.so")
 
-Q4_0, Q8_0, Q4_K, F32, F16 = 2, 8, 12, 0, 1
+Q4_0, Q8_0, Q4_K, Q6_K, F32, F16 = 2, 8, 12, 14, 0, 1
 REDUCE_FUSED_P2P, REDUCE_NCCL, REDUCE_HOST_CALLBACK = 0, 1, 2
 STEP_QKV, STEP_W13, STEP_WO, STEP_W2 = 0, 1, 2, 3
 PHASE_ATTENTION, PHASE_FFN, PHASE_HEAD = 0, 1, 2   # tp.rs:203-206 ReducePhase, + the head merge
@@ -41,7 +41,7 @@ class SynthSpec(ctypes.Structure):
                 ("vocab", ctypes.c_int32), ("ctx", ctypes.c_int32), ("rope_base", ctypes.c_float),
                 ("eps", ctypes.c_float), ("tied", ctypes.c_int32), ("t_embd", ctypes.c_int32),
                 ("t_attn", ctypes.c_int32), ("t_ffn", ctypes.c_int32), ("t_out", ctypes.c_int32),
-                ("seed", ctypes.c_uint64)]
+                ("seed", ctypes.c_uint64), ("t_down", ctypes.c_int32)]
 
     def replace(self, **kw):
         s = SynthSpec()
@@ -55,9 +55,9 @@ class SynthSpec(ctypes.Structure):
 
 
 def spec(emb, layers, heads, kv_heads, head_dim, ffn, vocab=128256, ctx=2048, tied=True, t_embd=Q4_0,
-         t_attn=Q4_0, t_ffn=Q4_0, t_out=Q4_0, seed=0, rope_base=500000.0, eps=1e-5):
+         t_attn=Q4_0, t_ffn=Q4_0, t_out=Q4_0, seed=0, rope_base=500000.0, eps=1e-5, t_down=0):
     return SynthSpec(emb, layers, heads, kv_heads, head_dim, ffn, vocab, ctx, rope_base, eps, int(tied), t_embd,
-                     t_attn, t_ffn, t_out, seed)
+                     t_attn, t_ffn, t_out, seed, t_down)
 
 
 # BASELINE.json configs (shapes; random-init N(0, 0.02) weights, seeded).
@@ -98,6 +98,8 @@ def lib():
         "ncm_rms_norm": (c_int, [c_p, c_p, c_p, c_int, c_f, c_p]),
         "ncm_fused_silu_mul": (c_int, [c_p, c_p, c_p, c_int, c_p]),
         "ncm_attention": (c_int, [c_p, c_p, c_p, c_p, c_int, c_int, c_int, c_int, c_p]),
+        "ncm_attention_kv": (c_int, [c_int, c_p, c_p, c_p, c_p, c_int, c_int, c_int, c_int, c_p]),
+        "ncm_model_set_kv_cache": (c_int, [c_p, c_int]),
         "ncm_gguf_write_synthetic": (c_int, [ctypes.c_char_p, ctypes.POINTER(SynthSpec), c_int]),
         "ncm_synth_tensor_host": (c_int, [ctypes.POINTER(SynthSpec), ctypes.c_char_p, c_int, c_i64, c_i64, c_i64,
                                           c_i64, c_i64, c_p]),
@@ -185,6 +187,15 @@ def attention(out_ptr, q_ptr, k_cache_ptr, v_cache_ptr, pos, heads, kv_heads, he
                             _stream(stream)))
 
 
+KV_F32, KV_F16, KV_Q8_0 = 0, 1, 2   # inference.rs:505-531 cache storage kinds
+
+
+def attention_kv(kind, out_ptr, q_ptr, k_cache_ptr, v_cache_ptr, pos, heads, kv_heads, head_dim, stream=0):
+    """inference.rs:4319-4458: attention over an F16 (KV_F16) or Q8_0 (KV_Q8_0) cache."""
+    _ck(lib().ncm_attention_kv(kind, out_ptr, q_ptr, k_cache_ptr, v_cache_ptr, pos, heads, kv_heads, head_dim,
+                               _stream(stream)))
+
+
 # ---------------------------------------------------------------- host helpers
 def write_synthetic_gguf(path, spec_, threads=None):
     threads = threads or os.cpu_count() or 4
@@ -192,8 +203,8 @@ def write_synthetic_gguf(path, spec_, threads=None):
 
 
 def synth_tensor_bytes(spec_, name, qtype, r0, r1, c0, c1, cols):
-    be = 256 if qtype == Q4_K else 32
-    bb = {Q4_0: 18, Q8_0: 34, Q4_K: 144}[qtype]
+    be = 256 if qtype in (Q4_K, Q6_K) else 32
+    bb = {Q4_0: 18, Q8_0: 34, Q4_K: 144, Q6_K: 210}[qtype]
     buf = (ctypes.c_uint8 * ((r1 - r0) * ((c1 - c0) // be) * bb))()
     _ck(lib().ncm_synth_tensor_host(ctypes.byref(spec_), name.encode(), qtype, r0, r1, c0, c1, cols, buf))
     return bytes(buf)
@@ -264,6 +275,10 @@ class Model:
 
     def reset(self):
         _ck(lib().ncm_model_reset(self._h))
+
+    def set_kv_cache(self, kind):
+        """KV_F32 / KV_F16 / KV_Q8_0 cache storage (NANOCAMELID_KV_CACHE_F16 / _Q8); clears it."""
+        _ck(lib().ncm_model_set_kv_cache(self._h, kind))
 
     def forward_pass(self, token, pos, want_logits=False):
         """inference.rs:3649 forward_pass + sample_logits(_, 0.0): returns (argmax, logits|None)."""

@@ -103,6 +103,11 @@ struct ncm_model {
     int8_t *att_q = nullptr, *act_q = nullptr;
     float *att_s = nullptr, *act_s = nullptr;
     bool act_quantised = false;   // the gate/up plan allows the quantised hand-off (32-row tiles)
+    bool has_q6k = false;         // a Q6_K head or down projection (one GPU, token-by-token prefill)
+    int kv_kind = KV_F32;         // KV-cache storage (F32, or the reference's opt-in F16 / Q8_0)
+    float *kv_sk = nullptr, *kv_sv = nullptr;   // F16 / Q8_0: staged f32 K / V rows [kMaxBatch][kw]
+    int8_t* hx_q = nullptr;       // the normed hidden as Q8_0 for a Q6_K head
+    float* hx_s = nullptr;
     int64_t prefetch_bytes = 320 * 1024;   // per CTA: next kernel's weights streamed into L2
     int *state = nullptr, *tokens = nullptr, *err = nullptr;
     int* h_stage = nullptr;   // pinned staging for small transfers
@@ -230,6 +235,15 @@ static ncm_status ensure_expf_table(int device) {
     return NCM_OK;
 }
 
+// Bytes of one position's K (or V) row in the cache's storage, and a layer's cache base.
+static size_t kv_row_bytes(const ncm_model* m) {
+    const size_t kw = (size_t)m->kh * m->hd;
+    return m->kv_kind == KV_F16 ? 2 * kw : m->kv_kind == KV_Q8_0 ? kw / 32 * 34 : 4 * kw;
+}
+static uint8_t* kv_layer(const ncm_model* m, float* cache, int l) {
+    return reinterpret_cast<uint8_t*>(cache) + (size_t)l * m->ctx * kv_row_bytes(m);
+}
+
 static ncm_status setup_buffers(ncm_model* m, const int* shares, int nshards, int shard) {
     {
         ncm_status s = ensure_expf_table(m->device);
@@ -264,12 +278,16 @@ static ncm_status setup_buffers(ncm_model* m, const int* shares, int nshards, in
     DALLOC(m->att_s, 4 * (qw / 32));
     DALLOC(m->act_q, m->fl);
     DALLOC(m->act_s, 4 * (m->fl / 32));
+    DALLOC(m->hx_q, m->emb);
+    DALLOC(m->hx_s, 4 * (m->emb / 32));
     DALLOC(m->kc, 4 * (size_t)m->layers * m->ctx * kw);
     DALLOC(m->vc, 4 * (size_t)m->layers * m->ctx * kw);
+    DALLOC(m->kv_sk, 4 * (size_t)kMaxBatch * kw);
+    DALLOC(m->kv_sv, 4 * (size_t)kMaxBatch * kw);
     m->dsplit = 1;
     while (m->dsplit * 2 * m->kh <= num_sms() && m->hd / (m->dsplit * 2) >= 4) m->dsplit *= 2;
     DALLOC(m->scores, 4 * (size_t)m->qh * m->ctx);
-    DALLOC(m->amax_part, 8 * num_sms());
+    DALLOC(m->amax_part, 8 * (size_t)std::max(num_sms(), (m->hr + 31) / 32));   // one per CTA of any head GEMV
     DALLOC(m->amax_cnt, 4);
     DALLOC(m->head_out, 8);
     DALLOC(m->gather, 8 * kMaxWorld);
@@ -414,16 +432,28 @@ static ncm_status build_tied_head(ncm_model* m) {
 
 static GemvParams base_params(ncm_model* m);
 
+// Q6_K (the output.weight / ffn_down type of Q4_K_M files) runs on the row-per-thread
+// GEMV, on one GPU, for the head and the down projections only.
+static ncm_status check_q6k(ncm_model* m, const DevMat& d, const char* what) {
+    if (d.cols % 256 || d.cols > 32768) return fail(NCM_EUNSUPPORTED, std::string(what) + ": Q6_K columns not 256-aligned");
+    if (m->world > 1) return fail(NCM_EUNSUPPORTED, std::string(what) + ": Q6_K tensors run on one GPU");
+    m->has_q6k = true;
+    return NCM_OK;
+}
+
 static ncm_status check_all_shapes(ncm_model* m) {
     ncm_status s;
     DALLOC(m->embd_ssq, 4 * (size_t)m->vocab);
     CKL(embed_ssq_launch(m->embd.type, m->embd.d, m->embd.pitch, m->emb, m->vocab, m->embd_ssq, m->stream));
     CK(cudaStreamSynchronize(m->stream));
-    if ((s = check_matrix_shape(m->head, "output"))) return s;
+    if (m->head.type == NCM_T_Q6_K) { if ((s = check_q6k(m, m->head, "output"))) return s; }
+    else if ((s = check_matrix_shape(m->head, "output"))) return s;
     for (auto& l : m->L) {
-        const DevMat* ms[] = {&l.wq, &l.wk, &l.wv, &l.wo, &l.w1, &l.w3, &l.w2};
+        const DevMat* ms[] = {&l.wq, &l.wk, &l.wv, &l.wo, &l.w1, &l.w3};
         for (auto d : ms)
             if ((s = check_matrix_shape(*d, "layer"))) return s;
+        if (l.w2.type == NCM_T_Q6_K) { if ((s = check_q6k(m, l.w2, "ffn_down"))) return s; }
+        else if ((s = check_matrix_shape(l.w2, "layer"))) return s;
         if (l.wq.type != l.wk.type || l.wq.type != l.wv.type || l.w1.type != l.w3.type)
             return fail(NCM_EUNSUPPORTED, "q/k/v (and gate/up) must share one quant type");
     }
@@ -545,7 +575,7 @@ extern "C" ncm_status ncm_model_create_synthetic(const ncm_synth_spec* spec, int
         TRY(synth_mat(m, sp, NM("attn_output"), sp.t_attn, QW, 0, H, m->q0 * hd, m->qh * hd, l.wo));
         TRY(synth_mat(m, sp, NM("ffn_gate"), sp.t_ffn, H, m->f0, m->fl, 0, H, l.w1));
         TRY(synth_mat(m, sp, NM("ffn_up"), sp.t_ffn, H, m->f0, m->fl, 0, H, l.w3));
-        TRY(synth_mat(m, sp, NM("ffn_down"), sp.t_ffn, F, 0, H, m->f0, m->fl, l.w2));
+        TRY(synth_mat(m, sp, NM("ffn_down"), sp.t_down ? sp.t_down : sp.t_ffn, F, 0, H, m->f0, m->fl, l.w2));
 #undef NM
     }
     if (cudaStreamSynchronize(m->stream) != cudaSuccess) { free_model(m); return fail(NCM_ECUDA, "synthetic init"); }
@@ -567,7 +597,7 @@ extern "C" ncm_status ncm_model_info(const ncm_model* m, int* out) {
 extern "C" ncm_status ncm_model_reset(ncm_model* m) {
     if (!m) return fail(NCM_EINVAL, "null model");
     CK(cudaSetDevice(m->device));
-    const size_t kvn = 4 * (size_t)m->layers * m->ctx * m->kh * m->hd;
+    const size_t kvn = kv_row_bytes(m) * m->layers * m->ctx;
     CK(cudaMemsetAsync(m->kc, 0, kvn, m->stream));
     CK(cudaMemsetAsync(m->vc, 0, kvn, m->stream));
     // Position and prompt length only: the step counter stays monotonic because the
@@ -576,6 +606,22 @@ extern "C" ncm_status ncm_model_reset(ncm_model* m) {
     CK(cudaMemsetAsync(m->state + ST_NPROMPT, 0, 4, m->stream));
     CK(cudaStreamSynchronize(m->stream));
     return NCM_OK;
+}
+
+// inference.rs:512-531 LlamaKvCache::new: the cache storage the reference selects with
+// NANOCAMELID_KV_CACHE_Q8 (Q8_0 blocks, when kv_width is a multiple of 32) or
+// NANOCAMELID_KV_CACHE_F16; f32 otherwise.  The cache is cleared and the position reset.
+extern "C" ncm_status ncm_model_set_kv_cache(ncm_model* m, int kind) {
+    if (!m || kind < KV_F32 || kind > KV_Q8_0) return fail(NCM_EINVAL, "bad KV-cache kind");
+    CK(cudaSetDevice(m->device));
+    CK(cudaStreamSynchronize(m->stream));
+    if (kind == KV_Q8_0 && (m->kh * m->hd) % 32) kind = KV_F32;
+    m->kv_kind = kind;   // every kind fits the f32 allocation
+    m->dirty = true;
+    for (auto& row : m->b_graph)
+        for (auto& gx : row)
+            if (gx) { cudaGraphExecDestroy(gx); gx = nullptr; }
+    return ncm_model_reset(m);
 }
 
 // ------------------------------------------------------------------ the decode step
@@ -660,6 +706,20 @@ static ncm_status host_reduce(ncm_model* m, void* dev, int n, int layer, int pha
 // wrote them (bit-identical to quantising x here).  `next` is prefetched into L2.
 static ncm_status row_parallel(ncm_model* m, const DevMat& w, const float* x, const int8_t* xq, const float* xs,
                                int slot, const GemvParams* next, cudaStream_t s) {
+    if (w.type == NCM_T_Q6_K) {
+        // one GPU (checked at load): quantise here unless the producer did, then hidden +=
+        if (!xq) {
+            CKL(batch_prep_launch(x, w.cols, w.cols, 1, nullptr, m->eps, nullptr, nullptr, m->act_q, m->act_s, nullptr,
+                                  s, true));
+            xq = m->act_q;
+            xs = m->act_s;
+        }
+        Q6Params q;
+        memset(&q, 0, sizeof q);
+        q.w = w.d; q.pitch = w.pitch; q.rows = w.rows; q.cols = w.cols; q.xq = xq; q.xs = xs; q.out = m->hidden;
+        CKL(q6k_gemv_launch(EPI_RESID, q, s, true));
+        return NCM_OK;
+    }
     GemvParams p = base_params(m);
     p.nseg = 1;
     p.total_rows = m->emb;
@@ -734,9 +794,19 @@ static int launch_qkv(ncm_model* m, int l, cudaStream_t s) {
     p.kcache = m->kc + (size_t)l * m->ctx * kw;
     p.vcache = m->vc + (size_t)l * m->ctx * kw;
     p.kv_width = kw;
+    if (m->kv_kind != KV_F32) {
+        // F16 / Q8_0 cache: the epilogue stages the f32 row, a store launch converts it
+        p.kcache = m->kv_sk;
+        p.vcache = m->kv_sv;
+        p.kv_stage = 1;
+    }
     if (l == 0) p.ssq_tok = m->embd_ssq;
     copy_pf(p, pf_of(m, {&L.wo}, false));
-    return launch_gemv({&L.wq, &L.wk, &L.wv}, nullptr, IN_F32_RMS, EPI_QKV, p, s);
+    int r = launch_gemv({&L.wq, &L.wk, &L.wv}, nullptr, IN_F32_RMS, EPI_QKV, p, s);
+    if (!r && m->kv_kind != KV_F32)
+        r = kv_store_launch(m->kv_kind, m->kv_sk, m->kv_sv, 1, kw, kv_layer(m, m->kc, l), kv_layer(m, m->vc, l),
+                            m->state + ST_POS, s, true);
+    return r;
 }
 
 // rms_norm -> quantize -> w1, w3 -> silu*mul (inference.rs:4679-4730) of layer l; the
@@ -764,6 +834,9 @@ static void attn_params(ncm_model* m, int l, AttnParams& a) {
     a.q = m->q;
     a.kc = m->kc + (size_t)l * m->ctx * kw;
     a.vc = m->vc + (size_t)l * m->ctx * kw;
+    a.kv_kind = m->kv_kind;
+    a.kc_raw = kv_layer(m, m->kc, l);
+    a.vc_raw = kv_layer(m, m->vc, l);
     a.out = m->att;
     a.scores = m->scores;
     a.state = m->state;
@@ -816,6 +889,18 @@ static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
     h.head_row0 = m->h0;
     if (m->world > 1 && m->reduce_mode == NCM_REDUCE_FUSED_P2P) h.tp = m->comm;
     if (m->world > 1 && m->reduce_mode != NCM_REDUCE_FUSED_P2P) h.head_out = m->head_out;
+    if (m->head.type == NCM_T_Q6_K) {
+        // output norm -> quantize (one prep launch), then the Q6_K GEMV with the argmax
+        CKL(batch_prep_launch(m->hidden, m->emb, m->emb, 1, m->out_norm, m->eps, nullptr, nullptr, m->hx_q, m->hx_s,
+                              nullptr, s, true));
+        Q6Params q;
+        memset(&q, 0, sizeof q);
+        q.w = m->head.d; q.pitch = m->head.pitch; q.rows = m->hr; q.cols = m->emb; q.xq = m->hx_q; q.xs = m->hx_s;
+        q.out = m->logits; q.amax_part = m->amax_part; q.counter = m->amax_cnt; q.head_row0 = m->h0;
+        q.state = m->state; q.tokens = m->tokens; q.ctx = m->ctx;
+        CKL(q6k_gemv_launch(EPI_ARGMAX, q, s, true));
+        return NCM_OK;
+    }
     CKL(launch_gemv({&m->head}, nullptr, IN_F32_RMS, EPI_ARGMAX, h, s));
     if (h.head_out && host_mode(m)) {
         // this shard's (logit, token); the host merges every shard's pair (strict '>' in
@@ -897,7 +982,7 @@ extern "C" ncm_status ncm_prefill_tokens(ncm_model* m, const int* prompt, int n_
     cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
     if (stream) m->ext_stream = st;
     CK(cudaStreamSynchronize(st));
-    if (n_prompt > 1 && (m->world == 1 || host_mode(m))) {
+    if (n_prompt > 1 && !m->has_q6k && (m->world == 1 || host_mode(m))) {
         // Eight prompt tokens per multi-row pass: every row's K/V and greedy token equal
         // the token-by-token prefill's bit for bit, so the state below is the one that
         // prefill leaves (tokens, position, prompt length, last token).
@@ -994,8 +1079,12 @@ extern "C" ncm_status ncm_debug_read(ncm_model* m, int which, int layer, float* 
         case 1: src = m->q; cap = (size_t)m->qh * m->hd; break;
         case 2: src = m->att; cap = (size_t)m->qh * m->hd; break;
         case 3: src = m->act; cap = m->fl; break;
-        case 4: src = m->kc + (size_t)layer * m->ctx * kw; cap = (size_t)m->ctx * kw; break;
-        case 5: src = m->vc + (size_t)layer * m->ctx * kw; cap = (size_t)m->ctx * kw; break;
+        case 4:
+            if (m->kv_kind != KV_F32) return fail(NCM_EINVAL, "the K / V caches are not f32");
+            src = m->kc + (size_t)layer * m->ctx * kw; cap = (size_t)m->ctx * kw; break;
+        case 5:
+            if (m->kv_kind != KV_F32) return fail(NCM_EINVAL, "the K / V caches are not f32");
+            src = m->vc + (size_t)layer * m->ctx * kw; cap = (size_t)m->ctx * kw; break;
         case 6: src = m->logits; cap = m->hr; break;
         default: return fail(NCM_EINVAL, "unknown buffer");
     }
@@ -1133,12 +1222,23 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s, bool wi
         p.kcache = m->kc + (size_t)l * m->ctx * kw;
         p.vcache = m->vc + (size_t)l * m->ctx * kw;
         p.kv_width = kw;
+        if (m->kv_kind != KV_F32) {
+            p.kcache = m->kv_sk;
+            p.vcache = m->kv_sv;
+            p.kv_stage = 1;
+        }
         CKL(launch_batch({&L.wq, &L.wk, &L.wv}, nullptr, EPI_QKV, p, s));
+        if (m->kv_kind != KV_F32)
+            CKL(kv_store_launch(m->kv_kind, m->kv_sk, m->kv_sv, ntok, kw, kv_layer(m, m->kc, l), kv_layer(m, m->vc, l),
+                                m->b_pos, s, true));
         AttnParams a;
         memset(&a, 0, sizeof a);
         a.q = m->b_q;
-        a.kc = p.kcache;
-        a.vc = p.vcache;
+        a.kc = m->kc + (size_t)l * m->ctx * kw;
+        a.vc = m->vc + (size_t)l * m->ctx * kw;
+        a.kv_kind = m->kv_kind;
+        a.kc_raw = kv_layer(m, m->kc, l);
+        a.vc_raw = kv_layer(m, m->vc, l);
         a.out = m->b_att;
         a.scores = m->b_scores;
         a.state = m->b_pos;   // b_pos[0] plays ST_POS (= 0): token z at *b_pos + z
@@ -1269,6 +1369,7 @@ extern "C" ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok
         return fail(NCM_EINVAL, "bad verify batch");
     if (m->world > 1 && !host_mode(m))
         return fail(NCM_EUNSUPPORTED, "multi-row verify under tensor parallelism runs with the host-callback reducer");
+    if (m->has_q6k) return fail(NCM_EUNSUPPORTED, "the multi-row pass has no Q6_K kernel");
     for (int i = 0; i < ntok; ++i)
         if (tokens[i] < 0 || tokens[i] >= m->vocab) return fail(NCM_EINVAL, "token id out of range");
     return run_rows(m, tokens, ntok, pos0, true, argmax_out);
@@ -1654,7 +1755,25 @@ static ncm_status seam_gemv(int qtype, const void* w, int64_t rows, int cols, co
 
 extern "C" ncm_status ncm_matmul_quantized(int qtype, const void* w, int64_t rows, int cols, const int8_t* x_i8,
                                           const float* x_scales, float* out, void* stream) {
-    if (!gemv_type_ok(qtype)) return fail(NCM_EUNSUPPORTED, "quant type outside Q4_0/Q8_0/Q4_K");
+    if (qtype == NCM_T_Q6_K) {
+        // inference.rs:3045-3087 matmul_q6_k
+        if (rows < 0 || rows >= (1ll << 31) || cols <= 0 || cols % 256 || cols > 32768)
+            return fail(NCM_EINVAL, "Q6_K: cols must be a positive multiple of 256, at most 32768");
+        if (rows == 0) return NCM_OK;
+        if (!w || !x_i8 || !x_scales || !out) return fail(NCM_EINVAL, "null pointer");
+        cudaStream_t s = (cudaStream_t)stream;
+        AsyncScratch tmp;
+        const uint8_t* base = nullptr;
+        int64_t pitch = 0;
+        ncm_status st = addressable_rows(w, rows, row_bytes(qtype, cols), 16, s, tmp, &base, &pitch);
+        if (st) return st;
+        Q6Params q;
+        memset(&q, 0, sizeof q);
+        q.w = base; q.pitch = pitch; q.rows = (int)rows; q.cols = cols; q.xq = x_i8; q.xs = x_scales; q.out = out;
+        CKL(q6k_gemv_launch(EPI_PLAIN, q, s, false));
+        return NCM_OK;
+    }
+    if (!gemv_type_ok(qtype)) return fail(NCM_EUNSUPPORTED, "quant type outside Q4_0/Q8_0/Q4_K/Q6_K");
     if (rows < 0 || rows >= (1ll << 31) || cols <= 0 || cols % 32 || cols % ncm_type_block_elems(qtype) ||
         cols > 32768)
         return fail(NCM_EINVAL, "cols must be a positive multiple of 32 (256 for Q4_K), at most 32768");
@@ -1764,6 +1883,40 @@ extern "C" ncm_status ncm_attention(float* out, const float* q, const float* k_c
     a.q = q; a.kc = k_cache; a.vc = v_cache; a.out = out; a.scores = scores; a.state = nullptr;
     a.pos_override = pos;
     a.heads = heads; a.kv_heads = kv_heads; a.hd = head_dim; a.kvw = kv_heads * head_dim; a.ctx = ctx;
+    a.dsplit = 4;
+    a.scale = 1.0f / sqrtf((float)head_dim);
+    int r = attention_launch(a, s, false);
+    cudaFreeAsync(scores, s);
+    CK(cudaStreamSynchronize(s));
+    if (r) return fail(NCM_ECUDA, "attention launch failed");
+    return NCM_OK;
+}
+
+// inference.rs:4142-4458 apply_attention_heads over an F16 (kind 1) or Q8_0 (kind 2) cache
+// ([ctx][kv_heads*head_dim] u16, or [ctx][kv_heads*head_dim/32] 34-byte blocks); kind 0
+// is ncm_attention.
+extern "C" ncm_status ncm_attention_kv(int kind, float* out, const float* q, const void* k_cache, const void* v_cache,
+                                      int pos, int heads, int kv_heads, int head_dim, void* stream) {
+    if (kind == KV_F32)
+        return ncm_attention(out, q, (const float*)k_cache, (const float*)v_cache, pos, heads, kv_heads, head_dim, stream);
+    if (kind != KV_F16 && kind != KV_Q8_0) return fail(NCM_EINVAL, "bad KV-cache kind");
+    if (!out || !q || !k_cache || !v_cache || pos < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads ||
+        heads / kv_heads > 8 || head_dim % 32 || head_dim > 256 || pos >= 16384)
+        return fail(NCM_EINVAL, "bad attention arguments");
+    cudaStream_t s = (cudaStream_t)stream;
+    {
+        int dev = 0;
+        CK(cudaGetDevice(&dev));
+        ncm_status st = ensure_expf_table(dev);
+        if (st) return st;
+    }
+    float* scores = nullptr;
+    CK(cudaMallocAsync((void**)&scores, 4 * (size_t)heads * (pos + 1), s));
+    AttnParams a;
+    memset(&a, 0, sizeof a);
+    a.q = q; a.out = out; a.scores = scores; a.pos_override = pos;
+    a.kv_kind = kind; a.kc_raw = k_cache; a.vc_raw = v_cache;
+    a.heads = heads; a.kv_heads = kv_heads; a.hd = head_dim; a.kvw = kv_heads * head_dim; a.ctx = pos + 1;
     a.dsplit = 4;
     a.scale = 1.0f / sqrtf((float)head_dim);
     int r = attention_launch(a, s, false);

@@ -195,7 +195,7 @@ std::vector<SynthTensor> synth_tensor_list(const ncm_synth_spec& s) {
         v.push_back({b + "ffn_norm.weight", NCM_T_F32, 1, H, true});
         v.push_back({b + "ffn_gate.weight", s.t_ffn, F, H, false});
         v.push_back({b + "ffn_up.weight", s.t_ffn, F, H, false});
-        v.push_back({b + "ffn_down.weight", s.t_ffn, H, F, false});
+        v.push_back({b + "ffn_down.weight", s.t_down ? s.t_down : s.t_ffn, H, F, false});
     }
     return v;
 }

@@ -508,6 +508,61 @@ __device__ __forceinline__ void terms_q4_k(const uint8_t* row, int u, const XUni
     t1 = x.s[1] * (sch * (float)wh - mnh * (float)x.sum[1]);
 }
 
+// Four rows' terms of unit u, every shared-memory load issued before the first dot so
+// that the rows' latency chains overlap (same arithmetic per row as the one-row forms).
+template <int QT, int N>
+__device__ __forceinline__ void unit_terms_n(const uint8_t* const (&rows)[N], int u, const XUnit& x, float (&t0)[N],
+                                             float (&t1)[N]) {
+    if constexpr (QT == NCM_T_Q4_0) {
+        uint32_t w[N][9];
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const uint32_t* p = reinterpret_cast<const uint32_t*>(rows[i] + 36 * u);
+#pragma unroll
+            for (int j = 0; j < 9; ++j) w[i][j] = p[j];
+        }
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            int a = 0, b = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t q = __funnelshift_r(w[i][k], w[i][k + 1], 16);
+                a = __dp4a((int)(q & 0x0f0f0f0fu), (int)x.w[k], a);
+                a = __dp4a((int)((q >> 4) & 0x0f0f0f0fu), (int)x.w[4 + k], a);
+                const uint32_t r = w[i][5 + k];
+                b = __dp4a((int)(r & 0x0f0f0f0fu), (int)x.w[8 + k], b);
+                b = __dp4a((int)((r >> 4) & 0x0f0f0f0fu), (int)x.w[12 + k], b);
+            }
+            a -= 8 * x.sum[0];
+            b -= 8 * x.sum[1];
+            t0[i] = f16_bits_to_f32(w[i][0] & 0xffff) * x.s[0] * (float)a;
+            t1[i] = f16_bits_to_f32(w[i][4] >> 16) * x.s[1] * (float)b;
+        }
+    } else if constexpr (QT == NCM_T_Q8_0) {
+        uint32_t w[N][17];
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const uint32_t* p = reinterpret_cast<const uint32_t*>(rows[i] + 68 * u);
+#pragma unroll
+            for (int j = 0; j < 17; ++j) w[i][j] = p[j];
+        }
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            int a = 0, b = 0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                a = __dp4a((int)__funnelshift_r(w[i][k], w[i][k + 1], 16), (int)x.w[k], a);
+                b = __dp4a((int)w[i][9 + k], (int)x.w[8 + k], b);
+            }
+            t0[i] = f16_bits_to_f32(w[i][0] & 0xffff) * x.s[0] * (float)a;
+            t1[i] = f16_bits_to_f32(w[i][8] >> 16) * x.s[1] * (float)b;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < N; ++i) terms_q4_k(rows[i], u, x, t0[i], t1[i], nullptr);
+    }
+}
+
 template <int QT>
 __device__ __forceinline__ void unit_terms(const uint8_t* row, int u, const XUnit& x, float& t0, float& t1) {
     if constexpr (QT == NCM_T_Q4_0) terms_q4_0(row, u, x, t0, t1, nullptr);
@@ -732,17 +787,18 @@ __device__ void prefetch_next_weights(const GemvParams& p) {
 
 // Warp roles: warps 0-7 compute per-block terms, warps 8-9 fold them row by row (and run
 // the epilogue), warp 10 issues the TMA loads.  Hand-offs use mbarriers only:
-//   full[s]  (TMA -> compute)      empty[s]  (compute -> producer: stage s reusable)
-// and the term slots are handed over with shared-memory flags (release / acquire):
-//   tflag[k]    (compute -> fold: uses of slot k whose terms are written)
-//   eflag[w][k] (fold warp w -> compute: uses of slot k folded)
+//   full[s]   (TMA -> compute)            empty[s]  (compute -> producer: stage s reusable)
+//   tfull[s]  (compute -> fold: terms of stage s written)
+//   tempty[s] (fold -> compute: term slot s folded)
+// All eight compute warps work on every stage (each takes a quarter of its row groups
+// for each of the eight 64-column units), so a stage is turned around in a few hundred
+// cycles and the ring keeps its stages in flight on the TMA side.
 
 template <int QT, int IN, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr bool DUAL = (EPI == EPI_SILU);
     __shared__ GemvSeqScratch sc;
-    __shared__ uint32_t tflag[kMaxStages], eflag[2][kMaxStages];
     __shared__ int s_last;
     __shared__ float xchg[kMaxFold];
     __shared__ float wv[2];
@@ -750,6 +806,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
 
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + 8;
+    uint64_t* tfull = full + 16;
+    uint64_t* tempty = full + 24;
     float* tbuf = reinterpret_cast<float*>(smem + p.t_off);
     uint8_t* stages = smem + p.stage_off;
     const int tid = threadIdx.x, lane = tid & 31;
@@ -766,10 +824,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
     if (tid == 0) {
         for (int s = 0; s < ns; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
-            tflag[s] = 0;
-            eflag[0][s] = 0;
-            eflag[1][s] = 0;
+            mbar_init(&empty[s], kComputeThreads / 32);
+            mbar_init(&tfull[s], kComputeThreads / 32);
+            mbar_init(&tempty[s], 2);
         }
         fence_mbar_init();
     }
@@ -813,50 +870,51 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
         // kernel's weights into L2 now (its first tiles then come from L2).
         prefetch_next_weights(p);
     } else if (tid < kComputeThreads) {
-        // (3a) compute warps: warp w owns ring slot w and computes every ns-th stage in
-        // full, so up to ns stages are in compute at once.  A lane keeps one 64-column
-        // unit (lane & 7) and walks the rows (lane >> 3) + 4k.
-        const int w = tid >> 5, u = lane & 7;
-        if (w < ns) {
-            int t = 0;
-            for (int cur = r_begin; cur < r_end;) {
-                const int n = tile_at(p, cur, r_end).n;
-                const int vrows = DUAL ? 2 * p.box_rows : n;
-                for (int c = 0; c < p.nchunk; ++c, ++t) {
-                    if (t % ns != w) continue;
-                    const uint32_t ph = (uint32_t)((t / ns) & 1);
-                    if (!mbar_wait(&full[w], ph, limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
-                    const uint32_t use = (uint32_t)(t / ns);
-                    if (!flag_wait_geq(&eflag[0][w], use, limit_ns) || !flag_wait_geq(&eflag[1][w], use, limit_ns))
-                        set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
-                    const uint8_t* sb = stages + (size_t)w * p.stage_bytes;
-                    float* T = tbuf + w * (kMaxFold * kTStride);
-                    XUnit x;
-                    load_xunit(smem, p, c * kUnits + u, x);
-                    const int v0 = lane >> 3, nk = (vrows - v0 + 3) >> 2;
-                    for (int k0 = 0; k0 < nk; k0 += 4) {
+        // (3a) compute warps: every warp on every stage.  Lane = (unit u = lane & 7, row
+        // group v0 = lane >> 3); warp w takes the virtual rows v0 + 4 w + 32 j.
+        const int w = tid >> 5, u = lane & 7, v0 = lane >> 3;
+        int t = 0;
+        for (int cur = r_begin; cur < r_end;) {
+            const int n = tile_at(p, cur, r_end).n;
+            const int vrows = DUAL ? 2 * p.box_rows : n;
+            for (int c = 0; c < p.nchunk; ++c, ++t) {
+                const int s = t % ns;
+                const uint32_t use = (uint32_t)(t / ns);
+                if (!mbar_wait(&full[s], use & 1, limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+                if (use > 0 && !mbar_wait(&tempty[s], (use - 1) & 1, limit_ns))
+                    set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+                const uint8_t* sb = stages + (size_t)s * p.stage_bytes;
+                float* T = tbuf + s * (kMaxFold * kTStride);
+                XUnit x;
+                load_xunit(smem, p, c * kUnits + u, x);
+                const uint8_t* rp[2];
+                bool ok[2];
+                int vr[2];
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk) {
-                            const int vr = v0 + 4 * (k0 + kk);
-                            const int mat = DUAL ? (vr >= p.box_rows) : 0;
-                            const int r = vr - mat * p.box_rows;
-                            if (k0 + kk < nk && r < n) {
-                                float t0, t1;
-                                unit_terms<QT>(sb + mat * box2_off + r * p.chunk_bytes, u, x, t0, t1);
-                                float* trow = T + vr * kTStride;
-                                trow[2 * u] = t0;
-                                trow[2 * u + 1] = t1;
-                            }
-                        }
-                    }
-                    __syncwarp();
-                    if (lane == 0) {
-                        mbar_arrive(&empty[w]);
-                        st_release_cta(&tflag[w], use + 1);
+                for (int j = 0; j < 2; ++j) {
+                    vr[j] = v0 + 4 * w + 32 * j;
+                    const int mat = DUAL ? (vr[j] >= p.box_rows) : 0;
+                    const int r = vr[j] - mat * p.box_rows;
+                    ok[j] = vr[j] < vrows && r < n;
+                    rp[j] = sb + mat * box2_off + (ok[j] ? r : 0) * p.chunk_bytes;
+                }
+                float t0[2], t1[2];
+                unit_terms_n<QT, 2>(rp, u, x, t0, t1);
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    if (ok[j]) {
+                        float* trow = T + vr[j] * kTStride;
+                        trow[2 * u] = t0[j];
+                        trow[2 * u + 1] = t1[j];
                     }
                 }
-                cur += n;
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&empty[s]);
+                    mbar_arrive(&tfull[s]);
+                }
             }
+            cur += n;
         }
     } else if (tid < kProducer) {
         // (3b) fold warps: sequential per-row sums in block order, then the epilogue.
@@ -866,16 +924,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
         float best_v = -INFINITY;
         int best_i = 0x7fffffff;
         const int nsb = p.nb / 8;
-        int s = 0;
-        uint32_t use = 0;   // ring slot of the next stage and how often it was used before
+        int t = 0;
         for (int cur = r_begin; cur < r_end;) {
             const TileCursor tc = tile_at(p, cur, r_end);
             const int n = tc.n;
             const bool live = DUAL ? (f < 2 * p.box_rows && (f % p.box_rows) < n) : (f < n);
             float acc = 0.0f;
             const float* trow0 = tbuf + f * kTStride;
-            for (int c = 0; c < p.nchunk; ++c) {
-                if (!flag_wait_geq(&tflag[s], use + 1, limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+            for (int c = 0; c < p.nchunk; ++c, ++t) {
+                const int s = t % ns;
+                const uint32_t use = (uint32_t)(t / ns);
+                if (!mbar_wait(&tfull[s], use & 1, limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
                 if (live) {
                     // all 16 terms into registers first, then the in-order adds
                     const float* trow = trow0 + s * (kMaxFold * kTStride);
@@ -907,8 +966,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
                     }
                 }
                 __syncwarp();
-                if (lane == 0) st_release_cta(&eflag[(tid >> 5) - (kFoldBase >> 5)][s], use + 1);
-                if (++s == ns) { s = 0; ++use; }
+                if (lane == 0) mbar_arrive(&tempty[s]);
             }
 
             // tile epilogue (rows cur .. cur+n-1 of segment tc.seg)
@@ -930,7 +988,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
                         }
                     }
                     if (sg.kind == SEG_Q) sg.out[lr] = v;
-                    else ((sg.kind == SEG_K ? p.kcache : p.vcache) + (size_t)pos * p.kv_width)[lr] = v;
+                    else ((sg.kind == SEG_K ? p.kcache : p.vcache) + (p.kv_stage ? (size_t)0 : (size_t)pos * p.kv_width))[lr] = v;
                 }
             } else if constexpr (EPI == EPI_SILU) {
                 if (f >= p.box_rows && f < p.box_rows + n) xchg[f - p.box_rows] = acc;
@@ -1099,22 +1157,28 @@ int gemv_plan(int qtype, int cols, int rows, bool dual, int in_mode, GemvParams&
     p.chunk_words = p.chunk_bytes / 4;
     p.total_rows = rows;
     int grid = num_sms();
-    const int ra = p.row_align > 2 ? p.row_align : 2;
+    if (p.row_align < 2) p.row_align = 2;
+    const int ra = p.row_align;
     int maxg = (rows + ra - 1) / ra;
     if (maxg < 1) maxg = 1;
     if (grid > maxg) grid = maxg;
     const int per_cta = (rows + grid - 1) / grid;
     // rows per tile: a stage (one tile x 512 columns) stays near 18 KB so that eight
-    // stages fit beside the activation
+    // stages fit beside the activation.  The CTA's rows are split into equal tiles (a
+    // TMA box always brings box_rows rows, so a short last tile would fetch rows that
+    // are not used).
     int maxr = qtype == NCM_T_Q8_0 ? 32 : 64;
     if (dual) maxr /= 2;
-    int br = (per_cta + 1) & ~1;
+    const int span = per_cta + ra;   // the most rows a CTA's aligned range can hold
+    const int ntiles = (span + maxr - 1) / maxr;
+    int br = (span + ntiles - 1) / ntiles;
+    br = (br + ra - 1) / ra * ra;
     if (br > maxr) br = maxr;
     if (br < 2) br = 2;
     p.box_rows = br;
     p.stage_bytes = (br * p.chunk_bytes + 127) / 128 * 128 * (dual ? 2 : 1);
     const int units = p.nchunk * kUnits;
-    int off = 128;
+    int off = 256;   // full / empty / tfull / tempty mbarriers
     p.xq_off = off;
     off += units * 80;
     p.xs_off = off;
@@ -1196,6 +1260,62 @@ __device__ __forceinline__ bool attn_vec_ok(const AttnParams& a) {
     return (((uintptr_t)a.q | (uintptr_t)a.kc | (uintptr_t)a.vc) & 15) == 0 && (a.kvw & 3) == 0;
 }
 
+// Scores over a Q8_0 cache (inference.rs:4319-4357 apply_attention_head_q8_0): q_head is
+// quantised like the store (per 32 values, f16-truncated scale), then per position
+// score = (sum over blocks, in order, of (s_q * s_k) * dot_i32) * scale (q8.rs:509-511).
+// The CTA's 32 positions x hd/32 blocks of K are copied into shared memory as words
+// (the 34-byte blocks are only 2-byte aligned) with their scales decoded.
+__device__ void attn_scores_q8(const AttnParams& a, const float* qsrc, float* scores, int kvh, int g, int p0, int np,
+                               float* qbuf, float* kbuf) {
+    // in the kernel's K tile buffer: [pos][block][8 words] (hd <= 256, padded) + scales;
+    // in its q buffer: [head][block][8 words] + scales
+    uint32_t* kw_s = reinterpret_cast<uint32_t*>(kbuf);
+    float* ksc = kbuf + 32 * 8 * 8 + 32;
+    uint32_t (*qw_s)[64] = reinterpret_cast<uint32_t (*)[64]>(qbuf);
+    float (*qsc)[8] = reinterpret_cast<float (*)[8]>(qbuf + 8 * 64);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, hd = a.hd, bph = hd / 32, bpw = a.kvw / 32;
+    const uint8_t* kb = reinterpret_cast<const uint8_t*>(a.kc_raw);
+    for (int i = tid; i < np * bph; i += 256) {
+        const int pp = i / bph, b = i % bph;
+        const uint16_t* src = reinterpret_cast<const uint16_t*>(kb + ((size_t)(p0 + pp) * bpw + (size_t)kvh * bph + b) * 34);
+        ksc[pp * 8 + b] = f16_bits_to_f32(src[0]);
+        uint32_t* dst = kw_s + (pp * 8 + b) * 8 + pp;   // + pp: rotate banks across positions
+#pragma unroll
+        for (int k = 0; k < 8; ++k) dst[k] = (uint32_t)src[1 + 2 * k] | ((uint32_t)src[2 + 2 * k] << 16);
+    }
+    // quantize_row_to_q8_0_blocks (inference.rs:4298-4317) of each query head of the group
+    for (int i = warp; i < g * bph; i += 8) {
+        const int h = i / bph, b = i % bph;
+        const float x = qsrc[h * hd + 32 * b + lane];
+        float mx = fabsf(x);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(NCM_FULL, mx, o));
+        const float sc = mx / 127.0f, inv = sc > 0.0f ? 1.0f / sc : 0.0f;
+        const int q = (int)fminf(fmaxf(roundf(x * inv), -127.0f), 127.0f);
+        // pack four lanes' bytes into a word
+        const uint32_t byte = (uint32_t)(q & 0xff) << (8 * (lane & 3));
+        uint32_t w = byte;
+        w |= __shfl_xor_sync(NCM_FULL, w, 1);
+        w |= __shfl_xor_sync(NCM_FULL, w, 2);
+        if ((lane & 3) == 0) qw_s[h][b * 8 + (lane >> 2)] = w;
+        if (lane == 0) qsc[h][b] = f16_bits_to_f32(ncm_f32_to_f16_trunc(sc));
+    }
+    __syncthreads();
+    for (int h = warp; h < g; h += 8) {
+        if (lane < np) {
+            float acc = 0.0f;
+            for (int b = 0; b < bph; ++b) {
+                const uint32_t* kr = kw_s + (lane * 8 + b) * 8 + lane;
+                int dot = 0;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) dot = __dp4a((int)qw_s[h][b * 8 + k], (int)kr[k], dot);
+                acc += qsc[h][b] * ksc[lane * 8 + b] * (float)dot;
+            }
+            scores[(size_t)(kvh * g + h) * a.ctx + p0 + lane] = acc * a.scale;
+        }
+    }
+}
+
 // Stage 1 (attn_scores_kernel): scores[h][p] = dot_f32(q_h, k_p) * scale with the dot a
 // sequential sum over head_dim (inference.rs:3570-3573, 4256); grid (kv head, 32
 // positions), warp = query head of the group, lane = position.  The K tile is loaded
@@ -1216,7 +1336,17 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const __grid_constant_
     const float* qsrc = a.q + (size_t)tz * a.tok_stride + (size_t)kvh * g * hd;
     float* scores = a.scores + (size_t)tz * a.heads * a.ctx;
     const float* ksrc = a.kc + (size_t)p0 * a.kvw + (size_t)kvh * hd;
-    if (attn_vec_ok(a)) {
+    if (a.kv_kind == KV_Q8_0) {
+        attn_scores_q8(a, qsrc, scores, kvh, g, p0, np, qs, ks);
+        return;
+    }
+    if (a.kv_kind == KV_F16) {
+        // decode_f16_head (inference.rs:4453-4458): exact f16 -> f32, then the f32 path
+        const uint16_t* k16 = reinterpret_cast<const uint16_t*>(a.kc_raw) + (size_t)p0 * a.kvw + (size_t)kvh * hd;
+        for (int i = tid; i < g * hd; i += 256) qs[i] = qsrc[i];
+        for (int i = tid; i < np * hd; i += 256)
+            ks[(i / hd) * (hd + 1) + i % hd] = f16_bits_to_f32(k16[(size_t)(i / hd) * a.kvw + i % hd]);
+    } else if (attn_vec_ok(a)) {
         const int per = hd >> 2;                 // float4 per row
         float4 qv[2], kv[8];
 #pragma unroll
@@ -1279,11 +1409,25 @@ __global__ void __launch_bounds__(256) attn_softmax_v_kernel(const __grid_consta
     const int d0 = blockIdx.y * dw;
     float* w = sm;
     float* vs = sm + ((g * a.ctx + 3) & ~3);
-    const bool vec = attn_vec_ok(a) && (dw & 3) == 0;
+    const bool vec = a.kv_kind == KV_F32 && attn_vec_ok(a) && (dw & 3) == 0;
     const float* vsrc = a.vc + (size_t)kvh * hd + d0;
     auto stage = [&](int c0) {
         const int np = min(a.vchunk, n - c0);
-        if (vec) {
+        if (a.kv_kind == KV_F16) {
+            // decode_f16_head (inference.rs:4453-4458)
+            const uint16_t* v16 = reinterpret_cast<const uint16_t*>(a.vc_raw) + (size_t)kvh * hd + d0;
+            for (int i = tid; i < np * dw; i += 256)
+                vs[i] = f16_bits_to_f32(v16[(size_t)(c0 + i / dw) * a.kvw + i % dw]);
+        } else if (a.kv_kind == KV_Q8_0) {
+            // inference.rs:4369-4379: value = q as f32 * block scale
+            const uint8_t* vb = reinterpret_cast<const uint8_t*>(a.vc_raw);
+            const int bph = hd / 32, bpw = a.kvw / 32;
+            for (int i = tid; i < np * dw; i += 256) {
+                const int pp = c0 + i / dw, d = d0 + i % dw;
+                const uint8_t* blk = vb + ((size_t)pp * bpw + (size_t)kvh * bph + d / 32) * 34;
+                vs[i] = (float)(int8_t)blk[2 + d % 32] * f16_bits_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
+            }
+        } else if (vec) {
             const int per = dw >> 2;
             for (int i = tid; i < np * per; i += 256)
                 cp_async16(vs + 4 * i, vsrc + (size_t)(c0 + i / per) * a.kvw + 4 * (i % per));
@@ -1385,7 +1529,50 @@ int attention_launch(const AttnParams& a0, cudaStream_t s, bool pdl) {
     return (int)cudaLaunchKernelEx(&cfg, attn_softmax_v_kernel, a);
 }
 
+// store_kv (inference.rs:539-568) for the F16 cache (fast_f32_to_f16 per value) and the
+// Q8_0 cache (quantize_row_to_q8_0_blocks, inference.rs:4298-4317: scale = max|x|/127,
+// inv = 1/scale or 0, q = round(x * inv) clamped, scale stored as truncated f16): one warp
+// per 32-value block, grid (blocks, token).
+__global__ void kv_store_kernel(int kind, const float* sk, const float* sv, int kw, uint8_t* kc, uint8_t* vc,
+                                const int* pos_dev) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int t = blockIdx.y, lane = threadIdx.x & 31;
+    const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (b >= kw / 32) return;
+    const int pos = pos_dev[0] + t;
+    for (int which = 0; which < 2; ++which) {
+        const float x = (which ? sv : sk)[(size_t)t * kw + 32 * b + lane];
+        uint8_t* cache = which ? vc : kc;
+        if (kind == KV_F16) {
+            reinterpret_cast<uint16_t*>(cache)[(size_t)pos * kw + 32 * b + lane] = ncm_f32_to_f16_trunc(x);
+        } else {
+            float mx = fabsf(x);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(NCM_FULL, mx, o));
+            const float sc = mx / 127.0f, inv = sc > 0.0f ? 1.0f / sc : 0.0f;
+            const int q = (int)fminf(fmaxf(roundf(x * inv), -127.0f), 127.0f);
+            uint8_t* blk = cache + ((size_t)pos * (kw / 32) + b) * 34;
+            blk[2 + lane] = (uint8_t)(int8_t)q;
+            if (lane == 0) {
+                const uint16_t h = ncm_f32_to_f16_trunc(sc);
+                blk[0] = (uint8_t)(h & 0xff);
+                blk[1] = (uint8_t)(h >> 8);
+            }
+        }
+    }
+}
+
 // ------------------------------------------------------------------ small kernels
+static cudaLaunchConfig_t small_cfg(dim3 g, dim3 b, cudaStream_t s, bool pdl, cudaLaunchAttribute* attr);
+int kv_store_launch(int kind, const float* sk, const float* sv, int ntok, int kw, void* kc, void* vc,
+                    const int* pos_dev, cudaStream_t s, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    const int nb = kw / 32;
+    cudaLaunchConfig_t cfg = small_cfg(dim3((nb + 7) / 8, ntok), dim3(256), s, pdl, attr);
+    return (int)cudaLaunchKernelEx(&cfg, kv_store_kernel, kind, sk, sv, kw, (uint8_t*)kc, (uint8_t*)vc, pos_dev);
+}
+
 // One element of a dequantised row (model.rs:1109-1132 load_f32_or_f16 semantics).
 __device__ __forceinline__ float dequant_elem(int type, const uint8_t* row, int i) {
     if (type == NCM_T_F32) return reinterpret_cast<const float*>(row)[i];
@@ -2067,7 +2254,8 @@ __global__ void __launch_bounds__(kBatchThreads, 1) ncm_qgemm_verify_kernel(cons
                             }
                         }
                         if (sg.kind == SEG_Q) sg.out[(size_t)tk * p.out_stride + lr] = o;
-                        else ((sg.kind == SEG_K ? p.kcache : p.vcache) + (size_t)(pos0 + tk) * p.kv_width)[lr] = o;
+                        else ((sg.kind == SEG_K ? p.kcache : p.vcache) +
+                              (size_t)(p.kv_stage ? tk : pos0 + tk) * p.kv_width)[lr] = o;
                     } else if constexpr (EPI == EPI_SILU) {
                         const float gg = v, uu = acc2[i];
                         const float sig = 1.0f / (1.0f + expf_cr(-gg));   // inference.rs:3385-3388
@@ -2352,4 +2540,187 @@ int embed_rows_launch(int type, const uint8_t* table, int64_t pitch, int emb, co
     return (int)cudaLaunchKernelEx(&cfg, embed_rows_kernel, type, table, pitch, emb, toks, hidden);
 }
 
+
+// ================================================================== Q6_K GEMV
+// matmul_q6_k (inference.rs:3045-3087) over Q6KBlock::dot_q8_scaled (q8.rs:2092-2150),
+// the x86 path: per super-block sum = 0, then for each 128-half the 256 products
+// (c * q) * x, c = (d * scale) * x_scale, added one at a time in the order l = 0..15 then
+// 16..31, quarters q1..q4 within each l; the row sum adds the super-block sums in order.
+// That is one sequential f32 chain per row, so each thread owns one row.  The thread
+// reads its row with 16-byte loads: a run of 8 super-blocks (1680 bytes) starts on a
+// 16-byte boundary, so with the run unrolled every super-block's byte offset is a
+// compile-time constant and its fields are assembled from the loaded words without
+// dynamic register indexing.  The activation is staged once per CTA as f32 (exact).
+template <int J>
+__device__ __forceinline__ uint32_t q6_word(const uint4 (&u)[14], int i) {
+    // 32-bit word i of super-block J of the run (its bytes 4i .. 4i+3)
+    constexpr int off = (210 * J) & 15;
+    const int b = off + 4 * i;                  // byte offset inside the 16-byte-aligned cover
+    const int q = b >> 2, sh = (b & 3) * 8;
+    auto w = [&](int k) -> uint32_t {
+        if (k >= 56) return 0u;   // past the cover (only its unused high half is asked for)
+        const uint4 v = u[k >> 2];
+        return (k & 3) == 0 ? v.x : (k & 3) == 1 ? v.y : (k & 3) == 2 ? v.z : v.w;
+    };
+    return sh ? __funnelshift_r(w(q), w(q + 1), sh) : w(q);
+}
+
+template <int J>
+__device__ __forceinline__ float q6k_block_sum(const uint4 (&u)[14], const float* x, const float* xs) {
+    float ws[16];
+    const uint32_t dw = q6_word<J>(u, 52);      // bytes 208..211: d at 208
+    const float d = f16_bits_to_f32(dw & 0xffff);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t sw = q6_word<J>(u, 48 + i);   // scales 192 + 4i ..
+#pragma unroll
+        for (int b = 0; b < 4; ++b) ws[4 * i + b] = d * (float)(int)(int8_t)(sw >> (8 * b));
+    }
+    float sum = 0.0f;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        float c[4][2];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            c[j][0] = ws[8 * half + 2 * j] * xs[4 * half + j];
+            c[j][1] = ws[8 * half + 2 * j + 1] * xs[4 * half + j];
+        }
+        const float* xh = x + 128 * half;
+#pragma unroll
+        for (int l4 = 0; l4 < 8; ++l4) {
+            const uint32_t a = q6_word<J>(u, 16 * half + l4);        // ql[64 half + 4 l4 ..]
+            const uint32_t b = q6_word<J>(u, 16 * half + 8 + l4);    // ql[64 half + 32 + 4 l4 ..]
+            const uint32_t h = q6_word<J>(u, 32 + 8 * half + l4);    // qh[32 half + 4 l4 ..]
+            const uint32_t q1 = (a & 0x0f0f0f0fu) | ((h & 0x03030303u) << 4);
+            const uint32_t q2 = (b & 0x0f0f0f0fu) | (((h >> 2) & 0x03030303u) << 4);
+            const uint32_t q3 = ((a >> 4) & 0x0f0f0f0fu) | (((h >> 4) & 0x03030303u) << 4);
+            const uint32_t q4 = ((b >> 4) & 0x0f0f0f0fu) | (((h >> 6) & 0x03030303u) << 4);
+            const int hi = l4 >= 4;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int l = 4 * l4 + k;
+                const float f1 = (float)((int)((q1 >> (8 * k)) & 0xff) - 32);
+                const float f2 = (float)((int)((q2 >> (8 * k)) & 0xff) - 32);
+                const float f3 = (float)((int)((q3 >> (8 * k)) & 0xff) - 32);
+                const float f4 = (float)((int)((q4 >> (8 * k)) & 0xff) - 32);
+                sum += c[0][hi] * f1 * xh[l];
+                sum += c[1][hi] * f2 * xh[l + 32];
+                sum += c[2][hi] * f3 * xh[l + 64];
+                sum += c[3][hi] * f4 * xh[l + 96];
+            }
+        }
+    }
+    return sum;
+}
+
+template <int J>
+__device__ __forceinline__ void q6k_run_step(const uint8_t* run, int nsb_left, const float* xr, const float* xsr,
+                                             float& acc) {
+    if (J >= nsb_left) return;
+    uint4 u[14];
+    const uint4* src = reinterpret_cast<const uint4*>(run + ((210 * J) & ~15));
+    const int nu = ((((210 * J) & 15) + 210 + 15) >> 4);   // 16-byte words covering the block
+#pragma unroll
+    for (int i = 0; i < 14; ++i) u[i] = i < nu ? __ldg(src + i) : make_uint4(0, 0, 0, 0);
+    acc += q6k_block_sum<J>(u, xr + 256 * J, xsr + 8 * J);   // inference.rs:3082 sum += block dot
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(128) ncm_q6k_gemv_kernel(const __grid_constant__ Q6Params p) {
+    extern __shared__ __align__(16) float q6x[];   // x as f32 [cols], then x scales [cols / 32]
+    __shared__ float wv[4];
+    __shared__ int wi[4];
+    __shared__ int s_last;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tid = threadIdx.x, lane = tid & 31;
+    float* xsf = q6x + p.cols;
+    for (int i = tid; i < p.cols; i += blockDim.x) q6x[i] = (float)p.xq[i];
+    for (int i = tid; i < p.cols / 32; i += blockDim.x) xsf[i] = p.xs[i];
+    __syncthreads();
+    const int r = blockIdx.x * blockDim.x + tid;
+    const int nsb = p.cols / 256;
+    float acc = 0.0f;
+    if (r < p.rows) {
+        const uint8_t* row = p.w + (size_t)r * p.pitch;
+        for (int g = 0; g < nsb; g += 8) {
+            const uint8_t* run = row + (size_t)g * 210;   // 1680 g / 8 bytes: 16-byte aligned
+            const int left = nsb - g;
+            const float* xr = q6x + 256 * g;
+            const float* xsr = xsf + 8 * g;
+            q6k_run_step<0>(run, left, xr, xsr, acc);
+            q6k_run_step<1>(run, left, xr, xsr, acc);
+            q6k_run_step<2>(run, left, xr, xsr, acc);
+            q6k_run_step<3>(run, left, xr, xsr, acc);
+            q6k_run_step<4>(run, left, xr, xsr, acc);
+            q6k_run_step<5>(run, left, xr, xsr, acc);
+            q6k_run_step<6>(run, left, xr, xsr, acc);
+            q6k_run_step<7>(run, left, xr, xsr, acc);
+        }
+        if constexpr (EPI == EPI_PLAIN) p.out[r] = acc;
+        else if constexpr (EPI == EPI_RESID) p.out[r] += acc;   // inference.rs:4744-4746
+        else if (p.out) p.out[r] = acc;
+    }
+    if constexpr (EPI == EPI_ARGMAX) {
+        // strict first-max (inference.rs:4838-4843): CTA, then the last CTA over all CTAs
+        float bv = r < p.rows ? acc : -INFINITY;
+        int bi = r < p.rows ? r : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(NCM_FULL, bv, o);
+            const int oi = __shfl_xor_sync(NCM_FULL, bi, o);
+            if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) { wv[tid >> 5] = bv; wi[tid >> 5] = bi; }
+        __syncthreads();
+        if (tid == 0) {
+            for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+                if (better(wv[w], wi[w], bv, bi)) { bv = wv[w]; bi = wi[w]; }
+            p.amax_part[blockIdx.x] = make_float2(bv, __int_as_float(bi));
+            __threadfence();
+            s_last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
+        }
+        __syncthreads();
+        if (s_last && tid == 0) {
+            __threadfence();
+            bv = -INFINITY;
+            bi = 0x7fffffff;
+            for (int c = 0; c < (int)gridDim.x; ++c) {
+                const float2 e = __ldcg(&p.amax_part[c]);
+                const int ei = __float_as_int(e.y);
+                if (better(e.x, ei, bv, bi)) { bv = e.x; bi = ei; }
+            }
+            const int tok = p.head_row0 + bi;
+            if (p.head_out) {
+                *p.head_out = make_float2(bv, __int_as_float(tok));
+            } else {
+                const int ps = p.state[ST_POS];
+                if (ps + 1 < p.ctx && ps + 1 >= p.state[ST_NPROMPT]) p.tokens[ps + 1] = tok;
+                p.state[ST_LAST_TOKEN] = tok;
+                p.state[ST_POS] = ps + 1;
+                p.state[ST_STEP] += 1;
+            }
+            *p.counter = 0u;
+        }
+    }
+}
+
+int q6k_gemv_launch(int epi, const Q6Params& p, cudaStream_t s, bool pdl) {
+    if (p.cols % 256 || (p.pitch & 15) || ((uintptr_t)p.w & 15)) return (int)cudaErrorInvalidValue;
+    const size_t smem = (size_t)p.cols * 4 + (size_t)(p.cols / 32) * 4;
+    int threads = 128;
+    while (threads > 32 && (int64_t)(p.rows + threads - 1) / threads < num_sms()) threads >>= 1;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = small_cfg(dim3((p.rows + threads - 1) / threads), dim3(threads), s, pdl, attr);
+    cfg.dynamicSmemBytes = smem;
+    const void* fn = epi == EPI_PLAIN ? (const void*)ncm_q6k_gemv_kernel<EPI_PLAIN>
+                   : epi == EPI_RESID ? (const void*)ncm_q6k_gemv_kernel<EPI_RESID>
+                                      : (const void*)ncm_q6k_gemv_kernel<EPI_ARGMAX>;
+    if (int r = set_smem_limit(fn, 200 * 1024)) return r;
+    if (smem > 200 * 1024) return (int)cudaErrorInvalidValue;
+    if (epi == EPI_PLAIN) return (int)cudaLaunchKernelEx(&cfg, ncm_q6k_gemv_kernel<EPI_PLAIN>, p);
+    if (epi == EPI_RESID) return (int)cudaLaunchKernelEx(&cfg, ncm_q6k_gemv_kernel<EPI_RESID>, p);
+    if (epi == EPI_ARGMAX) return (int)cudaLaunchKernelEx(&cfg, ncm_q6k_gemv_kernel<EPI_ARGMAX>, p);
+    return (int)cudaErrorInvalidValue;
+}
 }  // namespace ncm

@@ -86,6 +86,8 @@ struct alignas(64) GemvParams {
     TpComm tp;
     int tp_slot;                  // layer*2 + phase
     int* err;
+    int kv_stage;                 // 1: K / V rows go to kcache / vcache as given (staging for an
+                                  //    F16 / Q8_0 cache), 0: the f32 cache rows at pos
     int row_align;                // CTA row ranges start at multiples of this (2, or 32 with qout)
     int8_t* qout;                 // EPI_SILU: the output rows also as Q8_0 blocks (box_rows == 32) ...
     float* qout_s;                //   ... and their scales: the next projection's quantised input
@@ -113,7 +115,13 @@ struct AttnParams {
     int tok_stride;          //   + z * tok_stride floats, scores at + z * heads * ctx
     int8_t* out_q;           // when set (one row, head_dim / dsplit == 32): the output also as Q8_0
     float* out_s;            //   blocks (quantize_f32_to_q8_0), the next projection's input
+    int kv_kind;             // cache storage: 0 f32 (kc / vc), 1 F16, 2 Q8_0 (kc_raw / vc_raw)
+    const void* kc_raw;
+    const void* vc_raw;
 };
+
+// KV-cache storage kinds (inference.rs:505-599; NANOCAMELID_KV_CACHE_F16 / _Q8).
+enum KvKind { KV_F32 = 0, KV_F16 = 1, KV_Q8_0 = 2 };
 
 // Multi-row (speculative verify) GEMV: ntok activation rows share every weight tile;
 // int8 tensor-core MMA forms the block dots (16 weight rows x 8 token rows per
@@ -144,6 +152,7 @@ struct alignas(64) BatchParams {
     int rope_half, head_dim;
     float* kcache; float* vcache;
     int kv_width;
+    int kv_stage;                 // 1: token t's K / V row at kcache / vcache + t * kv_width (staging)
     float2* amax_part;            // EPI_ARGMAX: [grid][kMaxBatch]
     unsigned* counter;
     int* argmax_out;              // [ntok] global vocab rows
@@ -152,7 +161,28 @@ struct alignas(64) BatchParams {
     int* err;
 };
 
+// Q6_K GEMV (q8.rs:2092-2150 dot_q8_scaled, inference.rs:3045-3087 matmul_q6_k): one
+// thread per output row folds the row's 256 products per super-block in the reference's
+// order.  Input: Q8_0 activation in global memory.  Epilogues EPI_PLAIN, EPI_RESID,
+// EPI_ARGMAX (one GPU, or head_out for a vocab shard).
+struct Q6Params {
+    const uint8_t* w;             // raw Q6_K rows, 16-byte aligned pitch
+    int64_t pitch;
+    int rows, cols;
+    const int8_t* xq;             // [cols]
+    const float* xs;              // [cols / 32]
+    float* out;                   // EPI_PLAIN: out[row]; EPI_RESID: out[row] += ; EPI_ARGMAX: logits (or null)
+    float2* amax_part;            // EPI_ARGMAX: [grid]
+    unsigned* counter;
+    int head_row0;
+    float2* head_out;             // set: this shard's (logit, token) only, state untouched
+    int* state;
+    int* tokens;
+    int ctx;
+};
+
 // Launchers (kernels.cu).
+int q6k_gemv_launch(int epi, const Q6Params& p, cudaStream_t s, bool pdl);
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -162,6 +192,10 @@ int gemv_plan(int qtype, int cols, int rows, bool dual, int in_mode, GemvParams&
 int gemv_tensor_map(CUtensorMap* tm, const void* base, int64_t rows, int pitch, int chunk_words, int box_rows);
 int gemv_launch(int qtype, int in_mode, int epi, const GemvParams& p, int grid, cudaStream_t s, bool pdl);
 int attention_launch(const AttnParams& a, cudaStream_t s, bool pdl);
+// store_kv (inference.rs:539-568) of ntok staged f32 K / V rows [ntok][kw] into an F16 or
+// Q8_0 cache (layer base kc / vc) at positions pos + t, pos = pos_dev[0] (+ pos_add).
+int kv_store_launch(int kind, const float* sk, const float* sv, int ntok, int kw, void* kc, void* vc,
+                    const int* pos_dev, cudaStream_t s, bool pdl);
 int embed_ssq_launch(int type, const uint8_t* table, int64_t pitch, int emb, int vocab, float* out, cudaStream_t s);
 int embed_launch(int type, const uint8_t* table, int64_t pitch, int emb, const int* tokens, const int* state,
                  float* hidden, cudaStream_t s, bool pdl);

@@ -12,6 +12,9 @@
 //   Q4_0 : q8.rs:2442-2488 quantize_f32_matrix_to_q4_0_blocks (d = signed-max/-8,
 //          q = trunc(x*id + 8.5) clamped to 0..15, f16 scale truncated).
 //   Q8_0 : q8.rs:2389-2440 quantize_f32_matrix_to_q8_0_blocks.
+//   Q6_K : the reference only decodes Q6_K (q8.rs:2026-2090); this encoder is our own
+//          (per 16-value group an i8 scale, d = max group scale / 127, 6-bit values
+//          q + 32 split into ql nibbles and qh bit pairs as q8.rs:2069-2077 reads them).
 //   Q4_K : the reference only decodes Q4_K (q8.rs:1193-1376); this encoder is our own
 //          (per 32-sub-block min/max, 6-bit scales/mins packed as q8.rs:2009-2018 reads
 //          them).  Any valid encoder serves: the oracle and the GPU read the same bytes.
@@ -29,7 +32,7 @@
 #define NCM_HD static inline
 #endif
 
-enum { NCM_T_F32 = 0, NCM_T_F16 = 1, NCM_T_Q4_0 = 2, NCM_T_Q8_0 = 8, NCM_T_Q4_K = 12 };
+enum { NCM_T_F32 = 0, NCM_T_F16 = 1, NCM_T_Q4_0 = 2, NCM_T_Q8_0 = 8, NCM_T_Q4_K = 12, NCM_T_Q6_K = 14 };
 
 // 0.02 * sqrt(3) / 65536 rounded to f32 (written in hex so every compiler agrees).
 #define NCM_SYNTH_SCALE 0x1.1bc77ap-21f
@@ -177,9 +180,45 @@ NCM_HD void ncm_encode_q4_k(const float* v, uint8_t* o) {
         }
 }
 
-NCM_HD int ncm_type_block_elems(int t) { return t == NCM_T_Q4_K ? 256 : (t == NCM_T_Q4_0 || t == NCM_T_Q8_0) ? 32 : 1; }
+// Q6_K block (210 bytes): ql[128] | qh[64] | scales i8[16] | d f16.  Element e of the
+// block: half = e / 128, quarter j = (e % 128) / 32, l = e % 32; its low 4 bits are the
+// low (j = 0, 1) or high (j = 2, 3) nibble of ql[64 half + l + 32 (j & 1)], its high 2
+// bits are bits 2j, 2j+1 of qh[32 half + l]; value = d * scales[e / 16] * (q - 32).
+NCM_HD void ncm_encode_q6_k(const float* v, uint8_t* o) {
+    float gs[16], maxgs = 0.0f;
+    for (int g = 0; g < 16; ++g) {
+        float amax = 0.0f;
+        for (int i = 0; i < 16; ++i) { float a = fabsf(v[16 * g + i]); if (a > amax) amax = a; }
+        gs[g] = amax / 31.0f;
+        if (gs[g] > maxgs) maxgs = gs[g];
+    }
+    uint16_t db = ncm_f32_to_f16_trunc(maxgs / 127.0f);
+    float d = ncm_f16_to_f32(db);
+    int sc[16];
+    for (int g = 0; g < 16; ++g) {
+        float a = d > 0.0f ? roundf(gs[g] / d) : 0.0f;
+        sc[g] = a < 0.0f ? 0 : (a > 127.0f ? 127 : (int)a);
+        o[192 + g] = (uint8_t)(int8_t)sc[g];
+    }
+    for (int i = 0; i < 192; ++i) o[i] = 0;
+    for (int e = 0; e < 256; ++e) {
+        float step = d * (float)sc[e / 16];
+        float t = step > 0.0f ? roundf(v[e] / step) : 0.0f;
+        int q = (t < -32.0f ? -32 : (t > 31.0f ? 31 : (int)t)) + 32;
+        int half = e / 128, j = (e % 128) / 32, l = e % 32;
+        int qi = 64 * half + l + 32 * (j & 1);
+        o[qi] |= (uint8_t)((q & 15) << (j >= 2 ? 4 : 0));
+        o[128 + 32 * half + l] |= (uint8_t)((q >> 4) << (2 * j));
+    }
+    ncm_put16(o + 208, db);
+}
+
+NCM_HD int ncm_type_block_elems(int t) {
+    return (t == NCM_T_Q4_K || t == NCM_T_Q6_K) ? 256 : (t == NCM_T_Q4_0 || t == NCM_T_Q8_0) ? 32 : 1;
+}
 NCM_HD int ncm_type_block_bytes(int t) {
-    return t == NCM_T_Q4_0 ? 18 : t == NCM_T_Q8_0 ? 34 : t == NCM_T_Q4_K ? 144 : t == NCM_T_F32 ? 4 : t == NCM_T_F16 ? 2 : 0;
+    return t == NCM_T_Q4_0 ? 18 : t == NCM_T_Q8_0 ? 34 : t == NCM_T_Q4_K ? 144 : t == NCM_T_Q6_K ? 210
+         : t == NCM_T_F32 ? 4 : t == NCM_T_F16 ? 2 : 0;
 }
 
 // Encode one block (or one element for F32/F16) of global tensor row `r` starting at
@@ -192,10 +231,11 @@ NCM_HD void ncm_synth_block(int type, uint64_t key, uint64_t r, uint64_t c, uint
         else ncm_put16(o, ncm_f32_to_f16_trunc(v));
         return;
     }
-    if (type == NCM_T_Q4_K) {
+    if (type == NCM_T_Q4_K || type == NCM_T_Q6_K) {
         float v[256];
         for (int i = 0; i < 256; ++i) v[i] = ncm_synth_value(key, base + i);
-        ncm_encode_q4_k(v, o);
+        if (type == NCM_T_Q4_K) ncm_encode_q4_k(v, o);
+        else ncm_encode_q6_k(v, o);
         return;
     }
     float v[32];

@@ -713,6 +713,8 @@ typedef struct {
     qmat head;                                 /* untied output.weight or tied Q4_0 requant */
     orc_layer* L;
     float *kc, *vc;                            /* [layer][ctx][kv_width] f32, inference.rs:505-547 */
+    int kv_kind;                               /* 0 f32, 1 F16, 2 Q8_0 storage (inference.rs:505-599) */
+    uint8_t *kq, *vq;                          /* the F16 / Q8_0 caches when kv_kind != 0 */
     /* workspace (inference.rs:601-695) */
     float *hidden, *residual, *norm_x, *q, *k, *v, *att, *gate, *up, *gu, *logits;
     int8_t* xq; float* xs;
@@ -819,6 +821,7 @@ typedef struct {
     float rope_base, eps;
     int32_t tied, t_embd, t_attn, t_ffn, t_out;
     uint64_t seed;
+    int32_t t_down;   /* ffn_down type (0: t_ffn) */
 } orc_synth_spec;
 
 static uint64_t syn_mix(uint64_t x) {   /* splitmix64 */
@@ -880,6 +883,38 @@ static void syn_encode_q4_k(const float* v, uint8_t* o) {
         }
 }
 
+/* Q6_K (the reference has no encoder, q8.rs:2026-2090 only decodes): per 16-value group
+ * an i8 scale round(group_max|x|/31 / d), d = max(group_max|x|/31) / 127 (f16, truncated),
+ * 6-bit q = round(x / (d scale)) + 32 clamped to 0..63, its low nibble in ql and its top two
+ * bits in qh where q8.rs:2069-2077 reads them. */
+static void syn_encode_q6_k(const float* v, uint8_t* o) {
+    float gs[16], maxgs = 0.0f;
+    for (int g = 0; g < 16; ++g) {
+        float amax = 0.0f;
+        for (int i = 0; i < 16; ++i) { float a = fabsf(v[16 * g + i]); if (a > amax) amax = a; }
+        gs[g] = amax / 31.0f;
+        if (gs[g] > maxgs) maxgs = gs[g];
+    }
+    uint16_t db = orc_f32_to_f16(maxgs / 127.0f);
+    float d = orc_f16_to_f32(db);
+    int sc[16];
+    for (int g = 0; g < 16; ++g) {
+        float a = d > 0.0f ? roundf(gs[g] / d) : 0.0f;
+        sc[g] = a < 0.0f ? 0 : (a > 127.0f ? 127 : (int)a);
+        o[192 + g] = (uint8_t)(int8_t)sc[g];
+    }
+    memset(o, 0, 192);
+    for (int e = 0; e < 256; ++e) {
+        float step = d * (float)sc[e / 16];
+        float t = step > 0.0f ? roundf(v[e] / step) : 0.0f;
+        int q = (t < -32.0f ? -32 : (t > 31.0f ? 31 : (int)t)) + 32;
+        int half = e / 128, j = (e % 128) / 32, l = e % 32;
+        o[64 * half + l + 32 * (j & 1)] |= (uint8_t)((q & 15) << (j >= 2 ? 4 : 0));
+        o[128 + 32 * half + l] |= (uint8_t)((q >> 4) << (2 * j));
+    }
+    o[208] = db & 0xff; o[209] = db >> 8;
+}
+
 /* Rows [r0, r0 + nrows) x columns [c0, c0 + ncols) of a synthetic tensor `cols` wide,
  * raw blocks, row-major, no padding. */
 void orc_synth_tensor(int type, uint64_t key, long r0, long nrows, long c0, long ncols, long cols, uint8_t* out) {
@@ -896,6 +931,7 @@ void orc_synth_tensor(int type, uint64_t key, long r0, long nrows, long c0, long
             if (type == T_Q4_0) orc_quantize_block_q4_0(v, o);
             else if (type == T_Q8_0) orc_quantize_block_q8_0(v, o);
             else if (type == T_Q4_K) syn_encode_q4_k(v, o);
+            else if (type == T_Q6_K) syn_encode_q6_k(v, o);
             else if (type == T_F32) memcpy(o, &v[0], 4);
             else { uint16_t h = orc_f32_to_f16(v[0]); o[0] = h & 0xff; o[1] = h >> 8; }
         }
@@ -943,7 +979,7 @@ orc_model* orc_model_create_synthetic(const orc_synth_spec* sp, int ctx_limit) {
 #define SQ(field, s, t, r, c) snprintf(nm, sizeof nm, "blk.%d." s ".weight", i); if (syn_mat(sp, nm, t, r, c, &l->field)) return NULL;
         SQ(wq, "attn_q", sp->t_attn, QW, H) SQ(wk, "attn_k", sp->t_attn, KW, H) SQ(wv, "attn_v", sp->t_attn, KW, H)
         SQ(wo, "attn_output", sp->t_attn, H, QW) SQ(w1, "ffn_gate", sp->t_ffn, F, H) SQ(w3, "ffn_up", sp->t_ffn, F, H)
-        SQ(w2, "ffn_down", sp->t_ffn, H, F)
+        SQ(w2, "ffn_down", sp->t_down ? sp->t_down : sp->t_ffn, H, F)
 #undef SQ
     }
     alloc_workspace(m);
@@ -967,6 +1003,25 @@ void orc_model_fill_kv(orc_model* m, int npos, uint64_t seed) {
     }
 }
 
+/* Bytes of one cached K (or V) row of kv_width values in the cache's storage type. */
+static size_t kv_row_bytes(const orc_model* m) {
+    return m->kv_kind == 1 ? 2 * (size_t)m->kvw : m->kv_kind == 2 ? (size_t)m->kvw / 32 * 34 : 4 * (size_t)m->kvw;
+}
+
+/* inference.rs:512-531: the cache storage the reference picks (NANOCAMELID_KV_CACHE_Q8 when
+ * kv_width is a multiple of 32, else NANOCAMELID_KV_CACHE_F16, else f32); kind 1 F16,
+ * kind 2 Q8_0.  Clears the cache. */
+int orc_model_set_kv_kind(orc_model* m, int kind) {
+    if (kind == 2 && m->kvw % 32) kind = 0;
+    m->kv_kind = kind;
+    free(m->kq); free(m->vq); m->kq = m->vq = NULL;
+    if (kind) {
+        size_t n = kv_row_bytes(m) * (size_t)m->layers * m->ctx;
+        m->kq = calloc(n, 1); m->vq = calloc(n, 1);
+    }
+    return kind;
+}
+
 int orc_model_info(const orc_model* m, int* out) {
     out[0] = m->emb; out[1] = m->layers; out[2] = m->ffn; out[3] = m->heads; out[4] = m->kv_heads;
     out[5] = m->hd; out[6] = m->vocab; out[7] = m->rope_dim; out[8] = m->ctx; out[9] = m->head.type;
@@ -975,12 +1030,45 @@ int orc_model_info(const orc_model* m, int* out) {
 void orc_model_reset(orc_model* m) {
     size_t kvn = (size_t)m->layers * m->ctx * m->kvw;
     memset(m->kc, 0, kvn * 4); memset(m->vc, 0, kvn * 4);
+    if (m->kv_kind) {
+        size_t n = kv_row_bytes(m) * (size_t)m->layers * m->ctx;
+        memset(m->kq, 0, n); memset(m->vq, 0, n);
+    }
 }
 const uint8_t* orc_model_head_blocks(const orc_model* m) { return m->head.data; }
 float* orc_model_hidden(orc_model* m) { return m->hidden; }
 
 static void mm(const qmat* w, const int8_t* xq, const float* xs, float* out) {
     orc_matmul_quantized(w->type, w->data, w->rows, w->cols, xq, xs, out);
+}
+
+/* inference.rs:539-568 store_kv at (layer, pos). */
+static void kv_store(orc_model* m, int li, int pos, const float* k, const float* v) {
+    size_t lo = (size_t)li * m->ctx * m->kvw;
+    if (m->kv_kind == 0) {
+        memcpy(m->kc + lo + (size_t)pos * m->kvw, k, 4 * (size_t)m->kvw);
+        memcpy(m->vc + lo + (size_t)pos * m->kvw, v, 4 * (size_t)m->kvw);
+        return;
+    }
+    size_t off = ((size_t)li * m->ctx + pos) * kv_row_bytes(m);
+    if (m->kv_kind == 1) {
+        orc_kv_store_f16(k, m->kvw, (uint16_t*)(m->kq + off));
+        orc_kv_store_f16(v, m->kvw, (uint16_t*)(m->vq + off));
+    } else {
+        orc_kv_quantize_row_q8_0(k, m->kvw, m->kq + off);
+        orc_kv_quantize_row_q8_0(v, m->kvw, m->vq + off);
+    }
+}
+
+/* inference.rs:4142-4292 (+ 4319-4458 for the F16 / Q8_0 caches) over layer li. */
+static void kv_attend(orc_model* m, int li, float* out, const float* q, int pos) {
+    if (m->kv_kind == 0) {
+        size_t lo = (size_t)li * m->ctx * m->kvw;
+        orc_attention(out, q, m->kc + lo, m->vc + lo, pos, m->heads, m->kv_heads, m->hd, m->kvw);
+        return;
+    }
+    size_t off = (size_t)li * m->ctx * kv_row_bytes(m);
+    orc_attention_kv(m->kv_kind, out, q, m->kq + off, m->vq + off, pos, m->heads, m->kv_heads, m->hd, m->kvw);
 }
 
 /* inference.rs:4505-4781 run_layer_range (dense FFN) for one token at `pos`. */
@@ -995,11 +1083,9 @@ static void run_layers(orc_model* m, int pos) {
         mm(&l->wv, m->xq, m->xs, m->v);
         orc_apply_rope(m->q, pos, m->heads, m->hd, m->rope_dim, m->base);
         orc_apply_rope(m->k, pos, m->kv_heads, m->hd, m->rope_dim, m->base);
-        size_t lo = (size_t)li * m->ctx * m->kvw;
-        memcpy(m->kc + lo + (size_t)pos * m->kvw, m->k, 4 * (size_t)m->kvw);
-        memcpy(m->vc + lo + (size_t)pos * m->kvw, m->v, 4 * (size_t)m->kvw);
+        kv_store(m, li, pos, m->k, m->v);
         memset(m->att, 0, 4 * (size_t)m->qw);
-        orc_attention(m->att, m->q, m->kc + lo, m->vc + lo, pos, m->heads, m->kv_heads, m->hd, m->kvw);
+        kv_attend(m, li, m->att, m->q, pos);
         orc_quantize_q8_0(m->att, m->qw, m->xq, m->xs);
         mm(&l->wo, m->xq, m->xs, m->hidden);
         for (int i = 0; i < m->emb; ++i) m->hidden[i] += m->residual[i];
@@ -1070,17 +1156,14 @@ void orc_prefill_batch(orc_model* m, const int* tokens, int n, int start_pos, fl
         orc_matmul_quantized_batch(l->wq.type, l->wq.data, l->wq.rows, H, n, xq, xs, q);
         orc_matmul_quantized_batch(l->wk.type, l->wk.data, l->wk.rows, H, n, xq, xs, k);
         orc_matmul_quantized_batch(l->wv.type, l->wv.data, l->wv.rows, H, n, xq, xs, v);
-        size_t lo = (size_t)li * m->ctx * KW;
         for (int t = 0; t < n; ++t) {
             int pos = start_pos + t;
             orc_apply_rope(q + (size_t)t * QW, pos, m->heads, m->hd, m->rope_dim, m->base);
             orc_apply_rope(k + (size_t)t * KW, pos, m->kv_heads, m->hd, m->rope_dim, m->base);
-            memcpy(m->kc + lo + (size_t)pos * KW, k + (size_t)t * KW, 4 * (size_t)KW);
-            memcpy(m->vc + lo + (size_t)pos * KW, v + (size_t)t * KW, 4 * (size_t)KW);
+            kv_store(m, li, pos, k + (size_t)t * KW, v + (size_t)t * KW);
         }
         memset(att, 0, 4 * (size_t)n * QW);
-        for (int t = 0; t < n; ++t)
-            orc_attention(att + (size_t)t * QW, q + (size_t)t * QW, m->kc + lo, m->vc + lo, start_pos + t, m->heads, m->kv_heads, m->hd, KW);
+        for (int t = 0; t < n; ++t) kv_attend(m, li, att + (size_t)t * QW, q + (size_t)t * QW, start_pos + t);
         for (int t = 0; t < n; ++t) orc_quantize_q8_0(att + (size_t)t * QW, QW, xq + (size_t)t * QW, xs + (size_t)t * (QW / 32));
         orc_matmul_quantized_batch(l->wo.type, l->wo.data, H, QW, n, xq, xs, hid);
         for (size_t i = 0; i < (size_t)n * H; ++i) hid[i] += res[i];

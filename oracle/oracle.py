@@ -22,7 +22,7 @@ class SynthSpec(ctypes.Structure):
                 ("vocab", ctypes.c_int32), ("ctx", ctypes.c_int32), ("rope_base", ctypes.c_float),
                 ("eps", ctypes.c_float), ("tied", ctypes.c_int32), ("t_embd", ctypes.c_int32),
                 ("t_attn", ctypes.c_int32), ("t_ffn", ctypes.c_int32), ("t_out", ctypes.c_int32),
-                ("seed", ctypes.c_uint64)]
+                ("seed", ctypes.c_uint64), ("t_down", ctypes.c_int32)]
 
     @classmethod
     def of(cls, spec):
@@ -72,6 +72,7 @@ def lib():
         "orc_model_load": (P, [ctypes.c_char_p, I]),
         "orc_model_create_synthetic": (P, [ctypes.POINTER(SynthSpec), I]),
         "orc_model_fill_kv": (None, [P, I, ctypes.c_uint64]),
+        "orc_model_set_kv_kind": (I, [P, I]),
         "orc_synth_key": (ctypes.c_uint64, [ctypes.c_uint64, ctypes.c_char_p]),
         "orc_synth_tensor": (None, [I, ctypes.c_uint64, L64, L64, L64, L64, L64, P]),
         "orc_generate_batched": (I, [P, P, I, I, I, P, P]),
@@ -138,8 +139,8 @@ def block_dots(qtype, w, rows, cols, xq):
 def synth_tensor(spec, name, qtype, r0, r1, c0, c1, cols):
     """Raw blocks of rows [r0, r1) x columns [c0, c1) of a synthetic tensor (the oracle's
     own generator)."""
-    be = 256 if qtype == 12 else (32 if qtype in (2, 8) else 1)
-    bb = {2: 18, 8: 34, 12: 144, 0: 4, 1: 2}[qtype]
+    be = 256 if qtype in (12, 14) else (32 if qtype in (2, 8) else 1)
+    bb = {2: 18, 8: 34, 12: 144, 14: 210, 0: 4, 1: 2}[qtype]
     out = np.zeros((r1 - r0) * ((c1 - c0) // be) * bb, dtype=np.uint8)
     sp = SynthSpec.of(spec)
     key = lib().orc_synth_key(sp.seed, name.encode())
@@ -186,6 +187,11 @@ class OracleModel:
         lg = np.zeros(self.vocab, dtype=np.float32) if want_last_logits else None
         lib().orc_generate_batched(self.h, ptr(p), len(p), n_gen, chunk, ptr(out), ptr(lg) if want_last_logits else None)
         return [int(v) for v in out[:n_gen]], lg
+
+    def set_kv_cache(self, kind):
+        """inference.rs:512-531: 0 f32, 1 F16 (NANOCAMELID_KV_CACHE_F16), 2 Q8_0
+        (NANOCAMELID_KV_CACHE_Q8); returns the kind in use.  Clears the cache."""
+        return lib().orc_model_set_kv_kind(self.h, kind)
 
     def fill_kv(self, npos, seed=0):
         lib().orc_model_fill_kv(self.h, npos, seed)

@@ -129,7 +129,7 @@ def tiny(ncm, **kw):
     return ncm.spec(d["emb"], d["layers"], d["heads"], d["kv_heads"], d["head_dim"], d["ffn"], vocab=d["vocab"],
                     ctx=d["ctx"], tied=d.get("tied", True), t_embd=d.get("t_embd", ncm.Q4_0),
                     t_attn=d.get("t_attn", ncm.Q4_0), t_ffn=d.get("t_ffn", ncm.Q4_0), t_out=d.get("t_out", ncm.Q4_0),
-                    seed=d.get("seed", 7))
+                    seed=d.get("seed", 7), t_down=d.get("t_down", 0))
 
 
 def test_gguf_writer_blocks_equal_host_generator(ncm, tmp_path):
@@ -154,7 +154,7 @@ def test_gguf_writer_blocks_equal_host_generator(ncm, tmp_path):
         assert part == exp, name
 
 
-@pytest.mark.parametrize("qtype", ["Q4_0", "Q8_0", "Q4_K"])
+@pytest.mark.parametrize("qtype", ["Q4_0", "Q8_0", "Q4_K", "Q6_K"])
 def test_oracle_generator_equals_product_generator(ncm, orc, qtype):
     """The oracle's own restatement of the synthetic-weight generator (used by the CPU
     baseline, which loads no product code) gives the product's bytes, slices included."""
@@ -163,12 +163,13 @@ def test_oracle_generator_equals_product_generator(ncm, orc, qtype):
     for name, rows, cols in [("blk.0.ffn_gate.weight", 5, 512), ("blk.1.ffn_down.weight", 3, 1024)]:
         assert orc.synth_tensor(sp, name, t, 0, rows, 0, cols, cols) == \
             ncm.synth_tensor_bytes(sp, name, t, 0, rows, 0, cols, cols), name
-        e = 256 if t == ncm.Q4_K else 32
+        e = 256 if t in (ncm.Q4_K, ncm.Q6_K) else 32
         assert orc.synth_tensor(sp, name, t, 1, 3, e, 3 * e, cols) == \
             ncm.synth_tensor_bytes(sp, name, t, 1, 3, e, 3 * e, cols), name
 
 
-@pytest.mark.parametrize("kw", [dict(tied=True), dict(tied=False, t_embd=8, t_attn=8, t_ffn=12, t_out=8, ffn=768)])
+@pytest.mark.parametrize("kw", [dict(tied=True), dict(tied=False, t_embd=8, t_attn=8, t_ffn=12, t_out=8, ffn=768),
+                                dict(tied=False, t_embd=8, t_attn=8, t_ffn=12, t_out=14, t_down=14, ffn=768)])
 def test_oracle_synthetic_model_equals_gguf_model(ncm, orc, tmp_path, kw):
     """orc_model_create_synthetic builds in memory exactly the model orc_model_load reads
     from the synthetic GGUF file; the batched prefill decodes like the token-by-token one."""

@@ -19,7 +19,7 @@ def tiny_spec(ncm, **kw):
     return ncm.spec(d["emb"], d["layers"], d["heads"], d["kv_heads"], d["head_dim"], d["ffn"], vocab=d["vocab"],
                     ctx=d["ctx"], tied=d.get("tied", True), t_embd=d.get("t_embd", ncm.Q4_0),
                     t_attn=d.get("t_attn", ncm.Q4_0), t_ffn=d.get("t_ffn", ncm.Q4_0), t_out=d.get("t_out", ncm.Q4_0),
-                    seed=d.get("seed", 7))
+                    seed=d.get("seed", 7), t_down=d.get("t_down", 0))
 
 
 def prompt_ids(n, vocab, seed=0):
@@ -36,6 +36,9 @@ VARIANTS = {
     # widths with an odd number of 32-value blocks (emb 288 = 9 blocks, ffn 800 = 25)
     "q8_0_odd_blocks": dict(tied=False, t_embd=8, t_attn=8, t_ffn=8, t_out=2, heads=9, kv_heads=3,
                             head_dim=32, emb=288, ffn=800),
+    # the Q4_K_M layout: Q6_K output.weight and ffn_down (inference.rs:3045-3087)
+    "q4k_ffn_q6k_head_down": dict(tied=False, t_embd=8, t_attn=8, t_ffn=12, t_out=14, t_down=14, emb=512,
+                                  ffn=1024),
 }
 
 
@@ -57,6 +60,8 @@ def test_greedy_decode_matches_oracle(ncm, orc, cuda, tmp_path, variant):
     t_got, lg_got = m.forward_pass(ref_tokens[-1], pos, want_logits=True)
     assert t_got == t_ref
     assert float(np.max(np.abs(lg_got - lg_ref))) <= 1e-3 * float(np.max(np.abs(lg_ref)))
+    # the strict-order kernels give the oracle's bits
+    assert np.array_equal(lg_got.view(np.uint32), lg_ref.view(np.uint32))
     m.close()
 
 
@@ -116,3 +121,26 @@ def test_config1_full_size_token_parity(ncm, orc, cuda, tmp_path):
     assert got == ref_tokens
     _, lg = m.forward_pass(ref_tokens[-1], 16 + 31, want_logits=True)
     assert float(np.max(np.abs(lg - ref_logits))) <= 1e-3 * float(np.max(np.abs(ref_logits)))
+
+
+@pytest.mark.parametrize("kind", [1, 2])
+def test_greedy_decode_with_f16_q8_kv_cache(ncm, orc, cuda, kind):
+    """The reference's opt-in KV caches (NANOCAMELID_KV_CACHE_F16 / _Q8, inference.rs:505-599,
+    4319-4458) through the whole decode, batched prefill and verify included: tokens and
+    logits equal the oracle's with the same cache, bit for bit."""
+    sp = tiny_spec(ncm, tied=False, heads=8, kv_heads=2, head_dim=64, emb=512, ffn=1024, seed=21)
+    ref = orc.OracleModel(spec=sp)
+    assert ref.set_kv_cache(kind) == kind
+    prompt = prompt_ids(11, sp.vocab, seed=4)
+    n_gen = 16
+    ref_tokens, ref_logits = ref.generate(prompt, n_gen, want_last_logits=True)
+    m = ncm.Model.synthetic(sp, device=0)
+    m.set_kv_cache(kind)
+    got = m.generate(prompt, n_gen)
+    assert got == ref_tokens
+    _, lg = m.forward_pass(got[-1], len(prompt) + n_gen - 1, want_logits=True)
+    assert np.array_equal(lg.view(np.uint32), ref_logits.view(np.uint32))
+    # one multi-row pass over the stored cache: each row's greedy token is the decode's
+    rows = m.verify_batch(got[:4], len(prompt))
+    assert rows == got[1:5]
+    m.close()

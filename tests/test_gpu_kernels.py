@@ -11,8 +11,8 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-BB = {2: 18, 8: 34, 12: 144}
-BE = {2: 32, 8: 32, 12: 256}
+BB = {2: 18, 8: 34, 12: 144, 14: 210}
+BE = {2: 32, 8: 32, 12: 256, 14: 256}
 
 
 def random_blocks(qtype, rows, cols, seed):
@@ -21,8 +21,9 @@ def random_blocks(qtype, rows, cols, seed):
     nb = rows * (cols // BE[qtype])
     raw = rng.integers(0, 256, size=(nb, BB[qtype]), dtype=np.uint8)
     scales = (rng.standard_normal(nb) * 0.01).astype(np.float16).view(np.uint16)
-    raw[:, 0] = scales & 0xFF
-    raw[:, 1] = scales >> 8
+    at = 208 if qtype == 14 else 0   # Q6_K keeps d at the end of its block
+    raw[:, at] = scales & 0xFF
+    raw[:, at + 1] = scales >> 8
     if qtype == 12:
         dmin = (np.abs(rng.standard_normal(nb)) * 0.003).astype(np.float16).view(np.uint16)
         raw[:, 2] = dmin & 0xFF
@@ -73,12 +74,12 @@ SHAPES = [(3, 64), (7, 256), (5, 32), (300, 96), (2049, 160), (64, 2080), (64, 2
           (96, 28672), (1, 8192)]
 
 
-@pytest.mark.parametrize("qtype", [2, 8, 12])
+@pytest.mark.parametrize("qtype", [2, 8, 12, 14])
 @pytest.mark.parametrize("rows,cols", SHAPES)
 def test_matmul_quantized_vs_oracle(ncm, orc, cuda, qtype, rows, cols):
     torch = cuda
     if cols % BE[qtype]:
-        pytest.skip("Q4_K needs 256-aligned columns")
+        pytest.skip("K-quants need 256-aligned columns")
     w = random_blocks(qtype, rows, cols, seed=rows + cols + qtype)
     x = np.random.default_rng(rows).standard_normal(cols).astype(np.float32)
     xq, xs = orc.quantize_q8_0(x)
@@ -266,3 +267,35 @@ def test_attention_bit_exact(ncm, orc, cuda):
         ncm.attention(o.data_ptr(), qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), pos, heads, kvh, hd)
         torch.cuda.synchronize()
         assert np.array_equal(o.cpu().numpy().view(np.uint32), ref.view(np.uint32)), (heads, kvh, hd, pos)
+
+
+@pytest.mark.parametrize("kind", [1, 2])
+def test_attention_f16_q8_cache_bit_exact(ncm, orc, cuda, kind):
+    """apply_attention_head_f16 / _q8_0 (inference.rs:4319-4458) over caches stored the
+    reference's way (truncating f16 per value; Q8_0 blocks with a truncated f16 scale):
+    outputs equal the oracle's bit for bit."""
+    torch = cuda
+    L = orc.lib()
+    rng = np.random.default_rng(31 + kind)
+    for heads, kvh, hd, pos in [(4, 2, 64, 0), (32, 8, 64, 47), (24, 8, 128, 200), (64, 8, 128, 1100)]:
+        kvw = kvh * hd
+        q = rng.standard_normal(heads * hd).astype(np.float32)
+        kf = (rng.standard_normal((pos + 1) * kvw) * 0.3).astype(np.float32)
+        vf = rng.standard_normal((pos + 1) * kvw).astype(np.float32)
+        if kind == 1:
+            kc = np.zeros((pos + 1) * kvw, dtype=np.uint16)
+            vc = np.zeros((pos + 1) * kvw, dtype=np.uint16)
+            L.orc_kv_store_f16(orc.ptr(kf), kf.size, orc.ptr(kc))
+            L.orc_kv_store_f16(orc.ptr(vf), vf.size, orc.ptr(vc))
+        else:
+            kc = np.zeros((pos + 1) * kvw // 32 * 34, dtype=np.uint8)
+            vc = np.zeros((pos + 1) * kvw // 32 * 34, dtype=np.uint8)
+            L.orc_kv_quantize_row_q8_0(orc.ptr(kf), kf.size, orc.ptr(kc))
+            L.orc_kv_quantize_row_q8_0(orc.ptr(vf), vf.size, orc.ptr(vc))
+        ref = np.zeros(heads * hd, dtype=np.float32)
+        L.orc_attention_kv(kind, orc.ptr(ref), orc.ptr(q), orc.ptr(kc), orc.ptr(vc), pos, heads, kvh, hd, kvw)
+        o = torch.zeros(heads * hd, dtype=torch.float32, device="cuda")
+        qd, kd, vd = dev(torch, q), dev(torch, kc), dev(torch, vc)
+        ncm.attention_kv(kind, o.data_ptr(), qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), pos, heads, kvh, hd)
+        torch.cuda.synchronize()
+        assert np.array_equal(o.cpu().numpy().view(np.uint32), ref.view(np.uint32)), (kind, heads, kvh, hd, pos)
