@@ -47,6 +47,8 @@ def parse():
     ap.add_argument("--verify-only", action="store_true",
                     help="config 5 target: time the multi-row verify pass (1/4/5/8 rows) and one graphed step")
     ap.add_argument("--verify-rows", default="1,4,5,8")
+    ap.add_argument("--kernels", action="store_true",
+                    help="per-kernel CUDA-event times of the decode step's GEMVs (one launch per layer in turn)")
     ap.add_argument("--gemv-only", action="store_true",
                     help="only the roofline GEMV (head-shaped Q4_0 matrix): the small case for ncu captures")
     return ap.parse_args()
@@ -229,7 +231,10 @@ def step_kernel_roofline(torch, ncm, m, sp, kind, peak, stream, world=1):
     tn = {2: "Q4_0", 8: "Q8_0", 12: "Q4_K"}
     H, F = sp.emb, sp.ffn // world
     qw, kw = sp.heads * sp.head_dim // world, sp.kv_heads * sp.head_dim // world
-    if kind == ncm.STEP_W13:
+    if kind in (ncm.STEP_WO, ncm.STEP_W2):
+        name, wbytes = "row-parallel", (H * (qw if kind == ncm.STEP_WO else F)) * bpw[sp.t_attn if kind == ncm.STEP_WO else sp.t_ffn]
+        io = 0
+    elif kind == ncm.STEP_W13:
         name, wbytes = f"ncm_qgemv_kernel<{tn[sp.t_ffn]},IN_F32_RMS,EPI_SILU> (ffn_gate+ffn_up {F}x{H} x2)", 2 * F * H * bpw[sp.t_ffn]
         io = H * 4 * 2 + F * 4
     else:
@@ -351,6 +356,32 @@ def run_b200(args, sp):
         nccl = {"value": round(args.steps / (n_ms / 1e3), 2), "unit": "tok/s", "ms_per_step": round(n_ms / args.steps, 4),
                 "reducer": "ncclAllReduce(sum) of the wo/w2 partial rows + residual add, ncclAllGather argmax merge"}
         m.tp_set_reducer(ncm.REDUCE_FUSED_P2P)
+    if args.kernels and world == 1:
+        peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"])
+        import numpy as np
+        out = {}
+        for name, kind in (("qkv", ncm.STEP_QKV), ("wo", ncm.STEP_WO), ("w13", ncm.STEP_W13), ("w2", ncm.STEP_W2)):
+            r = step_kernel_roofline(torch, ncm, m, sp, kind, peak, stream)
+            out[name] = {"us": r["launch_us"], "GBps": r["achieved"], "frac": r["frac"]} if kind in (
+                ncm.STEP_QKV, ncm.STEP_W13) else {"us": r["launch_us"]}
+            # one more launch alone, with its phase stamps (relative to the earliest entry)
+            torch.cuda.synchronize()
+            m.launch_step_kernel(kind, min(1, sp.layers - 1), stream.cuda_stream)
+            torch.cuda.synchronize()
+            ts = m.debug_stamps(16 * 148).reshape(148, 16).astype(np.int64)
+            t0 = ts[:, 0].min()
+            rel = lambda i: ts[:, i] - t0
+            us = lambda a: round(float(a) / 1e3, 2)
+            out[name]["stamps_us"] = {
+                "pdl_max": us(rel(1).max()), "prologue_avg": us((ts[:, 2] - ts[:, 1]).mean()),
+                "prologue_max": us((ts[:, 2] - ts[:, 1]).max()), "last_issue_avg": us(rel(3).mean()),
+                "compute_end_avg": us(rel(11).mean()), "fold_end_avg": us(rel(4).mean()),
+                "fold_end_max": us(rel(4).max()), "exit_max": us(rel(6).max()),
+                "epilogue_avg": us(ts[:, 5].mean()), "c_wait_data_avg": us(ts[:, 7].mean()),
+                "c_wait_slot_avg": us(ts[:, 8].mean()), "f_wait_terms_avg": us(ts[:, 9].mean()),
+                "p_wait_stage_avg": us(ts[:, 10].mean())}
+        print(json.dumps({"kernels": out, "tok_s": round(tok_s, 2), "ms_per_step": round(ms / args.steps, 4),
+                          "env": {k: v for k, v in os.environ.items() if k.startswith("NCM_TUNE")}}), flush=True)
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {"hbm_gbs": 6650.0}
     peak = float(peaks.get("hbm_gbs", 6650.0))

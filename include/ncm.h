@@ -202,6 +202,14 @@ ncm_status ncm_debug_read(ncm_model* m, int which, int layer, float* out, int64_
 enum { NCM_STEP_QKV = 0, NCM_STEP_W13 = 1, NCM_STEP_WO = 2, NCM_STEP_W2 = 3 };
 ncm_status ncm_launch_step_kernel(ncm_model* m, int kind, int layer, void* stream);
 
+/* Measurement seam (no reference counterpart): per-CTA global-timer stamps (ns) of the
+ * GEMV pipeline phases recorded by the last ncm_launch_step_kernel launch: out[16 * cta +
+ * i], i = 0 entry, 1 after the dependent-launch wait, 2 prologue done, 3 last weight load
+ * issued, 4 last fold done, 5 time in tile epilogues, 6 exit, 7 / 8 compute warp 0 time
+ * waiting for weights / for a free term slot, 9 fold time waiting for terms, 10 producer
+ * time waiting for a free stage, 11 compute warp 0 done.  n entries (<= 16 per SM). */
+ncm_status ncm_debug_stamps(ncm_model* m, uint64_t* out, int n);
+
 /* ---------------------------------------------------------------- speculative decoding
  * speculative.rs:381-389 prefill_pass_batch + compute_logits_from_hidden +
  * sample_logits(_, 0.0) per row: tokens[ntok] (1 <= ntok <= 8) at positions

@@ -118,6 +118,7 @@ def lib():
         "ncm_get_hidden": (c_int, [c_p, c_p]),
         "ncm_debug_read": (c_int, [c_p, c_int, c_int, c_p, c_i64]),
         "ncm_launch_step_kernel": (c_int, [c_p, c_int, c_int, c_p]),
+        "ncm_debug_stamps": (c_int, [c_p, c_p, c_int]),
         "ncm_tp_export": (c_int, [c_p, pu8]),
         "ncm_tp_import": (c_int, [c_p, pu8, c_int, c_int]),
         "ncm_nccl_unique_id": (c_int, [pu8]),
@@ -312,6 +313,13 @@ class Model:
     def launch_step_kernel(self, kind, layer, stream=0):
         """One launch of the decode step's GEMV of `kind` (STEP_*) for `layer` (timing)."""
         _ck(lib().ncm_launch_step_kernel(self._h, kind, layer, _stream(stream)))
+
+    def debug_stamps(self, n):
+        """Phase stamps of the last launch_step_kernel (uint64[n]); see include/ncm.h."""
+        import numpy as np
+        out = np.zeros(n, dtype=np.uint64)
+        _ck(lib().ncm_debug_stamps(self._h, out.ctypes.data_as(ctypes.c_void_p), n))
+        return out
 
     def hidden(self):
         import numpy as np

@@ -5,6 +5,7 @@
 #include <dlfcn.h>
 #include <math.h>
 #include <string.h>
+#include <stdlib.h>
 #include <algorithm>
 #include <initializer_list>
 #include <mutex>
@@ -108,7 +109,10 @@ struct ncm_model {
     float *kv_sk = nullptr, *kv_sv = nullptr;   // F16 / Q8_0: staged f32 K / V rows [kMaxBatch][kw]
     int8_t* hx_q = nullptr;       // the normed hidden as Q8_0 for a Q6_K head
     float* hx_s = nullptr;
-    int64_t prefetch_bytes = 320 * 1024;   // per CTA: next kernel's weights streamed into L2
+    int64_t prefetch_bytes = 0;   // per CTA: next kernel's weights streamed into L2 (0: off)
+    int tune = 0;                 // measurement knobs
+    uint64_t* dbg_ts = nullptr;   // measurement probe buffer [num_sms][8], filled by step-kernel seam launches
+    bool dbg_on = false;
     int *state = nullptr, *tokens = nullptr, *err = nullptr;
     int* h_stage = nullptr;   // pinned staging for small transfers
     cudaStream_t ext_stream = nullptr;   // caller stream of the last prefill / decode, until synced
@@ -278,6 +282,7 @@ static ncm_status setup_buffers(ncm_model* m, const int* shares, int nshards, in
     DALLOC(m->att_s, 4 * (qw / 32));
     DALLOC(m->act_q, m->fl);
     DALLOC(m->act_s, 4 * (m->fl / 32));
+    DALLOC(m->dbg_ts, 8 * 16 * (size_t)num_sms());
     DALLOC(m->hx_q, m->emb);
     DALLOC(m->hx_s, 4 * (m->emb / 32));
     DALLOC(m->kc, 4 * (size_t)m->layers * m->ctx * kw);
@@ -342,10 +347,61 @@ static ncm_status check_matrix_shape(const DevMat& d, const char* what) {
     return NCM_OK;
 }
 
+// Shard upload through pinned staging: the mapped file's row slices are packed into one
+// of two pinned buffers while the other one's asynchronous copy to HBM runs, so host
+// reads and PCIe transfers overlap and only this rank's slice is ever touched.
+struct PinnedStager {
+    static constexpr size_t kBytes = 64u << 20;
+    uint8_t* buf[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    int next = 0;
+    cudaStream_t s = nullptr;
+    bool init(cudaStream_t st) {
+        s = st;
+        for (int i = 0; i < 2; ++i) {
+            if (cudaMallocHost((void**)&buf[i], kBytes) != cudaSuccess) return false;
+            if (cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming) != cudaSuccess) return false;
+        }
+        return true;
+    }
+    ~PinnedStager() {
+        if (s) cudaStreamSynchronize(s);
+        for (int i = 0; i < 2; ++i) {
+            if (buf[i]) cudaFreeHost(buf[i]);
+            if (done[i]) cudaEventDestroy(done[i]);
+        }
+    }
+    // rows of rb bytes from src (stride src_pitch) to dst (stride dst_pitch)
+    cudaError_t copy(uint8_t* dst, size_t dst_pitch, const uint8_t* src, size_t src_pitch, size_t rb, size_t rows) {
+        const size_t per = std::max<size_t>(1, kBytes / std::max<size_t>(rb, 1));
+        for (size_t r0 = 0; r0 < rows; r0 += per) {
+            const size_t nr = std::min(per, rows - r0);
+            const int i = next;
+            next ^= 1;
+            cudaError_t e = cudaEventSynchronize(done[i]);   // the buffer's previous copy
+            if (e != cudaSuccess) return e;
+            uint8_t* b = buf[i];
+            if (rb > kBytes) {   // a single row larger than the buffer: plain copy
+                e = cudaMemcpy2D(dst + r0 * dst_pitch, dst_pitch, src + r0 * src_pitch, src_pitch, rb, nr,
+                                 cudaMemcpyHostToDevice);
+                if (e != cudaSuccess) return e;
+                continue;
+            }
+            for (size_t r = 0; r < nr; ++r) memcpy(b + r * rb, src + (r0 + r) * src_pitch, rb);
+            e = cudaMemcpy2DAsync(dst + r0 * dst_pitch, dst_pitch, b, rb, rb, nr, cudaMemcpyHostToDevice, s);
+            if (e != cudaSuccess) return e;
+            e = cudaEventRecord(done[i], s);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
+    }
+};
+
 // Upload rows [r0,r0+nrows) x cols [c0,c0+ncols) of a GGUF tensor (raw blocks unchanged;
 // row pitch rounded up to 16 bytes so every row tile is a legal bulk copy).
 static ncm_status upload_slice(ncm_model* m, const GgufFile& g, const char* name, int expect_rows, int expect_cols,
-                               int r0, int nrows, int c0, int ncols, DevMat& out) {
+                               int r0, int nrows, int c0, int ncols, DevMat& out, PinnedStager* stg = nullptr,
+                               uint8_t* dst = nullptr) {
     const GgufTensor* t = g.find(name);
     if (!t) return fail(NCM_EIO, std::string("missing tensor ") + name);
     if (t->dims.size() != 2 || (int)t->dims[0] != expect_cols || (int)t->dims[1] != expect_rows)
@@ -357,9 +413,11 @@ static ncm_status upload_slice(ncm_model* m, const GgufFile& g, const char* name
     out.pitch = (rb + 15) / 16 * 16;
     const int be = ncm_type_block_elems(t->type);
     if (c0 % be || ncols % be) return fail(NCM_EINVAL, std::string("column slice not block aligned: ") + name);
-    DALLOC(out.d, (size_t)out.pitch * nrows);
+    if (dst) out.d = dst;
+    else DALLOC(out.d, (size_t)out.pitch * nrows);
     const uint8_t* src = g.data(*t) + (size_t)r0 * full_rb + (size_t)(c0 / be) * ncm_type_block_bytes(t->type);
-    CK(cudaMemcpy2D(out.d, out.pitch, src, full_rb, rb, nrows, cudaMemcpyHostToDevice));
+    if (stg) CK(stg->copy(out.d, out.pitch, src, full_rb, rb, nrows));
+    else CK(cudaMemcpy2D(out.d, out.pitch, src, full_rb, rb, nrows, cudaMemcpyHostToDevice));
     return NCM_OK;
 }
 
@@ -465,6 +523,10 @@ static ncm_status check_all_shapes(ncm_model* m) {
     w.row_align = 32;
     const int g = m->fl % 32 == 0 ? gemv_plan(m->L[0].w1.type, m->emb, m->fl, true, IN_F32_RMS, w) : -1;
     m->act_quantised = g > 0 && w.box_rows == 32;
+    // tuning knobs for measurement runs (unset in normal use)
+    if (const char* e = getenv("NCM_TUNE_ACTQ")) m->act_quantised = m->act_quantised && atoi(e) != 0;
+    if (const char* e = getenv("NCM_TUNE_PREFETCH_KB")) m->prefetch_bytes = (int64_t)atoi(e) * 1024;
+    if (const char* e = getenv("NCM_TUNE_BITS")) m->tune = atoi(e);
     return NCM_OK;
 }
 
@@ -496,12 +558,14 @@ extern "C" ncm_status ncm_model_load(const char* path, int ctx_limit, int device
     m->ctx = (ctx_limit > 0 && ctx_limit < g.ctx) ? ctx_limit : g.ctx;
     if (m->emb <= 0 || m->layers <= 0 || m->ctx <= 0) { free_model(m); return fail(NCM_EIO, "incomplete llama metadata"); }
     if ((s = setup_buffers(m, shares, nshards, shard))) { free_model(m); return s; }
+    PinnedStager stg;
+    if (!stg.init(m->stream)) { free_model(m); return fail(NCM_ECUDA, "pinned staging buffers"); }
     const int H = m->emb, QW = m->heads * m->hd, KW = m->kv_heads * m->hd, F = m->ffn;
     const int hd = m->hd;
 #define TRY(x) do { if ((s = (x))) { free_model(m); return s; } } while (0)
-    TRY(upload_slice(m, g, "token_embd.weight", m->vocab, H, 0, m->vocab, 0, H, m->embd));
+    TRY(upload_slice(m, g, "token_embd.weight", m->vocab, H, 0, m->vocab, 0, H, m->embd, &stg));
     TRY(upload_f32(m, g, "output_norm.weight", H, &m->out_norm));
-    if (g.find("output.weight")) TRY(upload_slice(m, g, "output.weight", m->vocab, H, m->h0, m->hr, 0, H, m->head));
+    if (g.find("output.weight")) TRY(upload_slice(m, g, "output.weight", m->vocab, H, m->h0, m->hr, 0, H, m->head, &stg));
     else TRY(build_tied_head(m));
     m->L.resize(m->layers);
     char nm[128];
@@ -510,13 +574,26 @@ extern "C" ncm_status ncm_model_load(const char* path, int ctx_limit, int device
 #define NM(s_) (snprintf(nm, sizeof nm, "blk.%d." s_ ".weight", i), nm)
         TRY(upload_f32(m, g, NM("attn_norm"), H, &l.attn_norm));
         TRY(upload_f32(m, g, NM("ffn_norm"), H, &l.ffn_norm));
-        TRY(upload_slice(m, g, NM("attn_q"), QW, H, m->q0 * hd, m->qh * hd, 0, H, l.wq));
-        TRY(upload_slice(m, g, NM("attn_k"), KW, H, m->k0 * hd, m->kh * hd, 0, H, l.wk));
-        TRY(upload_slice(m, g, NM("attn_v"), KW, H, m->k0 * hd, m->kh * hd, 0, H, l.wv));
-        TRY(upload_slice(m, g, NM("attn_output"), H, QW, 0, H, m->q0 * hd, m->qh * hd, l.wo));
-        TRY(upload_slice(m, g, NM("ffn_gate"), F, H, m->f0, m->fl, 0, H, l.w1));
-        TRY(upload_slice(m, g, NM("ffn_up"), F, H, m->f0, m->fl, 0, H, l.w3));
-        TRY(upload_slice(m, g, NM("ffn_down"), H, F, 0, H, m->f0, m->fl, l.w2));
+        // q, k and v rows back to back in one buffer when they share a type (one tensor map)
+        uint8_t* qkv = nullptr;
+        const GgufTensor *tq = g.find(NM("attn_q")), *tk = g.find(NM("attn_k")), *tv = g.find(NM("attn_v"));
+        if (tq && tk && tv && tq->type == tk->type && tq->type == tv->type && ncm_type_block_bytes(tq->type) > 0) {
+            const size_t pitch = (row_bytes(tq->type, H) + 15) / 16 * 16;
+            TRY(dalloc(m, (void**)&qkv, pitch * (size_t)(m->qh + 2 * m->kh) * hd));
+            TRY(upload_slice(m, g, NM("attn_q"), QW, H, m->q0 * hd, m->qh * hd, 0, H, l.wq, &stg, qkv));
+            TRY(upload_slice(m, g, NM("attn_k"), KW, H, m->k0 * hd, m->kh * hd, 0, H, l.wk, &stg,
+                             qkv + pitch * m->qh * hd));
+            TRY(upload_slice(m, g, NM("attn_v"), KW, H, m->k0 * hd, m->kh * hd, 0, H, l.wv, &stg,
+                             qkv + pitch * (m->qh + m->kh) * hd));
+        } else {
+            TRY(upload_slice(m, g, NM("attn_q"), QW, H, m->q0 * hd, m->qh * hd, 0, H, l.wq, &stg));
+            TRY(upload_slice(m, g, NM("attn_k"), KW, H, m->k0 * hd, m->kh * hd, 0, H, l.wk, &stg));
+            TRY(upload_slice(m, g, NM("attn_v"), KW, H, m->k0 * hd, m->kh * hd, 0, H, l.wv, &stg));
+        }
+        TRY(upload_slice(m, g, NM("attn_output"), H, QW, 0, H, m->q0 * hd, m->qh * hd, l.wo, &stg));
+        TRY(upload_slice(m, g, NM("ffn_gate"), F, H, m->f0, m->fl, 0, H, l.w1, &stg));
+        TRY(upload_slice(m, g, NM("ffn_up"), F, H, m->f0, m->fl, 0, H, l.w3, &stg));
+        TRY(upload_slice(m, g, NM("ffn_down"), H, F, 0, H, m->f0, m->fl, l.w2, &stg));
 #undef NM
     }
     TRY(check_all_shapes(m));
@@ -526,12 +603,13 @@ extern "C" ncm_status ncm_model_load(const char* path, int ctx_limit, int device
 }
 
 static ncm_status synth_mat(ncm_model* m, const ncm_synth_spec& sp, const char* name, int type, int full_cols,
-                            int r0, int nrows, int c0, int ncols, DevMat& out) {
+                            int r0, int nrows, int c0, int ncols, DevMat& out, uint8_t* dst = nullptr) {
     out.type = type;
     out.rows = nrows;
     out.cols = ncols;
     out.pitch = (row_bytes(type, ncols) + 15) / 16 * 16;
-    DALLOC(out.d, (size_t)out.pitch * nrows);
+    if (dst) out.d = dst;
+    else DALLOC(out.d, (size_t)out.pitch * nrows);
     CKL(synth_launch(type, ncm_synth_key(sp.seed, name), r0, nrows, c0, ncols, full_cols, out.d, out.pitch, m->stream));
     return NCM_OK;
 }
@@ -569,9 +647,15 @@ extern "C" ncm_status ncm_model_create_synthetic(const ncm_synth_spec* spec, int
 #define NM(s_) (snprintf(nm, sizeof nm, "blk.%d." s_ ".weight", i), nm)
         TRY(ones(m, H, &l.attn_norm));
         TRY(ones(m, H, &l.ffn_norm));
-        TRY(synth_mat(m, sp, NM("attn_q"), sp.t_attn, H, m->q0 * hd, m->qh * hd, 0, H, l.wq));
-        TRY(synth_mat(m, sp, NM("attn_k"), sp.t_attn, H, m->k0 * hd, m->kh * hd, 0, H, l.wk));
-        TRY(synth_mat(m, sp, NM("attn_v"), sp.t_attn, H, m->k0 * hd, m->kh * hd, 0, H, l.wv));
+        // q, k and v rows back to back in one buffer (one tensor map for the fused GEMV)
+        uint8_t* qkv = nullptr;
+        const size_t qkv_pitch = (row_bytes(sp.t_attn, H) + 15) / 16 * 16;
+        TRY(dalloc(m, (void**)&qkv, qkv_pitch * (size_t)(m->qh + 2 * m->kh) * hd));
+        TRY(synth_mat(m, sp, NM("attn_q"), sp.t_attn, H, m->q0 * hd, m->qh * hd, 0, H, l.wq, qkv));
+        TRY(synth_mat(m, sp, NM("attn_k"), sp.t_attn, H, m->k0 * hd, m->kh * hd, 0, H, l.wk,
+                      qkv + qkv_pitch * m->qh * hd));
+        TRY(synth_mat(m, sp, NM("attn_v"), sp.t_attn, H, m->k0 * hd, m->kh * hd, 0, H, l.wv,
+                      qkv + qkv_pitch * (m->qh + m->kh) * hd));
         TRY(synth_mat(m, sp, NM("attn_output"), sp.t_attn, QW, 0, H, m->q0 * hd, m->qh * hd, l.wo));
         TRY(synth_mat(m, sp, NM("ffn_gate"), sp.t_ffn, H, m->f0, m->fl, 0, H, l.w1));
         TRY(synth_mat(m, sp, NM("ffn_up"), sp.t_ffn, H, m->f0, m->fl, 0, H, l.w3));
@@ -639,6 +723,8 @@ static GemvParams base_params(ncm_model* m) {
     p.tp.world = 1;
     p.tp.timeout_ns = m->timeout_ns;
     p.row_align = 2;
+    p.tune = m->tune;
+    p.dbg_ts = m->dbg_on ? m->dbg_ts : nullptr;
     return p;
 }
 
@@ -802,7 +888,17 @@ static int launch_qkv(ncm_model* m, int l, cudaStream_t s) {
     }
     if (l == 0) p.ssq_tok = m->embd_ssq;
     copy_pf(p, pf_of(m, {&L.wo}, false));
-    int r = launch_gemv({&L.wq, &L.wk, &L.wv}, nullptr, IN_F32_RMS, EPI_QKV, p, s);
+    int r;
+    if (L.wk.d == L.wq.d + (size_t)L.wq.pitch * L.wq.rows && L.wv.d == L.wk.d + (size_t)L.wk.pitch * L.wk.rows &&
+        L.wq.pitch == L.wk.pitch && L.wq.pitch == L.wv.pitch) {
+        // one buffer: one tensor map, tiles across the q / k / v boundaries
+        DevMat all = L.wq;
+        all.rows = qw + 2 * kw;
+        p.fused = 1;
+        r = launch_gemv({&all}, nullptr, IN_F32_RMS, EPI_QKV, p, s);
+    } else {
+        r = launch_gemv({&L.wq, &L.wk, &L.wv}, nullptr, IN_F32_RMS, EPI_QKV, p, s);
+    }
     if (!r && m->kv_kind != KV_F32)
         r = kv_store_launch(m->kv_kind, m->kv_sk, m->kv_sv, 1, kw, kv_layer(m, m->kc, l), kv_layer(m, m->vc, l),
                             m->state + ST_POS, s, true);
@@ -1109,6 +1205,11 @@ extern "C" ncm_status ncm_launch_step_kernel(ncm_model* m, int kind, int layer, 
     if (!m || layer < 0 || layer >= m->layers) return fail(NCM_EINVAL, "bad layer");
     CK(cudaSetDevice(m->device));
     cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+    struct Probe {   // the phase stamps are recorded by these seam launches only
+        ncm_model* m;
+        Probe(ncm_model* mm) : m(mm) { m->dbg_on = true; }
+        ~Probe() { m->dbg_on = false; }
+    } probe(m);
     switch (kind) {
         case NCM_STEP_QKV: CKL(launch_qkv(m, layer, s)); return NCM_OK;
         case NCM_STEP_W13: CKL(launch_w13(m, layer, s)); return NCM_OK;
@@ -1121,6 +1222,16 @@ extern "C" ncm_status ncm_launch_step_kernel(ncm_model* m, int kind, int layer, 
                                     : row_parallel(m, m->L[layer].w2, m->act, nullptr, nullptr, 0, nullptr, s);
         default: return fail(NCM_EINVAL, "unknown step kernel");
     }
+}
+
+// Measurement seam: the phase stamps (global-timer ns) the last ncm_launch_step_kernel
+// launch recorded, [CTA][16] as the GEMV kernel documents them; n = entries to copy.
+extern "C" ncm_status ncm_debug_stamps(ncm_model* m, uint64_t* out, int n) {
+    if (!m || !out || n < 0 || n > 16 * num_sms()) return fail(NCM_EINVAL, "bad arguments");
+    CK(cudaSetDevice(m->device));
+    CK(cudaDeviceSynchronize());
+    CK(cudaMemcpy(out, m->dbg_ts, 8 * (size_t)n, cudaMemcpyDeviceToHost));
+    return NCM_OK;
 }
 
 // ------------------------------------------------------------------ multi-row verify

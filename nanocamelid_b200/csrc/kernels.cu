@@ -656,7 +656,19 @@ __device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, GemvSeqScratch
                 tot = p.ssq_tok[p.tokens[p.state[ST_POS]]];
             } else {
                 // inference.rs:698-701: sum += val * val, sequential.
-                tot = seq_sum_nonneg<kGemvThreads>([&](int i) { float v = xf[i]; return v * v; }, p.cols, sc, tid);
+                if (p.tune & 1) {
+                    // measurement knob: an unordered tree sum (wrong last bits) to time the exact sum
+                    float part = 0.0f;
+                    for (int i = tid; i < p.cols; i += blockDim.x) part += xf[i] * xf[i];
+                    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(NCM_FULL, part, o);
+                    if ((tid & 31) == 0) sc.wsum[tid >> 5] = part;
+                    __syncthreads();
+                    tot = 0.0f;
+                    for (int w = 0; w < kGemvThreads / 32; ++w) tot += sc.wsum[w];
+                    __syncthreads();
+                } else {
+                    tot = seq_sum_nonneg<kGemvThreads>([&](int i) { float v = xf[i]; return v * v; }, p.cols, sc, tid);
+                }
             }
             scale = 1.0f / sqrtf(tot / (float)p.cols + p.eps);
         }
@@ -666,7 +678,7 @@ __device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, GemvSeqScratch
         // every element is rounded exactly as in the one-thread quantiser.
         const int li = tid & 3;
         const unsigned qmask = 0xFu << (tid & 28);
-        for (int b = tid >> 2; b < nblk; b += blockDim.x >> 2) {
+        for (int b = tid >> 2; b < ((p.tune & 2) ? 0 : nblk); b += blockDim.x >> 2) {
             uint32_t* dst = reinterpret_cast<uint32_t*>(smem + p.xq_off + 80 * (b >> 1) + 32 * (b & 1));
             const int c = (li + b) & 3;
             if (b < p.nb) {
@@ -730,11 +742,19 @@ __device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, GemvSeqScratch
 struct TileCursor {
     int seg, n;
 };
-__device__ __forceinline__ TileCursor tile_at(const GemvParams& p, int cur, int r_end) {
+// With p.fused the segments' matrices lie back to back in one buffer under one tensor
+// map (tm[0]): tiles run across segment boundaries and each row finds its segment in the
+// epilogue.  Otherwise a tile stays inside one segment (its own tensor map).
+__device__ __forceinline__ int seg_of(const GemvParams& p, int row) {
     int s = 0;
 #pragma unroll
     for (int i = 1; i < kMaxSeg; ++i)
-        if (i < p.nseg && cur >= p.seg[i].row_begin) s = i;
+        if (i < p.nseg && row >= p.seg[i].row_begin) s = i;
+    return s;
+}
+__device__ __forceinline__ TileCursor tile_at(const GemvParams& p, int cur, int r_end) {
+    if (p.fused) return {0, min(p.box_rows, r_end - cur)};
+    const int s = seg_of(p, cur);
     const int seg_end = p.seg[s].row_begin + p.seg[s].rows;
     const int n = min(p.box_rows, min(r_end, seg_end) - cur);
     return {s, n};
@@ -790,9 +810,17 @@ __device__ void prefetch_next_weights(const GemvParams& p) {
 //   full[s]   (TMA -> compute)            empty[s]  (compute -> producer: stage s reusable)
 //   tfull[s]  (compute -> fold: terms of stage s written)
 //   tempty[s] (fold -> compute: term slot s folded)
-// All eight compute warps work on every stage (each takes a quarter of its row groups
-// for each of the eight 64-column units), so a stage is turned around in a few hundred
-// cycles and the ring keeps its stages in flight on the TMA side.
+// All eight compute warps work on every stage (warp w takes the row groups 4w .. 4w+3
+// and 32 + 4w .. 32 + 4w+3 of each of the eight 64-column units), so a stage is turned
+// around in a few hundred cycles and the ring keeps its stages in flight on the TMA side.
+
+// Measurement probe: when p.dbg_ts is set, per-CTA global-timer stamps (ns) of the
+// pipeline's phases: [0] entry, [1] after the PDL wait, [2] prologue done, [3] last TMA
+// issued, [4] last fold done, [5] fold-thread time in tile epilogues, [6] exit,
+// [7] compute warp 0: waiting for stage data, [8] waiting for a free term slot,
+// [9] fold warp 0: waiting for terms, [10] producer: waiting for a free stage,
+// [11] compute warp 0: end of its loop.
+#define NCM_TS(i, v) do { if (p.dbg_ts) p.dbg_ts[(size_t)blockIdx.x * 16 + (i)] = (v); } while (0)
 
 template <int QT, int IN, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid_constant__ GemvParams p) {
@@ -835,10 +863,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
     // (1) producer: first stages before the PDL wait (weights are constant).
     int icur = r_begin, ichunk = 0, tprod = 0;
     uint64_t pol = 0;
+    uint64_t tpw = 0;
     auto issue = [&]() {
         const int s = tprod % ns;
+        const uint64_t tp0 = p.dbg_ts ? global_timer_ns() : 0;
         if (tprod >= ns && !mbar_wait(&empty[s], (uint32_t)(((tprod / ns) & 1) ^ 1), limit_ns))
             set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+        if (p.dbg_ts) tpw += global_timer_ns() - tp0;
         TileCursor tc = tile_at(p, icur, r_end);
         const int y = icur - p.seg[tc.seg].row_begin;
         const int x = ichunk * p.chunk_words;
@@ -856,15 +887,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
         // norm weights are constant: stage them before waiting for the previous kernel
         stage_f32(reinterpret_cast<float*>(smem + p.nw_off), p.norm_w, p.cols, tid, blockDim.x);
     }
+    if (tid == 0 && p.dbg_ts) NCM_TS(0, global_timer_ns());
     pdl_launch_dependents();
     pdl_wait();
+    if (tid == 0 && p.dbg_ts) NCM_TS(1, global_timer_ns());
 
     // (2) activation -> shared memory (all threads).
     gemv_prologue<IN>(smem, p, sc);
     __syncthreads();
+    if (tid == 0 && p.dbg_ts) NCM_TS(2, global_timer_ns());
 
     if (tid == kProducer) {
         while (icur < r_end) issue();
+        if (p.dbg_ts) { NCM_TS(3, global_timer_ns()); NCM_TS(10, tpw); }
         // Every load of this CTA is issued: HBM would idle through this kernel's tail, the
         // kernel boundary and the next kernel's prologue, so stream the start of the next
         // kernel's weights into L2 now (its first tiles then come from L2).
@@ -874,34 +909,40 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
         // group v0 = lane >> 3); warp w takes the virtual rows v0 + 4 w + 32 j.
         const int w = tid >> 5, u = lane & 7, v0 = lane >> 3;
         int t = 0;
+        uint64_t twait = 0, tslot = 0;
         for (int cur = r_begin; cur < r_end;) {
             const int n = tile_at(p, cur, r_end).n;
             const int vrows = DUAL ? 2 * p.box_rows : n;
             for (int c = 0; c < p.nchunk; ++c, ++t) {
                 const int s = t % ns;
                 const uint32_t use = (uint32_t)(t / ns);
+                const uint64_t tw0 = (p.dbg_ts && tid == 0) ? global_timer_ns() : 0;
                 if (!mbar_wait(&full[s], use & 1, limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+                if (p.dbg_ts && tid == 0) twait += global_timer_ns() - tw0;
+                const uint64_t tw1 = (p.dbg_ts && tid == 0) ? global_timer_ns() : 0;
                 if (use > 0 && !mbar_wait(&tempty[s], (use - 1) & 1, limit_ns))
                     set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+                if (p.dbg_ts && tid == 0) tslot += global_timer_ns() - tw1;
                 const uint8_t* sb = stages + (size_t)s * p.stage_bytes;
                 float* T = tbuf + s * (kMaxFold * kTStride);
                 XUnit x;
                 load_xunit(smem, p, c * kUnits + u, x);
-                const uint8_t* rp[2];
-                bool ok[2];
-                int vr[2];
+                constexpr int NJ = 512 / kComputeThreads;   // rows per lane: 64 rows x 8 units per stage
+                const uint8_t* rp[NJ];
+                bool ok[NJ];
+                int vr[NJ];
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    vr[j] = v0 + 4 * w + 32 * j;
+                for (int j = 0; j < NJ; ++j) {
+                    vr[j] = v0 + 4 * w + (kComputeThreads / 8) * j;
                     const int mat = DUAL ? (vr[j] >= p.box_rows) : 0;
                     const int r = vr[j] - mat * p.box_rows;
                     ok[j] = vr[j] < vrows && r < n;
                     rp[j] = sb + mat * box2_off + (ok[j] ? r : 0) * p.chunk_bytes;
                 }
-                float t0[2], t1[2];
-                unit_terms_n<QT, 2>(rp, u, x, t0, t1);
+                float t0[NJ], t1[NJ];
+                unit_terms_n<QT, NJ>(rp, u, x, t0, t1);
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
+                for (int j = 0; j < NJ; ++j) {
                     if (ok[j]) {
                         float* trow = T + vr[j] * kTStride;
                         trow[2 * u] = t0[j];
@@ -916,6 +957,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
             }
             cur += n;
         }
+        if (tid == 0 && p.dbg_ts) { NCM_TS(7, twait); NCM_TS(8, tslot); NCM_TS(11, global_timer_ns()); }
     } else if (tid < kProducer) {
         // (3b) fold warps: sequential per-row sums in block order, then the epilogue.
         const int f = tid - kFoldBase;
@@ -925,6 +967,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
         int best_i = 0x7fffffff;
         const int nsb = p.nb / 8;
         int t = 0;
+        uint64_t tepi = 0, tfw = 0;
         for (int cur = r_begin; cur < r_end;) {
             const TileCursor tc = tile_at(p, cur, r_end);
             const int n = tc.n;
@@ -934,7 +977,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
             for (int c = 0; c < p.nchunk; ++c, ++t) {
                 const int s = t % ns;
                 const uint32_t use = (uint32_t)(t / ns);
+                const uint64_t tf0 = (p.dbg_ts && f == 0) ? global_timer_ns() : 0;
                 if (!mbar_wait(&tfull[s], use & 1, limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+                if (p.dbg_ts && f == 0) tfw += global_timer_ns() - tf0;
                 if (live) {
                     // all 16 terms into registers first, then the in-order adds
                     const float* trow = trow0 + s * (kMaxFold * kTStride);
@@ -969,13 +1014,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
                 if (lane == 0) mbar_arrive(&tempty[s]);
             }
 
+            const uint64_t te0 = (p.dbg_ts && f == 0) ? global_timer_ns() : 0;
             // tile epilogue (rows cur .. cur+n-1 of segment tc.seg)
             const Seg& sg = p.seg[tc.seg];
             const int lrow0 = cur - sg.row_begin;
             if constexpr (EPI == EPI_QKV) {
                 const float other = __shfl_xor_sync(NCM_FULL, acc, 1);
                 if (f < n) {
-                    const int lr = lrow0 + f;
+                    // the row's own segment (tiles of a fused q/k/v buffer span segments)
+                    const Seg& sg = p.seg[p.fused ? seg_of(p, cur + f) : tc.seg];
+                    const int lr = cur + f - sg.row_begin;
                     float v = acc;
                     if (sg.kind != SEG_V) {
                         // inference.rs:904-933 apply_rope_cached, NORM pairs (2i, 2i+1).
@@ -1036,8 +1084,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
                     }
                 }
             }
+            if (p.dbg_ts && f == 0) tepi += global_timer_ns() - te0;
             cur += n;
         }
+        if (p.dbg_ts && f == 0) { NCM_TS(4, global_timer_ns()); NCM_TS(5, tepi); NCM_TS(9, tfw); }
         if constexpr (EPI == EPI_ARGMAX) {
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
@@ -1131,6 +1181,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
             p.hidden[r] += s;
         }
     }
+    if (tid == 0 && p.dbg_ts) NCM_TS(6, global_timer_ns());
 }
 
 // ------------------------------------------------------------------ GEMV planning / launch

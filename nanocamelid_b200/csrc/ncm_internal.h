@@ -57,6 +57,7 @@ struct alignas(64) GemvParams {
     CUtensorMap tm2;              // EPI_SILU: the up matrix (same shape as tm[0])
     Seg seg[kMaxSeg];
     int nseg;
+    int fused;                    // 1: the segments' matrices are one buffer under tm[0]
     int total_rows;
     int cols, nb, nchunk;         // columns, 32-column blocks per row, 512-column chunks per row
     int chunk_words, chunk_bytes; // TMA box inner extent per row
@@ -89,6 +90,8 @@ struct alignas(64) GemvParams {
     int kv_stage;                 // 1: K / V rows go to kcache / vcache as given (staging for an
                                   //    F16 / Q8_0 cache), 0: the f32 cache rows at pos
     int row_align;                // CTA row ranges start at multiples of this (2, or 32 with qout)
+    int tune;                     // measurement knobs (0 in normal use)
+    uint64_t* dbg_ts;             // measurement probe: per-CTA phase stamps [grid][8] (null in normal use)
     int8_t* qout;                 // EPI_SILU: the output rows also as Q8_0 blocks (box_rows == 32) ...
     float* qout_s;                //   ... and their scales: the next projection's quantised input
     // L2 prefetch of the next kernel's weights once this CTA has issued its own loads:
