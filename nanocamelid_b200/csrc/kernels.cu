@@ -225,8 +225,27 @@ __device__ __forceinline__ T warp_incl_scan(T v, int lane) {
     return v;
 }
 
+// Barrier among the NT threads that take part: the whole CTA (BAR == 0) or named
+// barrier BAR with NT threads (a CTA whose other warps run on).
+template <int NT, int BAR>
+__device__ __forceinline__ void group_sync() {
+    if constexpr (BAR == 0) __syncthreads();
+    else asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
+}
+template <int NT, int BAR>
+__device__ __forceinline__ int group_sync_or(int pred) {
+    if constexpr (BAR == 0) {
+        return __syncthreads_or(pred);
+    } else {
+        int r;
+        asm volatile("{ .reg .pred p, q; setp.ne.s32 p, %1, 0; bar.red.or.pred q, %2, %3, p; selp.s32 %0, 1, 0, q; }"
+                     : "=r"(r) : "r"(pred), "n"(BAR), "n"(NT) : "memory");
+        return r;
+    }
+}
+
 // One segment (at most KM * NT terms) continuing from the exact value carry.
-template <int NT, int KM, class Term>
+template <int NT, int KM, int BAR = 0, class Term>
 __device__ float seq_sum_segment(const Term& term, int seg0, int segn, float carry, SeqSumScratchT<NT>& sc,
                                  int rank) {
     constexpr int kList = SeqSumScratchT<NT>::kList;
@@ -247,7 +266,7 @@ __device__ float seq_sum_segment(const Term& term, int seg0, int segn, float car
     float base = 0.0f;
     if (NT > 32) {
         if (member && lane == 31) sc.wsum[warp] = incl;
-        __syncthreads();
+        group_sync<NT, BAR>();
         if (member)
             for (int w = 0; w < warp; ++w) base += sc.wsum[w];
     }
@@ -296,7 +315,7 @@ __device__ float seq_sum_segment(const Term& term, int seg0, int segn, float car
     uint32_t cb = 0, ub = 0;
     if (NT > 32) {
         if (member && lane == 31) { sc.wcnt[warp] = ci; sc.wunc[warp] = ui; }
-        __syncthreads();
+        group_sync<NT, BAR>();
         if (member)
             for (int w = 0; w < warp; ++w) { cb += sc.wcnt[w]; ub += sc.wunc[w]; }
     }
@@ -310,7 +329,7 @@ __device__ float seq_sum_segment(const Term& term, int seg0, int segn, float car
             cr += c[q];
         }
     }
-    if (NT > 32) ovf = __syncthreads_or(ovf); else ovf = __any_sync(NCM_FULL, ovf);
+    if (NT > 32) ovf = group_sync_or<NT, BAR>(ovf); else ovf = __any_sync(NCM_FULL, ovf);
     // (4) the walk, by warp 0 in lockstep
     if (rank < 32) {
         float x = carry;
@@ -343,7 +362,7 @@ __device__ float seq_sum_segment(const Term& term, int seg0, int segn, float car
         }
         if (rank == 0) sc.result = x;
     }
-    if (NT == 32) __syncwarp(); else __syncthreads();
+    if (NT == 32) __syncwarp(); else group_sync<NT, BAR>();
     return sc.result;
 }
 
@@ -351,7 +370,7 @@ __device__ float seq_sum_segment(const Term& term, int seg0, int segn, float car
 // index among them; the terms are read through term(i).  All NT threads get the result;
 // with NT > 32 every thread of the CTA must call (threads beyond NT only take part in
 // the barriers).
-template <int NT, class Term>
+template <int NT, int BAR = 0, class Term>
 __device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT>& sc, int rank) {
     if (n <= 0) return 0.0f;
     if (NT == 32 && n <= kSeqSerial) {
@@ -359,12 +378,12 @@ __device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT>& sc,
         for (int i = 0; i < n; i += 32) x = seq_fold<32>(term, i, min(32, n - i), x);
         return x;
     }
-    if (n <= 9 * NT) return seq_sum_segment<NT, 9>(term, 0, n, 0.0f, sc, rank);
-    if (n <= 13 * NT) return seq_sum_segment<NT, 13>(term, 0, n, 0.0f, sc, rank);
-    if (n <= 17 * NT) return seq_sum_segment<NT, 17>(term, 0, n, 0.0f, sc, rank);
+    if (n <= 9 * NT) return seq_sum_segment<NT, 9, BAR>(term, 0, n, 0.0f, sc, rank);
+    if (n <= 13 * NT) return seq_sum_segment<NT, 13, BAR>(term, 0, n, 0.0f, sc, rank);
+    if (n <= 17 * NT) return seq_sum_segment<NT, 17, BAR>(term, 0, n, 0.0f, sc, rank);
     float x = 0.0f;
     for (int seg0 = 0; seg0 < n; seg0 += 33 * NT)
-        x = seq_sum_segment<NT, 33>(term, seg0, min(n - seg0, 33 * NT), x, sc, rank);
+        x = seq_sum_segment<NT, 33, BAR>(term, seg0, min(n - seg0, 33 * NT), x, sc, rank);
     return x;
 }
 
@@ -1371,44 +1390,46 @@ __device__ void attn_scores_q8(const AttnParams& a, const float* qsrc, float* sc
 // sequential sum over head_dim (inference.rs:3570-3573, 4256); grid (kv head, 32
 // positions), warp = query head of the group, lane = position.  The K tile is loaded
 // with all its loads in flight at once, then transposed into a padded shared array.
-__global__ void __launch_bounds__(256) attn_scores_kernel(const __grid_constant__ AttnParams a) {
-    __shared__ __align__(16) float qs[8 * 256];
-    __shared__ float ks[32 * 257];
-    pdl_launch_dependents();
-    pdl_wait();
-    const int tz = blockIdx.z;
-    const int pos = (a.pos_override >= 0 ? a.pos_override : a.state[ST_POS]) + tz;
+// One (kv head, 32-position tile, row) item by 256 threads (BAR: 0 = the whole CTA, else
+// the named barrier of the 256 threads); qs / ks are the shared tiles (8 x 256 and
+// 32 x 257 floats).  Activations written by other CTAs of the same launch are read
+// through L2 (ld.global.cg).
+template <int BAR>
+__device__ void attn_scores_body(const AttnParams& a, int kvh, int ty, int tz, float* qs, float* ks) {
+    const int pos = (a.pos_override >= 0 ? a.pos_override : __ldcg(&a.state[ST_POS])) + tz;
     const int n = pos + 1;
-    const int p0 = blockIdx.y * 32;
+    const int p0 = ty * 32;
     if (p0 >= n) return;
-    const int kvh = blockIdx.x, g = a.heads / a.kv_heads, hd = a.hd;
+    const int g = a.heads / a.kv_heads, hd = a.hd;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int np = min(32, n - p0);
     const float* qsrc = a.q + (size_t)tz * a.tok_stride + (size_t)kvh * g * hd;
     float* scores = a.scores + (size_t)tz * a.heads * a.ctx;
     const float* ksrc = a.kc + (size_t)p0 * a.kvw + (size_t)kvh * hd;
-    if (a.kv_kind == KV_Q8_0) {
-        attn_scores_q8(a, qsrc, scores, kvh, g, p0, np, qs, ks);
-        return;
+    if constexpr (BAR == 0) {
+        if (a.kv_kind == KV_Q8_0) {
+            attn_scores_q8(a, qsrc, scores, kvh, g, p0, np, qs, ks);
+            return;
+        }
     }
     if (a.kv_kind == KV_F16) {
         // decode_f16_head (inference.rs:4453-4458): exact f16 -> f32, then the f32 path
         const uint16_t* k16 = reinterpret_cast<const uint16_t*>(a.kc_raw) + (size_t)p0 * a.kvw + (size_t)kvh * hd;
-        for (int i = tid; i < g * hd; i += 256) qs[i] = qsrc[i];
+        for (int i = tid; i < g * hd; i += 256) qs[i] = __ldcg(&qsrc[i]);
         for (int i = tid; i < np * hd; i += 256)
-            ks[(i / hd) * (hd + 1) + i % hd] = f16_bits_to_f32(k16[(size_t)(i / hd) * a.kvw + i % hd]);
+            ks[(i / hd) * (hd + 1) + i % hd] = f16_bits_to_f32(__ldcg(&k16[(size_t)(i / hd) * a.kvw + i % hd]));
     } else if (attn_vec_ok(a)) {
         const int per = hd >> 2;                 // float4 per row
         float4 qv[2], kv[8];
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
             const int i = tid + 256 * k;
-            if (i < g * per) qv[k] = reinterpret_cast<const float4*>(qsrc)[i];
+            if (i < g * per) qv[k] = __ldcg(reinterpret_cast<const float4*>(qsrc) + i);
         }
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
             const int i = tid + 256 * k;
-            if (i < np * per) kv[k] = *reinterpret_cast<const float4*>(ksrc + (size_t)(i / per) * a.kvw + 4 * (i % per));
+            if (i < np * per) kv[k] = __ldcg(reinterpret_cast<const float4*>(ksrc + (size_t)(i / per) * a.kvw + 4 * (i % per)));
         }
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
@@ -1424,10 +1445,11 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const __grid_constant_
             }
         }
     } else {
-        for (int i = tid; i < g * hd; i += 256) qs[i] = qsrc[i];
-        for (int i = tid; i < np * hd; i += 256) ks[(i / hd) * (hd + 1) + i % hd] = ksrc[(size_t)(i / hd) * a.kvw + i % hd];
+        for (int i = tid; i < g * hd; i += 256) qs[i] = __ldcg(&qsrc[i]);
+        for (int i = tid; i < np * hd; i += 256)
+            ks[(i / hd) * (hd + 1) + i % hd] = __ldcg(&ksrc[(size_t)(i / hd) * a.kvw + i % hd]);
     }
-    __syncthreads();
+    group_sync<256, BAR>();
     for (int h = warp; h < g; h += 8) {
         if (lane < np) {
             const float* q = qs + h * hd;
@@ -1440,103 +1462,144 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const __grid_constant_
     }
 }
 
-// Stage 2 (attn_softmax_v_kernel): grid (kv head, dim split).  softmax
-// (inference.rs:3522-3540: max, exp(x - max), sequential sum, *= 1/sum) per query head
-// by one warp each, then out[d] = sum_p w_p * v_p[d] sequential over p per (head, dim)
-// (attn_output zeroed, add_weighted_f32_scalar inference.rs:3619-3623).  The CTA's V
-// columns are copied into shared memory by cp.async, the first chunk while the softmax
-// runs.
-__global__ void __launch_bounds__(256) attn_softmax_v_kernel(const __grid_constant__ AttnParams a) {
-    extern __shared__ __align__(16) float sm[];   // w[g][n] softmax weights, then V chunk
-    __shared__ SeqSumScratchW scr[8];
+__global__ void __launch_bounds__(256) attn_scores_kernel(const __grid_constant__ AttnParams a) {
+    __shared__ __align__(16) float qs[8 * 256];
+    __shared__ float ks[32 * 257];
     pdl_launch_dependents();
     pdl_wait();
-    const int tz = blockIdx.z;
-    const int pos = (a.pos_override >= 0 ? a.pos_override : a.state[ST_POS]) + tz;
+    attn_scores_body<0>(a, blockIdx.x, blockIdx.y, blockIdx.z, qs, ks);
+}
+
+// Stage 2 (attn_softmax_kernel): one CTA of 256 threads per (query head, row).  softmax
+// (inference.rs:3522-3540): max (order free), e_p = exp(s_p - max), the sequential sum of
+// the e_p (seq_sum_nonneg, exact), inv = 1 / sum, w_p = e_p * inv; the weights overwrite
+// the scores in place.  e is a shared buffer of at least pos + 1 floats, red 8 floats.
+template <int BAR>
+__device__ void attn_softmax_body(const AttnParams& a, int h, int tz, float* e, SeqSumScratch& sc, float* red) {
+    const int pos = (a.pos_override >= 0 ? a.pos_override : __ldcg(&a.state[ST_POS])) + tz;
     const int n = pos + 1;
-    const int kvh = blockIdx.x, g = a.heads / a.kv_heads, hd = a.hd;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int dw = hd / a.dsplit;
-    const int d0 = blockIdx.y * dw;
-    float* w = sm;
-    float* vs = sm + ((g * a.ctx + 3) & ~3);
-    const bool vec = a.kv_kind == KV_F32 && attn_vec_ok(a) && (dw & 3) == 0;
-    const float* vsrc = a.vc + (size_t)kvh * hd + d0;
-    auto stage = [&](int c0) {
-        const int np = min(a.vchunk, n - c0);
-        if (a.kv_kind == KV_F16) {
+    const int tid = threadIdx.x & 255, warp = tid >> 5, lane = tid & 31;
+    float* srow = a.scores + ((size_t)tz * a.heads + h) * a.ctx;
+    float mx = -INFINITY;
+    for (int p = tid; p < n; p += 256) {
+        const float v = __ldcg(&srow[p]);
+        e[p] = v;
+        mx = fmaxf(mx, v);   // max is order independent (no NaNs)
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(NCM_FULL, mx, o));
+    if (lane == 0) red[warp] = mx;
+    group_sync<256, BAR>();
+    mx = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+    for (int p = tid; p < n; p += 256) e[p] = expf_cr(e[p] - mx);
+    group_sync<256, BAR>();
+    const float sum = seq_sum_nonneg<256, BAR>([&](int i) { return e[i]; }, n, sc, tid);
+    const float inv = 1.0f / sum;
+    for (int p = tid; p < n; p += 256) srow[p] = e[p] * inv;
+}
+
+__global__ void __launch_bounds__(256) attn_softmax_kernel(const __grid_constant__ AttnParams a) {
+    extern __shared__ __align__(16) float e[];
+    __shared__ SeqSumScratch sc;
+    __shared__ float red[8];
+    pdl_launch_dependents();
+    pdl_wait();
+    attn_softmax_body<0>(a, blockIdx.x, blockIdx.z, e, sc, red);
+}
+
+// Stage 3 (attn_av_kernel): out[d] = sum_p w_p * v_p[d], sequential over p per (head, dim)
+// (attn_output zeroed, add_weighted_f32_scalar inference.rs:3619-3623).  One item = (kv
+// head, 32-dimension block, group of HG query heads of that kv head, row): warp = query
+// head, lane = dimension, so each thread carries one chain and a warp's output is one
+// Q8_0 block for the output projection.  The item's V columns (128 bytes a position,
+// shared by its HG warps) and weights stream through a ring of kAvStages chunks of
+// kAvChunk positions by cp.async, so the loads of later chunks are in flight while a
+// chunk's chain runs.  buf holds kAvStages * av_stage_floats(HG) floats.
+constexpr int kAvChunk = 64;
+constexpr int kAvStages = 4;
+__host__ __device__ constexpr int av_stage_floats(int hg) { return kAvChunk * 32 + hg * kAvChunk; }
+
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int HG, int BAR>
+__device__ void attn_av_body(const AttnParams& a, int kvh, int db, int hgrp, int tz, float* buf, int rank) {
+    constexpr int NT = HG * 32;
+    const int pos = (a.pos_override >= 0 ? a.pos_override : __ldcg(&a.state[ST_POS])) + tz;
+    const int n = pos + 1;
+    const int g = a.heads / a.kv_heads;
+    const int warp = rank >> 5, lane = rank & 31;
+    const int h0 = kvh * g + hgrp * HG;
+    const int d0 = db * 32;
+    const float* wbase = a.scores + ((size_t)tz * a.heads + h0) * a.ctx;
+    const bool vec = a.kv_kind == KV_F32 && attn_vec_ok(a);
+    const float* vsrc = a.vc + (size_t)kvh * a.hd + d0;
+    const int nchunk = (n + kAvChunk - 1) / kAvChunk;
+    constexpr int SF = av_stage_floats(HG);
+    auto stage = [&](int k) {
+        float* vs = buf + (k % kAvStages) * SF;
+        float* ws = vs + kAvChunk * 32;
+        const int c0 = k * kAvChunk, np = min(kAvChunk, n - c0);
+        if (vec) {
+            for (int i = rank; i < np * 8; i += NT) cp_async16(vs + 4 * i, vsrc + (size_t)(c0 + (i >> 3)) * a.kvw + 4 * (i & 7));
+        } else if (a.kv_kind == KV_F16) {
             // decode_f16_head (inference.rs:4453-4458)
-            const uint16_t* v16 = reinterpret_cast<const uint16_t*>(a.vc_raw) + (size_t)kvh * hd + d0;
-            for (int i = tid; i < np * dw; i += 256)
-                vs[i] = f16_bits_to_f32(v16[(size_t)(c0 + i / dw) * a.kvw + i % dw]);
+            const uint16_t* v16 = reinterpret_cast<const uint16_t*>(a.vc_raw) + (size_t)kvh * a.hd + d0;
+            for (int i = rank; i < np * 32; i += NT)
+                vs[i] = f16_bits_to_f32(__ldcg(&v16[(size_t)(c0 + (i >> 5)) * a.kvw + (i & 31)]));
         } else if (a.kv_kind == KV_Q8_0) {
-            // inference.rs:4369-4379: value = q as f32 * block scale
+            // inference.rs:4369-4379: value = q as f32 * block scale (one 34-byte block)
             const uint8_t* vb = reinterpret_cast<const uint8_t*>(a.vc_raw);
-            const int bph = hd / 32, bpw = a.kvw / 32;
-            for (int i = tid; i < np * dw; i += 256) {
-                const int pp = c0 + i / dw, d = d0 + i % dw;
-                const uint8_t* blk = vb + ((size_t)pp * bpw + (size_t)kvh * bph + d / 32) * 34;
-                vs[i] = (float)(int8_t)blk[2 + d % 32] * f16_bits_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
+            const int bpw = a.kvw / 32;
+            for (int i = rank; i < np * 32; i += NT) {
+                const uint8_t* blk = vb + ((size_t)(c0 + (i >> 5)) * bpw + (size_t)(kvh * a.hd + d0) / 32) * 34;
+                vs[i] = (float)(int8_t)blk[2 + (i & 31)] * f16_bits_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
             }
-        } else if (vec) {
-            const int per = dw >> 2;
-            for (int i = tid; i < np * per; i += 256)
-                cp_async16(vs + 4 * i, vsrc + (size_t)(c0 + i / per) * a.kvw + 4 * (i % per));
-            cp_async_commit();
         } else {
-            for (int i = tid; i < np * dw; i += 256) vs[i] = vsrc[(size_t)(c0 + i / dw) * a.kvw + i % dw];
+            for (int i = rank; i < np * 32; i += NT) vs[i] = __ldcg(&vsrc[(size_t)(c0 + (i >> 5)) * a.kvw + (i & 31)]);
+        }
+        for (int i = rank; i < HG * np; i += NT) {
+            const int hh = i / np, p = i - hh * np;
+            cp_async4(ws + hh * kAvChunk + p, wbase + (size_t)hh * a.ctx + c0 + p);
         }
     };
-    stage(0);
-    if (warp < g) {
-        const int h = kvh * g + warp;
-        const float* srow = a.scores + (size_t)tz * a.heads * a.ctx + (size_t)h * a.ctx;
-        float* wr = w + warp * n;
-        float mx = -INFINITY;
-        for (int p = lane; p < n; p += 32) {
-            float v = srow[p];
-            wr[p] = v;
-            mx = fmaxf(mx, v);   // max is order independent (no NaNs)
-        }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(NCM_FULL, mx, o));
-        for (int p = lane; p < n; p += 32) wr[p] = expf_cr(wr[p] - mx);
-        __syncwarp();
-        const float sum = seq_sum_nonneg<32>([&](int i) { return wr[i]; }, n, scr[warp], lane);
-        const float inv = 1.0f / sum;
-        for (int p = lane; p < n; p += 32) wr[p] = wr[p] * inv;
+    for (int k = 0; k < kAvStages - 1; ++k) {
+        if (k < nchunk) stage(k);
+        cp_async_commit();
     }
-    const int item = tid, h = item / dw, d = item % dw;
-    const bool live = item < g * dw;
-    const float* wr = w + h * n;
     float acc = 0.0f;
-    for (int c0 = 0; c0 < n; c0 += a.vchunk) {
-        if (c0 > 0) {
-            __syncthreads();   // every thread is done with the previous chunk
-            stage(c0);
+    for (int k = 0; k < nchunk; ++k) {
+        if (k + kAvStages - 1 < nchunk) stage(k + kAvStages - 1);
+        cp_async_commit();
+        cp_async_wait_group<kAvStages - 1>();   // chunk k has landed (this thread's copies)
+        group_sync<NT, BAR>();                   // ... and every thread's
+        const float* vs = buf + (k % kAvStages) * SF;
+        const float* ws = vs + kAvChunk * 32 + warp * kAvChunk;
+        const int np = min(kAvChunk, n - k * kAvChunk);
+        int p = 0;
+        for (; p + 4 <= np; p += 4) {
+            const float4 w4 = *reinterpret_cast<const float4*>(ws + p);
+            const float v0 = vs[p * 32 + lane], v1 = vs[(p + 1) * 32 + lane];
+            const float v2 = vs[(p + 2) * 32 + lane], v3 = vs[(p + 3) * 32 + lane];
+            acc += w4.x * v0;
+            acc += w4.y * v1;
+            acc += w4.z * v2;
+            acc += w4.w * v3;
         }
-        if (vec) cp_async_wait_all();
-        __syncthreads();
-        if (live) {
-            const int np = min(a.vchunk, n - c0);
-            const float* wp = wr + c0;
-            const float* vp = vs + d;
-            int p = 0;
-            for (; p + 4 <= np; p += 4) {
-                const float w0 = wp[p], w1 = wp[p + 1], w2 = wp[p + 2], w3 = wp[p + 3];
-                const float v0 = vp[p * dw], v1 = vp[(p + 1) * dw], v2 = vp[(p + 2) * dw], v3 = vp[(p + 3) * dw];
-                acc += w0 * v0;
-                acc += w1 * v1;
-                acc += w2 * v2;
-                acc += w3 * v3;
-            }
-            for (; p < np; ++p) acc += wp[p] * vp[p * dw];
-        }
+        for (; p < np; ++p) acc += ws[p] * vs[p * 32 + lane];
+        group_sync<NT, BAR>();                   // the slot may be refilled
     }
-    if (live) a.out[(size_t)tz * a.tok_stride + (size_t)(kvh * g + h) * hd + d0 + d] = acc;
-    if (a.out_q && warp < g) {
-        // dw == 32: warp h holds one 32-value block of head h; quantise it for the output
-        // projection (quantize_f32_to_q8_0, inference.rs:991-1029)
+    const int h = h0 + warp;
+    a.out[(size_t)tz * a.tok_stride + (size_t)h * a.hd + d0 + lane] = acc;
+    if (a.out_q) {
+        // quantize_f32_to_q8_0 of this 32-value block for the output projection
+        // (inference.rs:991-1029)
         float amax = fabsf(acc);
 #pragma unroll
         for (int k = 16; k > 0; k >>= 1) amax = fmaxf(amax, __shfl_xor_sync(NCM_FULL, amax, k));
@@ -1546,23 +1609,32 @@ __global__ void __launch_bounds__(256) attn_softmax_v_kernel(const __grid_consta
             const float inv = 1.0f / scale;
             q = (int)fminf(fmaxf(roundf(acc * inv), -127.0f), 127.0f);
         }
-        const size_t o = (size_t)(kvh * g + h) * hd + d0;
-        a.out_q[o + d] = (int8_t)q;
-        if (d == 0) a.out_s[o >> 5] = scale;
+        const size_t o = (size_t)h * a.hd + d0;
+        a.out_q[o + lane] = (int8_t)q;
+        if (lane == 0) a.out_s[o >> 5] = scale;
     }
 }
 
+template <int HG>
+__global__ void __launch_bounds__(HG * 32) attn_av_kernel(const __grid_constant__ AttnParams a) {
+    extern __shared__ __align__(16) float buf[];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int nd = a.hd / 32;
+    attn_av_body<HG, 0>(a, blockIdx.x, blockIdx.y % nd, blockIdx.y / nd, blockIdx.z, buf, threadIdx.x);
+}
+
+// Query heads per attention item: the largest divisor of the group size g that is at
+// most 2 (two warps share one staged V slice; more would serialise the chains of one
+// SM's warps on its issue slots).
+int attn_group_heads(int g) { return g % 2 == 0 ? 2 : 1; }
+
 int attention_launch(const AttnParams& a0, cudaStream_t s, bool pdl) {
     constexpr int kMaxSmem = 200 * 1024;
-    if (int r = set_smem_limit((const void*)attn_softmax_v_kernel, kMaxSmem)) return r;
     AttnParams a = a0;
-    const int g = a.heads / a.kv_heads, dw = a.hd / a.dsplit;
-    const size_t wbytes = (size_t)((g * a.ctx + 3) & ~3) * sizeof(float);
-    if (wbytes + 32 * dw * sizeof(float) > (size_t)kMaxSmem || g * dw > 256) return (int)cudaErrorInvalidValue;
-    int vchunk = (int)std::min<size_t>((kMaxSmem - wbytes) / (dw * sizeof(float)), 32768 / (dw * sizeof(float)) * 4);
-    vchunk = std::min(vchunk, (a.ctx + 31) & ~31);
-    vchunk = std::max(32, vchunk & ~31);
-    a.vchunk = vchunk;
+    const int g = a.heads / a.kv_heads;
+    if (a.hd % 32 || a.heads % a.kv_heads || (size_t)a.ctx * 4 > (size_t)kMaxSmem) return (int)cudaErrorInvalidValue;
+    if (int r = set_smem_limit((const void*)attn_softmax_kernel, kMaxSmem)) return r;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -1575,9 +1647,17 @@ int attention_launch(const AttnParams& a0, cudaStream_t s, bool pdl) {
     cfg.gridDim = dim3(a.kv_heads, (a.ctx + 31) / 32, nz);
     int r = (int)cudaLaunchKernelEx(&cfg, attn_scores_kernel, a);
     if (r) return r;
-    cfg.gridDim = dim3(a.kv_heads, a.dsplit, nz);
-    cfg.dynamicSmemBytes = wbytes + (size_t)vchunk * dw * sizeof(float);
-    return (int)cudaLaunchKernelEx(&cfg, attn_softmax_v_kernel, a);
+    // the softmax of the last row reaches position pos + ntok - 1 (at most ctx - 1)
+    cfg.gridDim = dim3(a.heads, 1, nz);
+    cfg.dynamicSmemBytes = (size_t)a.ctx * 4;
+    r = (int)cudaLaunchKernelEx(&cfg, attn_softmax_kernel, a);
+    if (r) return r;
+    const int hg = attn_group_heads(g);
+    cfg.gridDim = dim3(a.kv_heads, (a.hd / 32) * (g / hg), nz);
+    cfg.blockDim = dim3(hg * 32);
+    cfg.dynamicSmemBytes = (size_t)kAvStages * av_stage_floats(hg) * 4;
+    if (hg == 2) return (int)cudaLaunchKernelEx(&cfg, attn_av_kernel<2>, a);
+    return (int)cudaLaunchKernelEx(&cfg, attn_av_kernel<1>, a);
 }
 
 // store_kv (inference.rs:539-568) for the F16 cache (fast_f32_to_f16 per value) and the
@@ -2772,6 +2852,559 @@ int q6k_gemv_launch(int epi, const Q6Params& p, cudaStream_t s, bool pdl) {
     if (epi == EPI_PLAIN) return (int)cudaLaunchKernelEx(&cfg, ncm_q6k_gemv_kernel<EPI_PLAIN>, p);
     if (epi == EPI_RESID) return (int)cudaLaunchKernelEx(&cfg, ncm_q6k_gemv_kernel<EPI_RESID>, p);
     if (epi == EPI_ARGMAX) return (int)cudaLaunchKernelEx(&cfg, ncm_q6k_gemv_kernel<EPI_ARGMAX>, p);
+    return (int)cudaErrorInvalidValue;
+}
+
+// ================================================================== persistent decode kernel
+// One launch = one decode token: for every layer the phases QKV, ATTN, WO, W13, W2, then
+// the head, each the same computation as the per-phase kernels above (same partition of
+// rows, same tiles, same fold order, same epilogues), so the results are bit-identical.
+// One CTA per SM runs all phases; between phases a grid-wide barrier (a counter in global
+// memory) orders the epilogues' global writes before the next phase's reads, which go
+// through L2 (ld.global.cg) since L1 is not coherent across SMs.  The producer warp
+// never waits on those barriers: it walks the whole token's tile sequence and keeps the
+// TMA ring full, so the weight stream runs on through every barrier, prologue and
+// attention phase (the gaps between kernel launches disappear).
+// Named barriers: 2 = prologue (compute + fold warps, 320 threads), 3 = grid-barrier
+// entry / exit (320), 4 = attention items (compute warps, 256), 1 = the fold warps.
+constexpr int kMkThreads = kProducer;   // compute + fold threads
+constexpr int kMkSoftmaxScratch = ((int)sizeof(SeqSumScratch) + 127) / 128 * 128;
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void mk_range(int rows, int align, int& r0, int& r1) {
+    const int nbk = gridDim.x;
+    r0 = (int)(((long long)blockIdx.x * rows / nbk)) & ~(align - 1);
+    r1 = (blockIdx.x + 1 == nbk) ? rows : ((int)(((long long)(blockIdx.x + 1) * rows / nbk)) & ~(align - 1));
+}
+
+// Grid-wide barrier number k (1, 2, ...) of this launch for the 320 compute / fold
+// threads of every CTA.  False once any device wait of the launch has failed.
+__device__ bool mk_grid_sync(const MkParams& P, unsigned k, int* s_abort) {
+    group_sync<kMkThreads, 3>();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(P.bar, 1u);
+        const unsigned target = k * gridDim.x;
+        if (ld_acquire_gpu(P.bar) < target) {
+            const uint64_t t0 = global_timer_ns();
+            for (uint32_t i = 1;; ++i) {
+                if (ld_acquire_gpu(P.bar) >= target) break;
+                if ((i & 255u) == 0 && global_timer_ns() - t0 > 4000000000ull) {
+                    set_dev_error(P.err, NCM_DEVERR_MBAR_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        *s_abort = *reinterpret_cast<volatile int*>(P.err) != 0;
+    }
+    group_sync<kMkThreads, 3>();
+    return !*s_abort;
+}
+
+// Prologue of a GEMV phase (320 threads): the activation as Q8_0 units in shared memory.
+// RMS phases (QKV, W13, HEAD) normalise the hidden state (layer 0's QKV: the embedding
+// row, dequantised here, whose sum of squares is the per-token table); WO / W2 copy the
+// producer phase's Q8_0 blocks.
+__device__ void mk_prologue(const MkParams& P, const MkPhase& F, uint8_t* smem, SeqSumScratchT<kMkThreads>& sc) {
+    const int tid = threadIdx.x;
+    const int nblk = F.nchunk * 16;
+    float2* xs = reinterpret_cast<float2*>(smem + P.xs_off);
+    int2* xsum = reinterpret_cast<int2*>(smem + P.xsum_off);
+    if (F.kind == MK_WO || F.kind == MK_W2) {
+        for (int g = tid; g < nblk / 2; g += kMkThreads) {
+            uint4* dst = reinterpret_cast<uint4*>(smem + P.xq_off + 80 * g);
+            if (2 * g < F.nb) {
+                const bool two = 2 * g + 1 < F.nb;
+                const uint4* src = reinterpret_cast<const uint4*>(F.xq + 64 * g);
+                int s0 = 0, s1 = 0;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint4 v = (i < 2 || two) ? __ldcg(src + i) : make_uint4(0, 0, 0, 0);
+                    dst[i] = v;
+                    int a = i < 2 ? s0 : s1;
+                    a = __dp4a((int)v.x, 0x01010101, a);
+                    a = __dp4a((int)v.y, 0x01010101, a);
+                    a = __dp4a((int)v.z, 0x01010101, a);
+                    a = __dp4a((int)v.w, 0x01010101, a);
+                    if (i < 2) s0 = a; else s1 = a;
+                }
+                xs[g] = make_float2(__ldcg(&F.xs[2 * g]), two ? __ldcg(&F.xs[2 * g + 1]) : 0.0f);
+                xsum[g] = make_int2(s0, s1);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+                xs[g] = make_float2(0.0f, 0.0f);
+                xsum[g] = make_int2(0, 0);
+            }
+        }
+        group_sync<kMkThreads, 2>();
+        return;
+    }
+    // RMS phases: x = hidden (f32, cols = emb) staged through L2 into the term region
+    float* xf = reinterpret_cast<float*>(smem + P.t_off);
+    const int n = F.cols;
+    float tot;
+    if (F.kind == MK_QKV && F.layer == 0) {
+        // inference.rs:4494-4503 embed_token: the token's row, dequantised; this CTA also
+        // writes the hidden rows it owns in the row-parallel phases (their residual)
+        const int tok = __ldcg(&P.tokens[__ldcg(&P.state[ST_POS])]);
+        const uint8_t* row = P.embd + (size_t)tok * P.embd_pitch;
+        for (int i = tid; i < n; i += kMkThreads) xf[i] = dequant_elem(P.embd_type, row, i);
+        int h0, h1;
+        mk_range(P.emb, 2, h0, h1);
+        for (int i = h0 + tid; i < h1; i += kMkThreads) P.hidden[i] = dequant_elem(P.embd_type, row, i);
+        group_sync<kMkThreads, 2>();
+        tot = __ldg(&P.ssq_tok[tok]);
+    } else {
+        const float4* src = reinterpret_cast<const float4*>(P.hidden);
+        for (int i = tid; i < n / 4; i += kMkThreads) reinterpret_cast<float4*>(xf)[i] = __ldcg(src + i);
+        group_sync<kMkThreads, 2>();
+        // inference.rs:698-701: sum += val * val, sequential (exact, seq_sum_nonneg)
+        tot = seq_sum_nonneg<kMkThreads, 2>([&](int i) { const float v = xf[i]; return v * v; }, n, sc, tid);
+    }
+    const float scale = 1.0f / sqrtf(tot / (float)n + P.eps);
+    // quantize_f32_to_q8_0 of x * scale * w (inference.rs:704, 991-1029), four lanes per block
+    const int li = tid & 3;
+    const unsigned qmask = 0xFu << (tid & 28);
+    for (int b = tid >> 2; b < nblk; b += kMkThreads >> 2) {
+        uint32_t* dst = reinterpret_cast<uint32_t*>(smem + P.xq_off + 80 * (b >> 1) + 32 * (b & 1));
+        const int c = (li + b) & 3;
+        if (b < F.nb) {
+            float v[8];
+            const float4* xb = reinterpret_cast<const float4*>(xf) + 8 * b + 2 * c;
+            const float4* wb = reinterpret_cast<const float4*>(F.norm_w) + 8 * b + 2 * c;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float4 x4 = xb[h], w4 = __ldg(wb + h);
+                v[4 * h] = x4.x * scale * w4.x;
+                v[4 * h + 1] = x4.y * scale * w4.y;
+                v[4 * h + 2] = x4.z * scale * w4.z;
+                v[4 * h + 3] = x4.w * scale * w4.w;
+            }
+            float amax = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+            amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 2));
+            const float scale_b = amax / 127.0f;
+            uint32_t w0 = 0, w1 = 0;
+            int sum = 0;
+            if (scale_b > 0.0f) {
+                const float inv = 1.0f / scale_b;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    float q = roundf(v[i] * inv);
+                    q = fminf(fmaxf(q, -127.0f), 127.0f);
+                    const int qi = (int)q;
+                    sum += qi;
+                    const uint32_t byte = (uint32_t)(qi & 0xff) << (8 * (i & 3));
+                    if (i < 4) w0 |= byte; else w1 |= byte;
+                }
+            }
+            sum += __shfl_xor_sync(qmask, sum, 1);
+            sum += __shfl_xor_sync(qmask, sum, 2);
+            dst[2 * c] = w0;
+            dst[2 * c + 1] = w1;
+            if (li == 0) {
+                reinterpret_cast<float*>(xs)[b] = scale_b;
+                reinterpret_cast<int*>(xsum)[b] = sum;
+            }
+        } else {
+            dst[2 * c] = 0;
+            dst[2 * c + 1] = 0;
+            if (li == 0) {
+                reinterpret_cast<float*>(xs)[b] = 0.0f;
+                reinterpret_cast<int*>(xsum)[b] = 0;
+            }
+        }
+    }
+    group_sync<kMkThreads, 2>();
+}
+
+__device__ __forceinline__ void mk_load_xunit(const uint8_t* smem, const MkParams& P, int g, XUnit& x) {
+    const uint4* src = reinterpret_cast<const uint4*>(smem + P.xq_off + 80 * g);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 v = src[i];
+        x.w[4 * i] = v.x; x.w[4 * i + 1] = v.y; x.w[4 * i + 2] = v.z; x.w[4 * i + 3] = v.w;
+    }
+    const float2 sv = reinterpret_cast<const float2*>(smem + P.xs_off)[g];
+    const int2 cv = reinterpret_cast<const int2*>(smem + P.xsum_off)[g];
+    x.s[0] = sv.x; x.s[1] = sv.y;
+    x.sum[0] = cv.x; x.sum[1] = cv.y;
+}
+
+template <int QT>
+__global__ void __launch_bounds__(kGemvThreads, 1) ncm_decode_kernel(const __grid_constant__ MkParams P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ SeqSumScratchT<kMkThreads> sc;
+    __shared__ float xchg[kMaxFold];
+    __shared__ float wv[2];
+    __shared__ int wi[2];
+    __shared__ int s_last, s_abort;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + 8;
+    uint64_t* tfull = full + 16;
+    uint64_t* tempty = full + 24;
+    float* tbuf = reinterpret_cast<float*>(smem + P.t_off);
+    uint8_t* stages = smem + P.stage_off;
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int ns = P.nstages;
+    const uint64_t limit_ns = 4000000000ull;
+    const int chunk_bytes = QT == NCM_T_Q8_0 ? 16 * 34 : 288;
+    const int chunk_words = chunk_bytes / 4;
+    if (tid == 0) {
+        for (int s = 0; s < ns; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kComputeThreads / 32);
+            mbar_init(&tfull[s], kComputeThreads / 32);
+            mbar_init(&tempty[s], 2);
+        }
+        fence_mbar_init();
+        s_abort = 0;
+    }
+    __syncthreads();
+
+    if (tid == kProducer) {
+        // ---- producer: the token's whole tile sequence, never waiting on grid barriers
+        const uint64_t pol = l2_evict_first_policy();
+        int t = 0;
+        bool stop = false;
+        for (int ph = 0; ph < P.nphase && !stop; ++ph) {
+            const MkPhase& F = P.phases[ph];
+            if (F.kind == MK_ATTN) continue;
+            const bool dual = F.kind == MK_W13;
+            const int box_bytes = F.box_rows * chunk_bytes;
+            const int box2_off = (box_bytes + 127) & ~127;
+            int r0, r1;
+            mk_range(F.rows, F.row_align, r0, r1);
+            for (int cur = r0; cur < r1 && !stop;) {
+                const int n = min(F.box_rows, r1 - cur);
+                for (int c = 0; c < F.nchunk; ++c, ++t) {
+                    const int s = t % ns;
+                    if (t >= ns && !mbar_wait(&empty[s], (uint32_t)(((t / ns) & 1) ^ 1), limit_ns)) {
+                        set_dev_error(P.err, NCM_DEVERR_MBAR_TIMEOUT);
+                        stop = true;
+                        break;
+                    }
+                    if (*reinterpret_cast<volatile int*>(P.err)) { stop = true; break; }
+                    mbar_arrive_expect_tx(&full[s], dual ? 2 * box_bytes : box_bytes);
+                    tma_load_2d(stages + (size_t)s * P.stage_bytes, &P.maps[F.map], c * chunk_words, cur, &full[s], pol);
+                    if (dual)
+                        tma_load_2d(stages + (size_t)s * P.stage_bytes + box2_off, &P.maps[F.map + 1], c * chunk_words,
+                                    cur, &full[s], pol);
+                }
+                cur += n;
+            }
+        }
+        if (stop) {
+            // wait (bounded) for every load still in flight before the CTA may exit
+            for (int k = max(0, t - ns); k < t; ++k) mbar_wait(&full[k % ns], (uint32_t)((k / ns) & 1), 100000000ull);
+        }
+    } else if (tid < kProducer) {
+        // ---- compute (warps 0-7) and fold (warps 8-9) through every phase
+        const bool is_fold = tid >= kFoldBase;
+        const int w = tid >> 5, u = lane & 7, v0 = lane >> 3, f = tid - kFoldBase;
+        int t = 0;
+        unsigned nbar = 0;
+        const int pos = __ldcg(&P.state[ST_POS]);
+        for (int ph = 0; ph < P.nphase; ++ph) {
+            const MkPhase& F = P.phases[ph];
+            if (ph > 0 && !mk_grid_sync(P, ++nbar, &s_abort)) break;
+            if (F.kind == MK_ATTN) {
+                // attention (inference.rs:4142-4292) by the compute warps, the three stages of
+                // attention_launch with grid barriers between them: score tiles, one softmax
+                // per query head, then the V items (by the first two warps of each CTA)
+                AttnParams a;
+                memset(&a, 0, sizeof a);
+                a.q = P.q; a.kc = F.kcache; a.vc = F.vcache; a.scores = P.scores; a.out = P.att;
+                a.state = P.state; a.pos_override = -1; a.heads = P.heads; a.kv_heads = P.kv_heads; a.hd = P.hd;
+                a.kvw = P.kvw; a.ctx = P.ctx; a.scale = P.attn_scale;
+                a.ntok = 1; a.tok_stride = 0; a.out_q = P.att_q; a.out_s = P.att_s; a.kv_kind = KV_F32;
+                a.kc_raw = F.kcache; a.vc_raw = F.vcache;
+                float* qs = reinterpret_cast<float*>(smem + P.xq_off);
+                float* ks = qs + 8 * 256;
+                const int ntile = (pos + 1 + 31) / 32;
+                if (!is_fold) {
+                    for (int it = blockIdx.x; it < P.kv_heads * ntile; it += gridDim.x) {
+                        attn_scores_body<4>(a, it % P.kv_heads, it / P.kv_heads, 0, qs, ks);
+                        group_sync<256, 4>();
+                    }
+                }
+                if (!mk_grid_sync(P, ++nbar, &s_abort)) break;
+                if (!is_fold) {
+                    SeqSumScratch* ssc = reinterpret_cast<SeqSumScratch*>(smem + P.xq_off);
+                    float* red = reinterpret_cast<float*>(smem + P.xq_off + kMkSoftmaxScratch);
+                    float* e = red + 32;
+                    for (int it = blockIdx.x; it < P.heads; it += gridDim.x) {
+                        attn_softmax_body<4>(a, it, 0, e, *ssc, red);
+                        group_sync<256, 4>();
+                    }
+                }
+                if (!mk_grid_sync(P, ++nbar, &s_abort)) break;
+                if (tid < 64) {
+                    float* buf = reinterpret_cast<float*>(smem + P.xq_off);
+                    const int nd = P.hd / 32, g = P.heads / P.kv_heads;
+                    const int items = P.kv_heads * nd * (g / 2);
+                    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+                        const int kvh = it % P.kv_heads, r = it / P.kv_heads;
+                        attn_av_body<2, 5>(a, kvh, r % nd, r / nd, 0, buf, tid);
+                    }
+                }
+                continue;
+            }
+            // ---- a GEMV phase
+            mk_prologue(P, F, smem, sc);
+            const bool dual = F.kind == MK_W13;
+            const int box_bytes = F.box_rows * chunk_bytes;
+            const int box2_off = (box_bytes + 127) & ~127;
+            int r0, r1;
+            mk_range(F.rows, F.row_align, r0, r1);
+            if (!is_fold) {
+                for (int cur = r0; cur < r1;) {
+                    const int n = min(F.box_rows, r1 - cur);
+                    const int vrows = dual ? 2 * F.box_rows : n;
+                    for (int c = 0; c < F.nchunk; ++c, ++t) {
+                        const int s = t % ns;
+                        const uint32_t use = (uint32_t)(t / ns);
+                        if (!mbar_wait(&full[s], use & 1, limit_ns)) set_dev_error(P.err, NCM_DEVERR_MBAR_TIMEOUT);
+                        if (use > 0 && !mbar_wait(&tempty[s], (use - 1) & 1, limit_ns))
+                            set_dev_error(P.err, NCM_DEVERR_MBAR_TIMEOUT);
+                        const uint8_t* sb = stages + (size_t)s * P.stage_bytes;
+                        float* T = tbuf + s * (kMaxFold * kTStride);
+                        XUnit x;
+                        mk_load_xunit(smem, P, c * kUnits + u, x);
+                        const uint8_t* rp[2];
+                        bool ok[2];
+                        int vr[2];
+#pragma unroll
+                        for (int j = 0; j < 2; ++j) {
+                            vr[j] = v0 + 4 * w + 32 * j;
+                            const int mat = dual ? (vr[j] >= F.box_rows) : 0;
+                            const int r = vr[j] - mat * F.box_rows;
+                            ok[j] = vr[j] < vrows && r < n;
+                            rp[j] = sb + mat * box2_off + (ok[j] ? r : 0) * chunk_bytes;
+                        }
+                        float t0[2], t1[2];
+                        unit_terms_n<QT, 2>(rp, u, x, t0, t1);
+#pragma unroll
+                        for (int j = 0; j < 2; ++j) {
+                            if (ok[j]) {
+                                float* trow = T + vr[j] * kTStride;
+                                trow[2 * u] = t0[j];
+                                trow[2 * u + 1] = t1[j];
+                            }
+                        }
+                        __syncwarp();
+                        if (lane == 0) {
+                            mbar_arrive(&empty[s]);
+                            mbar_arrive(&tfull[s]);
+                        }
+                    }
+                    cur += n;
+                }
+            } else {
+                float best_v = -INFINITY;
+                int best_i = 0x7fffffff;
+                const int nsb = F.nb / 8;
+                for (int cur = r0; cur < r1;) {
+                    const int n = min(F.box_rows, r1 - cur);
+                    const bool live = dual ? (f < 2 * F.box_rows && (f % F.box_rows) < n) : (f < n);
+                    float acc = 0.0f;
+                    const float* trow0 = tbuf + f * kTStride;
+                    for (int c = 0; c < F.nchunk; ++c, ++t) {
+                        const int s = t % ns;
+                        const uint32_t use = (uint32_t)(t / ns);
+                        if (!mbar_wait(&tfull[s], use & 1, limit_ns)) set_dev_error(P.err, NCM_DEVERR_MBAR_TIMEOUT);
+                        if (live) {
+                            const float* trow = trow0 + s * (kMaxFold * kTStride);
+                            float tv[16];
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) tv[j] = trow[j];
+                            asm volatile("" ::: "memory");
+                            if constexpr (QT == NCM_T_Q4_K) {
+                                const int nsbc = min(2, nsb - 2 * c);
+#pragma unroll
+                                for (int q = 0; q < 2; ++q) {
+                                    if (q < nsbc) {
+                                        float ssum = 0.0f;   // q8.rs:1342
+#pragma unroll
+                                        for (int j = 0; j < 8; ++j) ssum += tv[8 * q + j];
+                                        acc += ssum;         // inference.rs:3129
+                                    }
+                                }
+                            } else {
+                                const int nbc = min(16, F.nb - 16 * c);
+                                if (nbc == 16) {
+#pragma unroll
+                                    for (int j = 0; j < 16; ++j) acc += tv[j];
+                                } else {
+#pragma unroll
+                                    for (int j = 0; j < 16; ++j)
+                                        if (j < nbc) acc += tv[j];
+                                }
+                            }
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[s]);
+                    }
+                    // tile epilogue: the per-phase kernels' epilogues
+                    if (F.kind == MK_QKV) {
+                        const float other = __shfl_xor_sync(NCM_FULL, acc, 1);
+                        if (f < n) {
+                            const int row = cur + f;
+                            const int kind = row >= F.seg_v ? SEG_V : (row >= F.seg_k ? SEG_K : SEG_Q);
+                            const int lr = row - (kind == SEG_V ? F.seg_v : (kind == SEG_K ? F.seg_k : 0));
+                            float v = acc;
+                            if (kind != SEG_V) {
+                                // inference.rs:904-933 apply_rope_cached, NORM pairs (2i, 2i+1)
+                                const int i = (lr % P.hd) >> 1;
+                                if (i < P.rope_half) {
+                                    const float2 scs = P.rope[(size_t)pos * P.rope_half + i];
+                                    const float x0 = (f & 1) ? other : acc;
+                                    const float x1 = (f & 1) ? acc : other;
+                                    v = (f & 1) ? (x0 * scs.x + x1 * scs.y) : (x0 * scs.y - x1 * scs.x);
+                                }
+                            }
+                            if (kind == SEG_Q) F.out[lr] = v;
+                            else ((kind == SEG_K ? F.kcache : F.vcache) + (size_t)pos * P.kvw)[lr] = v;
+                        }
+                    } else if (F.kind == MK_W13) {
+                        if (f >= F.box_rows && f < F.box_rows + n) xchg[f - F.box_rows] = acc;
+                        asm volatile("bar.sync 1, 64;" ::: "memory");
+                        float o = 0.0f;
+                        if (f < n) {
+                            const float g = acc, uu = xchg[f];
+                            const float sig = 1.0f / (1.0f + expf_cr(-g));   // inference.rs:3385-3388
+                            o = g * sig * uu;
+                            F.out[cur + f] = o;
+                        }
+                        if (f < 32) {
+                            // 32-row tile (box_rows 32, 32-aligned ranges): one Q8_0 block for w2
+                            float amax = fabsf(o);
+#pragma unroll
+                            for (int k = 16; k > 0; k >>= 1) amax = fmaxf(amax, __shfl_xor_sync(NCM_FULL, amax, k));
+                            const float scale = amax / 127.0f;
+                            int q = 0;
+                            if (scale > 0.0f) {
+                                const float inv = 1.0f / scale;
+                                q = (int)fminf(fmaxf(roundf(o * inv), -127.0f), 127.0f);
+                            }
+                            F.qout[cur + f] = (int8_t)q;
+                            if (f == 0) F.qout_s[cur >> 5] = scale;
+                        }
+                        asm volatile("bar.sync 1, 64;" ::: "memory");
+                    } else if (F.kind == MK_HEAD) {
+                        if (f < n) {
+                            const int lr = cur + f;
+                            if (F.out) F.out[lr] = acc;
+                            if (better(acc, lr, best_v, best_i)) { best_v = acc; best_i = lr; }
+                        }
+                    } else if (f < n) {
+                        float* h = F.out + cur + f;
+                        *h = __ldcg(h) + acc;   // inference.rs:4670-4672 / 4744-4746
+                    }
+                    cur += n;
+                }
+                if (F.kind == MK_HEAD) {
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const float ov = __shfl_xor_sync(NCM_FULL, best_v, o);
+                        const int oi = __shfl_xor_sync(NCM_FULL, best_i, o);
+                        if (better(ov, oi, best_v, best_i)) { best_v = ov; best_i = oi; }
+                    }
+                    if (lane == 0) { wv[f >> 5] = best_v; wi[f >> 5] = best_i; }
+                    asm volatile("bar.sync 1, 64;" ::: "memory");
+                    if (f == 0) {
+                        // CTA first-max, then the last CTA merges every CTA's (inference.rs:4838-4843)
+                        float bv = wv[0];
+                        int bi = wi[0];
+                        if (better(wv[1], wi[1], bv, bi)) { bv = wv[1]; bi = wi[1]; }
+                        P.amax_part[blockIdx.x] = make_float2(bv, __int_as_float(bi));
+                        __threadfence();
+                        const unsigned prev = atomicAdd(P.amax_cnt, 1u);
+                        if (prev == gridDim.x - 1) {
+                            __threadfence();
+                            bv = -INFINITY;
+                            bi = 0x7fffffff;
+                            for (int c = 0; c < (int)gridDim.x; ++c) {
+                                const float2 e = __ldcg(&P.amax_part[c]);
+                                const int ei = __float_as_int(e.y);
+                                if (better(e.x, ei, bv, bi)) { bv = e.x; bi = ei; }
+                            }
+                            const int tok = P.head_row0 + bi;
+                            if (pos + 1 < P.ctx && pos + 1 >= P.state[ST_NPROMPT]) P.tokens[pos + 1] = tok;
+                            P.state[ST_LAST_TOKEN] = tok;
+                            P.state[ST_POS] = pos + 1;
+                            P.state[ST_STEP] = P.state[ST_STEP] + 1;
+                            *P.amax_cnt = 0u;
+                        }
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
+bool mk_box_rows(int qtype, int cols, int rows, bool dual, int row_align, int slot_bytes, int* box_rows) {
+    // the tiling of gemv_plan, for one CTA per SM
+    const int chunk_bytes = qtype == NCM_T_Q8_0 ? 16 * 34 : 288;
+    int grid = num_sms();
+    const int ra = row_align < 2 ? 2 : row_align;
+    const int maxg = std::max(1, (rows + ra - 1) / ra);
+    if (grid > maxg) grid = maxg;
+    const int per_cta = (rows + grid - 1) / grid;
+    int maxr = qtype == NCM_T_Q8_0 ? 32 : 64;
+    if (dual) maxr /= 2;
+    const int span = per_cta + ra;
+    const int ntiles = (span + maxr - 1) / maxr;
+    int br = (span + ntiles - 1) / ntiles;
+    br = (br + ra - 1) / ra * ra;
+    if (br > maxr) br = maxr;
+    if (br < 2) br = 2;
+    const int need = (br * chunk_bytes + 127) / 128 * 128 * (dual ? 2 : 1);
+    if (need > slot_bytes) return false;
+    *box_rows = br;
+    (void)cols;
+    return true;
+}
+
+size_t mk_attn_bytes(int ctx) {
+    const size_t scores = 4 * (8 * 256 + 32 * 257);
+    const size_t softmax = kMkSoftmaxScratch + 32 * 4 + (size_t)ctx * 4;
+    const size_t av = (size_t)kAvStages * av_stage_floats(2) * 4;
+    return std::max(scores, std::max(softmax, av));
+}
+
+int mk_launch(int qtype, const MkParams& p, cudaStream_t s) {
+    const void* fn = qtype == NCM_T_Q4_0 ? (const void*)ncm_decode_kernel<NCM_T_Q4_0>
+                   : qtype == NCM_T_Q8_0 ? (const void*)ncm_decode_kernel<NCM_T_Q8_0>
+                                         : (const void*)ncm_decode_kernel<NCM_T_Q4_K>;
+    // the limit is per kernel and device, set once: the largest the static part leaves
+    cudaFuncAttributes fa{};
+    if (cudaError_t e = cudaFuncGetAttributes(&fa, fn)) return (int)e;
+    const int room = 227 * 1024 - (int)fa.sharedSizeBytes;
+    if (p.smem_bytes > room) return (int)cudaErrorInvalidValue;
+    if (int r = set_smem_limit(fn, room)) return r;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(num_sms());
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = p.smem_bytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;   // every CTA resident (grid barriers)
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (qtype == NCM_T_Q4_0) return (int)cudaLaunchKernelEx(&cfg, ncm_decode_kernel<NCM_T_Q4_0>, p);
+    if (qtype == NCM_T_Q8_0) return (int)cudaLaunchKernelEx(&cfg, ncm_decode_kernel<NCM_T_Q8_0>, p);
+    if (qtype == NCM_T_Q4_K) return (int)cudaLaunchKernelEx(&cfg, ncm_decode_kernel<NCM_T_Q4_K>, p);
     return (int)cudaErrorInvalidValue;
 }
 }  // namespace ncm

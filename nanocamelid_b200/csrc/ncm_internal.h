@@ -111,12 +111,11 @@ struct AttnParams {
     float* out;              // [heads_local * hd]
     const int* state;
     int pos_override;        // >= 0: use instead of state[ST_POS]
-    int heads, kv_heads, hd, kvw, ctx, dsplit;
-    int vchunk;              // positions of V staged in shared memory at a time (set by attention_launch)
+    int heads, kv_heads, hd, kvw, ctx;
     float scale;
     int ntok;                // rows in one launch (grid z): token z at position pos + z, q / out at
     int tok_stride;          //   + z * tok_stride floats, scores at + z * heads * ctx
-    int8_t* out_q;           // when set (one row, head_dim / dsplit == 32): the output also as Q8_0
+    int8_t* out_q;           // when set (one row): the output also as Q8_0
     float* out_s;            //   blocks (quantize_f32_to_q8_0), the next projection's input
     int kv_kind;             // cache storage: 0 f32 (kc / vc), 1 F16, 2 Q8_0 (kc_raw / vc_raw)
     const void* kc_raw;
@@ -183,6 +182,55 @@ struct Q6Params {
     int* tokens;
     int ctx;
 };
+
+// Persistent decode kernel: one launch runs a whole token (every layer's GEMVs and
+// attention, then the head) on one CTA per SM, with grid-wide barriers between phases and
+// the weight ring streaming across them.
+enum MkKind { MK_QKV = 0, MK_ATTN = 1, MK_WO = 2, MK_W13 = 3, MK_W2 = 4, MK_HEAD = 5 };
+struct MkPhase {
+    int kind, layer;
+    int map;                      // tensor map index (MK_W13: gate at map, up at map + 1)
+    int rows, cols, nb, nchunk, box_rows, row_align;
+    const float* norm_w;          // QKV / W13 / HEAD: RMS weights
+    const int8_t* xq;             // WO / W2: the producing phase's Q8_0 output
+    const float* xs;
+    float* out;                   // QKV: q, WO / W2: hidden, W13: act, HEAD: logits
+    int8_t* qout;                 // W13: act as Q8_0
+    float* qout_s;
+    float* kcache;                // QKV / ATTN: this layer's caches [ctx][kv_width]
+    float* vcache;
+    int seg_k, seg_v;             // QKV: first k row and first v row of the fused row space
+};
+struct MkParams {
+    const CUtensorMap* maps;      // device array, 64-byte aligned
+    const MkPhase* phases;
+    int nphase;
+    int emb, heads, kv_heads, hd, kvw, ctx, rope_half;
+    float eps, attn_scale;
+    const float2* rope;
+    int embd_type;
+    const uint8_t* embd;
+    int64_t embd_pitch;
+    const float* ssq_tok;
+    float* hidden;
+    float* q;
+    float* att;
+    int8_t* att_q;
+    float* att_s;
+    float* scores;
+    int* state;
+    int* tokens;
+    float2* amax_part;
+    unsigned* amax_cnt;
+    int head_row0;
+    unsigned* bar;                // grid barrier counter, zeroed before each launch
+    int* err;
+    int nstages, stage_bytes, xq_off, xs_off, xsum_off, t_off, stage_off, attn_bytes, smem_bytes;
+};
+// Fills the box rows of a phase for a ring slot of slot_bytes; false if it cannot fit.
+bool mk_box_rows(int qtype, int cols, int rows, bool dual, int row_align, int slot_bytes, int* box_rows);
+int mk_launch(int qtype, const MkParams& p, cudaStream_t s);
+size_t mk_attn_bytes(int ctx);   // shared memory the attention phase uses (before the ring)
 
 // Launchers (kernels.cu).
 int q6k_gemv_launch(int epi, const Q6Params& p, cudaStream_t s, bool pdl);
