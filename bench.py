@@ -379,7 +379,9 @@ def run_b200(args, sp):
                 "fold_end_max": us(rel(4).max()), "exit_max": us(rel(6).max()),
                 "epilogue_avg": us(ts[:, 5].mean()), "c_wait_data_avg": us(ts[:, 7].mean()),
                 "c_wait_slot_avg": us(ts[:, 8].mean()), "f_wait_terms_avg": us(ts[:, 9].mean()),
-                "p_wait_stage_avg": us(ts[:, 10].mean())}
+                "p_wait_stage_avg": us(ts[:, 10].mean()),
+                "stage_x_avg": us((ts[:, 12] - ts[:, 1]).mean()) if ts[:, 12].max() > 0 else None,
+                "seq_sum_avg": us((ts[:, 13] - ts[:, 12]).mean()) if ts[:, 13].max() > 0 else None}
         print(json.dumps({"kernels": out, "tok_s": round(tok_s, 2), "ms_per_step": round(ms / args.steps, 4),
                           "env": {k: v for k, v in os.environ.items() if k.startswith("NCM_TUNE")}}), flush=True)
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")

@@ -110,6 +110,7 @@ struct ncm_model {
     int8_t* hx_q = nullptr;       // the normed hidden as Q8_0 for a Q6_K head
     float* hx_s = nullptr;
     int64_t prefetch_bytes = 0;   // per CTA: next kernel's weights streamed into L2 (0: off)
+    int cgroups = 4;              // GEMV compute-warp groups (stages worked on at once)
     int tune = 0;                 // measurement knobs
     uint64_t* dbg_ts = nullptr;   // measurement probe buffer [num_sms][8], filled by step-kernel seam launches
     bool dbg_on = false;
@@ -118,13 +119,6 @@ struct ncm_model {
     cudaStream_t ext_stream = nullptr;   // caller stream of the last prefill / decode, until synced
     std::vector<void*> allocs;
     cudaGraphExec_t g_full = nullptr, g_nohead = nullptr;
-    // persistent decode kernel (one launch per token) when the model qualifies
-    bool mk_tried = false, mk_on = false;
-    int mk_qt = 0;
-    MkParams mk{};
-    CUtensorMap* mk_maps = nullptr;
-    MkPhase* mk_phases = nullptr;
-    unsigned* mk_bar = nullptr;
     bool dirty = true;
     // multi-row verify buffers (allocated on first use): [kMaxBatch][...]
     float *b_hidden = nullptr, *b_q = nullptr, *b_att = nullptr, *b_act = nullptr;
@@ -530,6 +524,7 @@ static ncm_status check_all_shapes(ncm_model* m) {
     // tuning knobs for measurement runs (unset in normal use)
     if (const char* e = getenv("NCM_TUNE_ACTQ")) m->act_quantised = m->act_quantised && atoi(e) != 0;
     if (const char* e = getenv("NCM_TUNE_PREFETCH_KB")) m->prefetch_bytes = (int64_t)atoi(e) * 1024;
+    if (const char* e = getenv("NCM_TUNE_CGROUPS")) m->cgroups = atoi(e);
     if (const char* e = getenv("NCM_TUNE_BITS")) m->tune = atoi(e);
     return NCM_OK;
 }
@@ -728,6 +723,7 @@ static GemvParams base_params(ncm_model* m) {
     p.tp.timeout_ns = m->timeout_ns;
     p.row_align = 2;
     p.tune = m->tune;
+    p.cgroups = m->cgroups;
     p.dbg_ts = m->dbg_on ? m->dbg_ts : nullptr;
     return p;
 }
@@ -1057,155 +1053,8 @@ static ncm_status check_err(ncm_model* m) {
 }
 
 // One decode step: the captured graph, or eagerly when a host reducer takes part.
-// ------------------------------------------------------------------ persistent decode kernel
-// One launch per decode token (ncm_decode_kernel): one CTA per SM runs every layer's
-// QKV, attention, wo, gate/up and down phases and the head, with grid barriers between
-// phases and the weight ring streaming across them.  Used for one-GPU models whose
-// layer and head matrices share one quant type, with the f32 KV cache; everything else
-// runs the per-phase kernels of enqueue_step (the same arithmetic, bit for bit).
-static bool mk_eligible(ncm_model* m, int* qt) {
-    if (m->world != 1 || m->kv_kind != KV_F32 || m->has_q6k || !m->act_quantised) return false;
-    if (getenv("NCM_TUNE_NO_MK")) return false;
-    const int t = m->head.type;
-    for (const Layer& l : m->L) {
-        const DevMat* ms[] = {&l.wq, &l.wk, &l.wv, &l.wo, &l.w1, &l.w3, &l.w2};
-        for (const DevMat* d : ms)
-            if (d->type != t) return false;
-        if (l.wk.d != l.wq.d + (size_t)l.wq.pitch * l.wq.rows || l.wv.d != l.wk.d + (size_t)l.wk.pitch * l.wk.rows)
-            return false;
-    }
-    if (t != NCM_T_Q4_0 && t != NCM_T_Q8_0 && t != NCM_T_Q4_K) return false;
-    *qt = t;
-    return true;
-}
-
-static ncm_status mk_build(ncm_model* m) {
-    m->mk_tried = true;
-    int qt = 0;
-    if (!mk_eligible(m, &qt)) return NCM_OK;
-    const int H = m->emb, qw = m->qh * m->hd, kw = m->kh * m->hd, F = m->fl, L = m->layers;
-    const int chunk_words = (qt == NCM_T_Q8_0 ? 16 * 34 : 288) / 4;
-    constexpr int kSlotMax = 20 * 1024;
-    // phases and their tilings
-    std::vector<MkPhase> ph;
-    std::vector<CUtensorMap> maps(5 * (size_t)L + 1);
-    int slot = 0;
-    auto tile = [&](int cols, int rows, bool dual, int ra, int* br) -> bool {
-        if (!mk_box_rows(qt, cols, rows, dual, ra, kSlotMax, br)) return false;
-        const int cb = chunk_words * 4;
-        slot = std::max(slot, ((*br * cb + 127) / 128 * 128) * (dual ? 2 : 1));
-        return true;
-    };
-    auto mkmap = [&](int idx, const uint8_t* base, int rows, int pitch, int br) -> int {
-        return gemv_tensor_map(&maps[idx], base, rows, pitch, chunk_words, br);
-    };
-    for (int l = 0; l < L; ++l) {
-        const Layer& Ly = m->L[l];
-        MkPhase p{};
-        // QKV (fused buffer)
-        p = MkPhase{};
-        p.kind = MK_QKV; p.layer = l; p.map = 5 * l; p.rows = qw + 2 * kw; p.cols = H; p.row_align = 2;
-        if (!tile(H, p.rows, false, 2, &p.box_rows)) return NCM_OK;
-        if (mkmap(p.map, Ly.wq.d, p.rows, Ly.wq.pitch, p.box_rows)) return NCM_OK;
-        p.norm_w = Ly.attn_norm; p.out = m->q;
-        p.kcache = m->kc + (size_t)l * m->ctx * kw; p.vcache = m->vc + (size_t)l * m->ctx * kw;
-        p.seg_k = qw; p.seg_v = qw + kw;
-        ph.push_back(p);
-        MkPhase a{};
-        a.kind = MK_ATTN; a.layer = l; a.kcache = p.kcache; a.vcache = p.vcache;
-        ph.push_back(a);
-        p = MkPhase{};
-        p.kind = MK_WO; p.layer = l; p.map = 5 * l + 1; p.rows = H; p.cols = qw; p.row_align = 2;
-        if (!tile(qw, H, false, 2, &p.box_rows)) return NCM_OK;
-        if (mkmap(p.map, Ly.wo.d, H, Ly.wo.pitch, p.box_rows)) return NCM_OK;
-        p.xq = m->att_q; p.xs = m->att_s; p.out = m->hidden;
-        ph.push_back(p);
-        p = MkPhase{};
-        p.kind = MK_W13; p.layer = l; p.map = 5 * l + 2; p.rows = F; p.cols = H; p.row_align = 32;
-        if (!tile(H, F, true, 32, &p.box_rows) || p.box_rows != 32) return NCM_OK;
-        if (mkmap(p.map, Ly.w1.d, F, Ly.w1.pitch, p.box_rows) || mkmap(p.map + 1, Ly.w3.d, F, Ly.w3.pitch, p.box_rows))
-            return NCM_OK;
-        p.norm_w = Ly.ffn_norm; p.out = m->act; p.qout = m->act_q; p.qout_s = m->act_s;
-        ph.push_back(p);
-        p = MkPhase{};
-        p.kind = MK_W2; p.layer = l; p.map = 5 * l + 4; p.rows = H; p.cols = F; p.row_align = 2;
-        if (!tile(F, H, false, 2, &p.box_rows)) return NCM_OK;
-        if (mkmap(p.map, Ly.w2.d, H, Ly.w2.pitch, p.box_rows)) return NCM_OK;
-        p.xq = m->act_q; p.xs = m->act_s; p.out = m->hidden;
-        ph.push_back(p);
-    }
-    MkPhase hp{};
-    hp.kind = MK_HEAD; hp.layer = L; hp.map = 5 * L; hp.rows = m->hr; hp.cols = H; hp.row_align = 2;
-    if (!tile(H, m->hr, false, 2, &hp.box_rows)) return NCM_OK;
-    if (mkmap(hp.map, m->head.d, m->hr, m->head.pitch, hp.box_rows)) return NCM_OK;
-    hp.norm_w = m->out_norm; hp.out = m->logits;
-    ph.push_back(hp);
-    int maxcols = 0;
-    for (MkPhase& p : ph) {
-        if (p.kind == MK_ATTN) continue;
-        p.nb = p.cols / 32;
-        p.nchunk = (p.cols + kChunkCols - 1) / kChunkCols;
-        maxcols = std::max(maxcols, p.cols);
-    }
-    // shared memory: barriers | xq units | xs | xsum | terms (also the f32 RMS input) | ring;
-    // the attention phase uses everything before the ring
-    const int units = (maxcols + kChunkCols - 1) / kChunkCols * kUnits;
-    const int g = m->qh / m->kh;
-    if (g % 2 || g > 8 || m->hd % 32) return NCM_OK;   // the attention items pair query heads
-    const size_t attn_need = mk_attn_bytes(m->ctx);
-    constexpr int kSmemMax = 227 * 1024 - 6 * 1024;   // beside the kernel's static shared memory
-    MkParams& P = m->mk;
-    P = MkParams{};
-    int ns = kMaxStages;
-    for (; ns >= 2; --ns) {
-        int off = 256;
-        P.xq_off = off; off += units * 80;
-        P.xs_off = off; off += units * 8;
-        P.xsum_off = off; off += units * 8;
-        off = (off + 127) / 128 * 128;
-        P.t_off = off;
-        size_t tb = std::max<size_t>((size_t)ns * kMaxFold * kTStride * 4, (size_t)H * 4);
-        if ((size_t)(off - P.xq_off) + tb < attn_need) tb = attn_need - (off - P.xq_off);
-        off += (int)((tb + 127) / 128 * 128);
-        P.stage_off = off;
-        P.attn_bytes = off - P.xq_off;
-        if (off + ns * slot <= kSmemMax) break;
-    }
-    if (ns < 2) return NCM_OK;
-    P.nstages = ns;
-    P.stage_bytes = slot;
-    P.smem_bytes = P.stage_off + ns * slot;
-    // device copies
-    DALLOC(m->mk_maps, sizeof(CUtensorMap) * maps.size());
-    DALLOC(m->mk_phases, sizeof(MkPhase) * ph.size());
-    DALLOC(m->mk_bar, 64);
-    CK(cudaMemcpy(m->mk_maps, maps.data(), sizeof(CUtensorMap) * maps.size(), cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(m->mk_phases, ph.data(), sizeof(MkPhase) * ph.size(), cudaMemcpyHostToDevice));
-    P.maps = m->mk_maps;
-    P.phases = m->mk_phases;
-    P.nphase = (int)ph.size();
-    P.emb = H; P.heads = m->qh; P.kv_heads = m->kh; P.hd = m->hd; P.kvw = kw; P.ctx = m->ctx;
-    P.rope_half = m->rope_dim / 2; P.eps = m->eps; P.attn_scale = 1.0f / sqrtf((float)m->hd);
-    P.rope = m->rope; P.embd_type = m->embd.type; P.embd = m->embd.d; P.embd_pitch = m->embd.pitch;
-    P.ssq_tok = m->embd_ssq; P.hidden = m->hidden; P.q = m->q; P.att = m->att; P.att_q = m->att_q;
-    P.att_s = m->att_s; P.scores = m->scores; P.state = m->state; P.tokens = m->tokens;
-    P.amax_part = m->amax_part; P.amax_cnt = m->amax_cnt; P.head_row0 = m->h0; P.bar = m->mk_bar; P.err = m->err;
-    m->mk_qt = qt;
-    m->mk_on = true;
-    return NCM_OK;
-}
-
 static ncm_status run_step(ncm_model* m, bool with_head, cudaStream_t s) {
     if (host_mode(m)) return enqueue_step(m, with_head, s);
-    if (!m->mk_tried) {
-        ncm_status st = mk_build(m);
-        if (st) return st;
-    }
-    if (with_head && m->mk_on) {
-        CK(cudaMemsetAsync(m->mk_bar, 0, 4, s));
-        CKL(mk_launch(m->mk_qt, m->mk, s));
-        return NCM_OK;
-    }
     CK(cudaGraphLaunch(with_head ? m->g_full : m->g_nohead, s));
     return NCM_OK;
 }

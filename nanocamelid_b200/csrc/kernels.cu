@@ -28,6 +28,7 @@
 #include <mutex>
 #include <set>
 #include <utility>
+#include <type_traits>
 #include "ncm_internal.h"
 #include "common.cuh"
 #include "synth.h"
@@ -668,6 +669,7 @@ __device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, GemvSeqScratch
         float* xf = reinterpret_cast<float*>(smem + p.xf_off);
         stage_f32(xf, p.x, p.cols, tid, blockDim.x);
         __syncthreads();
+        if (tid == 0 && p.dbg_ts) p.dbg_ts[(size_t)blockIdx.x * 16 + 12] = global_timer_ns();
         if constexpr (IN == IN_F32_RMS) {
             float tot;
             if (p.ssq_tok) {
@@ -690,6 +692,7 @@ __device__ void gemv_prologue(uint8_t* smem, const GemvParams& p, GemvSeqScratch
                 }
             }
             scale = 1.0f / sqrtf(tot / (float)p.cols + p.eps);
+            if (tid == 0 && p.dbg_ts) p.dbg_ts[(size_t)blockIdx.x * 16 + 13] = global_timer_ns();
         }
         // Four lanes per 32-value block (quantize_f32_to_q8_0, inference.rs:991-1029):
         // lane li takes elements 8c .. 8c+7 with c = (li + b) & 3 (bank rotation); the
@@ -829,9 +832,10 @@ __device__ void prefetch_next_weights(const GemvParams& p) {
 //   full[s]   (TMA -> compute)            empty[s]  (compute -> producer: stage s reusable)
 //   tfull[s]  (compute -> fold: terms of stage s written)
 //   tempty[s] (fold -> compute: term slot s folded)
-// All eight compute warps work on every stage (warp w takes the row groups 4w .. 4w+3
-// and 32 + 4w .. 32 + 4w+3 of each of the eight 64-column units), so a stage is turned
-// around in a few hundred cycles and the ring keeps its stages in flight on the TMA side.
+// The eight compute warps form p.cgroups groups (4 by default: two warps each); group g
+// works on the stages t with t % cgroups == g, so four stages' dot products are in
+// progress at once and the latency of one stage's shared-memory loads, dp4a chains and
+// term stores overlaps the others' (one group per stage left the SM mostly waiting).
 
 // Measurement probe: when p.dbg_ts is set, per-CTA global-timer stamps (ns) of the
 // pipeline's phases: [0] entry, [1] after the PDL wait, [2] prologue done, [3] last TMA
@@ -871,8 +875,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
     if (tid == 0) {
         for (int s = 0; s < ns; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kComputeThreads / 32);
-            mbar_init(&tfull[s], kComputeThreads / 32);
+            mbar_init(&empty[s], kComputeThreads / 32 / p.cgroups);
+            mbar_init(&tfull[s], kComputeThreads / 32 / p.cgroups);
             mbar_init(&tempty[s], 2);
         }
         fence_mbar_init();
@@ -924,58 +928,68 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
         // kernel's weights into L2 now (its first tiles then come from L2).
         prefetch_next_weights(p);
     } else if (tid < kComputeThreads) {
-        // (3a) compute warps: every warp on every stage.  Lane = (unit u = lane & 7, row
-        // group v0 = lane >> 3); warp w takes the virtual rows v0 + 4 w + 32 j.
-        const int w = tid >> 5, u = lane & 7, v0 = lane >> 3;
-        int t = 0;
+        // (3a) compute warps in G groups of 8/G warps: group gi takes the stages t with
+        // t % G == gi, so G stages are worked on at once.  Lane = (unit u = lane & 7, row
+        // group v0 = lane >> 3); warp wi of the group takes the virtual rows
+        // v0 + 4 wi + (32 / G) j, j < 2 G.
         uint64_t twait = 0, tslot = 0;
-        for (int cur = r_begin; cur < r_end;) {
-            const int n = tile_at(p, cur, r_end).n;
-            const int vrows = DUAL ? 2 * p.box_rows : n;
-            for (int c = 0; c < p.nchunk; ++c, ++t) {
-                const int s = t % ns;
-                const uint32_t use = (uint32_t)(t / ns);
-                const uint64_t tw0 = (p.dbg_ts && tid == 0) ? global_timer_ns() : 0;
-                if (!mbar_wait(&full[s], use & 1, limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
-                if (p.dbg_ts && tid == 0) twait += global_timer_ns() - tw0;
-                const uint64_t tw1 = (p.dbg_ts && tid == 0) ? global_timer_ns() : 0;
-                if (use > 0 && !mbar_wait(&tempty[s], (use - 1) & 1, limit_ns))
-                    set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
-                if (p.dbg_ts && tid == 0) tslot += global_timer_ns() - tw1;
-                const uint8_t* sb = stages + (size_t)s * p.stage_bytes;
-                float* T = tbuf + s * (kMaxFold * kTStride);
-                XUnit x;
-                load_xunit(smem, p, c * kUnits + u, x);
-                constexpr int NJ = 512 / kComputeThreads;   // rows per lane: 64 rows x 8 units per stage
-                const uint8_t* rp[NJ];
-                bool ok[NJ];
-                int vr[NJ];
+        auto compute = [&](auto gc) {
+            constexpr int G = decltype(gc)::value;
+            constexpr int WPG = kComputeThreads / 32 / G;   // warps per group
+            const int w = tid >> 5, gi = w / WPG, wi = w % WPG, u = lane & 7, v0 = lane >> 3;
+            int t = 0;
+            for (int cur = r_begin; cur < r_end;) {
+                const int n = tile_at(p, cur, r_end).n;
+                const int vrows = DUAL ? 2 * p.box_rows : n;
+                for (int c = 0; c < p.nchunk; ++c, ++t) {
+                    if (t % G != gi) continue;
+                    const int s = t % ns;
+                    const uint32_t use = (uint32_t)(t / ns);
+                    const uint64_t tw0 = (p.dbg_ts && tid == 0) ? global_timer_ns() : 0;
+                    if (!mbar_wait(&full[s], use & 1, limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+                    if (p.dbg_ts && tid == 0) twait += global_timer_ns() - tw0;
+                    const uint64_t tw1 = (p.dbg_ts && tid == 0) ? global_timer_ns() : 0;
+                    if (use > 0 && !mbar_wait(&tempty[s], (use - 1) & 1, limit_ns))
+                        set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
+                    if (p.dbg_ts && tid == 0) tslot += global_timer_ns() - tw1;
+                    const uint8_t* sb = stages + (size_t)s * p.stage_bytes;
+                    float* T = tbuf + s * (kMaxFold * kTStride);
+                    XUnit x;
+                    load_xunit(smem, p, c * kUnits + u, x);
+                    constexpr int NJ = 2 * G;
+                    const uint8_t* rp[NJ];
+                    bool ok[NJ];
+                    int vr[NJ];
 #pragma unroll
-                for (int j = 0; j < NJ; ++j) {
-                    vr[j] = v0 + 4 * w + (kComputeThreads / 8) * j;
-                    const int mat = DUAL ? (vr[j] >= p.box_rows) : 0;
-                    const int r = vr[j] - mat * p.box_rows;
-                    ok[j] = vr[j] < vrows && r < n;
-                    rp[j] = sb + mat * box2_off + (ok[j] ? r : 0) * p.chunk_bytes;
-                }
-                float t0[NJ], t1[NJ];
-                unit_terms_n<QT, NJ>(rp, u, x, t0, t1);
+                    for (int j = 0; j < NJ; ++j) {
+                        vr[j] = v0 + 4 * wi + (32 / G) * j;
+                        const int mat = DUAL ? (vr[j] >= p.box_rows) : 0;
+                        const int r = vr[j] - mat * p.box_rows;
+                        ok[j] = vr[j] < vrows && r < n;
+                        rp[j] = sb + mat * box2_off + (ok[j] ? r : 0) * p.chunk_bytes;
+                    }
+                    float t0[NJ], t1[NJ];
+                    unit_terms_n<QT, NJ>(rp, u, x, t0, t1);
 #pragma unroll
-                for (int j = 0; j < NJ; ++j) {
-                    if (ok[j]) {
-                        float* trow = T + vr[j] * kTStride;
-                        trow[2 * u] = t0[j];
-                        trow[2 * u + 1] = t1[j];
+                    for (int j = 0; j < NJ; ++j) {
+                        if (ok[j]) {
+                            float* trow = T + vr[j] * kTStride;
+                            trow[2 * u] = t0[j];
+                            trow[2 * u + 1] = t1[j];
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&empty[s]);
+                        mbar_arrive(&tfull[s]);
                     }
                 }
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&empty[s]);
-                    mbar_arrive(&tfull[s]);
-                }
+                cur += n;
             }
-            cur += n;
-        }
+        };
+        if (p.cgroups == 4) compute(std::integral_constant<int, 4>{});
+        else if (p.cgroups == 2) compute(std::integral_constant<int, 2>{});
+        else compute(std::integral_constant<int, 1>{});
         if (tid == 0 && p.dbg_ts) { NCM_TS(7, twait); NCM_TS(8, tslot); NCM_TS(11, global_timer_ns()); }
     } else if (tid < kProducer) {
         // (3b) fold warps: sequential per-row sums in block order, then the epilogue.
@@ -1227,6 +1241,7 @@ int gemv_plan(int qtype, int cols, int rows, bool dual, int in_mode, GemvParams&
     p.chunk_words = p.chunk_bytes / 4;
     p.total_rows = rows;
     int grid = num_sms();
+    if (p.cgroups != 1 && p.cgroups != 2 && p.cgroups != 4) p.cgroups = 4;
     if (p.row_align < 2) p.row_align = 2;
     const int ra = p.row_align;
     int maxg = (rows + ra - 1) / ra;
@@ -1480,11 +1495,20 @@ __device__ void attn_softmax_body(const AttnParams& a, int h, int tz, float* e, 
     const int n = pos + 1;
     const int tid = threadIdx.x & 255, warp = tid >> 5, lane = tid & 31;
     float* srow = a.scores + ((size_t)tz * a.heads + h) * a.ctx;
+    constexpr int kReg = 8;   // rows up to 2048 positions stay in registers
+    float r[kReg];
     float mx = -INFINITY;
-    for (int p = tid; p < n; p += 256) {
-        const float v = __ldcg(&srow[p]);
-        e[p] = v;
-        mx = fmaxf(mx, v);   // max is order independent (no NaNs)
+    if (n <= kReg * 256) {
+#pragma unroll
+        for (int k = 0; k < kReg; ++k) r[k] = tid + 256 * k < n ? __ldcg(&srow[tid + 256 * k]) : -INFINITY;
+#pragma unroll
+        for (int k = 0; k < kReg; ++k) mx = fmaxf(mx, r[k]);   // max is order independent (no NaNs)
+    } else {
+        for (int p = tid; p < n; p += 256) {
+            const float v = __ldcg(&srow[p]);
+            e[p] = v;
+            mx = fmaxf(mx, v);
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(NCM_FULL, mx, o));
@@ -1493,11 +1517,26 @@ __device__ void attn_softmax_body(const AttnParams& a, int h, int tz, float* e, 
     mx = red[0];
 #pragma unroll
     for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
-    for (int p = tid; p < n; p += 256) e[p] = expf_cr(e[p] - mx);
+    if (n <= kReg * 256) {
+#pragma unroll
+        for (int k = 0; k < kReg; ++k)
+            if (tid + 256 * k < n) {
+                r[k] = expf_cr(r[k] - mx);
+                e[tid + 256 * k] = r[k];
+            }
+    } else {
+        for (int p = tid; p < n; p += 256) e[p] = expf_cr(e[p] - mx);
+    }
     group_sync<256, BAR>();
     const float sum = seq_sum_nonneg<256, BAR>([&](int i) { return e[i]; }, n, sc, tid);
     const float inv = 1.0f / sum;
-    for (int p = tid; p < n; p += 256) srow[p] = e[p] * inv;
+    if (n <= kReg * 256) {
+#pragma unroll
+        for (int k = 0; k < kReg; ++k)
+            if (tid + 256 * k < n) srow[tid + 256 * k] = r[k] * inv;
+    } else {
+        for (int p = tid; p < n; p += 256) srow[p] = e[p] * inv;
+    }
 }
 
 __global__ void __launch_bounds__(256) attn_softmax_kernel(const __grid_constant__ AttnParams a) {
@@ -1583,14 +1622,19 @@ __device__ void attn_av_body(const AttnParams& a, int kvh, int db, int hgrp, int
         const float* ws = vs + kAvChunk * 32 + warp * kAvChunk;
         const int np = min(kAvChunk, n - k * kAvChunk);
         int p = 0;
-        for (; p + 4 <= np; p += 4) {
-            const float4 w4 = *reinterpret_cast<const float4*>(ws + p);
-            const float v0 = vs[p * 32 + lane], v1 = vs[(p + 1) * 32 + lane];
-            const float v2 = vs[(p + 2) * 32 + lane], v3 = vs[(p + 3) * 32 + lane];
-            acc += w4.x * v0;
-            acc += w4.y * v1;
-            acc += w4.z * v2;
-            acc += w4.w * v3;
+        // 16 positions a step, every shared-memory load issued before the first add (the
+        // adds stay in position order)
+        for (; p + 16 <= np; p += 16) {
+            float wv[16], vv[16];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 w4 = *reinterpret_cast<const float4*>(ws + p + 4 * q);
+                wv[4 * q] = w4.x; wv[4 * q + 1] = w4.y; wv[4 * q + 2] = w4.z; wv[4 * q + 3] = w4.w;
+            }
+#pragma unroll
+            for (int q = 0; q < 16; ++q) vv[q] = vs[(p + q) * 32 + lane];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) acc += wv[q] * vv[q];
         }
         for (; p < np; ++p) acc += ws[p] * vs[p * 32 + lane];
         group_sync<NT, BAR>();                   // the slot may be refilled
@@ -2855,556 +2899,4 @@ int q6k_gemv_launch(int epi, const Q6Params& p, cudaStream_t s, bool pdl) {
     return (int)cudaErrorInvalidValue;
 }
 
-// ================================================================== persistent decode kernel
-// One launch = one decode token: for every layer the phases QKV, ATTN, WO, W13, W2, then
-// the head, each the same computation as the per-phase kernels above (same partition of
-// rows, same tiles, same fold order, same epilogues), so the results are bit-identical.
-// One CTA per SM runs all phases; between phases a grid-wide barrier (a counter in global
-// memory) orders the epilogues' global writes before the next phase's reads, which go
-// through L2 (ld.global.cg) since L1 is not coherent across SMs.  The producer warp
-// never waits on those barriers: it walks the whole token's tile sequence and keeps the
-// TMA ring full, so the weight stream runs on through every barrier, prologue and
-// attention phase (the gaps between kernel launches disappear).
-// Named barriers: 2 = prologue (compute + fold warps, 320 threads), 3 = grid-barrier
-// entry / exit (320), 4 = attention items (compute warps, 256), 1 = the fold warps.
-constexpr int kMkThreads = kProducer;   // compute + fold threads
-constexpr int kMkSoftmaxScratch = ((int)sizeof(SeqSumScratch) + 127) / 128 * 128;
-
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void mk_range(int rows, int align, int& r0, int& r1) {
-    const int nbk = gridDim.x;
-    r0 = (int)(((long long)blockIdx.x * rows / nbk)) & ~(align - 1);
-    r1 = (blockIdx.x + 1 == nbk) ? rows : ((int)(((long long)(blockIdx.x + 1) * rows / nbk)) & ~(align - 1));
-}
-
-// Grid-wide barrier number k (1, 2, ...) of this launch for the 320 compute / fold
-// threads of every CTA.  False once any device wait of the launch has failed.
-__device__ bool mk_grid_sync(const MkParams& P, unsigned k, int* s_abort) {
-    group_sync<kMkThreads, 3>();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(P.bar, 1u);
-        const unsigned target = k * gridDim.x;
-        if (ld_acquire_gpu(P.bar) < target) {
-            const uint64_t t0 = global_timer_ns();
-            for (uint32_t i = 1;; ++i) {
-                if (ld_acquire_gpu(P.bar) >= target) break;
-                if ((i & 255u) == 0 && global_timer_ns() - t0 > 4000000000ull) {
-                    set_dev_error(P.err, NCM_DEVERR_MBAR_TIMEOUT);
-                    break;
-                }
-            }
-        }
-        *s_abort = *reinterpret_cast<volatile int*>(P.err) != 0;
-    }
-    group_sync<kMkThreads, 3>();
-    return !*s_abort;
-}
-
-// Prologue of a GEMV phase (320 threads): the activation as Q8_0 units in shared memory.
-// RMS phases (QKV, W13, HEAD) normalise the hidden state (layer 0's QKV: the embedding
-// row, dequantised here, whose sum of squares is the per-token table); WO / W2 copy the
-// producer phase's Q8_0 blocks.
-__device__ void mk_prologue(const MkParams& P, const MkPhase& F, uint8_t* smem, SeqSumScratchT<kMkThreads>& sc) {
-    const int tid = threadIdx.x;
-    const int nblk = F.nchunk * 16;
-    float2* xs = reinterpret_cast<float2*>(smem + P.xs_off);
-    int2* xsum = reinterpret_cast<int2*>(smem + P.xsum_off);
-    if (F.kind == MK_WO || F.kind == MK_W2) {
-        for (int g = tid; g < nblk / 2; g += kMkThreads) {
-            uint4* dst = reinterpret_cast<uint4*>(smem + P.xq_off + 80 * g);
-            if (2 * g < F.nb) {
-                const bool two = 2 * g + 1 < F.nb;
-                const uint4* src = reinterpret_cast<const uint4*>(F.xq + 64 * g);
-                int s0 = 0, s1 = 0;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint4 v = (i < 2 || two) ? __ldcg(src + i) : make_uint4(0, 0, 0, 0);
-                    dst[i] = v;
-                    int a = i < 2 ? s0 : s1;
-                    a = __dp4a((int)v.x, 0x01010101, a);
-                    a = __dp4a((int)v.y, 0x01010101, a);
-                    a = __dp4a((int)v.z, 0x01010101, a);
-                    a = __dp4a((int)v.w, 0x01010101, a);
-                    if (i < 2) s0 = a; else s1 = a;
-                }
-                xs[g] = make_float2(__ldcg(&F.xs[2 * g]), two ? __ldcg(&F.xs[2 * g + 1]) : 0.0f);
-                xsum[g] = make_int2(s0, s1);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) dst[i] = make_uint4(0, 0, 0, 0);
-                xs[g] = make_float2(0.0f, 0.0f);
-                xsum[g] = make_int2(0, 0);
-            }
-        }
-        group_sync<kMkThreads, 2>();
-        return;
-    }
-    // RMS phases: x = hidden (f32, cols = emb) staged through L2 into the term region
-    float* xf = reinterpret_cast<float*>(smem + P.t_off);
-    const int n = F.cols;
-    float tot;
-    if (F.kind == MK_QKV && F.layer == 0) {
-        // inference.rs:4494-4503 embed_token: the token's row, dequantised; this CTA also
-        // writes the hidden rows it owns in the row-parallel phases (their residual)
-        const int tok = __ldcg(&P.tokens[__ldcg(&P.state[ST_POS])]);
-        const uint8_t* row = P.embd + (size_t)tok * P.embd_pitch;
-        for (int i = tid; i < n; i += kMkThreads) xf[i] = dequant_elem(P.embd_type, row, i);
-        int h0, h1;
-        mk_range(P.emb, 2, h0, h1);
-        for (int i = h0 + tid; i < h1; i += kMkThreads) P.hidden[i] = dequant_elem(P.embd_type, row, i);
-        group_sync<kMkThreads, 2>();
-        tot = __ldg(&P.ssq_tok[tok]);
-    } else {
-        const float4* src = reinterpret_cast<const float4*>(P.hidden);
-        for (int i = tid; i < n / 4; i += kMkThreads) reinterpret_cast<float4*>(xf)[i] = __ldcg(src + i);
-        group_sync<kMkThreads, 2>();
-        // inference.rs:698-701: sum += val * val, sequential (exact, seq_sum_nonneg)
-        tot = seq_sum_nonneg<kMkThreads, 2>([&](int i) { const float v = xf[i]; return v * v; }, n, sc, tid);
-    }
-    const float scale = 1.0f / sqrtf(tot / (float)n + P.eps);
-    // quantize_f32_to_q8_0 of x * scale * w (inference.rs:704, 991-1029), four lanes per block
-    const int li = tid & 3;
-    const unsigned qmask = 0xFu << (tid & 28);
-    for (int b = tid >> 2; b < nblk; b += kMkThreads >> 2) {
-        uint32_t* dst = reinterpret_cast<uint32_t*>(smem + P.xq_off + 80 * (b >> 1) + 32 * (b & 1));
-        const int c = (li + b) & 3;
-        if (b < F.nb) {
-            float v[8];
-            const float4* xb = reinterpret_cast<const float4*>(xf) + 8 * b + 2 * c;
-            const float4* wb = reinterpret_cast<const float4*>(F.norm_w) + 8 * b + 2 * c;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const float4 x4 = xb[h], w4 = __ldg(wb + h);
-                v[4 * h] = x4.x * scale * w4.x;
-                v[4 * h + 1] = x4.y * scale * w4.y;
-                v[4 * h + 2] = x4.z * scale * w4.z;
-                v[4 * h + 3] = x4.w * scale * w4.w;
-            }
-            float amax = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-            amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 1));
-            amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 2));
-            const float scale_b = amax / 127.0f;
-            uint32_t w0 = 0, w1 = 0;
-            int sum = 0;
-            if (scale_b > 0.0f) {
-                const float inv = 1.0f / scale_b;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    float q = roundf(v[i] * inv);
-                    q = fminf(fmaxf(q, -127.0f), 127.0f);
-                    const int qi = (int)q;
-                    sum += qi;
-                    const uint32_t byte = (uint32_t)(qi & 0xff) << (8 * (i & 3));
-                    if (i < 4) w0 |= byte; else w1 |= byte;
-                }
-            }
-            sum += __shfl_xor_sync(qmask, sum, 1);
-            sum += __shfl_xor_sync(qmask, sum, 2);
-            dst[2 * c] = w0;
-            dst[2 * c + 1] = w1;
-            if (li == 0) {
-                reinterpret_cast<float*>(xs)[b] = scale_b;
-                reinterpret_cast<int*>(xsum)[b] = sum;
-            }
-        } else {
-            dst[2 * c] = 0;
-            dst[2 * c + 1] = 0;
-            if (li == 0) {
-                reinterpret_cast<float*>(xs)[b] = 0.0f;
-                reinterpret_cast<int*>(xsum)[b] = 0;
-            }
-        }
-    }
-    group_sync<kMkThreads, 2>();
-}
-
-__device__ __forceinline__ void mk_load_xunit(const uint8_t* smem, const MkParams& P, int g, XUnit& x) {
-    const uint4* src = reinterpret_cast<const uint4*>(smem + P.xq_off + 80 * g);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint4 v = src[i];
-        x.w[4 * i] = v.x; x.w[4 * i + 1] = v.y; x.w[4 * i + 2] = v.z; x.w[4 * i + 3] = v.w;
-    }
-    const float2 sv = reinterpret_cast<const float2*>(smem + P.xs_off)[g];
-    const int2 cv = reinterpret_cast<const int2*>(smem + P.xsum_off)[g];
-    x.s[0] = sv.x; x.s[1] = sv.y;
-    x.sum[0] = cv.x; x.sum[1] = cv.y;
-}
-
-template <int QT>
-__global__ void __launch_bounds__(kGemvThreads, 1) ncm_decode_kernel(const __grid_constant__ MkParams P) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ SeqSumScratchT<kMkThreads> sc;
-    __shared__ float xchg[kMaxFold];
-    __shared__ float wv[2];
-    __shared__ int wi[2];
-    __shared__ int s_last, s_abort;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + 8;
-    uint64_t* tfull = full + 16;
-    uint64_t* tempty = full + 24;
-    float* tbuf = reinterpret_cast<float*>(smem + P.t_off);
-    uint8_t* stages = smem + P.stage_off;
-    const int tid = threadIdx.x, lane = tid & 31;
-    const int ns = P.nstages;
-    const uint64_t limit_ns = 4000000000ull;
-    const int chunk_bytes = QT == NCM_T_Q8_0 ? 16 * 34 : 288;
-    const int chunk_words = chunk_bytes / 4;
-    if (tid == 0) {
-        for (int s = 0; s < ns; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kComputeThreads / 32);
-            mbar_init(&tfull[s], kComputeThreads / 32);
-            mbar_init(&tempty[s], 2);
-        }
-        fence_mbar_init();
-        s_abort = 0;
-    }
-    __syncthreads();
-
-    if (tid == kProducer) {
-        // ---- producer: the token's whole tile sequence, never waiting on grid barriers
-        const uint64_t pol = l2_evict_first_policy();
-        int t = 0;
-        bool stop = false;
-        for (int ph = 0; ph < P.nphase && !stop; ++ph) {
-            const MkPhase& F = P.phases[ph];
-            if (F.kind == MK_ATTN) continue;
-            const bool dual = F.kind == MK_W13;
-            const int box_bytes = F.box_rows * chunk_bytes;
-            const int box2_off = (box_bytes + 127) & ~127;
-            int r0, r1;
-            mk_range(F.rows, F.row_align, r0, r1);
-            for (int cur = r0; cur < r1 && !stop;) {
-                const int n = min(F.box_rows, r1 - cur);
-                for (int c = 0; c < F.nchunk; ++c, ++t) {
-                    const int s = t % ns;
-                    if (t >= ns && !mbar_wait(&empty[s], (uint32_t)(((t / ns) & 1) ^ 1), limit_ns)) {
-                        set_dev_error(P.err, NCM_DEVERR_MBAR_TIMEOUT);
-                        stop = true;
-                        break;
-                    }
-                    if (*reinterpret_cast<volatile int*>(P.err)) { stop = true; break; }
-                    mbar_arrive_expect_tx(&full[s], dual ? 2 * box_bytes : box_bytes);
-                    tma_load_2d(stages + (size_t)s * P.stage_bytes, &P.maps[F.map], c * chunk_words, cur, &full[s], pol);
-                    if (dual)
-                        tma_load_2d(stages + (size_t)s * P.stage_bytes + box2_off, &P.maps[F.map + 1], c * chunk_words,
-                                    cur, &full[s], pol);
-                }
-                cur += n;
-            }
-        }
-        if (stop) {
-            // wait (bounded) for every load still in flight before the CTA may exit
-            for (int k = max(0, t - ns); k < t; ++k) mbar_wait(&full[k % ns], (uint32_t)((k / ns) & 1), 100000000ull);
-        }
-    } else if (tid < kProducer) {
-        // ---- compute (warps 0-7) and fold (warps 8-9) through every phase
-        const bool is_fold = tid >= kFoldBase;
-        const int w = tid >> 5, u = lane & 7, v0 = lane >> 3, f = tid - kFoldBase;
-        int t = 0;
-        unsigned nbar = 0;
-        const int pos = __ldcg(&P.state[ST_POS]);
-        for (int ph = 0; ph < P.nphase; ++ph) {
-            const MkPhase& F = P.phases[ph];
-            if (ph > 0 && !mk_grid_sync(P, ++nbar, &s_abort)) break;
-            if (F.kind == MK_ATTN) {
-                // attention (inference.rs:4142-4292) by the compute warps, the three stages of
-                // attention_launch with grid barriers between them: score tiles, one softmax
-                // per query head, then the V items (by the first two warps of each CTA)
-                AttnParams a;
-                memset(&a, 0, sizeof a);
-                a.q = P.q; a.kc = F.kcache; a.vc = F.vcache; a.scores = P.scores; a.out = P.att;
-                a.state = P.state; a.pos_override = -1; a.heads = P.heads; a.kv_heads = P.kv_heads; a.hd = P.hd;
-                a.kvw = P.kvw; a.ctx = P.ctx; a.scale = P.attn_scale;
-                a.ntok = 1; a.tok_stride = 0; a.out_q = P.att_q; a.out_s = P.att_s; a.kv_kind = KV_F32;
-                a.kc_raw = F.kcache; a.vc_raw = F.vcache;
-                float* qs = reinterpret_cast<float*>(smem + P.xq_off);
-                float* ks = qs + 8 * 256;
-                const int ntile = (pos + 1 + 31) / 32;
-                if (!is_fold) {
-                    for (int it = blockIdx.x; it < P.kv_heads * ntile; it += gridDim.x) {
-                        attn_scores_body<4>(a, it % P.kv_heads, it / P.kv_heads, 0, qs, ks);
-                        group_sync<256, 4>();
-                    }
-                }
-                if (!mk_grid_sync(P, ++nbar, &s_abort)) break;
-                if (!is_fold) {
-                    SeqSumScratch* ssc = reinterpret_cast<SeqSumScratch*>(smem + P.xq_off);
-                    float* red = reinterpret_cast<float*>(smem + P.xq_off + kMkSoftmaxScratch);
-                    float* e = red + 32;
-                    for (int it = blockIdx.x; it < P.heads; it += gridDim.x) {
-                        attn_softmax_body<4>(a, it, 0, e, *ssc, red);
-                        group_sync<256, 4>();
-                    }
-                }
-                if (!mk_grid_sync(P, ++nbar, &s_abort)) break;
-                if (tid < 64) {
-                    float* buf = reinterpret_cast<float*>(smem + P.xq_off);
-                    const int nd = P.hd / 32, g = P.heads / P.kv_heads;
-                    const int items = P.kv_heads * nd * (g / 2);
-                    for (int it = blockIdx.x; it < items; it += gridDim.x) {
-                        const int kvh = it % P.kv_heads, r = it / P.kv_heads;
-                        attn_av_body<2, 5>(a, kvh, r % nd, r / nd, 0, buf, tid);
-                    }
-                }
-                continue;
-            }
-            // ---- a GEMV phase
-            mk_prologue(P, F, smem, sc);
-            const bool dual = F.kind == MK_W13;
-            const int box_bytes = F.box_rows * chunk_bytes;
-            const int box2_off = (box_bytes + 127) & ~127;
-            int r0, r1;
-            mk_range(F.rows, F.row_align, r0, r1);
-            if (!is_fold) {
-                for (int cur = r0; cur < r1;) {
-                    const int n = min(F.box_rows, r1 - cur);
-                    const int vrows = dual ? 2 * F.box_rows : n;
-                    for (int c = 0; c < F.nchunk; ++c, ++t) {
-                        const int s = t % ns;
-                        const uint32_t use = (uint32_t)(t / ns);
-                        if (!mbar_wait(&full[s], use & 1, limit_ns)) set_dev_error(P.err, NCM_DEVERR_MBAR_TIMEOUT);
-                        if (use > 0 && !mbar_wait(&tempty[s], (use - 1) & 1, limit_ns))
-                            set_dev_error(P.err, NCM_DEVERR_MBAR_TIMEOUT);
-                        const uint8_t* sb = stages + (size_t)s * P.stage_bytes;
-                        float* T = tbuf + s * (kMaxFold * kTStride);
-                        XUnit x;
-                        mk_load_xunit(smem, P, c * kUnits + u, x);
-                        const uint8_t* rp[2];
-                        bool ok[2];
-                        int vr[2];
-#pragma unroll
-                        for (int j = 0; j < 2; ++j) {
-                            vr[j] = v0 + 4 * w + 32 * j;
-                            const int mat = dual ? (vr[j] >= F.box_rows) : 0;
-                            const int r = vr[j] - mat * F.box_rows;
-                            ok[j] = vr[j] < vrows && r < n;
-                            rp[j] = sb + mat * box2_off + (ok[j] ? r : 0) * chunk_bytes;
-                        }
-                        float t0[2], t1[2];
-                        unit_terms_n<QT, 2>(rp, u, x, t0, t1);
-#pragma unroll
-                        for (int j = 0; j < 2; ++j) {
-                            if (ok[j]) {
-                                float* trow = T + vr[j] * kTStride;
-                                trow[2 * u] = t0[j];
-                                trow[2 * u + 1] = t1[j];
-                            }
-                        }
-                        __syncwarp();
-                        if (lane == 0) {
-                            mbar_arrive(&empty[s]);
-                            mbar_arrive(&tfull[s]);
-                        }
-                    }
-                    cur += n;
-                }
-            } else {
-                float best_v = -INFINITY;
-                int best_i = 0x7fffffff;
-                const int nsb = F.nb / 8;
-                for (int cur = r0; cur < r1;) {
-                    const int n = min(F.box_rows, r1 - cur);
-                    const bool live = dual ? (f < 2 * F.box_rows && (f % F.box_rows) < n) : (f < n);
-                    float acc = 0.0f;
-                    const float* trow0 = tbuf + f * kTStride;
-                    for (int c = 0; c < F.nchunk; ++c, ++t) {
-                        const int s = t % ns;
-                        const uint32_t use = (uint32_t)(t / ns);
-                        if (!mbar_wait(&tfull[s], use & 1, limit_ns)) set_dev_error(P.err, NCM_DEVERR_MBAR_TIMEOUT);
-                        if (live) {
-                            const float* trow = trow0 + s * (kMaxFold * kTStride);
-                            float tv[16];
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) tv[j] = trow[j];
-                            asm volatile("" ::: "memory");
-                            if constexpr (QT == NCM_T_Q4_K) {
-                                const int nsbc = min(2, nsb - 2 * c);
-#pragma unroll
-                                for (int q = 0; q < 2; ++q) {
-                                    if (q < nsbc) {
-                                        float ssum = 0.0f;   // q8.rs:1342
-#pragma unroll
-                                        for (int j = 0; j < 8; ++j) ssum += tv[8 * q + j];
-                                        acc += ssum;         // inference.rs:3129
-                                    }
-                                }
-                            } else {
-                                const int nbc = min(16, F.nb - 16 * c);
-                                if (nbc == 16) {
-#pragma unroll
-                                    for (int j = 0; j < 16; ++j) acc += tv[j];
-                                } else {
-#pragma unroll
-                                    for (int j = 0; j < 16; ++j)
-                                        if (j < nbc) acc += tv[j];
-                                }
-                            }
-                        }
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&tempty[s]);
-                    }
-                    // tile epilogue: the per-phase kernels' epilogues
-                    if (F.kind == MK_QKV) {
-                        const float other = __shfl_xor_sync(NCM_FULL, acc, 1);
-                        if (f < n) {
-                            const int row = cur + f;
-                            const int kind = row >= F.seg_v ? SEG_V : (row >= F.seg_k ? SEG_K : SEG_Q);
-                            const int lr = row - (kind == SEG_V ? F.seg_v : (kind == SEG_K ? F.seg_k : 0));
-                            float v = acc;
-                            if (kind != SEG_V) {
-                                // inference.rs:904-933 apply_rope_cached, NORM pairs (2i, 2i+1)
-                                const int i = (lr % P.hd) >> 1;
-                                if (i < P.rope_half) {
-                                    const float2 scs = P.rope[(size_t)pos * P.rope_half + i];
-                                    const float x0 = (f & 1) ? other : acc;
-                                    const float x1 = (f & 1) ? acc : other;
-                                    v = (f & 1) ? (x0 * scs.x + x1 * scs.y) : (x0 * scs.y - x1 * scs.x);
-                                }
-                            }
-                            if (kind == SEG_Q) F.out[lr] = v;
-                            else ((kind == SEG_K ? F.kcache : F.vcache) + (size_t)pos * P.kvw)[lr] = v;
-                        }
-                    } else if (F.kind == MK_W13) {
-                        if (f >= F.box_rows && f < F.box_rows + n) xchg[f - F.box_rows] = acc;
-                        asm volatile("bar.sync 1, 64;" ::: "memory");
-                        float o = 0.0f;
-                        if (f < n) {
-                            const float g = acc, uu = xchg[f];
-                            const float sig = 1.0f / (1.0f + expf_cr(-g));   // inference.rs:3385-3388
-                            o = g * sig * uu;
-                            F.out[cur + f] = o;
-                        }
-                        if (f < 32) {
-                            // 32-row tile (box_rows 32, 32-aligned ranges): one Q8_0 block for w2
-                            float amax = fabsf(o);
-#pragma unroll
-                            for (int k = 16; k > 0; k >>= 1) amax = fmaxf(amax, __shfl_xor_sync(NCM_FULL, amax, k));
-                            const float scale = amax / 127.0f;
-                            int q = 0;
-                            if (scale > 0.0f) {
-                                const float inv = 1.0f / scale;
-                                q = (int)fminf(fmaxf(roundf(o * inv), -127.0f), 127.0f);
-                            }
-                            F.qout[cur + f] = (int8_t)q;
-                            if (f == 0) F.qout_s[cur >> 5] = scale;
-                        }
-                        asm volatile("bar.sync 1, 64;" ::: "memory");
-                    } else if (F.kind == MK_HEAD) {
-                        if (f < n) {
-                            const int lr = cur + f;
-                            if (F.out) F.out[lr] = acc;
-                            if (better(acc, lr, best_v, best_i)) { best_v = acc; best_i = lr; }
-                        }
-                    } else if (f < n) {
-                        float* h = F.out + cur + f;
-                        *h = __ldcg(h) + acc;   // inference.rs:4670-4672 / 4744-4746
-                    }
-                    cur += n;
-                }
-                if (F.kind == MK_HEAD) {
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) {
-                        const float ov = __shfl_xor_sync(NCM_FULL, best_v, o);
-                        const int oi = __shfl_xor_sync(NCM_FULL, best_i, o);
-                        if (better(ov, oi, best_v, best_i)) { best_v = ov; best_i = oi; }
-                    }
-                    if (lane == 0) { wv[f >> 5] = best_v; wi[f >> 5] = best_i; }
-                    asm volatile("bar.sync 1, 64;" ::: "memory");
-                    if (f == 0) {
-                        // CTA first-max, then the last CTA merges every CTA's (inference.rs:4838-4843)
-                        float bv = wv[0];
-                        int bi = wi[0];
-                        if (better(wv[1], wi[1], bv, bi)) { bv = wv[1]; bi = wi[1]; }
-                        P.amax_part[blockIdx.x] = make_float2(bv, __int_as_float(bi));
-                        __threadfence();
-                        const unsigned prev = atomicAdd(P.amax_cnt, 1u);
-                        if (prev == gridDim.x - 1) {
-                            __threadfence();
-                            bv = -INFINITY;
-                            bi = 0x7fffffff;
-                            for (int c = 0; c < (int)gridDim.x; ++c) {
-                                const float2 e = __ldcg(&P.amax_part[c]);
-                                const int ei = __float_as_int(e.y);
-                                if (better(e.x, ei, bv, bi)) { bv = e.x; bi = ei; }
-                            }
-                            const int tok = P.head_row0 + bi;
-                            if (pos + 1 < P.ctx && pos + 1 >= P.state[ST_NPROMPT]) P.tokens[pos + 1] = tok;
-                            P.state[ST_LAST_TOKEN] = tok;
-                            P.state[ST_POS] = pos + 1;
-                            P.state[ST_STEP] = P.state[ST_STEP] + 1;
-                            *P.amax_cnt = 0u;
-                        }
-                    }
-                }
-            }
-        }
-    }
-    __syncthreads();
-}
-
-bool mk_box_rows(int qtype, int cols, int rows, bool dual, int row_align, int slot_bytes, int* box_rows) {
-    // the tiling of gemv_plan, for one CTA per SM
-    const int chunk_bytes = qtype == NCM_T_Q8_0 ? 16 * 34 : 288;
-    int grid = num_sms();
-    const int ra = row_align < 2 ? 2 : row_align;
-    const int maxg = std::max(1, (rows + ra - 1) / ra);
-    if (grid > maxg) grid = maxg;
-    const int per_cta = (rows + grid - 1) / grid;
-    int maxr = qtype == NCM_T_Q8_0 ? 32 : 64;
-    if (dual) maxr /= 2;
-    const int span = per_cta + ra;
-    const int ntiles = (span + maxr - 1) / maxr;
-    int br = (span + ntiles - 1) / ntiles;
-    br = (br + ra - 1) / ra * ra;
-    if (br > maxr) br = maxr;
-    if (br < 2) br = 2;
-    const int need = (br * chunk_bytes + 127) / 128 * 128 * (dual ? 2 : 1);
-    if (need > slot_bytes) return false;
-    *box_rows = br;
-    (void)cols;
-    return true;
-}
-
-size_t mk_attn_bytes(int ctx) {
-    const size_t scores = 4 * (8 * 256 + 32 * 257);
-    const size_t softmax = kMkSoftmaxScratch + 32 * 4 + (size_t)ctx * 4;
-    const size_t av = (size_t)kAvStages * av_stage_floats(2) * 4;
-    return std::max(scores, std::max(softmax, av));
-}
-
-int mk_launch(int qtype, const MkParams& p, cudaStream_t s) {
-    const void* fn = qtype == NCM_T_Q4_0 ? (const void*)ncm_decode_kernel<NCM_T_Q4_0>
-                   : qtype == NCM_T_Q8_0 ? (const void*)ncm_decode_kernel<NCM_T_Q8_0>
-                                         : (const void*)ncm_decode_kernel<NCM_T_Q4_K>;
-    // the limit is per kernel and device, set once: the largest the static part leaves
-    cudaFuncAttributes fa{};
-    if (cudaError_t e = cudaFuncGetAttributes(&fa, fn)) return (int)e;
-    const int room = 227 * 1024 - (int)fa.sharedSizeBytes;
-    if (p.smem_bytes > room) return (int)cudaErrorInvalidValue;
-    if (int r = set_smem_limit(fn, room)) return r;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(num_sms());
-    cfg.blockDim = dim3(kGemvThreads);
-    cfg.dynamicSmemBytes = p.smem_bytes;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;   // every CTA resident (grid barriers)
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (qtype == NCM_T_Q4_0) return (int)cudaLaunchKernelEx(&cfg, ncm_decode_kernel<NCM_T_Q4_0>, p);
-    if (qtype == NCM_T_Q8_0) return (int)cudaLaunchKernelEx(&cfg, ncm_decode_kernel<NCM_T_Q8_0>, p);
-    if (qtype == NCM_T_Q4_K) return (int)cudaLaunchKernelEx(&cfg, ncm_decode_kernel<NCM_T_Q4_K>, p);
-    return (int)cudaErrorInvalidValue;
-}
 }  // namespace ncm

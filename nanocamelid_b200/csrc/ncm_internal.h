@@ -91,6 +91,7 @@ struct alignas(64) GemvParams {
                                   //    F16 / Q8_0 cache), 0: the f32 cache rows at pos
     int row_align;                // CTA row ranges start at multiples of this (2, or 32 with qout)
     int tune;                     // measurement knobs (0 in normal use)
+    int cgroups;                  // compute-warp groups (1, 2 or 4; 0: 4): stages worked on at once
     uint64_t* dbg_ts;             // measurement probe: per-CTA phase stamps [grid][8] (null in normal use)
     int8_t* qout;                 // EPI_SILU: the output rows also as Q8_0 blocks (box_rows == 32) ...
     float* qout_s;                //   ... and their scales: the next projection's quantised input
@@ -183,54 +184,6 @@ struct Q6Params {
     int ctx;
 };
 
-// Persistent decode kernel: one launch runs a whole token (every layer's GEMVs and
-// attention, then the head) on one CTA per SM, with grid-wide barriers between phases and
-// the weight ring streaming across them.
-enum MkKind { MK_QKV = 0, MK_ATTN = 1, MK_WO = 2, MK_W13 = 3, MK_W2 = 4, MK_HEAD = 5 };
-struct MkPhase {
-    int kind, layer;
-    int map;                      // tensor map index (MK_W13: gate at map, up at map + 1)
-    int rows, cols, nb, nchunk, box_rows, row_align;
-    const float* norm_w;          // QKV / W13 / HEAD: RMS weights
-    const int8_t* xq;             // WO / W2: the producing phase's Q8_0 output
-    const float* xs;
-    float* out;                   // QKV: q, WO / W2: hidden, W13: act, HEAD: logits
-    int8_t* qout;                 // W13: act as Q8_0
-    float* qout_s;
-    float* kcache;                // QKV / ATTN: this layer's caches [ctx][kv_width]
-    float* vcache;
-    int seg_k, seg_v;             // QKV: first k row and first v row of the fused row space
-};
-struct MkParams {
-    const CUtensorMap* maps;      // device array, 64-byte aligned
-    const MkPhase* phases;
-    int nphase;
-    int emb, heads, kv_heads, hd, kvw, ctx, rope_half;
-    float eps, attn_scale;
-    const float2* rope;
-    int embd_type;
-    const uint8_t* embd;
-    int64_t embd_pitch;
-    const float* ssq_tok;
-    float* hidden;
-    float* q;
-    float* att;
-    int8_t* att_q;
-    float* att_s;
-    float* scores;
-    int* state;
-    int* tokens;
-    float2* amax_part;
-    unsigned* amax_cnt;
-    int head_row0;
-    unsigned* bar;                // grid barrier counter, zeroed before each launch
-    int* err;
-    int nstages, stage_bytes, xq_off, xs_off, xsum_off, t_off, stage_off, attn_bytes, smem_bytes;
-};
-// Fills the box rows of a phase for a ring slot of slot_bytes; false if it cannot fit.
-bool mk_box_rows(int qtype, int cols, int rows, bool dual, int row_align, int slot_bytes, int* box_rows);
-int mk_launch(int qtype, const MkParams& p, cudaStream_t s);
-size_t mk_attn_bytes(int ctx);   // shared memory the attention phase uses (before the ring)
 
 // Launchers (kernels.cu).
 int q6k_gemv_launch(int epi, const Q6Params& p, cudaStream_t s, bool pdl);
