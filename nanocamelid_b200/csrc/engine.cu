@@ -111,6 +111,7 @@ struct ncm_model {
     float* hx_s = nullptr;
     int64_t prefetch_bytes = 0;   // per CTA: next kernel's weights streamed into L2 (0: off)
     int cgroups = 4;              // GEMV compute-warp groups (stages worked on at once)
+    int av_tma = 1;               // attention V chunks by TMA (f32 cache)
     int tune = 0;                 // measurement knobs
     uint64_t* dbg_ts = nullptr;   // measurement probe buffer [num_sms][8], filled by step-kernel seam launches
     bool dbg_on = false;
@@ -525,6 +526,7 @@ static ncm_status check_all_shapes(ncm_model* m) {
     if (const char* e = getenv("NCM_TUNE_ACTQ")) m->act_quantised = m->act_quantised && atoi(e) != 0;
     if (const char* e = getenv("NCM_TUNE_PREFETCH_KB")) m->prefetch_bytes = (int64_t)atoi(e) * 1024;
     if (const char* e = getenv("NCM_TUNE_CGROUPS")) m->cgroups = atoi(e);
+    if (const char* e = getenv("NCM_TUNE_AV_TMA")) m->av_tma = atoi(e);
     if (const char* e = getenv("NCM_TUNE_BITS")) m->tune = atoi(e);
     return NCM_OK;
 }
@@ -946,6 +948,8 @@ static void attn_params(ncm_model* m, int l, AttnParams& a) {
     a.out_q = m->att_q;
     a.out_s = m->att_s;
     a.scale = 1.0f / sqrtf((float)m->hd);   // inference.rs:4653
+    a.vmap_on = m->av_tma;
+    a.err = m->err;
 }
 
 static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
@@ -1361,6 +1365,8 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s, bool wi
         a.scale = 1.0f / sqrtf((float)m->hd);
         a.ntok = ntok;
         a.tok_stride = qw;
+        a.vmap_on = m->av_tma;
+        a.err = m->err;
         CKL(attention_launch(a, s, true));
         BatchParams o = batch_base(m, ntok);
         if (prologue_quant(ntok, qw)) {
@@ -1993,6 +1999,7 @@ extern "C" ncm_status ncm_attention(float* out, const float* q, const float* k_c
     a.pos_override = pos;
     a.heads = heads; a.kv_heads = kv_heads; a.hd = head_dim; a.kvw = kv_heads * head_dim; a.ctx = ctx;
     a.scale = 1.0f / sqrtf((float)head_dim);
+    a.vmap_on = 1;
     int r = attention_launch(a, s, false);
     cudaFreeAsync(scores, s);
     CK(cudaStreamSynchronize(s));

@@ -272,42 +272,57 @@ __device__ float seq_sum_segment(const Term& term, int seg0, int segn, float car
             for (int w = 0; w < warp; ++w) base += sc.wsum[w];
     }
     const float off = base + excl;
-    // (2) certify each term.  Fast path: the chunk's two ends certify one binade for
-    // the whole chunk (S is monotone), then a term is uncertain only if it is a tie.
+    // (2) certify each term, four at a time: when the approximate prefix at both ends of
+    // a run of four (widened by the error margin of its last index) lies in one binade,
+    // S does too over the whole run (S is monotone), and a term of the run is uncertain
+    // only if it is a tie; a run that straddles a binade edge is certified term by term.
+    // A lane's runs take the same branch as its neighbours' except near the few binade
+    // crossings, so the warp rarely executes both.  The first chunk of a sum (running
+    // value near zero, crossing binades every few terms) is listed whole.
     uint32_t c[KM];
     uint64_t umask = 0;   // KM may exceed 32
     uint32_t cnt = 0;
     const int nq = min(KM, max(0, segn - i0));
-    bool chunk_ok = false;
-    int ec = 150;
-    if (nq > 0) {
-        const float a0 = carry + off, a1 = carry + (off + loc[KM - 1]);
-        const float mg = (float)(seg0 + i0 + KM + 128) * 0x1p-22f;
-        ec = (int)(__float_as_uint(a0) >> 23);
-        chunk_ok = (ec >= 24) & (ec <= 253) & ((int)(__float_as_uint(a0 * (1.0f - mg)) >> 23) == ec) &
-                   ((int)(__float_as_uint(a1 * (1.0f + mg)) >> 23) == ec);
-    }
-    if (chunk_ok) {
-        const float inv = seq_inv_ulp(ec);
+    const bool first = seg0 + i0 == 0 && carry == 0.0f;
+    constexpr int kRun = 4;
 #pragma unroll
-        for (int q = 0; q < KM; ++q) {
-            uint32_t cq;
-            const bool ok = seq_units(v[q] * inv, cq);   // padding terms are 0: ok, count 0
-            c[q] = cq;
-            umask |= ok ? 0ull : (1ull << q);
-            cnt += cq;
-        }
-    } else {
+    for (int q0 = 0; q0 < KM; q0 += kRun) {
+        const int q1 = q0 + kRun - 1 < KM - 1 ? q0 + kRun - 1 : KM - 1;
+        const float alo = carry + (q0 ? off + loc[q0 - 1] : off);
+        const float ahi = carry + (off + loc[q1]);
+        const float mg = (float)(seg0 + i0 + q1 + 1 + 128) * 0x1p-22f;
+        const int er = (int)(__float_as_uint(alo) >> 23);
+        const bool run_ok = !first & (er >= 24) & (er <= 253) &
+                            ((int)(__float_as_uint(alo * (1.0f - mg)) >> 23) == er) &
+                            ((int)(__float_as_uint(ahi * (1.0f + mg)) >> 23) == er);
+        if (run_ok) {
+            const float inv = seq_inv_ulp(er);
 #pragma unroll
-        for (int q = 0; q < KM; ++q) {
-            const float ae = carry + (q ? off + loc[q - 1] : off);
-            const float ai = carry + (off + loc[q]);
-            const bool valid = q < nq;
-            uint32_t cq;
-            const bool cert = seq_certain(v[q], ae, ai, seg0 + i0 + q, cq);
-            c[q] = valid ? cq : 0u;
-            umask |= (valid & !cert) ? (1ull << q) : 0ull;
-            cnt += c[q];
+            for (int q = q0; q <= q1; ++q) {
+                uint32_t cq;
+                const bool ok = seq_units(v[q] * inv, cq);   // padding terms are 0: ok, count 0
+                c[q] = cq;
+                umask |= ok ? 0ull : (1ull << q);
+                cnt += cq;
+            }
+        } else if (first) {
+#pragma unroll
+            for (int q = q0; q <= q1; ++q) {
+                c[q] = 0u;
+                umask |= q < nq ? (1ull << q) : 0ull;
+            }
+        } else {
+#pragma unroll
+            for (int q = q0; q <= q1; ++q) {
+                const float ae = carry + (q ? off + loc[q - 1] : off);
+                const float ai = carry + (off + loc[q]);
+                const bool valid = q < nq;
+                uint32_t cq;
+                const bool cert = seq_certain(v[q], ae, ai, seg0 + i0 + q, cq);
+                c[q] = valid ? cq : 0u;
+                umask |= (valid & !cert) ? (1ull << q) : 0ull;
+                cnt += c[q];
+            }
         }
     }
     const uint32_t nunc = __popcll(umask);
@@ -382,6 +397,7 @@ __device__ float seq_sum_nonneg(const Term& term, int n, SeqSumScratchT<NT>& sc,
     if (n <= 9 * NT) return seq_sum_segment<NT, 9, BAR>(term, 0, n, 0.0f, sc, rank);
     if (n <= 13 * NT) return seq_sum_segment<NT, 13, BAR>(term, 0, n, 0.0f, sc, rank);
     if (n <= 17 * NT) return seq_sum_segment<NT, 17, BAR>(term, 0, n, 0.0f, sc, rank);
+    if (n <= 25 * NT) return seq_sum_segment<NT, 25, BAR>(term, 0, n, 0.0f, sc, rank);
     float x = 0.0f;
     for (int seg0 = 0; seg0 < n; seg0 += 33 * NT)
         x = seq_sum_segment<NT, 33, BAR>(term, seg0, min(n - seg0, 33 * NT), x, sc, rank);
@@ -837,6 +853,23 @@ __device__ void prefetch_next_weights(const GemvParams& p) {
 // progress at once and the latency of one stage's shared-memory loads, dp4a chains and
 // term stores overlaps the others' (one group per stage left the SM mostly waiting).
 
+// quantize_f32_to_q8_0 (inference.rs:991-1029) of one 32-value block held one value per
+// lane: scale = max|x| / 127, q = round(x * (1 / scale)) clamped to +-127 (zero block:
+// scale 0, values 0).  Writes this lane's int8, returns the block scale.
+__device__ __forceinline__ float q8_block_quantise(float v, int8_t* q_out) {
+    float amax = fabsf(v);
+#pragma unroll
+    for (int k = 16; k > 0; k >>= 1) amax = fmaxf(amax, __shfl_xor_sync(NCM_FULL, amax, k));
+    const float scale = amax / 127.0f;
+    int q = 0;
+    if (scale > 0.0f) {
+        const float inv = 1.0f / scale;
+        q = (int)fminf(fmaxf(roundf(v * inv), -127.0f), 127.0f);
+    }
+    *q_out = (int8_t)q;
+    return scale;
+}
+
 // Measurement probe: when p.dbg_ts is set, per-CTA global-timer stamps (ns) of the
 // pipeline's phases: [0] entry, [1] after the PDL wait, [2] prologue done, [3] last TMA
 // issued, [4] last fold done, [5] fold-thread time in tile epilogues, [6] exit,
@@ -1084,19 +1117,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ncm_qgemv_kernel(const __grid
                 }
                 if (p.qout && f < 32) {
                     // The tile is one 32-row block (box_rows == 32, 32-aligned row ranges):
-                    // fold warp 8 holds it and quantises it for the down projection
-                    // (quantize_f32_to_q8_0, inference.rs:991-1029).
-                    float amax = fabsf(o);
-#pragma unroll
-                    for (int k = 16; k > 0; k >>= 1) amax = fmaxf(amax, __shfl_xor_sync(NCM_FULL, amax, k));
-                    const float scale = amax / 127.0f;
-                    int q = 0;
-                    if (scale > 0.0f) {
-                        const float inv = 1.0f / scale;
-                        q = (int)fminf(fmaxf(roundf(o * inv), -127.0f), 127.0f);
-                    }
-                    p.qout[lrow0 + f] = (int8_t)q;
-                    if (f == 0) p.qout_s[(lrow0) >> 5] = scale;
+                    // fold warp 8 holds it and quantises it for the down projection.
+                    const float scale = q8_block_quantise(o, p.qout + lrow0 + f);
+                    if (f == 0) p.qout_s[lrow0 >> 5] = scale;
                 }
                 asm volatile("bar.sync 1, 64;" ::: "memory");
             } else {
@@ -1550,15 +1573,16 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(const __grid_constant
 
 // Stage 3 (attn_av_kernel): out[d] = sum_p w_p * v_p[d], sequential over p per (head, dim)
 // (attn_output zeroed, add_weighted_f32_scalar inference.rs:3619-3623).  One item = (kv
-// head, 32-dimension block, group of HG query heads of that kv head, row): warp = query
-// head, lane = dimension, so each thread carries one chain and a warp's output is one
+// head, 32-dimension block, group of W * HPW query heads of that kv head, row): lane =
+// dimension, warp w carries the chains of HPW heads (independent adds that interleave:
+// one chain alone stalls on each add's latency), and a warp's output per head is one
 // Q8_0 block for the output projection.  The item's V columns (128 bytes a position,
-// shared by its HG warps) and weights stream through a ring of kAvStages chunks of
+// shared by all its heads) and weights stream through a ring of kAvStages chunks of
 // kAvChunk positions by cp.async, so the loads of later chunks are in flight while a
-// chunk's chain runs.  buf holds kAvStages * av_stage_floats(HG) floats.
+// chunk's chains run.  buf holds kAvStages * av_stage_floats(W * HPW) floats.
 constexpr int kAvChunk = 64;
 constexpr int kAvStages = 4;
-__host__ __device__ constexpr int av_stage_floats(int hg) { return kAvChunk * 32 + hg * kAvChunk; }
+__host__ __device__ constexpr int av_stage_floats(int heads) { return kAvChunk * 32 + heads * kAvChunk; }
 
 __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
@@ -1566,20 +1590,20 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
 template <int N>
 __device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-template <int HG, int BAR>
+template <int W, int HPW>
 __device__ void attn_av_body(const AttnParams& a, int kvh, int db, int hgrp, int tz, float* buf, int rank) {
-    constexpr int NT = HG * 32;
+    constexpr int NT = W * 32, HC = W * HPW;   // threads, heads of the item
     const int pos = (a.pos_override >= 0 ? a.pos_override : __ldcg(&a.state[ST_POS])) + tz;
     const int n = pos + 1;
     const int g = a.heads / a.kv_heads;
     const int warp = rank >> 5, lane = rank & 31;
-    const int h0 = kvh * g + hgrp * HG;
+    const int h0 = kvh * g + hgrp * HC;
     const int d0 = db * 32;
     const float* wbase = a.scores + ((size_t)tz * a.heads + h0) * a.ctx;
     const bool vec = a.kv_kind == KV_F32 && attn_vec_ok(a);
     const float* vsrc = a.vc + (size_t)kvh * a.hd + d0;
     const int nchunk = (n + kAvChunk - 1) / kAvChunk;
-    constexpr int SF = av_stage_floats(HG);
+    constexpr int SF = av_stage_floats(HC);
     auto stage = [&](int k) {
         float* vs = buf + (k % kAvStages) * SF;
         float* ws = vs + kAvChunk * 32;
@@ -1602,9 +1626,9 @@ __device__ void attn_av_body(const AttnParams& a, int kvh, int db, int hgrp, int
         } else {
             for (int i = rank; i < np * 32; i += NT) vs[i] = __ldcg(&vsrc[(size_t)(c0 + (i >> 5)) * a.kvw + (i & 31)]);
         }
-        for (int i = rank; i < HG * np; i += NT) {
-            const int hh = i / np, p = i - hh * np;
-            cp_async4(ws + hh * kAvChunk + p, wbase + (size_t)hh * a.ctx + c0 + p);
+        for (int p = rank; p < np; p += NT) {
+#pragma unroll
+            for (int hh = 0; hh < HC; ++hh) cp_async4(ws + hh * kAvChunk + p, wbase + (size_t)hh * a.ctx + c0 + p);
         }
     };
 #pragma unroll
@@ -1612,18 +1636,142 @@ __device__ void attn_av_body(const AttnParams& a, int kvh, int db, int hgrp, int
         if (k < nchunk) stage(k);
         cp_async_commit();
     }
-    float acc = 0.0f;
+    float acc[HPW];
+#pragma unroll
+    for (int j = 0; j < HPW; ++j) acc[j] = 0.0f;
     for (int k = 0; k < nchunk; ++k) {
         if (k + kAvStages - 1 < nchunk) stage(k + kAvStages - 1);
         cp_async_commit();
         cp_async_wait_group<kAvStages - 1>();   // chunk k has landed (this thread's copies)
-        group_sync<NT, BAR>();                   // ... and every thread's
+        group_sync<NT, 0>();                     // ... and every thread's
         const float* vs = buf + (k % kAvStages) * SF;
-        const float* ws = vs + kAvChunk * 32 + warp * kAvChunk;
+        const float* ws = vs + kAvChunk * 32 + warp * HPW * kAvChunk;
         const int np = min(kAvChunk, n - k * kAvChunk);
         int p = 0;
-        // 16 positions a step, every shared-memory load issued before the first add (the
-        // adds stay in position order)
+        // 8 positions a step, every shared-memory load issued before the first add (each
+        // chain's adds stay in position order)
+        for (; p + 8 <= np; p += 8) {
+            float vv[8], wv[HPW][8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) vv[q] = vs[(p + q) * 32 + lane];
+#pragma unroll
+            for (int j = 0; j < HPW; ++j) {
+                const float4 x0 = *reinterpret_cast<const float4*>(ws + j * kAvChunk + p);
+                const float4 x1 = *reinterpret_cast<const float4*>(ws + j * kAvChunk + p + 4);
+                wv[j][0] = x0.x; wv[j][1] = x0.y; wv[j][2] = x0.z; wv[j][3] = x0.w;
+                wv[j][4] = x1.x; wv[j][5] = x1.y; wv[j][6] = x1.z; wv[j][7] = x1.w;
+            }
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+#pragma unroll
+                for (int j = 0; j < HPW; ++j) acc[j] += wv[j][q] * vv[q];
+        }
+        for (; p < np; ++p) {
+            const float v = vs[p * 32 + lane];
+#pragma unroll
+            for (int j = 0; j < HPW; ++j) acc[j] += ws[j * kAvChunk + p] * v;
+        }
+        group_sync<NT, 0>();                     // the slot may be refilled
+    }
+#pragma unroll
+    for (int j = 0; j < HPW; ++j) {
+        const int h = h0 + warp * HPW + j;
+        a.out[(size_t)tz * a.tok_stride + (size_t)h * a.hd + d0 + lane] = acc[j];
+        if (a.out_q) {
+            // quantize_f32_to_q8_0 of this 32-value block for the output projection
+            // (inference.rs:991-1029)
+            float amax = fabsf(acc[j]);
+#pragma unroll
+            for (int k = 16; k > 0; k >>= 1) amax = fmaxf(amax, __shfl_xor_sync(NCM_FULL, amax, k));
+            const float scale = amax / 127.0f;
+            int q = 0;
+            if (scale > 0.0f) {
+                const float inv = 1.0f / scale;
+                q = (int)fminf(fmaxf(roundf(acc[j] * inv), -127.0f), 127.0f);
+            }
+            const size_t o = (size_t)h * a.hd + d0;
+            a.out_q[o + lane] = (int8_t)q;
+            if (lane == 0) a.out_s[o >> 5] = scale;
+        }
+    }
+}
+
+// The same V items with the f32 cache's chunks brought by the TMA engine: one 2-D tiled
+// load (32 floats x kAvChunk positions of this kv head's dimension block) per chunk into
+// a ring of kAvStages slots tracked by mbarriers, issued by thread 0; the weights still
+// come by cp.async.  One chain per thread (W warps = W query heads).
+template <int W>
+__global__ void __launch_bounds__(W * 32) attn_av_tma_kernel(const __grid_constant__ AttnParams a) {
+    extern __shared__ __align__(128) float buf[];   // [slot][kAvChunk][32] V, then [slot][W][kAvChunk] w
+    __shared__ __align__(8) uint64_t full[kAvStages];
+    constexpr int NT = W * 32;
+    const int rank = threadIdx.x, warp = rank >> 5, lane = rank & 31;
+    if (rank == 0) {
+        for (int k = 0; k < kAvStages; ++k) mbar_init(&full[k], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+    pdl_wait();
+    const int nd = a.hd / 32;
+    const int kvh = blockIdx.x, db = blockIdx.y % nd, hgrp = blockIdx.y / nd, tz = blockIdx.z;
+    const int pos = (a.pos_override >= 0 ? a.pos_override : __ldcg(&a.state[ST_POS])) + tz;
+    const int n = pos + 1;
+    const int g = a.heads / a.kv_heads;
+    const int h0 = kvh * g + hgrp * W;
+    const int d0 = db * 32;
+    const float* wbase = a.scores + ((size_t)tz * a.heads + h0) * a.ctx;
+    const int nchunk = (n + kAvChunk - 1) / kAvChunk;
+    float* vbuf = buf;
+    float* wbuf = buf + kAvStages * kAvChunk * 32;
+    const uint64_t limit_ns = 1000000000ull;
+    const uint64_t pol = l2_evict_first_policy();
+    auto issue_v = [&](int k) {   // thread 0
+        uint64_t* bar = &full[k % kAvStages];
+        mbar_arrive_expect_tx(bar, kAvChunk * 32 * 4);
+        tma_load_2d(vbuf + (k % kAvStages) * kAvChunk * 32, &a.vmap, kvh * a.hd + d0, k * kAvChunk, bar, pol);
+    };
+    auto stage_w = [&](int k) {
+        float* ws = wbuf + (k % kAvStages) * W * kAvChunk;
+        const int c0 = k * kAvChunk, np = min(kAvChunk, n - c0);
+        for (int p = rank; p < np; p += NT) {
+#pragma unroll
+            for (int hh = 0; hh < W; ++hh) cp_async4(ws + hh * kAvChunk + p, wbase + (size_t)hh * a.ctx + c0 + p);
+        }
+    };
+#pragma unroll
+    for (int k = 0; k < kAvStages - 1; ++k) {
+        if (k < nchunk) {
+            if (rank == 0) issue_v(k);
+            stage_w(k);
+        }
+        cp_async_commit();
+    }
+    float acc = 0.0f;
+    bool ok = true;
+    for (int k = 0; k < nchunk; ++k) {
+        if (k + kAvStages - 1 < nchunk) {
+            if (rank == 0) issue_v(k + kAvStages - 1);
+            stage_w(k + kAvStages - 1);
+        }
+        cp_async_commit();
+        cp_async_wait_group<kAvStages - 1>();
+        if (!mbar_wait(&full[k % kAvStages], (uint32_t)((k / kAvStages) & 1), limit_ns)) {
+            if (a.err) set_dev_error(a.err, NCM_DEVERR_MBAR_TIMEOUT);
+            ok = false;
+        }
+        if (!__syncthreads_and(ok)) {
+            // a load that never landed: wait (bounded) for the copies still in flight
+            cp_async_wait_group<0>();
+            if (rank == 0)
+                for (int j = k; j < nchunk && j < k + kAvStages; ++j)
+                    mbar_wait(&full[j % kAvStages], (uint32_t)((j / kAvStages) & 1), 100000000ull);
+            return;
+        }
+        const float* vs = vbuf + (k % kAvStages) * kAvChunk * 32;
+        const float* ws = wbuf + (k % kAvStages) * W * kAvChunk + warp * kAvChunk;
+        const int np = min(kAvChunk, n - k * kAvChunk);
+        int p = 0;
         for (; p + 16 <= np; p += 16) {
             float wv[16], vv[16];
 #pragma unroll
@@ -1637,14 +1785,12 @@ __device__ void attn_av_body(const AttnParams& a, int kvh, int db, int hgrp, int
             for (int q = 0; q < 16; ++q) acc += wv[q] * vv[q];
         }
         for (; p < np; ++p) acc += ws[p] * vs[p * 32 + lane];
-        group_sync<NT, BAR>();                   // the slot may be refilled
+        __syncthreads();   // the slot may be refilled
     }
     const int h = h0 + warp;
     a.out[(size_t)tz * a.tok_stride + (size_t)h * a.hd + d0 + lane] = acc;
     if (a.out_q) {
-        // quantize_f32_to_q8_0 of this 32-value block for the output projection
-        // (inference.rs:991-1029)
-        float amax = fabsf(acc);
+        float amax = fabsf(acc);   // quantize_f32_to_q8_0 of this block (inference.rs:991-1029)
 #pragma unroll
         for (int k = 16; k > 0; k >>= 1) amax = fmaxf(amax, __shfl_xor_sync(NCM_FULL, amax, k));
         const float scale = amax / 127.0f;
@@ -1659,19 +1805,14 @@ __device__ void attn_av_body(const AttnParams& a, int kvh, int db, int hgrp, int
     }
 }
 
-template <int HG>
-__global__ void __launch_bounds__(HG * 32) attn_av_kernel(const __grid_constant__ AttnParams a) {
+template <int W, int HPW>
+__global__ void __launch_bounds__(W * 32) attn_av_kernel(const __grid_constant__ AttnParams a) {
     extern __shared__ __align__(16) float buf[];
     pdl_launch_dependents();
     pdl_wait();
     const int nd = a.hd / 32;
-    attn_av_body<HG, 0>(a, blockIdx.x, blockIdx.y % nd, blockIdx.y / nd, blockIdx.z, buf, threadIdx.x);
+    attn_av_body<W, HPW>(a, blockIdx.x, blockIdx.y % nd, blockIdx.y / nd, blockIdx.z, buf, threadIdx.x);
 }
-
-// Query heads per attention item: the largest divisor of the group size g that is at
-// most 2 (two warps share one staged V slice; more would serialise the chains of one
-// SM's warps on its issue slots).
-int attn_group_heads(int g) { return g % 2 == 0 ? 2 : 1; }
 
 int attention_launch(const AttnParams& a0, cudaStream_t s, bool pdl) {
     constexpr int kMaxSmem = 200 * 1024;
@@ -1696,12 +1837,34 @@ int attention_launch(const AttnParams& a0, cudaStream_t s, bool pdl) {
     cfg.dynamicSmemBytes = (size_t)a.ctx * 4;
     r = (int)cudaLaunchKernelEx(&cfg, attn_softmax_kernel, a);
     if (r) return r;
-    const int hg = attn_group_heads(g);
-    cfg.gridDim = dim3(a.kv_heads, (a.hd / 32) * (g / hg), nz);
-    cfg.blockDim = dim3(hg * 32);
-    cfg.dynamicSmemBytes = (size_t)kAvStages * av_stage_floats(hg) * 4;
-    if (hg == 2) return (int)cudaLaunchKernelEx(&cfg, attn_av_kernel<2>, a);
-    return (int)cudaLaunchKernelEx(&cfg, attn_av_kernel<1>, a);
+    // heads per item: two warps of one chain each when the group allows (measured on the
+    // 70B shape at 1k positions: more chains per warp, or more heads per item, are slower
+    // -- the items then stream their V slices with fewer CTAs)
+    const int w = g % 2 == 0 ? 2 : 1;
+    if (a.vmap_on && a.kv_kind == KV_F32 && (((uintptr_t)a.vc) & 15) == 0 && (a.kvw & 3) == 0) {
+        EncodeTiledFn enc = encode_tiled_fn();
+        if (enc) {
+            cuuint64_t gdim[2] = {(cuuint64_t)a.kvw, (cuuint64_t)a.ctx};
+            cuuint64_t gstride[1] = {(cuuint64_t)a.kvw * 4};
+            cuuint32_t box[2] = {32, (cuuint32_t)kAvChunk};
+            cuuint32_t estride[2] = {1, 1};
+            CUresult cr = enc(&a.vmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(a.vc), gdim, gstride, box,
+                              estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (cr == CUDA_SUCCESS) {
+                cfg.gridDim = dim3(a.kv_heads, (a.hd / 32) * (g / w), nz);
+                cfg.blockDim = dim3(w * 32);
+                cfg.dynamicSmemBytes = (size_t)kAvStages * kAvChunk * (32 + w) * 4;
+                if (w == 2) return (int)cudaLaunchKernelEx(&cfg, attn_av_tma_kernel<2>, a);
+                return (int)cudaLaunchKernelEx(&cfg, attn_av_tma_kernel<1>, a);
+            }
+        }
+    }
+    cfg.gridDim = dim3(a.kv_heads, (a.hd / 32) * (g / w), nz);
+    cfg.blockDim = dim3(w * 32);
+    cfg.dynamicSmemBytes = (size_t)kAvStages * av_stage_floats(w) * 4;
+    if (w == 2) return (int)cudaLaunchKernelEx(&cfg, attn_av_kernel<2, 1>, a);
+    return (int)cudaLaunchKernelEx(&cfg, attn_av_kernel<1, 1>, a);
 }
 
 // store_kv (inference.rs:539-568) for the F16 cache (fast_f32_to_f16 per value) and the

@@ -92,6 +92,7 @@ struct alignas(64) GemvParams {
     int row_align;                // CTA row ranges start at multiples of this (2, or 32 with qout)
     int tune;                     // measurement knobs (0 in normal use)
     int cgroups;                  // compute-warp groups (1, 2 or 4; 0: 4): stages worked on at once
+
     uint64_t* dbg_ts;             // measurement probe: per-CTA phase stamps [grid][8] (null in normal use)
     int8_t* qout;                 // EPI_SILU: the output rows also as Q8_0 blocks (box_rows == 32) ...
     float* qout_s;                //   ... and their scales: the next projection's quantised input
@@ -104,7 +105,8 @@ struct alignas(64) GemvParams {
     int64_t pf_bytes;
 };
 
-struct AttnParams {
+struct alignas(64) AttnParams {
+    CUtensorMap vmap;        // optional: this layer's f32 V cache [ctx][kvw], box 32 x kAvChunk (vmap_on)
     const float* q;          // [heads_local * hd] roped
     const float* kc;         // layer cache [ctx][kvw]
     const float* vc;
@@ -121,6 +123,8 @@ struct AttnParams {
     int kv_kind;             // cache storage: 0 f32 (kc / vc), 1 F16, 2 Q8_0 (kc_raw / vc_raw)
     const void* kc_raw;
     const void* vc_raw;
+    int vmap_on;             // V chunks by TMA through vmap (f32 cache)
+    int* err;                // device error word for bounded waits (may be null)
 };
 
 // KV-cache storage kinds (inference.rs:505-599; NANOCAMELID_KV_CACHE_F16 / _Q8).
