@@ -41,6 +41,9 @@ def parse():
     ap.add_argument("--vocab", type=int, default=0, help="small case for profiler captures: smaller vocab")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="profiler captures: one decode step at the last prompt position instead of the prefill "
+                         "(the earlier K/V rows stay zero; the step's work is the same)")
     ap.add_argument("--spec", action="store_true",
                     help="BASELINE config 5: greedy speculative decoding, draft = config 1, target = config-3 "
                          "shape all Q4_0, k = 4, 128-token prompt, 256 tokens (one GPU)")
@@ -297,7 +300,10 @@ def run_b200(args, sp):
     rng = np.random.default_rng(0)
     prompt = [int(v) for v in rng.integers(0, sp.vocab, args.prompt)]
     stream = torch.cuda.Stream()
-    m.prefill(prompt, stream.cuda_stream)
+    if args.no_prefill:
+        m.forward_pass(prompt[-1], len(prompt) - 1)
+    else:
+        m.prefill(prompt, stream.cuda_stream)
     m.decode_steps(args.warmup, stream.cuda_stream)
     torch.cuda.synchronize()
     if world > 1:
@@ -397,7 +403,7 @@ def run_b200(args, sp):
         whole = {"bytes_per_token_per_gpu": int(bpt), "achieved_gbs": round(bpt * tok_s / 1e9, 1),
                  "frac_of_measured_hbm": round(bpt * tok_s / 1e9 / peak, 4)}
         cpu = None if (args.no_cpu or world > 1) else cpu_sample(args, sp)
-        launches_per_step = 2 + 6 * sp.layers + (0 if world == 1 or args.reducer == "p2p" else 2 * sp.layers + 1)
+        launches_per_step = 2 + 7 * sp.layers + (0 if world == 1 or args.reducer == "p2p" else 2 * sp.layers + 1)
         cfg = bench_config(args, world, shares)
         cfg["l2"] = "inputs larger than L2 (weights %.2f GB/token/GPU)" % (bpt / 1e9)
         line = {"metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,

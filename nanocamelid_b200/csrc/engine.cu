@@ -112,6 +112,7 @@ struct ncm_model {
     int64_t prefetch_bytes = 0;   // per CTA: next kernel's weights streamed into L2 (0: off)
     int cgroups = 4;              // GEMV compute-warp groups (stages worked on at once)
     int av_tma = 1;               // attention V chunks by TMA (f32 cache)
+    int bcgroups = 0;             // multi-row GEMV compute-warp groups (0: the plan's default)
     int tune = 0;                 // measurement knobs
     uint64_t* dbg_ts = nullptr;   // measurement probe buffer [num_sms][8], filled by step-kernel seam launches
     bool dbg_on = false;
@@ -527,6 +528,7 @@ static ncm_status check_all_shapes(ncm_model* m) {
     if (const char* e = getenv("NCM_TUNE_PREFETCH_KB")) m->prefetch_bytes = (int64_t)atoi(e) * 1024;
     if (const char* e = getenv("NCM_TUNE_CGROUPS")) m->cgroups = atoi(e);
     if (const char* e = getenv("NCM_TUNE_AV_TMA")) m->av_tma = atoi(e);
+    if (const char* e = getenv("NCM_TUNE_BCGROUPS")) m->bcgroups = atoi(e);
     if (const char* e = getenv("NCM_TUNE_BITS")) m->tune = atoi(e);
     return NCM_OK;
 }
@@ -1265,6 +1267,7 @@ static BatchParams batch_base(ncm_model* m, int ntok) {
     BatchParams p;
     memset(&p, 0, sizeof p);
     p.ntok = ntok;
+    p.cgroups = m->bcgroups;
     p.rope = m->rope;
     p.rope_half = m->rope_dim / 2;
     p.head_dim = m->hd;

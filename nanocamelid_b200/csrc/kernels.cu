@@ -2388,8 +2388,8 @@ __global__ void __launch_bounds__(kBatchThreads, 1) ncm_qgemm_verify_kernel(cons
     if (tid == 0) {
         for (int s = 0; s < ns; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 8);
-            mbar_init(&tfull[s], 8);
+            mbar_init(&empty[s], 8 / p.cgroups);
+            mbar_init(&tfull[s], 8 / p.cgroups);
             mbar_init(&tempty[s], kBatchFoldWarps);
         }
         fence_mbar_init();
@@ -2499,15 +2499,24 @@ __global__ void __launch_bounds__(kBatchThreads, 1) ncm_qgemm_verify_kernel(cons
     if (tid == kBatchProducer) {
         while (icur < r_end) issue();
     } else if (warp < 8) {
-        // compute: warp -> slab warp % S, blocks bl0 .. bl0 + 16 S / 8 - 1 of every stage
+        // compute: p.cgroups groups of 8 / cgroups warps, group gi on the stages t with
+        // t % cgroups == gi (several stages in progress at once); warp wi of a group ->
+        // slab wi % S, blocks bl0 .. bl0 + nbw - 1 of its stages, nbw = 16 S / (8 / cgroups)
+        const int G = p.cgroups, WG = 8 / G, gi = warp / WG, wi = warp % WG;
         const int g = lane >> 2, t = lane & 3;
-        const int sl = warp % S, nbw = 2 * S, bl0 = (warp / S) * nbw;
+        const int sl = wi % S, nbw = 16 * S / WG, bl0 = (wi / S) * nbw;
         const int ra = 16 * sl + g;
+        auto terms = [&](const uint8_t* tl, int c, float4* T) {
+            if (nbw == 2) batch_terms<QT, 2>(tl, p.chunk_bytes, ra, g, t, c, bl0, xq, xq_pitch, xs, xsum, p.nb, p.ntok, T);
+            else if (nbw == 4) batch_terms<QT, 4>(tl, p.chunk_bytes, ra, g, t, c, bl0, xq, xq_pitch, xs, xsum, p.nb, p.ntok, T);
+            else batch_terms<QT, 8>(tl, p.chunk_bytes, ra, g, t, c, bl0, xq, xq_pitch, xs, xsum, p.nb, p.ntok, T);
+        };
         int tc_ = 0;
         for (int cur = r_begin; cur < r_end;) {
             const int n = batch_tile_at(p, cur, r_end).n;
             const bool active = 16 * sl < n;
             for (int c = 0; c < p.nchunk; ++c, ++tc_) {
+                if (tc_ % G != gi) continue;
                 const int s = tc_ % ns;
                 const uint32_t u = (uint32_t)(tc_ / ns);
                 if (!mbar_wait(&full[s], u & 1, limit_ns)) set_dev_error(p.err, NCM_DEVERR_MBAR_TIMEOUT);
@@ -2515,19 +2524,8 @@ __global__ void __launch_bounds__(kBatchThreads, 1) ncm_qgemm_verify_kernel(cons
                 if (active) {
                     const uint8_t* tile = stages + (size_t)s * p.stage_bytes;
                     float4* T = tbase + (size_t)s * tslot + sl * 16 * 32 + lane;
-                    if (nbw == 2)
-                        batch_terms<QT, 2>(tile, p.chunk_bytes, ra, g, t, c, bl0, xq, xq_pitch, xs, xsum, p.nb, p.ntok, T);
-                    else
-                        batch_terms<QT, 4>(tile, p.chunk_bytes, ra, g, t, c, bl0, xq, xq_pitch, xs, xsum, p.nb, p.ntok, T);
-                    if (DUAL) {
-                        float4* T2 = T + S * 16 * 32;
-                        if (nbw == 2)
-                            batch_terms<QT, 2>(tile + box2_off, p.chunk_bytes, ra, g, t, c, bl0, xq, xq_pitch, xs, xsum,
-                                               p.nb, p.ntok, T2);
-                        else
-                            batch_terms<QT, 4>(tile + box2_off, p.chunk_bytes, ra, g, t, c, bl0, xq, xq_pitch, xs, xsum,
-                                               p.nb, p.ntok, T2);
-                    }
+                    terms(tile, c, T);
+                    if (DUAL) terms(tile + box2_off, c, T + S * 16 * 32);
                 }
                 __syncwarp();
                 if (lane == 0) {
@@ -2698,6 +2696,8 @@ int batch_plan(int qtype, int cols, int rows, bool dual, int ntok, BatchParams& 
             while (ns > 2 && off + ns * (stage_bytes + t_bytes) > kBatchSmemLimit) --ns;
             if (off + ns * (stage_bytes + t_bytes) > kBatchSmemLimit || (!xg && ns < 4)) continue;
             p.nslab = S;
+            if (p.cgroups != 1 && p.cgroups != 2 && p.cgroups != 4) p.cgroups = 2;
+            if (S == 2 && p.cgroups == 4) p.cgroups = 2;
             p.box_rows = br;
             p.stage_bytes = stage_bytes;
             p.nstages = ns;

@@ -142,6 +142,7 @@ struct alignas(64) BatchParams {
     int cols, nb, nchunk, chunk_words, chunk_bytes, box_rows, stage_bytes, nstages;
     int xq_off, xs_off, xsum_off, stage_off, smem_bytes, xq_pitch;
     int nslab;                    // 16-row slabs per tile (one fold warp each)
+    int cgroups;                  // compute-warp groups (1, 2, or 4 with one slab; 0: 2)
     int t_off;                    // term ring (one slot per stage)
     int ntok;
     const int8_t* xq;             // [ntok][cols] quantised rows
