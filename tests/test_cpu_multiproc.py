@@ -20,7 +20,8 @@ def _free_port():
 
 def _worker(rank, world, port, shares, result_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    # a file rendezvous in the test's own directory: no TCP port to race for
+    dist.init_process_group("gloo", init_method="file://" + os.path.join(result_dir, "pg_store"), rank=rank, world_size=world)
     try:
         import nanocamelid_b200 as ncm
         from nanocamelid_b200 import tp
@@ -45,7 +46,8 @@ def test_two_rank_plan_exchange(tmp_path, shares):
 
 def _bad_worker(rank, world, port, result_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    # a file rendezvous in the test's own directory: no TCP port to race for
+    dist.init_process_group("gloo", init_method="file://" + os.path.join(result_dir, "pg_store"), rank=rank, world_size=world)
     try:
         import nanocamelid_b200 as ncm
         from nanocamelid_b200 import tp
@@ -71,7 +73,8 @@ def test_two_rank_plan_mismatch_is_rejected(tmp_path):
 
 def _reducer_worker(rank, world, port, result_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    # a file rendezvous in the test's own directory: no TCP port to race for
+    dist.init_process_group("gloo", init_method="file://" + os.path.join(result_dir, "pg_store"), rank=rank, world_size=world)
     try:
         import numpy as np
         import nanocamelid_b200 as ncm

@@ -44,7 +44,8 @@ def _worker(rank, world, port, path, shares, reducer, prompt, n_gen, out_dir):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    # a file rendezvous in the test's own directory: no TCP port to race for
+    dist.init_process_group("gloo", init_method="file://" + os.path.join(out_dir, "pg_store"), rank=rank, world_size=world)
     try:
         import nanocamelid_b200 as ncm
         from nanocamelid_b200 import tp
@@ -96,7 +97,8 @@ def _silent_worker(rank, world, port, path, out_dir):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    # a file rendezvous in the test's own directory: no TCP port to race for
+    dist.init_process_group("gloo", init_method="file://" + os.path.join(out_dir, "pg_store"), rank=rank, world_size=world)
     try:
         import nanocamelid_b200 as ncm
         from nanocamelid_b200 import tp
