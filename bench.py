@@ -421,49 +421,72 @@ def run_b200(args, sp):
 
 
 def run_spec(args, ncm):
-    """Config 5 on one GPU: tokens emitted per second by ncm_spec_generate (host-driven
-    draft/verify loop, synchronous), next to the target's plain greedy decode."""
+    """Config 5: tokens emitted per second by ncm_spec_generate (host-driven draft/verify
+    loop, synchronous), next to the target's plain greedy decode.  Under torchrun the
+    target is tensor parallel over the ranks (KV-head shares, the fused NVLink reducer for
+    both the one-row steps and the multi-row verify); every rank runs its own full draft."""
     import numpy as np
     import torch
+    import torch.distributed as dist
+    from nanocamelid_b200 import tp
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     target_sp, draft_sp = ncm.CONFIGS["cfg5_target_q4_0"], ncm.CONFIGS["cfg1_1b_q4_0"]
     n_prompt, n_gen, k = 128, 256, 4
     ctx = n_prompt + n_gen + 2 * k + 2
     prompt = [int(v) for v in np.random.default_rng(0).integers(0, target_sp.vocab, n_prompt)]
-    target = ncm.Model.synthetic(target_sp, ctx_limit=ctx, device=0)
-    draft = ncm.Model.synthetic(draft_sp, ctx_limit=ctx, device=0)
+    shares = (([int(v) for v in args.shares.split(",")] if args.shares else tp.default_shares(target_sp.kv_heads, world))
+              if world > 1 else None)
+    target = ncm.Model.synthetic(target_sp, ctx_limit=ctx, device=local, shares=shares, shard=rank)
+    if world > 1:
+        tp.connect(target, rank, world, ncm.REDUCE_FUSED_P2P)
+    draft = ncm.Model.synthetic(draft_sp, ctx_limit=ctx, device=local)
+
+    def timed(fn):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        r = fn()
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([dt], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt = float(t.item())
+        return r, dt
+
     target.spec_generate(draft, prompt, 8, k=k)                     # warm-up (graphs, buffers)
     target.reset(); draft.reset()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    toks, (drafted, accepted) = target.spec_generate(draft, prompt, n_gen, k=k)
-    torch.cuda.synchronize()
-    dt_spec = time.perf_counter() - t0
-    ref = ncm.Model.synthetic(target_sp, ctx_limit=ctx, device=0)
-    ref.generate(prompt, 8)
-    ref.reset()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    greedy = ref.generate(prompt, n_gen)
-    torch.cuda.synchronize()
-    dt_greedy = time.perf_counter() - t0
+    (toks, (drafted, accepted)), dt_spec = timed(lambda: target.spec_generate(draft, prompt, n_gen, k=k))
+    target.reset()
+    target.generate(prompt, 8)
+    target.reset()
+    greedy, dt_greedy = timed(lambda: target.generate(prompt, n_gen))
     # prompt-lookup drafting (the reference's default draft source) on the same target
     target.reset()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    ng_toks, (ng_drafted, ng_accepted) = target.ngram_generate(prompt, n_gen, k=k)
-    torch.cuda.synchronize()
-    dt_ngram = time.perf_counter() - t0
-    vms, step_ms = verify_times(ncm, target, n_prompt)
-    print(json.dumps({"metric": "bs1 speculative decode tok/s", "value": round(n_gen / dt_spec, 2), "unit": "tok/s",
-                      "n_gpus": 1, "higher_is_better": True, "data": "synthetic",
-                      "config": {"workload": "cfg5: draft cfg1_1b_q4_0, target cfg5_target_q4_0 (8B shape, Q4_0)",
-                                 "k": k, "prompt": n_prompt, "tokens": n_gen},
-                      "acceptance": round(accepted / max(1, drafted), 4), "drafted": drafted, "accepted": accepted,
-                      "target_greedy_tok_s": round(n_gen / dt_greedy, 2), "tokens_equal_greedy": toks == greedy,
-                      "verify_ms_by_rows": vms, "target_step_ms": step_ms,
-                      "ngram": {"tok_s": round(n_gen / dt_ngram, 2), "drafted": ng_drafted, "accepted": ng_accepted,
-                                "tokens_equal_greedy": ng_toks == greedy},
-                      "timing": "wall clock around the call (prefill included), synchronous"}))
+    (ng_toks, (ng_drafted, ng_accepted)), dt_ngram = timed(lambda: target.ngram_generate(prompt, n_gen, k=k))
+    vms, step_ms = verify_times(ncm, target, n_prompt) if world == 1 else (None, None)
+    if rank == 0:
+        print(json.dumps({"metric": "bs1 speculative decode tok/s", "value": round(n_gen / dt_spec, 2), "unit": "tok/s",
+                          "n_gpus": world, "higher_is_better": True, "data": "synthetic",
+                          "config": {"workload": "cfg5: draft cfg1_1b_q4_0, target cfg5_target_q4_0 (8B shape, Q4_0)",
+                                     "k": k, "prompt": n_prompt, "tokens": n_gen,
+                                     "parallelism": f"tp{world}" if world > 1 else "tp1", "shares": shares},
+                          "acceptance": round(accepted / max(1, drafted), 4), "drafted": drafted, "accepted": accepted,
+                          "target_greedy_tok_s": round(n_gen / dt_greedy, 2), "tokens_equal_greedy": toks == greedy,
+                          "verify_ms_by_rows": vms, "target_step_ms": step_ms,
+                          "ngram": {"tok_s": round(n_gen / dt_ngram, 2), "drafted": ng_drafted, "accepted": ng_accepted,
+                                    "tokens_equal_greedy": ng_toks == greedy},
+                          "timing": "wall clock around the call (prefill included), synchronous, max over ranks"}),
+              flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def verify_times(ncm, target, n_prompt, reps=10, rows=(1, 4, 5, 8)):

@@ -172,7 +172,8 @@ ncm_status ncm_model_set_kv_cache(ncm_model* m, int kind);
  * Synchronous. */
 ncm_status ncm_forward_pass(ncm_model* m, int token, int pos, float* logits, int* argmax);
 
-/* bin/cluster_tp_node.rs:808-875 run_reference loop: prompt token by token, then
+/* bin/cluster_tp_node.rs:808-875 run_reference loop: the prompt (eight tokens per
+ * multi-row pass, with the same K/V and state as token by token), then
  * n_gen greedy tokens.  Host buffers; the decode loop runs device-resident (CUDA
  * graph replays, no per-token host sync).  out_tokens[n_gen]. */
 ncm_status ncm_generate(ncm_model* m, const int* prompt, int n_prompt, int n_gen, int* out_tokens);
@@ -216,7 +217,10 @@ ncm_status ncm_debug_stamps(ncm_model* m, uint64_t* out, int n);
  * pos0 .. pos0+ntok-1 through the target in one multi-row pass (each weight tile read
  * once for all rows; int8 tensor-core block dots), K/V stored at those positions;
  * argmax_out[t] = greedy token after row t.  Each row equals the one-token step at its
- * position bit for bit.  The model's decode position is not changed.  One GPU. */
+ * position bit for bit.  The model's decode position is not changed.  On a shard,
+ * every rank calls it with the same arguments: the rows' partial sums and head pairs
+ * are reduced by the model's reducer (fused NVLink, NCCL or the host callback) and every
+ * rank gets the same tokens. */
 ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok, int pos0, int* argmax_out);
 
 /* speculative.rs:299-494 speculative_decoding_step at temperature 0, from a prompt:

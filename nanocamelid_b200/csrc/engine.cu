@@ -140,6 +140,10 @@ struct ncm_model {
     TpComm comm{};
     uint8_t* comm_base = nullptr;
     size_t comm_bytes = 0, off_flags = 0, off_hx = 0, off_hflags = 0;
+    size_t off_rrecv = 0, off_rflags = 0, off_rhx = 0, off_rhflags = 0;
+    TpRows rows{};                // multi-row reductions over the peers' areas
+    unsigned* rows_ctr = nullptr; // their epochs (this rank's own memory)
+    float2* rows_gather = nullptr;   // NCCL variant: [W][kMaxBatch] gathered head pairs
     std::vector<void*> ipc_open;
     nccl_comm nccl = nullptr;
     uint64_t timeout_ns = 10000000000ull;
@@ -333,9 +337,26 @@ static ncm_status setup_buffers(ncm_model* m, const int* shares, int nshards, in
         off = (off + 255) / 256 * 256;
         m->off_hflags = off;
         off += 4 * W;
+        // multi-row passes: rrecv[2][W][kMaxBatch * H] f32 | rflags[grid_max][W] u32 |
+        // hrecv[2][W][kMaxBatch] float2 | rhflags[W] u32
+        off = (off + 255) / 256 * 256;
+        m->off_rrecv = off;
+        off += 4 * 2 * W * (size_t)kMaxBatch * m->emb;
+        off = (off + 255) / 256 * 256;
+        m->off_rflags = off;
+        off += 4 * gm * W;
+        off = (off + 255) / 256 * 256;
+        m->off_rhx = off;
+        off += 8 * 2 * W * (size_t)kMaxBatch;
+        off = (off + 255) / 256 * 256;
+        m->off_rhflags = off;
+        off += 4 * W;
         m->comm_bytes = (off + 4095) / 4096 * 4096;
         DALLOC(m->comm_base, m->comm_bytes);
         CK(cudaMemset(m->comm_base, 0, m->comm_bytes));
+        DALLOC(m->rows_ctr, 16);
+        CK(cudaMemset(m->rows_ctr, 0, 16));
+        DALLOC(m->rows_gather, sizeof(float2) * W * kMaxBatch);
     }
     return NCM_OK;
 }
@@ -1083,7 +1104,7 @@ extern "C" ncm_status ncm_prefill_tokens(ncm_model* m, const int* prompt, int n_
     cudaStream_t st = stream ? (cudaStream_t)stream : m->stream;
     if (stream) m->ext_stream = st;
     CK(cudaStreamSynchronize(st));
-    if (n_prompt > 1 && !m->has_q6k && (m->world == 1 || host_mode(m))) {
+    if (n_prompt > 1 && !m->has_q6k) {
         // Eight prompt tokens per multi-row pass: every row's K/V and greedy token equal
         // the token-by-token prefill's bit for bit, so the state below is the one that
         // prefill leaves (tokens, position, prompt length, last token).
@@ -1300,14 +1321,26 @@ static int launch_batch(std::initializer_list<const DevMat*> mats, const DevMat*
 // ntok rows at once (tp.rs:349-363 per row), residual add.
 static ncm_status batch_row_parallel(ncm_model* m, const DevMat& w, BatchParams& p, int ntok, int layer, int phase,
                                      cudaStream_t s) {
-    if (!host_mode(m)) {
+    if (m->world == 1) {
         CKL(launch_batch({&w}, nullptr, EPI_RESID, p, s));
         return NCM_OK;
     }
     p.seg[0] = {m->b_part, m->emb, 0, SEG_OUT};
     p.out_stride = m->emb;
     CKL(launch_batch({&w}, nullptr, EPI_PLAIN, p, s));
-    ncm_status st = host_reduce(m, m->b_part, ntok * m->emb, layer, phase, s);
+    const int n = ntok * m->emb;
+    if (m->reduce_mode == NCM_REDUCE_FUSED_P2P) {
+        // every row's partial summed over NVLink in rank order, plus the residual
+        CKL(tp_rows_reduce_launch(m->rows, m->b_part, m->b_hidden, n, s));
+        return NCM_OK;
+    }
+    if (m->reduce_mode == NCM_REDUCE_NCCL) {
+        int r = g_nccl.AllReduce(m->b_part, m->b_part, (size_t)n, kNcclFloat, kNcclSum, m->nccl, s);
+        if (r != 0) return fail(NCM_EPEER, "ncclAllReduce failed");
+        CKL(resid_add_launch(m->b_hidden, m->b_part, n, s, true));
+        return NCM_OK;
+    }
+    ncm_status st = host_reduce(m, m->b_part, n, layer, phase, s);
     if (st) return st;
     CKL(resid_add_launch(m->b_hidden, m->b_part, ntok * m->emb, s, true));
     return NCM_OK;
@@ -1430,6 +1463,19 @@ static ncm_status enqueue_verify(ncm_model* m, int ntok, cudaStream_t s, bool wi
         for (int t = 0; t < ntok; ++t) memcpy(m->h_stage + 16 + t, m->h_red + 2 * t + 1, 4);
         return NCM_OK;
     }
+    if (m->world > 1) {
+        // each row's (logit, token) of this vocab shard, merged per row in rank order
+        h.pair_out = m->b_pairs;
+        CKL(launch_batch({&m->head}, nullptr, EPI_ARGMAX, h, s));
+        if (m->reduce_mode == NCM_REDUCE_FUSED_P2P) {
+            CKL(tp_rows_argmax_launch(m->rows, m->b_pairs, ntok, m->b_arg, s));
+        } else {
+            int r = g_nccl.AllGather(m->b_pairs, m->rows_gather, 2 * (size_t)kMaxBatch, kNcclFloat, m->nccl, s);
+            if (r != 0) return fail(NCM_EPEER, "ncclAllGather failed");
+            CKL(rows_argmax_merge_launch(m->rows_gather, m->world, ntok, m->b_arg, s));
+        }
+        return NCM_OK;
+    }
     CKL(launch_batch({&m->head}, nullptr, EPI_ARGMAX, h, s));
     return NCM_OK;
 }
@@ -1485,8 +1531,6 @@ static ncm_status run_rows(ncm_model* m, const int* tokens, int ntok, int pos0, 
 extern "C" ncm_status ncm_verify_batch(ncm_model* m, const int* tokens, int ntok, int pos0, int* argmax_out) {
     if (!m || !tokens || !argmax_out || ntok < 1 || ntok > kMaxBatch || pos0 < 0 || pos0 + ntok > m->ctx)
         return fail(NCM_EINVAL, "bad verify batch");
-    if (m->world > 1 && !host_mode(m))
-        return fail(NCM_EUNSUPPORTED, "multi-row verify under tensor parallelism runs with the host-callback reducer");
     if (m->has_q6k) return fail(NCM_EUNSUPPORTED, "the multi-row pass has no Q6_K kernel");
     for (int i = 0; i < ntok; ++i)
         if (tokens[i] < 0 || tokens[i] >= m->vocab) return fail(NCM_EINVAL, "token id out of range");
@@ -1636,8 +1680,6 @@ extern "C" ncm_status ncm_ngram_generate(ncm_model* m, const int* prompt, int n_
     if (!m || !prompt || !out_tokens || n_prompt < 1 || n_gen < 0 || k < 0)
         return fail(NCM_EINVAL, "bad n-gram speculative arguments");
     if (n_prompt + n_gen > m->ctx) return fail(NCM_EINVAL, "prompt + generation exceeds the context");
-    if (k > 0 && m->world > 1 && !host_mode(m))
-        return fail(NCM_EUNSUPPORTED, "multi-row verify under tensor parallelism runs with the host-callback reducer");
     if (stats) stats[0] = stats[1] = 0;
     ncm_status st = ncm_prefill_tokens(m, prompt, n_prompt, nullptr);
     if (st) return st;
@@ -1728,7 +1770,18 @@ extern "C" ncm_status ncm_tp_import(ncm_model* m, const uint8_t* handles, int wo
         c.flags[d] = (unsigned*)(base + m->off_flags);
         c.hx[d] = (float2*)(base + m->off_hx);
         c.hflags[d] = (unsigned*)(base + m->off_hflags);
+        m->rows.rrecv[d] = (float*)(base + m->off_rrecv);
+        m->rows.rflags[d] = (unsigned*)(base + m->off_rflags);
+        m->rows.hrecv[d] = (float2*)(base + m->off_rhx);
+        m->rows.hflags[d] = (unsigned*)(base + m->off_rhflags);
     }
+    m->rows.world = world;
+    m->rows.rank = rank;
+    m->rows.grid_max = num_sms();
+    m->rows.ctr = m->rows_ctr;
+    m->rows.stride = (size_t)kMaxBatch * m->emb;
+    m->rows.timeout_ns = m->timeout_ns;
+    m->rows.err = m->err;
     m->comm = c;
     m->tp_ready = true;
     m->dirty = true;
@@ -1784,6 +1837,7 @@ extern "C" ncm_status ncm_tp_set_timeout_ns(ncm_model* m, uint64_t ns) {
     if (!m || ns == 0) return fail(NCM_EINVAL, "bad arguments");
     m->timeout_ns = ns;
     m->comm.timeout_ns = ns;
+    m->rows.timeout_ns = ns;
     m->dirty = true;
     return NCM_OK;
 }

@@ -2020,6 +2020,128 @@ int argmax_merge_launch(const float2* gathered, int world, int* tokens, int* sta
     return (int)cudaLaunchKernelEx(&cfg, argmax_merge_kernel, gathered, world, tokens, state, ctx);
 }
 
+// ------------------------------------------------------------------ multi-row TP reductions
+// The row-parallel sum of a multi-row pass (tp.rs:349-363, every row): each CTA takes a
+// slice of the ntok x H partials, stores it into slot [me] of every rank's receive area
+// (NVLink stores for peers), publishes one flag per rank after a system-scope fence, waits
+// (bounded) for the same CTA of every rank, then sums the slice in rank order from 0.0f
+// and adds it to the residual -- the same bits on every rank, and the same bits as the
+// one-row fused reduction and the host reducer.
+__global__ void tp_rows_reduce_kernel(const __grid_constant__ TpRows t, const float* part, float* hidden, int n) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ unsigned s_epoch;
+    if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile unsigned*>(&t.ctr[0]) + 1u;
+    __syncthreads();
+    const unsigned epoch = s_epoch;
+    const int W = t.world, me = t.rank;
+    const size_t par = (size_t)(epoch & 1u) * W;
+    const int slice = (n + gridDim.x - 1) / gridDim.x;
+    const int lo = blockIdx.x * slice, hi = min(n, lo + slice);
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const float v = part[i];
+        for (int d = 0; d < W; ++d) t.rrecv[d][(par + me) * t.stride + i] = v;
+    }
+    __syncthreads();
+    unsigned* fl = nullptr;
+    if (threadIdx.x == 0) {
+        fence_acq_rel_sys();
+        for (int d = 0; d < W; ++d) st_relaxed_sys(&t.rflags[d][(size_t)blockIdx.x * W + me], epoch);
+    }
+    if ((int)threadIdx.x < W) {
+        fl = &t.rflags[me][(size_t)blockIdx.x * W + threadIdx.x];
+        if (!wait_flag_sys(fl, epoch, t.timeout_ns)) set_dev_error(t.err, NCM_DEVERR_PEER_TIMEOUT);
+    }
+    __syncthreads();
+    const float* base = t.rrecv[me] + par * t.stride;
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        float sum = 0.0f;
+        for (int src = 0; src < W; ++src) sum += __ldcg(base + (size_t)src * t.stride + i);
+        hidden[i] += sum;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // the last CTA of this rank to finish advances the epoch for the next use
+        __threadfence();
+        if (atomicAdd(&t.ctr[1], 1u) == gridDim.x - 1) {
+            t.ctr[1] = 0u;
+            t.ctr[0] = epoch;
+            __threadfence();
+        }
+    }
+}
+
+int tp_rows_reduce_launch(const TpRows& t, const float* part, float* hidden, int n, cudaStream_t s) {
+    const int grid = std::max(1, std::min(t.grid_max, (n + 1023) / 1024));
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = small_cfg(dim3(grid), dim3(256), s, true, attr);
+    return (int)cudaLaunchKernelEx(&cfg, tp_rows_reduce_kernel, t, part, hidden, n);
+}
+
+// Each row's head pair (logit, global token) of this vocab shard to every rank, then the
+// merge in rank order, the first strictly greater logit winning (cluster_tp_node.rs:
+// 1185-1204, per row) -- one CTA, one thread per row.
+__global__ void tp_rows_argmax_kernel(const __grid_constant__ TpRows t, const float2* pairs, int ntok,
+                                      int* argmax_out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const unsigned epoch = *reinterpret_cast<volatile unsigned*>(&t.ctr[2]) + 1u;
+    const int W = t.world, me = t.rank;
+    const size_t par = (size_t)(epoch & 1u) * W;
+    const int r = threadIdx.x;
+    if (r < ntok)
+        for (int d = 0; d < W; ++d) t.hrecv[d][(par + me) * kMaxBatch + r] = pairs[r];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        fence_acq_rel_sys();
+        for (int d = 0; d < W; ++d) st_relaxed_sys(&t.hflags[d][me], epoch);
+    }
+    if ((int)threadIdx.x < W && !wait_flag_sys(&t.hflags[me][threadIdx.x], epoch, t.timeout_ns))
+        set_dev_error(t.err, NCM_DEVERR_PEER_TIMEOUT);
+    __syncthreads();
+    if (r < ntok) {
+        float mv = 0.0f;
+        int mt = 0;
+        for (int src = 0; src < W; ++src) {
+            const float2 e = __ldcg(&t.hrecv[me][(par + src) * kMaxBatch + r]);
+            if (src == 0 || e.x > mv) { mv = e.x; mt = __float_as_int(e.y); }
+        }
+        argmax_out[r] = mt;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        t.ctr[2] = epoch;
+    }
+}
+
+int tp_rows_argmax_launch(const TpRows& t, const float2* pairs, int ntok, int* argmax_out, cudaStream_t s) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = small_cfg(dim3(1), dim3(32), s, true, attr);
+    return (int)cudaLaunchKernelEx(&cfg, tp_rows_argmax_kernel, t, pairs, ntok, argmax_out);
+}
+
+// The NCCL variant's merge: gathered = [world][kMaxBatch] pairs after ncclAllGather.
+__global__ void rows_argmax_merge_kernel(const float2* gathered, int world, int ntok, int* argmax_out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int r = threadIdx.x;
+    if (r >= ntok) return;
+    float mv = 0.0f;
+    int mt = 0;
+    for (int src = 0; src < world; ++src) {
+        const float2 e = gathered[(size_t)src * kMaxBatch + r];
+        if (src == 0 || e.x > mv) { mv = e.x; mt = __float_as_int(e.y); }
+    }
+    argmax_out[r] = mt;
+}
+
+int rows_argmax_merge_launch(const float2* gathered, int world, int ntok, int* argmax_out, cudaStream_t s) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = small_cfg(dim3(1), dim3(32), s, true, attr);
+    return (int)cudaLaunchKernelEx(&cfg, rows_argmax_merge_kernel, gathered, world, ntok, argmax_out);
+}
+
 __global__ void advance_kernel(int* state) {
     pdl_launch_dependents();
     pdl_wait();

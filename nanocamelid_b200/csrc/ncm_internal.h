@@ -52,6 +52,27 @@ struct TpComm {
     uint64_t timeout_ns;
 };
 
+// Device-side reduction of a multi-row pass's row-parallel partials and head pairs
+// under tensor parallelism (speculative verify, batched prefill): the same rank-order
+// sums as the one-row fused reduction, as stand-alone kernels after the batch GEMV.
+// Exchange areas (every rank's own, IPC-mapped by its peers):
+//   rrecv[dst] -> [2 parities][world][kMaxBatch * H] f32, rflags[dst] -> [grid_max][world]
+//   hrecv[dst] -> [2][world][kMaxBatch] float2,           hflags[dst] -> [world]
+// The epoch of each use comes from a counter in this rank's own memory (every rank runs
+// the same sequence of multi-row reductions): the kernel reads it at the start and the
+// last CTA to finish advances it.
+struct TpRows {
+    int world, rank, grid_max;
+    float* rrecv[kMaxWorld];
+    unsigned* rflags[kMaxWorld];
+    float2* hrecv[kMaxWorld];
+    unsigned* hflags[kMaxWorld];
+    unsigned* ctr;                // [4]: reduce epoch, reduce CTAs done, head epoch, (unused)
+    size_t stride;                // floats per (parity, rank) slot of rrecv: kMaxBatch * H
+    uint64_t timeout_ns;
+    int* err;
+};
+
 struct alignas(64) GemvParams {
     CUtensorMap tm[kMaxSeg];      // weights: dims {pitch/4 words, rows}, box {chunk_words, box_rows}
     CUtensorMap tm2;              // EPI_SILU: the up matrix (same shape as tm[0])
@@ -209,6 +230,9 @@ int embed_ssq_launch(int type, const uint8_t* table, int64_t pitch, int emb, int
 int embed_launch(int type, const uint8_t* table, int64_t pitch, int emb, const int* tokens, const int* state,
                  float* hidden, cudaStream_t s, bool pdl);
 int resid_add_launch(float* hidden, const float* part, int n, cudaStream_t s, bool pdl);
+int tp_rows_reduce_launch(const TpRows& t, const float* part, float* hidden, int n, cudaStream_t s);
+int tp_rows_argmax_launch(const TpRows& t, const float2* pairs, int ntok, int* argmax_out, cudaStream_t s);
+int rows_argmax_merge_launch(const float2* gathered, int world, int ntok, int* argmax_out, cudaStream_t s);
 int argmax_merge_launch(const float2* gathered, int world, int* tokens, int* state, int ctx, cudaStream_t s, bool pdl);
 int advance_launch(int* state, cudaStream_t s, bool pdl);
 int quantize_launch(const float* x, int n, int8_t* xq, float* xs, cudaStream_t s);

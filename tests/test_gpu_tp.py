@@ -251,3 +251,59 @@ def test_tp_speculative_with_host_reducer_on_one_gpu(ncm, orc, cuda, tmp_path, k
     finally:
         for m in models + drafts:
             m.close()
+
+
+def _rows_worker(rank, world, port, path, dpath, shares, reducer, prompt, n_gen, out_dir):
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method="file://" + os.path.join(out_dir, "pg_store"), rank=rank, world_size=world)
+    try:
+        import nanocamelid_b200 as ncm
+        from nanocamelid_b200 import tp
+        m = ncm.Model.load(path, device=rank, shares=shares, shard=rank)
+        draft = ncm.Model.load(dpath, device=rank)
+        mode = {"p2p": ncm.REDUCE_FUSED_P2P, "nccl": ncm.REDUCE_NCCL}[reducer]
+        tp.connect(m, rank, world, mode)
+        greedy = m.generate(prompt, n_gen)          # 13-token prompt: 8- and 5-row prefill passes
+        m.reset()
+        spec, stats = m.spec_generate(draft, prompt, n_gen, k=4)   # 5-row verify passes
+        json.dump({"greedy": greedy, "spec": spec}, open(os.path.join(out_dir, f"r{rank}.json"), "w"))
+        dist.barrier()
+        m.close()
+        draft.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.multigpu
+@pytest.mark.parametrize("reducer", ["p2p", "nccl"])
+@pytest.mark.parametrize("kvh,heads,shares", [(2, 4, [1, 1]), (8, 8, [2, 3, 3])])
+def test_tp_multirow_passes_on_device_reducers(ncm, orc, tmp_path, reducer, kvh, heads, shares):
+    """Multi-row passes of a sharded target with the device reducers, one process per
+    GPU: the batched prefill (8 + 5 rows) and the speculative verify (k = 4, 5 rows) sum
+    every row's row-parallel partials over NVLink in rank order (p2p) or with
+    ncclAllReduce (nccl), and merge every row's head pair across the vocab shards.  The
+    p2p reducer's greedy and speculative tokens both equal the oracle TP's greedy decode
+    (tp.rs:349-363 per row, speculative.rs:365-373); the NCCL reducer's ranks agree."""
+    world = len(shares)
+    if _ngpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    sp = _spec(ncm, kvh, heads)
+    d = dict(TINY)
+    dsp = ncm.spec(d["emb"], 1, 4, 2, d["emb"] // 4, 512, vocab=d["vocab"], ctx=d["ctx"], tied=True, seed=12)
+    path, dpath = str(tmp_path / "m.gguf"), str(tmp_path / "d.gguf")
+    ncm.write_synthetic_gguf(path, sp)
+    ncm.write_synthetic_gguf(dpath, dsp)
+    prompt = [int(v) for v in np.random.default_rng(5).integers(0, sp.vocab, size=13)]
+    n_gen = 20
+    ref = orc.OracleTP(orc.OracleModel(path), shares).generate(prompt, n_gen)
+    mp.spawn(_rows_worker, args=(world, _free_port(), path, dpath, shares, reducer, prompt, n_gen, str(tmp_path)),
+             nprocs=world, join=True)
+    out = [json.load(open(tmp_path / f"r{r}.json")) for r in range(world)]
+    assert all(o == out[0] for o in out), out
+    assert len(out[0]["greedy"]) == n_gen and len(out[0]["spec"]) == n_gen
+    if reducer == "p2p":
+        assert out[0]["greedy"] == ref and out[0]["spec"] == ref, (out[0], ref)
