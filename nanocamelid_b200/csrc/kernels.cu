@@ -1805,6 +1805,133 @@ __global__ void __launch_bounds__(W * 32) attn_av_tma_kernel(const __grid_consta
     }
 }
 
+// Softmax and V accumulation in one launch (f32 cache through the TMA ring): one
+// 256-thread CTA per (kv head, 32-dimension block, W query heads).  The first V chunks
+// are requested before anything else, so they arrive while the softmax runs; then four
+// warps per head compute that head's softmax (as attn_softmax_kernel: max, exp, the exact
+// sequential sum, * 1/sum) into shared memory -- each of the head's hd/32 CTAs computes
+// it, in parallel -- and warps 0 .. W-1 run the V chains as attn_av_tma_kernel does.  It
+// saves the softmax launch and its round trip through global memory.
+constexpr int kSvThreads = 256;
+template <int W>
+__global__ void __launch_bounds__(kSvThreads) attn_sv_kernel(const __grid_constant__ AttnParams a) {
+    extern __shared__ __align__(128) float buf[];   // V ring [S][kAvChunk][32] | w [W][ctx4]
+    __shared__ __align__(8) uint64_t full[kAvStages];
+    __shared__ SeqSumScratchT<128> sc[W];
+    __shared__ float red[8];
+    constexpr int S = kAvStages;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int k = 0; k < S; ++k) mbar_init(&full[k], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+    pdl_wait();
+    const int nd = a.hd / 32;
+    const int kvh = blockIdx.x, db = blockIdx.y % nd, hgrp = blockIdx.y / nd, tz = blockIdx.z;
+    const int pos = (a.pos_override >= 0 ? a.pos_override : __ldcg(&a.state[ST_POS])) + tz;
+    const int n = pos + 1;
+    const int g = a.heads / a.kv_heads;
+    const int h0 = kvh * g + hgrp * W;
+    const int d0 = db * 32;
+    const int ctx4 = (a.ctx + 3) & ~3;
+    float* vbuf = buf;
+    float* wsm = buf + S * kAvChunk * 32;
+    const int nchunk = (n + kAvChunk - 1) / kAvChunk;
+    const uint64_t limit_ns = 1000000000ull;
+    const uint64_t pol = l2_evict_first_policy();
+    auto issue_v = [&](int k) {   // thread 0
+        uint64_t* bar = &full[k % S];
+        mbar_arrive_expect_tx(bar, kAvChunk * 32 * 4);
+        tma_load_2d(vbuf + (k % S) * kAvChunk * 32, &a.vmap, kvh * a.hd + d0, k * kAvChunk, bar, pol);
+    };
+    if (tid == 0)
+        for (int k = 0; k < S - 1 && k < nchunk; ++k) issue_v(k);
+    // ---- softmax of head h0 + j by warps 4j .. 4j+3 (inference.rs:3522-3540)
+    const int j = warp >> 2, t = tid & 127;
+    if (j < W) {
+        const float* srow = a.scores + ((size_t)tz * a.heads + h0 + j) * a.ctx;
+        float* e = wsm + j * ctx4;
+        float mx = -INFINITY;
+        for (int p = t; p < n; p += 128) {
+            const float v = __ldcg(&srow[p]);
+            e[p] = v;
+            mx = fmaxf(mx, v);   // max is order independent (no NaNs)
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(NCM_FULL, mx, o));
+        if (lane == 0) red[warp] = mx;
+        if (j == 0) group_sync<128, 1>(); else group_sync<128, 2>();
+        mx = fmaxf(fmaxf(red[4 * j], red[4 * j + 1]), fmaxf(red[4 * j + 2], red[4 * j + 3]));
+        for (int p = t; p < n; p += 128) e[p] = expf_cr(e[p] - mx);
+        float sum;
+        if (j == 0) {
+            group_sync<128, 1>();
+            sum = seq_sum_nonneg<128, 1>([&](int i) { return e[i]; }, n, sc[0], t);
+        } else {
+            group_sync<128, 2>();
+            sum = seq_sum_nonneg<128, 2>([&](int i) { return e[i]; }, n, sc[W - 1], t);
+        }
+        const float inv = 1.0f / sum;
+        for (int p = t; p < n; p += 128) e[p] = e[p] * inv;
+    }
+    __syncthreads();
+    // ---- V chains: warp h < W, lane = dimension
+    float acc = 0.0f;
+    for (int k = 0; k < nchunk; ++k) {
+        if (tid == 0 && k + S - 1 < nchunk) issue_v(k + S - 1);
+        bool ok = mbar_wait(&full[k % S], (uint32_t)((k / S) & 1), limit_ns);
+        if (!ok && a.err) set_dev_error(a.err, NCM_DEVERR_MBAR_TIMEOUT);
+        if (!__syncthreads_and(ok)) {
+            // a load that never landed: wait (bounded) for the copies still in flight
+            if (tid == 0)
+                for (int q = k; q < nchunk && q < k + S; ++q)
+                    mbar_wait(&full[q % S], (uint32_t)((q / S) & 1), 100000000ull);
+            return;
+        }
+        if (warp < W) {
+            const float* vs = vbuf + (k % S) * kAvChunk * 32;
+            const int c0 = k * kAvChunk;
+            const float* ws = wsm + warp * ctx4 + c0;
+            const int np = min(kAvChunk, n - c0);
+            int p = 0;
+            for (; p + 16 <= np; p += 16) {
+                float wv[16], vv[16];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 w4 = *reinterpret_cast<const float4*>(ws + p + 4 * q);
+                    wv[4 * q] = w4.x; wv[4 * q + 1] = w4.y; wv[4 * q + 2] = w4.z; wv[4 * q + 3] = w4.w;
+                }
+#pragma unroll
+                for (int q = 0; q < 16; ++q) vv[q] = vs[(p + q) * 32 + lane];
+#pragma unroll
+                for (int q = 0; q < 16; ++q) acc += wv[q] * vv[q];
+            }
+            for (; p < np; ++p) acc += ws[p] * vs[p * 32 + lane];
+        }
+        __syncthreads();   // the slot may be refilled
+    }
+    if (warp < W) {
+        const int h = h0 + warp;
+        a.out[(size_t)tz * a.tok_stride + (size_t)h * a.hd + d0 + lane] = acc;
+        if (a.out_q) {
+            float amax = fabsf(acc);   // quantize_f32_to_q8_0 of this block (inference.rs:991-1029)
+#pragma unroll
+            for (int k = 16; k > 0; k >>= 1) amax = fmaxf(amax, __shfl_xor_sync(NCM_FULL, amax, k));
+            const float scale = amax / 127.0f;
+            int q = 0;
+            if (scale > 0.0f) {
+                const float inv = 1.0f / scale;
+                q = (int)fminf(fmaxf(roundf(acc * inv), -127.0f), 127.0f);
+            }
+            const size_t o = (size_t)h * a.hd + d0;
+            a.out_q[o + lane] = (int8_t)q;
+            if (lane == 0) a.out_s[o >> 5] = scale;
+        }
+    }
+}
+
 template <int W, int HPW>
 __global__ void __launch_bounds__(W * 32) attn_av_kernel(const __grid_constant__ AttnParams a) {
     extern __shared__ __align__(16) float buf[];
@@ -1812,6 +1939,20 @@ __global__ void __launch_bounds__(W * 32) attn_av_kernel(const __grid_constant__
     pdl_wait();
     const int nd = a.hd / 32;
     attn_av_body<W, HPW>(a, blockIdx.x, blockIdx.y % nd, blockIdx.y / nd, blockIdx.z, buf, threadIdx.x);
+}
+
+// The V cache of a layer as a 2-D tensor map: {kvw floats, ctx rows}, box 32 x kAvChunk.
+static int encode_v_map(AttnParams& a) {
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return (int)cudaErrorNotSupported;
+    cuuint64_t gdim[2] = {(cuuint64_t)a.kvw, (cuuint64_t)a.ctx};
+    cuuint64_t gstride[1] = {(cuuint64_t)a.kvw * 4};
+    cuuint32_t box[2] = {32, (cuuint32_t)kAvChunk};
+    cuuint32_t estride[2] = {1, 1};
+    CUresult cr = enc(&a.vmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(a.vc), gdim, gstride, box, estride,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return cr == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
 }
 
 int attention_launch(const AttnParams& a0, cudaStream_t s, bool pdl) {
@@ -1832,6 +1973,19 @@ int attention_launch(const AttnParams& a0, cudaStream_t s, bool pdl) {
     cfg.gridDim = dim3(a.kv_heads, (a.ctx + 31) / 32, nz);
     int r = (int)cudaLaunchKernelEx(&cfg, attn_scores_kernel, a);
     if (r) return r;
+    const int w = g % 2 == 0 ? 2 : 1;
+    const size_t sv_smem = (size_t)kAvStages * kAvChunk * 32 * 4 + (size_t)w * ((a.ctx + 3) & ~3) * 4;
+    if (a.vmap_on && a.sv_on && a.kv_kind == KV_F32 && (((uintptr_t)a.vc) & 15) == 0 && (a.kvw & 3) == 0 &&
+        sv_smem <= (size_t)kMaxSmem && encode_v_map(a) == 0) {
+        // softmax and V accumulation in one launch
+        if (int r2 = set_smem_limit((const void*)attn_sv_kernel<1>, kMaxSmem)) return r2;
+        if (int r2 = set_smem_limit((const void*)attn_sv_kernel<2>, kMaxSmem)) return r2;
+        cfg.gridDim = dim3(a.kv_heads, (a.hd / 32) * (g / w), nz);
+        cfg.blockDim = dim3(kSvThreads);
+        cfg.dynamicSmemBytes = sv_smem;
+        if (w == 2) return (int)cudaLaunchKernelEx(&cfg, attn_sv_kernel<2>, a);
+        return (int)cudaLaunchKernelEx(&cfg, attn_sv_kernel<1>, a);
+    }
     // the softmax of the last row reaches position pos + ntok - 1 (at most ctx - 1)
     cfg.gridDim = dim3(a.heads, 1, nz);
     cfg.dynamicSmemBytes = (size_t)a.ctx * 4;
@@ -1840,25 +1994,13 @@ int attention_launch(const AttnParams& a0, cudaStream_t s, bool pdl) {
     // heads per item: two warps of one chain each when the group allows (measured on the
     // 70B shape at 1k positions: more chains per warp, or more heads per item, are slower
     // -- the items then stream their V slices with fewer CTAs)
-    const int w = g % 2 == 0 ? 2 : 1;
-    if (a.vmap_on && a.kv_kind == KV_F32 && (((uintptr_t)a.vc) & 15) == 0 && (a.kvw & 3) == 0) {
-        EncodeTiledFn enc = encode_tiled_fn();
-        if (enc) {
-            cuuint64_t gdim[2] = {(cuuint64_t)a.kvw, (cuuint64_t)a.ctx};
-            cuuint64_t gstride[1] = {(cuuint64_t)a.kvw * 4};
-            cuuint32_t box[2] = {32, (cuuint32_t)kAvChunk};
-            cuuint32_t estride[2] = {1, 1};
-            CUresult cr = enc(&a.vmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(a.vc), gdim, gstride, box,
-                              estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-            if (cr == CUDA_SUCCESS) {
-                cfg.gridDim = dim3(a.kv_heads, (a.hd / 32) * (g / w), nz);
-                cfg.blockDim = dim3(w * 32);
-                cfg.dynamicSmemBytes = (size_t)kAvStages * kAvChunk * (32 + w) * 4;
-                if (w == 2) return (int)cudaLaunchKernelEx(&cfg, attn_av_tma_kernel<2>, a);
-                return (int)cudaLaunchKernelEx(&cfg, attn_av_tma_kernel<1>, a);
-            }
-        }
+    if (a.vmap_on && a.kv_kind == KV_F32 && (((uintptr_t)a.vc) & 15) == 0 && (a.kvw & 3) == 0 &&
+        encode_v_map(a) == 0) {
+        cfg.gridDim = dim3(a.kv_heads, (a.hd / 32) * (g / w), nz);
+        cfg.blockDim = dim3(w * 32);
+        cfg.dynamicSmemBytes = (size_t)kAvStages * kAvChunk * (32 + w) * 4;
+        if (w == 2) return (int)cudaLaunchKernelEx(&cfg, attn_av_tma_kernel<2>, a);
+        return (int)cudaLaunchKernelEx(&cfg, attn_av_tma_kernel<1>, a);
     }
     cfg.gridDim = dim3(a.kv_heads, (a.hd / 32) * (g / w), nz);
     cfg.blockDim = dim3(w * 32);

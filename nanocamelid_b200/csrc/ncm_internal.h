@@ -145,6 +145,7 @@ struct alignas(64) AttnParams {
     const void* kc_raw;
     const void* vc_raw;
     int vmap_on;             // V chunks by TMA through vmap (f32 cache)
+    int sv_on;               // with vmap_on: softmax and V accumulation in one launch
     int* err;                // device error word for bounded waits (may be null)
 };
 
