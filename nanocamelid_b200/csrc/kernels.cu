@@ -1700,6 +1700,50 @@ __device__ void attn_av_body(const AttnParams& a, int kvh, int db, int hgrp, int
 // load (32 floats x kAvChunk positions of this kv head's dimension block) per chunk into
 // a ring of kAvStages slots tracked by mbarriers, issued by thread 0; the weights still
 // come by cp.async.  One chain per thread (W warps = W query heads).
+// One chunk of a V chain: acc += w_p * v_p[lane] for p = 0 .. np-1 in order (ws: the
+// chunk's weights, vs: its [position][32] values, both in shared memory, ws 16-byte
+// aligned).  A full chunk runs as four groups of 16 positions with the next group's
+// loads issued before the current group's adds, so only the adds' own latency is serial.
+__device__ __forceinline__ float av_chunk_chain(const float* ws, const float* vs, int np, int lane, float acc) {
+    if (np == kAvChunk) {
+        float wv[2][16], vv[2][16];
+        auto load = [&](int gq, int b) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 w4 = *reinterpret_cast<const float4*>(ws + 16 * gq + 4 * q);
+                wv[b][4 * q] = w4.x; wv[b][4 * q + 1] = w4.y; wv[b][4 * q + 2] = w4.z; wv[b][4 * q + 3] = w4.w;
+            }
+#pragma unroll
+            for (int q = 0; q < 16; ++q) vv[b][q] = vs[(16 * gq + q) * 32 + lane];
+        };
+        load(0, 0);
+        asm volatile("" ::: "memory");
+#pragma unroll
+        for (int gq = 0; gq < kAvChunk / 16; ++gq) {
+            if (gq + 1 < kAvChunk / 16) load(gq + 1, (gq + 1) & 1);
+            asm volatile("" ::: "memory");   // the next group's loads stay ahead of these adds
+#pragma unroll
+            for (int q = 0; q < 16; ++q) acc += wv[gq & 1][q] * vv[gq & 1][q];
+        }
+        return acc;
+    }
+    int p = 0;
+    for (; p + 16 <= np; p += 16) {
+        float wv[16], vv[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 w4 = *reinterpret_cast<const float4*>(ws + p + 4 * q);
+            wv[4 * q] = w4.x; wv[4 * q + 1] = w4.y; wv[4 * q + 2] = w4.z; wv[4 * q + 3] = w4.w;
+        }
+#pragma unroll
+        for (int q = 0; q < 16; ++q) vv[q] = vs[(p + q) * 32 + lane];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) acc += wv[q] * vv[q];
+    }
+    for (; p < np; ++p) acc += ws[p] * vs[p * 32 + lane];
+    return acc;
+}
+
 template <int W>
 __global__ void __launch_bounds__(W * 32) attn_av_tma_kernel(const __grid_constant__ AttnParams a) {
     extern __shared__ __align__(128) float buf[];   // [slot][kAvChunk][32] V, then [slot][W][kAvChunk] w
@@ -1771,20 +1815,7 @@ __global__ void __launch_bounds__(W * 32) attn_av_tma_kernel(const __grid_consta
         const float* vs = vbuf + (k % kAvStages) * kAvChunk * 32;
         const float* ws = wbuf + (k % kAvStages) * W * kAvChunk + warp * kAvChunk;
         const int np = min(kAvChunk, n - k * kAvChunk);
-        int p = 0;
-        for (; p + 16 <= np; p += 16) {
-            float wv[16], vv[16];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float4 w4 = *reinterpret_cast<const float4*>(ws + p + 4 * q);
-                wv[4 * q] = w4.x; wv[4 * q + 1] = w4.y; wv[4 * q + 2] = w4.z; wv[4 * q + 3] = w4.w;
-            }
-#pragma unroll
-            for (int q = 0; q < 16; ++q) vv[q] = vs[(p + q) * 32 + lane];
-#pragma unroll
-            for (int q = 0; q < 16; ++q) acc += wv[q] * vv[q];
-        }
-        for (; p < np; ++p) acc += ws[p] * vs[p * 32 + lane];
+        acc = av_chunk_chain(ws, vs, np, lane, acc);
         __syncthreads();   // the slot may be refilled
     }
     const int h = h0 + warp;
@@ -1895,20 +1926,7 @@ __global__ void __launch_bounds__(kSvThreads) attn_sv_kernel(const __grid_consta
             const int c0 = k * kAvChunk;
             const float* ws = wsm + warp * ctx4 + c0;
             const int np = min(kAvChunk, n - c0);
-            int p = 0;
-            for (; p + 16 <= np; p += 16) {
-                float wv[16], vv[16];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float4 w4 = *reinterpret_cast<const float4*>(ws + p + 4 * q);
-                    wv[4 * q] = w4.x; wv[4 * q + 1] = w4.y; wv[4 * q + 2] = w4.z; wv[4 * q + 3] = w4.w;
-                }
-#pragma unroll
-                for (int q = 0; q < 16; ++q) vv[q] = vs[(p + q) * 32 + lane];
-#pragma unroll
-                for (int q = 0; q < 16; ++q) acc += wv[q] * vv[q];
-            }
-            for (; p < np; ++p) acc += ws[p] * vs[p * 32 + lane];
+            acc = av_chunk_chain(ws, vs, np, lane, acc);
         }
         __syncthreads();   // the slot may be refilled
     }
