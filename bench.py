@@ -403,7 +403,10 @@ def run_b200(args, sp):
         whole = {"bytes_per_token_per_gpu": int(bpt), "achieved_gbs": round(bpt * tok_s / 1e9, 1),
                  "frac_of_measured_hbm": round(bpt * tok_s / 1e9 / peak, 4)}
         cpu = None if (args.no_cpu or world > 1) else cpu_sample(args, sp)
-        launches_per_step = 2 + 7 * sp.layers + (0 if world == 1 or args.reducer == "p2p" else 2 * sp.layers + 1)
+        # per layer: q/k/v, attention (scores + softmax + V, or scores + one softmax·V launch
+        # for GQA groups under 8 heads), wo, gate/up, down; plus embed and head
+        attn = 3 if sp.heads // sp.kv_heads >= 8 else 2
+        launches_per_step = 2 + (4 + attn) * sp.layers + (0 if world == 1 or args.reducer == "p2p" else 2 * sp.layers + 1)
         cfg = bench_config(args, world, shares)
         cfg["l2"] = "inputs larger than L2 (weights %.2f GB/token/GPU)" % (bpt / 1e9)
         line = {"metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
