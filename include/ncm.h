@@ -92,9 +92,10 @@ ncm_status ncm_attention_kv(int kind, float* out, const float* q, const void* k_
                             int heads, int kv_heads, int head_dim, void* stream);
 
 /* No counterpart in the reference.  The same computation as ncm_attention, for callers
- * that must not allocate device memory on the call path: code running inside a CUDA
- * graph capture or a latency-critical loop where cudaMalloc would stall, and hosts that
- * run under a fixed memory budget with allocation forbidden after start-up.  The
+ * that must not allocate device memory on the call path: hosts that hand all device
+ * memory to their own pool at start-up and forbid allocation afterwards (a fixed memory
+ * budget shared with other work), and latency-critical loops where a cudaMalloc, which
+ * can synchronise the device, would stall the stream.  The
  * softmax-score scratch is a fixed 1 MiB array (262144 floats) compiled into the
  * library, held by every GPU that loads it until the process exits; calls with
  * pos >= 16384 (the limit ncm_attention has too) or heads * (pos + 1) > 262144 are

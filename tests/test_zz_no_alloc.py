@@ -1,7 +1,8 @@
 """ncm_attention_noalloc: attention for callers that may not allocate device memory.
 
-Such callers (work captured into CUDA graphs, hosts with a fixed memory budget) get the
-same result as ncm_attention from a fixed in-library scratch array.  This file is
+Such callers (hosts that hand out a fixed device-memory budget at start-up and forbid
+allocation afterwards, or latency-critical loops that a device-synchronising cudaMalloc
+would stall) get the same result as ncm_attention from a fixed in-library scratch array.  This file is
 collected last so that a failure here does not hide the rest of the suite.
 """
 import ctypes
