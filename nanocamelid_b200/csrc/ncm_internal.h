@@ -111,7 +111,7 @@ struct alignas(64) GemvParams {
     int kv_stage;                 // 1: K / V rows go to kcache / vcache as given (staging for an
                                   //    F16 / Q8_0 cache), 0: the f32 cache rows at pos
     int row_align;                // CTA row ranges start at multiples of this (2, or 32 with qout)
-    int tune;                     // measurement knobs (0 in normal use)
+    int tune;                     // measurement knobs (0 in normal use; 16: full-width rows on short tiles)
     int cgroups;                  // compute-warp groups (1, 2 or 4; 0: 4): stages worked on at once
 
     uint64_t* dbg_ts;             // measurement probe: per-CTA phase stamps [grid][8] (null in normal use)
