@@ -354,8 +354,11 @@ def run_b200(args, sp):
                "api": "ncm_forward_pass (host token -> device step -> host argmax, synchronous)"}
     nccl = None
     if world > 1 and args.reducer == "p2p":
-        # the NCCL-allreduce baseline of the same decode (same shards, positions rewritten)
+        # the NCCL-allreduce baseline of the same decode (same shards): back to the fused
+        # run's start, so that it rewrites the same positions and stays inside the context
         m.tp_set_reducer(ncm.REDUCE_NCCL)
+        p_start = max(args.prompt, args.prompt + args.warmup - 3)
+        m.forward_pass(toks[p_start], p_start)
         m.decode_steps(2, stream.cuda_stream)
         torch.cuda.synchronize()
         n_ms = timed_steps(args.steps)

@@ -10,6 +10,7 @@
 #define NCM_DEVERR_MBAR_TIMEOUT 0x1
 #define NCM_DEVERR_PEER_TIMEOUT 0x2
 #define NCM_DEVERR_BAD_ARG 0x4
+#define NCM_DEVERR_CTX_FULL 0x8   // a decode step started at or past the context limit
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -983,7 +983,8 @@ static void attn_params(ncm_model* m, int l, AttnParams& a) {
 }
 
 static ncm_status enqueue_step(ncm_model* m, bool with_head, cudaStream_t s) {
-    CKL(embed_launch(m->embd.type, m->embd.d, m->embd.pitch, m->emb, m->tokens, m->state, m->hidden, s, true));
+    CKL(embed_launch(m->embd.type, m->embd.d, m->embd.pitch, m->emb, m->tokens, m->state, m->ctx, m->err, m->hidden, s,
+                     true));
     for (int l = 0; l < m->layers; ++l) {
         const Layer& L = m->L[l];
         CKL(launch_qkv(m, l, s));
@@ -1081,6 +1082,8 @@ static ncm_status check_err(ncm_model* m) {
     if (e) {
         CK(cudaMemset(m->err, 0, 4));
         if (e & NCM_DEVERR_PEER_TIMEOUT) return fail(NCM_ETIMEOUT, "a device-side wait on a peer GPU timed out");
+        if (e & NCM_DEVERR_CTX_FULL)
+            return fail(NCM_EINVAL, "a decode step ran past the context limit (the position was held at the last slot)");
         return fail(NCM_ECUDA, "device error word " + std::to_string(e));
     }
     return NCM_OK;

@@ -2119,11 +2119,23 @@ __device__ __forceinline__ float dequant_elem(int type, const uint8_t* row, int 
 
 // inference.rs:4494-4503 embed_token: one row of the dequantised token_embd table,
 // dequantised on demand for the current token.
+// A step that starts at or past the context limit (the caller decoded more tokens than
+// the context holds) would store K/V past the cache: the position is clamped to the last
+// slot here, before any later kernel of the step reads it (they all read it after their
+// dependent-launch wait), and the error word tells the host.
 __global__ void embed_kernel(int type, const uint8_t* table, int64_t pitch, int emb, const int* tokens,
-                             const int* state, float* hidden) {
+                             int* state, int ctx, int* err, float* hidden) {
     pdl_launch_dependents();
     pdl_wait();
-    const int tok = tokens[state[ST_POS]];
+    int ps = state[ST_POS];
+    if (ps >= ctx || ps < 0) {
+        ps = ps < 0 ? 0 : ctx - 1;
+        if (blockIdx.x == 0 && threadIdx.x == 0) {
+            state[ST_POS] = ps;
+            set_dev_error(err, NCM_DEVERR_CTX_FULL);
+        }
+    }
+    const int tok = tokens[ps];
     const uint8_t* row = table + (size_t)tok * pitch;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < emb; i += gridDim.x * blockDim.x)
         hidden[i] = dequant_elem(type, row, i);
@@ -2159,11 +2171,11 @@ static cudaLaunchConfig_t small_cfg(dim3 g, dim3 b, cudaStream_t s, bool pdl, cu
     return cfg;
 }
 
-int embed_launch(int type, const uint8_t* table, int64_t pitch, int emb, const int* tokens, const int* state,
-                 float* hidden, cudaStream_t s, bool pdl) {
+int embed_launch(int type, const uint8_t* table, int64_t pitch, int emb, const int* tokens, int* state, int ctx,
+                 int* err, float* hidden, cudaStream_t s, bool pdl) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = small_cfg(dim3((emb + 255) / 256), dim3(256), s, pdl, attr);
-    return (int)cudaLaunchKernelEx(&cfg, embed_kernel, type, table, pitch, emb, tokens, state, hidden);
+    return (int)cudaLaunchKernelEx(&cfg, embed_kernel, type, table, pitch, emb, tokens, state, ctx, err, hidden);
 }
 
 __global__ void resid_add_kernel(float* hidden, const float* part, int n) {

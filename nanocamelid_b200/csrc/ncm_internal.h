@@ -228,8 +228,8 @@ int attention_launch(const AttnParams& a, cudaStream_t s, bool pdl);
 int kv_store_launch(int kind, const float* sk, const float* sv, int ntok, int kw, void* kc, void* vc,
                     const int* pos_dev, cudaStream_t s, bool pdl);
 int embed_ssq_launch(int type, const uint8_t* table, int64_t pitch, int emb, int vocab, float* out, cudaStream_t s);
-int embed_launch(int type, const uint8_t* table, int64_t pitch, int emb, const int* tokens, const int* state,
-                 float* hidden, cudaStream_t s, bool pdl);
+int embed_launch(int type, const uint8_t* table, int64_t pitch, int emb, const int* tokens, int* state, int ctx,
+                 int* err, float* hidden, cudaStream_t s, bool pdl);
 int resid_add_launch(float* hidden, const float* part, int n, cudaStream_t s, bool pdl);
 int tp_rows_reduce_launch(const TpRows& t, const float* part, float* hidden, int n, cudaStream_t s);
 int tp_rows_argmax_launch(const TpRows& t, const float2* pairs, int ntok, int* argmax_out, cudaStream_t s);

@@ -107,6 +107,26 @@ def test_bad_arguments_fail_loudly(ncm, cuda, tmp_path):
         ncm.Model.load(tmp_path / "missing.gguf")
 
 
+def test_decode_past_the_context_is_an_error_not_an_overrun(ncm, cuda):
+    """Graph-replayed steps read the position on the device, so the host cannot stop a
+    caller that decodes more tokens than the context holds.  The step's first kernel holds
+    the position at the last slot (no K/V row is stored past the cache) and the error
+    word makes the next synchronising call fail; the model stays usable."""
+    sp = tiny_spec(ncm, ctx=16)
+    m = ncm.Model.synthetic(sp, device=0)
+    p = prompt_ids(4, sp.vocab, seed=3)
+    first = m.generate(p, 8)
+    m.reset()
+    m.generate(p, 12)                      # positions 0..15: the context is full
+    m.decode_steps(6)                      # past the context
+    with pytest.raises(ncm.NcmError, match="context limit"):
+        m.sync_tokens(sp.ctx)
+    _, pos = m.sync_tokens(sp.ctx)          # the error word was cleared
+    assert pos <= sp.ctx
+    m.reset()
+    assert m.generate(p, 8) == first
+
+
 @pytest.mark.slow
 def test_config1_full_size_token_parity(ncm, orc, cuda, tmp_path):
     """Llama-3.2-1B shape, Q4_0, tied head, 16-token prompt, 32 greedy tokens."""
