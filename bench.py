@@ -271,6 +271,18 @@ def args_config_key(sp):
     return "gemv_q4_0_70b" if sp.emb == 8192 else f"gemv_emb{sp.emb}"
 
 
+def decode_context(prompt, warmup, steps):
+    """Context slots the decode bench needs: the prompt, the warm-up and timed steps, and a
+    margin (the e2e and NCCL-baseline phases rewrite positions inside this range)."""
+    return prompt + warmup + steps + 8
+
+
+def nccl_phase_start(prompt, warmup):
+    """Position the NCCL-baseline phase restarts from: one forward_pass there and two
+    untimed steps bring it to the fused phase's first timed position (prompt + warmup)."""
+    return max(prompt, prompt + warmup - 3)
+
+
 def run_b200(args, sp):
     import numpy as np
     import torch
@@ -290,7 +302,7 @@ def run_b200(args, sp):
             raise SystemExit(f"--shares lists {len(shares)} ranks for {world} processes")
     else:
         shares = None
-    ctx = args.prompt + args.warmup + args.steps + 8
+    ctx = decode_context(args.prompt, args.warmup, args.steps)
     m = ncm.Model.synthetic(sp, ctx_limit=ctx, device=local, shares=shares, shard=rank)
     if world > 1:
         # peers' exchange areas and an NCCL communicator: the fused reducer is timed first,
@@ -357,7 +369,7 @@ def run_b200(args, sp):
         # the NCCL-allreduce baseline of the same decode (same shards): back to the fused
         # run's start, so that it rewrites the same positions and stays inside the context
         m.tp_set_reducer(ncm.REDUCE_NCCL)
-        p_start = max(args.prompt, args.prompt + args.warmup - 3)
+        p_start = nccl_phase_start(args.prompt, args.warmup)
         m.forward_pass(toks[p_start], p_start)
         m.decode_steps(2, stream.cuda_stream)
         torch.cuda.synchronize()

@@ -35,3 +35,20 @@ def test_reference_arm_other_ranks_do_no_work():
              "--steps", "2", "--warmup", "1")
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip() == ""
+
+
+def test_decode_phases_stay_inside_the_context():
+    """Every phase of the decode bench (fused timed steps, then the NCCL baseline, which
+    restarts with one forward_pass and two untimed steps) writes positions below ctx."""
+    sys.path.insert(0, ROOT)
+    import bench
+    for prompt in (64, 1024):
+        for warmup in (0, 1, 3, 5, 8):
+            for steps in (1, 20, 60, 120, 500):
+                ctx = bench.decode_context(prompt, warmup, steps)
+                assert prompt + warmup + steps <= ctx          # fused phase: last step at pos - 1
+                start = bench.nccl_phase_start(prompt, warmup)
+                assert start >= prompt
+                assert start + 1 + 2 + steps <= ctx          # NCCL phase
+                if warmup >= 3:                               # the same timed positions
+                    assert start + 3 == prompt + warmup
