@@ -183,7 +183,9 @@ ncm_status ncm_generate(ncm_model* m, const int* prompt, int n_prompt, int n_gen
  * `stream` without host synchronisation (bench path).  ncm_sync_tokens waits for the
  * model's stream and for the last caller stream given to prefill / decode (which must
  * stay valid until then), copies the token history [0, count) to host and checks the
- * device error word. */
+ * device error word.  The position lives on the device, so a step that would start at or
+ * past the context limit is held at the last slot (nothing is stored past the K/V cache)
+ * and the next checking call returns NCM_EINVAL. */
 ncm_status ncm_decode_steps(ncm_model* m, int n, void* stream);
 ncm_status ncm_prefill_tokens(ncm_model* m, const int* prompt, int n_prompt, void* stream);
 ncm_status ncm_sync_tokens(ncm_model* m, int* tokens, int count, int* pos_out);
